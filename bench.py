@@ -1,0 +1,324 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Gated DeltaNet hot path; prints ONE JSON line.
+
+Default workload (N=1): batched decode, B = 256 independent sequences per GPU,
+each with its own fp32 32x128x128 state pre-filled N(0, 0.05^2) and bf16
+activations N(0,1), through one DeltaNet layer of the 35B-class dims with
+seeded Q8_0 weights.  A step is one decode token for all 256 sequences; K
+timed steps after W warm-up steps.  Every step streams the 512 MiB of state
+in and out of HBM (inputs larger than L2, so no flush is needed).
+
+Multi-GPU (torchrun): every rank runs its own 256 sequences -- the decode
+path shards by sequence with no collective ("scaling": "weak"); the only
+collectives are the barrier and the max-over-ranks of the timing.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+--impl reference times the reference's own CPU implementation of the path
+(the in-place build in oracle/_ref, unmodified dispatch; else the bit-identical
+port) on this host's cores, a bounded sample of sequences per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "gated-DeltaNet tok/s (decode B=256, prefill T=4k); % of HBM/TC roofline"
+BATCH = 256
+# dram__bytes_read.sum + dram__bytes_write.sum of one gdn_state_kernel launch at
+# B = 256, from the ncu capture summarised in profiles/gdn_state_kernel_decode_b256.md
+# (None until that capture exists).
+NCU_STATE_TRAFFIC = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: str):
+        self.index = index
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.tmp.flush()
+        rows = [r.split(",") for r in Path(self.tmp.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if len(r) > 8 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 8 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            if len(r) > 8:
+                for i, n in enumerate(names):
+                    if r[5 + i].strip().lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def state_kernel_bytes(cfg, B):
+    """Algorithmic HBM bytes of one gdn_state_kernel launch: state read + write,
+    the conv'd q/k/v, z, gates read once, the fp16 gated output written once."""
+    d2 = cfg.head_dim * cfg.head_dim
+    return (B * cfg.num_v_heads * d2 * 4 * 2 + B * cfg.qkv_dim * 4 + B * cfg.inner * 4 + B * 2 * cfg.num_v_heads * 4
+            + B * cfg.inner * 2)
+
+
+def step_bytes(cfg, B):
+    """Algorithmic HBM bytes of one decode step at batch B (the per-step
+    figure of the roofline): state r+w, conv window (3 rows read, 1 written),
+    conv weights, Q8_0 weights once, activations in/out."""
+    w = (cfg.in_proj_rows * cfg.hidden + cfg.hidden * cfg.inner) // 32 * 34
+    return (B * cfg.num_v_heads * cfg.head_dim * cfg.head_dim * 8 + B * 4 * cfg.qkv_dim * 4 + cfg.qkv_dim * 16 + w
+            + B * cfg.hidden * 2 + B * cfg.hidden * 4)
+
+
+def cpu_reference_run(cfg, tensors, n_calls, seqs, act_mode):
+    """Times n_calls of the reference's deltanet_forward over `seqs` prefilled sequences."""
+    from oracle import oracle as O
+    from winmoe_b200 import synth
+    orc = O.ref() if O.ref_available() else O.port()
+    kind = "reference" if O.ref_available() else "port"
+    states = [synth.prefilled_state(cfg, b) for b in range(seqs)]
+    convs = [np.zeros((4, cfg.qkv_dim), np.float32) for _ in range(seqs)]
+    poss = [np.zeros(1, np.int32) for _ in range(seqs)]
+    xs = synth.hidden_states(n_calls, cfg.hidden, seed=11)
+    orc.deltanet_forward(cfg, xs[0], states[0].copy(), convs[0].copy(), poss[0].copy(), tensors, act_mode=act_mode)
+    t0 = time.perf_counter()
+    for i in range(n_calls):
+        b = i % seqs
+        orc.deltanet_forward(cfg, xs[i], states[b], convs[b], poss[b], tensors, act_mode=act_mode)
+    dt = time.perf_counter() - t0
+    return dt, kind
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from winmoe_b200 import synth
+    from winmoe_b200.config import DIMS_35B as cfg
+    tensors = synth.layer_tensors(cfg)
+    per_step = 4  # sequence-tokens of the B=256 workload timed per step
+    dt_w, kind = cpu_reference_run(cfg, tensors, per_step * args.warmup, per_step, 0) if args.warmup else (0, None)
+    dt, kind = cpu_reference_run(cfg, tensors, per_step * args.steps, per_step, 0)
+    toks = per_step * args.steps
+    v = toks / dt
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode B=256 (config 2), reference deltanet_forward per sequence-token",
+                   "hidden": cfg.hidden, "k_heads": cfg.num_k_heads, "v_heads": cfg.num_v_heads,
+                   "head_dim": cfg.head_dim, "weights": "Q8_0"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
+                         "sample": f"{per_step} sequence-tokens per step x {args.steps} steps of the B=256 decode "
+                                   "workload (prefilled states), engine/runtime/deltanet_impl.h:deltanet_forward "
+                                   "with its unmodified Q8_0/Q8_K dispatch, OpenMP over all host threads"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world, rank, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    from winmoe_b200 import layer as L, synth
+    from winmoe_b200._lib import lib
+    from winmoe_b200.config import DIMS_35B as cfg
+
+    B, K, W = BATCH, args.steps, args.warmup
+    tensors = synth.layer_tensors(cfg)
+    w = L.DeltaNetWeights.upload(cfg, tensors.in_proj, tensors.out_proj, tensors.conv1d_w, tensors.ssm_a,
+                                 tensors.dt_bias, tensors.head_norm, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(7 + 1000 * rank)
+    st = L.DeltaNetState.zeros(cfg, B, dev)
+    st.S.normal_(0.0, 0.05, generator=gen)
+    xs = torch.randn((W + K, B, cfg.hidden), generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty((B, cfg.hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    # --- device-resident inputs (value)
+    for i in range(W):
+        L.decode_step(w, st, xs[i], out, stream)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    smi_id = vis[torch.cuda.current_device()] if vis else str(torch.cuda.current_device())
+    with ClockSampler(smi_id) as clk:
+        e0.record(stream)
+        for i in range(K):
+            L.decode_step(w, st, xs[W + i], out, stream)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    clocks = clk.summary()
+    value = B * K * world / (ms / 1e3)
+
+    # --- end to end through the public API: pinned host x in, host out back, every step
+    xh = torch.empty((K + W, B, cfg.hidden), dtype=torch.bfloat16, pin_memory=True)
+    xh.copy_(xs.cpu())
+    oh = torch.empty((B, cfg.hidden), dtype=torch.float32, pin_memory=True)
+    xd = torch.empty((B, cfg.hidden), dtype=torch.bfloat16, device=dev)
+    for i in range(W):
+        xd.copy_(xh[i], non_blocking=True)
+        L.decode_step(w, st, xd, out, stream)
+        oh.copy_(out, non_blocking=True)
+    barrier()
+    e0.record(stream)
+    for i in range(K):
+        xd.copy_(xh[W + i], non_blocking=True)
+        L.decode_step(w, st, xd, out, stream)
+        oh.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+    e2e = B * K * world / (ms_e2e / 1e3)
+
+    # --- per-kernel durations (separate pass: events around each phase, per step)
+    import ctypes as C
+    h = lib()
+    h.gdn_profile_enable(1)
+    phases = []
+    buf = (C.c_float * 4)()
+    for i in range(K):
+        L.decode_step(w, st, xs[W + i], out, stream)
+        n = h.gdn_decode_phase_ms(buf, 4)
+        phases.append([buf[j] for j in range(n)])
+    h.gdn_profile_enable(0)
+    ph = np.mean(np.array(phases), axis=0)
+    state_ms = float(ph[2])
+    hbm_peak, tc_peak, peak_src = measured_peaks()
+    sk_bytes = state_kernel_bytes(cfg, B)
+    achieved = sk_bytes / (state_ms / 1e3) / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "operand_dtypes": {"state": "f32", "x": "bf16", "projections": "f16 x f16 -> f32 (tcgen05, TMEM)"},
+        "data": "synthetic",
+        "config": {"workload": "decode B=256 per GPU (config 2): one DeltaNet layer, one token for 256 sequences "
+                               "per step", "batch_per_gpu": B, "hidden": cfg.hidden, "k_heads": cfg.num_k_heads,
+                   "v_heads": cfg.num_v_heads, "head_dim": cfg.head_dim, "weights": "Q8_0 (seeded)",
+                   "state": "fp32 N(0,0.05^2) prefilled", "parallelism": f"sequence-sharded x{world}, no collective",
+                   "l2": "inputs larger than L2: 512 MiB of state read+written per step"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": B * cfg.hidden * 2,
+                "d2h_bytes_per_step": B * cfg.hidden * 4},
+        "gpu_launches": 5 * K,
+        "roofline": {"bound": "hbm", "kernel": "gdn_state_kernel", "achieved": achieved, "peak": hbm_peak,
+                     "unit": "GB/s", "frac": achieved / hbm_peak, "peak_source": peak_src,
+                     "traffic": NCU_STATE_TRAFFIC, "algorithmic_bytes_per_launch": sk_bytes,
+                     "launch_ms": state_ms},
+        "phases_ms": {"in_proj": float(ph[0]), "prep": float(ph[1]), "state": float(ph[2]),
+                      "out_proj": float(ph[3])},
+        "step_roofline": {"algorithmic_bytes_per_step": step_bytes(cfg, B),
+                          "achieved_gbs": step_bytes(cfg, B) / (ms / K / 1e3) / 1e9,
+                          "frac": step_bytes(cfg, B) / (ms / K / 1e3) / 1e9 / hbm_peak},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dt, kind = cpu_reference_run(cfg, tensors, 64, 4, 0)
+        line["cpu_baseline"] = {
+            "value": 64 / dt, "unit": "tok/s", "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+            "kind": kind, "sample": "64 sequence-tokens (4 prefilled sequences x 16 tokens) of the B=256 decode "
+                                    "workload through the reference's deltanet_forward, unmodified dispatch"}
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

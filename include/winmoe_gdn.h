@@ -1,0 +1,201 @@
+/*
+ * winmoe_gdn.h -- C ABI of the B200 (sm_100a) Gated DeltaNet hot path.
+ *
+ * Two groups of entry points, both exported by winmoe_b200/libwinmoe_gdn.so:
+ *
+ *  1. The reference engine's DeltaNet offload API, same names and signatures
+ *     as engine/runtime/gpu_offload.h:19-53 (gpu_init ... gpu_get_ssm_out_buf),
+ *     so engine/runtime/winmoe_inference.c links against this library without
+ *     source changes (its call sites: 868, 938-942, 1215-1226, 1437-1440).
+ *     Host pointers in, host pointers out, 0 = ok / -1 = error, one host
+ *     thread, module-owned device buffers -- as in the reference.
+ *
+ *  2. gdn_* entry points: device pointers, a caller stream, no hidden
+ *     allocation, every call returns a gdn_status.  These cover what the
+ *     reference does on the CPU in deltanet_forward
+ *     (engine/runtime/deltanet_impl.h:145-377) -- for a batch of sequences
+ *     (decode) or a run of tokens of one sequence (chunked prefill) -- and the
+ *     GGUF Q8_0 / Q4_K dequant + GEMV kernels behind quant_matvec
+ *     (engine/runtime/transformer.h:157-194).
+ *
+ * Conventions: all pointers of group 2 are device pointers unless stated;
+ * `stream` is a cudaStream_t (NULL = legacy default stream); every call is
+ * stream-ordered and returns after enqueueing.  Shapes use int64_t.
+ * No entry point aborts or exits; on error the status is returned and
+ * gdn_last_error() describes it (thread-local string).
+ */
+#ifndef WINMOE_GDN_H
+#define WINMOE_GDN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+
+typedef enum gdn_status {
+    GDN_OK = 0,
+    GDN_ERR_CUDA = -1,    /* a CUDA call failed (the reference's CHECK_CUDA -1, gpu_offload.cu:23-29) */
+    GDN_ERR_SHAPE = -2,   /* a dimension is out of range or not a multiple the kernel needs */
+    GDN_ERR_TYPE = -3,    /* unsupported GGML type id or activation dtype */
+    GDN_ERR_TIMEOUT = -4, /* a bounded device-side wait gave up (read with gdn_check_device_error) */
+    GDN_ERR_STATE = -5,   /* not initialised / layer not uploaded (gpu_offload.cu:1078) */
+    GDN_ERR_ARG = -6,     /* NULL or misaligned pointer, workspace too small */
+    GDN_ERR_NOMEM = -7    /* an allocation of the legacy API failed */
+} gdn_status;
+
+/* Activation dtypes accepted by the gdn_* entry points. */
+enum { GDN_DTYPE_F32 = 0, GDN_DTYPE_BF16 = 1, GDN_DTYPE_F16 = 2 };
+
+/* GGML type ids (engine/runtime/gguf_parser.h:21-29). */
+enum { GDN_GGML_F32 = 0, GDN_GGML_Q8_0 = 8, GDN_GGML_Q4_K = 12 };
+
+/* Head maps of the Q/K key group shared by a value head h (hpg = Hv / Hk). */
+enum {
+    GDN_HEAD_MAP_GROUPED = 0,    /* g = h / hpg: engine/runtime/deltanet_impl.h:280 (default) */
+    GDN_HEAD_MAP_INTERLEAVED = 1 /* g = h % Hk:  engine/runtime/winmoe_inference.c:1330 */
+};
+
+/* Description of the last error on this host thread ("" if none). */
+GDN_API const char* gdn_last_error(void);
+/* ABI version of this library (major*100 + minor). */
+GDN_API int gdn_abi_version(void);
+/* Reads and clears the device error word that bounded waits set; returns
+ * GDN_OK or GDN_ERR_TIMEOUT.  Synchronises `stream`. */
+GDN_API int gdn_check_device_error(void* stream);
+
+/* ------------------------------------------------------------ quant blocks */
+
+/*
+ * Q8_0 in HBM.  GGUF stores a Q8_0 row as blocks of {fp16 d; int8 qs[32]}
+ * (34 bytes, engine/runtime/q8_dequant.h:15-18).  On the device the library
+ * keeps the same numbers as two planes: qs [rows][cols] int8 and
+ * d [rows][cols/32] fp16 bits, so that every load is 16-byte aligned and the
+ * tensor-core path can move tiles with TMA.  Dequantised weights are the
+ * same floats d*q either way.
+ *
+ * gdn_q8_0_repack: GGUF blocks (device) -> planes (device).  cols % 32 == 0.
+ * Replaces the raw-block cudaMemcpy of gpu_upload_deltanet_weights
+ * (engine/runtime/gpu_offload.cu:1056-1061).
+ */
+GDN_API int gdn_q8_0_repack(const void* blocks, int8_t* qs, uint16_t* d,
+                    int64_t rows, int64_t cols, void* stream);
+
+/* Dequantise Q8_0 planes to fp32, bit-exact with q8_dequant_row
+ * (engine/runtime/q8_dequant.h:116-126): out[r][c] = float(d) * q. */
+GDN_API int gdn_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out,
+                     int64_t rows, int64_t cols, void* stream);
+
+/*
+ * y[m][n] = sum_k x[m][k] * W[n][k] with W Q8_0 planes [n_rows][k].
+ * The quant_matvec of engine/runtime/transformer.h:157-194 (type 8), for a
+ * batch of m activation rows, with fp32 accumulation of fp32 activations
+ * (the semantics of q8_matvec_kernel, engine/runtime/gpu_offload.cu:152-199).
+ * x_dtype: GDN_DTYPE_F32 or GDN_DTYPE_BF16.  k % 32 == 0.
+ * Dequantises in registers (CUDA cores) for small m; for m >= 64 and
+ * k % 64 == 0 it runs the tcgen05 tensor-core kernel with fp16 operands
+ * (weights rounded once to fp16, activations converted to fp16) and fp32
+ * accumulation in TMEM.
+ */
+GDN_API int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k,
+                  const void* x, int x_dtype, int64_t m, float* y, void* stream);
+
+/*
+ * Q4_K: GGUF superblocks of 256 weights, {fp16 d; fp16 dmin; u8 scales[12];
+ * u8 qs[128]} (144 bytes, engine/runtime/q4k_dequant.h:28-33), used as stored.
+ * gdn_q4_k_dequant: fp32 weights in the GGML nibble layout with the float
+ * formula of engine/runtime/gpu_offload.cu:237-250, w = (d*sc)*q - (dmin*m),
+ * each operation rounded once; cols % 256 == 0.
+ */
+GDN_API int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, void* stream);
+
+/* y[m][n] = sum_k x[m][k] * W[n][k], W Q4_K [n_rows][k], fp32 activations
+ * and accumulation (q4k_matvec_kernel, engine/runtime/gpu_offload.cu:206-268),
+ * dequantised in registers.  x_dtype: F32 or BF16.  k % 256 == 0. */
+GDN_API int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k,
+                  const void* x, int x_dtype, int64_t m, float* y, void* stream);
+
+/* ---------------------------------------------------------------- the layer */
+
+/* Dimensions, as dn_init_dims derives them (engine/runtime/deltanet_impl.h:32-44):
+ * Hv = inner / head_dim, hpg = Hv / Hk, KEY = Hk*d, QKV = 2*KEY + inner. */
+typedef struct gdn_dims {
+    int32_t hidden;      /* model width (2048 for the 35B-class config) */
+    int32_t num_k_heads; /* Hk, ssm.group_count (16) */
+    int32_t num_v_heads; /* Hv = ssm.inner_size / ssm.state_size (32) */
+    int32_t head_dim;    /* d, ssm.state_size; must be 128 */
+} gdn_dims;
+
+/*
+ * One layer's weights on the device (the DeltaNet fields of LayerWeights,
+ * engine/runtime/transformer.h:63-78).
+ *   in_*: the fused input projection, rows in this order:
+ *         attn_qkv (QKV rows) | attn_gate = z (inner) | ssm_beta (Hv) | ssm_alpha (Hv);
+ *         cols = hidden.  (Rows are independent in a GEMV, so stacking the
+ *         reference's four tensors is exact.)
+ *   out_*: ssm_out, rows = hidden, cols = inner.
+ *   weight_type: GDN_GGML_Q8_0 (planes in *_qs/*_d) or GDN_GGML_Q4_K
+ *         (raw superblocks in *_blocks).
+ *   conv1d_w [QKV][4] fp32 (ssm_conv1d.weight, tap k=0 oldest);
+ *   ssm_a [Hv] (= -exp(A_log)), dt_bias [Hv], head_norm [head_dim] or NULL.
+ */
+typedef struct gdn_layer {
+    gdn_dims dims;
+    int32_t weight_type;
+    int32_t head_map;
+    const int8_t* in_qs;
+    const uint16_t* in_d;
+    const int8_t* out_qs;
+    const uint16_t* out_d;
+    const void* in_blocks;
+    const void* out_blocks;
+    const float* conv1d_w;
+    const float* ssm_a;
+    const float* dt_bias;
+    const float* head_norm;
+} gdn_layer;
+
+/* Bytes of scratch gdn_decode_step needs for `batch` sequences. */
+GDN_API size_t gdn_decode_workspace_size(const gdn_dims* dims, int64_t batch);
+
+/*
+ * One decode token for `batch` independent sequences: deltanet_forward
+ * (engine/runtime/deltanet_impl.h:145-377) applied to each sequence b.
+ *   x   [batch][hidden] (x_dtype F32 or BF16);  out [batch][hidden] fp32.
+ *   S   [batch][Hv][d][d] fp32, row = key index, col = value index (DeltaNetState.S);
+ *   conv_buf [batch][4][QKV] fp32 circular window, conv_pos [batch] int32
+ *   (DeltaNetState.conv_buf / conv_pos) -- all updated in place.
+ *   workspace: >= gdn_decode_workspace_size bytes of device memory, 256-aligned.
+ */
+GDN_API int gdn_decode_step(const gdn_layer* layer, int64_t batch,
+                    const void* x, int x_dtype, float* out,
+                    float* S, float* conv_buf, int32_t* conv_pos,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Optional phase timing of gdn_decode_step, for benchmarks.  While enabled
+ * (on the calling thread's current device), every gdn_decode_step records a
+ * CUDA event before and after each of its phases on its stream.
+ * gdn_decode_phase_ms waits for the events of the most recent call and
+ * writes up to n phase durations in milliseconds:
+ *   [0] input projection  [1] conv/L2/gates  [2] state update  [3] out_proj
+ * Returns the number of phases written.  No counterpart in the reference
+ * (which times whole tokens with QueryPerformanceCounter,
+ * engine/runtime/winmoe_inference.c:1031-1037).
+ */
+GDN_API int gdn_profile_enable(int on);
+GDN_API int gdn_decode_phase_ms(float* ms, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WINMOE_GDN_H */

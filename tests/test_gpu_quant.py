@@ -1,0 +1,97 @@
+"""GPU parity of the GGUF quant kernels against the CPU oracle.
+
+Bit-exact: Q8_0 / Q4_K dequantised weights (the north-star requirement).
+Tolerances: CUDA-core GEMVs with fp32 activations vs the oracle's
+fp32-activation projections, rel-L2 <= 1e-5 (only the summation order
+differs); the tcgen05 GEMM (fp16 operands, fp32 accumulation) vs an fp32
+product of the same fp16-rounded operands, rel-L2 <= 1e-5, and vs the fp32
+oracle, rel-L2 <= 2e-3 (one fp16 rounding of each weight and activation).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from winmoe_b200 import layer as L, synth
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.mark.parametrize("rows,cols", [(96, 256), (12352, 2048), (2048, 4096), (7, 32)])
+def test_q8_0_dequant_bit_exact(rows, cols):
+    blocks = synth.q8_0_blocks(rows, cols, seed=100 + rows)
+    qs, d = L.q8_0_planes(blocks, rows, cols, DEV)
+    got = L.dequant_q8_0(qs, d).cpu().numpy()
+    want = O.port().q8_0_dequant(blocks, rows * cols).reshape(rows, cols)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    qs_np, d_np = synth.q8_0_split(blocks, rows, cols)
+    assert np.array_equal(qs.cpu().numpy(), qs_np)
+    assert np.array_equal(d.cpu().numpy().view(np.uint16), d_np)
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 512), (12352, 2048), (2048, 4096), (3, 256)])
+def test_q4_k_dequant_bit_exact(rows, cols):
+    blocks = synth.q4_k_blocks(rows, cols, seed=200 + rows)
+    dev = torch.from_numpy(blocks.reshape(-1)).to(DEV)
+    got = L.dequant_q4_k(dev, rows, cols).cpu().numpy()
+    want = O.port().q4_k_dequant(blocks, rows * cols).reshape(rows, cols)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 13, 32])
+@pytest.mark.parametrize("n,k", [(12352, 2048), (2048, 4096), (50, 96)])
+def test_q8_0_gemv_fp32(m, n, k):
+    blocks = synth.q8_0_blocks(n, k, seed=300 + n)
+    x = synth.hidden_states(m, k, seed=301)
+    qs, d = L.q8_0_planes(blocks, n, k, DEV)
+    y = L.gemm_q8_0(qs, d, torch.from_numpy(x).to(DEV)).cpu().numpy()
+    P = O.port()
+    for i in range(m):
+        want = P.quant_matvec(blocks, x[i], n, k, 8, O.ACT_FP32)
+        assert rel_l2(y[i], want) <= 1e-5, i
+
+
+@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("n,k", [(12352, 2048), (2048, 4096), (64, 2048)])
+def test_q4_k_gemv_fp32(m, n, k):
+    blocks = synth.q4_k_blocks(n, k, seed=400 + n)
+    x = synth.hidden_states(m, k, seed=401)
+    dev = torch.from_numpy(blocks.reshape(-1)).to(DEV)
+    y = L.gemm_q4_k(dev, n, k, torch.from_numpy(x).to(DEV)).cpu().numpy()
+    P = O.port()
+    for i in range(m):
+        want = P.quant_matvec(blocks, x[i], n, k, 12, O.ACT_FP32)
+        assert rel_l2(y[i], want) <= 1e-5, i
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 12352, 2048), (256, 2048, 4096), (200, 300, 2048),
+                                   (64, 128, 128), (1000, 12352, 2048), (4096, 2048, 4096)])
+def test_q8_0_gemm_tensor_core(m, n, k):
+    blocks = synth.q8_0_blocks(n, k, seed=500 + n + k)
+    qs, d = L.q8_0_planes(blocks, n, k, DEV)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m + n + k)).to(torch.float16).to(DEV)
+    y = L.gemm_q8_0(qs, d, x).double()
+    w16 = torch.from_numpy(synth.q8_0_dequant_np(blocks, n, k)).to(torch.float16).to(DEV)
+    want16 = x.double() @ w16.double().T
+    err = ((y - want16).norm() / want16.norm()).item()
+    assert err <= 1e-5, err
+    w32 = torch.from_numpy(synth.q8_0_dequant_np(blocks, n, k)).double().to(DEV)
+    want32 = x.double() @ w32.T
+    err32 = ((y - want32).norm() / want32.norm()).item()
+    assert err32 <= 2e-3, err32
+    # every row and column tile was written (no stale rows from a bad tile map)
+    rows_err = ((y - want16).norm(dim=1) / want16.norm(dim=1)).max().item()
+    assert rows_err <= 1e-4, rows_err
+
+
+def test_no_device_timeout_flag():
+    from winmoe_b200._lib import lib
+    torch.cuda.synchronize()
+    assert lib().gdn_check_device_error(None) == 0

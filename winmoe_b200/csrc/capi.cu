@@ -1,0 +1,136 @@
+// The gdn_* C ABI (include/winmoe_gdn.h): argument checks, error strings, the
+// device error word, and dispatch to the kernels.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "gdn_common.cuh"
+#include "quant.cuh"
+#include "decode.cuh"
+
+namespace gdn {
+
+static thread_local char g_errbuf[512] = "";
+
+int fail(int st, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_errbuf, sizeof(g_errbuf), fmt, ap);
+    va_end(ap);
+    return st;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return GDN_OK;
+    snprintf(g_errbuf, sizeof(g_errbuf), "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+    return GDN_ERR_CUDA;
+}
+
+// One error word per device, a __device__ variable (no allocation).
+__device__ uint32_t g_device_error_word;
+
+uint32_t* device_error_word() {
+    static uint32_t* ptrs[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (ptrs[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error_word) != cudaSuccess) return nullptr;
+        ptrs[dev] = static_cast<uint32_t*>(p);
+    }
+    return ptrs[dev];
+}
+
+static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+static int check_act_dtype(int dt) {
+    if (dt == GDN_DTYPE_F32 || dt == GDN_DTYPE_BF16 || dt == GDN_DTYPE_F16) return GDN_OK;
+    return fail(GDN_ERR_TYPE, "activation dtype %d is not supported (0=f32, 1=bf16, 2=f16)", dt);
+}
+
+}  // namespace gdn
+
+using namespace gdn;
+
+extern "C" {
+
+const char* gdn_last_error(void) { return g_errbuf; }
+
+int gdn_abi_version(void) { return 100; }
+
+int gdn_check_device_error(void* stream) {
+    GDN_CUDA(cudaStreamSynchronize(as_stream(stream)));
+    uint32_t w = 0;
+    GDN_CUDA(cudaMemcpyFromSymbol(&w, g_device_error_word, sizeof(w)));
+    if (w == 0) return GDN_OK;
+    const uint32_t zero = 0;
+    GDN_CUDA(cudaMemcpyToSymbol(g_device_error_word, &zero, sizeof(zero)));
+    if (w & DEV_ERR_TIMEOUT) return fail(GDN_ERR_TIMEOUT, "a bounded device-side wait timed out (word 0x%x)", w);
+    return fail(GDN_ERR_SHAPE, "a device-side bounds check failed (word 0x%x)", w);
+}
+
+int gdn_q8_0_repack(const void* blocks, int8_t* qs, uint16_t* d, int64_t rows, int64_t cols, void* stream) {
+    if (rows < 0 || cols < 0 || cols % 32 != 0) return fail(GDN_ERR_SHAPE, "q8_0 repack: cols %% 32 != 0");
+    if (!blocks || !qs || !d) return fail(GDN_ERR_ARG, "q8_0 repack: NULL pointer");
+    if (!aligned(qs, 16) || !aligned(d, 2)) return fail(GDN_ERR_ARG, "q8_0 repack: qs must be 16-byte aligned");
+    return launch_q8_0_repack(blocks, qs, d, rows, cols, as_stream(stream));
+}
+
+int gdn_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t rows, int64_t cols, void* stream) {
+    if (rows < 0 || cols < 0 || cols % 32 != 0) return fail(GDN_ERR_SHAPE, "q8_0 dequant: cols %% 32 != 0");
+    if (!qs || !d || !out) return fail(GDN_ERR_ARG, "q8_0 dequant: NULL pointer");
+    if (!aligned(qs, 16) || !aligned(out, 16)) return fail(GDN_ERR_ARG, "q8_0 dequant: qs/out must be 16-byte aligned");
+    return launch_q8_0_dequant(qs, d, out, rows, cols, as_stream(stream));
+}
+
+int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k, const void* x, int x_dtype,
+                  int64_t m, float* y, void* stream) {
+    if (n_rows < 0 || m < 0 || k <= 0 || k % 32 != 0) return fail(GDN_ERR_SHAPE, "q8_0 gemm: k must be a positive multiple of 32");
+    if (!qs || !d || !x || !y) return fail(GDN_ERR_ARG, "q8_0 gemm: NULL pointer");
+    int st = check_act_dtype(x_dtype);
+    if (st) return st;
+    if (!aligned(qs, 16)) return fail(GDN_ERR_ARG, "q8_0 gemm: qs must be 16-byte aligned");
+    if (n_rows == 0 || m == 0) return GDN_OK;
+    cudaStream_t s = as_stream(stream);
+    if (m >= 64 && k % 64 == 0 && x_dtype == GDN_DTYPE_F16 && aligned(x, 16))
+        return launch_q8_0_gemm_tc(qs, d, n_rows, k, static_cast<const __half*>(x), m, y, s);
+    return launch_q8_0_gemv(qs, d, n_rows, k, x, x_dtype, m, y, s);
+}
+
+int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, void* stream) {
+    if (rows < 0 || cols < 0 || cols % 256 != 0) return fail(GDN_ERR_SHAPE, "q4_k dequant: cols %% 256 != 0");
+    if (!blocks || !out) return fail(GDN_ERR_ARG, "q4_k dequant: NULL pointer");
+    if (!aligned(blocks, 16) || !aligned(out, 16)) return fail(GDN_ERR_ARG, "q4_k dequant: pointers must be 16-byte aligned");
+    return launch_q4_k_dequant(blocks, out, rows, cols, as_stream(stream));
+}
+
+int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
+                  void* stream) {
+    if (n_rows < 0 || m < 0 || k <= 0 || k % 256 != 0) return fail(GDN_ERR_SHAPE, "q4_k gemm: k must be a positive multiple of 256");
+    if (!blocks || !x || !y) return fail(GDN_ERR_ARG, "q4_k gemm: NULL pointer");
+    int st = check_act_dtype(x_dtype);
+    if (st) return st;
+    if (!aligned(blocks, 16)) return fail(GDN_ERR_ARG, "q4_k gemm: blocks must be 16-byte aligned");
+    if (n_rows == 0 || m == 0) return GDN_OK;
+    return launch_q4_k_gemv(blocks, n_rows, k, x, x_dtype, m, y, as_stream(stream));
+}
+
+size_t gdn_decode_workspace_size(const gdn_dims* dims, int64_t batch) {
+    if (dims == nullptr || batch <= 0) return 0;
+    return decode_workspace_bytes(*dims, batch);
+}
+
+int gdn_decode_step(const gdn_layer* layer, int64_t batch, const void* x, int x_dtype, float* out, float* S,
+                    float* conv_buf, int32_t* conv_pos, void* workspace, size_t workspace_bytes, void* stream) {
+    return decode_step(layer, batch, x, x_dtype, out, S, conv_buf, conv_pos, workspace, workspace_bytes,
+                       as_stream(stream));
+}
+
+int gdn_profile_enable(int on) { return profile_enable(on); }
+
+int gdn_decode_phase_ms(float* ms, int n) {
+    if (ms == nullptr || n < 0) return fail(GDN_ERR_ARG, "gdn_decode_phase_ms: bad buffer");
+    return phase_ms(ms, n);
+}
+
+}  // extern "C"

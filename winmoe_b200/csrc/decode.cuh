@@ -1,0 +1,14 @@
+// The decode step and its helpers (decode.cu).
+#pragma once
+#include "gdn_common.cuh"
+
+namespace gdn {
+
+size_t decode_workspace_bytes(const gdn_dims& d, int64_t batch);
+int validate_layer(const gdn_layer* L);
+int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
+                int32_t* conv_pos, void* ws, size_t ws_bytes, cudaStream_t s);
+int profile_enable(int on);
+int phase_ms(float* ms, int n);
+
+}  // namespace gdn

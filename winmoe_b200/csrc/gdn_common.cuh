@@ -1,0 +1,56 @@
+// Shared definitions of the sm_100a Gated DeltaNet library: status plumbing,
+// dtype loads, and the device error word that bounded waits report through.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/winmoe_gdn.h"
+
+namespace gdn {
+
+// Sets the thread-local error string; returns `st` so call sites can write
+// `return fail(GDN_ERR_SHAPE, "...")`.
+int fail(int st, const char* fmt, ...);
+// Maps a CUDA error to GDN_ERR_CUDA with its name; GDN_OK if none.
+int cuda_status(cudaError_t e, const char* what);
+
+#define GDN_CUDA(call)                                                  \
+    do {                                                                \
+        cudaError_t e__ = (call);                                       \
+        if (e__ != cudaSuccess) return ::gdn::cuda_status(e__, #call);  \
+    } while (0)
+
+// After a launch: reports configuration errors (not asynchronous faults).
+#define GDN_LAUNCH_CHECK(name)                                          \
+    do {                                                                \
+        cudaError_t e__ = cudaGetLastError();                           \
+        if (e__ != cudaSuccess) return ::gdn::cuda_status(e__, name);   \
+    } while (0)
+
+// Device error word: bit 0 = a bounded wait gave up.  Kernels OR into it and
+// return; gdn_check_device_error reads and clears it.
+enum : uint32_t { DEV_ERR_TIMEOUT = 1u, DEV_ERR_BOUNDS = 2u };
+uint32_t* device_error_word();  // per-device, allocated once on first use
+
+// Spin limit of bounded waits, in SM clock cycles (~1 s at 1.9 GHz).
+constexpr long long kWaitCycles = 2000000000LL;
+
+__device__ __forceinline__ float load_act(const void* p, int dtype, size_t i) {
+    if (dtype == GDN_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    if (dtype == GDN_DTYPE_F16) return __half2float(static_cast<const __half*>(p)[i]);
+    return static_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ float fp16_bits_to_float(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace gdn

@@ -1,0 +1,372 @@
+// GGUF Q8_0 / Q4_K kernels on CUDA cores: repack, bit-exact dequant, and the
+// dequant-in-registers GEMV used for small activation batches (decode B=1..63,
+// the Q4_K projection sweep).  The tensor-core path for large batches lives in
+// gemm_tc.cu.
+//
+// Reference semantics:
+//   Q8_0 block {fp16 d; int8 qs[32]}          engine/runtime/q8_dequant.h:15-18
+//   Q8_0 dequant w = d*q                       engine/runtime/q8_dequant.h:116-126
+//   Q8_0 GEMV, fp32 activations                engine/runtime/gpu_offload.cu:152-199
+//   Q4_K block {d; dmin; scales[12]; qs[128]}  engine/runtime/q4k_dequant.h:28-33
+//   Q4_K scale/min decode                      engine/runtime/gpu_offload.cu:90-98
+//   Q4_K dequant (d*sc)*q - dmin*m, GGML nibble layout
+//                                              engine/runtime/gpu_offload.cu:237-250
+#include "gdn_common.cuh"
+#include "quant.cuh"
+
+namespace gdn {
+
+// ------------------------------------------------------------------ helpers
+
+// float(q) for the four signed bytes of `w`: sets each byte (biased by 128) as
+// the low mantissa bits of 2^23 and subtracts 2^23+128.  Exact.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float f[4]) {
+    const uint32_t u = w ^ 0x80808080u;
+    f[0] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
+    f[1] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
+    f[2] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
+    f[3] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+}
+
+// float of the 4-bit values 0..15 in the low nibbles of the four bytes of `w`.
+__device__ __forceinline__ void u4x4_to_f32(uint32_t w, float f[4]) {
+    const uint32_t u = w & 0x0F0F0F0Fu;
+    f[0] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388608.0f;
+    f[1] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388608.0f;
+    f[2] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388608.0f;
+    f[3] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388608.0f;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ------------------------------------------------------------ Q8_0 planes
+
+__global__ void q8_0_repack_kernel(const uint8_t* __restrict__ blocks, int8_t* __restrict__ qs,
+                                   uint16_t* __restrict__ d, int64_t nblocks) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    const uint8_t* b = blocks + i * 34;
+    d[i] = (uint16_t)(b[0] | (b[1] << 8));
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        w[j] = (uint32_t)b[2 + 4 * j] | ((uint32_t)b[3 + 4 * j] << 8) | ((uint32_t)b[4 + 4 * j] << 16) |
+               ((uint32_t)b[5 + 4 * j] << 24);
+    uint4* dst = reinterpret_cast<uint4*>(qs + i * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// One thread per 16 weights.  out = float(d) * float(q), a single rounding,
+// as q8_dequant_row computes it.
+__global__ void q8_0_dequant_kernel(const int8_t* __restrict__ qs, const uint16_t* __restrict__ d,
+                                    float* __restrict__ out, int64_t n16) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n16) return;
+    const uint4 q = reinterpret_cast<const uint4*>(qs)[i];
+    const float s = fp16_bits_to_float(d[i >> 1]);
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+    float4* o = reinterpret_cast<float4*>(out + i * 16);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float f[4];
+        i8x4_to_f32(qw[j], f);
+        o[j] = make_float4(__fmul_rn(s, f[0]), __fmul_rn(s, f[1]), __fmul_rn(s, f[2]), __fmul_rn(s, f[3]));
+    }
+}
+
+// Activation rows staged in shared memory as fp32: xs[m][k].
+__device__ __forceinline__ void stage_x(float* xs, const void* x, int dtype, int64_t m0, int mb,
+                                        int64_t k) {
+    const int64_t n = (int64_t)mb * k;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) xs[i] = load_act(x, dtype, m0 * k + i);
+}
+
+// Q8_0 GEMV: each warp owns one weight row at a time; lane l reads the 16-byte
+// chunks l, l+32, ... of the row's int8 plane (coalesced 512 B per warp load)
+// and the fp16 scale of the 32-block each chunk belongs to.  The block sum
+// sum(q*x) is scaled by d once per 16-chunk.  MB activation rows share every
+// weight load.
+template <int MB>
+__global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict__ qs,
+                                                       const uint16_t* __restrict__ dsc,
+                                                       int64_t n_rows, int64_t k, const void* x,
+                                                       int x_dtype, int64_t m0, int mb,
+                                                       float* __restrict__ y, int rows_per_block) {
+    extern __shared__ float xs[];
+    stage_x(xs, x, x_dtype, m0, mb, k);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int64_t nchunk = k >> 4;
+    const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
+    for (int64_t r = row0 + warp; r < row0 + rows_per_block && r < n_rows; r += nwarps) {
+        const uint4* qrow = reinterpret_cast<const uint4*>(qs + r * k);
+        const uint16_t* drow = dsc + r * (k >> 5);
+        float acc[MB];
+#pragma unroll
+        for (int m = 0; m < MB; m++) acc[m] = 0.0f;
+        for (int64_t c = lane; c < nchunk; c += 32) {
+            const uint4 q = __ldg(qrow + c);
+            const float s = fp16_bits_to_float(__ldg(drow + (c >> 1)));
+            float f[16];
+            i8x4_to_f32(q.x, f);
+            i8x4_to_f32(q.y, f + 4);
+            i8x4_to_f32(q.z, f + 8);
+            i8x4_to_f32(q.w, f + 12);
+#pragma unroll
+            for (int m = 0; m < MB; m++) {
+                if (m < mb) {
+                    const float4* xv = reinterpret_cast<const float4*>(xs + (int64_t)m * k + c * 16);
+                    float bs = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const float4 v = xv[j];
+                        bs = fmaf(f[4 * j + 0], v.x, bs);
+                        bs = fmaf(f[4 * j + 1], v.y, bs);
+                        bs = fmaf(f[4 * j + 2], v.z, bs);
+                        bs = fmaf(f[4 * j + 3], v.w, bs);
+                    }
+                    acc[m] = fmaf(s, bs, acc[m]);
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MB; m++) {
+            if (m < mb) {
+                const float v = warp_sum(acc[m]);
+                if (lane == 0) y[(m0 + m) * n_rows + r] = v;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------- Q4_K
+
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* sc, int& s, int& m) {
+    if (j < 4) {
+        s = sc[j] & 63;
+        m = sc[j + 4] & 63;
+    } else {
+        s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+}
+
+// One thread per (superblock, chunk c, 16-byte half): 32 weights out.
+__global__ void q4_k_dequant_kernel(const uint8_t* __restrict__ blocks, float* __restrict__ out,
+                                    int64_t nsb) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nsb * 8) return;
+    const int64_t sb = t >> 3;
+    const int c = (int)(t & 7) >> 1, half = (int)(t & 1);
+    const uint8_t* blk = blocks + sb * 144;
+    const float d = fp16_bits_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+    const float dmin = fp16_bits_to_float((uint16_t)(blk[2] | (blk[3] << 8)));
+    int s_lo, m_lo, s_hi, m_hi;
+    q4k_scale_min(2 * c, blk + 4, s_lo, m_lo);
+    q4k_scale_min(2 * c + 1, blk + 4, s_hi, m_hi);
+    const float sl = __fmul_rn(d, (float)s_lo), ml = __fmul_rn(dmin, (float)m_lo);
+    const float sh = __fmul_rn(d, (float)s_hi), mh = __fmul_rn(dmin, (float)m_hi);
+    const uint4 q = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c + 16 * half);
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+    float* o_lo = out + sb * 256 + 64 * c + 16 * half;
+    float* o_hi = o_lo + 32;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float lo[4], hi[4];
+        u4x4_to_f32(qw[j], lo);
+        u4x4_to_f32(qw[j] >> 4, hi);
+        reinterpret_cast<float4*>(o_lo)[j] =
+            make_float4(__fsub_rn(__fmul_rn(sl, lo[0]), ml), __fsub_rn(__fmul_rn(sl, lo[1]), ml),
+                        __fsub_rn(__fmul_rn(sl, lo[2]), ml), __fsub_rn(__fmul_rn(sl, lo[3]), ml));
+        reinterpret_cast<float4*>(o_hi)[j] =
+            make_float4(__fsub_rn(__fmul_rn(sh, hi[0]), mh), __fsub_rn(__fmul_rn(sh, hi[1]), mh),
+                        __fsub_rn(__fmul_rn(sh, hi[2]), mh), __fsub_rn(__fmul_rn(sh, hi[3]), mh));
+    }
+}
+
+// Q4_K GEMV.  Lane l of a warp covers superblock (iter*4 + l/8) of the row and
+// the 16 qs bytes (l%8)*16.. of it, i.e. chunk c = (l%8)/2, bytes j0 = 16*(l%2).
+// With the sums of x over each 16-group precomputed (xsum16), a sub-block's
+// contribution is sc*sum(q*x) - m*sum(x): one FMA per weight and activation row.
+template <int MB>
+__global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restrict__ blocks,
+                                                       int64_t n_rows, int64_t k, const void* x,
+                                                       int x_dtype, int64_t m0, int mb,
+                                                       float* __restrict__ y, int rows_per_block) {
+    extern __shared__ float xs[];  // [mb][k] then xsum16 [mb][k/16]
+    float* xsum = xs + (int64_t)mb * k;
+    stage_x(xs, x, x_dtype, m0, mb, k);
+    __syncthreads();
+    const int64_t ng = k >> 4;
+    for (int64_t i = threadIdx.x; i < (int64_t)mb * ng; i += blockDim.x) {
+        const float* p = xs + i * 16;
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; j++) s += p[j];
+        xsum[i] = s;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int64_t nsb = k >> 8;
+    const int sub = lane >> 3, c = (lane & 7) >> 1, half = lane & 1;
+    const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
+    for (int64_t r = row0 + warp; r < row0 + rows_per_block && r < n_rows; r += nwarps) {
+        const uint8_t* row = blocks + r * nsb * 144;
+        float acc[MB];
+#pragma unroll
+        for (int m = 0; m < MB; m++) acc[m] = 0.0f;
+        for (int64_t sb = sub; sb < nsb; sb += 4) {
+            const uint8_t* blk = row + sb * 144;
+            const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * c + 16 * half));
+            const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
+            const float d = fp16_bits_to_float((uint16_t)(hdr.x & 0xFFFFu));
+            const float dmin = fp16_bits_to_float((uint16_t)(hdr.x >> 16));
+            int s_lo, m_lo, s_hi, m_hi;
+            q4k_scale_min(2 * c, hb + 4, s_lo, m_lo);
+            q4k_scale_min(2 * c + 1, hb + 4, s_hi, m_hi);
+            const float sl = d * (float)s_lo, ml = dmin * (float)m_lo;
+            const float sh = d * (float)s_hi, mh = dmin * (float)m_hi;
+            float lo[16], hi[16];
+            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                u4x4_to_f32(qw[j], lo + 4 * j);
+                u4x4_to_f32(qw[j] >> 4, hi + 4 * j);
+            }
+            const int64_t klo = sb * 256 + 64 * c + 16 * half;
+#pragma unroll
+            for (int m = 0; m < MB; m++) {
+                if (m < mb) {
+                    const float* xl = xs + (int64_t)m * k + klo;
+                    const float* xh = xl + 32;
+                    float al = 0.0f, ah = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        al = fmaf(lo[j], xl[j], al);
+                        ah = fmaf(hi[j], xh[j], ah);
+                    }
+                    const float sxl = xsum[(int64_t)m * ng + (klo >> 4)];
+                    const float sxh = xsum[(int64_t)m * ng + (klo >> 4) + 2];
+                    acc[m] += (sl * al - ml * sxl) + (sh * ah - mh * sxh);
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MB; m++) {
+            if (m < mb) {
+                const float v = warp_sum(acc[m]);
+                if (lane == 0) y[(m0 + m) * n_rows + r] = v;
+            }
+        }
+    }
+}
+
+// -------------------------------------------------------------- launchers
+
+static int smem_optin(const void* fn, size_t bytes) {
+    if (bytes <= 48 * 1024) return GDN_OK;
+    GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    return GDN_OK;
+}
+
+int launch_q8_0_repack(const void* blocks, int8_t* qs, uint16_t* d, int64_t rows, int64_t cols,
+                       cudaStream_t s) {
+    const int64_t nb = rows * (cols / 32);
+    if (nb == 0) return GDN_OK;
+    q8_0_repack_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t*>(blocks), qs,
+                                                                     d, nb);
+    GDN_LAUNCH_CHECK("q8_0_repack_kernel");
+    return GDN_OK;
+}
+
+int launch_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t rows, int64_t cols,
+                        cudaStream_t s) {
+    const int64_t n16 = rows * cols / 16;
+    if (n16 == 0) return GDN_OK;
+    q8_0_dequant_kernel<<<(unsigned)((n16 + 255) / 256), 256, 0, s>>>(qs, d, out, n16);
+    GDN_LAUNCH_CHECK("q8_0_dequant_kernel");
+    return GDN_OK;
+}
+
+// Activation rows per pass, chosen so that the staged rows fit in shared memory.
+static int gemv_rows_per_pass(int64_t m, int64_t k, int per_k_floats) {
+    int mb = (int)(m < 8 ? m : 8);
+    while (mb > 1 && (size_t)mb * k * per_k_floats * 4 > 200 * 1024) mb--;
+    return mb;
+}
+
+template <int MB>
+static int run_q8_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
+                       int64_t m0, int mb, float* y, cudaStream_t s) {
+    const size_t smem = (size_t)mb * k * sizeof(float);
+    int st = smem_optin((const void*)q8_0_gemv_kernel<MB>, smem);
+    if (st) return st;
+    const int rpb = 32;
+    q8_0_gemv_kernel<MB><<<(unsigned)((n + rpb - 1) / rpb), 256, smem, s>>>(qs, d, n, k, x, dt, m0, mb, y, rpb);
+    GDN_LAUNCH_CHECK("q8_0_gemv_kernel");
+    return GDN_OK;
+}
+
+int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
+                     int64_t m, float* y, cudaStream_t s) {
+    const int mbmax = gemv_rows_per_pass(m, k, 1);
+    if ((size_t)k * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q8_0 gemv: k=%lld too large", (long long)k);
+    for (int64_t m0 = 0; m0 < m; m0 += mbmax) {
+        const int mb = (int)((m - m0) < mbmax ? (m - m0) : mbmax);
+        int st;
+        if (mb == 1) st = run_q8_gemv<1>(qs, d, n, k, x, dt, m0, mb, y, s);
+        else if (mb <= 2) st = run_q8_gemv<2>(qs, d, n, k, x, dt, m0, mb, y, s);
+        else if (mb <= 4) st = run_q8_gemv<4>(qs, d, n, k, x, dt, m0, mb, y, s);
+        else st = run_q8_gemv<8>(qs, d, n, k, x, dt, m0, mb, y, s);
+        if (st) return st;
+    }
+    return GDN_OK;
+}
+
+int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s) {
+    const int64_t nsb = rows * cols / 256;
+    if (nsb == 0) return GDN_OK;
+    q4_k_dequant_kernel<<<(unsigned)((nsb * 8 + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t*>(blocks),
+                                                                         out, nsb);
+    GDN_LAUNCH_CHECK("q4_k_dequant_kernel");
+    return GDN_OK;
+}
+
+template <int MB>
+static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m0, int mb,
+                       float* y, cudaStream_t s) {
+    const size_t smem = (size_t)mb * (k + k / 16) * sizeof(float);
+    int st = smem_optin((const void*)q4_k_gemv_kernel<MB>, smem);
+    if (st) return st;
+    const int rpb = 32;
+    q4_k_gemv_kernel<MB><<<(unsigned)((n + rpb - 1) / rpb), 256, smem, s>>>(
+        static_cast<const uint8_t*>(w), n, k, x, dt, m0, mb, y, rpb);
+    GDN_LAUNCH_CHECK("q4_k_gemv_kernel");
+    return GDN_OK;
+}
+
+int launch_q4_k_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
+                     cudaStream_t s) {
+    if ((size_t)(k + k / 16) * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q4_k gemv: k=%lld too large", (long long)k);
+    const int mbmax = gemv_rows_per_pass(m, k + k / 16, 1);
+    for (int64_t m0 = 0; m0 < m; m0 += mbmax) {
+        const int mb = (int)((m - m0) < mbmax ? (m - m0) : mbmax);
+        int st;
+        if (mb == 1) st = run_q4_gemv<1>(w, n, k, x, dt, m0, mb, y, s);
+        else if (mb <= 2) st = run_q4_gemv<2>(w, n, k, x, dt, m0, mb, y, s);
+        else if (mb <= 4) st = run_q4_gemv<4>(w, n, k, x, dt, m0, mb, y, s);
+        else st = run_q4_gemv<8>(w, n, k, x, dt, m0, mb, y, s);
+        if (st) return st;
+    }
+    return GDN_OK;
+}
+
+}  // namespace gdn
