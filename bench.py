@@ -288,7 +288,8 @@ def run_ours(args):
                    "l2": "inputs larger than L2: 512 MiB of state read+written per step"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": B * cfg.hidden * 2,
                 "d2h_bytes_per_step": B * cfg.hidden * 4},
-        "gpu_launches": 5 * K,
+        # per step: in_proj (tcgen05) + gate-row GEMV + state + conv_pos bump + out_proj (tcgen05) + split-K sum
+        "gpu_launches": 6 * K,
         "roofline": {"bound": "hbm", "kernel": "gdn_state_kernel", "achieved": achieved, "peak": hbm_peak,
                      "unit": "GB/s", "frac": achieved / hbm_peak, "peak_source": peak_src,
                      "traffic": NCU_STATE_TRAFFIC, "algorithmic_bytes_per_launch": sk_bytes,

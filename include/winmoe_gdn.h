@@ -95,19 +95,26 @@ GDN_API int gdn_q8_0_repack(const void* blocks, int8_t* qs, uint16_t* d,
 GDN_API int gdn_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out,
                      int64_t rows, int64_t cols, void* stream);
 
+/* Precision flags of gdn_q8_0_gemm. */
+enum {
+    GDN_GEMM_EXACT = 0, /* fp32-GEMV accuracy (the reference's fp32-activation projection) */
+    GDN_GEMM_FAST = 1   /* tensor cores with one fp16/bf16 weight operand */
+};
+
 /*
  * y[m][n] = sum_k x[m][k] * W[n][k] with W Q8_0 planes [n_rows][k].
- * The quant_matvec of engine/runtime/transformer.h:157-194 (type 8), for a
- * batch of m activation rows, with fp32 accumulation of fp32 activations
- * (the semantics of q8_matvec_kernel, engine/runtime/gpu_offload.cu:152-199).
- * x_dtype: GDN_DTYPE_F32 or GDN_DTYPE_BF16.  k % 32 == 0.
- * Dequantises in registers (CUDA cores) for small m; for m >= 64 and
- * k % 64 == 0 it runs the tcgen05 tensor-core kernel with fp16 operands
- * (weights rounded once to fp16, activations converted to fp16) and fp32
- * accumulation in TMEM.
+ * The quant_matvec of engine/runtime/transformer.h:157-194 (type 8) for a
+ * batch of m activation rows (the reference computes one row per call, with
+ * fp32 activations on its GPU route: q8_matvec_kernel,
+ * engine/runtime/gpu_offload.cu:152-199).  x_dtype: F32, BF16 or F16; k % 32 == 0.
+ * Small m, or fp32 x: CUDA cores, dequantising in registers, fp32 math.
+ * m >= 64 with fp16/bf16 x and k % 64 == 0: tcgen05 tensor cores, fp32
+ * accumulation in TMEM; GDN_GEMM_EXACT splits each weight into hi + lo
+ * operands (two MMAs) so that only the summation order differs from fp32,
+ * GDN_GEMM_FAST uses one operand (weights rounded once to the x type).
  */
 GDN_API int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k,
-                  const void* x, int x_dtype, int64_t m, float* y, void* stream);
+                  const void* x, int x_dtype, int64_t m, float* y, int flags, void* stream);
 
 /*
  * Q4_K: GGUF superblocks of 256 weights, {fp16 d; fp16 dmin; u8 scales[12];

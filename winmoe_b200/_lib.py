@@ -20,6 +20,7 @@ STATUS_NAMES = {
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 GGML_F32, GGML_Q8_0, GGML_Q4_K = 0, 8, 12
 HEAD_MAP_GROUPED, HEAD_MAP_INTERLEAVED = 0, 1
+GEMM_EXACT, GEMM_FAST = 0, 1
 
 
 class GDNError(RuntimeError):
@@ -53,7 +54,7 @@ SIGNATURES = {
     "gdn_check_device_error": (_int, [_vp]),
     "gdn_q8_0_repack": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "gdn_q8_0_dequant": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
-    "gdn_q8_0_gemm": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _i64, _vp, _vp]),
+    "gdn_q8_0_gemm": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _i64, _vp, _int, _vp]),
     "gdn_q4_k_dequant": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "gdn_q4_k_gemm": (_int, [_vp, _i64, _i64, _vp, _int, _i64, _vp, _vp]),
     "gdn_decode_workspace_size": (_sz, [C.POINTER(gdn_dims), _i64]),

@@ -84,7 +84,7 @@ int gdn_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t ro
 }
 
 int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k, const void* x, int x_dtype,
-                  int64_t m, float* y, void* stream) {
+                  int64_t m, float* y, int flags, void* stream) {
     if (n_rows < 0 || m < 0 || k <= 0 || k % 32 != 0) return fail(GDN_ERR_SHAPE, "q8_0 gemm: k must be a positive multiple of 32");
     if (!qs || !d || !x || !y) return fail(GDN_ERR_ARG, "q8_0 gemm: NULL pointer");
     int st = check_act_dtype(x_dtype);
@@ -92,9 +92,13 @@ int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k
     if (!aligned(qs, 16)) return fail(GDN_ERR_ARG, "q8_0 gemm: qs must be 16-byte aligned");
     if (n_rows == 0 || m == 0) return GDN_OK;
     cudaStream_t s = as_stream(stream);
-    if (m >= 64 && k % 64 == 0 && x_dtype == GDN_DTYPE_F16 && aligned(x, 16))
-        return launch_q8_0_gemm_tc(qs, d, n_rows, k, static_cast<const __half*>(x), m, y, s);
-    return launch_q8_0_gemv(qs, d, n_rows, k, x, x_dtype, m, y, s);
+    if (flags != GDN_GEMM_EXACT && flags != GDN_GEMM_FAST) return fail(GDN_ERR_ARG, "q8_0 gemm: unknown flags %d", flags);
+    if (m >= 64 && k % 64 == 0 && x_dtype != GDN_DTYPE_F32 && aligned(x, 16) && aligned(d, 4)) {
+        TcOptions opt;
+        opt.split_precision = (flags == GDN_GEMM_EXACT);
+        return launch_q8_0_gemm_tc(qs, d, n_rows, k, x, x_dtype == GDN_DTYPE_BF16, m, y, n_rows, opt, s);
+    }
+    return launch_q8_0_gemv(qs, d, n_rows, k, x, x_dtype, m, y, n_rows, s);
 }
 
 int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, void* stream) {
@@ -112,7 +116,7 @@ int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, 
     if (st) return st;
     if (!aligned(blocks, 16)) return fail(GDN_ERR_ARG, "q4_k gemm: blocks must be 16-byte aligned");
     if (n_rows == 0 || m == 0) return GDN_OK;
-    return launch_q4_k_gemv(blocks, n_rows, k, x, x_dtype, m, y, as_stream(stream));
+    return launch_q4_k_gemv(blocks, n_rows, k, x, x_dtype, m, y, n_rows, as_stream(stream));
 }
 
 size_t gdn_decode_workspace_size(const gdn_dims* dims, int64_t batch) {

@@ -130,10 +130,10 @@ int launch_qkv_gate(int layer, int si, const float* normed, int hidden, int qkv_
     GDN_CUDA(cudaMemcpyAsync(s.d_normed, s.h_normed, sizeof(float) * hidden, cudaMemcpyHostToDevice, g.h2d));
     GDN_CUDA(cudaEventRecord(s.ev_h2d_normed, g.h2d));
     GDN_CUDA(cudaStreamWaitEvent(g.compute, s.ev_h2d_normed, 0));
-    if ((st = launch_q8_0_gemv(L.qkv.qs, L.qkv.d, qkv_dim, hidden, s.d_normed, GDN_DTYPE_F32, 1, s.d_qkv, g.compute)))
+    if ((st = launch_q8_0_gemv(L.qkv.qs, L.qkv.d, qkv_dim, hidden, s.d_normed, GDN_DTYPE_F32, 1, s.d_qkv, qkv_dim, g.compute)))
         return st;
     if ((st = launch_q8_0_gemv(L.gate.qs, L.gate.d, gate_dim, hidden, s.d_normed, GDN_DTYPE_F32, 1, s.d_gate,
-                               g.compute)))
+                               gate_dim, g.compute)))
         return st;
     GDN_CUDA(cudaEventRecord(s.ev_qkv_gate, g.compute));
     GDN_CUDA(cudaStreamWaitEvent(g.d2h, s.ev_qkv_gate, 0));
@@ -159,7 +159,7 @@ int launch_ssm_out(int layer, int si, const float* gated, int gated_dim, int out
     GDN_CUDA(cudaEventRecord(s.ev_h2d_gated, g.h2d));
     GDN_CUDA(cudaStreamWaitEvent(g.compute, s.ev_h2d_gated, 0));
     if ((st = launch_q8_0_gemv(L.out.qs, L.out.d, out_dim, gated_dim, s.d_gated, GDN_DTYPE_F32, 1, s.d_ssm,
-                               g.compute)))
+                               out_dim, g.compute)))
         return st;
     GDN_CUDA(cudaEventRecord(s.ev_ssm, g.compute));
     GDN_CUDA(cudaStreamWaitEvent(g.d2h, s.ev_ssm, 0));

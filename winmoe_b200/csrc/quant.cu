@@ -89,15 +89,17 @@ __device__ __forceinline__ void stage_x(float* xs, const void* x, int dtype, int
 // Q8_0 GEMV: each warp owns one weight row at a time; lane l reads the 16-byte
 // chunks l, l+32, ... of the row's int8 plane (coalesced 512 B per warp load)
 // and the fp16 scale of the 32-block each chunk belongs to.  The block sum
-// sum(q*x) is scaled by d once per 16-chunk.  MB activation rows share every
-// weight load.
+// sum(q*x) is scaled by d once per 16-chunk.  The MB activation rows of block
+// row blockIdx.y share every weight load.
 template <int MB>
 __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict__ qs,
                                                        const uint16_t* __restrict__ dsc,
                                                        int64_t n_rows, int64_t k, const void* x,
-                                                       int x_dtype, int64_t m0, int mb,
-                                                       float* __restrict__ y, int rows_per_block) {
+                                                       int x_dtype, int64_t m, float* __restrict__ y,
+                                                       int64_t ldy, int rows_per_block) {
     extern __shared__ float xs[];
+    const int64_t m0 = (int64_t)blockIdx.y * MB;
+    const int mb = (int)min((int64_t)MB, m - m0);
     stage_x(xs, x, x_dtype, m0, mb, k);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
         const uint16_t* drow = dsc + r * (k >> 5);
         float acc[MB];
 #pragma unroll
-        for (int m = 0; m < MB; m++) acc[m] = 0.0f;
+        for (int j = 0; j < MB; j++) acc[j] = 0.0f;
         for (int64_t c = lane; c < nchunk; c += 32) {
             const uint4 q = __ldg(qrow + c);
             const float s = fp16_bits_to_float(__ldg(drow + (c >> 1)));
@@ -119,27 +121,27 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
             i8x4_to_f32(q.z, f + 8);
             i8x4_to_f32(q.w, f + 12);
 #pragma unroll
-            for (int m = 0; m < MB; m++) {
-                if (m < mb) {
-                    const float4* xv = reinterpret_cast<const float4*>(xs + (int64_t)m * k + c * 16);
+            for (int j = 0; j < MB; j++) {
+                if (j < mb) {
+                    const float4* xv = reinterpret_cast<const float4*>(xs + (int64_t)j * k + c * 16);
                     float bs = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const float4 v = xv[j];
-                        bs = fmaf(f[4 * j + 0], v.x, bs);
-                        bs = fmaf(f[4 * j + 1], v.y, bs);
-                        bs = fmaf(f[4 * j + 2], v.z, bs);
-                        bs = fmaf(f[4 * j + 3], v.w, bs);
+                    for (int e = 0; e < 4; e++) {
+                        const float4 v = xv[e];
+                        bs = fmaf(f[4 * e + 0], v.x, bs);
+                        bs = fmaf(f[4 * e + 1], v.y, bs);
+                        bs = fmaf(f[4 * e + 2], v.z, bs);
+                        bs = fmaf(f[4 * e + 3], v.w, bs);
                     }
-                    acc[m] = fmaf(s, bs, acc[m]);
+                    acc[j] = fmaf(s, bs, acc[j]);
                 }
             }
         }
 #pragma unroll
-        for (int m = 0; m < MB; m++) {
-            if (m < mb) {
-                const float v = warp_sum(acc[m]);
-                if (lane == 0) y[(m0 + m) * n_rows + r] = v;
+        for (int j = 0; j < MB; j++) {
+            if (j < mb) {
+                const float v = warp_sum(acc[j]);
+                if (lane == 0) y[(m0 + j) * ldy + r] = v;
             }
         }
     }
@@ -197,9 +199,11 @@ __global__ void q4_k_dequant_kernel(const uint8_t* __restrict__ blocks, float* _
 template <int MB>
 __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restrict__ blocks,
                                                        int64_t n_rows, int64_t k, const void* x,
-                                                       int x_dtype, int64_t m0, int mb,
-                                                       float* __restrict__ y, int rows_per_block) {
+                                                       int x_dtype, int64_t m, float* __restrict__ y,
+                                                       int64_t ldy, int rows_per_block) {
     extern __shared__ float xs[];  // [mb][k] then xsum16 [mb][k/16]
+    const int64_t m0 = (int64_t)blockIdx.y * MB;
+    const int mb = (int)min((int64_t)MB, m - m0);
     float* xsum = xs + (int64_t)mb * k;
     stage_x(xs, x, x_dtype, m0, mb, k);
     __syncthreads();
@@ -221,7 +225,7 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
         const uint8_t* row = blocks + r * nsb * 144;
         float acc[MB];
 #pragma unroll
-        for (int m = 0; m < MB; m++) acc[m] = 0.0f;
+        for (int j = 0; j < MB; j++) acc[j] = 0.0f;
         for (int64_t sb = sub; sb < nsb; sb += 4) {
             const uint8_t* blk = row + sb * 144;
             const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
@@ -243,27 +247,27 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
             }
             const int64_t klo = sb * 256 + 64 * c + 16 * half;
 #pragma unroll
-            for (int m = 0; m < MB; m++) {
-                if (m < mb) {
-                    const float* xl = xs + (int64_t)m * k + klo;
+            for (int j = 0; j < MB; j++) {
+                if (j < mb) {
+                    const float* xl = xs + (int64_t)j * k + klo;
                     const float* xh = xl + 32;
                     float al = 0.0f, ah = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        al = fmaf(lo[j], xl[j], al);
-                        ah = fmaf(hi[j], xh[j], ah);
+                    for (int e = 0; e < 16; e++) {
+                        al = fmaf(lo[e], xl[e], al);
+                        ah = fmaf(hi[e], xh[e], ah);
                     }
-                    const float sxl = xsum[(int64_t)m * ng + (klo >> 4)];
-                    const float sxh = xsum[(int64_t)m * ng + (klo >> 4) + 2];
-                    acc[m] += (sl * al - ml * sxl) + (sh * ah - mh * sxh);
+                    const float sxl = xsum[(int64_t)j * ng + (klo >> 4)];
+                    const float sxh = xsum[(int64_t)j * ng + (klo >> 4) + 2];
+                    acc[j] += (sl * al - ml * sxl) + (sh * ah - mh * sxh);
                 }
             }
         }
 #pragma unroll
-        for (int m = 0; m < MB; m++) {
-            if (m < mb) {
-                const float v = warp_sum(acc[m]);
-                if (lane == 0) y[(m0 + m) * n_rows + r] = v;
+        for (int j = 0; j < MB; j++) {
+            if (j < mb) {
+                const float v = warp_sum(acc[j]);
+                if (lane == 0) y[(m0 + j) * ldy + r] = v;
             }
         }
     }
@@ -296,39 +300,38 @@ int launch_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t
     return GDN_OK;
 }
 
-// Activation rows per pass, chosen so that the staged rows fit in shared memory.
-static int gemv_rows_per_pass(int64_t m, int64_t k, int per_k_floats) {
-    int mb = (int)(m < 8 ? m : 8);
-    while (mb > 1 && (size_t)mb * k * per_k_floats * 4 > 200 * 1024) mb--;
+// Activation rows per block (a template size: 1, 2, 4 or 8): the smallest one
+// that covers min(m, 8) rows, halved while the staged rows overflow shared memory.
+static int pick_mb(int64_t m, int64_t floats_per_row) {
+    int mb = m >= 5 ? 8 : m >= 3 ? 4 : m >= 2 ? 2 : 1;
+    while (mb > 1 && (size_t)mb * floats_per_row * 4 > 200 * 1024) mb >>= 1;
     return mb;
 }
 
 template <int MB>
 static int run_q8_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
-                       int64_t m0, int mb, float* y, cudaStream_t s) {
-    const size_t smem = (size_t)mb * k * sizeof(float);
+                       int64_t m, float* y, int64_t ldy, cudaStream_t s) {
+    const size_t smem = (size_t)MB * k * sizeof(float);
     int st = smem_optin((const void*)q8_0_gemv_kernel<MB>, smem);
     if (st) return st;
     const int rpb = 32;
-    q8_0_gemv_kernel<MB><<<(unsigned)((n + rpb - 1) / rpb), 256, smem, s>>>(qs, d, n, k, x, dt, m0, mb, y, rpb);
+    const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
+    q8_0_gemv_kernel<MB><<<grid, 256, smem, s>>>(qs, d, n, k, x, dt, m, y, ldy, rpb);
     GDN_LAUNCH_CHECK("q8_0_gemv_kernel");
     return GDN_OK;
 }
 
 int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
-                     int64_t m, float* y, cudaStream_t s) {
-    const int mbmax = gemv_rows_per_pass(m, k, 1);
+                     int64_t m, float* y, int64_t ldy, cudaStream_t s) {
     if ((size_t)k * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q8_0 gemv: k=%lld too large", (long long)k);
-    for (int64_t m0 = 0; m0 < m; m0 += mbmax) {
-        const int mb = (int)((m - m0) < mbmax ? (m - m0) : mbmax);
-        int st;
-        if (mb == 1) st = run_q8_gemv<1>(qs, d, n, k, x, dt, m0, mb, y, s);
-        else if (mb <= 2) st = run_q8_gemv<2>(qs, d, n, k, x, dt, m0, mb, y, s);
-        else if (mb <= 4) st = run_q8_gemv<4>(qs, d, n, k, x, dt, m0, mb, y, s);
-        else st = run_q8_gemv<8>(qs, d, n, k, x, dt, m0, mb, y, s);
-        if (st) return st;
+    if (m <= 0 || n <= 0) return GDN_OK;
+    if ((m + 7) / 8 > 65535) return fail(GDN_ERR_SHAPE, "q8_0 gemv: m=%lld too large", (long long)m);
+    switch (pick_mb(m, k)) {
+        case 1: return run_q8_gemv<1>(qs, d, n, k, x, dt, m, y, ldy, s);
+        case 2: return run_q8_gemv<2>(qs, d, n, k, x, dt, m, y, ldy, s);
+        case 4: return run_q8_gemv<4>(qs, d, n, k, x, dt, m, y, ldy, s);
+        default: return run_q8_gemv<8>(qs, d, n, k, x, dt, m, y, ldy, s);
     }
-    return GDN_OK;
 }
 
 int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s) {
@@ -341,32 +344,29 @@ int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t co
 }
 
 template <int MB>
-static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m0, int mb,
-                       float* y, cudaStream_t s) {
-    const size_t smem = (size_t)mb * (k + k / 16) * sizeof(float);
+static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
+                       int64_t ldy, cudaStream_t s) {
+    const size_t smem = (size_t)MB * (k + k / 16) * sizeof(float);
     int st = smem_optin((const void*)q4_k_gemv_kernel<MB>, smem);
     if (st) return st;
     const int rpb = 32;
-    q4_k_gemv_kernel<MB><<<(unsigned)((n + rpb - 1) / rpb), 256, smem, s>>>(
-        static_cast<const uint8_t*>(w), n, k, x, dt, m0, mb, y, rpb);
+    const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
+    q4_k_gemv_kernel<MB><<<grid, 256, smem, s>>>(static_cast<const uint8_t*>(w), n, k, x, dt, m, y, ldy, rpb);
     GDN_LAUNCH_CHECK("q4_k_gemv_kernel");
     return GDN_OK;
 }
 
 int launch_q4_k_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
-                     cudaStream_t s) {
+                     int64_t ldy, cudaStream_t s) {
     if ((size_t)(k + k / 16) * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q4_k gemv: k=%lld too large", (long long)k);
-    const int mbmax = gemv_rows_per_pass(m, k + k / 16, 1);
-    for (int64_t m0 = 0; m0 < m; m0 += mbmax) {
-        const int mb = (int)((m - m0) < mbmax ? (m - m0) : mbmax);
-        int st;
-        if (mb == 1) st = run_q4_gemv<1>(w, n, k, x, dt, m0, mb, y, s);
-        else if (mb <= 2) st = run_q4_gemv<2>(w, n, k, x, dt, m0, mb, y, s);
-        else if (mb <= 4) st = run_q4_gemv<4>(w, n, k, x, dt, m0, mb, y, s);
-        else st = run_q4_gemv<8>(w, n, k, x, dt, m0, mb, y, s);
-        if (st) return st;
+    if (m <= 0 || n <= 0) return GDN_OK;
+    if ((m + 7) / 8 > 65535) return fail(GDN_ERR_SHAPE, "q4_k gemv: m=%lld too large", (long long)m);
+    switch (pick_mb(m, k + k / 16)) {
+        case 1: return run_q4_gemv<1>(w, n, k, x, dt, m, y, ldy, s);
+        case 2: return run_q4_gemv<2>(w, n, k, x, dt, m, y, ldy, s);
+        case 4: return run_q4_gemv<4>(w, n, k, x, dt, m, y, ldy, s);
+        default: return run_q4_gemv<8>(w, n, k, x, dt, m, y, ldy, s);
     }
-    return GDN_OK;
 }
 
 }  // namespace gdn

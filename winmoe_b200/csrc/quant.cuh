@@ -8,18 +8,27 @@ namespace gdn {
 int launch_q8_0_repack(const void* blocks, int8_t* qs, uint16_t* d, int64_t rows, int64_t cols, cudaStream_t s);
 int launch_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t rows, int64_t cols,
                         cudaStream_t s);
-// y[m][n] = x[m][:] . W[n][:] on CUDA cores, dequantising in registers.
+// y[m][ldy] = x[m][:] . W[n][:] on CUDA cores, dequantising in registers.
 int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int x_dtype,
-                     int64_t m, float* y, cudaStream_t s);
+                     int64_t m, float* y, int64_t ldy, cudaStream_t s);
 int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s);
 int launch_q4_k_gemv(const void* blocks, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
-                     cudaStream_t s);
+                     int64_t ldy, cudaStream_t s);
 
-// Tensor-core (tcgen05) Q8_0 GEMM: y[m][n] = a[m][:] . W[n][:], a fp16
-// [m][k] row-major (k % 64 == 0, 16-byte aligned rows), fp32 out.
-int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const __half* a, int64_t m,
-                        float* y, cudaStream_t s);
-// fp32 / bf16 activations -> fp16 (for the tensor-core operand).
-int launch_to_f16(const void* x, int x_dtype, __half* out, int64_t count, cudaStream_t s);
+// Options of the tensor-core GEMM.
+struct TcOptions {
+    bool split_precision = false;  // weights as hi + lo operands (two MMAs): fp32-GEMV accuracy
+    int splits = 1;                // split-K factor (partials in `workspace`, then a fixed-order sum)
+    void* workspace = nullptr;
+    size_t workspace_bytes = 0;
+};
+size_t gemm_tc_workspace_bytes(int64_t m, int64_t n, int splits);
+
+// Tensor-core (tcgen05) Q8_0 GEMM: y[m][ldy] = a[m][:] . W[n][:], a fp16 or
+// bf16 [m][k] row-major (k % 64 == 0, 16-byte aligned), fp32 out.
+int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* a, bool a_bf16,
+                        int64_t m, float* y, int64_t ldy, const TcOptions& opt, cudaStream_t s);
+// fp32 / bf16 / fp16 activations -> fp16 or bf16 (the tensor-core operand).
+int launch_convert(const void* x, int x_dtype, void* out, bool to_bf16, int64_t count, cudaStream_t s);
 
 }  // namespace gdn

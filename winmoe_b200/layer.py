@@ -203,14 +203,16 @@ def decode_step(w: DeltaNetWeights, state: DeltaNetState, x: torch.Tensor, out: 
 
 
 def gemm_q8_0(qs: torch.Tensor, d: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None,
-              stream=None) -> torch.Tensor:
-    """y[m][n] = x[m] . W[n] for Q8_0 planes (quant_matvec type 8, batched)."""
+              fast: bool = False, stream=None) -> torch.Tensor:
+    """y[m][n] = x[m] . W[n] for Q8_0 planes (quant_matvec type 8, batched).
+    fast=False keeps fp32-GEMV accuracy; fast=True lets m >= 64 fp16/bf16
+    batches use one tensor-core weight operand (weights rounded once)."""
     n, k = qs.shape
     m = x.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=x.device)
     check(lib().gdn_q8_0_gemm(qs.data_ptr(), d.data_ptr(), n, k, x.data_ptr(), _act_dtype(x), m, out.data_ptr(),
-                              _stream(stream, x.device)))
+                              _lib.GEMM_FAST if fast else _lib.GEMM_EXACT, _stream(stream, x.device)))
     return out
 
 
