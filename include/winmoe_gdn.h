@@ -107,11 +107,14 @@ enum {
  * batch of m activation rows (the reference computes one row per call, with
  * fp32 activations on its GPU route: q8_matvec_kernel,
  * engine/runtime/gpu_offload.cu:152-199).  x_dtype: F32, BF16 or F16; k % 32 == 0.
- * Small m, or fp32 x: CUDA cores, dequantising in registers, fp32 math.
- * m >= 64 with fp16/bf16 x and k % 64 == 0: tcgen05 tensor cores, fp32
- * accumulation in TMEM; GDN_GEMM_EXACT splits each weight into hi + lo
- * operands (two MMAs) so that only the summation order differs from fp32,
- * GDN_GEMM_FAST uses one operand (weights rounded once to the x type).
+ * m >= 64, k % 64 == 0, 16-byte aligned x: tcgen05 tensor cores with fp32
+ * accumulation in TMEM --
+ *   GDN_GEMM_EXACT, fp16 x: each weight split into exact hi + lo fp16
+ *     operands (two MMAs), so only the summation order differs from fp32;
+ *   GDN_GEMM_FAST, fp16 or bf16 x: one operand, weights rounded once to the
+ *     x type.
+ * Every other case (small m, fp32 x, bf16 x with EXACT): CUDA cores,
+ * dequantising in registers, fp32 math.
  */
 GDN_API int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k,
                   const void* x, int x_dtype, int64_t m, float* y, int flags, void* stream);

@@ -67,7 +67,8 @@ def test_decode_b1_64_steps(t35, w35):
     assert int(st.conv_pos.cpu()[0]) == int(pos_ref[0]) == 64
 
 
-@pytest.mark.parametrize("B,dtype", [(3, torch.float32), (8, torch.bfloat16), (64, torch.bfloat16)])
+@pytest.mark.parametrize("B,dtype", [(3, torch.float32), (8, torch.bfloat16), (64, torch.bfloat16),
+                                     (64, torch.float32), (96, torch.float16), (130, torch.bfloat16)])
 def test_decode_batched_prefilled(t35, w35, B, dtype):
     """Independent sequences with prefilled states (config 2 style), a few steps."""
     cfg = DIMS_35B

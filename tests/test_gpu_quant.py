@@ -79,7 +79,8 @@ GEMM_SHAPES = [(128, 256, 64), (256, 12352, 2048), (256, 2048, 4096), (200, 300,
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
 @pytest.mark.parametrize("xdt", [torch.float16, torch.bfloat16])
 def test_q8_0_gemm_tensor_core_exact(m, n, k, xdt):
-    """Split-precision weights: the fp32 product of the same activations, up to summation order."""
+    """Exact mode: the fp32 product of the same activations up to summation order
+    (fp16 x: tensor cores with hi + lo weight operands; bf16 x: CUDA cores)."""
     blocks = synth.q8_0_blocks(n, k, seed=500 + n + k)
     qs, d = L.q8_0_planes(blocks, n, k, DEV)
     x = torch.randn(m, k, generator=torch.Generator().manual_seed(m + n + k)).to(xdt).to(DEV)

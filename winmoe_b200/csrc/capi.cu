@@ -41,6 +41,18 @@ uint32_t* device_error_word() {
     return ptrs[dev];
 }
 
+int sm_count() {
+    static int counts[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (counts[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        counts[dev] = n;
+    }
+    return counts[dev];
+}
+
 static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 static int check_act_dtype(int dt) {
@@ -93,7 +105,9 @@ int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k
     if (n_rows == 0 || m == 0) return GDN_OK;
     cudaStream_t s = as_stream(stream);
     if (flags != GDN_GEMM_EXACT && flags != GDN_GEMM_FAST) return fail(GDN_ERR_ARG, "q8_0 gemm: unknown flags %d", flags);
-    if (m >= 64 && k % 64 == 0 && x_dtype != GDN_DTYPE_F32 && aligned(x, 16) && aligned(d, 4)) {
+    const bool tc_shape = m >= 64 && k % 64 == 0 && aligned(x, 16) && aligned(d, 4);
+    const bool tc = tc_shape && (flags == GDN_GEMM_FAST ? x_dtype != GDN_DTYPE_F32 : x_dtype == GDN_DTYPE_F16);
+    if (tc) {
         TcOptions opt;
         opt.split_precision = (flags == GDN_GEMM_EXACT);
         return launch_q8_0_gemm_tc(qs, d, n_rows, k, x, x_dtype == GDN_DTYPE_BF16, m, y, n_rows, opt, s);

@@ -15,7 +15,10 @@
 // CTA per (value head, sequence)), conv_pos_bump, out_proj.
 // The state kernel is the HBM-bound part: every (sequence, value head) owns a
 // 128x128 fp32 state (64 KiB) that is read once and written once per token.
+#include <algorithm>
+
 #include "gdn_common.cuh"
+#include "ptx_sm100.cuh"
 #include "quant.cuh"
 #include "decode.cuh"
 
@@ -25,180 +28,240 @@ constexpr int HD = 128;  // head_dim (the reference's AVX loops assume 128 too)
 
 // ------------------------------------------------------------- state kernel
 //
-// grid (Hv, B), block 256 = 8 warps.
-// Prologue: the state loads are issued first; meanwhile thread t < 128 runs
-// the causal conv1d + SiLU for channel t of q (key group g) and of v (head h),
-// thread t >= 128 for channel t-128 of k.  Window slot p%4 (the oldest, never
-// read this step) receives the raw projection; the q/k slots are written by
-// the first value head of the group only, the v slots by head h.  q and k are
-// L2-normalised (double-precision sums), thread 0 computes the gates.
-// Recurrence: warp w owns state rows [16w, 16w+16), lane l columns
-// [4l, 4l+4): 16 float4 registers per thread, so each warp load/store moves
-// one full 512-byte state row.
-__global__ void __launch_bounds__(256, 2) gdn_state_kernel(
+// Persistent: one CTA (256 threads) per SM walks a contiguous range of tiles
+// tile = ((b * Hk + g) * hpg + u), i.e. (sequence b, value head h = the u-th
+// head of key group g).  The 64 KiB fp32 state of each tile is brought into a
+// kStateBufs-deep shared-memory ring by cp.async.bulk (mbarrier completion), so
+// HBM always has the next tiles' loads in flight while this one is computed;
+// the updated state goes back to HBM with coalesced 16-byte stores straight
+// from registers.
+//
+// Per tile, before waiting on its state:
+//   * when the key group changes: causal conv1d + SiLU of the q and k channels
+//     of group g (thread t < 128: q[t], t >= 128: k[t-128]), L2 norms with
+//     double-precision sums (deltanet_impl.h:85-91, 264-267);
+//   * conv1d + SiLU of v (head h), gates decay/beta of head h (247-261).
+//   Window slot p%4 (the oldest, never read this step) receives the raw
+//   projection: v slots by their head, q/k slots by the group's first head.
+// Recurrence: warp w owns state rows [16w, 16w+16), lane l columns [4l, 4l+4)
+// (16 float4 registers per thread; one warp access = one 512-byte row).
+constexpr int kStateBufs = 3;
+constexpr int kTileFloats = HD * HD;
+constexpr uint32_t kTileBytes = kTileFloats * 4;
+
+struct StateSmem {
+    float S[kStateBufs][kTileFloats];
+    float q[HD], k[HD], v[HD], delta[HD];
+    float red[8][HD];
+    double dred[8];
+    float gate[2];
+    uint64_t full[kStateBufs];
+};
+
+__global__ void __launch_bounds__(256, 1) gdn_state_kernel(
     const float* __restrict__ proj, int64_t np, float* __restrict__ S, float* __restrict__ conv_buf,
     const int32_t* __restrict__ conv_pos, const float* __restrict__ conv_w, const float* __restrict__ ssm_a,
     const float* __restrict__ dt_bias, const float* __restrict__ head_norm, float* __restrict__ gated,
-    __half* __restrict__ gated_h, int qkv, int key_dim, int hv, int hk, int head_map) {
-    const int h = blockIdx.x, b = blockIdx.y;
+    __half* __restrict__ gated_h, int qkv, int key_dim, int hv, int hk, int head_map, int64_t n_tiles,
+    int64_t tiles_per_cta, uint32_t* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    StateSmem& sm = *reinterpret_cast<StateSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     const int t = threadIdx.x, w = t >> 5, l = t & 31;
     const int hpg = hv / hk;
-    const int g = head_map ? (h % hk) : (h / hpg);
-    const bool qk_writer = head_map ? (h < hk) : (h % hpg == 0);
     const int inner = hv * HD;
-
-    __shared__ float sq[HD], sk[HD], sv[HD], sdelta[HD];
-    __shared__ float red[8][HD];
-    __shared__ double dred[8];
-    __shared__ float sgate[2];
-
-    float* Sh = S + ((int64_t)b * hv + h) * HD * HD;
-    const float4* Sv = reinterpret_cast<const float4*>(Sh);
-    float4 s[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) s[i] = Sv[(16 * w + i) * (HD / 4) + l];
-
-    // ---- conv1d + SiLU (deltanet_impl.h:218-236)
-    const float* pr = proj + (int64_t)b * np;
+    const int64_t first = (int64_t)blockIdx.x * tiles_per_cta;
+    const int64_t last = min(first + tiles_per_cta, n_tiles);
+    const int count = (int)max((int64_t)0, last - first);
     const bool conv_on = conv_w != nullptr && conv_buf != nullptr;
-    const int p = conv_on ? conv_pos[b] : 0;
-    float* win = conv_on ? conv_buf + (int64_t)b * 4 * qkv : nullptr;
-    auto conv = [&](int ch, bool write) -> float {
-        const float raw = pr[ch];
-        if (!conv_on) return raw;
-        const float4 wk = reinterpret_cast<const float4*>(conv_w)[ch];
-        const float x0 = win[(int64_t)((p - 3) & 3) * qkv + ch];
-        const float x1 = win[(int64_t)((p - 2) & 3) * qkv + ch];
-        const float x2 = win[(int64_t)((p - 1) & 3) * qkv + ch];
-        if (write) win[(int64_t)(p & 3) * qkv + ch] = raw;
-        float sum = 0.0f;
-        sum = __fadd_rn(sum, __fmul_rn(wk.x, x0));
-        sum = __fadd_rn(sum, __fmul_rn(wk.y, x1));
-        sum = __fadd_rn(sum, __fmul_rn(wk.z, x2));
-        sum = __fadd_rn(sum, __fmul_rn(wk.w, raw));
-        const float sig = 1.0f / (1.0f + expf(-sum));
-        return __fmul_rn(sum, sig);
+
+    auto tile_head = [&](int64_t tile, int64_t& b, int& g, int& u) {
+        u = (int)(tile % hpg);
+        const int64_t bg = tile / hpg;
+        g = (int)(bg % hk);
+        b = bg / hk;
+        return head_map ? (g + u * hk) : (g * hpg + u);
     };
-    float a_qk, a_v = 0.0f;
-    if (t < HD) {
-        a_qk = conv(g * HD + t, qk_writer);
-        a_v = conv(2 * key_dim + h * HD + t, true);
-    } else {
-        a_qk = conv(key_dim + g * HD + (t - HD), qk_writer);
-    }
-    // ---- L2 norm of q (warps 0-3) and k (warps 4-7), deltanet_impl.h:85-91, 264-267
-    double ss = (double)a_qk * (double)a_qk;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (l == 0) dred[w] = ss;
-    // ---- gates (deltanet_impl.h:247-261)
+    auto state_ptr = [&](int64_t tile) {
+        int64_t b;
+        int g, u;
+        const int h = tile_head(tile, b, g, u);
+        return S + (b * hv + h) * (int64_t)kTileFloats;
+    };
+    const uint32_t sbuf0 = sm100::smem_u32(&sm.S[0][0]);
+    auto issue = [&](int i) {  // local tile i -> ring slot i % kStateBufs
+        const int slot = i % kStateBufs;
+        const uint32_t bar = sm100::smem_u32(&sm.full[slot]);
+        sm100::mbar_arrive_expect_tx(bar, kTileBytes);
+        sm100::bulk_load(sbuf0 + slot * kTileBytes, state_ptr(first + i), kTileBytes, bar);
+    };
+
     if (t == 0) {
-        const float beta_raw = pr[qkv + inner + h];
-        const float alpha_raw = pr[qkv + inner + hv + h];
-        float a = 0.99f;
-        if (ssm_a != nullptr && dt_bias != nullptr) {
-            const float x = alpha_raw + dt_bias[h];
-            const float sp = log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f);
-            a = expf(ssm_a[h] * sp);
-        }
-        a = (a > 1.0f) ? 1.0f : a;
-        a = (a < 0.0f) ? 0.0f : a;
-        if (isnan(a)) a = 0.99f;
-        float bt;
-        if (beta_raw >= 0.0f) {
-            bt = 1.0f / (1.0f + expf(-beta_raw));
-        } else {
-            const float z = expf(beta_raw);
-            bt = z / (1.0f + z);
-        }
-        sgate[0] = a;
-        sgate[1] = bt;
+        for (int i = 0; i < kStateBufs; i++) sm100::mbar_init(sm100::smem_u32(&sm.full[i]), 1);
+        sm100::fence_barrier_init();
+        for (int i = 0; i < kStateBufs && i < count; i++) issue(i);
     }
     __syncthreads();
-    {
-        const int base = (t < HD) ? 0 : 4;
-        const double tot = dred[base] + dred[base + 1] + dred[base + 2] + dred[base + 3];
-        const float inv = 1.0f / (sqrtf((float)tot) + 1e-6f);
+
+    int64_t cur_bg = -1;
+    bool ok = true;
+    for (int i = 0; i < count; i++) {
+        const int64_t tile = first + i;
+        int64_t b;
+        int g, u;
+        const int h = tile_head(tile, b, g, u);
+        const float* pr = proj + b * np;
+        const int p = conv_on ? conv_pos[b] : 0;
+        float* win = conv_on ? conv_buf + b * 4 * (int64_t)qkv : nullptr;
+        auto conv = [&](int ch, bool write) -> float {
+            const float raw = pr[ch];
+            if (!conv_on) return raw;
+            const float4 wk = reinterpret_cast<const float4*>(conv_w)[ch];
+            const float x0 = win[(int64_t)((p - 3) & 3) * qkv + ch];
+            const float x1 = win[(int64_t)((p - 2) & 3) * qkv + ch];
+            const float x2 = win[(int64_t)((p - 1) & 3) * qkv + ch];
+            if (write) win[(int64_t)(p & 3) * qkv + ch] = raw;
+            float sum = 0.0f;
+            sum = __fadd_rn(sum, __fmul_rn(wk.x, x0));
+            sum = __fadd_rn(sum, __fmul_rn(wk.y, x1));
+            sum = __fadd_rn(sum, __fmul_rn(wk.z, x2));
+            sum = __fadd_rn(sum, __fmul_rn(wk.w, raw));
+            const float sig = 1.0f / (1.0f + expf(-sum));
+            return __fmul_rn(sum, sig);
+        };
+
+        // ---- q/k of a new key group: conv1d + SiLU + L2 norm (conv 218-236, L2 264-267)
+        const int64_t bg = tile / hpg;
+        const bool new_group = (bg != cur_bg);
+        cur_bg = bg;
+        float a_qk = 0.0f;
+        if (new_group) {
+            a_qk = (t < HD) ? conv(g * HD + t, u == 0) : conv(key_dim + g * HD + (t - HD), u == 0);
+            double ss = (double)a_qk * (double)a_qk;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (l == 0) sm.dred[w] = ss;
+        }
+        // ---- v of head h and its gates (gates 247-261)
+        if (t < HD) sm.v[t] = conv(2 * key_dim + h * HD + t, true);
+        if (t == 0) {
+            const float beta_raw = pr[qkv + inner + h];
+            const float alpha_raw = pr[qkv + inner + hv + h];
+            float a = 0.99f;
+            if (ssm_a != nullptr && dt_bias != nullptr) {
+                const float x = alpha_raw + dt_bias[h];
+                const float sp = log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f);
+                a = expf(ssm_a[h] * sp);
+            }
+            a = (a > 1.0f) ? 1.0f : a;
+            a = (a < 0.0f) ? 0.0f : a;
+            if (isnan(a)) a = 0.99f;
+            float bt;
+            if (beta_raw >= 0.0f) {
+                bt = 1.0f / (1.0f + expf(-beta_raw));
+            } else {
+                const float z = expf(beta_raw);
+                bt = z / (1.0f + z);
+            }
+            sm.gate[0] = a;
+            sm.gate[1] = bt;
+        }
+        __syncthreads();
+        if (new_group) {
+            const int base = (t < HD) ? 0 : 4;
+            const double tot = sm.dred[base] + sm.dred[base + 1] + sm.dred[base + 2] + sm.dred[base + 3];
+            const float inv = 1.0f / (sqrtf((float)tot) + 1e-6f);
+            if (t < HD) sm.q[t] = __fmul_rn(a_qk, inv);
+            else sm.k[t - HD] = __fmul_rn(a_qk, inv);
+        }
+
+        // ---- this tile's state: wait for the ring slot, copy it to registers
+        const int slot = i % kStateBufs;
+        ok = ok && sm100::mbar_wait(sm100::smem_u32(&sm.full[slot]), (uint32_t)((i / kStateBufs) & 1), err);
+        const float4* Sv = reinterpret_cast<const float4*>(&sm.S[slot][0]);
+        float4 s[16];
+#pragma unroll
+        for (int r = 0; r < 16; r++) s[r] = Sv[(16 * w + r) * (HD / 4) + l];
+        __syncthreads();  // slot drained; q/k visible
+        if (t == 0 && ok && i + kStateBufs < count) {  // after a timed-out wait no new copy is issued
+            sm100::fence_proxy_async_smem();
+            issue(i + kStateBufs);
+        }
+        const float dg = sm.gate[0], bt = sm.gate[1];
+
+        // ---- decay + retrieve (deltanet_impl.h:298-307)
+        float4 rp = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < 16; r++) {
+            const float kr = sm.k[16 * w + r];
+            s[r].x = __fmul_rn(s[r].x, dg);
+            s[r].y = __fmul_rn(s[r].y, dg);
+            s[r].z = __fmul_rn(s[r].z, dg);
+            s[r].w = __fmul_rn(s[r].w, dg);
+            rp.x = fmaf(kr, s[r].x, rp.x);
+            rp.y = fmaf(kr, s[r].y, rp.y);
+            rp.z = fmaf(kr, s[r].z, rp.z);
+            rp.w = fmaf(kr, s[r].w, rp.w);
+        }
+        reinterpret_cast<float4*>(sm.red[w])[l] = rp;
+        __syncthreads();
         if (t < HD) {
-            sq[t] = __fmul_rn(a_qk, inv);
-            sv[t] = a_v;
-        } else {
-            sk[t - HD] = __fmul_rn(a_qk, inv);
+            float rr = 0.0f;
+#pragma unroll
+            for (int ww = 0; ww < 8; ww++) rr += sm.red[ww][t];
+            sm.delta[t] = __fmul_rn(bt, __fsub_rn(sm.v[t], rr));  // deltanet_impl.h:311-317
         }
-    }
-    __syncthreads();
-    const float dg = sgate[0], bt = sgate[1];
+        __syncthreads();
 
-    // ---- decay + retrieve (deltanet_impl.h:298-307)
-    float4 rp = make_float4(0.f, 0.f, 0.f, 0.f);
+        // ---- update + output read (deltanet_impl.h:320-347); the state goes back to HBM
+        const float4 dl = reinterpret_cast<const float4*>(sm.delta)[l];
+        float4 op = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4* So = reinterpret_cast<float4*>(state_ptr(tile));
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
-        const float kr = sk[16 * w + i];
-        s[i].x = __fmul_rn(s[i].x, dg);
-        s[i].y = __fmul_rn(s[i].y, dg);
-        s[i].z = __fmul_rn(s[i].z, dg);
-        s[i].w = __fmul_rn(s[i].w, dg);
-        rp.x = fmaf(kr, s[i].x, rp.x);
-        rp.y = fmaf(kr, s[i].y, rp.y);
-        rp.z = fmaf(kr, s[i].z, rp.z);
-        rp.w = fmaf(kr, s[i].w, rp.w);
-    }
-    reinterpret_cast<float4*>(red[w])[l] = rp;
-    __syncthreads();
-    if (t < HD) {
-        float r = 0.0f;
-#pragma unroll
-        for (int ww = 0; ww < 8; ww++) r += red[ww][t];
-        sdelta[t] = __fmul_rn(bt, __fsub_rn(sv[t], r));  // deltanet_impl.h:311-317
-    }
-    __syncthreads();
+        for (int r = 0; r < 16; r++) {
+            const float kr = sm.k[16 * w + r];
+            const float qr = sm.q[16 * w + r];
+            s[r].x = fmaf(kr, dl.x, s[r].x);
+            s[r].y = fmaf(kr, dl.y, s[r].y);
+            s[r].z = fmaf(kr, dl.z, s[r].z);
+            s[r].w = fmaf(kr, dl.w, s[r].w);
+            op.x = fmaf(qr, s[r].x, op.x);
+            op.y = fmaf(qr, s[r].y, op.y);
+            op.z = fmaf(qr, s[r].z, op.z);
+            op.w = fmaf(qr, s[r].w, op.w);
+            So[(16 * w + r) * (HD / 4) + l] = s[r];
+        }
+        __syncthreads();  // every warp is done with red[] and dred[]
+        reinterpret_cast<float4*>(sm.red[w])[l] = op;
+        __syncthreads();
 
-    // ---- update + output read (deltanet_impl.h:320-347)
-    const float4 dl = reinterpret_cast<const float4*>(sdelta)[l];
-    float4 op = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4* So = reinterpret_cast<float4*>(Sh);
+        // ---- output, per-head RMSNorm (deltanet_impl.h:350-361) and SiLU(z) gate (364-371)
+        float o = 0.0f;
+        if (t < HD) {
+            for (int ww = 0; ww < 8; ww++) o += sm.red[ww][t];
+            o = __fmul_rn(o, 1.0f / sqrtf((float)HD));
+            double so = (double)o * (double)o;
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
-        const float kr = sk[16 * w + i];
-        const float qr = sq[16 * w + i];
-        s[i].x = fmaf(kr, dl.x, s[i].x);
-        s[i].y = fmaf(kr, dl.y, s[i].y);
-        s[i].z = fmaf(kr, dl.z, s[i].z);
-        s[i].w = fmaf(kr, dl.w, s[i].w);
-        op.x = fmaf(qr, s[i].x, op.x);
-        op.y = fmaf(qr, s[i].y, op.y);
-        op.z = fmaf(qr, s[i].z, op.z);
-        op.w = fmaf(qr, s[i].w, op.w);
-        So[(16 * w + i) * (HD / 4) + l] = s[i];
-    }
-    __syncthreads();  // every warp is done with red[] and dred[] from the passes above
-    reinterpret_cast<float4*>(red[w])[l] = op;
-    __syncthreads();
-
-    // ---- output, per-head RMSNorm (deltanet_impl.h:350-361) and SiLU(z) gate (364-371)
-    float o = 0.0f;
-    if (t < HD) {
-        for (int ww = 0; ww < 8; ww++) o += red[ww][t];
-        o = __fmul_rn(o, 1.0f / sqrtf((float)HD));
-        double so = (double)o * (double)o;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) so += __shfl_xor_sync(0xffffffffu, so, off);
-        if (l == 0) dred[w] = so;
-    }
-    __syncthreads();
-    if (t < HD) {
-        const double tot = dred[0] + dred[1] + dred[2] + dred[3];
-        const float inv = 1.0f / sqrtf((float)(tot / HD) + 1e-6f);
-        float nv = __fmul_rn(o, inv);
-        if (head_norm != nullptr) nv = __fmul_rn(nv, head_norm[t]);
-        float zv = pr[qkv + h * HD + t];
-        zv = fminf(fmaxf(zv, -88.0f), 88.0f);
-        const float gv = __fmul_rn(nv, zv / (1.0f + expf(-zv)));
-        const int64_t idx = (int64_t)b * inner + h * HD + t;
-        if (gated != nullptr) gated[idx] = gv;
-        if (gated_h != nullptr) gated_h[idx] = __float2half_rn(gv);
+            for (int off = 16; off > 0; off >>= 1) so += __shfl_xor_sync(0xffffffffu, so, off);
+            if (l == 0) sm.dred[w] = so;
+        }
+        __syncthreads();
+        if (t < HD) {
+            const double tot = sm.dred[0] + sm.dred[1] + sm.dred[2] + sm.dred[3];
+            const float inv = 1.0f / sqrtf((float)(tot / HD) + 1e-6f);
+            float nv = __fmul_rn(o, inv);
+            if (head_norm != nullptr) nv = __fmul_rn(nv, head_norm[t]);
+            float zv = pr[qkv + h * HD + t];
+            zv = fminf(fmaxf(zv, -88.0f), 88.0f);
+            const float gv = __fmul_rn(nv, zv / (1.0f + expf(-zv)));
+            const int64_t idx = b * inner + h * HD + t;
+            if (gated != nullptr) gated[idx] = gv;
+            if (gated_h != nullptr) gated_h[idx] = __float2half_rn(gv);
+        }
+        __syncthreads();  // dred / q / k / v reused by the next tile
     }
 }
+
+size_t state_kernel_smem() { return sizeof(StateSmem) + 128; }
 
 // conv_pos[b] += 1 once every head of the step has read it (deltanet_impl.h:222).
 __global__ void conv_pos_bump_kernel(int32_t* __restrict__ conv_pos, int64_t B) {
@@ -333,30 +396,31 @@ int validate_layer(const gdn_layer* L) {
 }
 
 // Input projection: proj[B][np] = x . in_proj^T.
-// Q8_0, B >= 64: rows [0, QKV+inner) on the tensor cores with split-precision
-// weights (x used as bf16 directly, else converted to fp16); the 2*Hv gate rows
-// (beta, alpha) on CUDA cores in fp32 -- exp(ssm_a * softplus(alpha)) magnifies
-// any rounding of alpha.  Otherwise one CUDA-core GEMV over all rows.
+// Q8_0, B >= 64: tensor cores with split-precision fp16 weights (exact) and
+// fp16 activations.  bf16/fp16 x converts to fp16 exactly, so every row --
+// including the gate rows, where exp(ssm_a * softplus(alpha)) magnifies any
+// rounding of alpha -- matches an fp32 GEMV up to summation order.  fp32 x
+// would be rounded by that conversion: then the 2*Hv gate rows run on CUDA
+// cores in fp32 instead.  Otherwise one CUDA-core GEMV over all rows.
 static int in_projection(const gdn_layer* L, const Dims& D, int64_t B, const void* x, int x_dtype,
                          const Workspace& ws, cudaStream_t s) {
     const int64_t hidden = L->dims.hidden;
     if (L->weight_type == GDN_GGML_Q4_K)
         return launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, B, ws.proj, D.np, s);
     if (B < kTcMinBatch) return launch_q8_0_gemv(L->in_qs, L->in_d, D.np, hidden, x, x_dtype, B, ws.proj, D.np, s);
-    const int64_t n_tc = (int64_t)D.qkv + D.inner;
     const void* a = x;
-    bool a_bf16 = (x_dtype == GDN_DTYPE_BF16);
     int st;
-    if (x_dtype == GDN_DTYPE_F32 || !aligned(x, 16)) {
+    if (x_dtype != GDN_DTYPE_F16 || !aligned(x, 16)) {
         if ((st = launch_convert(x, x_dtype, ws.xconv, false, B * hidden, s))) return st;
         a = ws.xconv;
-        a_bf16 = false;
     }
     TcOptions opt;
     opt.split_precision = true;
-    if ((st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_tc, hidden, a, a_bf16, B, ws.proj, D.np, opt, s))) return st;
-    return launch_q8_0_gemv(L->in_qs + n_tc * hidden, L->in_d + n_tc * (hidden / 32), 2 * D.hv, hidden, x, x_dtype, B,
-                            ws.proj + n_tc, D.np, s);
+    const int64_t n_tc = (x_dtype == GDN_DTYPE_F32) ? (int64_t)D.qkv + D.inner : D.np;
+    if ((st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_tc, hidden, a, false, B, ws.proj, D.np, opt, s))) return st;
+    if (n_tc == D.np) return GDN_OK;
+    return launch_q8_0_gemv(L->in_qs + n_tc * hidden, L->in_d + n_tc * (hidden / 32), D.np - n_tc, hidden, x,
+                            x_dtype, B, ws.proj + n_tc, D.np, s);
 }
 
 int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
@@ -382,10 +446,18 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
     if ((st = in_projection(L, D, B, x, x_dtype, ws, s))) return st;
     if ((st = mark(pe, 1, s))) return st;
     if ((st = mark(pe, 2, s))) return st;  // the conv/L2/gates phase is fused into the state kernel
-    gdn_state_kernel<<<dim3(D.hv, (unsigned)B), 256, 0, s>>>(
-        ws.proj, D.np, S, conv ? conv_buf : nullptr, conv_pos, conv ? L->conv1d_w : nullptr, L->ssm_a, L->dt_bias,
-        L->head_norm, tc_out ? nullptr : ws.gated, tc_out ? ws.gated_h : nullptr, D.qkv, D.key, D.hv, D.hk,
-        L->head_map);
+    {
+        const int64_t n_tiles = B * D.hv;
+        const int64_t ctas = std::min<int64_t>(n_tiles, sm_count());
+        const int64_t per = (n_tiles + ctas - 1) / ctas;
+        const size_t smem = state_kernel_smem();
+        GDN_CUDA(cudaFuncSetAttribute((const void*)gdn_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
+        gdn_state_kernel<<<(unsigned)((n_tiles + per - 1) / per), 256, smem, s>>>(
+            ws.proj, D.np, S, conv ? conv_buf : nullptr, conv_pos, conv ? L->conv1d_w : nullptr, L->ssm_a,
+            L->dt_bias, L->head_norm, tc_out ? nullptr : ws.gated, tc_out ? ws.gated_h : nullptr, D.qkv, D.key, D.hv,
+            D.hk, L->head_map, n_tiles, per, device_error_word());
+    }
     GDN_LAUNCH_CHECK("gdn_state_kernel");
     if (conv) {
         conv_pos_bump_kernel<<<(unsigned)((B + 255) / 256), 256, 0, s>>>(conv_pos, B);

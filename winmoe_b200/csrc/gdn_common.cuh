@@ -34,7 +34,8 @@ int cuda_status(cudaError_t e, const char* what);
 // Device error word: bit 0 = a bounded wait gave up.  Kernels OR into it and
 // return; gdn_check_device_error reads and clears it.
 enum : uint32_t { DEV_ERR_TIMEOUT = 1u, DEV_ERR_BOUNDS = 2u };
-uint32_t* device_error_word();  // per-device, allocated once on first use
+uint32_t* device_error_word();  // per-device __device__ word, looked up once per device
+int sm_count();                  // SMs of the current device (cached per device)
 
 // Spin limit of bounded waits, in SM clock cycles (~1 s at 1.9 GHz).
 constexpr long long kWaitCycles = 2000000000LL;

@@ -81,6 +81,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Untiled bulk copy global -> shared of `bytes` (a multiple of 16; both
+// addresses 16-byte aligned), completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 // -------------------------------------------------------------------- tcgen05
 
 // Allocates `ncols` TMEM columns (power of two >= 32); the base address is

@@ -300,6 +300,15 @@ int launch_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t
     return GDN_OK;
 }
 
+// Weight rows per block (a multiple of the 8 warps, at most 32): fewer when
+// the grid would otherwise leave SMs idle (few weight rows, e.g. the gates).
+static int rows_per_block(int64_t n, int64_t groups) {
+    const int64_t want = 2 * (int64_t)sm_count();
+    int rpb = 32;
+    while (rpb > 8 && ((n + rpb - 1) / rpb) * groups < want) rpb -= 8;
+    return rpb;
+}
+
 // Activation rows per block (a template size: 1, 2, 4 or 8): the smallest one
 // that covers min(m, 8) rows, halved while the staged rows overflow shared memory.
 static int pick_mb(int64_t m, int64_t floats_per_row) {
@@ -314,7 +323,7 @@ static int run_q8_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k
     const size_t smem = (size_t)MB * k * sizeof(float);
     int st = smem_optin((const void*)q8_0_gemv_kernel<MB>, smem);
     if (st) return st;
-    const int rpb = 32;
+    const int rpb = rows_per_block(n, (m + MB - 1) / MB);
     const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
     q8_0_gemv_kernel<MB><<<grid, 256, smem, s>>>(qs, d, n, k, x, dt, m, y, ldy, rpb);
     GDN_LAUNCH_CHECK("q8_0_gemv_kernel");
@@ -349,7 +358,7 @@ static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int d
     const size_t smem = (size_t)MB * (k + k / 16) * sizeof(float);
     int st = smem_optin((const void*)q4_k_gemv_kernel<MB>, smem);
     if (st) return st;
-    const int rpb = 32;
+    const int rpb = rows_per_block(n, (m + MB - 1) / MB);
     const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
     q4_k_gemv_kernel<MB><<<grid, 256, smem, s>>>(static_cast<const uint8_t*>(w), n, k, x, dt, m, y, ldy, rpb);
     GDN_LAUNCH_CHECK("q4_k_gemv_kernel");
