@@ -181,3 +181,24 @@ def test_legacy_offload_api(t35):
     assert h.gpu_launch_qkv_gate(0, 0, vp(x), cfg.hidden + 32, cfg.qkv_dim, cfg.inner) == -1
     h.gpu_shutdown()
     assert h.gpu_is_initialized() == 0
+
+
+@pytest.mark.parametrize("cfg,B", [(GDNConfig(256, 1, 3, 128), 2), (GDNConfig(768, 3, 6, 128), 70)])
+def test_decode_odd_shapes(cfg, B):
+    """Odd value-head counts (padded projection rows) and a batch above the tensor-core threshold."""
+    t = synth.layer_tensors(cfg, layer=5)
+    w = L.DeltaNetWeights.upload(cfg, t.in_proj, t.out_proj, t.conv1d_w, t.ssm_a, t.dt_bias, t.head_norm,
+                                 device=DEV)
+    S0 = np.stack([synth.prefilled_state(cfg, b) for b in range(B)])
+    xs = synth.hidden_states(3 * B, cfg.hidden, seed=21).reshape(3, B, cfg.hidden)
+    xs_t = torch.from_numpy(xs).to(torch.bfloat16)
+    st = L.DeltaNetState.zeros(cfg, B, DEV)
+    st.S.copy_(torch.from_numpy(S0))
+    outs = [L.decode_step(w, st, xs_t[s].to(DEV).contiguous()).cpu().numpy() for s in range(3)]
+    for b in sorted({0, B // 2, B - 1}):
+        want, S_ref, cb_ref, _ = run_oracle(cfg, t, xs_t.float().numpy()[:, b], S0=S0[b])
+        for s in range(3):
+            assert rel_l2(outs[s][b], want[s]) <= TOL, (b, s)
+        assert rel_l2(st.S[b].cpu().numpy(), S_ref) <= TOL
+        assert rel_l2(st.conv_buf[b].cpu().numpy(), cb_ref) <= TOL
+    assert (st.conv_pos.cpu().numpy() == 3).all()

@@ -10,9 +10,9 @@
 // (conv 218-236, gates 247-261, L2 264-267, recurrence 279-348, norm 350-361,
 // gate 364-371, out_proj 374).
 //
-// Kernels per step: the projections (tensor-core GEMMs for B >= 64, CUDA-core
-// GEMVs below), gdn_state_kernel (everything between the projections, one
-// CTA per (value head, sequence)), conv_pos_bump, out_proj.
+// Kernels per step: the input projection (tensor-core GEMM for B >= 64,
+// CUDA-core GEMV below), gdn_prep_kernel (conv1d, SiLU, L2 norms, gates),
+// gdn_state_kernel (recurrence, RMSNorm, output gate), out_proj.
 // The state kernel is the HBM-bound part: every (sequence, value head) owns a
 // 128x128 fp32 state (64 KiB) that is read once and written once per token.
 #include <algorithm>
@@ -26,124 +26,34 @@ namespace gdn {
 
 constexpr int HD = 128;  // head_dim (the reference's AVX loops assume 128 too)
 
-// ------------------------------------------------------------- state kernel
+// -------------------------------------------------------------- prep kernel
 //
-// Persistent: one CTA (256 threads) per SM walks a contiguous range of tiles
-// tile = ((b * Hk + g) * hpg + u), i.e. (sequence b, value head h = the u-th
-// head of key group g).  The 64 KiB fp32 state of each tile is brought into a
-// kStateBufs-deep shared-memory ring by cp.async.bulk (mbarrier completion), so
-// HBM always has the next tiles' loads in flight while this one is computed;
-// the updated state goes back to HBM with coalesced 16-byte stores straight
-// from registers.
-//
-// Per tile, before waiting on its state:
-//   * when the key group changes: causal conv1d + SiLU of the q and k channels
-//     of group g (thread t < 128: q[t], t >= 128: k[t-128]), L2 norms with
-//     double-precision sums (deltanet_impl.h:85-91, 264-267);
-//   * conv1d + SiLU of v (head h), gates decay/beta of head h (247-261).
-//   Window slot p%4 (the oldest, never read this step) receives the raw
-//   projection: v slots by their head, q/k slots by the group's first head.
-// Recurrence: warp w owns state rows [16w, 16w+16), lane l columns [4l, 4l+4)
-// (16 float4 registers per thread; one warp access = one 512-byte row).
-constexpr int kStateBufs = 3;
-constexpr int kTileFloats = HD * HD;
-constexpr uint32_t kTileBytes = kTileFloats * 4;
-
-struct StateSmem {
-    float S[kStateBufs][kTileFloats];
-    float q[HD], k[HD], v[HD], delta[HD];
-    float red[8][HD];
-    double dred[8];
-    float gate[2];
-    uint64_t full[kStateBufs];
-};
-
-__global__ void __launch_bounds__(256, 1) gdn_state_kernel(
-    const float* __restrict__ proj, int64_t np, float* __restrict__ S, float* __restrict__ conv_buf,
-    const int32_t* __restrict__ conv_pos, const float* __restrict__ conv_w, const float* __restrict__ ssm_a,
-    const float* __restrict__ dt_bias, const float* __restrict__ head_norm, float* __restrict__ gated,
-    __half* __restrict__ gated_h, int qkv, int key_dim, int hv, int hk, int head_map, int64_t n_tiles,
-    int64_t tiles_per_cta, uint32_t* __restrict__ err) {
-    extern __shared__ uint8_t smem_raw[];
-    StateSmem& sm = *reinterpret_cast<StateSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    const int t = threadIdx.x, w = t >> 5, l = t & 31;
-    const int hpg = hv / hk;
-    const int inner = hv * HD;
-    const int64_t first = (int64_t)blockIdx.x * tiles_per_cta;
-    const int64_t last = min(first + tiles_per_cta, n_tiles);
-    const int count = (int)max((int64_t)0, last - first);
-    const bool conv_on = conv_w != nullptr && conv_buf != nullptr;
-
-    auto tile_head = [&](int64_t tile, int64_t& b, int& g, int& u) {
-        u = (int)(tile % hpg);
-        const int64_t bg = tile / hpg;
-        g = (int)(bg % hk);
-        b = bg / hk;
-        return head_map ? (g + u * hk) : (g * hpg + u);
-    };
-    auto state_ptr = [&](int64_t tile) {
-        int64_t b;
-        int g, u;
-        const int h = tile_head(tile, b, g, u);
-        return S + (b * hv + h) * (int64_t)kTileFloats;
-    };
-    const uint32_t sbuf0 = sm100::smem_u32(&sm.S[0][0]);
-    auto issue = [&](int i) {  // local tile i -> ring slot i % kStateBufs
-        const int slot = i % kStateBufs;
-        const uint32_t bar = sm100::smem_u32(&sm.full[slot]);
-        sm100::mbar_arrive_expect_tx(bar, kTileBytes);
-        sm100::bulk_load(sbuf0 + slot * kTileBytes, state_ptr(first + i), kTileBytes, bar);
-    };
-
-    if (t == 0) {
-        for (int i = 0; i < kStateBufs; i++) sm100::mbar_init(sm100::smem_u32(&sm.full[i]), 1);
-        sm100::fence_barrier_init();
-        for (int i = 0; i < kStateBufs && i < count; i++) issue(i);
-    }
-    __syncthreads();
-
-    int64_t cur_bg = -1;
-    bool ok = true;
-    for (int i = 0; i < count; i++) {
-        const int64_t tile = first + i;
-        int64_t b;
-        int g, u;
-        const int h = tile_head(tile, b, g, u);
-        const float* pr = proj + b * np;
-        const int p = conv_on ? conv_pos[b] : 0;
-        float* win = conv_on ? conv_buf + b * 4 * (int64_t)qkv : nullptr;
-        auto conv = [&](int ch, bool write) -> float {
-            const float raw = pr[ch];
-            if (!conv_on) return raw;
-            const float4 wk = reinterpret_cast<const float4*>(conv_w)[ch];
-            const float x0 = win[(int64_t)((p - 3) & 3) * qkv + ch];
-            const float x1 = win[(int64_t)((p - 2) & 3) * qkv + ch];
-            const float x2 = win[(int64_t)((p - 1) & 3) * qkv + ch];
-            if (write) win[(int64_t)(p & 3) * qkv + ch] = raw;
-            float sum = 0.0f;
-            sum = __fadd_rn(sum, __fmul_rn(wk.x, x0));
-            sum = __fadd_rn(sum, __fmul_rn(wk.y, x1));
-            sum = __fadd_rn(sum, __fmul_rn(wk.z, x2));
-            sum = __fadd_rn(sum, __fmul_rn(wk.w, raw));
-            const float sig = 1.0f / (1.0f + expf(-sum));
-            return __fmul_rn(sum, sig);
-        };
-
-        // ---- q/k of a new key group: conv1d + SiLU + L2 norm (conv 218-236, L2 264-267)
-        const int64_t bg = tile / hpg;
-        const bool new_group = (bg != cur_bg);
-        cur_bg = bg;
-        float a_qk = 0.0f;
-        if (new_group) {
-            a_qk = (t < HD) ? conv(g * HD + t, u == 0) : conv(key_dim + g * HD + (t - HD), u == 0);
-            double ss = (double)a_qk * (double)a_qk;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            if (l == 0) sm.dred[w] = ss;
-        }
-        // ---- v of head h and its gates (gates 247-261)
-        if (t < HD) sm.v[t] = conv(2 * key_dim + h * HD + t, true);
-        if (t == 0) {
+// One warp per (sequence b, 128-channel chunk hc of the qkv vector): chunk hc
+// is q head hc (hc < Hk), k head hc-Hk (hc < 2Hk) or v head hc-2Hk.  Lane l
+// owns channels 4l..4l+3 (16-byte loads and stores):
+//   window slot p%4 <- raw projection; out = sum_k w[c][k] * window[(p+1-4+k)%4]
+//   (k = 0 oldest, k = 3 the value just stored), then SiLU (deltanet_impl.h:218-236);
+//   q/k heads are L2-normalised with a double-precision sum (85-91, 264-267).
+// One extra warp per sequence (hc = QKV/128) computes the gates of all heads
+// (247-261) into gates[b][h] = {decay, beta, 0, 0}.
+__global__ void __launch_bounds__(256) gdn_prep_kernel(const float* __restrict__ proj, int64_t np,
+                                                       float* __restrict__ act, float4* __restrict__ gates,
+                                                       float* __restrict__ conv_buf,
+                                                       const int32_t* __restrict__ conv_pos,
+                                                       const float* __restrict__ conv_w,
+                                                       const float* __restrict__ ssm_a,
+                                                       const float* __restrict__ dt_bias, int64_t B, int qkv,
+                                                       int key_dim, int hv) {
+    const int lane = threadIdx.x & 31;
+    const int nchunk = qkv / HD + 1;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (gw >= B * nchunk) return;
+    const int64_t b = gw / nchunk;
+    const int hc = (int)(gw % nchunk);
+    const float* pr = proj + b * np;
+    if (hc == nchunk - 1) {
+        const int inner = hv * HD;
+        for (int h = lane; h < hv; h += 32) {
             const float beta_raw = pr[qkv + inner + h];
             const float alpha_raw = pr[qkv + inner + hv + h];
             float a = 0.99f;
@@ -162,37 +72,135 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
                 const float z = expf(beta_raw);
                 bt = z / (1.0f + z);
             }
-            sm.gate[0] = a;
-            sm.gate[1] = bt;
+            gates[b * hv + h] = make_float4(a, bt, 0.0f, 0.0f);
         }
-        __syncthreads();
-        if (new_group) {
-            const int base = (t < HD) ? 0 : 4;
-            const double tot = sm.dred[base] + sm.dred[base + 1] + sm.dred[base + 2] + sm.dred[base + 3];
-            const float inv = 1.0f / (sqrtf((float)tot) + 1e-6f);
-            if (t < HD) sm.q[t] = __fmul_rn(a_qk, inv);
-            else sm.k[t - HD] = __fmul_rn(a_qk, inv);
+        return;
+    }
+    const int ch = hc * HD + 4 * lane;
+    float4 xv = *reinterpret_cast<const float4*>(pr + ch);
+    if (conv_buf != nullptr && conv_w != nullptr) {
+        const int p = conv_pos[b];
+        float* win = conv_buf + b * 4 * (int64_t)qkv;
+        const float4 o0 = *reinterpret_cast<const float4*>(win + (int64_t)((p - 3) & 3) * qkv + ch);
+        const float4 o1 = *reinterpret_cast<const float4*>(win + (int64_t)((p - 2) & 3) * qkv + ch);
+        const float4 o2 = *reinterpret_cast<const float4*>(win + (int64_t)((p - 1) & 3) * qkv + ch);
+        *reinterpret_cast<float4*>(win + (int64_t)(p & 3) * qkv + ch) = xv;
+        const float4* wv = reinterpret_cast<const float4*>(conv_w) + ch;  // 4 channels x 4 taps
+        float in[4] = {xv.x, xv.y, xv.z, xv.w};
+        const float h0[4] = {o0.x, o0.y, o0.z, o0.w}, h1[4] = {o1.x, o1.y, o1.z, o1.w};
+        const float h2[4] = {o2.x, o2.y, o2.z, o2.w};
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const float4 w = wv[c];
+            float sum = 0.0f;
+            sum = __fadd_rn(sum, __fmul_rn(w.x, h0[c]));
+            sum = __fadd_rn(sum, __fmul_rn(w.y, h1[c]));
+            sum = __fadd_rn(sum, __fmul_rn(w.z, h2[c]));
+            sum = __fadd_rn(sum, __fmul_rn(w.w, in[c]));
+            const float sig = 1.0f / (1.0f + expf(-sum));
+            in[c] = __fmul_rn(sum, sig);
         }
+        xv = make_float4(in[0], in[1], in[2], in[3]);
+    }
+    if (ch < 2 * key_dim) {
+        double ss = (double)xv.x * xv.x + (double)xv.y * xv.y + (double)xv.z * xv.z + (double)xv.w * xv.w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / (sqrtf((float)ss) + 1e-6f);
+        xv = make_float4(__fmul_rn(xv.x, inv), __fmul_rn(xv.y, inv), __fmul_rn(xv.z, inv), __fmul_rn(xv.w, inv));
+    }
+    *reinterpret_cast<float4*>(act + b * qkv + ch) = xv;
+}
 
-        // ---- this tile's state: wait for the ring slot, copy it to registers
-        const int slot = i % kStateBufs;
-        ok = ok && sm100::mbar_wait(sm100::smem_u32(&sm.full[slot]), (uint32_t)((i / kStateBufs) & 1), err);
-        const float4* Sv = reinterpret_cast<const float4*>(&sm.S[slot][0]);
+// ------------------------------------------------------------- state kernel
+//
+// Persistent: one CTA (256 threads) per SM walks a contiguous range of tiles
+// (sequence b, value head h).  Everything a tile reads -- its 64 KiB fp32
+// state, the conv'd q and k of its key group, v and z of head h, and its
+// gates -- is brought into a kStateBufs-deep shared-memory ring by
+// cp.async.bulk with one mbarrier per slot, so the loop itself issues no
+// global loads and HBM always has the next tiles in flight.  The updated
+// state goes back to HBM with coalesced 16-byte stores straight from
+// registers.  Recurrence: warp w owns state rows [16w, 16w+16), lane l
+// columns [4l, 4l+4) (16 float4 registers per thread; one warp access = one
+// 512-byte row).  The CTA holding head 0 of sequence b advances conv_pos[b]
+// (the prep kernel, which read it, has finished).
+constexpr int kStateBufs = 3;
+constexpr int kTileFloats = HD * HD;
+constexpr uint32_t kTileBytes = kTileFloats * 4;
+constexpr uint32_t kVecBytes = HD * 4;
+
+struct StateSlot {
+    float S[kTileFloats];
+    float q[HD], k[HD], v[HD], z[HD];
+    float4 gate;
+};
+
+struct StateSmem {
+    StateSlot slot[kStateBufs];
+    float delta[HD];
+    float red[8][HD];
+    double dred[4];
+    uint64_t full[kStateBufs];
+};
+
+__global__ void __launch_bounds__(256, 1) gdn_state_kernel(
+    const float* __restrict__ act, const float4* __restrict__ gates, const float* __restrict__ proj, int64_t np,
+    float* __restrict__ S, const float* __restrict__ head_norm, float* __restrict__ gated,
+    __half* __restrict__ gated_h, int32_t* __restrict__ conv_pos, int qkv, int key_dim, int hv, int hk,
+    int head_map, int64_t n_tiles, int64_t tiles_per_cta, uint32_t* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    StateSmem& sm = *reinterpret_cast<StateSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    const int t = threadIdx.x, w = t >> 5, l = t & 31;
+    const int hpg = hv / hk;
+    const int inner = hv * HD;
+    const int64_t first = (int64_t)blockIdx.x * tiles_per_cta;
+    const int64_t last = min(first + tiles_per_cta, n_tiles);
+    const int count = (int)max((int64_t)0, last - first);
+
+    // tile -> (b, h); tiles run over the heads of a sequence in order
+    auto issue = [&](int i) {
+        const int64_t tile = first + i;
+        const int64_t b = tile / hv;
+        const int h = (int)(tile % hv);
+        const int g = head_map ? (h % hk) : (h / hpg);
+        StateSlot& sl = sm.slot[i % kStateBufs];
+        const uint32_t bar = sm100::smem_u32(&sm.full[i % kStateBufs]);
+        const float* a = act + b * qkv;
+        sm100::mbar_arrive_expect_tx(bar, kTileBytes + 4 * kVecBytes + 16);
+        sm100::bulk_load(sm100::smem_u32(sl.S), S + (b * hv + h) * (int64_t)kTileFloats, kTileBytes, bar);
+        sm100::bulk_load(sm100::smem_u32(sl.q), a + g * HD, kVecBytes, bar);
+        sm100::bulk_load(sm100::smem_u32(sl.k), a + key_dim + g * HD, kVecBytes, bar);
+        sm100::bulk_load(sm100::smem_u32(sl.v), a + 2 * key_dim + h * HD, kVecBytes, bar);
+        sm100::bulk_load(sm100::smem_u32(sl.z), proj + b * np + qkv + h * HD, kVecBytes, bar);
+        sm100::bulk_load(sm100::smem_u32(&sl.gate), gates + b * hv + h, 16, bar);
+    };
+
+    if (t == 0) {
+        for (int i = 0; i < kStateBufs; i++) sm100::mbar_init(sm100::smem_u32(&sm.full[i]), 1);
+        sm100::fence_barrier_init();
+        for (int i = 0; i < kStateBufs && i < count; i++) issue(i);
+    }
+    __syncthreads();
+
+    bool ok = true;
+    for (int i = 0; i < count; i++) {
+        const int64_t tile = first + i;
+        const int64_t b = tile / hv;
+        const int h = (int)(tile % hv);
+        StateSlot& sl = sm.slot[i % kStateBufs];
+        ok = ok && sm100::mbar_wait(sm100::smem_u32(&sm.full[i % kStateBufs]), (uint32_t)((i / kStateBufs) & 1), err);
+        const float4* Sv = reinterpret_cast<const float4*>(sl.S);
         float4 s[16];
 #pragma unroll
         for (int r = 0; r < 16; r++) s[r] = Sv[(16 * w + r) * (HD / 4) + l];
-        __syncthreads();  // slot drained; q/k visible
-        if (t == 0 && ok && i + kStateBufs < count) {  // after a timed-out wait no new copy is issued
-            sm100::fence_proxy_async_smem();
-            issue(i + kStateBufs);
-        }
-        const float dg = sm.gate[0], bt = sm.gate[1];
+        const float dg = sl.gate.x, bt = sl.gate.y;
 
         // ---- decay + retrieve (deltanet_impl.h:298-307)
         float4 rp = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int r = 0; r < 16; r++) {
-            const float kr = sm.k[16 * w + r];
+            const float kr = sl.k[16 * w + r];
             s[r].x = __fmul_rn(s[r].x, dg);
             s[r].y = __fmul_rn(s[r].y, dg);
             s[r].z = __fmul_rn(s[r].z, dg);
@@ -208,18 +216,18 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
             float rr = 0.0f;
 #pragma unroll
             for (int ww = 0; ww < 8; ww++) rr += sm.red[ww][t];
-            sm.delta[t] = __fmul_rn(bt, __fsub_rn(sm.v[t], rr));  // deltanet_impl.h:311-317
+            sm.delta[t] = __fmul_rn(bt, __fsub_rn(sl.v[t], rr));  // deltanet_impl.h:311-317
         }
         __syncthreads();
 
         // ---- update + output read (deltanet_impl.h:320-347); the state goes back to HBM
         const float4 dl = reinterpret_cast<const float4*>(sm.delta)[l];
         float4 op = make_float4(0.f, 0.f, 0.f, 0.f);
-        float4* So = reinterpret_cast<float4*>(state_ptr(tile));
+        float4* So = reinterpret_cast<float4*>(S + (b * hv + h) * (int64_t)kTileFloats);
 #pragma unroll
         for (int r = 0; r < 16; r++) {
-            const float kr = sm.k[16 * w + r];
-            const float qr = sm.q[16 * w + r];
+            const float kr = sl.k[16 * w + r];
+            const float qr = sl.q[16 * w + r];
             s[r].x = fmaf(kr, dl.x, s[r].x);
             s[r].y = fmaf(kr, dl.y, s[r].y);
             s[r].z = fmaf(kr, dl.z, s[r].z);
@@ -230,7 +238,7 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
             op.w = fmaf(qr, s[r].w, op.w);
             So[(16 * w + r) * (HD / 4) + l] = s[r];
         }
-        __syncthreads();  // every warp is done with red[] and dred[]
+        __syncthreads();  // every warp is done with red[]
         reinterpret_cast<float4*>(sm.red[w])[l] = op;
         __syncthreads();
 
@@ -250,24 +258,23 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
             const float inv = 1.0f / sqrtf((float)(tot / HD) + 1e-6f);
             float nv = __fmul_rn(o, inv);
             if (head_norm != nullptr) nv = __fmul_rn(nv, head_norm[t]);
-            float zv = pr[qkv + h * HD + t];
+            float zv = sl.z[t];
             zv = fminf(fmaxf(zv, -88.0f), 88.0f);
             const float gv = __fmul_rn(nv, zv / (1.0f + expf(-zv)));
             const int64_t idx = b * inner + h * HD + t;
             if (gated != nullptr) gated[idx] = gv;
             if (gated_h != nullptr) gated_h[idx] = __float2half_rn(gv);
         }
-        __syncthreads();  // dred / q / k / v reused by the next tile
+        if (t == 0 && h == 0 && conv_pos != nullptr) conv_pos[b] += 1;
+        __syncthreads();  // slot i % kStateBufs fully consumed
+        if (t == 0 && ok && i + kStateBufs < count) {  // after a timed-out wait no new copy is issued
+            sm100::fence_proxy_async_smem();
+            issue(i + kStateBufs);
+        }
     }
 }
 
 size_t state_kernel_smem() { return sizeof(StateSmem) + 128; }
-
-// conv_pos[b] += 1 once every head of the step has read it (deltanet_impl.h:222).
-__global__ void conv_pos_bump_kernel(int32_t* __restrict__ conv_pos, int64_t B) {
-    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b < B) conv_pos[b] += 1;
-}
 
 // ----------------------------------------------------------- phase timing
 
@@ -298,7 +305,8 @@ constexpr int kOutSplits = 4;
 
 struct Dims {
     int hv, hk, key, inner, qkv;
-    int64_t np;
+    int64_t np;   // projection width: QKV + inner + 2 Hv
+    int64_t ldp;  // its row stride in the workspace, a multiple of 4 floats (16-byte rows)
 };
 
 Dims dims_of(const gdn_dims& d) {
@@ -309,11 +317,14 @@ Dims dims_of(const gdn_dims& d) {
     r.inner = r.hv * HD;
     r.qkv = 2 * r.key + r.inner;
     r.np = (int64_t)r.qkv + r.inner + 2 * r.hv;
+    r.ldp = (r.np + 3) / 4 * 4;
     return r;
 }
 
 struct Workspace {
     float* proj = nullptr;      // [B][np]
+    float* act = nullptr;       // [B][QKV] conv'd, SiLU'd, q/k L2-normalised
+    float4* gates = nullptr;    // [B][Hv] {decay, beta, 0, 0}
     float* gated = nullptr;     // [B][inner] fp32 (CUDA-core out_proj)
     __half* gated_h = nullptr;  // [B][inner] fp16 (tensor-core out_proj)
     void* xconv = nullptr;      // [B][hidden] 2-byte operand copy of x
@@ -332,7 +343,9 @@ Workspace carve(const gdn_dims& d, int64_t B, void* base) {
         off += round_up(bytes, 256);
         return r;
     };
-    w.proj = reinterpret_cast<float*>(take((size_t)B * D.np * 4));
+    w.proj = reinterpret_cast<float*>(take((size_t)B * D.ldp * 4));
+    w.act = reinterpret_cast<float*>(take((size_t)B * D.qkv * 4));
+    w.gates = reinterpret_cast<float4*>(take((size_t)B * D.hv * 16));
     w.gated = reinterpret_cast<float*>(take((size_t)B * D.inner * 4));
     w.gated_h = reinterpret_cast<__half*>(take((size_t)B * D.inner * 2));
     w.xconv = take((size_t)B * d.hidden * 2);
@@ -406,8 +419,8 @@ static int in_projection(const gdn_layer* L, const Dims& D, int64_t B, const voi
                          const Workspace& ws, cudaStream_t s) {
     const int64_t hidden = L->dims.hidden;
     if (L->weight_type == GDN_GGML_Q4_K)
-        return launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, B, ws.proj, D.np, s);
-    if (B < kTcMinBatch) return launch_q8_0_gemv(L->in_qs, L->in_d, D.np, hidden, x, x_dtype, B, ws.proj, D.np, s);
+        return launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, B, ws.proj, D.ldp, s);
+    if (B < kTcMinBatch) return launch_q8_0_gemv(L->in_qs, L->in_d, D.np, hidden, x, x_dtype, B, ws.proj, D.ldp, s);
     const void* a = x;
     int st;
     if (x_dtype != GDN_DTYPE_F16 || !aligned(x, 16)) {
@@ -417,10 +430,10 @@ static int in_projection(const gdn_layer* L, const Dims& D, int64_t B, const voi
     TcOptions opt;
     opt.split_precision = true;
     const int64_t n_tc = (x_dtype == GDN_DTYPE_F32) ? (int64_t)D.qkv + D.inner : D.np;
-    if ((st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_tc, hidden, a, false, B, ws.proj, D.np, opt, s))) return st;
+    if ((st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_tc, hidden, a, false, B, ws.proj, D.ldp, opt, s))) return st;
     if (n_tc == D.np) return GDN_OK;
     return launch_q8_0_gemv(L->in_qs + n_tc * hidden, L->in_d + n_tc * (hidden / 32), D.np - n_tc, hidden, x,
-                            x_dtype, B, ws.proj + n_tc, D.np, s);
+                            x_dtype, B, ws.proj + n_tc, D.ldp, s);
 }
 
 int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
@@ -445,7 +458,14 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
     if ((st = mark(pe, 0, s))) return st;
     if ((st = in_projection(L, D, B, x, x_dtype, ws, s))) return st;
     if ((st = mark(pe, 1, s))) return st;
-    if ((st = mark(pe, 2, s))) return st;  // the conv/L2/gates phase is fused into the state kernel
+    {
+        const int64_t warps = B * (D.qkv / HD + 1);
+        gdn_prep_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(
+            ws.proj, D.ldp, ws.act, ws.gates, conv ? conv_buf : nullptr, conv_pos, conv ? L->conv1d_w : nullptr,
+            L->ssm_a, L->dt_bias, B, D.qkv, D.key, D.hv);
+        GDN_LAUNCH_CHECK("gdn_prep_kernel");
+    }
+    if ((st = mark(pe, 2, s))) return st;
     {
         const int64_t n_tiles = B * D.hv;
         const int64_t ctas = std::min<int64_t>(n_tiles, sm_count());
@@ -454,14 +474,10 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
         GDN_CUDA(cudaFuncSetAttribute((const void*)gdn_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)smem));
         gdn_state_kernel<<<(unsigned)((n_tiles + per - 1) / per), 256, smem, s>>>(
-            ws.proj, D.np, S, conv ? conv_buf : nullptr, conv_pos, conv ? L->conv1d_w : nullptr, L->ssm_a,
-            L->dt_bias, L->head_norm, tc_out ? nullptr : ws.gated, tc_out ? ws.gated_h : nullptr, D.qkv, D.key, D.hv,
-            D.hk, L->head_map, n_tiles, per, device_error_word());
-    }
-    GDN_LAUNCH_CHECK("gdn_state_kernel");
-    if (conv) {
-        conv_pos_bump_kernel<<<(unsigned)((B + 255) / 256), 256, 0, s>>>(conv_pos, B);
-        GDN_LAUNCH_CHECK("conv_pos_bump_kernel");
+            ws.act, ws.gates, ws.proj, D.ldp, S, L->head_norm, tc_out ? nullptr : ws.gated,
+            tc_out ? ws.gated_h : nullptr, conv ? conv_pos : nullptr, D.qkv, D.key, D.hv, D.hk, L->head_map, n_tiles,
+            per, device_error_word());
+        GDN_LAUNCH_CHECK("gdn_state_kernel");
     }
     if ((st = mark(pe, 3, s))) return st;
     if (L->weight_type == GDN_GGML_Q4_K) {
