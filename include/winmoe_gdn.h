@@ -191,6 +191,26 @@ GDN_API int gdn_decode_step(const gdn_layer* layer, int64_t batch,
                     float* S, float* conv_buf, int32_t* conv_pos,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Bytes of scratch gdn_prefill needs for a prompt of T tokens. */
+GDN_API size_t gdn_prefill_workspace_size(const gdn_dims* dims, int64_t T);
+
+/*
+ * Prefill: T tokens of ONE sequence through the layer, the result of T
+ * consecutive deltanet_forward calls (engine/runtime/deltanet_impl.h:145-377;
+ * the reference feeds prompts token by token, winmoe_inference.c:2286-2291).
+ * Computed in chunks of 64 tokens in the WY form (bf16 tensor-core products,
+ * fp32 state and triangular solve); the projections run on the tensor cores
+ * (one fp16 weight operand; the beta/alpha gate rows exact).
+ *   x [T][hidden] (F32, BF16 or F16);  out [T][hidden] fp32.
+ *   S [Hv][d][d], conv_buf [4][QKV], conv_pos [1]: the sequence's state,
+ *   read as the state before the prompt and updated to the state after it,
+ *   in the layout of gdn_decode_step (ready for decoding).
+ *   workspace: >= gdn_prefill_workspace_size bytes, 256-aligned.
+ */
+GDN_API int gdn_prefill(const gdn_layer* layer, int64_t T, const void* x, int x_dtype, float* out,
+                        float* S, float* conv_buf, int32_t* conv_pos,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 /*
  * Optional phase timing of gdn_decode_step, for benchmarks.  While enabled
  * (on the calling thread's current device), every gdn_decode_step records a

@@ -7,6 +7,7 @@
 #include "gdn_common.cuh"
 #include "quant.cuh"
 #include "decode.cuh"
+#include "prefill.cuh"
 
 namespace gdn {
 
@@ -142,6 +143,16 @@ int gdn_decode_step(const gdn_layer* layer, int64_t batch, const void* x, int x_
                     float* conv_buf, int32_t* conv_pos, void* workspace, size_t workspace_bytes, void* stream) {
     return decode_step(layer, batch, x, x_dtype, out, S, conv_buf, conv_pos, workspace, workspace_bytes,
                        as_stream(stream));
+}
+
+size_t gdn_prefill_workspace_size(const gdn_dims* dims, int64_t T) {
+    if (dims == nullptr || T <= 0) return 0;
+    return prefill_workspace_bytes(*dims, T);
+}
+
+int gdn_prefill(const gdn_layer* layer, int64_t T, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
+                int32_t* conv_pos, void* workspace, size_t workspace_bytes, void* stream) {
+    return prefill(layer, T, x, x_dtype, out, S, conv_buf, conv_pos, workspace, workspace_bytes, as_stream(stream));
 }
 
 int gdn_profile_enable(int on) { return profile_enable(on); }

@@ -1,0 +1,759 @@
+// Chunked prefill of the Gated DeltaNet layer: T tokens of one sequence.
+//
+// The reference has no prefill path: prompt tokens go one at a time through
+// deltanet_forward (engine/runtime/winmoe_inference.c:2286-2291 drives
+// engine/runtime/deltanet_impl.h:145-377).  This computes the same recurrence
+//   S_t = a_t S_{t-1} + k_t d_t^T,  d_t = b_t (v_t - a_t S_{t-1}^T k_t),
+//   o_t = S_t^T q_t / sqrt(d)
+// chunk by chunk (C = 64 tokens).  With G_i the inclusive cumulative log decay
+// inside a chunk, gam_i = exp(G_i), e_i = exp(G_63 - G_i) and
+// L[i][j] = b_i exp(G_i - G_j) (k_i . k_j) for j < i, the chunk's deltas are
+//   D = U' - W' S0,   (I + L) W' = diag(b gam) K,   (I + L) U' = diag(b) V,
+// its outputs
+//   O = scale * (diag(gam) Q S0 + P D),   P[i][j] = exp(G_i - G_j) (q_i . k_j), j <= i,
+// and the state it hands on
+//   S_end = gam_63 S0 + (diag(e) K)^T D.
+// Every exponent is a difference G_i - G_j with i >= j (<= 0): no division by
+// a cumulative decay.  Log decays are clamped at -110, below which exp() is 0
+// in fp32 whatever the rest of the sum, so a decay that underflows to 0 in the
+// reference (expf, deltanet_impl.h:251) zeroes the same products here.
+//
+// Kernels: prep (conv1d + SiLU + L2 norm, token-parallel), gates, window
+// hand-off, K1 chunk_local (W', U', e*K, cumulative G; fp32 forward
+// substitution), K2 chunk_scan (state passing, sequential over chunks,
+// parallel over heads x 32-column slabs), K3 chunk_out (outputs, per-head
+// RMSNorm and SiLU(z) gate).  The in/out projections are the tensor-core
+// GEMMs of gemm_tc.cu.
+#include <algorithm>
+
+#include "gdn_common.cuh"
+#include "quant.cuh"
+#include "prefill.cuh"
+#include "warp_mma.cuh"
+
+namespace gdn {
+
+using wmma16::bf16;
+
+namespace {
+
+constexpr int HD = 128;                 // head dim
+constexpr int CH = 64;                  // chunk length
+constexpr int BV = 32;                  // state columns per scan CTA
+constexpr float kLogDecayMin = -110.0f;  // exp() of anything <= this is 0 in fp32
+constexpr int LDH = HD + 8;             // padded smem row (bf16 elements) of 128-wide tiles
+constexpr int LDC = CH + 8;             // ... of 64-wide tiles
+constexpr int LDV = BV + 8;             // ... of BV-wide tiles
+
+struct PDims {
+    int hk, hv, key, inner, qkv;
+    int64_t np, ldp, T, Tp, nc;
+};
+
+PDims pdims(const gdn_dims& d, int64_t T) {
+    PDims r;
+    r.hk = d.num_k_heads;
+    r.hv = d.num_v_heads;
+    r.key = r.hk * HD;
+    r.inner = r.hv * HD;
+    r.qkv = 2 * r.key + r.inner;
+    r.np = (int64_t)r.qkv + r.inner + 2 * r.hv;
+    r.ldp = (r.np + 3) / 4 * 4;
+    r.T = T;
+    r.nc = (T + CH - 1) / CH;
+    r.Tp = r.nc * CH;
+    return r;
+}
+
+struct PWork {
+    float* proj;      // [T][ldp] raw projections
+    void* xconv;      // [T][hidden] fp16 operand copy of x
+    float* partial;   // split-K partials of the gate rows
+    size_t partial_bytes;
+    bf16 *qn, *kn;    // [Hk][Tp][128] conv'd, SiLU'd, L2-normalised
+    bf16* vb;         // [Hv][Tp][128] conv'd, SiLU'd
+    float *glog, *beta, *gcum;  // [Hv][Tp]
+    float* gchunk;    // [Hv][nc] gam_63 of every chunk
+    bf16 *wp, *up, *ek;  // [Hv][Tp][128] W', U', e*K
+    bf16* sc;         // [Hv][nc][128][128] state at each chunk start
+    bf16* dl;         // [Hv][Tp][128] chunk deltas D
+    __half* gated;    // [T][inner] out_proj operand
+    size_t total;
+};
+
+constexpr int kGateSplits = 4;
+
+PWork pcarve(const gdn_dims& d, int64_t T, void* base) {
+    const PDims D = pdims(d, T);
+    PWork w;
+    char* p = static_cast<char*>(base);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char* r = p ? p + off : nullptr;
+        off += round_up(bytes, 256);
+        return r;
+    };
+    w.proj = reinterpret_cast<float*>(take((size_t)T * D.ldp * 4));
+    w.xconv = take((size_t)T * d.hidden * 2);
+    w.partial_bytes = gemm_tc_workspace_bytes(T, 2 * D.hv, kGateSplits);
+    w.partial = reinterpret_cast<float*>(take(w.partial_bytes));
+    const size_t kv = (size_t)D.Tp * HD * 2;
+    w.qn = reinterpret_cast<bf16*>(take(kv * D.hk));
+    w.kn = reinterpret_cast<bf16*>(take(kv * D.hk));
+    w.vb = reinterpret_cast<bf16*>(take(kv * D.hv));
+    w.glog = reinterpret_cast<float*>(take((size_t)D.Tp * D.hv * 4));
+    w.beta = reinterpret_cast<float*>(take((size_t)D.Tp * D.hv * 4));
+    w.gcum = reinterpret_cast<float*>(take((size_t)D.Tp * D.hv * 4));
+    w.gchunk = reinterpret_cast<float*>(take((size_t)D.nc * D.hv * 4));
+    w.wp = reinterpret_cast<bf16*>(take(kv * D.hv));
+    w.up = reinterpret_cast<bf16*>(take(kv * D.hv));
+    w.ek = reinterpret_cast<bf16*>(take(kv * D.hv));
+    w.sc = reinterpret_cast<bf16*>(take((size_t)D.nc * D.hv * HD * HD * 2));
+    w.dl = reinterpret_cast<bf16*>(take(kv * D.hv));
+    w.gated = reinterpret_cast<__half*>(take((size_t)T * D.inner * 2));
+    w.total = off;
+    return w;
+}
+
+// ------------------------------------------------------------------ prep
+//
+// One warp per (token t, 128-channel chunk hc of qkv); lane l owns channels
+// 4l..4l+3.  Causal conv1d over tokens t-3..t (taps k = 0 oldest .. 3 = t),
+// where tokens before the prompt come from the conv window of the state:
+// token -j (j = 1..3) sits in slot (p0 - j) mod 4 (deltanet_impl.h:220-230).
+// Then SiLU; q/k chunks are L2-normalised (double sum, deltanet_impl.h:85-91).
+// Padding tokens (t >= T) are written as zeros.
+__global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T,
+                                                           int64_t Tp, const float* __restrict__ conv_buf,
+                                                           const int32_t* __restrict__ conv_pos,
+                                                           const float* __restrict__ conv_w, bf16* __restrict__ qn,
+                                                           bf16* __restrict__ kn, bf16* __restrict__ vb, int qkv,
+                                                           int hk) {
+    const int lane = threadIdx.x & 31;
+    const int nchunk = qkv / HD;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (gw >= Tp * nchunk) return;
+    const int64_t t = gw / nchunk;
+    const int hc = (int)(gw % nchunk);
+    bf16* dst;
+    if (hc < hk) dst = qn + ((int64_t)hc * Tp + t) * HD;
+    else if (hc < 2 * hk) dst = kn + ((int64_t)(hc - hk) * Tp + t) * HD;
+    else dst = vb + ((int64_t)(hc - 2 * hk) * Tp + t) * HD;
+    dst += 4 * lane;
+    if (t >= T) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(0u, 0u);
+        return;
+    }
+    const int ch = hc * HD + 4 * lane;
+    float4 xv = *reinterpret_cast<const float4*>(proj + t * ldp + ch);
+    if (conv_buf != nullptr && conv_w != nullptr) {
+        const int p0 = *conv_pos;
+        float4 hist[3];
+#pragma unroll
+        for (int j = 0; j < 3; j++) {  // hist[j] = raw projection of token t - 3 + j
+            const int64_t tt = t - 3 + j;
+            hist[j] = tt >= 0 ? *reinterpret_cast<const float4*>(proj + tt * ldp + ch)
+                              : *reinterpret_cast<const float4*>(conv_buf + (int64_t)((p0 + (int)tt) & 3) * qkv + ch);
+        }
+        const float4* wv = reinterpret_cast<const float4*>(conv_w) + ch;
+        float in[4] = {xv.x, xv.y, xv.z, xv.w};
+        const float h0[4] = {hist[0].x, hist[0].y, hist[0].z, hist[0].w};
+        const float h1[4] = {hist[1].x, hist[1].y, hist[1].z, hist[1].w};
+        const float h2[4] = {hist[2].x, hist[2].y, hist[2].z, hist[2].w};
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const float4 w = wv[c];
+            float sum = 0.0f;
+            sum = __fadd_rn(sum, __fmul_rn(w.x, h0[c]));
+            sum = __fadd_rn(sum, __fmul_rn(w.y, h1[c]));
+            sum = __fadd_rn(sum, __fmul_rn(w.z, h2[c]));
+            sum = __fadd_rn(sum, __fmul_rn(w.w, in[c]));
+            const float sig = 1.0f / (1.0f + expf(-sum));
+            in[c] = __fmul_rn(sum, sig);
+        }
+        xv = make_float4(in[0], in[1], in[2], in[3]);
+    }
+    if (hc < 2 * hk) {
+        double ss = (double)xv.x * xv.x + (double)xv.y * xv.y + (double)xv.z * xv.z + (double)xv.w * xv.w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / (sqrtf((float)ss) + 1e-6f);
+        xv = make_float4(__fmul_rn(xv.x, inv), __fmul_rn(xv.y, inv), __fmul_rn(xv.z, inv), __fmul_rn(xv.w, inv));
+    }
+    *reinterpret_cast<uint2*>(dst) = make_uint2(wmma16::pack_bf16(xv.x, xv.y), wmma16::pack_bf16(xv.z, xv.w));
+}
+
+// Gates per (head h, token t): log decay log(a) = ssm_a * softplus(alpha + dt_bias)
+// with the reference's clamps (a in [0, 1], NaN -> 0.99, no ssm_a/dt_bias -> 0.99;
+// deltanet_impl.h:247-257) kept in log space, and beta = stable sigmoid (260).
+__global__ void prefill_gates_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T, int64_t Tp,
+                                     const float* __restrict__ ssm_a, const float* __restrict__ dt_bias,
+                                     float* __restrict__ glog, float* __restrict__ beta, int qkv, int hv) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= Tp * hv) return;
+    const int h = (int)(i / Tp);
+    const int64_t t = i % Tp;
+    if (t >= T) {
+        glog[i] = 0.0f;
+        beta[i] = 0.0f;
+        return;
+    }
+    const float* pr = proj + t * ldp + qkv + hv * HD;
+    const float beta_raw = pr[h], alpha_raw = pr[hv + h];
+    float gl = logf(0.99f);
+    if (ssm_a != nullptr && dt_bias != nullptr) {
+        const float x = alpha_raw + dt_bias[h];
+        gl = ssm_a[h] * (log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f));
+        if (isnan(gl)) gl = logf(0.99f);
+        gl = fminf(gl, 0.0f);
+    }
+    glog[i] = fmaxf(gl, kLogDecayMin);
+    float bt;
+    if (beta_raw >= 0.0f) {
+        bt = 1.0f / (1.0f + expf(-beta_raw));
+    } else {
+        const float z = expf(beta_raw);
+        bt = z / (1.0f + z);
+    }
+    beta[i] = bt;
+}
+
+// Conv window after the prompt: slot (p0 + i) mod 4 holds the raw projection of
+// token i for the last min(T, 4) tokens; conv_pos advances by T.  Runs after
+// the prep kernel, which read the window as it was.  One block: every thread
+// reads conv_pos before the barrier, thread 0 advances it after.
+__global__ void __launch_bounds__(1024) prefill_window_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T,
+                                                              float* __restrict__ conv_buf,
+                                                              int32_t* __restrict__ conv_pos, int qkv) {
+    const int p0 = *conv_pos;
+    for (int ch = threadIdx.x; ch < qkv; ch += blockDim.x)
+        for (int64_t i = (T > 4 ? T - 4 : 0); i < T; i++)
+            conv_buf[(int64_t)((p0 + (int)i) & 3) * qkv + ch] = proj[i * ldp + ch];
+    __syncthreads();
+    if (threadIdx.x == 0) *conv_pos = p0 + (int32_t)T;
+}
+
+// -------------------------------------------------------- K1: chunk_local
+//
+// grid (nc, Hv), 256 threads.  L = strictly lower b_i exp(G_i - G_j) K K^T from
+// a bf16 tensor-core product; then (I + L) X = R solved by fp32 forward
+// substitution with one thread per column of X: threads 0..127 produce W'
+// (R = diag(b gam) K), threads 128..255 produce U' (R = diag(b) V).  Threads
+// 0..127 also write e*K; the chunk's cumulative G and gam_63 go to HBM.
+struct LocalSmem {
+    bf16 k[CH][LDH];
+    float L[CH][CH];
+    float G[CH], beta[CH];
+};
+
+__global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict__ kn, const bf16* __restrict__ vb,
+                                                          const float* __restrict__ glog,
+                                                          const float* __restrict__ beta, bf16* __restrict__ wp,
+                                                          bf16* __restrict__ up, bf16* __restrict__ ek,
+                                                          float* __restrict__ gcum, float* __restrict__ gchunk,
+                                                          int64_t Tp, int hk, int hv, int head_map) {
+    extern __shared__ uint8_t smem_raw[];
+    LocalSmem& sm = *reinterpret_cast<LocalSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    const int c = blockIdx.x, h = blockIdx.y;
+    const int g = head_map ? (h % hk) : (h / (hv / hk));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t t0 = (int64_t)c * CH;
+    const bf16* kc = kn + ((int64_t)g * Tp + t0) * HD;
+    for (int i = tid; i < CH * HD / 8; i += 256) {
+        const int r = i / (HD / 8), q = i % (HD / 8);
+        wmma16::cp_async16(&sm.k[r][q * 8], kc + r * HD + q * 8);
+    }
+    wmma16::cp_async_commit();
+    if (warp == 0) {  // inclusive cumulative log decay, 2 tokens per lane
+        const float* gl = glog + (int64_t)h * Tp + t0;
+        const float a = gl[2 * lane], b = gl[2 * lane + 1];
+        float s = a + b;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float u = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += u;
+        }
+        float excl = __shfl_up_sync(0xffffffffu, s, 1);
+        if (lane == 0) excl = 0.0f;
+        sm.G[2 * lane] = excl + a;
+        sm.G[2 * lane + 1] = (excl + a) + b;
+    } else if (warp == 1) {
+        sm.beta[2 * lane] = beta[(int64_t)h * Tp + t0 + 2 * lane];
+        sm.beta[2 * lane + 1] = beta[(int64_t)h * Tp + t0 + 2 * lane + 1];
+    }
+    wmma16::cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- L = mask(b_i exp(G_i - G_j) K K^T): warp -> (m tile warp%4, n tiles 4*(warp/4) .. +3)
+    {
+        const int mt = warp & 3, nb = (warp >> 2) * 4;
+        float acc[4][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+            uint32_t a[4];
+            wmma16::load_a(a, &sm.k[0][0], LDH, 16 * mt, 16 * kk);
+#pragma unroll
+            for (int np2 = 0; np2 < 2; np2++) {
+                uint32_t b[4];
+                wmma16::load_b_nk(b, &sm.k[0][0], LDH, 16 * kk, 8 * (nb + 2 * np2));
+                wmma16::mma(acc[2 * np2], a, b[0], b[1]);
+                wmma16::mma(acc[2 * np2 + 1], a, b[2], b[3]);
+            }
+        }
+        const int gq = lane >> 2, qq = lane & 3;
+#pragma unroll
+        for (int n = 0; n < 4; n++) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int i = 16 * mt + gq + ((e >> 1) << 3);
+                const int j = 8 * (nb + n) + 2 * qq + (e & 1);
+                sm.L[i][j] = (j < i) ? sm.beta[i] * expf(sm.G[i] - sm.G[j]) * acc[n][e] : 0.0f;
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- forward substitution, one column per thread
+    const int col = tid & (HD - 1);
+    const bool is_w = tid < HD;
+    float x[CH];
+    const float G63 = sm.G[CH - 1];
+    if (is_w) {
+#pragma unroll
+        for (int i = 0; i < CH; i++) x[i] = sm.beta[i] * expf(sm.G[i]) * __bfloat162float(sm.k[i][col]);
+    } else {
+        const bf16* vc = vb + ((int64_t)h * Tp + t0) * HD + col;
+#pragma unroll
+        for (int i = 0; i < CH; i++) x[i] = sm.beta[i] * __bfloat162float(vc[(int64_t)i * HD]);
+    }
+#pragma unroll
+    for (int i = 1; i < CH; i++) {
+        float s = x[i];
+#pragma unroll
+        for (int kq = 0; kq < i; kq += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(&sm.L[i][kq]);
+            s = fmaf(-l4.x, x[kq], s);
+            if (kq + 1 < i) s = fmaf(-l4.y, x[kq + 1], s);
+            if (kq + 2 < i) s = fmaf(-l4.z, x[kq + 2], s);
+            if (kq + 3 < i) s = fmaf(-l4.w, x[kq + 3], s);
+        }
+        x[i] = s;
+    }
+    bf16* dst = (is_w ? wp : up) + ((int64_t)h * Tp + t0) * HD + col;
+#pragma unroll
+    for (int i = 0; i < CH; i++) dst[(int64_t)i * HD] = __float2bfloat16_rn(x[i]);
+    if (is_w) {
+        bf16* e = ek + ((int64_t)h * Tp + t0) * HD + col;
+#pragma unroll
+        for (int i = 0; i < CH; i++)
+            e[(int64_t)i * HD] = __float2bfloat16_rn(expf(G63 - sm.G[i]) * __bfloat162float(sm.k[i][col]));
+    }
+    if (tid < CH) gcum[(int64_t)h * Tp + t0 + tid] = sm.G[tid];
+    if (tid == 0) gchunk[(int64_t)h * (Tp / CH) + c] = expf(G63);
+}
+
+// --------------------------------------------------------- K2: chunk_scan
+//
+// grid (128 / BV, Hv), 128 threads; sequential over the chunks of the prompt.
+// The state slab S[:, 32 columns] lives in fp32 mma accumulators (warp w owns
+// key rows 32w..32w+31).  Per chunk: S -> bf16 (smem, and HBM as the chunk's
+// start state), D = U' - W' S (warp w: token rows 16w..16w+15), then
+// S = gam_63 S + (e K)^T D.  The next chunk's W', e*K and U' stream in with
+// cp.async while this one is computed.
+struct ScanSmem {
+    bf16 w[2][CH][LDH];
+    bf16 e[2][CH][LDH];
+    bf16 u[2][CH][LDV];
+    bf16 s[HD][LDV];
+    bf16 d[CH][LDV];
+};
+
+__global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict__ wp, const bf16* __restrict__ up,
+                                                         const bf16* __restrict__ ek,
+                                                         const float* __restrict__ gchunk, float* __restrict__ S,
+                                                         bf16* __restrict__ sc, bf16* __restrict__ dl, int64_t Tp,
+                                                         int64_t nc) {
+    extern __shared__ uint8_t smem_raw[];
+    ScanSmem& sm = *reinterpret_cast<ScanSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    const int slab = blockIdx.x, h = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq = lane >> 2, qq = lane & 3;
+    const int v0 = slab * BV;
+    float* Sh = S + (int64_t)h * HD * HD;
+
+    // state slab -> accumulators: acc[mt][n][e] = S[32w + 16mt + gq + 8(e>>1)][v0 + 8n + 2qq + (e&1)]
+    float acc[2][BV / 8][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+        for (int n = 0; n < BV / 8; n++)
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                acc[mt][n][e] =
+                    Sh[(int64_t)(32 * warp + 16 * mt + gq + ((e >> 1) << 3)) * HD + v0 + 8 * n + 2 * qq + (e & 1)];
+
+    auto prefetch = [&](int64_t c, int buf) {
+        const int64_t base = ((int64_t)h * Tp + c * CH) * HD;
+        for (int i = tid; i < CH * HD / 8; i += 128) {
+            const int r = i / (HD / 8), q = i % (HD / 8);
+            wmma16::cp_async16(&sm.w[buf][r][q * 8], wp + base + r * HD + q * 8);
+            wmma16::cp_async16(&sm.e[buf][r][q * 8], ek + base + r * HD + q * 8);
+        }
+        for (int i = tid; i < CH * BV / 8; i += 128) {
+            const int r = i / (BV / 8), q = i % (BV / 8);
+            wmma16::cp_async16(&sm.u[buf][r][q * 8], up + base + r * HD + v0 + q * 8);
+        }
+        wmma16::cp_async_commit();
+    };
+    prefetch(0, 0);
+
+    for (int64_t c = 0; c < nc; c++) {
+        const int buf = (int)(c & 1);
+        // ---- chunk start state: bf16 copy in smem (B operand) and in HBM (for the output kernel)
+        bf16* scc = sc + (((int64_t)h * nc + c) * HD) * HD;
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+            for (int n = 0; n < BV / 8; n++)
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    const int r = 32 * warp + 16 * mt + gq + 8 * hf;
+                    const int cl = 8 * n + 2 * qq;
+                    const uint32_t pk = wmma16::pack_bf16(acc[mt][n][2 * hf], acc[mt][n][2 * hf + 1]);
+                    *reinterpret_cast<uint32_t*>(&sm.s[r][cl]) = pk;
+                    *reinterpret_cast<uint32_t*>(scc + (int64_t)r * HD + v0 + cl) = pk;
+                }
+        if (c + 1 < nc) {
+            prefetch(c + 1, buf ^ 1);
+            wmma16::cp_async_wait<1>();
+        } else {
+            wmma16::cp_async_wait<0>();
+        }
+        __syncthreads();
+
+        // ---- D = U' - W' S   (token rows 16w..16w+15, all BV columns)
+        float dacc[BV / 8][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+            uint32_t a[4];
+            wmma16::load_a(a, &sm.w[buf][0][0], LDH, 16 * warp, 16 * kk);
+#pragma unroll
+            for (int np2 = 0; np2 < BV / 16; np2++) {
+                uint32_t b[4];
+                wmma16::load_b_kn(b, &sm.s[0][0], LDV, 16 * kk, 16 * np2);
+                wmma16::mma(dacc[2 * np2], a, b[0], b[1]);
+                wmma16::mma(dacc[2 * np2 + 1], a, b[2], b[3]);
+            }
+        }
+        bf16* dlc = dl + ((int64_t)h * Tp + c * CH) * HD + v0;
+#pragma unroll
+        for (int n = 0; n < BV / 8; n++)
+#pragma unroll
+            for (int hf = 0; hf < 2; hf++) {
+                const int r = 16 * warp + gq + 8 * hf;
+                const int cl = 8 * n + 2 * qq;
+                const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(&sm.u[buf][r][cl]);
+                const float2 uf = __bfloat1622float2(u2);
+                const uint32_t pk = wmma16::pack_bf16(uf.x - dacc[n][2 * hf], uf.y - dacc[n][2 * hf + 1]);
+                *reinterpret_cast<uint32_t*>(&sm.d[r][cl]) = pk;
+                *reinterpret_cast<uint32_t*>(dlc + (int64_t)r * HD + cl) = pk;
+            }
+        __syncthreads();
+
+        // ---- S = gam_63 S + (e K)^T D   (key rows 32w..32w+31)
+        const float gC = gchunk[(int64_t)h * nc + c];
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+            for (int n = 0; n < BV / 8; n++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) acc[mt][n][e] *= gC;
+#pragma unroll
+        for (int kk = 0; kk < CH / 16; kk++) {
+#pragma unroll
+            for (int mt = 0; mt < 2; mt++) {
+                uint32_t a[4];
+                wmma16::load_a_t(a, &sm.e[buf][0][0], LDH, 32 * warp + 16 * mt, 16 * kk);
+#pragma unroll
+                for (int np2 = 0; np2 < BV / 16; np2++) {
+                    uint32_t b[4];
+                    wmma16::load_b_kn(b, &sm.d[0][0], LDV, 16 * kk, 16 * np2);
+                    wmma16::mma(acc[mt][2 * np2], a, b[0], b[1]);
+                    wmma16::mma(acc[mt][2 * np2 + 1], a, b[2], b[3]);
+                }
+            }
+        }
+        __syncthreads();  // sm.s, sm.d and this buffer are rewritten next chunk
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+        for (int n = 0; n < BV / 8; n++)
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                Sh[(int64_t)(32 * warp + 16 * mt + gq + ((e >> 1) << 3)) * HD + v0 + 8 * n + 2 * qq + (e & 1)] =
+                    acc[mt][n][e];
+}
+
+// ---------------------------------------------------------- K3: chunk_out
+//
+// grid (nc, Hv), 128 threads; warp w owns token rows 16w..16w+15 of the chunk.
+//   P = mask(exp(G_i - G_j) Q K^T)                      (bf16, smem)
+//   O = scale * (diag(gam) Q S0 + P D)                   (fp32 accumulators)
+// then per token: RMSNorm over the head's 128 values times the norm weight
+// (deltanet_impl.h:350-361) and the SiLU(z) gate (364-371) -> fp16 out_proj operand.
+struct OutSmem {
+    bf16 q[CH][LDH];
+    bf16 k[CH][LDH];
+    bf16 s[HD][LDH];
+    bf16 d[CH][LDH];
+    bf16 p[CH][LDC];
+    float G[CH];
+};
+
+__global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__ qn, const bf16* __restrict__ kn,
+                                                        const bf16* __restrict__ sc, const bf16* __restrict__ dl,
+                                                        const float* __restrict__ gcum,
+                                                        const float* __restrict__ proj, int64_t ldp,
+                                                        const float* __restrict__ head_norm,
+                                                        __half* __restrict__ gated, int64_t T, int64_t Tp, int hk,
+                                                        int hv, int qkv, int head_map) {
+    extern __shared__ uint8_t smem_raw[];
+    OutSmem& sm = *reinterpret_cast<OutSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    const int c = blockIdx.x, h = blockIdx.y;
+    const int g = head_map ? (h % hk) : (h / (hv / hk));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq = lane >> 2, qq = lane & 3;
+    const int64_t t0 = (int64_t)c * CH;
+    const int64_t nc = Tp / CH;
+    {
+        const bf16* qc = qn + ((int64_t)g * Tp + t0) * HD;
+        const bf16* kc = kn + ((int64_t)g * Tp + t0) * HD;
+        const bf16* dc = dl + ((int64_t)h * Tp + t0) * HD;
+        const bf16* s0 = sc + (((int64_t)h * nc + c) * HD) * HD;
+        for (int i = tid; i < CH * HD / 8; i += 128) {
+            const int r = i / (HD / 8), q = i % (HD / 8);
+            wmma16::cp_async16(&sm.q[r][q * 8], qc + r * HD + q * 8);
+            wmma16::cp_async16(&sm.k[r][q * 8], kc + r * HD + q * 8);
+            wmma16::cp_async16(&sm.d[r][q * 8], dc + r * HD + q * 8);
+        }
+        for (int i = tid; i < HD * HD / 8; i += 128) {
+            const int r = i / (HD / 8), q = i % (HD / 8);
+            wmma16::cp_async16(&sm.s[r][q * 8], s0 + r * HD + q * 8);
+        }
+        wmma16::cp_async_commit();
+        if (tid < CH) sm.G[tid] = gcum[(int64_t)h * Tp + t0 + tid];
+        wmma16::cp_async_wait<0>();
+        __syncthreads();
+    }
+    const int rA = 16 * warp + gq, rB = rA + 8;  // this thread's two token rows
+    // ---- P = mask(exp(G_i - G_j) Q K^T), only this warp's rows
+    {
+        float pacc[CH / 8][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+            uint32_t a[4];
+            wmma16::load_a(a, &sm.q[0][0], LDH, 16 * warp, 16 * kk);
+#pragma unroll
+            for (int np2 = 0; np2 < CH / 16; np2++) {
+                uint32_t b[4];
+                wmma16::load_b_nk(b, &sm.k[0][0], LDH, 16 * kk, 16 * np2);
+                wmma16::mma(pacc[2 * np2], a, b[0], b[1]);
+                wmma16::mma(pacc[2 * np2 + 1], a, b[2], b[3]);
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < CH / 8; n++) {
+            const int j = 8 * n + 2 * qq;
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int i = (e >> 1) ? rB : rA, jj = j + (e & 1);
+                v[e] = (jj <= i) ? expf(sm.G[i] - sm.G[jj]) * pacc[n][e] : 0.0f;
+            }
+            *reinterpret_cast<uint32_t*>(&sm.p[rA][j]) = wmma16::pack_bf16(v[0], v[1]);
+            *reinterpret_cast<uint32_t*>(&sm.p[rB][j]) = wmma16::pack_bf16(v[2], v[3]);
+        }
+    }
+    __syncwarp();
+    // ---- O = diag(gam) Q S0 + P D
+    float o[HD / 8][4] = {};
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; kk++) {
+        uint32_t a[4];
+        wmma16::load_a(a, &sm.q[0][0], LDH, 16 * warp, 16 * kk);
+#pragma unroll
+        for (int np2 = 0; np2 < HD / 16; np2++) {
+            uint32_t b[4];
+            wmma16::load_b_kn(b, &sm.s[0][0], LDH, 16 * kk, 16 * np2);
+            wmma16::mma(o[2 * np2], a, b[0], b[1]);
+            wmma16::mma(o[2 * np2 + 1], a, b[2], b[3]);
+        }
+    }
+    const float gamA = expf(sm.G[rA]), gamB = expf(sm.G[rB]);
+#pragma unroll
+    for (int n = 0; n < HD / 8; n++) {
+        o[n][0] *= gamA;
+        o[n][1] *= gamA;
+        o[n][2] *= gamB;
+        o[n][3] *= gamB;
+    }
+#pragma unroll
+    for (int kk = 0; kk < CH / 16; kk++) {
+        uint32_t a[4];
+        wmma16::load_a(a, &sm.p[0][0], LDC, 16 * warp, 16 * kk);
+#pragma unroll
+        for (int np2 = 0; np2 < HD / 16; np2++) {
+            uint32_t b[4];
+            wmma16::load_b_kn(b, &sm.d[0][0], LDH, 16 * kk, 16 * np2);
+            wmma16::mma(o[2 * np2], a, b[0], b[1]);
+            wmma16::mma(o[2 * np2 + 1], a, b[2], b[3]);
+        }
+    }
+    // ---- scale, per-token RMSNorm over the head, SiLU(z) gate
+    const float scale = 1.0f / sqrtf((float)HD);
+    double ssA = 0.0, ssB = 0.0;
+#pragma unroll
+    for (int n = 0; n < HD / 8; n++) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[n][e] = __fmul_rn(o[n][e], scale);
+        ssA += (double)o[n][0] * o[n][0] + (double)o[n][1] * o[n][1];
+        ssB += (double)o[n][2] * o[n][2] + (double)o[n][3] * o[n][3];
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+        ssA += __shfl_xor_sync(0xffffffffu, ssA, off);
+        ssB += __shfl_xor_sync(0xffffffffu, ssB, off);
+    }
+    const float invA = 1.0f / sqrtf((float)(ssA / HD) + 1e-6f);
+    const float invB = 1.0f / sqrtf((float)(ssB / HD) + 1e-6f);
+    const int inner = hv * HD;
+#pragma unroll
+    for (int hf = 0; hf < 2; hf++) {
+        const int64_t t = t0 + (hf ? rB : rA);
+        if (t >= T) continue;
+        const float inv = hf ? invB : invA;
+        const float* z = proj + t * ldp + qkv + h * HD;
+        __half* gout = gated + t * inner + h * HD;
+#pragma unroll
+        for (int n = 0; n < HD / 8; n++) {
+            const int v = 8 * n + 2 * qq;
+            const float2 zz = *reinterpret_cast<const float2*>(z + v);
+            float r2[2];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                float nv = __fmul_rn(o[n][2 * hf + e], inv);
+                if (head_norm != nullptr) nv = __fmul_rn(nv, head_norm[v + e]);
+                float zv = e ? zz.y : zz.x;
+                zv = fminf(fmaxf(zv, -88.0f), 88.0f);
+                r2[e] = __fmul_rn(nv, zv / (1.0f + expf(-zv)));
+            }
+            *reinterpret_cast<__half2*>(gout + v) = __floats2half2_rn(r2[0], r2[1]);
+        }
+    }
+}
+
+template <typename K>
+int set_smem(K kern, size_t bytes) {
+    GDN_CUDA(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    return GDN_OK;
+}
+
+}  // namespace
+
+size_t prefill_workspace_bytes(const gdn_dims& d, int64_t T) { return pcarve(d, T, nullptr).total; }
+
+int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
+            int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s) {
+    int st = validate_layer(L);
+    if (st) return st;
+    if (T <= 0 || T > (int64_t)1 << 26) return fail(GDN_ERR_SHAPE, "T must be in [1, 2^26] (got %lld)", (long long)T);
+    if (!x || !out || !S || !conv_pos) return fail(GDN_ERR_ARG, "x, out, S and conv_pos must be non-NULL");
+    if (x_dtype != GDN_DTYPE_F32 && x_dtype != GDN_DTYPE_BF16 && x_dtype != GDN_DTYPE_F16)
+        return fail(GDN_ERR_TYPE, "x_dtype %d is not supported", x_dtype);
+    if (!aligned(out, 16) || !aligned(S, 16)) return fail(GDN_ERR_ARG, "out and S must be 16-byte aligned");
+    const gdn_dims& d = L->dims;
+    const size_t need = prefill_workspace_bytes(d, T);
+    if (wsp == nullptr || ws_bytes < need || !aligned(wsp, 256))
+        return fail(GDN_ERR_ARG, "workspace must be 256-aligned and hold %zu bytes (got %zu)", need, ws_bytes);
+    const PDims D = pdims(d, T);
+    const PWork W = pcarve(d, T, wsp);
+    const bool conv = (L->conv1d_w != nullptr && conv_buf != nullptr);
+    const int64_t hidden = d.hidden;
+
+    // ---- input projection -> proj [T][ldp]
+    if (L->weight_type == GDN_GGML_Q4_K) {
+        st = launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, T, W.proj, D.ldp, s);
+        if (st) return st;
+    } else {
+        const void* a = x;
+        if (x_dtype != GDN_DTYPE_F16 || !aligned(x, 16)) {
+            if ((st = launch_convert(x, x_dtype, W.xconv, false, T * hidden, s))) return st;
+            a = W.xconv;
+        }
+        const int64_t n_main = (int64_t)D.qkv + D.inner;
+        TcOptions fast;  // q, k, v, z rows: one fp16 weight operand
+        if ((st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_main, hidden, a, false, T, W.proj, D.ldp, fast, s)))
+            return st;
+        const int8_t* gq = L->in_qs + n_main * hidden;
+        const uint16_t* gd = L->in_d + n_main * (hidden / 32);
+        if (x_dtype == GDN_DTYPE_F32) {
+            // the fp16 copy of fp32 x is rounded: the gate rows stay on fp32 CUDA cores
+            st = launch_q8_0_gemv(gq, gd, 2 * D.hv, hidden, x, x_dtype, T, W.proj + n_main, D.ldp, s);
+        } else {
+            TcOptions exact;  // beta/alpha rows: exact hi + lo weights (exp(ssm_a * softplus(alpha)) is sensitive)
+            exact.split_precision = true;
+            exact.splits = kGateSplits;
+            exact.workspace = W.partial;
+            exact.workspace_bytes = W.partial_bytes;
+            st = launch_q8_0_gemm_tc(gq, gd, 2 * D.hv, hidden, a, false, T, W.proj + n_main, D.ldp, exact, s);
+        }
+        if (st) return st;
+    }
+
+    // ---- conv1d + SiLU + L2 norm, gates, window hand-off
+    {
+        const int64_t warps = D.Tp * (D.qkv / HD);
+        prefill_prep_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(
+            W.proj, D.ldp, T, D.Tp, conv ? conv_buf : nullptr, conv_pos, conv ? L->conv1d_w : nullptr, W.qn, W.kn,
+            W.vb, D.qkv, D.hk);
+        GDN_LAUNCH_CHECK("prefill_prep_kernel");
+        const int64_t n = D.Tp * D.hv;
+        prefill_gates_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W.proj, D.ldp, T, D.Tp, L->ssm_a,
+                                                                           L->dt_bias, W.glog, W.beta, D.qkv, D.hv);
+        GDN_LAUNCH_CHECK("prefill_gates_kernel");
+        if (conv) {
+            prefill_window_kernel<<<1, 1024, 0, s>>>(W.proj, D.ldp, T, conv_buf, conv_pos, D.qkv);
+            GDN_LAUNCH_CHECK("prefill_window_kernel");
+        }
+    }
+
+    // ---- chunked recurrence
+    {
+        const size_t sm1 = sizeof(LocalSmem) + 128;
+        if ((st = set_smem(chunk_local_kernel, sm1))) return st;
+        chunk_local_kernel<<<dim3((unsigned)D.nc, (unsigned)D.hv), 256, sm1, s>>>(
+            W.kn, W.vb, W.glog, W.beta, W.wp, W.up, W.ek, W.gcum, W.gchunk, D.Tp, D.hk, D.hv, L->head_map);
+        GDN_LAUNCH_CHECK("chunk_local_kernel");
+        const size_t sm2 = sizeof(ScanSmem) + 128;
+        if ((st = set_smem(chunk_scan_kernel, sm2))) return st;
+        chunk_scan_kernel<<<dim3(HD / BV, (unsigned)D.hv), 128, sm2, s>>>(W.wp, W.up, W.ek, W.gchunk, S, W.sc, W.dl,
+                                                                          D.Tp, D.nc);
+        GDN_LAUNCH_CHECK("chunk_scan_kernel");
+        const size_t sm3 = sizeof(OutSmem) + 128;
+        if ((st = set_smem(chunk_out_kernel, sm3))) return st;
+        chunk_out_kernel<<<dim3((unsigned)D.nc, (unsigned)D.hv), 128, sm3, s>>>(
+            W.qn, W.kn, W.sc, W.dl, W.gcum, W.proj, D.ldp, L->head_norm, W.gated, T, D.Tp, D.hk, D.hv, D.qkv,
+            L->head_map);
+        GDN_LAUNCH_CHECK("chunk_out_kernel");
+    }
+
+    // ---- output projection
+    if (L->weight_type == GDN_GGML_Q4_K)
+        return launch_q4_k_gemv(L->out_blocks, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
+    TcOptions fast;
+    if (T >= 64) return launch_q8_0_gemm_tc(L->out_qs, L->out_d, hidden, D.inner, W.gated, false, T, out, hidden, fast, s);
+    return launch_q8_0_gemv(L->out_qs, L->out_d, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
+}
+
+}  // namespace gdn

@@ -1,0 +1,12 @@
+// Chunked prefill (prefill.cu).
+#pragma once
+#include "gdn_common.cuh"
+
+namespace gdn {
+
+size_t prefill_workspace_bytes(const gdn_dims& d, int64_t T);
+int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
+            int32_t* conv_pos, void* ws, size_t ws_bytes, cudaStream_t s);
+int validate_layer(const gdn_layer* L);
+
+}  // namespace gdn

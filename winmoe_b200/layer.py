@@ -8,6 +8,7 @@ all arithmetic runs in the library's CUDA kernels.
   DeltaNetWeights   one layer's weights on the device (Q8_0 planes or Q4_K blocks)
   DeltaNetState     S [B][Hv][d][d], conv window [B][4][QKV], conv_pos [B]
   decode_step       one token for B sequences (gdn_decode_step)
+  prefill           T prompt tokens of one sequence, chunked (gdn_prefill)
   deltanet_forward  the reference's own signature, one token of one sequence
 """
 from __future__ import annotations
@@ -199,6 +200,39 @@ def decode_step(w: DeltaNetWeights, state: DeltaNetState, x: torch.Tensor, out: 
     check(lib().gdn_decode_step(C.byref(w.struct()), B, x.data_ptr(), _act_dtype(x), out.data_ptr(),
                                 state.S.data_ptr(), state.conv_buf.data_ptr(), state.conv_pos.data_ptr(),
                                 base, nbytes, _stream(stream, x.device)))
+    return out
+
+
+def prefill_workspace(cfg: GDNConfig, T: int, device) -> torch.Tensor:
+    """Cached scratch for gdn_prefill (allocated by torch, outside the C ABI)."""
+    device = torch.device(device)
+    dims = _lib.gdn_dims(cfg.hidden, cfg.num_k_heads, cfg.num_v_heads, cfg.head_dim)
+    need = lib().gdn_prefill_workspace_size(C.byref(dims), T)
+    key = (device, "prefill", need)
+    ws = _ws_cache.get(key)
+    if ws is None:
+        ws = torch.empty(need + 256, dtype=torch.uint8, device=device)
+        _ws_cache[key] = ws
+    return ws
+
+
+def prefill(w: DeltaNetWeights, state: DeltaNetState, x: torch.Tensor, seq: int = 0,
+            out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """T prompt tokens of sequence `seq` of `state` (chunked WY form): x [T][hidden]
+    -> out [T][hidden] fp32; the sequence's S, conv window and conv_pos end up
+    as after T deltanet_forward calls, ready for decode_step."""
+    cfg = w.cfg
+    if x.dim() != 2 or x.shape[1] != cfg.hidden or not x.is_cuda or not x.is_contiguous():
+        raise GDNError(-2, f"x must be a contiguous CUDA tensor of shape (T, {cfg.hidden})")
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty((T, cfg.hidden), dtype=torch.float32, device=x.device)
+    ws = prefill_workspace(cfg, T, x.device)
+    base = (ws.data_ptr() + 255) // 256 * 256
+    nbytes = ws.numel() - (base - ws.data_ptr())
+    check(lib().gdn_prefill(C.byref(w.struct()), T, x.data_ptr(), _act_dtype(x), out.data_ptr(),
+                            state.S[seq].data_ptr(), state.conv_buf[seq].data_ptr(), state.conv_pos[seq:].data_ptr(),
+                            base, nbytes, _stream(stream, x.device)))
     return out
 
 
