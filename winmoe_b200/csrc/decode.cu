@@ -301,7 +301,7 @@ inline int mark(PhaseEvents* pe, int i, cudaStream_t s) {
 // Tensor-core projections pay off once a batch fills an M=128 tile reasonably.
 constexpr int64_t kTcMinBatch = 64;
 // Split-K factor of the tensor-core out_proj (K = inner is long, N = hidden short).
-constexpr int kOutSplits = 4;
+constexpr int kOutSplits = 8;
 
 struct Dims {
     int hv, hk, key, inner, qkv;
@@ -355,6 +355,8 @@ Workspace carve(const gdn_dims& d, int64_t B, void* base) {
     return w;
 }
 }  // namespace
+
+int phase_mark(int i, cudaStream_t s) { return mark(phase_events(), i, s); }
 
 int profile_enable(int on) {
     int dev = 0;

@@ -28,6 +28,7 @@
 
 #include "gdn_common.cuh"
 #include "quant.cuh"
+#include "decode.cuh"
 #include "prefill.cuh"
 #include "warp_mma.cuh"
 
@@ -682,6 +683,7 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     const int64_t hidden = d.hidden;
 
     // ---- input projection -> proj [T][ldp]
+    if ((st = phase_mark(0, s))) return st;
     if (L->weight_type == GDN_GGML_Q4_K) {
         st = launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, T, W.proj, D.ldp, s);
         if (st) return st;
@@ -712,6 +714,7 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     }
 
     // ---- conv1d + SiLU + L2 norm, gates, window hand-off
+    if ((st = phase_mark(1, s))) return st;
     {
         const int64_t warps = D.Tp * (D.qkv / HD);
         prefill_prep_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(
@@ -729,6 +732,7 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     }
 
     // ---- chunked recurrence
+    if ((st = phase_mark(2, s))) return st;
     {
         const size_t sm1 = sizeof(LocalSmem) + 128;
         if ((st = set_smem(chunk_local_kernel, sm1))) return st;
@@ -749,11 +753,17 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     }
 
     // ---- output projection
-    if (L->weight_type == GDN_GGML_Q4_K)
-        return launch_q4_k_gemv(L->out_blocks, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
-    TcOptions fast;
-    if (T >= 64) return launch_q8_0_gemm_tc(L->out_qs, L->out_d, hidden, D.inner, W.gated, false, T, out, hidden, fast, s);
-    return launch_q8_0_gemv(L->out_qs, L->out_d, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
+    if ((st = phase_mark(3, s))) return st;
+    if (L->weight_type == GDN_GGML_Q4_K) {
+        st = launch_q4_k_gemv(L->out_blocks, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
+    } else if (T >= 64) {
+        TcOptions fast;
+        st = launch_q8_0_gemm_tc(L->out_qs, L->out_d, hidden, D.inner, W.gated, false, T, out, hidden, fast, s);
+    } else {
+        st = launch_q8_0_gemv(L->out_qs, L->out_d, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
+    }
+    if (st) return st;
+    return phase_mark(4, s);
 }
 
 }  // namespace gdn
