@@ -19,14 +19,17 @@
 //            summation order (the decode path's 1e-3 parity bound).
 //
 // One CTA computes MT x 128 rows (tokens) by BN columns (weight rows) over its
-// K range in BK = 64 steps, through a STAGES-deep ring:
-//   warp 0     TMA producer: MT activation tiles (128B swizzle) + int8 weight tile
-//   warp 1     TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
-//   warps 2-9  dequant int8 -> operand type into the swizzled B tile(s), shared
-//              by the MT activation tiles; then the epilogue (tcgen05.ld TMEM ->
-//              registers -> global fp32), two warps per TMEM lane quadrant
-// Barriers: full[s] (TMA bytes landed), deq[s] (256 dequant arrivals),
-// empty[s] (MMA done reading stage s, via tcgen05.commit), accf (all MMAs done).
+// K range in BK = 64 steps:
+//   warp 0      TMA producer of the activation tiles (128B swizzle)
+//   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
+//   warp 2      TMA producer of the int8 weight tiles
+//   warps 3-10  dequant int8 -> operand type into the swizzled B tile(s), shared
+//               by the MT activation tiles; then the epilogue (tcgen05.ld TMEM ->
+//               registers -> global fp32), two warps per TMEM lane quadrant
+// The three rings (activation, dequantised weight, raw weight) have separate
+// full/empty mbarriers, so the raw weight slot is refilled as soon as the
+// dequant warps have read it rather than after the MMA -- the weight stream
+// from HBM runs several k-tiles ahead of the tensor cores.
 // Split-K (grid.z > 1) writes fp32 partials that a second kernel sums in a
 // fixed order, so results do not depend on scheduling.
 #include <cuda.h>
@@ -44,20 +47,26 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kDeqThreads = 256;
-constexpr int kThreads = 64 + kDeqThreads;
+constexpr int kDeqWarp0 = 3;  // warps 0: A producer, 1: MMA issuer + TMEM owner, 2: weight producer
+constexpr int kThreads = 32 * kDeqWarp0 + kDeqThreads;
 constexpr int kWin = 8;  // k-tiles per scale window (16 fp16 scales = 32 bytes per row)
 
-template <int BN, int MT, int STAGES, bool SPLIT>
+// Shared memory: three rings, each with its own depth --
+//   A   [SA]  MT activation tiles (128 x 64, 128B-swizzled), freed by the MMA
+//   B16 [S16] the dequantised weight tile(s) (hi, and lo when split), freed by the MMA
+//   B8  [S8]  the raw int8 weight tile, freed as soon as the dequant warps have read it
+template <int BN, int MT, int SA, int S16, int S8, bool SPLIT>
 struct TcLayout {
     static constexpr uint32_t A_BYTES = BM * BK * 2;  // one 128-row activation tile
     static constexpr uint32_t B16_BYTES = BN * BK * 2;
     static constexpr uint32_t B8_BYTES = BN * BK;
     static constexpr int NB = SPLIT ? 2 : 1;
     static constexpr uint32_t A_OFF = 0;
-    static constexpr uint32_t B16_OFF = A_OFF + STAGES * MT * A_BYTES;
-    static constexpr uint32_t B8_OFF = B16_OFF + STAGES * NB * B16_BYTES;
-    static constexpr uint32_t BAR_OFF = B8_OFF + STAGES * B8_BYTES;
-    static constexpr uint32_t NBARS = 3 * STAGES + 1;
+    static constexpr uint32_t B16_OFF = A_OFF + SA * MT * A_BYTES;
+    static constexpr uint32_t B8_OFF = B16_OFF + S16 * NB * B16_BYTES;
+    static constexpr uint32_t BAR_OFF = B8_OFF + S8 * B8_BYTES;
+    // a_full[SA] a_empty[SA] b16_full[S16] b16_empty[S16] b8_full[S8] b8_empty[S8] accf
+    static constexpr uint32_t NBARS = 2 * SA + 2 * S16 + 2 * S8 + 1;
     static constexpr uint32_t TMEM_SLOT_OFF = BAR_OFF + NBARS * 8;
     static constexpr uint32_t BYTES = TMEM_SLOT_OFF + 16;
     static constexpr size_t SMEM = BYTES + 1024;  // + alignment slack
@@ -135,19 +144,23 @@ __device__ __forceinline__ void store_chunk(uint8_t* tile, int rr, int c, const 
     *reinterpret_cast<uint4*>(row + (((2 * c + 1) ^ (rr & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-template <int BN, int MT, int STAGES, bool BF16, bool SPLIT>
+template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     q8_0_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const uint16_t* __restrict__ dsc, int n, int k, int m, float* __restrict__ y, int64_t ldy,
                         int kt_per_split, uint32_t* __restrict__ err) {
-    using L = TcLayout<BN, MT, STAGES, SPLIT>;
+    using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    auto full_bar = [&](int s) { return sbase + L::BAR_OFF + 8u * s; };
-    auto deq_bar = [&](int s) { return sbase + L::BAR_OFF + 8u * (STAGES + s); };
-    auto empty_bar = [&](int s) { return sbase + L::BAR_OFF + 8u * (2 * STAGES + s); };
-    const uint32_t accf_bar = sbase + L::BAR_OFF + 8u * (3 * STAGES);
+    const uint32_t bar0 = sbase + L::BAR_OFF;
+    auto a_full = [&](int s) { return bar0 + 8u * s; };
+    auto a_empty = [&](int s) { return bar0 + 8u * (SA + s); };
+    auto b16_full = [&](int s) { return bar0 + 8u * (2 * SA + s); };
+    auto b16_empty = [&](int s) { return bar0 + 8u * (2 * SA + S16 + s); };
+    auto b8_full = [&](int s) { return bar0 + 8u * (2 * SA + 2 * S16 + s); };
+    auto b8_empty = [&](int s) { return bar0 + 8u * (2 * SA + 2 * S16 + S8 + s); };
+    const uint32_t accf_bar = bar0 + 8u * (2 * SA + 2 * S16 + 2 * S8);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::TMEM_SLOT_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -157,10 +170,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int KT = min(kt_per_split, KT_total - kt0);  // k-tiles of this CTA (>= 1 by construction)
 
     if (warp == 0 && lane == 0) {
-        for (int s = 0; s < STAGES; s++) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(deq_bar(s), kDeqThreads);
-            mbar_init(empty_bar(s), 1);
+        for (int s = 0; s < SA; s++) {
+            mbar_init(a_full(s), 1);
+            mbar_init(a_empty(s), 1);
+        }
+        for (int s = 0; s < S16; s++) {
+            mbar_init(b16_full(s), kDeqThreads);
+            mbar_init(b16_empty(s), 1);
+        }
+        for (int s = 0; s < S8; s++) {
+            mbar_init(b8_full(s), 1);
+            mbar_init(b8_empty(s), kDeqThreads);
         }
         mbar_init(accf_bar, 1);
         fence_barrier_init();
@@ -176,40 +196,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp == 0 || warp == 2) {
+        // ---- producers: warp 0 streams activation tiles, warp 2 int8 weight tiles
         if (lane == 0) {
+            const bool is_a = (warp == 0);
+            const int depth = is_a ? SA : S8;
             int issued = 0;
             bool ok = true;
-            for (int t = 0; t < KT && ok; t++) {
-                const int s = t % STAGES, r = t / STAGES;
-                if (t >= STAGES) ok = mbar_wait(empty_bar(s), (r - 1) & 1, err);
+            for (int t = 0; t < KT; t++) {
+                const int s = t % depth, r = t / depth;
+                if (t >= depth) ok = mbar_wait(is_a ? a_empty(s) : b8_empty(s), (r - 1) & 1, err);
                 if (!ok) break;
-                mbar_arrive_expect_tx(full_bar(s), MT * L::A_BYTES + L::B8_BYTES);
+                if (is_a) {
+                    mbar_arrive_expect_tx(a_full(s), MT * L::A_BYTES);
 #pragma unroll
-                for (int mt = 0; mt < MT; mt++)
-                    tma_load_2d(sbase + L::A_OFF + (s * MT + mt) * L::A_BYTES, &tm_a, (kt0 + t) * BK, m0 + mt * BM,
-                                full_bar(s));
-                tma_load_2d(sbase + L::B8_OFF + s * L::B8_BYTES, &tm_b, (kt0 + t) * BK, n0, full_bar(s));
+                    for (int mt = 0; mt < MT; mt++)
+                        tma_load_2d(sbase + L::A_OFF + (s * MT + mt) * L::A_BYTES, &tm_a, (kt0 + t) * BK,
+                                    m0 + mt * BM, a_full(s));
+                } else {
+                    mbar_arrive_expect_tx(b8_full(s), L::B8_BYTES);
+                    tma_load_2d(sbase + L::B8_OFF + s * L::B8_BYTES, &tm_b, (kt0 + t) * BK, n0, b8_full(s));
+                }
                 issued++;
             }
             if (!ok) {
                 // Give the loads already issued a bounded chance to land before exit.
-                for (int t = (issued > STAGES ? issued - STAGES : 0); t < issued; t++)
-                    mbar_wait(full_bar(t % STAGES), (t / STAGES) & 1, err);
+                for (int t = (issued > depth ? issued - depth : 0); t < issued; t++)
+                    mbar_wait(is_a ? a_full(t % depth) : b8_full(t % depth), (t / depth) & 1, err);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16(BM, BN, BF16);
             for (int t = 0; t < KT; t++) {
-                const int s = t % STAGES, r = t / STAGES;
-                // the A tiles (TMA) and the dequantised B tile(s) of this stage
-                if (!(mbar_wait(full_bar(s), r & 1, err) && mbar_wait(deq_bar(s), r & 1, err))) break;
+                const int sa = t % SA, s16 = t % S16;
+                if (!(mbar_wait(a_full(sa), (t / SA) & 1, err) && mbar_wait(b16_full(s16), (t / S16) & 1, err)))
+                    break;
                 tc_fence_after();
-                const uint32_t b0 = sbase + L::B16_OFF + s * L::NB * L::B16_BYTES;
+                const uint32_t b0 = sbase + L::B16_OFF + s16 * L::NB * L::B16_BYTES;
 #pragma unroll
                 for (int mt = 0; mt < MT; mt++) {
-                    const uint32_t a0 = sbase + L::A_OFF + (s * MT + mt) * L::A_BYTES;
+                    const uint32_t a0 = sbase + L::A_OFF + (sa * MT + mt) * L::A_BYTES;
                     const uint32_t acc_col = tmem + (uint32_t)(mt * L::NB * BN);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++) {
@@ -220,41 +247,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                             mma_f16_ss(acc_col + BN, ad, umma_desc_sw128(b0 + L::B16_BYTES + kk * 32), idesc, acc);
                     }
                 }
-                mma_commit(empty_bar(s));
+                mma_commit(a_empty(sa));
+                mma_commit(b16_empty(s16));
             }
             mma_commit(accf_bar);
         }
     } else {
-        // ---- dequant: BN rows x 4 chunks of 16 per stage over 256 threads
-        constexpr int UNITS = BN * 4 / kDeqThreads;  // (row, chunk) units per thread: 1 or 2 or 4
-        constexpr int CPT = UNITS < 4 ? UNITS : 4;   // chunks of one row per thread
-        constexpr int RPT = UNITS / CPT;             // rows per thread
-        const int i = threadIdx.x - 64;
+        // ---- dequant: BN rows x 4 chunks of 16 per k-tile over 256 threads
+        constexpr int UNITS = BN * 4 / kDeqThreads;  // (row, chunk) units per thread: 1, 2 or 4
+        constexpr int CPT = UNITS;                   // chunks of one row per thread
+        const int i = threadIdx.x - 32 * kDeqWarp0;
         const int kb = k >> 5;
-        int rows[RPT], c0;
-        const uint16_t* drow[RPT];
-#pragma unroll
-        for (int j = 0; j < RPT; j++) {
-            rows[j] = (RPT == 1) ? i / (4 / CPT) : i + kDeqThreads * j;
-            const int gr = n0 + rows[j];
-            drow[j] = gr < n ? dsc + (int64_t)gr * kb + 2 * kt0 : nullptr;
-        }
-        c0 = (RPT == 1) ? (i % (4 / CPT)) * CPT : 0;
+        const int rr = i / (4 / CPT);
+        const int c0 = (i % (4 / CPT)) * CPT;
+        const int gr = n0 + rr;
+        const uint16_t* drow = gr < n ? dsc + (int64_t)gr * kb + 2 * kt0 : nullptr;
         // Scales are prefetched kWin k-tiles ahead in registers when every row's
-        // window is 16-byte aligned; otherwise they are read per stage.
+        // window is 16-byte aligned; otherwise they are read per k-tile.
         const bool windowed = (kb % 8 == 0) && (kt0 % 4 == 0);
-        uint4 cur[RPT][2], nxt[RPT][2];
-        auto load_win = [&](uint4 (&dst)[RPT][2], int w) {
-#pragma unroll
-            for (int j = 0; j < RPT; j++) {
-                const int t = w * kWin;
-                if (drow[j] != nullptr && t < KT) {
-                    const uint4* p = reinterpret_cast<const uint4*>(drow[j] + 2 * t);
-                    dst[j][0] = __ldg(p);
-                    dst[j][1] = (t + 4 < KT) ? __ldg(p + 1) : make_uint4(0, 0, 0, 0);
-                } else {
-                    dst[j][0] = dst[j][1] = make_uint4(0, 0, 0, 0);
-                }
+        uint4 cur[2], nxt[2];
+        auto load_win = [&](uint4 (&dst)[2], int w) {
+            const int t = w * kWin;
+            if (drow != nullptr && t < KT) {
+                const uint4* p = reinterpret_cast<const uint4*>(drow + 2 * t);
+                dst[0] = __ldg(p);
+                dst[1] = (t + 4 < KT) ? __ldg(p + 1) : make_uint4(0, 0, 0, 0);
+            } else {
+                dst[0] = dst[1] = make_uint4(0, 0, 0, 0);
             }
         };
         if (windowed) {
@@ -264,44 +283,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int w = 0; w * kWin < KT && ok; w++) {
             if (windowed && w > 0) {
-#pragma unroll
-                for (int j = 0; j < RPT; j++) {
-                    cur[j][0] = nxt[j][0];
-                    cur[j][1] = nxt[j][1];
-                }
+                cur[0] = nxt[0];
+                cur[1] = nxt[1];
                 load_win(nxt, w + 1);
             }
 #pragma unroll
             for (int u = 0; u < kWin; u++) {
                 const int t = w * kWin + u;
                 if (t >= KT) break;
-                const int s = t % STAGES, r = t / STAGES;
-                ok = mbar_wait(full_bar(s), r & 1, err);
+                const int s8 = t % S8, s16 = t % S16;
+                ok = mbar_wait(b8_full(s8), (t / S8) & 1, err);
                 if (!ok) break;
-                const uint8_t* b8 = smem + L::B8_OFF + s * L::B8_BYTES;
-                uint8_t* bhi = smem + L::B16_OFF + s * L::NB * L::B16_BYTES;
+                // raw int8 chunks of this thread -> registers; the slot is released at once
+                const uint4* src = reinterpret_cast<const uint4*>(smem + L::B8_OFF + s8 * L::B8_BYTES + rr * BK);
+                uint4 raw[CPT];
 #pragma unroll
-                for (int j = 0; j < RPT; j++) {
-                    const int rr = rows[j];
-                    uint32_t sc2;
-                    if (windowed) {
-                        const uint4 v = cur[j][u >> 2];
-                        sc2 = (u & 3) == 0 ? v.x : (u & 3) == 1 ? v.y : (u & 3) == 2 ? v.z : v.w;
-                    } else {
-                        sc2 = drow[j] != nullptr ? __ldg(reinterpret_cast<const uint32_t*>(drow[j] + 2 * t)) : 0u;
-                    }
-                    const uint4* src = reinterpret_cast<const uint4*>(b8 + rr * BK);
+                for (int cc = 0; cc < CPT; cc++) raw[cc] = src[c0 + cc];
+                mbar_arrive(b8_empty(s8));
+                uint32_t sc2;
+                if (windowed) {
+                    const uint4 v = cur[u >> 2];
+                    sc2 = (u & 3) == 0 ? v.x : (u & 3) == 1 ? v.y : (u & 3) == 2 ? v.z : v.w;
+                } else {
+                    sc2 = drow != nullptr ? __ldg(reinterpret_cast<const uint32_t*>(drow + 2 * t)) : 0u;
+                }
+                if (t >= S16) ok = mbar_wait(b16_empty(s16), ((t / S16) - 1) & 1, err);
+                if (!ok) break;
+                uint8_t* bhi = smem + L::B16_OFF + s16 * L::NB * L::B16_BYTES;
 #pragma unroll
-                    for (int cc = 0; cc < CPT; cc++) {
-                        const int c = c0 + cc;
-                        uint32_t hi[8], lo[8];
-                        dequant16<BF16, SPLIT>(src[c], (uint16_t)(c < 2 ? (sc2 & 0xFFFFu) : (sc2 >> 16)), hi, lo);
-                        store_chunk(bhi, rr, c, hi);
-                        if (SPLIT) store_chunk(bhi + L::B16_BYTES, rr, c, lo);
-                    }
+                for (int cc = 0; cc < CPT; cc++) {
+                    const int c = c0 + cc;
+                    uint32_t hi[8], lo[8];
+                    dequant16<BF16, SPLIT>(raw[cc], (uint16_t)(c < 2 ? (sc2 & 0xFFFFu) : (sc2 >> 16)), hi, lo);
+                    store_chunk(bhi, rr, c, hi);
+                    if (SPLIT) store_chunk(bhi + L::B16_BYTES, rr, c, lo);
                 }
                 fence_proxy_async_smem();
-                mbar_arrive(deq_bar(s));
+                mbar_arrive(b16_full(s16));
             }
         }
         // ---- epilogue: warp quadrant q reads TMEM lanes [32q, 32q+32); the two
@@ -310,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
         tc_fence_after();
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int half = (warp - kDeqWarp0) >> 2;
         float* ybase = y + (int64_t)blockIdx.z * (int64_t)m * ldy;  // split-K partial slice
         const bool vec_ok = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
         if (ok) {
@@ -417,10 +435,10 @@ int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint
 
 namespace {
 
-template <int BN, int MT, int STAGES, bool BF16, bool SPLIT>
+template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT>
 int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* a, int64_t m, float* out,
            int64_t ld_out, int splits, int kt_per, cudaStream_t s) {
-    using L = TcLayout<BN, MT, STAGES, SPLIT>;
+    using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
     CUtensorMap ma, mb;
     int st = make_map_2d(&ma, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, (uint64_t)k,
                          (uint64_t)m, (uint64_t)k * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -428,7 +446,7 @@ int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void
     st = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, qs, (uint64_t)k, (uint64_t)n, (uint64_t)k, BK, BN,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
-    auto kern = q8_0_gemm_tc_kernel<BN, MT, STAGES, BF16, SPLIT>;
+    auto kern = q8_0_gemm_tc_kernel<BN, MT, SA, S16, S8, BF16, SPLIT>;
     GDN_CUDA(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM));
     const dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM * MT - 1) / (BM * MT)), (unsigned)splits);
     kern<<<grid, kThreads, L::SMEM, s>>>(ma, mb, d, (int)n, (int)k, (int)m, out, ld_out, kt_per,
@@ -476,17 +494,18 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
         ld_out = n;
     }
     // Two M tiles per CTA share each dequantised weight tile once m > 128.
+    // Ring depths <SA, S16, S8> fill ~224 KB of shared memory.
     const bool two = m > BM;
     int st;
     if (opt.split_precision) {
-        st = two ? run_tc<128, 2, 3, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                 : run_tc<128, 1, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+        st = two ? run_tc<128, 2, 4, 2, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
+                 : run_tc<128, 1, 6, 3, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
     } else if (a_bf16) {
-        st = two ? run_tc<128, 2, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                 : run_tc<256, 1, 3, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+        st = two ? run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
+                 : run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
     } else {
-        st = two ? run_tc<128, 2, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                 : run_tc<256, 1, 3, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+        st = two ? run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
+                 : run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
     }
     if (st || splits == 1) return st;
     const int64_t cnt = m * n;

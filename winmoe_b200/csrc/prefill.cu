@@ -118,12 +118,16 @@ PWork pcarve(const gdn_dims& d, int64_t T, void* base) {
 
 // ------------------------------------------------------------------ prep
 //
-// One warp per (token t, 128-channel chunk hc of qkv); lane l owns channels
-// 4l..4l+3.  Causal conv1d over tokens t-3..t (taps k = 0 oldest .. 3 = t),
+// One warp per (128-channel chunk hc of qkv, block of kTokBlock tokens); lane
+// l owns channels 4l..4l+3.  The warp walks its tokens keeping the last three
+// raw projections in registers, so each projection row and the conv weights
+// are read once.  Causal conv1d over tokens t-3..t (taps k = 0 oldest .. 3 = t),
 // where tokens before the prompt come from the conv window of the state:
 // token -j (j = 1..3) sits in slot (p0 - j) mod 4 (deltanet_impl.h:220-230).
 // Then SiLU; q/k chunks are L2-normalised (double sum, deltanet_impl.h:85-91).
 // Padding tokens (t >= T) are written as zeros.
+constexpr int kTokBlock = 16;
+
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T,
                                                            int64_t Tp, const float* __restrict__ conv_buf,
                                                            const int32_t* __restrict__ conv_pos,
@@ -133,55 +137,68 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
     const int lane = threadIdx.x & 31;
     const int nchunk = qkv / HD;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (gw >= Tp * nchunk) return;
-    const int64_t t = gw / nchunk;
+    const int64_t nblk = Tp / kTokBlock;
+    if (gw >= nblk * nchunk) return;
     const int hc = (int)(gw % nchunk);
+    const int64_t tb = (gw / nchunk) * kTokBlock;
     bf16* dst;
-    if (hc < hk) dst = qn + ((int64_t)hc * Tp + t) * HD;
-    else if (hc < 2 * hk) dst = kn + ((int64_t)(hc - hk) * Tp + t) * HD;
-    else dst = vb + ((int64_t)(hc - 2 * hk) * Tp + t) * HD;
+    if (hc < hk) dst = qn + (int64_t)hc * Tp * HD;
+    else if (hc < 2 * hk) dst = kn + (int64_t)(hc - hk) * Tp * HD;
+    else dst = vb + (int64_t)(hc - 2 * hk) * Tp * HD;
     dst += 4 * lane;
-    if (t >= T) {
-        *reinterpret_cast<uint2*>(dst) = make_uint2(0u, 0u);
-        return;
-    }
     const int ch = hc * HD + 4 * lane;
-    float4 xv = *reinterpret_cast<const float4*>(proj + t * ldp + ch);
-    if (conv_buf != nullptr && conv_w != nullptr) {
-        const int p0 = *conv_pos;
-        float4 hist[3];
+    const bool conv = conv_buf != nullptr && conv_w != nullptr;
+    float4 wv[4] = {};
+    float4 hist[3] = {};  // raw projections of tokens t-3, t-2, t-1
+    if (conv) {
 #pragma unroll
-        for (int j = 0; j < 3; j++) {  // hist[j] = raw projection of token t - 3 + j
-            const int64_t tt = t - 3 + j;
+        for (int c = 0; c < 4; c++) wv[c] = reinterpret_cast<const float4*>(conv_w)[ch + c];
+        const int p0 = *conv_pos;
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+            const int64_t tt = tb - 3 + j;
             hist[j] = tt >= 0 ? *reinterpret_cast<const float4*>(proj + tt * ldp + ch)
                               : *reinterpret_cast<const float4*>(conv_buf + (int64_t)((p0 + (int)tt) & 3) * qkv + ch);
         }
-        const float4* wv = reinterpret_cast<const float4*>(conv_w) + ch;
-        float in[4] = {xv.x, xv.y, xv.z, xv.w};
-        const float h0[4] = {hist[0].x, hist[0].y, hist[0].z, hist[0].w};
-        const float h1[4] = {hist[1].x, hist[1].y, hist[1].z, hist[1].w};
-        const float h2[4] = {hist[2].x, hist[2].y, hist[2].z, hist[2].w};
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const float4 w = wv[c];
-            float sum = 0.0f;
-            sum = __fadd_rn(sum, __fmul_rn(w.x, h0[c]));
-            sum = __fadd_rn(sum, __fmul_rn(w.y, h1[c]));
-            sum = __fadd_rn(sum, __fmul_rn(w.z, h2[c]));
-            sum = __fadd_rn(sum, __fmul_rn(w.w, in[c]));
-            const float sig = 1.0f / (1.0f + expf(-sum));
-            in[c] = __fmul_rn(sum, sig);
+    }
+    for (int64_t t = tb; t < tb + kTokBlock; t++) {
+        if (t >= T) {
+            *reinterpret_cast<uint2*>(dst + t * HD) = make_uint2(0u, 0u);
+            continue;
         }
-        xv = make_float4(in[0], in[1], in[2], in[3]);
-    }
-    if (hc < 2 * hk) {
-        double ss = (double)xv.x * xv.x + (double)xv.y * xv.y + (double)xv.z * xv.z + (double)xv.w * xv.w;
+        const float4 raw = *reinterpret_cast<const float4*>(proj + t * ldp + ch);
+        float4 xv = raw;
+        if (conv) {
+            float in[4] = {raw.x, raw.y, raw.z, raw.w};
+            const float h0[4] = {hist[0].x, hist[0].y, hist[0].z, hist[0].w};
+            const float h1[4] = {hist[1].x, hist[1].y, hist[1].z, hist[1].w};
+            const float h2[4] = {hist[2].x, hist[2].y, hist[2].z, hist[2].w};
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / (sqrtf((float)ss) + 1e-6f);
-        xv = make_float4(__fmul_rn(xv.x, inv), __fmul_rn(xv.y, inv), __fmul_rn(xv.z, inv), __fmul_rn(xv.w, inv));
+            for (int c = 0; c < 4; c++) {
+                const float4 w = wv[c];
+                float sum = 0.0f;
+                sum = __fadd_rn(sum, __fmul_rn(w.x, h0[c]));
+                sum = __fadd_rn(sum, __fmul_rn(w.y, h1[c]));
+                sum = __fadd_rn(sum, __fmul_rn(w.z, h2[c]));
+                sum = __fadd_rn(sum, __fmul_rn(w.w, in[c]));
+                const float sig = 1.0f / (1.0f + expf(-sum));
+                in[c] = __fmul_rn(sum, sig);
+            }
+            xv = make_float4(in[0], in[1], in[2], in[3]);
+            hist[0] = hist[1];
+            hist[1] = hist[2];
+            hist[2] = raw;
+        }
+        if (hc < 2 * hk) {
+            double ss = (double)xv.x * xv.x + (double)xv.y * xv.y + (double)xv.z * xv.z + (double)xv.w * xv.w;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = 1.0f / (sqrtf((float)ss) + 1e-6f);
+            xv = make_float4(__fmul_rn(xv.x, inv), __fmul_rn(xv.y, inv), __fmul_rn(xv.z, inv), __fmul_rn(xv.w, inv));
+        }
+        *reinterpret_cast<uint2*>(dst + t * HD) =
+            make_uint2(wmma16::pack_bf16(xv.x, xv.y), wmma16::pack_bf16(xv.z, xv.w));
     }
-    *reinterpret_cast<uint2*>(dst) = make_uint2(wmma16::pack_bf16(xv.x, xv.y), wmma16::pack_bf16(xv.z, xv.w));
 }
 
 // Gates per (head h, token t): log decay log(a) = ssm_a * softplus(alpha + dt_bias)
@@ -329,16 +346,16 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
     }
 #pragma unroll
     for (int i = 1; i < CH; i++) {
-        float s = x[i];
+        float s0 = x[i], s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;  // four chains keep the FMA pipe busy
 #pragma unroll
         for (int kq = 0; kq < i; kq += 4) {
             const float4 l4 = *reinterpret_cast<const float4*>(&sm.L[i][kq]);
-            s = fmaf(-l4.x, x[kq], s);
-            if (kq + 1 < i) s = fmaf(-l4.y, x[kq + 1], s);
-            if (kq + 2 < i) s = fmaf(-l4.z, x[kq + 2], s);
-            if (kq + 3 < i) s = fmaf(-l4.w, x[kq + 3], s);
+            s0 = fmaf(-l4.x, x[kq], s0);
+            if (kq + 1 < i) s1 = fmaf(-l4.y, x[kq + 1], s1);
+            if (kq + 2 < i) s2 = fmaf(-l4.z, x[kq + 2], s2);
+            if (kq + 3 < i) s3 = fmaf(-l4.w, x[kq + 3], s3);
         }
-        x[i] = s;
+        x[i] = (s0 + s1) + (s2 + s3);
     }
     bf16* dst = (is_w ? wp : up) + ((int64_t)h * Tp + t0) * HD + col;
 #pragma unroll
@@ -361,12 +378,15 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
 // start state), D = U' - W' S (warp w: token rows 16w..16w+15), then
 // S = gam_63 S + (e K)^T D.  The next chunk's W', e*K and U' stream in with
 // cp.async while this one is computed.
+constexpr int kMaxChunksInSmem = 2048;  // per-chunk decays staged in smem (T up to 128K tokens)
+
 struct ScanSmem {
     bf16 w[2][CH][LDH];
     bf16 e[2][CH][LDH];
     bf16 u[2][CH][LDV];
     bf16 s[HD][LDV];
     bf16 d[CH][LDV];
+    float gc[kMaxChunksInSmem];
 };
 
 __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict__ wp, const bf16* __restrict__ up,
@@ -407,6 +427,9 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
         wmma16::cp_async_commit();
     };
     prefetch(0, 0);
+    const bool gc_smem = nc <= kMaxChunksInSmem;
+    if (gc_smem)
+        for (int64_t i = tid; i < nc; i += 128) sm.gc[i] = gchunk[(int64_t)h * nc + i];
 
     for (int64_t c = 0; c < nc; c++) {
         const int buf = (int)(c & 1);
@@ -420,9 +443,8 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
                 for (int hf = 0; hf < 2; hf++) {
                     const int r = 32 * warp + 16 * mt + gq + 8 * hf;
                     const int cl = 8 * n + 2 * qq;
-                    const uint32_t pk = wmma16::pack_bf16(acc[mt][n][2 * hf], acc[mt][n][2 * hf + 1]);
-                    *reinterpret_cast<uint32_t*>(&sm.s[r][cl]) = pk;
-                    *reinterpret_cast<uint32_t*>(scc + (int64_t)r * HD + v0 + cl) = pk;
+                    *reinterpret_cast<uint32_t*>(&sm.s[r][cl]) =
+                        wmma16::pack_bf16(acc[mt][n][2 * hf], acc[mt][n][2 * hf + 1]);
                 }
         if (c + 1 < nc) {
             prefetch(c + 1, buf ^ 1);
@@ -431,6 +453,10 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
             wmma16::cp_async_wait<0>();
         }
         __syncthreads();
+        for (int i = tid; i < HD * BV / 8; i += 128) {  // chunk start state -> HBM, 16-byte stores
+            const int r = i / (BV / 8), q = i % (BV / 8);
+            *reinterpret_cast<uint4*>(scc + (int64_t)r * HD + v0 + q * 8) = *reinterpret_cast<const uint4*>(&sm.s[r][q * 8]);
+        }
 
         // ---- D = U' - W' S   (token rows 16w..16w+15, all BV columns)
         float dacc[BV / 8][4] = {};
@@ -455,14 +481,17 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
                 const int cl = 8 * n + 2 * qq;
                 const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(&sm.u[buf][r][cl]);
                 const float2 uf = __bfloat1622float2(u2);
-                const uint32_t pk = wmma16::pack_bf16(uf.x - dacc[n][2 * hf], uf.y - dacc[n][2 * hf + 1]);
-                *reinterpret_cast<uint32_t*>(&sm.d[r][cl]) = pk;
-                *reinterpret_cast<uint32_t*>(dlc + (int64_t)r * HD + cl) = pk;
+                *reinterpret_cast<uint32_t*>(&sm.d[r][cl]) =
+                    wmma16::pack_bf16(uf.x - dacc[n][2 * hf], uf.y - dacc[n][2 * hf + 1]);
             }
         __syncthreads();
+        for (int i = tid; i < CH * BV / 8; i += 128) {  // deltas -> HBM, 16-byte stores
+            const int r = i / (BV / 8), q = i % (BV / 8);
+            *reinterpret_cast<uint4*>(dlc + (int64_t)r * HD + q * 8) = *reinterpret_cast<const uint4*>(&sm.d[r][q * 8]);
+        }
 
         // ---- S = gam_63 S + (e K)^T D   (key rows 32w..32w+31)
-        const float gC = gchunk[(int64_t)h * nc + c];
+        const float gC = gc_smem ? sm.gc[c] : gchunk[(int64_t)h * nc + c];
 #pragma unroll
         for (int mt = 0; mt < 2; mt++)
 #pragma unroll
@@ -716,7 +745,7 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     // ---- conv1d + SiLU + L2 norm, gates, window hand-off
     if ((st = phase_mark(1, s))) return st;
     {
-        const int64_t warps = D.Tp * (D.qkv / HD);
+        const int64_t warps = (D.Tp / kTokBlock) * (D.qkv / HD);
         prefill_prep_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(
             W.proj, D.ldp, T, D.Tp, conv ? conv_buf : nullptr, conv_pos, conv ? L->conv1d_w : nullptr, W.qn, W.kn,
             W.vb, D.qkv, D.hk);
