@@ -110,6 +110,29 @@ def test_q8_0_gemm_tensor_core_fast(m, n, k, xdt):
     assert ((y - want32).norm() / want32.norm()).item() <= (2e-3 if xdt == torch.float16 else 8e-3)
 
 
+@pytest.mark.parametrize("m,n,k", [(70, 2560, 512), (128, 2560, 512), (100, 12352, 2048)])
+@pytest.mark.parametrize("xdt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("fast", [True, False])
+def test_q8_0_gemm_tensor_core_repeatable(m, n, k, xdt, fast):
+    """One-M-tile shapes (the prefill in_proj of short prompts), 12 launches in a
+    row: every launch bit-identical, and every 32-column epilogue group close to
+    the fp64 product (a group read out of TMEM too early shows up here)."""
+    blocks = synth.q8_0_blocks(n, k, seed=700 + n + k)
+    qs, d = L.q8_0_planes(blocks, n, k, DEV)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m + k)).to(xdt).to(DEV)
+    w = torch.from_numpy(synth.q8_0_dequant_np(blocks, n, k)).to(DEV)
+    if fast:
+        w = w.to(xdt)
+    want = x.double() @ w.double().T
+    ys = [L.gemm_q8_0(qs, d, x, fast=fast) for _ in range(12)]
+    torch.cuda.synchronize()
+    for i, y in enumerate(ys):
+        assert torch.equal(y, ys[0]), f"launch {i} differs from launch 0"
+    diff = (ys[0].double() - want).reshape(m, n // 32, 32).norm(dim=(0, 2))
+    ref = want.reshape(m, n // 32, 32).norm(dim=(0, 2))
+    assert (diff / ref).max().item() <= 1e-4
+
+
 def test_no_device_timeout_flag():
     from winmoe_b200._lib import lib
     torch.cuda.synchronize()

@@ -266,9 +266,11 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
             if (gated_h != nullptr) gated_h[idx] = __float2half_rn(gv);
         }
         if (t == 0 && h == 0 && conv_pos != nullptr) conv_pos[b] += 1;
+        // Every thread orders its generic reads of the slot before the bulk copy
+        // that refills it (async proxy), then the barrier hands the slot over.
+        sm100::fence_proxy_async_smem();
         __syncthreads();  // slot i % kStateBufs fully consumed
         if (t == 0 && ok && i + kStateBufs < count) {  // after a timed-out wait no new copy is issued
-            sm100::fence_proxy_async_smem();
             issue(i + kStateBufs);
         }
     }

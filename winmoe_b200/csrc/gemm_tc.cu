@@ -299,6 +299,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint4 raw[CPT];
 #pragma unroll
                 for (int cc = 0; cc < CPT; cc++) raw[cc] = src[c0 + cc];
+                // The next write to this slot is a TMA (async proxy): the generic
+                // reads above must be ordered before it by a proxy fence, or the
+                // refill can overtake a late read (one weight row goes stale).
+                fence_proxy_async_smem();
                 mbar_arrive(b8_empty(s8));
                 uint32_t sc2;
                 if (windowed) {
@@ -339,16 +343,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
                 for (int cg = half * 32; cg < BN; cg += 64) {
                     uint32_t v[32];
-                    tmem_ld_32x32b_x32(tbase + (uint32_t)cg, v);
+                    tmem_load_32x32b_x32(tbase + (uint32_t)cg, v);
                     if (SPLIT) {
                         uint32_t vl[32];
-                        tmem_ld_32x32b_x32(tbase + (uint32_t)(BN + cg), vl);
-                        tmem_ld_wait();
+                        tmem_load_32x32b_x32(tbase + (uint32_t)(BN + cg), vl);
 #pragma unroll
                         for (int j = 0; j < 32; j++)
                             v[j] = __float_as_uint(fmaf(__uint_as_float(vl[j]), 1.0f / 2048.0f, __uint_as_float(v[j])));
-                    } else {
-                        tmem_ld_wait();
                     }
                     if (row < m) {
                         float* yr = ybase + (int64_t)row * ldy + n0 + cg;

@@ -60,7 +60,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     return true;
 }
 
-// Generic-proxy writes to shared memory -> visible to the async proxy (MMA reads).
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy ones: writes that an MMA reads next, and reads of a slot that a
+// TMA overwrites next.
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -125,18 +127,24 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 }
 
 // 32 lanes x 32 columns of 32-bit TMEM -> 32 registers per thread (lane = thread).
-__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+// The load and its tcgen05.wait::ld sit in ONE asm statement: the destination
+// registers are written asynchronously, and with the wait in a separate
+// statement the compiler may copy an output register between the two (reading
+// it before the data has landed).  Here the outputs are only defined once the
+// wait has returned.
+__device__ __forceinline__ void tmem_load_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
+        : "r"(taddr)
+        : "memory");
 }
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // UMMA shared-memory descriptor of a K-major tile in the 128-byte swizzle
 // layout: rows of 128 bytes, 8-row groups 1024 bytes apart (SBO), the tile
