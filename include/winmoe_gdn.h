@@ -191,6 +191,29 @@ GDN_API int gdn_decode_step(const gdn_layer* layer, int64_t batch,
                     float* S, float* conv_buf, int32_t* conv_pos,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the fixed scratch behind gdn_decode_step_noalloc (8 MiB). */
+#define GDN_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+
+/*
+ * gdn_decode_step without a caller workspace and without any allocation: no
+ * counterpart in the reference (its deltanet_forward keeps its scratch on the
+ * CPU stack).  Same arguments, results and errors as gdn_decode_step; the
+ * scratch is one static device array per device, GDN_NOALLOC_SCRATCH_BYTES
+ * long, so batches whose gdn_decode_workspace_size exceeds it are rejected
+ * with GDN_ERR_SHAPE (the 35B layer fits up to 47 sequences).
+ *   - The first call on each device (with that device current) resolves the
+ *     scratch address with cudaGetSymbolAddress; make that first call before
+ *     any stream capture.
+ *   - Nothing in the scratch has to start at zero: every byte a kernel reads
+ *     is written earlier in the same call, so it is never cleared.
+ *   - One scratch per device: calls whose GPU work overlaps (different streams
+ *     without ordering between them, or several host threads) race on it.
+ *     Issue them on one stream, or order the streams with events.
+ */
+GDN_API int gdn_decode_step_noalloc(const gdn_layer* layer, int64_t batch,
+                                    const void* x, int x_dtype, float* out,
+                                    float* S, float* conv_buf, int32_t* conv_pos, void* stream);
+
 /* Bytes of scratch gdn_prefill needs for a prompt of T tokens. */
 GDN_API size_t gdn_prefill_workspace_size(const gdn_dims* dims, int64_t T);
 

@@ -1,0 +1,98 @@
+"""gdn_decode_step_noalloc (fixed static scratch, no allocation) against
+gdn_decode_step (caller workspace), both called through the C ABI.
+
+Two decode tokens in a row from the same state; outputs, S, the conv window
+and conv_pos must agree within the decode parity bound (rel-L2 1e-3).  The
+file name sorts last so it also runs after every other GPU test; it passes
+on its own in a fresh process too (the first call sets up the scratch).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from winmoe_b200 import GDNConfig, layer as L, synth
+from winmoe_b200._lib import check, gdn_dims, lib
+from winmoe_b200.config import DIMS_35B
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 1e-3
+DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+SCRATCH_BYTES = 8 << 20  # GDN_NOALLOC_SCRATCH_BYTES
+
+
+def rel_l2(a, b):
+    a = a.double().cpu()
+    b = b.double().cpu()
+    return float((a - b).norm() / max(b.norm().item(), 1e-30))
+
+
+def stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def setup(cfg, batch):
+    t = synth.layer_tensors(cfg, layer=2)
+    w = L.DeltaNetWeights.upload(cfg, t.in_proj, t.out_proj, t.conv1d_w, t.ssm_a, t.dt_bias, t.head_norm,
+                                 device=DEV)
+    st = L.DeltaNetState.zeros(cfg, batch, DEV)
+    for b in range(batch):
+        st.S[b] = torch.from_numpy(synth.prefilled_state(cfg, b))
+    return w, st
+
+
+def step_workspace(w, st, x, out):
+    """The existing entry point with a caller workspace."""
+    cfg = w.cfg
+    dims = gdn_dims(cfg.hidden, cfg.num_k_heads, cfg.num_v_heads, cfg.head_dim)
+    ws = torch.empty(lib().gdn_decode_workspace_size(C.byref(dims), x.shape[0]), dtype=torch.uint8, device=DEV)
+    check(lib().gdn_decode_step(C.byref(w.struct()), x.shape[0], x.data_ptr(), DTYPES[x.dtype], out.data_ptr(),
+                                st.S.data_ptr(), st.conv_buf.data_ptr(), st.conv_pos.data_ptr(), ws.data_ptr(),
+                                ws.numel(), stream()))
+
+
+def step_noalloc(w, st, x, out):
+    return lib().gdn_decode_step_noalloc(C.byref(w.struct()), x.shape[0], x.data_ptr(), DTYPES[x.dtype],
+                                         out.data_ptr(), st.S.data_ptr(), st.conv_buf.data_ptr(),
+                                         st.conv_pos.data_ptr(), stream())
+
+
+@pytest.mark.parametrize("cfg,batch,dtype", [
+    (DIMS_35B, 1, torch.float32),                    # the reference engine's single-sequence decode
+    (DIMS_35B, 32, torch.bfloat16),                  # CUDA-core projections, 5.4 MiB of scratch
+    (GDNConfig(512, 2, 4, 128), 64, torch.bfloat16),  # tensor-core projections and split-K out_proj
+])
+def test_noalloc_matches_workspace_entry(cfg, batch, dtype):
+    w, st_ref = setup(cfg, batch)
+    st_new = st_ref.clone()
+    gen = torch.Generator().manual_seed(batch)
+    for _ in range(2):
+        x = torch.randn((batch, cfg.hidden), generator=gen).to(dtype).to(DEV)
+        y_ref = torch.empty((batch, cfg.hidden), dtype=torch.float32, device=DEV)
+        y_new = torch.full_like(y_ref, float("nan"))
+        step_workspace(w, st_ref, x, y_ref)
+        check(step_noalloc(w, st_new, x, y_new))
+        torch.cuda.synchronize()
+        assert rel_l2(y_new, y_ref) <= TOL
+        assert rel_l2(st_new.S, st_ref.S) <= TOL
+        assert rel_l2(st_new.conv_buf, st_ref.conv_buf) <= TOL
+        assert torch.equal(st_new.conv_pos, st_ref.conv_pos)
+    assert lib().gdn_check_device_error(stream()) == 0
+
+
+def test_noalloc_rejects_batches_above_the_scratch():
+    cfg = DIMS_35B
+    dims = gdn_dims(cfg.hidden, cfg.num_k_heads, cfg.num_v_heads, cfg.head_dim)
+    batch = 48
+    assert lib().gdn_decode_workspace_size(C.byref(dims), batch) > SCRATCH_BYTES
+    w, st = setup(cfg, batch)
+    x = torch.zeros((batch, cfg.hidden), dtype=torch.float32, device=DEV)
+    y = torch.zeros_like(x)
+    S0 = st.S.clone()
+    rc = step_noalloc(w, st, x, y)
+    assert rc == -2  # GDN_ERR_SHAPE
+    assert "scratch" in lib().gdn_last_error().decode()
+    torch.cuda.synchronize()
+    assert torch.equal(st.S, S0) and int(st.conv_pos.sum()) == 0  # nothing ran

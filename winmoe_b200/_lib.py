@@ -59,6 +59,7 @@ SIGNATURES = {
     "gdn_q4_k_gemm": (_int, [_vp, _i64, _i64, _vp, _int, _i64, _vp, _vp]),
     "gdn_decode_workspace_size": (_sz, [C.POINTER(gdn_dims), _i64]),
     "gdn_decode_step": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "gdn_decode_step_noalloc": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
     "gdn_prefill_workspace_size": (_sz, [C.POINTER(gdn_dims), _i64]),
     "gdn_prefill": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gdn_profile_enable": (_int, [_int]),

@@ -4,6 +4,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "gdn_common.cuh"
 #include "quant.cuh"
 #include "decode.cuh"
@@ -142,6 +144,47 @@ size_t gdn_decode_workspace_size(const gdn_dims* dims, int64_t batch) {
 int gdn_decode_step(const gdn_layer* layer, int64_t batch, const void* x, int x_dtype, float* out, float* S,
                     float* conv_buf, int32_t* conv_pos, void* workspace, size_t workspace_bytes, void* stream) {
     return decode_step(layer, batch, x, x_dtype, out, S, conv_buf, conv_pos, workspace, workspace_bytes,
+                       as_stream(stream));
+}
+
+// Scratch of gdn_decode_step_noalloc: a file-scope device array (one per
+// device, zero-initialised storage of the module, never allocated by a call).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GDN_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on the current device, resolved once per
+// device (cudaGetSymbolAddress with that device current) and cached.
+static int noalloc_scratch(void** out) {
+    static void* ptrs[64] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    GDN_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(GDN_ERR_ARG, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (ptrs[dev] == nullptr) {
+        void* p = nullptr;
+        GDN_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        if (!aligned(p, 256)) return fail(GDN_ERR_CUDA, "static scratch is not 256-byte aligned");
+        ptrs[dev] = p;
+    }
+    *out = ptrs[dev];
+    return GDN_OK;
+}
+
+int gdn_decode_step_noalloc(const gdn_layer* layer, int64_t batch, const void* x, int x_dtype, float* out, float* S,
+                            float* conv_buf, int32_t* conv_pos, void* stream) {
+    int st = validate_layer(layer);
+    if (st) return st;
+    if (batch <= 0 || batch > 65535)
+        return fail(GDN_ERR_SHAPE, "batch must be in [1, 65535] (got %lld)", (long long)batch);
+    const size_t need = decode_workspace_bytes(layer->dims, batch);
+    if (need > GDN_NOALLOC_SCRATCH_BYTES)
+        return fail(GDN_ERR_SHAPE,
+                    "gdn_decode_step_noalloc: batch %lld needs %zu bytes of scratch, more than the fixed %zu; "
+                    "use gdn_decode_step with a caller workspace",
+                    (long long)batch, need, (size_t)GDN_NOALLOC_SCRATCH_BYTES);
+    void* ws = nullptr;
+    if ((st = noalloc_scratch(&ws))) return st;
+    return decode_step(layer, batch, x, x_dtype, out, S, conv_buf, conv_pos, ws, GDN_NOALLOC_SCRATCH_BYTES,
                        as_stream(stream));
 }
 
