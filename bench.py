@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the T=4096 prefill leg")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the T=4096 prefill leg (one GPU); the line's value is the prefill's tok/s")
     return ap.parse_args()
 
 
@@ -261,6 +263,22 @@ def run_ours(args):
     tensors = synth.layer_tensors(cfg)
     w = L.DeltaNetWeights.upload(cfg, tensors.in_proj, tensors.out_proj, tensors.conv1d_w, tensors.ssm_a,
                                  tensors.dt_bias, tensors.head_norm, device=dev)
+    if args.prefill_only:
+        if world > 1:
+            raise SystemExit("--prefill-only runs on one GPU")
+        hbm_peak, tc_peak, peak_src = measured_peaks()
+        pre = run_prefill(cfg, w, dev, K, W, tc_peak, peak_src)
+        line = {"metric": METRIC, "value": pre["value"], "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+                "ms_per_step": pre["ms_per_prefill"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": pre["workload"], "hidden": cfg.hidden, "k_heads": cfg.num_k_heads,
+                           "v_heads": cfg.num_v_heads, "head_dim": cfg.head_dim, "weights": "Q8_0 (seeded)"},
+                # per prefill: x -> fp16, in_proj GEMM, gate-row GEMM + split-K sum, prep, gates, window,
+                # chunk_local, chunk_scan, chunk_out, out_proj GEMM
+                "gpu_launches": 11 * K, "roofline": pre["roofline"], "prefill": pre}
+        print(json.dumps(line), flush=True)
+        return
+
     gen = torch.Generator(device=dev).manual_seed(7 + 1000 * rank)
     st = L.DeltaNetState.zeros(cfg, B, dev)
     st.S.normal_(0.0, 0.05, generator=gen)

@@ -24,8 +24,9 @@
 //   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
 //   warp 2      TMA producer of the int8 weight tiles
 //   warps 3-10  dequant int8 -> operand type into the swizzled B tile(s), shared
-//               by the MT activation tiles; then the epilogue (tcgen05.ld TMEM ->
-//               registers -> global fp32), two warps per TMEM lane quadrant
+//               by the MT activation tiles (one mbarrier arrival per warp); then
+//               the epilogue (tcgen05.ld TMEM -> registers -> staged in shared
+//               memory -> coalesced global fp32), two warps per TMEM lane quadrant
 // The three rings (activation, dequantised weight, raw weight) have separate
 // full/empty mbarriers, so the raw weight slot is refilled as soon as the
 // dequant warps have read it rather than after the MMA -- the weight stream
@@ -48,6 +49,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kDeqThreads = 256;
 constexpr int kDeqWarp0 = 3;  // warps 0: A producer, 1: MMA issuer + TMEM owner, 2: weight producer
+constexpr int kDeqWarps = kDeqThreads / 32;
 constexpr int kThreads = 32 * kDeqWarp0 + kDeqThreads;
 constexpr int kWin = 8;  // k-tiles per scale window (16 fp16 scales = 32 bytes per row)
 
@@ -74,6 +76,7 @@ struct TcLayout {
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM budget");
     static_assert(BN % 64 == 0 && BN <= 256, "BN");
+    static_assert(SA * MT * A_BYTES >= 8u * 32u * 36u * 4u, "epilogue staging lives in the activation ring");
 };
 
 // 16 int8 weights (uint4) times scale -> 16 operand elements: hi[8] words (and
@@ -175,12 +178,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(a_empty(s), 1);
         }
         for (int s = 0; s < S16; s++) {
-            mbar_init(b16_full(s), kDeqThreads);
+            mbar_init(b16_full(s), kDeqWarps);
             mbar_init(b16_empty(s), 1);
         }
         for (int s = 0; s < S8; s++) {
             mbar_init(b8_full(s), 1);
-            mbar_init(b8_empty(s), kDeqThreads);
+            mbar_init(b8_empty(s), kDeqWarps);
         }
         mbar_init(accf_bar, 1);
         fence_barrier_init();
@@ -292,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int t = w * kWin + u;
                 if (t >= KT) break;
                 const int s8 = t % S8, s16 = t % S16;
-                ok = mbar_wait(b8_full(s8), (t / S8) & 1, err);
+                ok = __all_sync(0xffffffffu, mbar_wait(b8_full(s8), (t / S8) & 1, err));
                 if (!ok) break;
                 // raw int8 chunks of this thread -> registers; the slot is released at once
                 const uint4* src = reinterpret_cast<const uint4*>(smem + L::B8_OFF + s8 * L::B8_BYTES + rr * BK);
@@ -303,7 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // reads above must be ordered before it by a proxy fence, or the
                 // refill can overtake a late read (one weight row goes stale).
                 fence_proxy_async_smem();
-                mbar_arrive(b8_empty(s8));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(b8_empty(s8));
                 uint32_t sc2;
                 if (windowed) {
                     const uint4 v = cur[u >> 2];
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                     sc2 = drow != nullptr ? __ldg(reinterpret_cast<const uint32_t*>(drow + 2 * t)) : 0u;
                 }
-                if (t >= S16) ok = mbar_wait(b16_empty(s16), ((t / S16) - 1) & 1, err);
+                if (t >= S16) ok = __all_sync(0xffffffffu, mbar_wait(b16_empty(s16), ((t / S16) - 1) & 1, err));
                 if (!ok) break;
                 uint8_t* bhi = smem + L::B16_OFF + s16 * L::NB * L::B16_BYTES;
 #pragma unroll
@@ -323,11 +327,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (SPLIT) store_chunk(bhi + L::B16_BYTES, rr, c, lo);
                 }
                 fence_proxy_async_smem();
-                mbar_arrive(b16_full(s16));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(b16_full(s16));
             }
         }
         // ---- epilogue: warp quadrant q reads TMEM lanes [32q, 32q+32); the two
-        // warps of a quadrant take alternate 32-column groups
+        // warps of a quadrant take alternate 32-column groups.  Each 32 x 32 block
+        // goes through a per-warp staging tile in the (drained) activation ring so
+        // that global stores write whole 128-byte row segments, 4 rows per store.
         if (ok) ok = mbar_wait(accf_bar, 0, err);
         ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
         tc_fence_after();
@@ -335,10 +342,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half = (warp - kDeqWarp0) >> 2;
         float* ybase = y + (int64_t)blockIdx.z * (int64_t)m * ldy;  // split-K partial slice
         const bool vec_ok = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+        constexpr int kPitch = 36;  // floats per staged row: 16-byte aligned, conflict-free
+        float* stg = reinterpret_cast<float*>(smem + L::A_OFF) + (warp - kDeqWarp0) * (32 * kPitch);
+        const int sr = lane >> 3, sc = (lane & 7) * 4;  // store phase: row within a group of 4, column
         if (ok) {
 #pragma unroll 1
             for (int mt = 0; mt < MT; mt++) {
-                const int row = m0 + mt * BM + q * 32 + lane;
+                const int row0 = m0 + mt * BM + q * 32;
                 const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(mt * L::NB * BN);
 #pragma unroll 1
                 for (int cg = half * 32; cg < BN; cg += 64) {
@@ -351,20 +361,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; j++)
                             v[j] = __float_as_uint(fmaf(__uint_as_float(vl[j]), 1.0f / 2048.0f, __uint_as_float(v[j])));
                     }
-                    if (row < m) {
-                        float* yr = ybase + (int64_t)row * ldy + n0 + cg;
-                        if (vec_ok && n0 + cg + 32 <= n) {
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(yr + j) =
-                                    make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-                        } else {
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<uint4*>(stg + lane * kPitch + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    __syncwarp();
+                    const int col = n0 + cg + sc;
 #pragma unroll
-                            for (int j = 0; j < 32; j++)
-                                if (n0 + cg + j < n) yr[j] = __uint_as_float(v[j]);
+                    for (int it = 0; it < 8; it++) {
+                        const int r = it * 4 + sr;
+                        if (row0 + r < m) {
+                            const float4 f = *reinterpret_cast<const float4*>(stg + r * kPitch + sc);
+                            float* yr = ybase + (int64_t)(row0 + r) * ldy + col;
+                            if (vec_ok && col + 4 <= n) {
+                                *reinterpret_cast<float4*>(yr) = f;
+                            } else {
+                                if (col < n) yr[0] = f.x;
+                                if (col + 1 < n) yr[1] = f.y;
+                                if (col + 2 < n) yr[2] = f.z;
+                                if (col + 3 < n) yr[3] = f.w;
+                            }
                         }
                     }
+                    __syncwarp();
                 }
             }
         }
@@ -501,12 +519,20 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
     if (opt.split_precision) {
         st = two ? run_tc<128, 2, 4, 2, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
                  : run_tc<128, 1, 6, 3, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
-    } else if (a_bf16) {
-        st = two ? run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                 : run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
     } else {
-        st = two ? run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                 : run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+        // One operand: 256-column tiles halve the activation traffic per MMA, as long
+        // as the grid still covers at least half of the SMs.
+        const int64_t tiles256 = (n + 255) / 256 * ((m + 2 * BM - 1) / (2 * BM)) * splits;
+        const bool wide = two && tiles256 * 2 >= sm_count();
+        if (a_bf16) {
+            st = !two ? run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
+                 : wide ? run_tc<256, 2, 3, 2, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
+                        : run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+        } else {
+            st = !two ? run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
+                 : wide ? run_tc<256, 2, 3, 2, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
+                        : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+        }
     }
     if (st || splits == 1) return st;
     const int64_t cnt = m * n;
