@@ -44,6 +44,8 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const float* __restrict__
                                                        const float* __restrict__ ssm_a,
                                                        const float* __restrict__ dt_bias, int64_t B, int qkv,
                                                        int key_dim, int hv) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int nchunk = qkv / HD + 1;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -149,6 +151,8 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
     float* __restrict__ S, const float* __restrict__ head_norm, float* __restrict__ gated,
     __half* __restrict__ gated_h, int32_t* __restrict__ conv_pos, int qkv, int key_dim, int hv, int hk,
     int head_map, int64_t n_tiles, int64_t tiles_per_cta, uint32_t* __restrict__ err) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     StateSmem& sm = *reinterpret_cast<StateSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     const int t = threadIdx.x, w = t >> 5, l = t & 31;
@@ -464,10 +468,10 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
     if ((st = mark(pe, 1, s))) return st;
     {
         const int64_t warps = B * (D.qkv / HD + 1);
-        gdn_prep_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(
-            ws.proj, D.ldp, ws.act, ws.gates, conv ? conv_buf : nullptr, conv_pos, conv ? L->conv1d_w : nullptr,
-            L->ssm_a, L->dt_bias, B, D.qkv, D.key, D.hv);
-        GDN_LAUNCH_CHECK("gdn_prep_kernel");
+        st = launch_pdl("gdn_prep_kernel", gdn_prep_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s,
+                        ws.proj, D.ldp, ws.act, ws.gates, conv ? conv_buf : nullptr, conv_pos,
+                        conv ? L->conv1d_w : nullptr, L->ssm_a, L->dt_bias, B, D.qkv, D.key, D.hv);
+        if (st) return st;
     }
     if ((st = mark(pe, 2, s))) return st;
     {
@@ -477,11 +481,11 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
         const size_t smem = state_kernel_smem();
         GDN_CUDA(cudaFuncSetAttribute((const void*)gdn_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)smem));
-        gdn_state_kernel<<<(unsigned)((n_tiles + per - 1) / per), 256, smem, s>>>(
-            ws.act, ws.gates, ws.proj, D.ldp, S, L->head_norm, tc_out ? nullptr : ws.gated,
-            tc_out ? ws.gated_h : nullptr, conv ? conv_pos : nullptr, D.qkv, D.key, D.hv, D.hk, L->head_map, n_tiles,
-            per, device_error_word());
-        GDN_LAUNCH_CHECK("gdn_state_kernel");
+        st = launch_pdl("gdn_state_kernel", gdn_state_kernel, dim3((unsigned)((n_tiles + per - 1) / per)), dim3(256),
+                        smem, s, ws.act, ws.gates, ws.proj, D.ldp, S, L->head_norm, tc_out ? nullptr : ws.gated,
+                        tc_out ? ws.gated_h : nullptr, conv ? conv_pos : nullptr, D.qkv, D.key, D.hv, D.hk,
+                        L->head_map, n_tiles, per, device_error_word());
+        if (st) return st;
     }
     if ((st = mark(pe, 3, s))) return st;
     if (L->weight_type == GDN_GGML_Q4_K) {

@@ -37,6 +37,32 @@ enum : uint32_t { DEV_ERR_TIMEOUT = 1u, DEV_ERR_BOUNDS = 2u };
 uint32_t* device_error_word();  // per-device __device__ word, looked up once per device
 int sm_count();                  // SMs of the current device (cached per device)
 
+// Programmatic dependent launch.  Kernels started with launch_pdl may be
+// scheduled while their predecessor in the stream is still running: each kernel
+// calls pdl_trigger() on entry (its own dependents may then be scheduled once
+// every CTA has started) and pdl_wait() before it touches any global memory that
+// an earlier kernel writes or reads (it returns once the predecessor has completed
+// and its writes are visible; without PDL it returns at once).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* name, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+               Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    return e == cudaSuccess ? 0 : cuda_status(e, name);
+}
+
 // Spin limit of bounded waits, in SM clock cycles (~1 s at 1.9 GHz).
 constexpr long long kWaitCycles = 2000000000LL;
 

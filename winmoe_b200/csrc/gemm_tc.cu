@@ -34,6 +34,7 @@
 // Split-K (grid.z > 1) writes fp32 partials that a second kernel sums in a
 // fixed order, so results do not depend on scheduling.
 #include <cuda.h>
+#include <algorithm>
 #include <type_traits>
 #include "gdn_common.cuh"
 #include "ptx_sm100.cuh"
@@ -153,6 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint16_t* __restrict__ dsc, int n, int k, int m, float* __restrict__ y, int64_t ldy,
                         int kt_per_split, uint32_t* __restrict__ err) {
     using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
+    pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
@@ -203,6 +205,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---- producers: warp 0 streams activation tiles, warp 2 int8 weight tiles
         if (lane == 0) {
             const bool is_a = (warp == 0);
+            // The weights never come from an earlier kernel, so their stream starts at
+            // once; the activations wait for the predecessor (programmatic launch).
+            if (is_a) pdl_wait();
             const int depth = is_a ? SA : S8;
             int issued = 0;
             bool ok = true;
@@ -400,6 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // y[r][c] = sum_z part[z][r][c], z in order (deterministic split-K reduction).
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t m, int64_t n,
                                      float* __restrict__ y, int64_t ldy) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= m * n) return;
     const int64_t r = i / n, c = i - r * n;
@@ -410,11 +417,73 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
 
 template <typename OutT>
 __global__ void convert_kernel(const void* __restrict__ x, int dtype, OutT* __restrict__ out, int64_t count) {
+    pdl_trigger();
+    pdl_wait();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= count) return;
     const float v = load_act(x, dtype, i);
     if constexpr (std::is_same<OutT, __half>::value) out[i] = __float2half_rn(v);
     else out[i] = __float2bfloat16_rn(v);
+}
+
+// 8 elements per thread: 16-byte loads (two for fp32 input) and one 16-byte store.
+__device__ __forceinline__ void load8(const float* p, float (&f)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+        f[2 * j] = v.x;
+        f[2 * j + 1] = v.y;
+    }
+}
+__device__ __forceinline__ void load8(const __half* p, float (&f)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+        f[2 * j] = v.x;
+        f[2 * j + 1] = v.y;
+    }
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <typename InT, typename OutT>
+__global__ void convert8_kernel(const InT* __restrict__ x, OutT* __restrict__ out, int64_t n8) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+        float f[8];
+        load8(x + 8 * i, f);
+        OutT* tag = nullptr;
+        *reinterpret_cast<uint4*>(out + 8 * i) =
+            make_uint4(pack2(f[0], f[1], tag), pack2(f[2], f[3], tag), pack2(f[4], f[5], tag), pack2(f[6], f[7], tag));
+    }
+}
+
+template <typename OutT>
+int launch_convert8(const void* x, int dtype, OutT* out, int64_t n8, cudaStream_t s) {
+    const unsigned g = (unsigned)std::min<int64_t>((n8 + 255) / 256, (int64_t)sm_count() * 8);
+    if (dtype == GDN_DTYPE_F32)
+        return launch_pdl("convert8_kernel", convert8_kernel<float, OutT>, dim3(g), dim3(256), 0, s,
+                          static_cast<const float*>(x), out, n8);
+    if (dtype == GDN_DTYPE_BF16)
+        return launch_pdl("convert8_kernel", convert8_kernel<__nv_bfloat16, OutT>, dim3(g), dim3(256), 0, s,
+                          static_cast<const __nv_bfloat16*>(x), out, n8);
+    return launch_pdl("convert8_kernel", convert8_kernel<__half, OutT>, dim3(g), dim3(256), 0, s,
+                      static_cast<const __half*>(x), out, n8);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -468,21 +537,24 @@ int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void
     auto kern = q8_0_gemm_tc_kernel<BN, MT, SA, S16, S8, BF16, SPLIT>;
     GDN_CUDA(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM));
     const dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM * MT - 1) / (BM * MT)), (unsigned)splits);
-    kern<<<grid, kThreads, L::SMEM, s>>>(ma, mb, d, (int)n, (int)k, (int)m, out, ld_out, kt_per,
-                                         device_error_word());
-    GDN_LAUNCH_CHECK("q8_0_gemm_tc_kernel");
-    return GDN_OK;
+    return launch_pdl("q8_0_gemm_tc_kernel", kern, grid, dim3(kThreads), L::SMEM, s, ma, mb, d, (int)n, (int)k,
+                      (int)m, out, ld_out, kt_per, device_error_word());
 }
 
 }  // namespace
 
 int launch_convert(const void* x, int x_dtype, void* out, bool to_bf16, int64_t count, cudaStream_t s) {
     if (count == 0) return GDN_OK;
+    if (count % 8 == 0 && aligned(x, 16) && aligned(out, 16)) {
+        if (to_bf16) return launch_convert8(x, x_dtype, static_cast<__nv_bfloat16*>(out), count / 8, s);
+        return launch_convert8(x, x_dtype, static_cast<__half*>(out), count / 8, s);
+    }
     const unsigned g = (unsigned)((count + 255) / 256);
-    if (to_bf16) convert_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(x, x_dtype, static_cast<__nv_bfloat16*>(out), count);
-    else convert_kernel<__half><<<g, 256, 0, s>>>(x, x_dtype, static_cast<__half*>(out), count);
-    GDN_LAUNCH_CHECK("convert_kernel");
-    return GDN_OK;
+    if (to_bf16)
+        return launch_pdl("convert_kernel", convert_kernel<__nv_bfloat16>, dim3(g), dim3(256), 0, s, x, x_dtype,
+                          static_cast<__nv_bfloat16*>(out), count);
+    return launch_pdl("convert_kernel", convert_kernel<__half>, dim3(g), dim3(256), 0, s, x, x_dtype,
+                      static_cast<__half*>(out), count);
 }
 
 size_t gemm_tc_workspace_bytes(int64_t m, int64_t n, int splits) {
@@ -497,8 +569,6 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
     if (ldy < n) return fail(GDN_ERR_SHAPE, "ldy < n");
     if (!aligned(a, 16) || !aligned(qs, 16) || !aligned(d, 4))
         return fail(GDN_ERR_ARG, "tensor-core GEMM operands must be 16-byte aligned (scales 4-byte)");
-    if (opt.split_precision && a_bf16)
-        return fail(GDN_ERR_TYPE, "split-precision tensor-core GEMM takes fp16 activations");
     const int KT = (int)(k / BK);
     int splits = opt.splits < 1 ? 1 : opt.splits;
     int kt_per = (KT + splits - 1) / splits;
@@ -514,6 +584,8 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
     }
     // Two M tiles per CTA share each dequantised weight tile once m > 128.
     // Ring depths <SA, S16, S8> fill ~224 KB of shared memory.
+    if (opt.split_precision && a_bf16)
+        return fail(GDN_ERR_TYPE, "split-precision tensor-core GEMM takes fp16 activations");
     const bool two = m > BM;
     int st;
     if (opt.split_precision) {
@@ -536,8 +608,9 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
     }
     if (st || splits == 1) return st;
     const int64_t cnt = m * n;
-    splitk_reduce_kernel<<<(unsigned)((cnt + 255) / 256), 256, 0, s>>>(out, splits, m, n, y, ldy);
-    GDN_LAUNCH_CHECK("splitk_reduce_kernel");
+    st = launch_pdl("splitk_reduce_kernel", splitk_reduce_kernel, dim3((unsigned)((cnt + 255) / 256)), dim3(256), 0,
+                    s, (const float*)out, splits, m, n, y, ldy);
+    if (st) return st;
     return GDN_OK;
 }
 

@@ -134,6 +134,8 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
                                                            const float* __restrict__ conv_w, bf16* __restrict__ qn,
                                                            bf16* __restrict__ kn, bf16* __restrict__ vb, int qkv,
                                                            int hk) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int nchunk = qkv / HD;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -207,6 +209,8 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
 __global__ void prefill_gates_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T, int64_t Tp,
                                      const float* __restrict__ ssm_a, const float* __restrict__ dt_bias,
                                      float* __restrict__ glog, float* __restrict__ beta, int qkv, int hv) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= Tp * hv) return;
     const int h = (int)(i / Tp);
@@ -243,6 +247,8 @@ __global__ void prefill_gates_kernel(const float* __restrict__ proj, int64_t ldp
 __global__ void __launch_bounds__(1024) prefill_window_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T,
                                                               float* __restrict__ conv_buf,
                                                               int32_t* __restrict__ conv_pos, int qkv) {
+    pdl_trigger();
+    pdl_wait();
     const int p0 = *conv_pos;
     for (int ch = threadIdx.x; ch < qkv; ch += blockDim.x)
         for (int64_t i = (T > 4 ? T - 4 : 0); i < T; i++)
@@ -270,6 +276,8 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
                                                           bf16* __restrict__ up, bf16* __restrict__ ek,
                                                           float* __restrict__ gcum, float* __restrict__ gchunk,
                                                           int64_t Tp, int hk, int hv, int head_map) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     LocalSmem& sm = *reinterpret_cast<LocalSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     const int c = blockIdx.x, h = blockIdx.y;
@@ -394,6 +402,8 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
                                                          const float* __restrict__ gchunk, float* __restrict__ S,
                                                          bf16* __restrict__ sc, bf16* __restrict__ dl, int64_t Tp,
                                                          int64_t nc) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     ScanSmem& sm = *reinterpret_cast<ScanSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     const int slab = blockIdx.x, h = blockIdx.y;
@@ -548,6 +558,8 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
                                                         const float* __restrict__ head_norm,
                                                         __half* __restrict__ gated, int64_t T, int64_t Tp, int hk,
                                                         int hv, int qkv, int head_map) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     OutSmem& sm = *reinterpret_cast<OutSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     const int c = blockIdx.x, h = blockIdx.y;
@@ -746,17 +758,18 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     if ((st = phase_mark(1, s))) return st;
     {
         const int64_t warps = (D.Tp / kTokBlock) * (D.qkv / HD);
-        prefill_prep_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(
-            W.proj, D.ldp, T, D.Tp, conv ? conv_buf : nullptr, conv_pos, conv ? L->conv1d_w : nullptr, W.qn, W.kn,
-            W.vb, D.qkv, D.hk);
-        GDN_LAUNCH_CHECK("prefill_prep_kernel");
+        st = launch_pdl("prefill_prep_kernel", prefill_prep_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0,
+                        s, W.proj, D.ldp, T, D.Tp, conv ? conv_buf : nullptr, conv_pos,
+                        conv ? L->conv1d_w : nullptr, W.qn, W.kn, W.vb, D.qkv, D.hk);
+        if (st) return st;
         const int64_t n = D.Tp * D.hv;
-        prefill_gates_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W.proj, D.ldp, T, D.Tp, L->ssm_a,
-                                                                           L->dt_bias, W.glog, W.beta, D.qkv, D.hv);
-        GDN_LAUNCH_CHECK("prefill_gates_kernel");
+        st = launch_pdl("prefill_gates_kernel", prefill_gates_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                        s, W.proj, D.ldp, T, D.Tp, L->ssm_a, L->dt_bias, W.glog, W.beta, D.qkv, D.hv);
+        if (st) return st;
         if (conv) {
-            prefill_window_kernel<<<1, 1024, 0, s>>>(W.proj, D.ldp, T, conv_buf, conv_pos, D.qkv);
-            GDN_LAUNCH_CHECK("prefill_window_kernel");
+            st = launch_pdl("prefill_window_kernel", prefill_window_kernel, dim3(1), dim3(1024), 0, s, W.proj, D.ldp,
+                            T, conv_buf, conv_pos, D.qkv);
+            if (st) return st;
         }
     }
 
@@ -765,20 +778,21 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     {
         const size_t sm1 = sizeof(LocalSmem) + 128;
         if ((st = set_smem(chunk_local_kernel, sm1))) return st;
-        chunk_local_kernel<<<dim3((unsigned)D.nc, (unsigned)D.hv), 256, sm1, s>>>(
-            W.kn, W.vb, W.glog, W.beta, W.wp, W.up, W.ek, W.gcum, W.gchunk, D.Tp, D.hk, D.hv, L->head_map);
-        GDN_LAUNCH_CHECK("chunk_local_kernel");
+        st = launch_pdl("chunk_local_kernel", chunk_local_kernel, dim3((unsigned)D.nc, (unsigned)D.hv), dim3(256),
+                        sm1, s, W.kn, W.vb, W.glog, W.beta, W.wp, W.up, W.ek, W.gcum, W.gchunk, D.Tp, D.hk, D.hv,
+                        L->head_map);
+        if (st) return st;
         const size_t sm2 = sizeof(ScanSmem) + 128;
         if ((st = set_smem(chunk_scan_kernel, sm2))) return st;
-        chunk_scan_kernel<<<dim3(HD / BV, (unsigned)D.hv), 128, sm2, s>>>(W.wp, W.up, W.ek, W.gchunk, S, W.sc, W.dl,
-                                                                          D.Tp, D.nc);
-        GDN_LAUNCH_CHECK("chunk_scan_kernel");
+        st = launch_pdl("chunk_scan_kernel", chunk_scan_kernel, dim3(HD / BV, (unsigned)D.hv), dim3(128), sm2, s,
+                        W.wp, W.up, W.ek, W.gchunk, S, W.sc, W.dl, D.Tp, D.nc);
+        if (st) return st;
         const size_t sm3 = sizeof(OutSmem) + 128;
         if ((st = set_smem(chunk_out_kernel, sm3))) return st;
-        chunk_out_kernel<<<dim3((unsigned)D.nc, (unsigned)D.hv), 128, sm3, s>>>(
-            W.qn, W.kn, W.sc, W.dl, W.gcum, W.proj, D.ldp, L->head_norm, W.gated, T, D.Tp, D.hk, D.hv, D.qkv,
-            L->head_map);
-        GDN_LAUNCH_CHECK("chunk_out_kernel");
+        st = launch_pdl("chunk_out_kernel", chunk_out_kernel, dim3((unsigned)D.nc, (unsigned)D.hv), dim3(128), sm3, s,
+                        W.qn, W.kn, W.sc, W.dl, W.gcum, W.proj, D.ldp, L->head_norm, W.gated, T, D.Tp, D.hk, D.hv,
+                        D.qkv, L->head_map);
+        if (st) return st;
     }
 
     // ---- output projection

@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
                                                        int64_t n_rows, int64_t k, const void* x,
                                                        int x_dtype, int64_t m, float* __restrict__ y,
                                                        int64_t ldy, int rows_per_block) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float xs[];
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
@@ -201,6 +203,8 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
                                                        int64_t n_rows, int64_t k, const void* x,
                                                        int x_dtype, int64_t m, float* __restrict__ y,
                                                        int64_t ldy, int rows_per_block) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float xs[];  // [mb][k] then xsum16 [mb][k/16]
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
@@ -325,9 +329,8 @@ static int run_q8_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k
     if (st) return st;
     const int rpb = rows_per_block(n, (m + MB - 1) / MB);
     const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
-    q8_0_gemv_kernel<MB><<<grid, 256, smem, s>>>(qs, d, n, k, x, dt, m, y, ldy, rpb);
-    GDN_LAUNCH_CHECK("q8_0_gemv_kernel");
-    return GDN_OK;
+    return launch_pdl("q8_0_gemv_kernel", q8_0_gemv_kernel<MB>, grid, dim3(256), smem, s, qs, d, n, k, x, dt, m, y,
+                      ldy, rpb);
 }
 
 int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
@@ -360,9 +363,8 @@ static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int d
     if (st) return st;
     const int rpb = rows_per_block(n, (m + MB - 1) / MB);
     const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
-    q4_k_gemv_kernel<MB><<<grid, 256, smem, s>>>(static_cast<const uint8_t*>(w), n, k, x, dt, m, y, ldy, rpb);
-    GDN_LAUNCH_CHECK("q4_k_gemv_kernel");
-    return GDN_OK;
+    return launch_pdl("q4_k_gemv_kernel", q4_k_gemv_kernel<MB>, grid, dim3(256), smem, s,
+                      static_cast<const uint8_t*>(w), n, k, x, dt, m, y, ldy, rpb);
 }
 
 int launch_q4_k_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
