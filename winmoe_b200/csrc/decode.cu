@@ -140,9 +140,8 @@ struct StateSlot {
 
 struct StateSmem {
     StateSlot slot[kStateBufs];
-    float delta[HD];
-    float red[8][HD];
-    double dred[4];
+    float red[8][HD];   // retrieve partials, one row per warp
+    float red2[8][HD];  // output partials
     uint64_t full[kStateBufs];
 };
 
@@ -187,6 +186,12 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
     }
     __syncthreads();
 
+    // Lane l owns value columns 4l..4l+3; warp w owns key rows 16w..16w+15.  Per
+    // tile two block barriers: (A) after the retrieve partials, from which every
+    // thread forms the delta of its own columns, and (B) after the output partials,
+    // from which every warp forms the whole output row (the RMSNorm needs all 128).
+    const float4 hn = head_norm != nullptr ? reinterpret_cast<const float4*>(head_norm)[l]
+                                           : make_float4(1.f, 1.f, 1.f, 1.f);
     bool ok = true;
     for (int i = 0; i < count; i++) {
         const int64_t tile = first + i;
@@ -199,84 +204,105 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
 #pragma unroll
         for (int r = 0; r < 16; r++) s[r] = Sv[(16 * w + r) * (HD / 4) + l];
         const float dg = sl.gate.x, bt = sl.gate.y;
+        const float4 vv = reinterpret_cast<const float4*>(sl.v)[l];
+        const float4 zz = reinterpret_cast<const float4*>(sl.z)[l];
+        float kr[16], qr[16];
+#pragma unroll
+        for (int r = 0; r < 16; r += 4) {
+            const float4 k4 = reinterpret_cast<const float4*>(sl.k + 16 * w)[r / 4];
+            const float4 q4 = reinterpret_cast<const float4*>(sl.q + 16 * w)[r / 4];
+            kr[r] = k4.x; kr[r + 1] = k4.y; kr[r + 2] = k4.z; kr[r + 3] = k4.w;
+            qr[r] = q4.x; qr[r + 1] = q4.y; qr[r + 2] = q4.z; qr[r + 3] = q4.w;
+        }
 
         // ---- decay + retrieve (deltanet_impl.h:298-307)
         float4 rp = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int r = 0; r < 16; r++) {
-            const float kr = sl.k[16 * w + r];
             s[r].x = __fmul_rn(s[r].x, dg);
             s[r].y = __fmul_rn(s[r].y, dg);
             s[r].z = __fmul_rn(s[r].z, dg);
             s[r].w = __fmul_rn(s[r].w, dg);
-            rp.x = fmaf(kr, s[r].x, rp.x);
-            rp.y = fmaf(kr, s[r].y, rp.y);
-            rp.z = fmaf(kr, s[r].z, rp.z);
-            rp.w = fmaf(kr, s[r].w, rp.w);
+            rp.x = fmaf(kr[r], s[r].x, rp.x);
+            rp.y = fmaf(kr[r], s[r].y, rp.y);
+            rp.z = fmaf(kr[r], s[r].z, rp.z);
+            rp.w = fmaf(kr[r], s[r].w, rp.w);
         }
         reinterpret_cast<float4*>(sm.red[w])[l] = rp;
-        __syncthreads();
-        if (t < HD) {
-            float rr = 0.0f;
+        __syncthreads();  // (A)
+        float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int ww = 0; ww < 8; ww++) rr += sm.red[ww][t];
-            sm.delta[t] = __fmul_rn(bt, __fsub_rn(sl.v[t], rr));  // deltanet_impl.h:311-317
+        for (int ww = 0; ww < 8; ww++) {
+            const float4 p = reinterpret_cast<const float4*>(sm.red[ww])[l];
+            rr.x += p.x;
+            rr.y += p.y;
+            rr.z += p.z;
+            rr.w += p.w;
         }
-        __syncthreads();
+        // delta = beta (v - S^T k)  (deltanet_impl.h:311-317)
+        const float4 dl = make_float4(__fmul_rn(bt, __fsub_rn(vv.x, rr.x)), __fmul_rn(bt, __fsub_rn(vv.y, rr.y)),
+                                      __fmul_rn(bt, __fsub_rn(vv.z, rr.z)), __fmul_rn(bt, __fsub_rn(vv.w, rr.w)));
 
         // ---- update + output read (deltanet_impl.h:320-347); the state goes back to HBM
-        const float4 dl = reinterpret_cast<const float4*>(sm.delta)[l];
         float4 op = make_float4(0.f, 0.f, 0.f, 0.f);
         float4* So = reinterpret_cast<float4*>(S + (b * hv + h) * (int64_t)kTileFloats);
 #pragma unroll
         for (int r = 0; r < 16; r++) {
-            const float kr = sl.k[16 * w + r];
-            const float qr = sl.q[16 * w + r];
-            s[r].x = fmaf(kr, dl.x, s[r].x);
-            s[r].y = fmaf(kr, dl.y, s[r].y);
-            s[r].z = fmaf(kr, dl.z, s[r].z);
-            s[r].w = fmaf(kr, dl.w, s[r].w);
-            op.x = fmaf(qr, s[r].x, op.x);
-            op.y = fmaf(qr, s[r].y, op.y);
-            op.z = fmaf(qr, s[r].z, op.z);
-            op.w = fmaf(qr, s[r].w, op.w);
+            s[r].x = fmaf(kr[r], dl.x, s[r].x);
+            s[r].y = fmaf(kr[r], dl.y, s[r].y);
+            s[r].z = fmaf(kr[r], dl.z, s[r].z);
+            s[r].w = fmaf(kr[r], dl.w, s[r].w);
+            op.x = fmaf(qr[r], s[r].x, op.x);
+            op.y = fmaf(qr[r], s[r].y, op.y);
+            op.z = fmaf(qr[r], s[r].z, op.z);
+            op.w = fmaf(qr[r], s[r].w, op.w);
             So[(16 * w + r) * (HD / 4) + l] = s[r];
         }
-        __syncthreads();  // every warp is done with red[]
-        reinterpret_cast<float4*>(sm.red[w])[l] = op;
-        __syncthreads();
+        reinterpret_cast<float4*>(sm.red2[w])[l] = op;
+        // The slot's last generic read is above: order them before the bulk copy
+        // that refills it (async proxy); barrier (B) hands the slot over.  (Handing
+        // it back before the update measured slower: more reads in flight against
+        // the write-back.)
+        sm100::fence_proxy_async_smem();
+        __syncthreads();  // (B)
+        if (t == 0 && ok && i + kStateBufs < count) issue(i + kStateBufs);  // no new copy after a timeout
 
         // ---- output, per-head RMSNorm (deltanet_impl.h:350-361) and SiLU(z) gate (364-371)
-        float o = 0.0f;
-        if (t < HD) {
-            for (int ww = 0; ww < 8; ww++) o += sm.red[ww][t];
-            o = __fmul_rn(o, 1.0f / sqrtf((float)HD));
-            double so = (double)o * (double)o;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) so += __shfl_xor_sync(0xffffffffu, so, off);
-            if (l == 0) sm.dred[w] = so;
+        for (int ww = 0; ww < 8; ww++) {
+            const float4 p = reinterpret_cast<const float4*>(sm.red2[ww])[l];
+            o.x += p.x;
+            o.y += p.y;
+            o.z += p.z;
+            o.w += p.w;
         }
-        __syncthreads();
-        if (t < HD) {
-            const double tot = sm.dred[0] + sm.dred[1] + sm.dred[2] + sm.dred[3];
-            const float inv = 1.0f / sqrtf((float)(tot / HD) + 1e-6f);
-            float nv = __fmul_rn(o, inv);
-            if (head_norm != nullptr) nv = __fmul_rn(nv, head_norm[t]);
-            float zv = sl.z[t];
-            zv = fminf(fmaxf(zv, -88.0f), 88.0f);
-            const float gv = __fmul_rn(nv, zv / (1.0f + expf(-zv)));
-            const int64_t idx = b * inner + h * HD + t;
-            if (gated != nullptr) gated[idx] = gv;
-            if (gated_h != nullptr) gated_h[idx] = __float2half_rn(gv);
+        const float sc = 1.0f / sqrtf((float)HD);
+        o = make_float4(__fmul_rn(o.x, sc), __fmul_rn(o.y, sc), __fmul_rn(o.z, sc), __fmul_rn(o.w, sc));
+        double so = (double)o.x * o.x + (double)o.y * o.y + (double)o.z * o.z + (double)o.w * o.w;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) so += __shfl_xor_sync(0xffffffffu, so, off);
+        if ((l >> 2) == w) {  // each warp writes 16 of the 128 columns
+            const float inv = 1.0f / sqrtf((float)(so / HD) + 1e-6f);
+            const float ov[4] = {o.x, o.y, o.z, o.w}, zv4[4] = {zz.x, zz.y, zz.z, zz.w};
+            const float hv4[4] = {hn.x, hn.y, hn.z, hn.w};
+            float gv[4];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float nv = __fmul_rn(ov[c], inv);
+                if (head_norm != nullptr) nv = __fmul_rn(nv, hv4[c]);
+                const float zv = fminf(fmaxf(zv4[c], -88.0f), 88.0f);
+                gv[c] = __fmul_rn(nv, zv / (1.0f + expf(-zv)));
+            }
+            const int64_t idx = b * inner + h * HD + 4 * l;
+            if (gated != nullptr) *reinterpret_cast<float4*>(gated + idx) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+            if (gated_h != nullptr) {
+                const __half2 h01 = __floats2half2_rn(gv[0], gv[1]), h23 = __floats2half2_rn(gv[2], gv[3]);
+                *reinterpret_cast<uint2*>(gated_h + idx) =
+                    make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+            }
         }
         if (t == 0 && h == 0 && conv_pos != nullptr) conv_pos[b] += 1;
-        // Every thread orders its generic reads of the slot before the bulk copy
-        // that refills it (async proxy), then the barrier hands the slot over.
-        sm100::fence_proxy_async_smem();
-        __syncthreads();  // slot i % kStateBufs fully consumed
-        if (t == 0 && ok && i + kStateBufs < count) {  // after a timed-out wait no new copy is issued
-            issue(i + kStateBufs);
-        }
     }
 }
 
