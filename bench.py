@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the T=4096 prefill leg")
+    ap.add_argument("--no-extra-legs", action="store_true",
+                    help="skip the batch-1 decode (config 1) and Q4_K sweep (config 4) legs")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the T=4096 prefill leg (one GPU); the line's value is the prefill's tok/s")
     return ap.parse_args()
@@ -196,13 +198,122 @@ def run_prefill(cfg, w, dev, steps, warmup, peak_tflops, peak_src):
     }
 
 
-def cpu_reference_run(cfg, tensors, n_calls, seqs, act_mode):
+def decode_b1_bytes(cfg):
+    """Algorithmic HBM bytes of one batch-1 decode token (config 1): Q8_0 weights
+    once, state read + write, conv window (3 rows read, 1 written), conv weights,
+    activations."""
+    w = (cfg.in_proj_rows * cfg.hidden + cfg.hidden * cfg.inner) // 32 * 34
+    d2 = cfg.head_dim * cfg.head_dim
+    act = (cfg.hidden + cfg.in_proj_rows + cfg.qkv_dim + cfg.inner + cfg.hidden) * 4
+    return w + cfg.num_v_heads * d2 * 8 + 4 * cfg.qkv_dim * 4 + cfg.qkv_dim * 16 + act
+
+
+def run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, with_cpu):
+    """Config 1: one sequence from a zero state, 64 fp32 tokens (seed 0), one token per step."""
+    import torch
+    from winmoe_b200 import layer as L, synth
+    steps = 64
+    xs = torch.from_numpy(synth.hidden_states(steps, cfg.hidden)).to(dev)
+    out = torch.empty((1, cfg.hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    warm = L.DeltaNetState.zeros(cfg, 1, dev)
+    for i in range(3):
+        L.decode_step(w, warm, xs[i:i + 1], out, stream)
+    st = L.DeltaNetState.zeros(cfg, 1, dev)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        L.decode_step(w, st, xs[i:i + 1], out, stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    nb = decode_b1_bytes(cfg)
+    ach = nb / (ms / 1e3) / 1e9
+    res = {"workload": "decode B=1 (config 1): 64 consecutive tokens of one sequence from a zero state, fp32 x",
+           "value": 1e3 / ms, "unit": "tok/s", "ms_per_token": ms, "steps": steps, "warmup": 3,
+           "roofline": {"bound": "hbm", "kernel": "whole decode step", "achieved": ach, "peak": hbm_peak,
+                        "unit": "GB/s", "frac": ach / hbm_peak, "peak_source": peak_src,
+                        "algorithmic_bytes_per_token": nb}}
+    if with_cpu:
+        dt, kind = cpu_reference_run(cfg, tensors, 64, 1, 0, zero_state=True)
+        res["cpu_baseline"] = {"value": 64 / dt, "unit": "tok/s",
+                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)), "kind": kind,
+                               "sample": "the same 64 tokens through the reference's deltanet_forward (unmodified "
+                                         "Q8_0/Q8_K dispatch)"}
+    return res
+
+
+def q4k_call_bytes(cfg, B):
+    """Config 4: Q4_K bytes of the four projections plus fp32 activations in and out."""
+    w = (cfg.in_proj_rows * cfg.hidden + cfg.hidden * cfg.inner) // 256 * 144
+    return w + B * (cfg.hidden + cfg.inner) * 4 * 2
+
+
+def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
+    """Config 4: the four projections as Q4_K, dequant-GEMV at batch 1 / 8 / 32."""
+    import torch
+    from winmoe_b200 import layer as L, synth
+    t = synth.layer_tensors(cfg, weight_type=12)
+    w_in = torch.from_numpy(t.in_proj).to(dev)
+    w_out = torch.from_numpy(t.out_proj).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    rows = {}
+    for B in (1, 8, 32):
+        gen = torch.Generator().manual_seed(40 + B)
+        xi = torch.randn((B, cfg.hidden), generator=gen).to(dev)
+        xo = torch.randn((B, cfg.inner), generator=gen).to(dev)
+        yi = torch.empty((B, cfg.in_proj_rows), dtype=torch.float32, device=dev)
+        yo = torch.empty((B, cfg.hidden), dtype=torch.float32, device=dev)
+
+        def call():
+            L.gemm_q4_k(w_in, cfg.in_proj_rows, cfg.hidden, xi, out=yi, stream=stream)
+            L.gemm_q4_k(w_out, cfg.hidden, cfg.inner, xo, out=yo, stream=stream)
+        for _ in range(3):
+            call()
+        reps = 50
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        nb = q4k_call_bytes(cfg, B)
+        ach = nb / (ms / 1e3) / 1e9
+        rows[f"B={B}"] = {"us_per_call": ms * 1e3, "tok_per_s": B / (ms / 1e3), "achieved_gbs": ach,
+                          "frac": ach / hbm_peak, "algorithmic_bytes_per_call": nb}
+    res = {"workload": "Q4_K projection sweep (config 4): in_proj (qkvz + ba rows) and out_proj, dequant-GEMV, "
+                       "fp32 activations; one call = the four projections for B tokens",
+           "roofline_peak": {"unit": "GB/s", "peak": hbm_peak, "peak_source": peak_src}, "batches": rows}
+    if with_cpu:
+        from oracle import oracle as O
+        orc = O.ref() if O.ref_available() else O.port()
+        x = synth.hidden_states(2, cfg.inner, seed=45)
+        t0 = time.perf_counter()
+        n = 4
+        for i in range(n):
+            orc.quant_matvec(t.in_proj, x[i % 2, :cfg.hidden], cfg.in_proj_rows, cfg.hidden, 12, O.ACT_EXACT)
+            orc.quant_matvec(t.out_proj, x[i % 2], cfg.hidden, cfg.inner, 12, O.ACT_EXACT)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": n / dt, "unit": "tok/s",
+                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                               "kind": "reference" if O.ref_available() else "port",
+                               "sample": f"{n} tokens through the reference's quant_matvec type 12 (q4k_matvec with "
+                                         "Q8_K activations) for the four projections; the reference has no batched "
+                                         "Q4_K GEMM, so B tokens cost B times this"}
+    return res
+
+
+def cpu_reference_run(cfg, tensors, n_calls, seqs, act_mode, zero_state=False):
     """Times n_calls of the reference's deltanet_forward over `seqs` prefilled sequences."""
     from oracle import oracle as O
     from winmoe_b200 import synth
     orc = O.ref() if O.ref_available() else O.port()
     kind = "reference" if O.ref_available() else "port"
-    states = [synth.prefilled_state(cfg, b) for b in range(seqs)]
+    states = [np.zeros((cfg.num_v_heads, cfg.head_dim, cfg.head_dim), np.float32) if zero_state
+              else synth.prefilled_state(cfg, b) for b in range(seqs)]
     convs = [np.zeros((4, cfg.qkv_dim), np.float32) for _ in range(seqs)]
     poss = [np.zeros(1, np.int32) for _ in range(seqs)]
     xs = synth.hidden_states(n_calls, cfg.hidden, seed=11)
@@ -381,6 +492,9 @@ def run_ours(args):
     }
     if world == 1 and not args.no_prefill:
         line["prefill"] = run_prefill(cfg, w, dev, min(K, 8), W, tc_peak, peak_src)
+    if world == 1 and not args.no_extra_legs:
+        line["decode_b1"] = run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, not args.no_cpu_baseline)
+        line["q4k_sweep"] = run_q4k_sweep(cfg, dev, hbm_peak, peak_src, not args.no_cpu_baseline)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, kind = cpu_reference_run(cfg, tensors, 64, 4, 0)
         cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))

@@ -86,6 +86,17 @@ __device__ __forceinline__ void stage_x(float* xs, const void* x, int dtype, int
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) xs[i] = load_act(x, dtype, m0 * k + i);
 }
 
+// The same with 4 floats of padding after every 16 (row length kp = k * 5 / 4):
+// 16-element chunks that consecutive lanes read start on distinct bank groups.
+__device__ __forceinline__ int64_t padded(int64_t i) { return i + ((i >> 4) << 2); }
+__device__ __forceinline__ void stage_x_padded(float* xs, const void* x, int dtype, int64_t m0, int mb,
+                                               int64_t k) {
+    const int64_t kp = k + (k >> 2);
+    for (int j = 0; j < mb; j++)
+        for (int64_t e = threadIdx.x; e < k; e += blockDim.x)
+            xs[j * kp + padded(e)] = load_act(x, dtype, (m0 + j) * k + e);
+}
+
 // Q8_0 GEMV: each warp owns one weight row at a time; lane l reads the 16-byte
 // chunks l, l+32, ... of the row's int8 plane (coalesced 512 B per warp load)
 // and the fp16 scale of the 32-block each chunk belongs to.  The block sum
@@ -99,10 +110,11 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
                                                        int64_t ldy, int rows_per_block) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ float xs[];
+    extern __shared__ float xs[];  // [mb][k * 5 / 4], padded (lane l reads chunk l)
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
-    stage_x(xs, x, x_dtype, m0, mb, k);
+    const int64_t kp = k + (k >> 2);
+    stage_x_padded(xs, x, x_dtype, m0, mb, k);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nwarps = blockDim.x >> 5;
@@ -114,28 +126,42 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
         float acc[MB];
 #pragma unroll
         for (int j = 0; j < MB; j++) acc[j] = 0.0f;
-        for (int64_t c = lane; c < nchunk; c += 32) {
-            const uint4 q = __ldg(qrow + c);
-            const float s = fp16_bits_to_float(__ldg(drow + (c >> 1)));
-            float f[16];
-            i8x4_to_f32(q.x, f);
-            i8x4_to_f32(q.y, f + 4);
-            i8x4_to_f32(q.z, f + 8);
-            i8x4_to_f32(q.w, f + 12);
+        for (int64_t c0 = lane; c0 < nchunk; c0 += 4 * 32) {  // four chunks per lane in flight
+            uint4 qv[4];
+            uint16_t sv[4];
 #pragma unroll
-            for (int j = 0; j < MB; j++) {
-                if (j < mb) {
-                    const float4* xv = reinterpret_cast<const float4*>(xs + (int64_t)j * k + c * 16);
-                    float bs = 0.0f;
+            for (int u = 0; u < 4; u++) {
+                const int64_t c = c0 + 32 * u;
+                if (c < nchunk) {
+                    qv[u] = __ldg(qrow + c);
+                    sv[u] = __ldg(drow + (c >> 1));
+                }
+            }
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float4 v = xv[e];
-                        bs = fmaf(f[4 * e + 0], v.x, bs);
-                        bs = fmaf(f[4 * e + 1], v.y, bs);
-                        bs = fmaf(f[4 * e + 2], v.z, bs);
-                        bs = fmaf(f[4 * e + 3], v.w, bs);
+            for (int u = 0; u < 4; u++) {
+                const int64_t c = c0 + 32 * u;
+                if (c >= nchunk) break;
+                const float s = fp16_bits_to_float(sv[u]);
+                float f[16];
+                i8x4_to_f32(qv[u].x, f);
+                i8x4_to_f32(qv[u].y, f + 4);
+                i8x4_to_f32(qv[u].z, f + 8);
+                i8x4_to_f32(qv[u].w, f + 12);
+#pragma unroll
+                for (int j = 0; j < MB; j++) {
+                    if (j < mb) {
+                        const float4* xv = reinterpret_cast<const float4*>(xs + (int64_t)j * kp + c * 20);
+                        float bs = 0.0f;
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const float4 v = xv[e];
+                            bs = fmaf(f[4 * e + 0], v.x, bs);
+                            bs = fmaf(f[4 * e + 1], v.y, bs);
+                            bs = fmaf(f[4 * e + 2], v.z, bs);
+                            bs = fmaf(f[4 * e + 3], v.w, bs);
+                        }
+                        acc[j] = fmaf(s, bs, acc[j]);
                     }
-                    acc[j] = fmaf(s, bs, acc[j]);
                 }
             }
         }
@@ -194,10 +220,10 @@ __global__ void q4_k_dequant_kernel(const uint8_t* __restrict__ blocks, float* _
     }
 }
 
-// Q4_K GEMV.  Lane l of a warp covers superblock (iter*4 + l/8) of the row and
-// the 16 qs bytes (l%8)*16.. of it, i.e. chunk c = (l%8)/2, bytes j0 = 16*(l%2).
-// With the sums of x over each 16-group precomputed (xsum16), a sub-block's
-// contribution is sc*sum(q*x) - m*sum(x): one FMA per weight and activation row.
+// Q4_K GEMV (quant_matvec type 12 with fp32 activations; the reference GPU
+// kernel is engine/runtime/gpu_offload.cu:237-250).  A sub-block's contribution
+// is (d sc) sum(q x) - (dmin m) sum(x); the MB activation rows of block row
+// blockIdx.y share every weight load.
 template <int MB>
 __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restrict__ blocks,
                                                        int64_t n_rows, int64_t k, const void* x,
@@ -205,35 +231,44 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
                                                        int64_t ldy, int rows_per_block) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ float xs[];  // [mb][k] then xsum16 [mb][k/16]
+    extern __shared__ float xs[];  // [mb][k]
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
-    float* xsum = xs + (int64_t)mb * k;
     stage_x(xs, x, x_dtype, m0, mb, k);
-    __syncthreads();
-    const int64_t ng = k >> 4;
-    for (int64_t i = threadIdx.x; i < (int64_t)mb * ng; i += blockDim.x) {
-        const float* p = xs + i * 16;
-        float s = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 16; j++) s += p[j];
-        xsum[i] = s;
-    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nwarps = blockDim.x >> 5;
     const int64_t nsb = k >> 8;
-    const int sub = lane >> 3, c = (lane & 7) >> 1, half = lane & 1;
+    // A warp walks one row's superblocks; lane l takes the 4 quant bytes
+    // 32c + 4g .. +3 (c = l / 8, g = l % 8): low nibbles are weights 64c + 4g + e
+    // (sub-block 2c), high nibbles weights 64c + 32 + 4g + e (sub-block 2c + 1).
+    // The warp reads the 128 quant bytes as one line and each quarter-warp reads
+    // 128 contiguous bytes of x.  w = (d sc) q - dmin m is summed as
+    // (d sc) sum(q x) - (dmin m) sum(x) per lane.
+    const int c = lane >> 3, g = lane & 7;
     const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
     for (int64_t r = row0 + warp; r < row0 + rows_per_block && r < n_rows; r += nwarps) {
         const uint8_t* row = blocks + r * nsb * 144;
         float acc[MB];
 #pragma unroll
         for (int j = 0; j < MB; j++) acc[j] = 0.0f;
-        for (int64_t sb = sub; sb < nsb; sb += 4) {
-            const uint8_t* blk = row + sb * 144;
-            const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-            const uint4 q = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * c + 16 * half));
+        for (int64_t sb0 = 0; sb0 < nsb; sb0 += 4) {  // four superblocks per warp in flight
+          uint4 hv[4];
+          uint32_t qv[4];
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+              if (sb0 + u < nsb) {
+                  const uint8_t* blk = row + (sb0 + u) * 144;
+                  hv[u] = __ldg(reinterpret_cast<const uint4*>(blk));
+                  qv[u] = __ldg(reinterpret_cast<const uint32_t*>(blk + 16 + 32 * c + 4 * g));
+              }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int64_t sb = sb0 + u;
+            if (sb >= nsb) break;
+            const uint4 hdr = hv[u];
+            const uint32_t qw = qv[u];
             const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
             const float d = fp16_bits_to_float((uint16_t)(hdr.x & 0xFFFFu));
             const float dmin = fp16_bits_to_float((uint16_t)(hdr.x >> 16));
@@ -242,30 +277,23 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
             q4k_scale_min(2 * c + 1, hb + 4, s_hi, m_hi);
             const float sl = d * (float)s_lo, ml = dmin * (float)m_lo;
             const float sh = d * (float)s_hi, mh = dmin * (float)m_hi;
-            float lo[16], hi[16];
-            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                u4x4_to_f32(qw[j], lo + 4 * j);
-                u4x4_to_f32(qw[j] >> 4, hi + 4 * j);
-            }
-            const int64_t klo = sb * 256 + 64 * c + 16 * half;
+            float lo[4], hi[4];
+            u4x4_to_f32(qw, lo);
+            u4x4_to_f32(qw >> 4, hi);
+            const int64_t klo = sb * 256 + 64 * c + 4 * g;
 #pragma unroll
             for (int j = 0; j < MB; j++) {
                 if (j < mb) {
-                    const float* xl = xs + (int64_t)j * k + klo;
-                    const float* xh = xl + 32;
-                    float al = 0.0f, ah = 0.0f;
-#pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        al = fmaf(lo[e], xl[e], al);
-                        ah = fmaf(hi[e], xh[e], ah);
-                    }
-                    const float sxl = xsum[(int64_t)j * ng + (klo >> 4)];
-                    const float sxh = xsum[(int64_t)j * ng + (klo >> 4) + 2];
+                    const float4 xl = *reinterpret_cast<const float4*>(xs + (int64_t)j * k + klo);
+                    const float4 xh = *reinterpret_cast<const float4*>(xs + (int64_t)j * k + klo + 32);
+                    const float al = fmaf(lo[3], xl.w, fmaf(lo[2], xl.z, fmaf(lo[1], xl.y, lo[0] * xl.x)));
+                    const float ah = fmaf(hi[3], xh.w, fmaf(hi[2], xh.z, fmaf(hi[1], xh.y, hi[0] * xh.x)));
+                    const float sxl = (xl.x + xl.y) + (xl.z + xl.w);
+                    const float sxh = (xh.x + xh.y) + (xh.z + xh.w);
                     acc[j] += (sl * al - ml * sxl) + (sh * ah - mh * sxh);
                 }
             }
+          }
         }
 #pragma unroll
         for (int j = 0; j < MB; j++) {
@@ -306,8 +334,11 @@ int launch_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t
 
 // Weight rows per block (a multiple of the 8 warps, at most 32): fewer when
 // the grid would otherwise leave SMs idle (few weight rows, e.g. the gates).
-static int rows_per_block(int64_t n, int64_t groups) {
-    const int64_t want = 2 * (int64_t)sm_count();
+static int rows_per_block(int64_t n, int64_t groups, int mb) {
+    // one activation row per block: x staging is trivial, so aim for ~8 resident
+    // blocks per SM (one weight row per warp in flight); with more rows, larger
+    // blocks amortise the staging
+    const int64_t want = (mb == 1 ? 8 : 2) * (int64_t)sm_count();
     int rpb = 32;
     while (rpb > 8 && ((n + rpb - 1) / rpb) * groups < want) rpb -= 8;
     return rpb;
@@ -324,10 +355,10 @@ static int pick_mb(int64_t m, int64_t floats_per_row) {
 template <int MB>
 static int run_q8_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
                        int64_t m, float* y, int64_t ldy, cudaStream_t s) {
-    const size_t smem = (size_t)MB * k * sizeof(float);
+    const size_t smem = (size_t)MB * (k + k / 4) * sizeof(float);
     int st = smem_optin((const void*)q8_0_gemv_kernel<MB>, smem);
     if (st) return st;
-    const int rpb = rows_per_block(n, (m + MB - 1) / MB);
+    const int rpb = rows_per_block(n, (m + MB - 1) / MB, MB);
     const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
     return launch_pdl("q8_0_gemv_kernel", q8_0_gemv_kernel<MB>, grid, dim3(256), smem, s, qs, d, n, k, x, dt, m, y,
                       ldy, rpb);
@@ -335,10 +366,10 @@ static int run_q8_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k
 
 int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
                      int64_t m, float* y, int64_t ldy, cudaStream_t s) {
-    if ((size_t)k * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q8_0 gemv: k=%lld too large", (long long)k);
+    if ((size_t)(k + k / 4) * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q8_0 gemv: k=%lld too large", (long long)k);
     if (m <= 0 || n <= 0) return GDN_OK;
     if ((m + 7) / 8 > 65535) return fail(GDN_ERR_SHAPE, "q8_0 gemv: m=%lld too large", (long long)m);
-    switch (pick_mb(m, k)) {
+    switch (pick_mb(m, k + k / 4)) {
         case 1: return run_q8_gemv<1>(qs, d, n, k, x, dt, m, y, ldy, s);
         case 2: return run_q8_gemv<2>(qs, d, n, k, x, dt, m, y, ldy, s);
         case 4: return run_q8_gemv<4>(qs, d, n, k, x, dt, m, y, ldy, s);
@@ -358,10 +389,10 @@ int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t co
 template <int MB>
 static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
                        int64_t ldy, cudaStream_t s) {
-    const size_t smem = (size_t)MB * (k + k / 16) * sizeof(float);
+    const size_t smem = (size_t)MB * k * sizeof(float);
     int st = smem_optin((const void*)q4_k_gemv_kernel<MB>, smem);
     if (st) return st;
-    const int rpb = rows_per_block(n, (m + MB - 1) / MB);
+    const int rpb = rows_per_block(n, (m + MB - 1) / MB, MB);
     const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
     return launch_pdl("q4_k_gemv_kernel", q4_k_gemv_kernel<MB>, grid, dim3(256), smem, s,
                       static_cast<const uint8_t*>(w), n, k, x, dt, m, y, ldy, rpb);
@@ -369,10 +400,10 @@ static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int d
 
 int launch_q4_k_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
                      int64_t ldy, cudaStream_t s) {
-    if ((size_t)(k + k / 16) * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q4_k gemv: k=%lld too large", (long long)k);
+    if ((size_t)k * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q4_k gemv: k=%lld too large", (long long)k);
     if (m <= 0 || n <= 0) return GDN_OK;
     if ((m + 7) / 8 > 65535) return fail(GDN_ERR_SHAPE, "q4_k gemv: m=%lld too large", (long long)m);
-    switch (pick_mb(m, k + k / 16)) {
+    switch (pick_mb(m, k)) {
         case 1: return run_q4_gemv<1>(w, n, k, x, dt, m, y, ldy, s);
         case 2: return run_q4_gemv<2>(w, n, k, x, dt, m, y, ldy, s);
         case 4: return run_q4_gemv<4>(w, n, k, x, dt, m, y, ldy, s);
