@@ -38,9 +38,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "gated-DeltaNet tok/s (decode B=256, prefill T=4k); % of HBM/TC roofline"
 BATCH = 256
 # dram__bytes_read.sum + dram__bytes_write.sum of one gdn_state_kernel launch at
-# B = 256, from the ncu capture summarised in profiles/gdn_state_kernel_decode_b256.md
-# (None until that capture exists).
-NCU_STATE_TRAFFIC = None
+# B = 256, from the ncu capture summarised in profiles/gdn_state_kernel_decode_b256.md.
+NCU_STATE_TRAFFIC = 549_619_712 + 479_335_680
 
 
 def parse():
