@@ -235,6 +235,43 @@ GDN_API int gdn_prefill(const gdn_layer* layer, int64_t T, const void* x, int x_
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * gdn_prefill without the output projection, for value heads sharded over
+ * GPUs: writes the gated head outputs (deltanet_impl.h:364-371, before the
+ * out_proj of :374) as fp16 bits gated[T][num_v_heads * head_dim].  `layer`
+ * may be a slice of a full layer (its value heads [h0, h1) with their key
+ * groups: in_proj rows, conv weights, ssm_a / dt_bias of those heads); the
+ * out_proj planes must still be set.  No single counterpart in the reference,
+ * whose layer runs on one device; the slice's rows are computed exactly as in
+ * the whole layer.  Same workspace as gdn_prefill.
+ */
+GDN_API int gdn_prefill_gated(const gdn_layer* layer, int64_t T, const void* x, int x_dtype, uint16_t* gated,
+                              float* S, float* conv_buf, int32_t* conv_pos,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * out_proj of gathered head outputs: out[t - t0][hidden] = W_out . g[t] for
+ * tokens t in [t0, t1), where g[t] is the concatenation over b of
+ * gated[b][t][inner / blocks] (fp16 bits, as gdn_prefill_gated writes them
+ * and an all-gather over `blocks` ranks stacks them).  Q8_0 planes out_qs /
+ * out_d [hidden][inner] (deltanet_impl.h:374).  T >= 64 runs on the tensor
+ * cores exactly as gdn_prefill's out_proj, so a sharded layer reproduces the
+ * single-GPU output bit for bit; T < 64 needs blocks == 1.
+ */
+GDN_API int gdn_out_proj_gathered(const int8_t* out_qs, const uint16_t* out_d, int64_t hidden, int64_t inner,
+                                  const uint16_t* gated, int blocks, int64_t T, int64_t t0, int64_t t1,
+                                  float* out, void* stream);
+
+/*
+ * Residual add + RMSNorm between stacked layers, per row of `hidden`:
+ *   x <- x + add            (winmoe_inference.c:1652; add may be NULL)
+ *   y  = (x * scale) * w,   scale = 1 / sqrtf(float(sum x^2 / hidden) + 1e-6)
+ *                           (attention.h:29-44, the sum in double; w NULL = ones)
+ * x, add fp32 [T][hidden]; y [T][hidden] in y_dtype (F32, BF16 or F16).
+ */
+GDN_API int gdn_add_rmsnorm(float* x, const float* add, const float* w, void* y, int y_dtype,
+                            int64_t T, int64_t hidden, void* stream);
+
+/*
  * Optional phase timing of gdn_decode_step / gdn_prefill, for benchmarks.
  * While enabled (on the calling thread's current device), every call records a
  * CUDA event before and after each of its phases on its stream.

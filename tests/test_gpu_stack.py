@@ -1,0 +1,145 @@
+"""GPU tests of the layer stack (config 5's path): the residual + RMSNorm glue
+against the oracle, head sharding bit-identical to the single-GPU layer, a
+2-layer stack against the reference's token-by-token recurrence, and a 2-rank
+NCCL run (skipped with fewer than two GPUs)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from winmoe_b200 import GDNConfig, layer as L, synth
+from winmoe_b200.config import DIMS_35B
+from winmoe_b200.stack import StackLayer, add_rmsnorm, out_proj_gathered, prefill_gated, prefill_stack
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 2e-2  # bf16-input prefill bound
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def test_add_rmsnorm_matches_oracle():
+    P = O.port()
+    T, H = 37, 2048
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn((T, H), generator=g) * 3
+    add = torch.randn((T, H), generator=g)
+    w = 1 + 0.1 * torch.randn(H, generator=g)
+    xs = (x + add).numpy()
+    want = np.stack([P.rmsnorm(xs[t], w.numpy()) for t in range(T)])
+    xd = x.to(DEV)
+    y32 = torch.empty((T, H), device=DEV)
+    add_rmsnorm(xd, add.to(DEV), w.to(DEV), y32)
+    np.testing.assert_array_equal(xd.cpu().numpy(), xs)  # the residual add is one fp32 add
+    assert np.abs(y32.cpu().numpy() - want).max() <= 1e-6 * np.abs(want).max()
+    yb = torch.empty((T, H), dtype=torch.bfloat16, device=DEV)
+    add_rmsnorm(xd, None, w.to(DEV), yb)  # no add: x unchanged
+    np.testing.assert_array_equal(xd.cpu().numpy(), xs)
+    wb = torch.from_numpy(want).to(torch.bfloat16).float().numpy()
+    assert np.abs(yb.float().cpu().numpy() - wb).max() <= 2 ** -7 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_head_sharding_is_bit_identical(world):
+    """The G-way head-sharded layer, emulated on one GPU (slices run in turn,
+    out_proj over gathered blocks per token slice), equals gdn_prefill."""
+    cfg = DIMS_35B
+    t = synth.layer_tensors(cfg, layer=2)
+    T = 256
+    x = torch.randn((T, cfg.hidden), generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).to(DEV)
+    w = L.DeltaNetWeights.upload(cfg, t.in_proj, t.out_proj, t.conv1d_w, t.ssm_a, t.dt_bias, t.head_norm,
+                                 device=DEV)
+    st = L.DeltaNetState.zeros(cfg, 1, DEV)
+    want = L.prefill(w, st, x)
+    layers = [StackLayer.upload(cfg, t, r, world, DEV) for r in range(world)]
+    states = [lay.state(DEV) for lay in layers]
+    gated = [prefill_gated(lay.heads, s, x) for lay, s in zip(layers, states)]
+    gathered = torch.stack(gated)  # [G][T][inner/G]
+    ts = T // world
+    got = torch.cat([out_proj_gathered(layers[r].out_qs, layers[r].out_d, cfg, gathered, r * ts, (r + 1) * ts)
+                     for r in range(world)])
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    for lay, s in zip(layers, states):
+        assert torch.equal(s.S[0], st.S[0, lay.h0:lay.h1])
+        assert torch.equal(s.conv_pos, st.conv_pos)
+
+
+def _oracle_stack(cfg, tensors, xs):
+    """Token by token through every layer: x <- x + deltanet_forward_l(rmsnorm(x)) (ones weight)."""
+    P = O.port()
+    n = len(tensors)
+    S = [np.zeros((cfg.num_v_heads, 128, 128), np.float32) for _ in range(n)]
+    cb = [np.zeros((4, cfg.qkv_dim), np.float32) for _ in range(n)]
+    pos = [np.zeros(1, np.int32) for _ in range(n)]
+    ones = np.ones(cfg.hidden, np.float32)
+    out = []
+    for x in xs:
+        x = x.copy()
+        for l in range(n):
+            normed = P.rmsnorm(x, ones)
+            x = x + P.deltanet_forward(cfg, normed, S[l], cb[l], pos[l], tensors[l], act_mode=O.ACT_FP32)
+        out.append(x)
+    return np.stack(out)
+
+
+def test_two_layer_stack_matches_oracle():
+    cfg = GDNConfig(512, 2, 4, 128)
+    T = 70
+    tensors = [synth.layer_tensors(cfg, layer=l) for l in range(2)]
+    xs = synth.hidden_states(T, cfg.hidden, seed=4)
+    want = _oracle_stack(cfg, tensors, xs)
+    layers = [StackLayer.upload(cfg, t, 0, 1, DEV) for t in tensors]
+    states = [lay.state(DEV) for lay in layers]
+    x = torch.from_numpy(xs).to(DEV)
+    prefill_stack(layers, states, x)
+    assert rel_l2(x.cpu().numpy() - xs, want - xs) <= TOL  # the layers' contribution
+
+
+def _nccl_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    cfg = DIMS_35B
+    T = 256
+    tensors = [synth.layer_tensors(cfg, layer=l) for l in range(2)]
+    x0 = torch.randn((T, cfg.hidden), generator=torch.Generator().manual_seed(3))
+    layers = [StackLayer.upload(cfg, t, rank, world, f"cuda:{rank}") for t in tensors]
+    states = [lay.state(f"cuda:{rank}") for lay in layers]
+    x = x0.to(f"cuda:{rank}")
+    prefill_stack(layers, states, x, None, rank, world)
+    res = x.cpu()
+    if rank == 0:  # the same stack on one GPU
+        layers1 = [StackLayer.upload(cfg, t, 0, 1, "cuda:0") for t in tensors]
+        states1 = [lay.state("cuda:0") for lay in layers1]
+        x1 = x0.to("cuda:0")
+        prefill_stack(layers1, states1, x1)
+        q.put(bool(torch.equal(res, x1.cpu())))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_nccl_stack_is_bit_identical():
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 1000
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    same = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert same

@@ -61,6 +61,9 @@ SIGNATURES = {
     "gdn_decode_step": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gdn_decode_step_noalloc": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
     "gdn_prefill_workspace_size": (_sz, [C.POINTER(gdn_dims), _i64]),
+    "gdn_prefill_gated": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "gdn_out_proj_gathered": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _i64, _i64, _i64, _vp, _vp]),
+    "gdn_add_rmsnorm": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _vp]),
     "gdn_prefill": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gdn_profile_enable": (_int, [_int]),
     "gdn_decode_phase_ms": (_int, [C.POINTER(C.c_float), _int]),

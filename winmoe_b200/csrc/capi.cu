@@ -10,6 +10,7 @@
 #include "quant.cuh"
 #include "decode.cuh"
 #include "prefill.cuh"
+#include "stack.cuh"
 
 namespace gdn {
 
@@ -195,7 +196,48 @@ size_t gdn_prefill_workspace_size(const gdn_dims* dims, int64_t T) {
 
 int gdn_prefill(const gdn_layer* layer, int64_t T, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
                 int32_t* conv_pos, void* workspace, size_t workspace_bytes, void* stream) {
-    return prefill(layer, T, x, x_dtype, out, S, conv_buf, conv_pos, workspace, workspace_bytes, as_stream(stream));
+    if (out == nullptr) return fail(GDN_ERR_ARG, "out must be non-NULL");
+    return prefill(layer, T, x, x_dtype, out, nullptr, S, conv_buf, conv_pos, workspace, workspace_bytes,
+                   as_stream(stream));
+}
+
+int gdn_prefill_gated(const gdn_layer* layer, int64_t T, const void* x, int x_dtype, uint16_t* gated, float* S,
+                      float* conv_buf, int32_t* conv_pos, void* workspace, size_t workspace_bytes, void* stream) {
+    if (gated == nullptr) return fail(GDN_ERR_ARG, "gated must be non-NULL");
+    return prefill(layer, T, x, x_dtype, nullptr, reinterpret_cast<__half*>(gated), S, conv_buf, conv_pos, workspace,
+                   workspace_bytes, as_stream(stream));
+}
+
+int gdn_out_proj_gathered(const int8_t* out_qs, const uint16_t* out_d, int64_t hidden, int64_t inner,
+                          const uint16_t* gated, int blocks, int64_t T, int64_t t0, int64_t t1, float* out,
+                          void* stream) {
+    if (!out_qs || !out_d || !gated || !out) return fail(GDN_ERR_ARG, "out_proj gathered: NULL pointer");
+    if (hidden <= 0 || inner <= 0 || inner % 64 != 0 || blocks < 1 || inner % ((int64_t)blocks * 64) != 0)
+        return fail(GDN_ERR_SHAPE, "out_proj gathered: inner=%lld must split into %d blocks of a multiple of 64",
+                    (long long)inner, blocks);
+    if (T <= 0 || t0 < 0 || t1 > T || t0 >= t1) return fail(GDN_ERR_SHAPE, "out_proj gathered: bad token range");
+    if (!aligned(gated, 16) || !aligned(out, 16) || !aligned(out_qs, 16))
+        return fail(GDN_ERR_ARG, "out_proj gathered: pointers must be 16-byte aligned");
+    cudaStream_t s = as_stream(stream);
+    if (T < 64) {  // gdn_prefill's out_proj below 64 tokens: the CUDA-core GEMV
+        if (blocks != 1) return fail(GDN_ERR_SHAPE, "out_proj gathered: T < 64 needs blocks == 1");
+        return launch_q8_0_gemv(out_qs, out_d, hidden, inner, gated + t0 * inner, GDN_DTYPE_F16, t1 - t0, out,
+                                hidden, s);
+    }
+    TcOptions opt;  // one fp16 weight operand, as gdn_prefill's out_proj
+    opt.a_blk_k = inner / blocks;
+    opt.a_rows = T;
+    opt.a_row0 = t0;
+    return launch_q8_0_gemm_tc(out_qs, out_d, hidden, inner, gated, false, t1 - t0, out, hidden, opt, s);
+}
+
+int gdn_add_rmsnorm(float* x, const float* add, const float* w, void* y, int y_dtype, int64_t T, int64_t hidden,
+                    void* stream) {
+    if (!x || !y) return fail(GDN_ERR_ARG, "add_rmsnorm: x and y must be non-NULL");
+    if (T < 0 || hidden <= 0 || T > INT32_MAX) return fail(GDN_ERR_SHAPE, "add_rmsnorm: bad shape");
+    if (y_dtype != GDN_DTYPE_F32 && y_dtype != GDN_DTYPE_BF16 && y_dtype != GDN_DTYPE_F16)
+        return fail(GDN_ERR_TYPE, "add_rmsnorm: y_dtype %d is not supported", y_dtype);
+    return launch_add_rmsnorm(x, add, w, y, y_dtype, T, hidden, as_stream(stream));
 }
 
 int gdn_profile_enable(int on) { return profile_enable(on); }

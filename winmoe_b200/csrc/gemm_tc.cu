@@ -152,7 +152,7 @@ template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     q8_0_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const uint16_t* __restrict__ dsc, int n, int k, int m, float* __restrict__ y, int64_t ldy,
-                        int kt_per_split, uint32_t* __restrict__ err) {
+                        int kt_per_split, int a_blk_k, int a_row0, uint32_t* __restrict__ err) {
     using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
@@ -217,10 +217,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 if (is_a) {
                     mbar_arrive_expect_tx(a_full(s), MT * L::A_BYTES);
+                    const int kk = (kt0 + t) * BK;
 #pragma unroll
-                    for (int mt = 0; mt < MT; mt++)
-                        tma_load_2d(sbase + L::A_OFF + (s * MT + mt) * L::A_BYTES, &tm_a, (kt0 + t) * BK,
-                                    m0 + mt * BM, a_full(s));
+                    for (int mt = 0; mt < MT; mt++) {
+                        const uint32_t dst = sbase + L::A_OFF + (s * MT + mt) * L::A_BYTES;
+                        if (a_blk_k > 0)  // activations stored as K blocks [k / a_blk_k][rows][a_blk_k]
+                            tma_load_3d(dst, &tm_a, kk % a_blk_k, a_row0 + m0 + mt * BM, kk / a_blk_k, a_full(s));
+                        else
+                            tma_load_2d(dst, &tm_a, kk, m0 + mt * BM, a_full(s));
+                    }
                 } else {
                     mbar_arrive_expect_tx(b8_full(s), L::B8_BYTES);
                     tma_load_2d(sbase + L::B8_OFF + s * L::B8_BYTES, &tm_b, (kt0 + t) * BK, n0, b8_full(s));
@@ -521,15 +526,39 @@ int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint
     return GDN_OK;
 }
 
+// 3-D map of activations stored as K blocks: [nblk][rows][blk_k], 128B-swizzled
+// boxes of BK x BM x 1.
+int make_map_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t blk_k, uint64_t rows,
+                uint64_t nblk, uint64_t row_bytes, uint64_t blk_bytes, uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn enc;
+    int st = get_encode(&enc);
+    if (st) return st;
+    const cuuint64_t dims[3] = {blk_k, rows, nblk};
+    const cuuint64_t strides[2] = {row_bytes, blk_bytes};
+    const cuuint32_t box[3] = {box_inner, box_outer, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GDN_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+    return GDN_OK;
+}
+
 namespace {
+
+struct ALayout {
+    int64_t blk_k = 0, rows = 0, row0 = 0;  // see TcOptions
+};
 
 template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT>
 int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* a, int64_t m, float* out,
-           int64_t ld_out, int splits, int kt_per, cudaStream_t s) {
+           int64_t ld_out, int splits, int kt_per, const ALayout& al, cudaStream_t s) {
     using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
     CUtensorMap ma, mb;
-    int st = make_map_2d(&ma, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, (uint64_t)k,
-                         (uint64_t)m, (uint64_t)k * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    const CUtensorMapDataType adt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    int st = al.blk_k > 0 ? make_map_3d(&ma, adt, a, (uint64_t)al.blk_k, (uint64_t)al.rows, (uint64_t)(k / al.blk_k),
+                                        (uint64_t)al.blk_k * 2, (uint64_t)al.rows * al.blk_k * 2, BK, BM)
+                          : make_map_2d(&ma, adt, a, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2, BK, BM,
+                                        CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     st = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, qs, (uint64_t)k, (uint64_t)n, (uint64_t)k, BK, BN,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -538,7 +567,7 @@ int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void
     GDN_CUDA(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM));
     const dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM * MT - 1) / (BM * MT)), (unsigned)splits);
     return launch_pdl("q8_0_gemm_tc_kernel", kern, grid, dim3(kThreads), L::SMEM, s, ma, mb, d, (int)n, (int)k,
-                      (int)m, out, ld_out, kt_per, device_error_word());
+                      (int)m, out, ld_out, kt_per, (int)al.blk_k, (int)al.row0, device_error_word());
 }
 
 }  // namespace
@@ -586,24 +615,35 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
     // Ring depths <SA, S16, S8> fill ~224 KB of shared memory.
     if (opt.split_precision && a_bf16)
         return fail(GDN_ERR_TYPE, "split-precision tensor-core GEMM takes fp16 activations");
+    ALayout al;
+    if (opt.a_blk_k > 0) {
+        if (opt.a_blk_k % BK != 0 || k % opt.a_blk_k != 0)
+            return fail(GDN_ERR_SHAPE, "K blocks must be a multiple of 64 that divides k");
+        if (opt.a_row0 < 0 || opt.a_row0 + m > opt.a_rows || opt.a_rows > INT32_MAX)
+            return fail(GDN_ERR_SHAPE, "rows [%lld, %lld) outside the %lld stored rows", (long long)opt.a_row0,
+                        (long long)(opt.a_row0 + m), (long long)opt.a_rows);
+        al.blk_k = opt.a_blk_k;
+        al.rows = opt.a_rows;
+        al.row0 = opt.a_row0;
+    }
     const bool two = m > BM;
     int st;
     if (opt.split_precision) {
-        st = two ? run_tc<128, 2, 4, 2, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                 : run_tc<128, 1, 6, 3, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+        st = two ? run_tc<128, 2, 4, 2, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
+                 : run_tc<128, 1, 6, 3, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
     } else {
         // One operand: 256-column tiles halve the activation traffic per MMA, as long
         // as the grid still covers at least half of the SMs.
         const int64_t tiles256 = (n + 255) / 256 * ((m + 2 * BM - 1) / (2 * BM)) * splits;
         const bool wide = two && tiles256 * 2 >= sm_count();
         if (a_bf16) {
-            st = !two ? run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                 : wide ? run_tc<256, 2, 3, 2, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                        : run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+            st = !two ? run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
+                 : wide ? run_tc<256, 2, 3, 2, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
+                        : run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
         } else {
-            st = !two ? run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                 : wide ? run_tc<256, 2, 3, 2, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s)
-                        : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, s);
+            st = !two ? run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
+                 : wide ? run_tc<256, 2, 3, 2, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
+                        : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
         }
     }
     if (st || splits == 1) return st;

@@ -705,15 +705,17 @@ int set_smem(K kern, size_t bytes) {
 
 size_t prefill_workspace_bytes(const gdn_dims& d, int64_t T) { return pcarve(d, T, nullptr).total; }
 
-int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
-            int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s) {
+int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, __half* gated_out, float* S,
+            float* conv_buf, int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s) {
     int st = validate_layer(L);
     if (st) return st;
     if (T <= 0 || T > (int64_t)1 << 26) return fail(GDN_ERR_SHAPE, "T must be in [1, 2^26] (got %lld)", (long long)T);
-    if (!x || !out || !S || !conv_pos) return fail(GDN_ERR_ARG, "x, out, S and conv_pos must be non-NULL");
+    if (!x || (!out && !gated_out) || !S || !conv_pos)
+        return fail(GDN_ERR_ARG, "x, the output, S and conv_pos must be non-NULL");
     if (x_dtype != GDN_DTYPE_F32 && x_dtype != GDN_DTYPE_BF16 && x_dtype != GDN_DTYPE_F16)
         return fail(GDN_ERR_TYPE, "x_dtype %d is not supported", x_dtype);
-    if (!aligned(out, 16) || !aligned(S, 16)) return fail(GDN_ERR_ARG, "out and S must be 16-byte aligned");
+    if ((out && !aligned(out, 16)) || (gated_out && !aligned(gated_out, 16)) || !aligned(S, 16))
+        return fail(GDN_ERR_ARG, "the output and S must be 16-byte aligned");
     const gdn_dims& d = L->dims;
     const size_t need = prefill_workspace_bytes(d, T);
     if (wsp == nullptr || ws_bytes < need || !aligned(wsp, 256))
@@ -790,13 +792,14 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
         const size_t sm3 = sizeof(OutSmem) + 128;
         if ((st = set_smem(chunk_out_kernel, sm3))) return st;
         st = launch_pdl("chunk_out_kernel", chunk_out_kernel, dim3((unsigned)D.nc, (unsigned)D.hv), dim3(128), sm3, s,
-                        W.qn, W.kn, W.sc, W.dl, W.gcum, W.proj, D.ldp, L->head_norm, W.gated, T, D.Tp, D.hk, D.hv,
-                        D.qkv, L->head_map);
+                        W.qn, W.kn, W.sc, W.dl, W.gcum, W.proj, D.ldp, L->head_norm,
+                        gated_out ? gated_out : W.gated, T, D.Tp, D.hk, D.hv, D.qkv, L->head_map);
         if (st) return st;
     }
 
-    // ---- output projection
+    // ---- output projection (the caller takes the gated heads instead when it shards them)
     if ((st = phase_mark(3, s))) return st;
+    if (gated_out) return phase_mark(4, s);
     if (L->weight_type == GDN_GGML_Q4_K) {
         st = launch_q4_k_gemv(L->out_blocks, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
     } else if (T >= 64) {

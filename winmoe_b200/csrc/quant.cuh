@@ -21,6 +21,9 @@ struct TcOptions {
     int splits = 1;                // split-K factor (partials in `workspace`, then a fixed-order sum)
     void* workspace = nullptr;
     size_t workspace_bytes = 0;
+    // Activations stored as K blocks a[k / a_blk_k][a_rows][a_blk_k] (0: plain
+    // [m][k]); the GEMM's m rows are rows a_row0 .. a_row0 + m - 1 of every block.
+    int64_t a_blk_k = 0, a_rows = 0, a_row0 = 0;
 };
 size_t gemm_tc_workspace_bytes(int64_t m, int64_t n, int splits);
 

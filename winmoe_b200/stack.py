@@ -1,0 +1,179 @@
+"""A stack of DeltaNet layers over one long prompt, value heads sharded over GPUs.
+
+The reference runs its layers one after the other on one device
+(engine/runtime/winmoe_inference.c:1155-1162, 1648-1653): per layer
+    normed = rmsnorm(hidden, attn_norm)          (attention.h:29-44)
+    o      = deltanet_forward(normed)            (deltanet_impl.h:145-377)
+    hidden = residual + o.
+Here a whole prompt of T tokens goes through each layer at once (chunked
+prefill), and with G ranks in a process group every rank owns Hv / G value
+heads with their key groups:
+
+  1. rank r slices the layer to heads [r Hv/G, (r+1) Hv/G) (`slice_layer`):
+     q/k rows of its key groups, v/z/beta/alpha rows and conv channels of its
+     heads -- a smaller layer of the same form, whose rows compute exactly as
+     in the whole layer;
+  2. `gdn_prefill_gated` runs the chunked prefill up to the output gate;
+  3. an NCCL all-gather stacks the G head blocks [G][T][inner / G];
+  4. each rank runs out_proj for its T / G tokens over the gathered blocks
+     (`gdn_out_proj_gathered`, the single-GPU k order, so bit-identical);
+  5. an all-gather of those [T / G][hidden] rows gives every rank the layer
+     output, and the next layer's `gdn_add_rmsnorm` adds it to the residual.
+
+With G = 1 the same code runs without collectives.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import GDNError, check, lib
+from .config import CONV_WIDTH, GDNConfig
+from .layer import DeltaNetState, DeltaNetWeights, _stream, prefill_workspace, q8_0_planes
+from .synth import LayerTensors
+
+
+def head_range(cfg: GDNConfig, rank: int, world: int) -> tuple[int, int]:
+    """Value heads [h0, h1) of `rank`; whole key groups per rank (grouped map)."""
+    hv, hpg = cfg.num_v_heads, cfg.heads_per_group
+    if hv % world or (hv // world) % hpg:
+        raise GDNError(-2, f"{hv} value heads in groups of {hpg} do not split over {world} ranks")
+    per = hv // world
+    return rank * per, (rank + 1) * per
+
+
+def slice_layer(cfg: GDNConfig, t: LayerTensors, h0: int, h1: int) -> tuple[GDNConfig, LayerTensors]:
+    """The layer restricted to value heads [h0, h1) (grouped head map), GGUF bytes.
+
+    in_proj rows (qkv | z | beta | alpha): q and k rows of key groups
+    [h0/hpg, h1/hpg), v and z rows of the heads, their beta and alpha rows.
+    out_proj keeps the heads' 32-column blocks of every row (the layer's own
+    out_proj is run on gathered heads instead, see module doc)."""
+    d, hpg = cfg.head_dim, cfg.heads_per_group
+    if h0 % hpg or h1 % hpg or not 0 <= h0 < h1 <= cfg.num_v_heads:
+        raise GDNError(-2, f"heads [{h0}, {h1}) are not whole key groups of {hpg}")
+    g0, g1 = h0 // hpg, h1 // hpg
+    key, qkv, inner, hv = cfg.key_dim, cfg.qkv_dim, cfg.inner, cfg.num_v_heads
+    rows = np.concatenate([np.arange(g0 * d, g1 * d), key + np.arange(g0 * d, g1 * d),
+                           2 * key + np.arange(h0 * d, h1 * d), qkv + np.arange(h0 * d, h1 * d),
+                           qkv + inner + np.arange(h0, h1), qkv + inner + hv + np.arange(h0, h1)])
+    sub = GDNConfig(cfg.hidden, g1 - g0, h1 - h0, d)
+    in_proj = np.ascontiguousarray(t.in_proj[rows])
+    conv_rows = rows[rows < qkv]  # the qkv channels, in the same order
+    conv = np.ascontiguousarray(t.conv1d_w.reshape(qkv, CONV_WIDTH)[conv_rows])
+    if t.weight_type == 8:
+        bpr = inner // 32  # Q8_0 blocks per out_proj row; head h owns blocks [h d/32, (h+1) d/32)
+        ob = t.out_proj.reshape(cfg.hidden, bpr, 34)[:, h0 * d // 32:h1 * d // 32]
+        out_proj = np.ascontiguousarray(ob.reshape(cfg.hidden, -1))
+    else:
+        raise GDNError(-3, "head sharding is implemented for Q8_0 layers")
+    return sub, LayerTensors(sub, t.weight_type, in_proj, out_proj, conv, np.ascontiguousarray(t.ssm_a[h0:h1]),
+                             np.ascontiguousarray(t.dt_bias[h0:h1]), t.head_norm)
+
+
+@dataclass
+class StackLayer:
+    """One layer of the stack on this rank: its head slice and the full out_proj."""
+    cfg: GDNConfig          # the whole layer
+    heads: DeltaNetWeights  # this rank's slice (gdn_prefill_gated)
+    out_qs: torch.Tensor    # full out_proj planes [hidden][inner] (gdn_out_proj_gathered)
+    out_d: torch.Tensor
+    h0: int
+    h1: int
+
+    @classmethod
+    def upload(cls, cfg: GDNConfig, t: LayerTensors, rank: int = 0, world: int = 1, device="cuda") -> "StackLayer":
+        h0, h1 = head_range(cfg, rank, world)
+        sub, ts = slice_layer(cfg, t, h0, h1)
+        w = DeltaNetWeights.upload(sub, ts.in_proj, ts.out_proj, ts.conv1d_w, ts.ssm_a, ts.dt_bias, ts.head_norm,
+                                   device=device)
+        out_qs, out_d = q8_0_planes(t.out_proj, cfg.hidden, cfg.inner, torch.device(device))
+        return cls(cfg, w, out_qs, out_d, h0, h1)
+
+    def state(self, device="cuda") -> DeltaNetState:
+        """Zero state of this rank's heads (S [1][Hv/G][d][d], conv window of its channels)."""
+        return DeltaNetState.zeros(self.heads.cfg, 1, device)
+
+
+def prefill_gated(w: DeltaNetWeights, state: DeltaNetState, x: torch.Tensor, out: torch.Tensor | None = None,
+                  stream=None) -> torch.Tensor:
+    """gdn_prefill_gated: x [T][hidden] -> gated head outputs [T][Hv*d] fp16."""
+    cfg = w.cfg
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty((T, cfg.inner), dtype=torch.float16, device=x.device)
+    ws = prefill_workspace(cfg, T, x.device)
+    base = (ws.data_ptr() + 255) // 256 * 256
+    check(lib().gdn_prefill_gated(C.byref(w.struct()), T, x.data_ptr(), _lib_dtype(x), out.data_ptr(),
+                                  state.S[0].data_ptr(), state.conv_buf[0].data_ptr(), state.conv_pos.data_ptr(),
+                                  base, ws.numel() - (base - ws.data_ptr()), _stream(stream, x.device)))
+    return out
+
+
+def out_proj_gathered(out_qs: torch.Tensor, out_d: torch.Tensor, cfg: GDNConfig, gathered: torch.Tensor, t0: int,
+                      t1: int, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """gdn_out_proj_gathered over gathered [G][T][inner/G] fp16 -> [t1-t0][hidden] fp32."""
+    G, T = gathered.shape[0], gathered.shape[1]
+    if out is None:
+        out = torch.empty((t1 - t0, cfg.hidden), dtype=torch.float32, device=gathered.device)
+    check(lib().gdn_out_proj_gathered(out_qs.data_ptr(), out_d.data_ptr(), cfg.hidden, cfg.inner,
+                                      gathered.data_ptr(), G, T, t0, t1, out.data_ptr(),
+                                      _stream(stream, gathered.device)))
+    return out
+
+
+def add_rmsnorm(x: torch.Tensor, add: torch.Tensor | None, w: torch.Tensor | None, y: torch.Tensor,
+                stream=None) -> torch.Tensor:
+    """gdn_add_rmsnorm: x += add (in place, if given); y = rmsnorm(x) * w."""
+    T, H = x.shape
+    check(lib().gdn_add_rmsnorm(x.data_ptr(), add.data_ptr() if add is not None else None,
+                                w.data_ptr() if w is not None else None, y.data_ptr(), _lib_dtype(y), T, H,
+                                _stream(stream, x.device)))
+    return y
+
+
+def _lib_dtype(t: torch.Tensor) -> int:
+    return {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[t.dtype]
+
+
+def layer_forward(layer: StackLayer, state: DeltaNetState, normed: torch.Tensor, group=None,
+                  rank: int = 0, world: int = 1) -> torch.Tensor:
+    """One layer on its rank's heads: normed [T][hidden] (the same on every rank)
+    -> the layer output [T][hidden] fp32 (the same on every rank)."""
+    import torch.distributed as dist
+    cfg = layer.cfg
+    T = normed.shape[0]
+    if T % world:
+        raise GDNError(-2, f"T={T} does not split over {world} ranks")
+    gated = prefill_gated(layer.heads, state, normed)
+    if world > 1:
+        gathered = torch.empty((world * T, gated.shape[1]), dtype=gated.dtype, device=gated.device)
+        dist.all_gather_into_tensor(gathered, gated, group=group)
+        gathered = gathered.view(world, T, -1)
+    else:
+        gathered = gated.view(1, T, -1)
+    ts = T // world
+    part = out_proj_gathered(layer.out_qs, layer.out_d, cfg, gathered, rank * ts, (rank + 1) * ts)
+    if world == 1:
+        return part
+    out = torch.empty((T, cfg.hidden), dtype=torch.float32, device=part.device)
+    dist.all_gather_into_tensor(out, part, group=group)
+    return out
+
+
+def prefill_stack(layers: list[StackLayer], states: list[DeltaNetState], x: torch.Tensor, group=None,
+                  rank: int = 0, world: int = 1, norm_dtype=torch.bfloat16) -> torch.Tensor:
+    """x [T][hidden] fp32 hidden states -> after len(layers) residual DeltaNet
+    layers (x <- x + DN_l(rmsnorm(x))), in place; rmsnorm weights are ones."""
+    T, H = x.shape
+    normed = torch.empty((T, H), dtype=norm_dtype, device=x.device)
+    delta = None
+    for layer, st in zip(layers, states):
+        add_rmsnorm(x, delta, None, normed)
+        delta = layer_forward(layer, st, normed, group, rank, world)
+    add_rmsnorm(x, delta, None, normed)  # the last residual add (normed: the next block's input)
+    return x
