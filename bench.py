@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the T=4096 prefill leg")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 48-layer T=32768 stack leg (config 5)")
     ap.add_argument("--no-extra-legs", action="store_true",
                     help="skip the batch-1 decode (config 1) and Q4_K sweep (config 4) legs")
     ap.add_argument("--prefill-only", action="store_true",
@@ -305,6 +306,76 @@ def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
     return res
 
 
+STACK_T, STACK_LAYERS = 32768, 48
+
+
+def run_stack(cfg, dev, world, rank, steps, warmup, tc_peak, peak_src, with_cpu, barrier, max_over_ranks):
+    """Config 5: T = 32768 prompt tokens through 48 residual DeltaNet layers
+    (x <- x + DN_l(rmsnorm(x))), value heads sharded over the ranks with NCCL
+    all-gathers (strong scaling: the same total work at every N)."""
+    import torch
+    from winmoe_b200 import synth
+    from winmoe_b200.stack import StackLayer, prefill_stack
+    T, NL = STACK_T, STACK_LAYERS
+    layers = []
+    for l in range(NL):
+        t = synth.layer_tensors_device(cfg, l, dev)
+        layers.append(StackLayer.upload(cfg, t, rank, world, dev))
+        del t
+    gen = torch.Generator(device=dev).manual_seed(5)
+    x0 = torch.randn((T, cfg.hidden), generator=gen, device=dev)
+    runs = warmup + steps
+    xs = [x0.clone() for _ in range(runs)]
+    states = [[lay.state(dev) for lay in layers] for _ in range(runs)]
+    stream = torch.cuda.current_stream(dev)
+    for i in range(warmup):
+        prefill_stack(layers, states[i], xs[i], None, rank, world)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(warmup, runs):
+        prefill_stack(layers, states[i], xs[i], None, rank, world)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+    flops = prefill_flops_per_token(cfg) * T * NL
+    ach = flops / (ms / 1e3) / 1e12
+    res = {"workload": f"long prefill (config 5): T={T} tokens through {NL} residual DeltaNet layers "
+                       "(rmsnorm, chunked prefill, out_proj), bf16 layer inputs, value heads sharded over the GPUs "
+                       "with NCCL all-gathers of the gated heads and of the out_proj token slices",
+           "value": T / (ms / 1e3), "unit": "tok/s", "ms_per_prompt": ms, "steps": steps, "warmup": warmup,
+           "n_gpus": world, "scaling": "strong", "layers": NL, "tokens": T,
+           "weights": "Q8_0, independent per layer, drawn on the device with torch's generator (same "
+                      "distributions and seeds as the parity tests' numpy draws, different values)",
+           "allgather_bytes_per_layer": T * cfg.inner * 2 + T * cfg.hidden * 4,
+           "roofline": {"bound": "tensor", "kernel": "whole stack", "achieved": ach, "peak": tc_peak * world,
+                        "unit": "TFLOP/s", "frac": ach / (tc_peak * world), "peak_source": peak_src,
+                        "algorithmic_flop_per_prompt": flops}}
+    if with_cpu and rank == 0 and world == 1:
+        from oracle import oracle as O
+        orc = O.ref() if O.ref_available() else O.port()
+        n_tok, n_layers = 64, 2
+        tensors = [synth.layer_tensors(cfg, layer=l) for l in range(n_layers)]
+        S = [np.zeros((cfg.num_v_heads, 128, 128), np.float32) for _ in range(n_layers)]
+        cb = [np.zeros((4, cfg.qkv_dim), np.float32) for _ in range(n_layers)]
+        pos = [np.zeros(1, np.int32) for _ in range(n_layers)]
+        ones = np.ones(cfg.hidden, np.float32)
+        xs_h = synth.hidden_states(n_tok, cfg.hidden, seed=5)
+        t0 = time.perf_counter()
+        for x in xs_h:
+            for l in range(n_layers):
+                x = x + orc.deltanet_forward(cfg, orc.rmsnorm(x, ones), S[l], cb[l], pos[l], tensors[l], act_mode=0)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": n_tok * n_layers / dt, "unit": "token-layers/s",
+                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                               "kind": "reference" if O.ref_available() else "port",
+                               "sample": f"prefix of {n_tok} tokens through layers 0-1 (rmsnorm + the reference's "
+                                         "deltanet_forward per token); the GPU figure in the same unit is "
+                                         f"value x {NL}"}
+    return res
+
+
 def cpu_reference_run(cfg, tensors, n_calls, seqs, act_mode, zero_state=False):
     """Times n_calls of the reference's deltanet_forward over `seqs` prefilled sequences."""
     from oracle import oracle as O
@@ -491,6 +562,9 @@ def run_ours(args):
     }
     if world == 1 and not args.no_prefill:
         line["prefill"] = run_prefill(cfg, w, dev, min(K, 8), W, tc_peak, peak_src)
+    if not args.no_stack:
+        line["stack"] = run_stack(cfg, dev, world, rank, min(K, 2), W, tc_peak, peak_src,
+                                  not args.no_cpu_baseline, barrier, max_over_ranks)
     if world == 1 and not args.no_extra_legs:
         line["decode_b1"] = run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, not args.no_cpu_baseline)
         line["q4k_sweep"] = run_q4k_sweep(cfg, dev, hbm_peak, peak_src, not args.no_cpu_baseline)

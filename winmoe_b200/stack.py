@@ -62,13 +62,17 @@ def slice_layer(cfg: GDNConfig, t: LayerTensors, h0: int, h1: int) -> tuple[GDNC
                            2 * key + np.arange(h0 * d, h1 * d), qkv + np.arange(h0 * d, h1 * d),
                            qkv + inner + np.arange(h0, h1), qkv + inner + hv + np.arange(h0, h1)])
     sub = GDNConfig(cfg.hidden, g1 - g0, h1 - h0, d)
-    in_proj = np.ascontiguousarray(t.in_proj[rows])
+    if isinstance(t.in_proj, torch.Tensor):  # device bytes: slice on the device
+        in_proj = t.in_proj[torch.from_numpy(rows).to(t.in_proj.device)].contiguous()
+    else:
+        in_proj = np.ascontiguousarray(t.in_proj[rows])
     conv_rows = rows[rows < qkv]  # the qkv channels, in the same order
     conv = np.ascontiguousarray(t.conv1d_w.reshape(qkv, CONV_WIDTH)[conv_rows])
     if t.weight_type == 8:
         bpr = inner // 32  # Q8_0 blocks per out_proj row; head h owns blocks [h d/32, (h+1) d/32)
         ob = t.out_proj.reshape(cfg.hidden, bpr, 34)[:, h0 * d // 32:h1 * d // 32]
-        out_proj = np.ascontiguousarray(ob.reshape(cfg.hidden, -1))
+        out_proj = (ob.contiguous().reshape(cfg.hidden, -1) if isinstance(ob, torch.Tensor)
+                    else np.ascontiguousarray(ob.reshape(cfg.hidden, -1)))
     else:
         raise GDNError(-3, "head sharding is implemented for Q8_0 layers")
     return sub, LayerTensors(sub, t.weight_type, in_proj, out_proj, conv, np.ascontiguousarray(t.ssm_a[h0:h1]),

@@ -119,6 +119,36 @@ def layer_tensors(cfg: GDNConfig, layer: int = 0, weight_type: int = 8) -> Layer
     return LayerTensors(cfg, weight_type, np.concatenate([qkvz, ba], axis=0), out, conv, ssm_a, dt_bias, norm)
 
 
+def layer_tensors_device(cfg: GDNConfig, layer: int, device) -> LayerTensors:
+    """Q8_0 layer tensors drawn on the device with torch's generator (same
+    distributions and per-layer seeds as layer_tensors, not the same values):
+    for stacks of many layers, where numpy generation would dominate the run.
+    in_proj / out_proj are device uint8 GGUF bytes; the small tensors come from
+    layer_tensors' numpy draws."""
+    import torch
+    dev = torch.device(device)
+    off = LAYER_SEED_STRIDE * layer
+
+    def q8(rows, cols, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        nb = cols // 32
+        d = (torch.randn((rows, nb), generator=g, device=dev).abs() * 0.02).to(torch.float16)
+        qs = torch.randint(-127, 128, (rows, nb, 32), generator=g, device=dev, dtype=torch.int8)
+        out = torch.empty((rows, nb, 34), dtype=torch.uint8, device=dev)
+        out[:, :, 0:2] = d.view(torch.uint8).view(rows, nb, 2)
+        out[:, :, 2:] = qs.view(torch.uint8)
+        return out.view(rows, nb * 34)
+
+    qkvz = q8(cfg.qkv_dim + cfg.inner, cfg.hidden, SEED_QKVZ + off)
+    ba = q8(2 * cfg.num_v_heads, cfg.hidden, SEED_BA + off)
+    out = q8(cfg.hidden, cfg.inner, SEED_OUT + off)
+    conv = (rng(SEED_CONV + off).standard_normal((cfg.qkv_dim, CONV_WIDTH)) * 0.5).astype(np.float32)
+    a_log = rng(SEED_ALOG + off).uniform(0.0, 2.7, size=cfg.num_v_heads)
+    norm = (1.0 + 0.1 * rng(SEED_NORM + off).standard_normal(cfg.head_dim)).astype(np.float32)
+    return LayerTensors(cfg, 8, torch.cat([qkvz, ba]), out, conv, (-np.exp(a_log)).astype(np.float32),
+                        np.zeros(cfg.num_v_heads, dtype=np.float32), norm)
+
+
 def hidden_states(n_tokens: int, hidden: int, seed: int = SEED_X) -> np.ndarray:
     """x ~ N(0,1), fp32 [n_tokens, hidden]."""
     return rng(seed).standard_normal((n_tokens, hidden)).astype(np.float32)
