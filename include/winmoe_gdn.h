@@ -97,8 +97,9 @@ GDN_API int gdn_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out,
 
 /* Precision flags of gdn_q8_0_gemm. */
 enum {
-    GDN_GEMM_EXACT = 0, /* fp32-GEMV accuracy (the reference's fp32-activation projection) */
-    GDN_GEMM_FAST = 1   /* tensor cores with one fp16/bf16 weight operand */
+    GDN_GEMM_EXACT = 0,    /* fp32-GEMV accuracy (the reference's fp32-activation projection) */
+    GDN_GEMM_FAST = 1,     /* tensor cores with one fp16/bf16 weight operand */
+    GDN_GEMM_REF_EXACT = 2 /* the reference CPU's quant_matvec bit for bit (fp32 x, see below) */
 };
 
 /*
@@ -118,6 +119,22 @@ enum {
  */
 GDN_API int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k,
                   const void* x, int x_dtype, int64_t m, float* y, int flags, void* stream);
+/*
+ * GDN_GEMM_REF_EXACT (x_dtype F32, k % 32 == 0, k <= 8192): each y[j] is what
+ * the reference's CPU quant_matvec(type 8) returns for x[j], bit for bit --
+ * with k >= 256 and n_rows >= 128 the activations are quantised to Q8_K
+ * (q8k_quant.h:32-104) and every 32-block term is fp16(d_w)*d_a*sum(q_w q_a)
+ * (q8_dot_q8k, q8_dequant.h:35-61), over the blocks of whole 256-value groups
+ * only, as the reference's branch sums them (q8_dequant.h:75-101); otherwise
+ * every block is the 16-lane fp32 dot of q8_dot_block (q8_dequant.h:21-32).
+ * Terms are added in block order.
+ * No counterpart on the reference's GPU route, which uses fp32 activations.
+ */
+
+/* quantize_row_q8_K (engine/runtime/q8k_quant.h:99-104) on the device: n fp32
+ * values (n % 256 == 0) -> n / 256 GGUF block_q8_K {float d; int8 qs[256];
+ * int16 bsums[16]} (292 bytes each), bit-identical to the CPU's. */
+GDN_API int gdn_quantize_q8_K(const float* x, void* out, int64_t n, void* stream);
 
 /*
  * Q4_K: GGUF superblocks of 256 weights, {fp16 d; fp16 dmin; u8 scales[12];
@@ -190,6 +207,23 @@ GDN_API int gdn_decode_step(const gdn_layer* layer, int64_t batch,
                     const void* x, int x_dtype, float* out,
                     float* S, float* conv_buf, int32_t* conv_pos,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Flags of gdn_decode_step_ex. */
+enum {
+    /* The five projections as the reference's CPU computes them
+     * (GDN_GEMM_REF_EXACT per tensor: Q8_K activations for attn_qkv, attn_gate
+     * and ssm_out, fp32 block dots for the 32-row ssm_beta / ssm_alpha); Q8_0
+     * layers and fp32 x only.  The rest of the step is the usual fp32 path. */
+    GDN_DECODE_REF_PROJECTIONS = 1
+};
+
+/* gdn_decode_step with flags (0 = gdn_decode_step).  Same workspace.  No
+ * counterpart in the reference: it selects the reference CPU's own projection
+ * arithmetic (ref-exact) instead of the fp32-activation GPU route. */
+GDN_API int gdn_decode_step_ex(const gdn_layer* layer, int64_t batch,
+                               const void* x, int x_dtype, float* out,
+                               float* S, float* conv_buf, int32_t* conv_pos,
+                               void* workspace, size_t workspace_bytes, int flags, void* stream);
 
 /* Size of the fixed scratch behind gdn_decode_step_noalloc (8 MiB). */
 #define GDN_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)

@@ -202,3 +202,30 @@ def test_decode_odd_shapes(cfg, B):
         assert rel_l2(st.S[b].cpu().numpy(), S_ref) <= TOL
         assert rel_l2(st.conv_buf[b].cpu().numpy(), cb_ref) <= TOL
     assert (st.conv_pos.cpu().numpy() == 3).all()
+
+
+def test_decode_reference_projections():
+    """gdn_decode_step_ex(GDN_DECODE_REF_PROJECTIONS): projections as the
+    reference's CPU computes them (Q8_K activations) -- far closer to the
+    reference's own unmodified layer (ref-exact) than the fp32-activation route."""
+    cfg = DIMS_35B
+    t = synth.layer_tensors(cfg, layer=1)
+    w = L.DeltaNetWeights.upload(cfg, t.in_proj, t.out_proj, t.conv1d_w, t.ssm_a, t.dt_bias, t.head_norm,
+                                 device=DEV)
+    B, steps = 3, 8
+    xs = np.stack([synth.hidden_states(B, cfg.hidden, seed=50 + i) for i in range(steps)])
+    orc = O.best()
+    err = {True: [], False: []}
+    for ref in (True, False):
+        st = L.DeltaNetState.zeros(cfg, B, DEV)
+        got = [L.decode_step(w, st, torch.from_numpy(xs[i]).to(DEV), ref_projections=ref).cpu().numpy()
+               for i in range(steps)]
+        for b in range(B):
+            S = np.zeros((cfg.num_v_heads, 128, 128), np.float32)
+            cb = np.zeros((4, cfg.qkv_dim), np.float32)
+            pos = np.zeros(1, np.int32)
+            for i in range(steps):
+                want = orc.deltanet_forward(cfg, xs[i, b], S, cb, pos, t, act_mode=O.ACT_EXACT)
+                err[ref].append(rel_l2(got[i][b], want))
+    assert max(err[True]) <= 1e-4, max(err[True])
+    assert max(err[True]) * 10 <= np.median(err[False]), (max(err[True]), np.median(err[False]))

@@ -137,3 +137,28 @@ def test_no_device_timeout_flag():
     from winmoe_b200._lib import lib
     torch.cuda.synchronize()
     assert lib().gdn_check_device_error(None) == 0
+
+
+def test_quantize_q8_K_bit_exact():
+    """quantize_row_q8_K on the device = the CPU's (d, qs and bsums), incl. an all-zero block."""
+    P = O.best()
+    g = np.random.default_rng(17)
+    x = (g.standard_normal(4 * 2048) * g.choice([1e-3, 1.0, 300.0], size=4 * 2048)).astype(np.float32)
+    x[256:512] = 0.0
+    want = P.quantize_q8_K(x)
+    got = L.quantize_q8_K(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("n,k", [(8192, 2048), (2048, 4096), (32, 2048), (100, 2048), (256, 2080)])
+@pytest.mark.parametrize("m", [1, 3, 9])
+def test_q8_0_gemm_ref_exact_bit_exact(n, k, m):
+    """GDN_GEMM_REF_EXACT = the reference CPU's quant_matvec(type 8), bit for bit:
+    Q8_K activations for n >= 128 and k % 256 == 0, fp32 block dots otherwise."""
+    P = O.best()
+    blocks = synth.q8_0_blocks(n, k, seed=800 + n + k)
+    qs, d = L.q8_0_planes(blocks, n, k, DEV)
+    x = synth.hidden_states(m, k, seed=n + m)
+    y = L.gemm_q8_0(qs, d, torch.from_numpy(x).to(DEV), ref_exact=True).cpu().numpy()
+    for i in range(m):
+        np.testing.assert_array_equal(y[i], P.quant_matvec(blocks, x[i], n, k, 8, O.ACT_EXACT))

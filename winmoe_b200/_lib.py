@@ -20,7 +20,7 @@ STATUS_NAMES = {
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 GGML_F32, GGML_Q8_0, GGML_Q4_K = 0, 8, 12
 HEAD_MAP_GROUPED, HEAD_MAP_INTERLEAVED = 0, 1
-GEMM_EXACT, GEMM_FAST = 0, 1
+GEMM_EXACT, GEMM_FAST, GEMM_REF_EXACT = 0, 1, 2
 
 
 class GDNError(RuntimeError):
@@ -59,7 +59,9 @@ SIGNATURES = {
     "gdn_q4_k_gemm": (_int, [_vp, _i64, _i64, _vp, _int, _i64, _vp, _vp]),
     "gdn_decode_workspace_size": (_sz, [C.POINTER(gdn_dims), _i64]),
     "gdn_decode_step": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "gdn_decode_step_ex": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _int, _vp]),
     "gdn_decode_step_noalloc": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
+    "gdn_quantize_q8_K": (_int, [_vp, _vp, _i64, _vp]),
     "gdn_prefill_workspace_size": (_sz, [C.POINTER(gdn_dims), _i64]),
     "gdn_prefill_gated": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gdn_out_proj_gathered": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _i64, _i64, _i64, _vp, _vp]),

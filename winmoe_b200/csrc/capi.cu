@@ -108,6 +108,11 @@ int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k
     if (!aligned(qs, 16)) return fail(GDN_ERR_ARG, "q8_0 gemm: qs must be 16-byte aligned");
     if (n_rows == 0 || m == 0) return GDN_OK;
     cudaStream_t s = as_stream(stream);
+    if (flags == GDN_GEMM_REF_EXACT) {
+        if (x_dtype != GDN_DTYPE_F32) return fail(GDN_ERR_TYPE, "q8_0 gemm: GDN_GEMM_REF_EXACT takes fp32 x");
+        if (!aligned(x, 16)) return fail(GDN_ERR_ARG, "q8_0 gemm: x must be 16-byte aligned");
+        return launch_q8_0_gemv_ref(qs, d, n_rows, k, static_cast<const float*>(x), m, y, n_rows, s);
+    }
     if (flags != GDN_GEMM_EXACT && flags != GDN_GEMM_FAST) return fail(GDN_ERR_ARG, "q8_0 gemm: unknown flags %d", flags);
     const bool tc_shape = m >= 64 && k % 64 == 0 && aligned(x, 16) && aligned(d, 4);
     const bool tc = tc_shape && (flags == GDN_GEMM_FAST ? x_dtype != GDN_DTYPE_F32 : x_dtype == GDN_DTYPE_F16);
@@ -117,6 +122,13 @@ int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k
         return launch_q8_0_gemm_tc(qs, d, n_rows, k, x, x_dtype == GDN_DTYPE_BF16, m, y, n_rows, opt, s);
     }
     return launch_q8_0_gemv(qs, d, n_rows, k, x, x_dtype, m, y, n_rows, s);
+}
+
+int gdn_quantize_q8_K(const float* x, void* out, int64_t n, void* stream) {
+    if (!x || !out) return fail(GDN_ERR_ARG, "quantize_q8_K: NULL pointer");
+    if (n < 0) return fail(GDN_ERR_SHAPE, "quantize_q8_K: n < 0");
+    if (!aligned(x, 16) || !aligned(out, 4)) return fail(GDN_ERR_ARG, "quantize_q8_K: x 16-byte, out 4-byte aligned");
+    return launch_quantize_q8_K(x, out, n, as_stream(stream));
 }
 
 int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, void* stream) {
@@ -187,6 +199,13 @@ int gdn_decode_step_noalloc(const gdn_layer* layer, int64_t batch, const void* x
     if ((st = noalloc_scratch(&ws))) return st;
     return decode_step(layer, batch, x, x_dtype, out, S, conv_buf, conv_pos, ws, GDN_NOALLOC_SCRATCH_BYTES,
                        as_stream(stream));
+}
+
+int gdn_decode_step_ex(const gdn_layer* layer, int64_t batch, const void* x, int x_dtype, float* out, float* S,
+                       float* conv_buf, int32_t* conv_pos, void* workspace, size_t workspace_bytes, int flags,
+                       void* stream) {
+    return decode_step(layer, batch, x, x_dtype, out, S, conv_buf, conv_pos, workspace, workspace_bytes,
+                       as_stream(stream), flags);
 }
 
 size_t gdn_prefill_workspace_size(const gdn_dims* dims, int64_t T) {

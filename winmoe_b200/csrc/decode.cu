@@ -470,10 +470,31 @@ static int in_projection(const gdn_layer* L, const Dims& D, int64_t B, const voi
                             x_dtype, B, ws.proj + n_tc, D.ldp, s);
 }
 
+// The projections as the reference's CPU computes them (quant_matvec per
+// tensor, engine/runtime/deltanet_impl.h:275-278 and 374): each of attn_qkv,
+// attn_gate, ssm_beta, ssm_alpha and ssm_out takes its own Q8_K or fp32
+// branch by its row count, bit for bit (launch_q8_0_gemv_ref).
+static int in_projection_ref(const gdn_layer* L, const Dims& D, int64_t B, const float* x, const Workspace& ws,
+                             cudaStream_t s) {
+    const int64_t hidden = L->dims.hidden, kb = hidden / 32;
+    const int64_t seg[4][2] = {{0, D.qkv}, {D.qkv, D.inner}, {(int64_t)D.qkv + D.inner, D.hv},
+                               {(int64_t)D.qkv + D.inner + D.hv, D.hv}};
+    for (const auto& g : seg) {
+        const int st = launch_q8_0_gemv_ref(L->in_qs + g[0] * hidden, L->in_d + g[0] * kb, g[1], hidden, x, B,
+                                            ws.proj + g[0], D.ldp, s);
+        if (st) return st;
+    }
+    return GDN_OK;
+}
+
 int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float* out, float* S, float* conv_buf,
-                int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s) {
+                int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s, int flags) {
     int st = validate_layer(L);
     if (st) return st;
+    const bool ref = (flags & GDN_DECODE_REF_PROJECTIONS) != 0;
+    if (flags & ~GDN_DECODE_REF_PROJECTIONS) return fail(GDN_ERR_ARG, "decode: unknown flags 0x%x", flags);
+    if (ref && (L->weight_type != GDN_GGML_Q8_0 || x_dtype != GDN_DTYPE_F32 || !aligned(x, 16)))
+        return fail(GDN_ERR_TYPE, "reference projections take a Q8_0 layer and 16-byte aligned fp32 x");
     if (B <= 0 || B > 65535) return fail(GDN_ERR_SHAPE, "batch must be in [1, 65535] (got %lld)", (long long)B);
     if (!x || !out || !S || !conv_pos) return fail(GDN_ERR_ARG, "x, out, S and conv_pos must be non-NULL");
     if (x_dtype != GDN_DTYPE_F32 && x_dtype != GDN_DTYPE_BF16 && x_dtype != GDN_DTYPE_F16)
@@ -485,12 +506,14 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
         return fail(GDN_ERR_ARG, "workspace must be 256-aligned and hold %zu bytes (got %zu)", need, ws_bytes);
     const Dims D = dims_of(d);
     const Workspace ws = carve(d, B, wsp);
-    const bool tc_out = (L->weight_type == GDN_GGML_Q8_0) && B >= kTcMinBatch;
+    const bool tc_out = !ref && (L->weight_type == GDN_GGML_Q8_0) && B >= kTcMinBatch;
     const bool conv = (L->conv1d_w != nullptr && conv_buf != nullptr);
     PhaseEvents* pe = phase_events();
 
     if ((st = mark(pe, 0, s))) return st;
-    if ((st = in_projection(L, D, B, x, x_dtype, ws, s))) return st;
+    if ((st = ref ? in_projection_ref(L, D, B, static_cast<const float*>(x), ws, s)
+                  : in_projection(L, D, B, x, x_dtype, ws, s)))
+        return st;
     if ((st = mark(pe, 1, s))) return st;
     {
         const int64_t warps = B * (D.qkv / HD + 1);
@@ -514,7 +537,9 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
         if (st) return st;
     }
     if ((st = mark(pe, 3, s))) return st;
-    if (L->weight_type == GDN_GGML_Q4_K) {
+    if (ref) {
+        st = launch_q8_0_gemv_ref(L->out_qs, L->out_d, d.hidden, D.inner, ws.gated, B, out, d.hidden, s);
+    } else if (L->weight_type == GDN_GGML_Q4_K) {
         st = launch_q4_k_gemv(L->out_blocks, d.hidden, D.inner, ws.gated, GDN_DTYPE_F32, B, out, d.hidden, s);
     } else if (tc_out) {
         TcOptions opt;

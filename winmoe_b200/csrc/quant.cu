@@ -13,6 +13,8 @@
 //                                              engine/runtime/gpu_offload.cu:237-250
 #include "gdn_common.cuh"
 #include "quant.cuh"
+#include <algorithm>
+#include <string.h>
 
 namespace gdn {
 
@@ -171,6 +173,176 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
                 const float v = warp_sum(acc[j]);
                 if (lane == 0) y[(m0 + j) * ldy + r] = v;
             }
+        }
+    }
+}
+
+// ---------------------------------------------- reference-exact projection
+//
+// quant_matvec type 8 exactly as the reference's CPU computes it
+// (engine/runtime/transformer.h:157-194 -> q8_matvec, q8_dequant.h:63-113):
+//   k >= 256 and n >= 128: x -> Q8_K per 256 values (quantize_block_q8_K,
+//     q8k_quant.h:32-93: d = amax / 127, q = RNE(x * (1/d)) clamped to +-127),
+//     every 32-block term (fp16(d_w) * d_a) * float(sum q_w q_a) (q8_dot_q8k,
+//     q8_dequant.h:35-61; the integer sum is exact); as in the reference
+//     (q8_dequant.h:75-79, 88-101) only the blocks of whole 256-value groups
+//     enter this branch's sum;
+//   otherwise: per 32-block, 16 lanes of two fused products, the
+//     _mm512_reduce_add_ps tree, times d_w (q8_dot_block, q8_dequant.h:21-32).
+// The row sum adds the block terms strictly in block order, as the reference's
+// loop does, so every output is bit-identical to the CPU's.
+
+// Q8_K block of 256 activations in shared memory: d, then qs.
+struct Q8KSmem {
+    float d;
+    int8_t qs[256];
+};
+
+// One warp quantises 256 values (quantize_block_q8_K); lane l holds x[8l..8l+7].
+__device__ __forceinline__ void quantize_q8_K_warp(const float (&v)[8], int lane, float& d_out, int8_t (&q)[8]) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (amax < 1e-10f) {
+        d_out = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) q[j] = 0;
+        return;
+    }
+    const float d = amax / 127.0f;  // correctly rounded division and reciprocal, as the CPU's
+    const float id = 1.0f / d;
+    d_out = d;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        int v8 = __float2int_rn(__fmul_rn(v[j], id));  // cvtps_epi32: round to nearest even
+        v8 = v8 < -127 ? -127 : (v8 > 127 ? 127 : v8);
+        q[j] = (int8_t)v8;
+    }
+}
+
+// GGUF block_q8_K {float d; int8 qs[256]; int16 bsums[16]} (292 bytes) per 256 values.
+__global__ void quantize_q8_K_kernel(const float* __restrict__ x, uint8_t* __restrict__ out, int64_t nblocks) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t blk = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (blk >= nblocks) return;
+    const int lane = threadIdx.x & 31;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = x[blk * 256 + lane * 8 + j];
+    float d;
+    int8_t q[8];
+    quantize_q8_K_warp(v, lane, d, q);
+    uint8_t* ob = out + blk * 292;
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        ob[4 + lane * 8 + j] = (uint8_t)q[j];
+        s += q[j];
+    }
+    s += __shfl_down_sync(0xffffffffu, s, 1);  // the 16-value group of lanes 2g, 2g+1
+    if ((lane & 1) == 0) {
+        const int16_t bs = (int16_t)s;
+        memcpy(ob + 4 + 256 + lane, &bs, 2);
+    }
+    if (lane == 0) memcpy(ob, &d, 4);
+}
+
+// The _mm512_reduce_add_ps tree over 16 lanes.
+__device__ __forceinline__ float hsum16_tree(const float (&a)[16]) {
+    float t3[8], t6[4];
+#pragma unroll
+    for (int i = 0; i < 8; i++) t3[i] = __fadd_rn(a[8 + i], a[i]);
+#pragma unroll
+    for (int i = 0; i < 4; i++) t6[i] = __fadd_rn(t3[4 + i], t3[i]);
+    return __fadd_rn(__fadd_rn(t6[0], t6[2]), __fadd_rn(t6[1], t6[3]));
+}
+
+// One warp per weight row, MB activation rows per block row (grid.y).  Lane l
+// forms the terms of blocks l, l+32, ...; the row sum replays them in order.
+constexpr int kRefMaxBlocksPerLane = 8;  // k <= 8192
+
+template <int MB>
+__global__ void __launch_bounds__(256) q8_0_gemv_ref_kernel(const int8_t* __restrict__ qs,
+                                                           const uint16_t* __restrict__ dsc, int64_t n_rows,
+                                                           int64_t k, const float* __restrict__ x, int64_t m,
+                                                           float* __restrict__ y, int64_t ldy, int use_q8k) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ uint8_t sm_raw[];
+    const int64_t m0 = (int64_t)blockIdx.y * MB;
+    const int mb = (int)min((int64_t)MB, m - m0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int64_t nk = k >> 8;
+    const int64_t nb = use_q8k ? nk * 8 : k >> 5;  // blocks that enter the sum
+    Q8KSmem* xq = reinterpret_cast<Q8KSmem*>(sm_raw);  // [mb][nk] when use_q8k
+    float* xf = reinterpret_cast<float*>(sm_raw);      // [mb][k] otherwise
+    if (use_q8k) {
+        for (int64_t qb = warp; qb < (int64_t)mb * nk; qb += nwarps) {
+            const int64_t j = qb / nk, kb = qb % nk;
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = x[(m0 + j) * k + kb * 256 + lane * 8 + e];
+            float d;
+            int8_t q[8];
+            quantize_q8_K_warp(v, lane, d, q);
+            Q8KSmem& b = xq[qb];
+#pragma unroll
+            for (int e = 0; e < 8; e++) b.qs[lane * 8 + e] = q[e];
+            if (lane == 0) b.d = d;
+        }
+    } else {
+        for (int64_t i = threadIdx.x; i < (int64_t)mb * k; i += blockDim.x) xf[i] = x[m0 * k + i];
+    }
+    __syncthreads();
+    for (int64_t r = (int64_t)blockIdx.x * nwarps + warp; r < n_rows; r += (int64_t)gridDim.x * nwarps) {
+        const int8_t* wrow = qs + r * k;
+        const uint16_t* drow = dsc + r * (k >> 5);
+        for (int j = 0; j < mb; j++) {
+            float t[kRefMaxBlocksPerLane];
+#pragma unroll
+            for (int u = 0; u < kRefMaxBlocksPerLane; u++) {
+                const int64_t b = lane + 32 * u;
+                t[u] = 0.0f;
+                if (b >= nb) continue;
+                const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(wrow + b * 32));
+                const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(wrow + b * 32 + 16));
+                const float dw = fp16_bits_to_float(__ldg(drow + b));  // drow: k / 32 scales per row
+                if (use_q8k) {
+                    const Q8KSmem& xb = xq[j * nk + (b >> 3)];
+                    const int* a4 = reinterpret_cast<const int*>(xb.qs + (b & 7) * 32);
+                    const int wv[8] = {(int)w0.x, (int)w0.y, (int)w0.z, (int)w0.w,
+                                       (int)w1.x, (int)w1.y, (int)w1.z, (int)w1.w};
+                    int isum = 0;
+#pragma unroll
+                    for (int e = 0; e < 8; e++) isum = __dp4a(wv[e], a4[e], isum);
+                    t[u] = __fmul_rn(__fmul_rn(dw, xb.d), (float)isum);
+                } else {
+                    const float* xv = xf + (int64_t)j * k + b * 32;
+                    const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    float f[32];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) i8x4_to_f32(wv[e], f + 4 * e);
+                    float acc[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) acc[i] = fmaf(f[i], xv[i], 0.0f);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) acc[i] = fmaf(f[16 + i], xv[16 + i], acc[i]);
+                    t[u] = __fmul_rn(dw, hsum16_tree(acc));
+                }
+            }
+            float sum = 0.0f;  // block order, as the reference's loop
+            for (int64_t b = 0; b < nb; b++) {
+                float tb = 0.0f;
+#pragma unroll
+                for (int u = 0; u < kRefMaxBlocksPerLane; u++)
+                    if ((b >> 5) == u) tb = __shfl_sync(0xffffffffu, t[u], (int)(b & 31));
+                sum = __fadd_rn(sum, tb);
+            }
+            if (lane == 0) y[(m0 + j) * ldy + r] = sum;
         }
     }
 }
@@ -375,6 +547,39 @@ int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, 
         case 4: return run_q8_gemv<4>(qs, d, n, k, x, dt, m, y, ldy, s);
         default: return run_q8_gemv<8>(qs, d, n, k, x, dt, m, y, ldy, s);
     }
+}
+
+int launch_quantize_q8_K(const float* x, void* out, int64_t n, cudaStream_t s) {
+    if (n % 256 != 0) return fail(GDN_ERR_SHAPE, "quantize_q8_K: the length must be a multiple of 256");
+    const int64_t nb = n / 256;
+    if (nb == 0) return GDN_OK;
+    return launch_pdl("quantize_q8_K_kernel", quantize_q8_K_kernel, dim3((unsigned)((nb + 7) / 8)), dim3(256), 0, s,
+                      x, static_cast<uint8_t*>(out), nb);
+}
+
+template <int MB>
+static int run_q8_gemv_ref(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const float* x, int64_t m,
+                           float* y, int64_t ldy, bool q8k, cudaStream_t s) {
+    const size_t smem = q8k ? (size_t)MB * (k / 256) * sizeof(Q8KSmem) : (size_t)MB * k * sizeof(float);
+    int st = smem_optin((const void*)q8_0_gemv_ref_kernel<MB>, smem);
+    if (st) return st;
+    const int64_t blocks_x = std::min<int64_t>((n + 7) / 8, (int64_t)sm_count() * 4);
+    const dim3 grid((unsigned)blocks_x, (unsigned)((m + MB - 1) / MB));
+    return launch_pdl("q8_0_gemv_ref_kernel", q8_0_gemv_ref_kernel<MB>, grid, dim3(256), smem, s, qs, d, n, k, x, m,
+                      y, ldy, q8k ? 1 : 0);
+}
+
+int launch_q8_0_gemv_ref(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const float* x, int64_t m,
+                         float* y, int64_t ldy, cudaStream_t s) {
+    if (k % 32 != 0 || k <= 0 || k / 32 > 32 * kRefMaxBlocksPerLane)
+        return fail(GDN_ERR_SHAPE, "reference-exact q8_0 gemv: k=%lld must be a multiple of 32 up to 8192",
+                    (long long)k);
+    if (m <= 0 || n <= 0) return GDN_OK;
+    if ((m + 7) / 8 > 65535) return fail(GDN_ERR_SHAPE, "reference-exact q8_0 gemv: m too large");
+    const bool q8k = k >= 256 && n >= 128;  // q8_matvec's Q8_K branch (q8_dequant.h:75-79)
+    if (!q8k && (size_t)8 * k * 4 > 200 * 1024) return run_q8_gemv_ref<1>(qs, d, n, k, x, m, y, ldy, q8k, s);
+    return m >= 8 ? run_q8_gemv_ref<8>(qs, d, n, k, x, m, y, ldy, q8k, s)
+                  : run_q8_gemv_ref<1>(qs, d, n, k, x, m, y, ldy, q8k, s);
 }
 
 int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s) {

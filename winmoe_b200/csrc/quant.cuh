@@ -9,6 +9,12 @@ int launch_q8_0_repack(const void* blocks, int8_t* qs, uint16_t* d, int64_t rows
 int launch_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t rows, int64_t cols,
                         cudaStream_t s);
 // y[m][ldy] = x[m][:] . W[n][:] on CUDA cores, dequantising in registers.
+// quant_matvec type 8 exactly as the reference's CPU computes it (Q8_K
+// activations when k % 256 == 0 and n >= 128, else fp32 block dots), bit for bit.
+int launch_q8_0_gemv_ref(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const float* x, int64_t m,
+                         float* y, int64_t ldy, cudaStream_t s);
+// quantize_row_q8_K: n fp32 values -> n / 256 GGUF block_q8_K (292 bytes each).
+int launch_quantize_q8_K(const float* x, void* out, int64_t n, cudaStream_t s);
 int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int x_dtype,
                      int64_t m, float* y, int64_t ldy, cudaStream_t s);
 int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s);

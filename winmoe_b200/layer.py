@@ -186,8 +186,10 @@ def _act_dtype(x: torch.Tensor) -> int:
 
 
 def decode_step(w: DeltaNetWeights, state: DeltaNetState, x: torch.Tensor, out: torch.Tensor | None = None,
-                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """One decode token for every sequence of `state`: x [B][hidden] -> out [B][hidden] fp32."""
+                stream: torch.cuda.Stream | None = None, ref_projections: bool = False) -> torch.Tensor:
+    """One decode token for every sequence of `state`: x [B][hidden] -> out [B][hidden] fp32.
+    ref_projections=True (fp32 x, Q8_0): the projections as the reference's CPU
+    computes them (Q8_K activations, gdn_decode_step_ex)."""
     B = state.batch
     cfg = w.cfg
     if x.shape != (B, cfg.hidden) or not x.is_cuda or not x.is_contiguous():
@@ -197,9 +199,9 @@ def decode_step(w: DeltaNetWeights, state: DeltaNetState, x: torch.Tensor, out: 
     ws = workspace(cfg, B, x.device)
     base = (ws.data_ptr() + 255) // 256 * 256
     nbytes = ws.numel() - (base - ws.data_ptr())
-    check(lib().gdn_decode_step(C.byref(w.struct()), B, x.data_ptr(), _act_dtype(x), out.data_ptr(),
-                                state.S.data_ptr(), state.conv_buf.data_ptr(), state.conv_pos.data_ptr(),
-                                base, nbytes, _stream(stream, x.device)))
+    check(lib().gdn_decode_step_ex(C.byref(w.struct()), B, x.data_ptr(), _act_dtype(x), out.data_ptr(),
+                                   state.S.data_ptr(), state.conv_buf.data_ptr(), state.conv_pos.data_ptr(),
+                                   base, nbytes, 1 if ref_projections else 0, _stream(stream, x.device)))
     return out
 
 
@@ -237,16 +239,27 @@ def prefill(w: DeltaNetWeights, state: DeltaNetState, x: torch.Tensor, seq: int 
 
 
 def gemm_q8_0(qs: torch.Tensor, d: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None,
-              fast: bool = False, stream=None) -> torch.Tensor:
+              fast: bool = False, stream=None, ref_exact: bool = False) -> torch.Tensor:
     """y[m][n] = x[m] . W[n] for Q8_0 planes (quant_matvec type 8, batched).
     fast=False keeps fp32-GEMV accuracy; fast=True lets m >= 64 fp16/bf16
-    batches use one tensor-core weight operand (weights rounded once)."""
+    batches use one tensor-core weight operand (weights rounded once);
+    ref_exact=True (fp32 x) reproduces the reference CPU's quant_matvec bit for
+    bit (Q8_K activations for n >= 128 and k % 256 == 0)."""
     n, k = qs.shape
     m = x.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    flags = _lib.GEMM_REF_EXACT if ref_exact else _lib.GEMM_FAST if fast else _lib.GEMM_EXACT
     check(lib().gdn_q8_0_gemm(qs.data_ptr(), d.data_ptr(), n, k, x.data_ptr(), _act_dtype(x), m, out.data_ptr(),
-                              _lib.GEMM_FAST if fast else _lib.GEMM_EXACT, _stream(stream, x.device)))
+                              flags, _stream(stream, x.device)))
+    return out
+
+
+def quantize_q8_K(x: torch.Tensor, stream=None) -> torch.Tensor:
+    """quantize_row_q8_K: fp32 x (numel % 256 == 0) -> GGUF block_q8_K bytes (292 per 256 values)."""
+    n = x.numel()
+    out = torch.empty(n // 256 * 292, dtype=torch.uint8, device=x.device)
+    check(lib().gdn_quantize_q8_K(x.data_ptr(), out.data_ptr(), n, _stream(stream, x.device)))
     return out
 
 
