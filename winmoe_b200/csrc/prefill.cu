@@ -18,6 +18,11 @@
 // in fp32 whatever the rest of the sum, so a decay that underflows to 0 in the
 // reference (expf, deltanet_impl.h:251) zeroes the same products here.
 //
+// Per-element exponentials and divisions (SiLU, the exp(G_i - G_j) factors, the
+// output gate) use the __expf / __fdividef intrinsics: their few-ulp errors sit
+// far below the bf16 rounding every one of these values goes through next, and
+// with IEEE expf and division the output kernel spent ~3/4 of its time there.
+//
 // Kernels: prep (conv1d + SiLU + L2 norm, token-parallel), gates, window
 // hand-off, K1 chunk_local (W', U', e*K, cumulative G; fp32 forward
 // substitution), K2 chunk_scan (state passing, sequential over chunks,
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
                 sum = __fadd_rn(sum, __fmul_rn(w.y, h1[c]));
                 sum = __fadd_rn(sum, __fmul_rn(w.z, h2[c]));
                 sum = __fadd_rn(sum, __fmul_rn(w.w, in[c]));
-                const float sig = 1.0f / (1.0f + expf(-sum));
+                const float sig = __fdividef(1.0f, 1.0f + __expf(-sum));
                 in[c] = __fmul_rn(sum, sig);
             }
             xv = make_float4(in[0], in[1], in[2], in[3]);
@@ -266,6 +271,7 @@ __global__ void __launch_bounds__(1024) prefill_window_kernel(const float* __res
 // 0..127 also write e*K; the chunk's cumulative G and gam_63 go to HBM.
 struct LocalSmem {
     bf16 k[CH][LDH];
+    bf16 v[CH][LDH];
     float L[CH][CH];
     float G[CH], beta[CH];
 };
@@ -285,9 +291,11 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t t0 = (int64_t)c * CH;
     const bf16* kc = kn + ((int64_t)g * Tp + t0) * HD;
+    const bf16* vcg = vb + ((int64_t)h * Tp + t0) * HD;
     for (int i = tid; i < CH * HD / 8; i += 256) {
         const int r = i / (HD / 8), q = i % (HD / 8);
         wmma16::cp_async16(&sm.k[r][q * 8], kc + r * HD + q * 8);
+        wmma16::cp_async16(&sm.v[r][q * 8], vcg + r * HD + q * 8);
     }
     wmma16::cp_async_commit();
     if (warp == 0) {  // inclusive cumulative log decay, 2 tokens per lane
@@ -333,7 +341,7 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
             for (int e = 0; e < 4; e++) {
                 const int i = 16 * mt + gq + ((e >> 1) << 3);
                 const int j = 8 * (nb + n) + 2 * qq + (e & 1);
-                sm.L[i][j] = (j < i) ? sm.beta[i] * expf(sm.G[i] - sm.G[j]) * acc[n][e] : 0.0f;
+                sm.L[i][j] = (j < i) ? sm.beta[i] * __expf(sm.G[i] - sm.G[j]) * acc[n][e] : 0.0f;
             }
         }
     }
@@ -346,11 +354,10 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
     const float G63 = sm.G[CH - 1];
     if (is_w) {
 #pragma unroll
-        for (int i = 0; i < CH; i++) x[i] = sm.beta[i] * expf(sm.G[i]) * __bfloat162float(sm.k[i][col]);
+        for (int i = 0; i < CH; i++) x[i] = sm.beta[i] * __expf(sm.G[i]) * __bfloat162float(sm.k[i][col]);
     } else {
-        const bf16* vc = vb + ((int64_t)h * Tp + t0) * HD + col;
 #pragma unroll
-        for (int i = 0; i < CH; i++) x[i] = sm.beta[i] * __bfloat162float(vc[(int64_t)i * HD]);
+        for (int i = 0; i < CH; i++) x[i] = sm.beta[i] * __bfloat162float(sm.v[i][col]);
     }
 #pragma unroll
     for (int i = 1; i < CH; i++) {
@@ -372,7 +379,7 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
         bf16* e = ek + ((int64_t)h * Tp + t0) * HD + col;
 #pragma unroll
         for (int i = 0; i < CH; i++)
-            e[(int64_t)i * HD] = __float2bfloat16_rn(expf(G63 - sm.G[i]) * __bfloat162float(sm.k[i][col]));
+            e[(int64_t)i * HD] = __float2bfloat16_rn(__expf(G63 - sm.G[i]) * __bfloat162float(sm.k[i][col]));
     }
     if (tid < CH) gcum[(int64_t)h * Tp + t0 + tid] = sm.G[tid];
     if (tid == 0) gchunk[(int64_t)h * (Tp / CH) + c] = expf(G63);
@@ -549,6 +556,7 @@ struct OutSmem {
     bf16 d[CH][LDH];
     bf16 p[CH][LDC];
     float G[CH];
+    float hn[HD];
 };
 
 __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__ qn, const bf16* __restrict__ kn,
@@ -585,10 +593,21 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
         }
         wmma16::cp_async_commit();
         if (tid < CH) sm.G[tid] = gcum[(int64_t)h * Tp + t0 + tid];
-        wmma16::cp_async_wait<0>();
-        __syncthreads();
+        sm.hn[tid] = head_norm != nullptr ? head_norm[tid] : 1.0f;
     }
     const int rA = 16 * warp + gq, rB = rA + 8;  // this thread's two token rows
+    // The gate inputs z of this thread's two rows and 32 columns, fetched now so
+    // the loads are in flight during the products below.
+    float2 zr[2][HD / 8];
+#pragma unroll
+    for (int hf = 0; hf < 2; hf++) {
+        const int64_t t = t0 + (hf ? rB : rA);
+        const float* z = proj + min(t, T - 1) * ldp + qkv + h * HD;
+#pragma unroll
+        for (int n = 0; n < HD / 8; n++) zr[hf][n] = *reinterpret_cast<const float2*>(z + 8 * n + 2 * qq);
+    }
+    wmma16::cp_async_wait<0>();
+    __syncthreads();
     // ---- P = mask(exp(G_i - G_j) Q K^T), only this warp's rows
     {
         float pacc[CH / 8][4] = {};
@@ -611,7 +630,7 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int i = (e >> 1) ? rB : rA, jj = j + (e & 1);
-                v[e] = (jj <= i) ? expf(sm.G[i] - sm.G[jj]) * pacc[n][e] : 0.0f;
+                v[e] = (jj <= i) ? __expf(sm.G[i] - sm.G[jj]) * pacc[n][e] : 0.0f;
             }
             *reinterpret_cast<uint32_t*>(&sm.p[rA][j]) = wmma16::pack_bf16(v[0], v[1]);
             *reinterpret_cast<uint32_t*>(&sm.p[rB][j]) = wmma16::pack_bf16(v[2], v[3]);
@@ -675,20 +694,19 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
         const int64_t t = t0 + (hf ? rB : rA);
         if (t >= T) continue;
         const float inv = hf ? invB : invA;
-        const float* z = proj + t * ldp + qkv + h * HD;
         __half* gout = gated + t * inner + h * HD;
 #pragma unroll
         for (int n = 0; n < HD / 8; n++) {
             const int v = 8 * n + 2 * qq;
-            const float2 zz = *reinterpret_cast<const float2*>(z + v);
+            const float2 zz = zr[hf][n];
             float r2[2];
 #pragma unroll
             for (int e = 0; e < 2; e++) {
                 float nv = __fmul_rn(o[n][2 * hf + e], inv);
-                if (head_norm != nullptr) nv = __fmul_rn(nv, head_norm[v + e]);
+                if (head_norm != nullptr) nv = __fmul_rn(nv, sm.hn[v + e]);
                 float zv = e ? zz.y : zz.x;
                 zv = fminf(fmaxf(zv, -88.0f), 88.0f);
-                r2[e] = __fmul_rn(nv, zv / (1.0f + expf(-zv)));
+                r2[e] = __fmul_rn(nv, __fdividef(zv, 1.0f + __expf(-zv)));
             }
             *reinterpret_cast<__half2*>(gout + v) = __floats2half2_rn(r2[0], r2[1]);
         }
