@@ -24,8 +24,8 @@
 // with IEEE expf and division the output kernel spent ~3/4 of its time there.
 //
 // Kernels: prep (conv1d + SiLU + L2 norm, token-parallel), gates, window
-// hand-off, K1 chunk_local (W', U', e*K, cumulative G; fp32 forward
-// substitution), K2 chunk_scan (state passing, sequential over chunks,
+// hand-off, K1 chunk_local (W', U', e*K, cumulative G; (I + L)^-1 by blocked
+// fp32 inversion, then W' and U' as tensor-core products), K2 chunk_scan (state passing, sequential over chunks,
 // parallel over heads x 32-column slabs), K3 chunk_out (outputs, per-head
 // RMSNorm and SiLU(z) gate).  The in/out projections are the tensor-core
 // GEMMs of gemm_tc.cu.
@@ -272,7 +272,11 @@ __global__ void __launch_bounds__(1024) prefill_window_kernel(const float* __res
 struct LocalSmem {
     bf16 k[CH][LDH];
     bf16 v[CH][LDH];
-    float L[CH][CH];
+    float L[CH][CH + 1];  // strictly lower part: b_i exp(G_i - G_j) k_i . k_j
+    float T[CH][CH + 1];  // (I + L)^-1, unit lower triangular
+    float M[3][16][17];   // block products of the inversion stages
+    bf16 th[2][CH][LDC];  // T diag(b gam) and T diag(b): high bf16 parts
+    bf16 tl[2][CH][LDC];  // ... and the low parts (x - hi)
     float G[CH], beta[CH];
 };
 
@@ -347,39 +351,113 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
     }
     __syncthreads();
 
-    // ---- forward substitution, one column per thread
-    const int col = tid & (HD - 1);
-    const bool is_w = tid < HD;
-    float x[CH];
-    const float G63 = sm.G[CH - 1];
-    if (is_w) {
+    // ---- T = (I + L)^-1 (fp32), blocked by 16: the four diagonal blocks by
+    // forward substitution (one thread per block column), then the lower
+    // off-diagonal blocks in order of their distance d from the diagonal,
+    //   T_ij = -T_ii sum_{k=j}^{i-1} L_ik T_kj   (i - j = d)
+    for (int e = tid; e < CH * (CH + 1); e += 256) (&sm.T[0][0])[e] = 0.0f;
+    __syncthreads();
+    if (tid < CH) {
+        const int o = (tid >> 4) * 16, jc = tid & 15;
+        float col[16];
 #pragma unroll
-        for (int i = 0; i < CH; i++) x[i] = sm.beta[i] * __expf(sm.G[i]) * __bfloat162float(sm.k[i][col]);
-    } else {
+        for (int i = 0; i < 16; i++) {
+            float acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < CH; i++) x[i] = sm.beta[i] * __bfloat162float(sm.v[i][col]);
-    }
-#pragma unroll
-    for (int i = 1; i < CH; i++) {
-        float s0 = x[i], s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;  // four chains keep the FMA pipe busy
-#pragma unroll
-        for (int kq = 0; kq < i; kq += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(&sm.L[i][kq]);
-            s0 = fmaf(-l4.x, x[kq], s0);
-            if (kq + 1 < i) s1 = fmaf(-l4.y, x[kq + 1], s1);
-            if (kq + 2 < i) s2 = fmaf(-l4.z, x[kq + 2], s2);
-            if (kq + 3 < i) s3 = fmaf(-l4.w, x[kq + 3], s3);
+            for (int kk = 0; kk < 16; kk++)
+                if (kk >= jc && kk < i) acc = fmaf(sm.L[o + i][o + kk], col[kk], acc);
+            col[i] = i < jc ? 0.0f : (i == jc ? 1.0f : -acc);
         }
-        x[i] = (s0 + s1) + (s2 + s3);
+#pragma unroll
+        for (int i = 0; i < 16; i++) sm.T[o + i][o + jc] = col[i];
     }
-    bf16* dst = (is_w ? wp : up) + ((int64_t)h * Tp + t0) * HD + col;
+    __syncthreads();
+    for (int d = 1; d < 4; d++) {
+        const int nblk = 4 - d;  // blocks (bj + d, bj), bj = 0 .. nblk - 1
+        for (int e = tid; e < nblk * 256; e += 256) {
+            const int q = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+            const int bi = q + d, bj = q;
+            float acc = 0.0f;
+            for (int kb = bj; kb < bi; kb++)
 #pragma unroll
-    for (int i = 0; i < CH; i++) dst[(int64_t)i * HD] = __float2bfloat16_rn(x[i]);
-    if (is_w) {
-        bf16* e = ek + ((int64_t)h * Tp + t0) * HD + col;
+                for (int kk = 0; kk < 16; kk++)
+                    acc = fmaf(sm.L[16 * bi + r][16 * kb + kk], sm.T[16 * kb + kk][16 * bj + cc], acc);
+            sm.M[q][r][cc] = acc;
+        }
+        __syncthreads();
+        for (int e = tid; e < nblk * 256; e += 256) {
+            const int q = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+            const int bi = q + d, bj = q;
+            float acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < CH; i++)
-            e[(int64_t)i * HD] = __float2bfloat16_rn(__expf(G63 - sm.G[i]) * __bfloat162float(sm.k[i][col]));
+            for (int kk = 0; kk < 16; kk++) acc = fmaf(sm.T[16 * bi + r][16 * bi + kk], sm.M[q][kk][cc], acc);
+            sm.T[16 * bi + r][16 * bj + cc] = -acc;
+        }
+        __syncthreads();
+    }
+
+    // ---- W' = (T diag(b gam)) K and U' = (T diag(b)) V on the tensor cores:
+    // K and V are exact bf16, the scaled T enters as hi + lo bf16 (16 bits).
+    for (int e = tid; e < CH * CH; e += 256) {
+        const int i = e >> 6, jc = e & 63;
+        const float t = sm.T[i][jc];
+        const float sc[2] = {sm.beta[jc] * __expf(sm.G[jc]), sm.beta[jc]};
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            const float x = t * sc[m];
+            const bf16 hi = __float2bfloat16_rn(x);
+            sm.th[m][i][jc] = hi;
+            sm.tl[m][i][jc] = __float2bfloat16_rn(x - __bfloat162float(hi));
+        }
+    }
+    __syncthreads();
+    {
+        const int gq = lane >> 2, qq = lane & 3;
+        const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            const bf16* rhs = m == 0 ? &sm.k[0][0] : &sm.v[0][0];
+            float acc[8][4] = {};
+#pragma unroll
+            for (int kk = 0; kk < CH / 16; kk++) {
+                uint32_t ah[4], al[4];
+                wmma16::load_a(ah, &sm.th[m][0][0], LDC, r0, 16 * kk);
+                wmma16::load_a(al, &sm.tl[m][0][0], LDC, r0, 16 * kk);
+#pragma unroll
+                for (int np2 = 0; np2 < 4; np2++) {
+                    uint32_t b[4];
+                    wmma16::load_b_kn(b, rhs, LDH, 16 * kk, n0 + 16 * np2);
+                    wmma16::mma(acc[2 * np2], ah, b[0], b[1]);
+                    wmma16::mma(acc[2 * np2 + 1], ah, b[2], b[3]);
+                    wmma16::mma(acc[2 * np2], al, b[0], b[1]);
+                    wmma16::mma(acc[2 * np2 + 1], al, b[2], b[3]);
+                }
+            }
+            bf16* dst = (m == 0 ? wp : up) + ((int64_t)h * Tp + t0) * HD;
+#pragma unroll
+            for (int n = 0; n < 8; n++) {
+                const int cl = n0 + 8 * n + 2 * qq;
+                *reinterpret_cast<uint32_t*>(dst + (int64_t)(r0 + gq) * HD + cl) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
+                *reinterpret_cast<uint32_t*>(dst + (int64_t)(r0 + gq + 8) * HD + cl) =
+                    wmma16::pack_bf16(acc[n][2], acc[n][3]);
+            }
+        }
+    }
+
+    // ---- e K with e_i = exp(G_63 - G_i): 8 bf16 per thread and store
+    const float G63 = sm.G[CH - 1];
+    for (int e = tid; e < CH * HD / 8; e += 256) {
+        const int i = e / (HD / 8), c8 = (e % (HD / 8)) * 8;
+        const float ei = __expf(G63 - sm.G[i]);
+        const uint4 kv = *reinterpret_cast<const uint4*>(&sm.k[i][c8]);
+        const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int w4 = 0; w4 < 4; w4++) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw[w4]));
+            ow[w4] = wmma16::pack_bf16(ei * f.x, ei * f.y);
+        }
+        *reinterpret_cast<uint4*>(ek + ((int64_t)h * Tp + t0 + i) * HD + c8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
     }
     if (tid < CH) gcum[(int64_t)h * Tp + t0 + tid] = sm.G[tid];
     if (tid == 0) gchunk[(int64_t)h * (Tp / CH) + c] = expf(G63);
