@@ -26,7 +26,7 @@
 // Kernels: prep (conv1d + SiLU + L2 norm, token-parallel), gates, window
 // hand-off, K1 chunk_local (W', U', e*K, cumulative G; (I + L)^-1 by blocked
 // fp32 inversion, then W' and U' as tensor-core products), K2 chunk_scan (state passing, sequential over chunks,
-// parallel over heads x 32-column slabs), K3 chunk_out (outputs, per-head
+// parallel over heads x 16-column slabs), K3 chunk_out (outputs, per-head
 // RMSNorm and SiLU(z) gate).  The in/out projections are the tensor-core
 // GEMMs of gemm_tc.cu.
 #include <algorithm>
@@ -45,7 +45,7 @@ namespace {
 
 constexpr int HD = 128;                 // head dim
 constexpr int CH = 64;                  // chunk length
-constexpr int BV = 32;                  // state columns per scan CTA
+constexpr int BV = 16;                  // state columns per scan CTA
 constexpr float kLogDecayMin = -110.0f;  // exp() of anything <= this is 0 in fp32
 constexpr int LDH = HD + 8;             // padded smem row (bf16 elements) of 128-wide tiles
 constexpr int LDC = CH + 8;             // ... of 64-wide tiles
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
 // --------------------------------------------------------- K2: chunk_scan
 //
 // grid (128 / BV, Hv), 128 threads; sequential over the chunks of the prompt.
-// The state slab S[:, 32 columns] lives in fp32 mma accumulators (warp w owns
+// The state slab S[:, BV columns] lives in fp32 mma accumulators (warp w owns
 // key rows 32w..32w+31).  Per chunk: S -> bf16 (smem, and HBM as the chunk's
 // start state), D = U' - W' S (warp w: token rows 16w..16w+15), then
 // S = gam_63 S + (e K)^T D.  The next chunk's W', e*K and U' stream in with
