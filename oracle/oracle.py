@@ -207,9 +207,27 @@ class Ref:
         self.h.refx_rmsnorm(_f(out), _f(x), _f(np.ascontiguousarray(w, np.float32)), x.size)
         return out
 
+    def gguf_probe(self, path) -> dict:
+        """The reference parser's view of a GGUF file (parse_gguf, gguf_parser.h:149-250)."""
+        meta = (C.c_longlong * 8)()
+        rc = self.h.refx_gguf_probe(str(path).encode(), meta)
+        if rc != 0:
+            raise OSError(f"parse_gguf returned {rc}")
+        keys = ("n_tensors", "hidden", "ssm_inner", "ssm_groups", "ssm_state", "ssm_conv", "layers", "data_start")
+        return dict(zip(keys, list(meta)))
+
+    def gguf_tensor(self, path, name: str) -> dict:
+        """find_tensor (gguf_parser.h:350-358): type, dims, offset of `name`."""
+        info = (C.c_longlong * 7)()
+        rc = self.h.refx_gguf_tensor(str(path).encode(), name.encode(), info)
+        if rc != 0:
+            raise KeyError(f"{name}: reference parser rc {rc}")
+        return {"type": info[0], "dims": tuple(info[2:2 + info[1]]), "offset": info[6]}
+
 
 _port: Port | None = None
 _ref: Ref | None = None
+
 
 
 def port() -> Port:

@@ -122,3 +122,44 @@ EXPORT float refx_fp16_to_fp32(uint16_t h) { return fp16_to_fp32(h); }
 EXPORT void refx_rmsnorm(float* out, const float* x, const float* w, int dim) {
     rmsnorm(out, x, w, dim);
 }
+
+/* parse_gguf / find_tensor (engine/runtime/gguf_parser.h:149-250, 350-358) on a
+ * file: the reference's own reading of a GGUF, to check files written and read
+ * by winmoe_b200.gguf.  meta: n_tensors, hidden, ssm inner, groups, state size,
+ * conv kernel, layers, data_start.  info: type, n_dims, dims[4], offset. */
+EXPORT int refx_gguf_probe(const char* path, long long* meta) {
+    GGUFModel* m = (GGUFModel*)calloc(1, sizeof(GGUFModel));
+    if (!m) return -2;
+    int rc = parse_gguf(path, m);
+    if (rc == 0) {
+        meta[0] = (long long)m->n_tensors;
+        meta[1] = m->hidden_dim;
+        meta[2] = m->ssm_inner_size;
+        meta[3] = m->ssm_group_count;
+        meta[4] = m->ssm_state_size;
+        meta[5] = m->ssm_conv_kernel;
+        meta[6] = m->num_layers;
+        meta[7] = (long long)m->data_start;
+    }
+    free(m);
+    return rc;
+}
+
+EXPORT int refx_gguf_tensor(const char* path, const char* name, long long* info) {
+    GGUFModel* m = (GGUFModel*)calloc(1, sizeof(GGUFModel));
+    if (!m) return -2;
+    int rc = parse_gguf(path, m);
+    if (rc == 0) {
+        TensorInfo* t = find_tensor(m, name);
+        if (!t) {
+            rc = -3;
+        } else {
+            info[0] = t->type;
+            info[1] = t->n_dims;
+            for (int d = 0; d < 4; d++) info[2 + d] = (long long)t->dims[d];
+            info[6] = (long long)t->offset;
+        }
+    }
+    free(m);
+    return rc;
+}

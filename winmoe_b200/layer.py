@@ -117,6 +117,16 @@ class DeltaNetWeights:
         return cls.upload(cfg, np.concatenate(parts), w_out, conv1d_w, ssm_a, dt_bias, head_norm,
                           weight_type=weight_type, **kw)
 
+    @classmethod
+    def from_gguf(cls, gguf, layer: int, head_map: int = _lib.HEAD_MAP_GROUPED, device="cuda") -> "DeltaNetWeights":
+        """DeltaNet layer `layer` of a GGUF model file (a path or winmoe_b200.gguf.GGUFFile),
+        by the reference's tensor names (winmoe_inference.c:311-392)."""
+        from .gguf import GGUFFile
+        g = gguf if isinstance(gguf, GGUFFile) else GGUFFile(gguf)
+        cfg, t = g.deltanet_layer(layer)
+        return cls.upload(cfg, t.in_proj, t.out_proj, t.conv1d_w, t.ssm_a, t.dt_bias, t.head_norm,
+                          weight_type=t.weight_type, head_map=head_map, device=device)
+
     @property
     def device(self) -> torch.device:
         t = self.in_qs if self.in_qs is not None else self.in_blocks
