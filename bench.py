@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the T=4096 prefill leg")
     ap.add_argument("--no-stack", action="store_true", help="skip the 48-layer T=32768 stack leg (config 5)")
+    ap.add_argument("--stack-mode", default="p2p", choices=["p2p", "gather"],
+                    help="N>1 stack leg: exchanges fused into the kernels as peer stores over NVLink, or NCCL "
+                         "all-gathers between the kernels")
     ap.add_argument("--no-extra-legs", action="store_true",
                     help="skip the batch-1 decode (config 1) and Q4_K sweep (config 4) legs")
     ap.add_argument("--prefill-only", action="store_true",
@@ -309,13 +312,17 @@ def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
 STACK_T, STACK_LAYERS = 32768, 48
 
 
-def run_stack(cfg, dev, world, rank, steps, warmup, tc_peak, peak_src, with_cpu, barrier, max_over_ranks):
+def run_stack(cfg, dev, world, rank, steps, warmup, tc_peak, peak_src, with_cpu, barrier, max_over_ranks,
+              mode="p2p"):
     """Config 5: T = 32768 prompt tokens through 48 residual DeltaNet layers
-    (x <- x + DN_l(rmsnorm(x))), value heads sharded over the ranks with NCCL
-    all-gathers (strong scaling: the same total work at every N)."""
+    (x <- x + DN_l(rmsnorm(x))), value heads sharded over the ranks (strong
+    scaling: the same total work at every N).  mode "p2p": the residual sharded
+    by tokens, the RMSNorm and the prefill's last kernel storing their rows
+    into the ranks that read them over NVLink (CUDA IPC); "gather": NCCL
+    all-gathers of the gated heads and of the out_proj rows."""
     import torch
     from winmoe_b200 import synth
-    from winmoe_b200.stack import StackLayer, prefill_stack
+    from winmoe_b200.stack import PeerStack, StackLayer, prefill_stack
     T, NL = STACK_T, STACK_LAYERS
     layers = []
     for l in range(NL):
@@ -328,27 +335,36 @@ def run_stack(cfg, dev, world, rank, steps, warmup, tc_peak, peak_src, with_cpu,
     xs = [x0.clone() for _ in range(runs)]
     states = [[lay.state(dev) for lay in layers] for _ in range(runs)]
     stream = torch.cuda.current_stream(dev)
+    peers = PeerStack(cfg, T, rank, world, None, dev) if world > 1 and mode == "p2p" else None
     for i in range(warmup):
-        prefill_stack(layers, states[i], xs[i], None, rank, world)
+        prefill_stack(layers, states[i], xs[i], None, rank, world, peers=peers)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(warmup, runs):
-        prefill_stack(layers, states[i], xs[i], None, rank, world)
+        prefill_stack(layers, states[i], xs[i], None, rank, world, peers=peers)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
+    if peers is not None:
+        peers.close()
     ms = max_over_ranks(e0.elapsed_time(e1)) / steps
     flops = prefill_flops_per_token(cfg) * T * NL
     ach = flops / (ms / 1e3) / 1e12
+    how = ("the residual sharded by tokens and the exchanges fused into the kernels: the RMSNorm stores each GPU's "
+           "rows into every GPU's layer input, the prefill's last kernel each token slice's head columns into the "
+           "out_proj operand of the GPU that owns the slice (peer stores over NVLink, CUDA IPC)"
+           if peers is not None else "NCCL all-gathers of the gated heads and of the out_proj token slices")
     res = {"workload": f"long prefill (config 5): T={T} tokens through {NL} residual DeltaNet layers "
                        "(rmsnorm, chunked prefill, out_proj), bf16 layer inputs, value heads sharded over the GPUs "
-                       "with NCCL all-gathers of the gated heads and of the out_proj token slices",
+                       f"with {how}", "stack_mode": mode if world > 1 else "single",
            "value": T / (ms / 1e3), "unit": "tok/s", "ms_per_prompt": ms, "steps": steps, "warmup": warmup,
            "n_gpus": world, "scaling": "strong", "layers": NL, "tokens": T,
            "weights": "Q8_0, independent per layer, drawn on the device with torch's generator (same "
                       "distributions and seeds as the parity tests' numpy draws, different values)",
-           "allgather_bytes_per_layer": T * cfg.inner * 2 + T * cfg.hidden * 4,
+           "exchanged_bytes_per_layer_per_gpu": (
+               (world - 1) * (T * cfg.hidden * 2 + (T // world) * cfg.inner * 2) // world if peers is not None
+               else (world - 1) * (T * cfg.inner * 2 + T * cfg.hidden * 4) // world),
            "roofline": {"bound": "tensor", "kernel": "whole stack", "achieved": ach, "peak": tc_peak * world,
                         "unit": "TFLOP/s", "frac": ach / (tc_peak * world), "peak_source": peak_src,
                         "algorithmic_flop_per_prompt": flops}}
@@ -564,7 +580,7 @@ def run_ours(args):
         line["prefill"] = run_prefill(cfg, w, dev, min(K, 8), W, tc_peak, peak_src)
     if not args.no_stack:
         line["stack"] = run_stack(cfg, dev, world, rank, min(K, 2), W, tc_peak, peak_src,
-                                  not args.no_cpu_baseline, barrier, max_over_ranks)
+                                  not args.no_cpu_baseline, barrier, max_over_ranks, args.stack_mode)
     if world == 1 and not args.no_extra_legs:
         line["decode_b1"] = run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, not args.no_cpu_baseline)
         line["q4k_sweep"] = run_q4k_sweep(cfg, dev, hbm_peak, peak_src, not args.no_cpu_baseline)

@@ -291,9 +291,50 @@ GDN_API int gdn_prefill_gated(const gdn_layer* layer, int64_t T, const void* x, 
  * cores exactly as gdn_prefill's out_proj, so a sharded layer reproduces the
  * single-GPU output bit for bit; T < 64 needs blocks == 1.
  */
+/*
+ * gdn_prefill_gated with each token slice's rows stored where the rank that
+ * owns the slice consumes them: with rows = T / ndst, token t's gated row
+ * [num_v_heads * head_dim] goes to dst[t / rows] + (t % rows) * ld + col0
+ * (fp16 bits; ld and col0 even, every dst 16-byte aligned).  With dst[r] =
+ * rank r's [T / G][inner] buffer opened with gdn_ipc_open and col0 = this
+ * rank's first head column, the chunked prefill's last kernel scatters the
+ * heads straight into the ranks' out_proj operands over NVLink: an
+ * all-to-all fused into the producer, each byte crossing once.  T % ndst == 0,
+ * ndst <= 8.  No counterpart in the reference (one device).
+ */
+GDN_API int gdn_prefill_scatter(const gdn_layer* layer, int64_t T, const void* x, int x_dtype,
+                                uint16_t* const* dst, int ndst, int64_t ld, int64_t col0,
+                                float* S, float* conv_buf, int32_t* conv_pos,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
 GDN_API int gdn_out_proj_gathered(const int8_t* out_qs, const uint16_t* out_d, int64_t hidden, int64_t inner,
                                   const uint16_t* gated, int blocks, int64_t T, int64_t t0, int64_t t1,
                                   float* out, void* stream);
+
+/*
+ * The same out_proj with the head blocks left where the ranks wrote them:
+ * blocks[b] points at rank b's gated[T][inner / blocks] (fp16 bits) -- this
+ * GPU's buffer or a peer's opened with gdn_ipc_open -- and the tensor cores
+ * read each token slice's K blocks straight from there (TMA loads over
+ * NVLink, no copy, no multicast), in the single-GPU k order.  T >= 64,
+ * blocks <= 8.  Replaces the all-gather of the gated heads: each rank reads
+ * only the rows of its own token range.  No counterpart in the reference.
+ */
+GDN_API int gdn_out_proj_blocks(const int8_t* out_qs, const uint16_t* out_d, int64_t hidden, int64_t inner,
+                                const uint16_t* const* blocks, int nblocks, int64_t T, int64_t t0, int64_t t1,
+                                float* out, void* stream);
+
+/*
+ * Device buffers shared between the processes of one node (CUDA IPC), for
+ * the head blocks above: gdn_ipc_alloc allocates `bytes` on the current
+ * device and writes its 64-byte handle; another process opens the handle with
+ * gdn_ipc_open (peer access over NVLink) and releases it with gdn_ipc_close;
+ * the owner frees it with gdn_ipc_free after every peer has closed it.
+ */
+GDN_API int gdn_ipc_alloc(size_t bytes, void** ptr, void* handle64);
+GDN_API int gdn_ipc_open(const void* handle64, void** ptr);
+GDN_API int gdn_ipc_close(void* ptr);
+GDN_API int gdn_ipc_free(void* ptr);
 
 /*
  * Residual add + RMSNorm between stacked layers, per row of `hidden`:
@@ -304,6 +345,16 @@ GDN_API int gdn_out_proj_gathered(const int8_t* out_qs, const uint16_t* out_d, i
  */
 GDN_API int gdn_add_rmsnorm(float* x, const float* add, const float* w, void* y, int y_dtype,
                             int64_t T, int64_t hidden, void* stream);
+
+/*
+ * gdn_add_rmsnorm over a token slice, y broadcast: row t of the slice is
+ * stored at y[b] + (row0 + t) * hidden for every b < ny (ny <= 8) -- every
+ * rank's [T][hidden] copy of the next layer's input, peers' copies opened
+ * with gdn_ipc_open, written over NVLink by the kernel that computes them
+ * (an all-gather fused into the RMSNorm).  No counterpart in the reference.
+ */
+GDN_API int gdn_add_rmsnorm_bcast(float* x, const float* add, const float* w, void* const* y, int ny,
+                                  int y_dtype, int64_t T, int64_t hidden, int64_t row0, void* stream);
 
 /*
  * Optional phase timing of gdn_decode_step / gdn_prefill, for benchmarks.

@@ -11,7 +11,8 @@ import torch
 from oracle import oracle as O
 from winmoe_b200 import GDNConfig, layer as L, synth
 from winmoe_b200.config import DIMS_35B
-from winmoe_b200.stack import StackLayer, add_rmsnorm, out_proj_gathered, prefill_gated, prefill_stack
+from winmoe_b200.stack import (PeerStack, StackLayer, add_rmsnorm, add_rmsnorm_bcast, out_proj_blocks,
+                               out_proj_gathered, prefill_gated, prefill_scatter, prefill_stack)
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -64,11 +65,43 @@ def test_head_sharding_is_bit_identical(world):
     ts = T // world
     got = torch.cat([out_proj_gathered(layers[r].out_qs, layers[r].out_d, cfg, gathered, r * ts, (r + 1) * ts)
                      for r in range(world)])
+    blocks = torch.cat([out_proj_blocks(layers[r].out_qs, layers[r].out_d, cfg, [g.data_ptr() for g in gated], T,
+                                        r * ts, (r + 1) * ts) for r in range(world)])
+    # the fused stack's form: each head slice's prefill stores its columns of
+    # token slice r into buffer r (one per rank), out_proj per buffer
+    slices = [torch.full((ts, cfg.inner), float("nan"), dtype=torch.float16, device=DEV) for _ in range(world)]
+    states2 = [lay.state(DEV) for lay in layers]
+    for r, (lay, s2) in enumerate(zip(layers, states2)):
+        prefill_scatter(lay.heads, s2, x, [b.data_ptr() for b in slices], cfg.inner, r * lay.heads.cfg.inner)
+    scattered = torch.cat([out_proj_gathered(layers[r].out_qs, layers[r].out_d, cfg, slices[r].view(1, ts, -1), 0, ts)
+                           for r in range(world)])
     torch.cuda.synchronize()
     assert torch.equal(got, want)
+    assert torch.equal(blocks, want)  # the K blocks read from separate buffers, as peers' would be
+    assert torch.equal(torch.cat(slices).view(T, -1), torch.cat(gated, dim=1))
+    assert torch.equal(scattered, want)
     for lay, s in zip(layers, states):
         assert torch.equal(s.S[0], st.S[0, lay.h0:lay.h1])
         assert torch.equal(s.conv_pos, st.conv_pos)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_add_rmsnorm_broadcast(dtype):
+    """Rows [row0, row0 + t) of every destination = the single-destination result."""
+    T, H, row0 = 96, 2048, 32
+    g = torch.Generator().manual_seed(6)
+    x = (torch.randn((T, H), generator=g) * 2).to(DEV)
+    add = torch.randn((T, H), generator=g).to(DEV)
+    x1 = x.clone()
+    want = torch.empty((T, H), dtype=dtype, device=DEV)
+    add_rmsnorm(x1, add, None, want)
+    dst = [torch.zeros((T + row0 + 5, H), dtype=dtype, device=DEV) for _ in range(3)]
+    add_rmsnorm_bcast(x, add, None, [d.data_ptr() for d in dst], dtype, row0)
+    torch.cuda.synchronize()
+    assert torch.equal(x, x1)
+    for d in dst:
+        assert torch.equal(d[row0:row0 + T], want)
+        assert not d[:row0].any() and not d[row0 + T:].any()
 
 
 def _oracle_stack(cfg, tensors, xs):
@@ -118,12 +151,19 @@ def _nccl_worker(rank, world, port, q):
     x = x0.to(f"cuda:{rank}")
     prefill_stack(layers, states, x, None, rank, world)
     res = x.cpu()
+    # the same with the exchanges fused into the kernels (peer stores over NVLink)
+    peers = PeerStack(cfg, T, rank, world, None, f"cuda:{rank}")
+    states_p = [lay.state(f"cuda:{rank}") for lay in layers]
+    xp = x0.to(f"cuda:{rank}")
+    prefill_stack(layers, states_p, xp, None, rank, world, peers=peers)
+    res_p = xp.cpu()
+    peers.close()
     if rank == 0:  # the same stack on one GPU
         layers1 = [StackLayer.upload(cfg, t, 0, 1, "cuda:0") for t in tensors]
         states1 = [lay.state("cuda:0") for lay in layers1]
         x1 = x0.to("cuda:0")
         prefill_stack(layers1, states1, x1)
-        q.put(bool(torch.equal(res, x1.cpu())))
+        q.put(bool(torch.equal(res, x1.cpu()) and torch.equal(res_p, x1.cpu())))
     dist.barrier()
     dist.destroy_process_group()
 

@@ -66,6 +66,14 @@ SIGNATURES = {
     "gdn_prefill_gated": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gdn_out_proj_gathered": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _i64, _i64, _i64, _vp, _vp]),
     "gdn_add_rmsnorm": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _vp]),
+    "gdn_add_rmsnorm_bcast": (_int, [_vp, _vp, _vp, C.POINTER(_vp), _int, _int, _i64, _i64, _i64, _vp]),
+    "gdn_prefill_scatter": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, C.POINTER(_vp), _int, _i64, _i64, _vp, _vp,
+                                   _vp, _vp, _sz, _vp]),
+    "gdn_out_proj_blocks": (_int, [_vp, _vp, _i64, _i64, C.POINTER(_vp), _int, _i64, _i64, _i64, _vp, _vp]),
+    "gdn_ipc_alloc": (_int, [_sz, C.POINTER(_vp), _vp]),
+    "gdn_ipc_open": (_int, [_vp, C.POINTER(_vp)]),
+    "gdn_ipc_close": (_int, [_vp]),
+    "gdn_ipc_free": (_int, [_vp]),
     "gdn_prefill": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gdn_profile_enable": (_int, [_int]),
     "gdn_decode_phase_ms": (_int, [C.POINTER(C.c_float), _int]),

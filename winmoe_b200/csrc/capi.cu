@@ -222,9 +222,31 @@ int gdn_prefill(const gdn_layer* layer, int64_t T, const void* x, int x_dtype, f
 
 int gdn_prefill_gated(const gdn_layer* layer, int64_t T, const void* x, int x_dtype, uint16_t* gated, float* S,
                       float* conv_buf, int32_t* conv_pos, void* workspace, size_t workspace_bytes, void* stream) {
-    if (gated == nullptr) return fail(GDN_ERR_ARG, "gated must be non-NULL");
-    return prefill(layer, T, x, x_dtype, nullptr, reinterpret_cast<__half*>(gated), S, conv_buf, conv_pos, workspace,
-                   workspace_bytes, as_stream(stream));
+    if (gated == nullptr || layer == nullptr) return fail(GDN_ERR_ARG, "gated and layer must be non-NULL");
+    RowDest dst{};
+    dst.ptr[0] = gated;
+    dst.n = 1;
+    dst.rows = T;
+    dst.ld = (int64_t)layer->dims.num_v_heads * 128;
+    return prefill(layer, T, x, x_dtype, nullptr, &dst, S, conv_buf, conv_pos, workspace, workspace_bytes,
+                   as_stream(stream));
+}
+
+int gdn_prefill_scatter(const gdn_layer* layer, int64_t T, const void* x, int x_dtype, uint16_t* const* dst, int ndst,
+                        int64_t ld, int64_t col0, float* S, float* conv_buf, int32_t* conv_pos, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    if (dst == nullptr || layer == nullptr) return fail(GDN_ERR_ARG, "prefill scatter: NULL pointer");
+    if (ndst < 1 || ndst > kMaxRowDest || T % ndst != 0)
+        return fail(GDN_ERR_SHAPE, "prefill scatter: T=%lld over %d destinations (1..%d)", (long long)T, ndst,
+                    kMaxRowDest);
+    RowDest d{};
+    for (int r = 0; r < ndst; r++) d.ptr[r] = dst[r];
+    d.n = ndst;
+    d.rows = T / ndst;
+    d.ld = ld;
+    d.col0 = col0;
+    return prefill(layer, T, x, x_dtype, nullptr, &d, S, conv_buf, conv_pos, workspace, workspace_bytes,
+                   as_stream(stream));
 }
 
 int gdn_out_proj_gathered(const int8_t* out_qs, const uint16_t* out_d, int64_t hidden, int64_t inner,
@@ -250,13 +272,90 @@ int gdn_out_proj_gathered(const int8_t* out_qs, const uint16_t* out_d, int64_t h
     return launch_q8_0_gemm_tc(out_qs, out_d, hidden, inner, gated, false, t1 - t0, out, hidden, opt, s);
 }
 
+int gdn_out_proj_blocks(const int8_t* out_qs, const uint16_t* out_d, int64_t hidden, int64_t inner,
+                        const uint16_t* const* blocks, int nblocks, int64_t T, int64_t t0, int64_t t1, float* out,
+                        void* stream) {
+    if (!out_qs || !out_d || !blocks || !out) return fail(GDN_ERR_ARG, "out_proj blocks: NULL pointer");
+    if (nblocks < 1 || nblocks > 8 || inner % ((int64_t)nblocks * 64) != 0)
+        return fail(GDN_ERR_SHAPE, "out_proj blocks: inner=%lld in %d blocks (1..8) of a multiple of 64",
+                    (long long)inner, nblocks);
+    if (T < 64 || t0 < 0 || t1 > T || t0 >= t1) return fail(GDN_ERR_SHAPE, "out_proj blocks: bad token range (T >= 64)");
+    if (!aligned(out, 16) || !aligned(out_qs, 16)) return fail(GDN_ERR_ARG, "out_proj blocks: misaligned pointer");
+    const void* ptrs[8];
+    for (int b = 0; b < nblocks; b++) ptrs[b] = blocks[b];
+    TcOptions opt;
+    opt.a_blk_k = inner / nblocks;
+    opt.a_rows = T;
+    opt.a_row0 = t0;
+    opt.a_block_ptrs = ptrs;
+    opt.a_nblocks = nblocks;
+    return launch_q8_0_gemm_tc(out_qs, out_d, hidden, inner, ptrs[0], false, t1 - t0, out, hidden, opt,
+                               as_stream(stream));
+}
+
+int gdn_ipc_alloc(size_t bytes, void** ptr, void* handle64) {
+    if (!ptr || !handle64 || bytes == 0) return fail(GDN_ERR_ARG, "ipc_alloc: bad argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    GDN_CUDA(cudaMalloc(ptr, bytes));
+    const cudaError_t e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle64), *ptr);
+    if (e != cudaSuccess) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        return cuda_status(e, "cudaIpcGetMemHandle");
+    }
+    return GDN_OK;
+}
+
+int gdn_ipc_open(const void* handle64, void** ptr) {
+    if (!ptr || !handle64) return fail(GDN_ERR_ARG, "ipc_open: bad argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    GDN_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return GDN_OK;
+}
+
+int gdn_ipc_close(void* ptr) {
+    GDN_CUDA(cudaIpcCloseMemHandle(ptr));
+    return GDN_OK;
+}
+
+int gdn_ipc_free(void* ptr) {
+    GDN_CUDA(cudaFree(ptr));
+    return GDN_OK;
+}
+
 int gdn_add_rmsnorm(float* x, const float* add, const float* w, void* y, int y_dtype, int64_t T, int64_t hidden,
                     void* stream) {
     if (!x || !y) return fail(GDN_ERR_ARG, "add_rmsnorm: x and y must be non-NULL");
     if (T < 0 || hidden <= 0 || T > INT32_MAX) return fail(GDN_ERR_SHAPE, "add_rmsnorm: bad shape");
     if (y_dtype != GDN_DTYPE_F32 && y_dtype != GDN_DTYPE_BF16 && y_dtype != GDN_DTYPE_F16)
         return fail(GDN_ERR_TYPE, "add_rmsnorm: y_dtype %d is not supported", y_dtype);
-    return launch_add_rmsnorm(x, add, w, y, y_dtype, T, hidden, as_stream(stream));
+    RowDest d{};
+    d.ptr[0] = y;
+    d.n = 1;
+    d.rows = T > 0 ? T : 1;
+    d.ld = hidden;
+    return launch_add_rmsnorm(x, add, w, d, y_dtype, T, hidden, as_stream(stream));
+}
+
+int gdn_add_rmsnorm_bcast(float* x, const float* add, const float* w, void* const* y, int ny, int y_dtype, int64_t T,
+                          int64_t hidden, int64_t row0, void* stream) {
+    if (!x || !y) return fail(GDN_ERR_ARG, "add_rmsnorm bcast: x and y must be non-NULL");
+    if (T < 0 || hidden <= 0 || T > INT32_MAX || row0 < 0) return fail(GDN_ERR_SHAPE, "add_rmsnorm bcast: bad shape");
+    if (ny < 1 || ny > kMaxRowDest) return fail(GDN_ERR_SHAPE, "add_rmsnorm bcast: %d destinations (1..%d)", ny,
+                                                kMaxRowDest);
+    if (y_dtype != GDN_DTYPE_F32 && y_dtype != GDN_DTYPE_BF16 && y_dtype != GDN_DTYPE_F16)
+        return fail(GDN_ERR_TYPE, "add_rmsnorm bcast: y_dtype %d is not supported", y_dtype);
+    RowDest d{};
+    for (int r = 0; r < ny; r++) {
+        if (y[r] == nullptr) return fail(GDN_ERR_ARG, "add_rmsnorm bcast: destination %d is NULL", r);
+        d.ptr[r] = y[r];
+    }
+    d.n = ny;
+    d.rows = T > 0 ? T : 1;
+    d.ld = hidden;
+    d.col0 = row0 * hidden;
+    return launch_add_rmsnorm(x, add, w, d, y_dtype, T, hidden, as_stream(stream));
 }
 
 int gdn_profile_enable(int on) { return profile_enable(on); }

@@ -37,6 +37,25 @@ enum : uint32_t { DEV_ERR_TIMEOUT = 1u, DEV_ERR_BOUNDS = 2u };
 uint32_t* device_error_word();  // per-device __device__ word, looked up once per device
 int sm_count();                  // SMs of the current device (cached per device)
 
+// Where a kernel writes row t of a [T][width] output: token slice r = t / rows
+// (rows = T for one destination) goes to ptr[r] + (t - r rows) ld + col0, in
+// elements.  With the ptr[r] of other GPUs (CUDA IPC) the writes are plain
+// peer stores over NVLink: a producer kernel scatters its rows to the ranks
+// that consume them, and every byte crosses the link once.
+constexpr int kMaxRowDest = 8;
+struct RowDest {
+    void* ptr[kMaxRowDest];
+    int64_t rows;  // rows per destination
+    int64_t ld;    // row pitch, elements
+    int64_t col0;  // first column, elements
+    int n;
+    template <typename E>
+    __device__ __forceinline__ E* row(int64_t t) const {
+        const int64_t r = t / rows;
+        return static_cast<E*>(ptr[r]) + (t - r * rows) * ld + col0;
+    }
+};
+
 // Programmatic dependent launch.  Kernels started with launch_pdl may be
 // scheduled while their predecessor in the stream is still running: each kernel
 // calls pdl_trigger() on entry (its own dependents may then be scheduled once

@@ -35,6 +35,7 @@
 // fixed order, so results do not depend on scheduling.
 #include <cuda.h>
 #include <algorithm>
+#include <string.h>
 #include <type_traits>
 #include "gdn_common.cuh"
 #include "ptx_sm100.cuh"
@@ -148,11 +149,19 @@ __device__ __forceinline__ void store_chunk(uint8_t* tile, int rr, int c, const 
     *reinterpret_cast<uint4*>(row + (((2 * c + 1) ^ (rr & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
+// Tensor maps of activation K blocks held in separate buffers (see TcOptions).
+constexpr int kMaxABlocks = 8;
+struct alignas(64) ABlockMaps {
+    CUtensorMap m[kMaxABlocks];
+    int n;  // 0: the activations are tm_a
+};
+
 template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     q8_0_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                        const uint16_t* __restrict__ dsc, int n, int k, int m, float* __restrict__ y, int64_t ldy,
-                        int kt_per_split, int a_blk_k, int a_row0, uint32_t* __restrict__ err) {
+                        const __grid_constant__ ABlockMaps am, const uint16_t* __restrict__ dsc, int n, int k, int m,
+                        float* __restrict__ y, int64_t ldy, int kt_per_split, int a_blk_k, int a_row0,
+                        uint32_t* __restrict__ err) {
     using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
@@ -221,7 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int mt = 0; mt < MT; mt++) {
                         const uint32_t dst = sbase + L::A_OFF + (s * MT + mt) * L::A_BYTES;
-                        if (a_blk_k > 0)  // activations stored as K blocks [k / a_blk_k][rows][a_blk_k]
+                        if (am.n > 0)  // K block kk / a_blk_k in its own buffer (possibly a peer's)
+                            tma_load_2d(dst, &am.m[kk / a_blk_k], kk % a_blk_k, a_row0 + m0 + mt * BM, a_full(s));
+                        else if (a_blk_k > 0)  // activations stored as K blocks [k / a_blk_k][rows][a_blk_k]
                             tma_load_3d(dst, &tm_a, kk % a_blk_k, a_row0 + m0 + mt * BM, kk / a_blk_k, a_full(s));
                         else
                             tma_load_2d(dst, &tm_a, kk, m0 + mt * BM, a_full(s));
@@ -547,6 +558,8 @@ namespace {
 
 struct ALayout {
     int64_t blk_k = 0, rows = 0, row0 = 0;  // see TcOptions
+    const void* const* block_ptrs = nullptr;
+    int nblocks = 0;
 };
 
 template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT>
@@ -555,10 +568,21 @@ int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void
     using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
     CUtensorMap ma, mb;
     const CUtensorMapDataType adt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    int st = al.blk_k > 0 ? make_map_3d(&ma, adt, a, (uint64_t)al.blk_k, (uint64_t)al.rows, (uint64_t)(k / al.blk_k),
+    ABlockMaps am;
+    memset(&am, 0, sizeof(am));
+    int st = GDN_OK;
+    if (al.nblocks > 0) {
+        for (int g = 0; g < al.nblocks && !st; g++)
+            st = make_map_2d(&am.m[g], adt, al.block_ptrs[g], (uint64_t)al.blk_k, (uint64_t)al.rows,
+                             (uint64_t)al.blk_k * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+        am.n = al.nblocks;
+        ma = am.m[0];  // a valid map for the prologue's prefetch
+    } else {
+        st = al.blk_k > 0 ? make_map_3d(&ma, adt, a, (uint64_t)al.blk_k, (uint64_t)al.rows, (uint64_t)(k / al.blk_k),
                                         (uint64_t)al.blk_k * 2, (uint64_t)al.rows * al.blk_k * 2, BK, BM)
                           : make_map_2d(&ma, adt, a, (uint64_t)k, (uint64_t)m, (uint64_t)k * 2, BK, BM,
                                         CU_TENSOR_MAP_SWIZZLE_128B);
+    }
     if (st) return st;
     st = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, qs, (uint64_t)k, (uint64_t)n, (uint64_t)k, BK, BN,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -566,7 +590,7 @@ int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void
     auto kern = q8_0_gemm_tc_kernel<BN, MT, SA, S16, S8, BF16, SPLIT>;
     GDN_CUDA(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM));
     const dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM * MT - 1) / (BM * MT)), (unsigned)splits);
-    return launch_pdl("q8_0_gemm_tc_kernel", kern, grid, dim3(kThreads), L::SMEM, s, ma, mb, d, (int)n, (int)k,
+    return launch_pdl("q8_0_gemm_tc_kernel", kern, grid, dim3(kThreads), L::SMEM, s, ma, mb, am, d, (int)n, (int)k,
                       (int)m, out, ld_out, kt_per, (int)al.blk_k, (int)al.row0, device_error_word());
 }
 
@@ -616,6 +640,16 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
     if (opt.split_precision && a_bf16)
         return fail(GDN_ERR_TYPE, "split-precision tensor-core GEMM takes fp16 activations");
     ALayout al;
+    if (opt.a_nblocks > 0) {
+        if (opt.a_nblocks > kMaxABlocks || opt.a_block_ptrs == nullptr || opt.a_blk_k * opt.a_nblocks != k)
+            return fail(GDN_ERR_SHAPE, "K blocks: %d buffers of %lld must cover k=%lld (at most %d)", opt.a_nblocks,
+                        (long long)opt.a_blk_k, (long long)k, kMaxABlocks);
+        for (int g = 0; g < opt.a_nblocks; g++)
+            if (opt.a_block_ptrs[g] == nullptr || !aligned(opt.a_block_ptrs[g], 16))
+                return fail(GDN_ERR_ARG, "K block %d: NULL or not 16-byte aligned", g);
+        al.block_ptrs = opt.a_block_ptrs;
+        al.nblocks = opt.a_nblocks;
+    }
     if (opt.a_blk_k > 0) {
         if (opt.a_blk_k % BK != 0 || k % opt.a_blk_k != 0)
             return fail(GDN_ERR_SHAPE, "K blocks must be a multiple of 64 that divides k");

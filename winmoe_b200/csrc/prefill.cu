@@ -642,7 +642,8 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
                                                         const float* __restrict__ gcum,
                                                         const float* __restrict__ proj, int64_t ldp,
                                                         const float* __restrict__ head_norm,
-                                                        __half* __restrict__ gated, int64_t T, int64_t Tp, int hk,
+                                                        __half* __restrict__ gated, const RowDest dst,
+                                                        int64_t T, int64_t Tp, int hk,
                                                         int hv, int qkv, int head_map) {
     pdl_trigger();
     pdl_wait();
@@ -772,7 +773,7 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
         const int64_t t = t0 + (hf ? rB : rA);
         if (t >= T) continue;
         const float inv = hf ? invB : invA;
-        __half* gout = gated + t * inner + h * HD;
+        __half* gout = (gated != nullptr ? gated + t * inner : dst.row<__half>(t)) + h * HD;
 #pragma unroll
         for (int n = 0; n < HD / 8; n++) {
             const int v = 8 * n + 2 * qq;
@@ -801,8 +802,8 @@ int set_smem(K kern, size_t bytes) {
 
 size_t prefill_workspace_bytes(const gdn_dims& d, int64_t T) { return pcarve(d, T, nullptr).total; }
 
-int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, __half* gated_out, float* S,
-            float* conv_buf, int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s) {
+int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, const RowDest* gated_out,
+            float* S, float* conv_buf, int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s) {
     int st = validate_layer(L);
     if (st) return st;
     if (T <= 0 || T > (int64_t)1 << 26) return fail(GDN_ERR_SHAPE, "T must be in [1, 2^26] (got %lld)", (long long)T);
@@ -810,9 +811,19 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
         return fail(GDN_ERR_ARG, "x, the output, S and conv_pos must be non-NULL");
     if (x_dtype != GDN_DTYPE_F32 && x_dtype != GDN_DTYPE_BF16 && x_dtype != GDN_DTYPE_F16)
         return fail(GDN_ERR_TYPE, "x_dtype %d is not supported", x_dtype);
-    if ((out && !aligned(out, 16)) || (gated_out && !aligned(gated_out, 16)) || !aligned(S, 16))
+    if ((out && !aligned(out, 16)) || !aligned(S, 16))
         return fail(GDN_ERR_ARG, "the output and S must be 16-byte aligned");
     const gdn_dims& d = L->dims;
+    if (gated_out) {
+        const RowDest& g = *gated_out;
+        if (g.n < 1 || g.n > kMaxRowDest || g.rows < 1 || g.rows * g.n != T || g.col0 < 0 ||
+            g.ld < g.col0 + (int64_t)d.num_v_heads * 128 || (g.ld | g.col0) % 2 != 0)
+            return fail(GDN_ERR_SHAPE, "gated destinations: %d x %lld rows must cover T=%lld, pitch %lld >= "
+                        "column %lld + %lld, both even", g.n, (long long)g.rows, (long long)T, (long long)g.ld,
+                        (long long)g.col0, (long long)d.num_v_heads * 128);
+        for (int r = 0; r < g.n; r++)
+            if (!aligned(g.ptr[r], 16)) return fail(GDN_ERR_ARG, "gated destination %d is NULL or misaligned", r);
+    }
     const size_t need = prefill_workspace_bytes(d, T);
     if (wsp == nullptr || ws_bytes < need || !aligned(wsp, 256))
         return fail(GDN_ERR_ARG, "workspace must be 256-aligned and hold %zu bytes (got %zu)", need, ws_bytes);
@@ -889,7 +900,8 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
         if ((st = set_smem(chunk_out_kernel, sm3))) return st;
         st = launch_pdl("chunk_out_kernel", chunk_out_kernel, dim3((unsigned)D.nc, (unsigned)D.hv), dim3(128), sm3, s,
                         W.qn, W.kn, W.sc, W.dl, W.gcum, W.proj, D.ldp, L->head_norm,
-                        gated_out ? gated_out : W.gated, T, D.Tp, D.hk, D.hv, D.qkv, L->head_map);
+                        gated_out ? nullptr : W.gated, gated_out ? *gated_out : RowDest{}, T, D.Tp, D.hk, D.hv,
+                        D.qkv, L->head_map);
         if (st) return st;
     }
 

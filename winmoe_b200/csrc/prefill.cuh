@@ -6,9 +6,9 @@ namespace gdn {
 
 size_t prefill_workspace_bytes(const gdn_dims& d, int64_t T);
 // out [T][hidden] fp32 after out_proj, or (out == NULL) the gated head outputs
-// before out_proj in gated_out [T][Hv*128] fp16.
-int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, __half* gated_out, float* S,
-            float* conv_buf, int32_t* conv_pos, void* ws, size_t ws_bytes, cudaStream_t s);
+// before out_proj: token t's [Hv*128] fp16 row goes to gated_out->row(t) (see RowDest).
+int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, const RowDest* gated_out,
+            float* S, float* conv_buf, int32_t* conv_pos, void* ws, size_t ws_bytes, cudaStream_t s);
 int validate_layer(const gdn_layer* L);
 
 }  // namespace gdn

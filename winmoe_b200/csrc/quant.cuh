@@ -30,6 +30,10 @@ struct TcOptions {
     // Activations stored as K blocks a[k / a_blk_k][a_rows][a_blk_k] (0: plain
     // [m][k]); the GEMM's m rows are rows a_row0 .. a_row0 + m - 1 of every block.
     int64_t a_blk_k = 0, a_rows = 0, a_row0 = 0;
+    // ... or the K blocks in separate buffers (this GPU's or peers' memory over
+    // NVLink, each [a_rows][a_blk_k]): a_block_ptrs[k / a_blk_k], a_nblocks <= 8
+    const void* const* a_block_ptrs = nullptr;
+    int a_nblocks = 0;
 };
 size_t gemm_tc_workspace_bytes(int64_t m, int64_t n, int splits);
 
