@@ -18,13 +18,16 @@
 // in fp32 whatever the rest of the sum, so a decay that underflows to 0 in the
 // reference (expf, deltanet_impl.h:251) zeroes the same products here.
 //
-// Per-element exponentials and divisions (SiLU, the exp(G_i - G_j) factors, the
-// output gate) use the __expf / __fdividef intrinsics: their few-ulp errors sit
-// far below the bf16 rounding every one of these values goes through next, and
-// with IEEE expf and division the output kernel spent ~3/4 of its time there.
+// Per-element exponentials (the exp(G_i - G_j) factors) use the __expf
+// intrinsic, and SiLU (conv output, output gate) one hardware tanh:
+// x sigmoid(x) = h + h tanh(h), h = x / 2, absolute error <= 2^-12 |x|.  These
+// errors sit below the bf16 / fp16 rounding every one of these values goes
+// through next; with IEEE expf and division the output kernel spent ~3/4 of its
+// time there, and with exp + divide per SiLU the prep kernel was bound by the
+// special-function pipe.
 //
-// Kernels: prep (conv1d + SiLU + L2 norm, token-parallel), gates, window
-// hand-off, K1 chunk_local (W', U', e*K, cumulative G; (I + L)^-1 by blocked
+// Kernels: prep (conv1d + SiLU + L2 norm, gates and the window hand-off,
+// token-parallel), K1 chunk_local (W', U', e*K, cumulative G; (I + L)^-1 by blocked
 // fp32 inversion, then W' and U' as tensor-core products), K2 chunk_scan (state passing, sequential over chunks,
 // parallel over heads x 16-column slabs), K3 chunk_out (outputs, per-head
 // RMSNorm and SiLU(z) gate).  The in/out projections are the tensor-core
@@ -50,6 +53,17 @@ constexpr float kLogDecayMin = -110.0f;  // exp() of anything <= this is 0 in fp
 constexpr int LDH = HD + 8;             // padded smem row (bf16 elements) of 128-wide tiles
 constexpr int LDC = CH + 8;             // ... of 64-wide tiles
 constexpr int LDV = BV + 8;             // ... of BV-wide tiles
+
+__device__ __forceinline__ float tanh_hw(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// SiLU(x) = x sigmoid(x) = x (1 + tanh(x / 2)) / 2: one special-function op.
+__device__ __forceinline__ float silu_fast(float x) {
+    const float h = 0.5f * x;
+    return fmaf(h, tanh_hw(h), h);
+}
 
 struct PDims {
     int hk, hv, key, inner, qkv;
@@ -123,31 +137,86 @@ PWork pcarve(const gdn_dims& d, int64_t T, void* base) {
 
 // ------------------------------------------------------------------ prep
 //
-// One warp per (128-channel chunk hc of qkv, block of kTokBlock tokens); lane
-// l owns channels 4l..4l+3.  The warp walks its tokens keeping the last three
-// raw projections in registers, so each projection row and the conv weights
-// are read once.  Causal conv1d over tokens t-3..t (taps k = 0 oldest .. 3 = t),
-// where tokens before the prompt come from the conv window of the state:
-// token -j (j = 1..3) sits in slot (p0 - j) mod 4 (deltanet_impl.h:220-230).
-// Then SiLU; q/k chunks are L2-normalised (double sum, deltanet_impl.h:85-91).
-// Padding tokens (t >= T) are written as zeros.
+// One kernel for everything between the input projection and the chunked
+// recurrence.  Warps per block of kTokBlock tokens: one per 128-channel chunk
+// hc of qkv, plus one gate warp.
+//
+// Chunk warps: lane l owns channels 4l..4l+3.  All kTokBlock raw projection
+// rows are loaded up front (16 loads in flight per lane), then the causal
+// conv1d over tokens t-3..t (taps k = 0 oldest .. 3 = t) runs from the last
+// token down, in place; tokens before the prompt come from the conv window of
+// the state: token -j (j = 1..3) sits in slot (p0 - j) mod 4
+// (deltanet_impl.h:220-230).  Then SiLU; q/k chunks are L2-normalised
+// (deltanet_impl.h:85-91), the sixteen butterflies interleaved.  The outputs
+// are rounded to bf16 next, so the conv taps contract to FMAs and the sum of
+// squares is fp32 (the reference's double sum and separate roundings move
+// these values by ~1e-7 relative, far below bf16's 2^-9).
+// Padding tokens (t >= T) are written as zeros.  The warp of token block 0
+// also writes the conv window after the prompt -- slot (p0 + i) mod 4 <- raw
+// projection of token i for the last min(T, 4) tokens -- after it has read the
+// old window: no other warp touches those channels' window.  (conv_pos is
+// advanced by the next kernel, once every warp here has read it.)
+//
+// Gate warp: lane = value head; per token the log decay log(a) = ssm_a *
+// softplus(alpha + dt_bias) with the reference's clamps (a in [0, 1], NaN ->
+// 0.99, no ssm_a/dt_bias -> 0.99; deltanet_impl.h:247-257) kept in log space,
+// and beta = stable sigmoid (260).
 constexpr int kTokBlock = 16;
 
-__global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T,
-                                                           int64_t Tp, const float* __restrict__ conv_buf,
+__global__ void __launch_bounds__(256, 2) prefill_prep_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T,
+                                                           int64_t Tp, float* __restrict__ conv_buf,
                                                            const int32_t* __restrict__ conv_pos,
                                                            const float* __restrict__ conv_w, bf16* __restrict__ qn,
-                                                           bf16* __restrict__ kn, bf16* __restrict__ vb, int qkv,
-                                                           int hk) {
+                                                           bf16* __restrict__ kn, bf16* __restrict__ vb,
+                                                           const float* __restrict__ ssm_a,
+                                                           const float* __restrict__ dt_bias, float* __restrict__ glog,
+                                                           float* __restrict__ beta, int qkv, int hk, int hv) {
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31;
-    const int nchunk = qkv / HD;
+    const int nchunk = qkv / HD + 1;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nblk = Tp / kTokBlock;
     if (gw >= nblk * nchunk) return;
     const int hc = (int)(gw % nchunk);
     const int64_t tb = (gw / nchunk) * kTokBlock;
+
+    if (hc == nchunk - 1) {  // ---- gates of all heads for this token block
+        const int64_t gate0 = (int64_t)qkv + (int64_t)hv * HD;
+        for (int h = lane; h < hv; h += 32) {
+            const float sa = ssm_a != nullptr ? ssm_a[h] : 0.0f;
+            const float db = dt_bias != nullptr ? dt_bias[h] : 0.0f;
+#pragma unroll 4
+            for (int64_t t = tb; t < tb + kTokBlock; t++) {
+                const int64_t i = (int64_t)h * Tp + t;
+                if (t >= T) {
+                    glog[i] = 0.0f;
+                    beta[i] = 0.0f;
+                    continue;
+                }
+                const float* pr = proj + t * ldp + gate0;
+                const float beta_raw = pr[h], alpha_raw = pr[hv + h];
+                float gl = logf(0.99f);
+                if (ssm_a != nullptr && dt_bias != nullptr) {
+                    const float x = alpha_raw + db;
+                    gl = sa * (log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f));
+                    if (isnan(gl)) gl = logf(0.99f);
+                    gl = fminf(gl, 0.0f);
+                }
+                glog[i] = fmaxf(gl, kLogDecayMin);
+                float bt;
+                if (beta_raw >= 0.0f) {
+                    bt = 1.0f / (1.0f + expf(-beta_raw));
+                } else {
+                    const float z = expf(beta_raw);
+                    bt = z / (1.0f + z);
+                }
+                beta[i] = bt;
+            }
+        }
+        return;
+    }
+
     bf16* dst;
     if (hc < hk) dst = qn + (int64_t)hc * Tp * HD;
     else if (hc < 2 * hk) dst = kn + (int64_t)(hc - hk) * Tp * HD;
@@ -155,11 +224,16 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
     dst += 4 * lane;
     const int ch = hc * HD + 4 * lane;
     const bool conv = conv_buf != nullptr && conv_w != nullptr;
-    float4 wv[4] = {};
-    float4 hist[3] = {};  // raw projections of tokens t-3, t-2, t-1
+
+    float4 x[kTokBlock];  // raw projections, then (in place) the outputs
+#pragma unroll
+    for (int j = 0; j < kTokBlock; j++)
+        x[j] = tb + j < T ? *reinterpret_cast<const float4*>(proj + (tb + j) * ldp + ch) : make_float4(0.f, 0.f, 0.f, 0.f);
     if (conv) {
+        float4 wv[4];
 #pragma unroll
         for (int c = 0; c < 4; c++) wv[c] = reinterpret_cast<const float4*>(conv_w)[ch + c];
+        float4 hist[3];  // raw projections of tokens tb-3, tb-2, tb-1
         const int p0 = *conv_pos;
 #pragma unroll
         for (int j = 0; j < 3; j++) {
@@ -167,99 +241,55 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const float* __restri
             hist[j] = tt >= 0 ? *reinterpret_cast<const float4*>(proj + tt * ldp + ch)
                               : *reinterpret_cast<const float4*>(conv_buf + (int64_t)((p0 + (int)tt) & 3) * qkv + ch);
         }
-    }
-    for (int64_t t = tb; t < tb + kTokBlock; t++) {
-        if (t >= T) {
-            *reinterpret_cast<uint2*>(dst + t * HD) = make_uint2(0u, 0u);
-            continue;
+        if (tb == 0) {  // the window after the prompt (the old one is read above, in program order)
+            for (int64_t i = (T > 4 ? T - 4 : 0); i < T; i++)
+                *reinterpret_cast<float4*>(conv_buf + (int64_t)((p0 + (int)i) & 3) * qkv + ch) =
+                    *reinterpret_cast<const float4*>(proj + i * ldp + ch);
         }
-        const float4 raw = *reinterpret_cast<const float4*>(proj + t * ldp + ch);
-        float4 xv = raw;
-        if (conv) {
-            float in[4] = {raw.x, raw.y, raw.z, raw.w};
-            const float h0[4] = {hist[0].x, hist[0].y, hist[0].z, hist[0].w};
-            const float h1[4] = {hist[1].x, hist[1].y, hist[1].z, hist[1].w};
-            const float h2[4] = {hist[2].x, hist[2].y, hist[2].z, hist[2].w};
+#pragma unroll
+        for (int j = kTokBlock - 1; j >= 0; j--) {  // x[j] needs raw x[j-3..j]: run from the top down
+            const float4 r0 = j >= 3 ? x[j - 3] : hist[j];
+            const float4 r1 = j >= 2 ? x[j - 2] : hist[j + 1];
+            const float4 r2 = j >= 1 ? x[j - 1] : hist[j + 2];
+            const float h0[4] = {r0.x, r0.y, r0.z, r0.w}, h1[4] = {r1.x, r1.y, r1.z, r1.w};
+            const float h2[4] = {r2.x, r2.y, r2.z, r2.w}, in[4] = {x[j].x, x[j].y, x[j].z, x[j].w};
+            float o[4];
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 const float4 w = wv[c];
-                float sum = 0.0f;
-                sum = __fadd_rn(sum, __fmul_rn(w.x, h0[c]));
-                sum = __fadd_rn(sum, __fmul_rn(w.y, h1[c]));
-                sum = __fadd_rn(sum, __fmul_rn(w.z, h2[c]));
-                sum = __fadd_rn(sum, __fmul_rn(w.w, in[c]));
-                const float sig = __fdividef(1.0f, 1.0f + __expf(-sum));
-                in[c] = __fmul_rn(sum, sig);
+                float sum = w.x * h0[c];
+                sum = fmaf(w.y, h1[c], sum);
+                sum = fmaf(w.z, h2[c], sum);
+                sum = fmaf(w.w, in[c], sum);
+                o[c] = silu_fast(sum);
             }
-            xv = make_float4(in[0], in[1], in[2], in[3]);
-            hist[0] = hist[1];
-            hist[1] = hist[2];
-            hist[2] = raw;
+            x[j] = make_float4(o[0], o[1], o[2], o[3]);
         }
-        if (hc < 2 * hk) {
-            double ss = (double)xv.x * xv.x + (double)xv.y * xv.y + (double)xv.z * xv.z + (double)xv.w * xv.w;
+    }
+    if (hc < 2 * hk) {
+        float ss[kTokBlock];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float inv = 1.0f / (sqrtf((float)ss) + 1e-6f);
-            xv = make_float4(__fmul_rn(xv.x, inv), __fmul_rn(xv.y, inv), __fmul_rn(xv.z, inv), __fmul_rn(xv.w, inv));
+        for (int j = 0; j < kTokBlock; j++)
+            ss[j] = fmaf(x[j].x, x[j].x, fmaf(x[j].y, x[j].y, fmaf(x[j].z, x[j].z, x[j].w * x[j].w)));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int j = 0; j < kTokBlock; j++) ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], o);
+#pragma unroll
+        for (int j = 0; j < kTokBlock; j++) {
+            // 1 / (sqrt(ss) + 1e-6) (deltanet_impl.h:89): the epsilon shifts the result by
+            // 1e-6 / sqrt(ss) relative, so above ss = 1e-4 one rsqrt is as good
+            const float inv = ss[j] > 1e-4f ? rsqrtf(ss[j]) : 1.0f / (sqrtf(ss[j]) + 1e-6f);
+            x[j] = make_float4(x[j].x * inv, x[j].y * inv, x[j].z * inv, x[j].w * inv);
         }
-        *reinterpret_cast<uint2*>(dst + t * HD) =
-            make_uint2(wmma16::pack_bf16(xv.x, xv.y), wmma16::pack_bf16(xv.z, xv.w));
     }
-}
-
-// Gates per (head h, token t): log decay log(a) = ssm_a * softplus(alpha + dt_bias)
-// with the reference's clamps (a in [0, 1], NaN -> 0.99, no ssm_a/dt_bias -> 0.99;
-// deltanet_impl.h:247-257) kept in log space, and beta = stable sigmoid (260).
-__global__ void prefill_gates_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T, int64_t Tp,
-                                     const float* __restrict__ ssm_a, const float* __restrict__ dt_bias,
-                                     float* __restrict__ glog, float* __restrict__ beta, int qkv, int hv) {
-    pdl_trigger();
-    pdl_wait();
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= Tp * hv) return;
-    const int h = (int)(i / Tp);
-    const int64_t t = i % Tp;
-    if (t >= T) {
-        glog[i] = 0.0f;
-        beta[i] = 0.0f;
-        return;
+#pragma unroll
+    for (int j = 0; j < kTokBlock; j++) {
+        const int64_t t = tb + j;
+        const uint2 v = t < T ? make_uint2(wmma16::pack_bf16(x[j].x, x[j].y), wmma16::pack_bf16(x[j].z, x[j].w))
+                              : make_uint2(0u, 0u);
+        *reinterpret_cast<uint2*>(dst + t * HD) = v;
     }
-    const float* pr = proj + t * ldp + qkv + hv * HD;
-    const float beta_raw = pr[h], alpha_raw = pr[hv + h];
-    float gl = logf(0.99f);
-    if (ssm_a != nullptr && dt_bias != nullptr) {
-        const float x = alpha_raw + dt_bias[h];
-        gl = ssm_a[h] * (log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f));
-        if (isnan(gl)) gl = logf(0.99f);
-        gl = fminf(gl, 0.0f);
-    }
-    glog[i] = fmaxf(gl, kLogDecayMin);
-    float bt;
-    if (beta_raw >= 0.0f) {
-        bt = 1.0f / (1.0f + expf(-beta_raw));
-    } else {
-        const float z = expf(beta_raw);
-        bt = z / (1.0f + z);
-    }
-    beta[i] = bt;
-}
-
-// Conv window after the prompt: slot (p0 + i) mod 4 holds the raw projection of
-// token i for the last min(T, 4) tokens; conv_pos advances by T.  Runs after
-// the prep kernel, which read the window as it was.  One block: every thread
-// reads conv_pos before the barrier, thread 0 advances it after.
-__global__ void __launch_bounds__(1024) prefill_window_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T,
-                                                              float* __restrict__ conv_buf,
-                                                              int32_t* __restrict__ conv_pos, int qkv) {
-    pdl_trigger();
-    pdl_wait();
-    const int p0 = *conv_pos;
-    for (int ch = threadIdx.x; ch < qkv; ch += blockDim.x)
-        for (int64_t i = (T > 4 ? T - 4 : 0); i < T; i++)
-            conv_buf[(int64_t)((p0 + (int)i) & 3) * qkv + ch] = proj[i * ldp + ch];
-    __syncthreads();
-    if (threadIdx.x == 0) *conv_pos = p0 + (int32_t)T;
 }
 
 // -------------------------------------------------------- K1: chunk_local
@@ -285,9 +315,12 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
                                                           const float* __restrict__ beta, bf16* __restrict__ wp,
                                                           bf16* __restrict__ up, bf16* __restrict__ ek,
                                                           float* __restrict__ gcum, float* __restrict__ gchunk,
-                                                          int64_t Tp, int hk, int hv, int head_map) {
+                                                          int64_t Tp, int hk, int hv, int head_map,
+                                                          int32_t* __restrict__ conv_pos, int64_t T) {
     pdl_trigger();
     pdl_wait();
+    // The prep kernel has read conv_pos and written the new window: advance it.
+    if (conv_pos != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *conv_pos += (int32_t)T;
     extern __shared__ uint8_t smem_raw[];
     LocalSmem& sm = *reinterpret_cast<LocalSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     const int c = blockIdx.x, h = blockIdx.y;
@@ -785,7 +818,7 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
                 if (head_norm != nullptr) nv = __fmul_rn(nv, sm.hn[v + e]);
                 float zv = e ? zz.y : zz.x;
                 zv = fminf(fmaxf(zv, -88.0f), 88.0f);
-                r2[e] = __fmul_rn(nv, __fdividef(zv, 1.0f + __expf(-zv)));
+                r2[e] = __fmul_rn(nv, silu_fast(zv));
             }
             *reinterpret_cast<__half2*>(gout + v) = __floats2half2_rn(r2[0], r2[1]);
         }
@@ -866,20 +899,12 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     // ---- conv1d + SiLU + L2 norm, gates, window hand-off
     if ((st = phase_mark(1, s))) return st;
     {
-        const int64_t warps = (D.Tp / kTokBlock) * (D.qkv / HD);
+        const int64_t warps = (D.Tp / kTokBlock) * (D.qkv / HD + 1);
         st = launch_pdl("prefill_prep_kernel", prefill_prep_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0,
                         s, W.proj, D.ldp, T, D.Tp, conv ? conv_buf : nullptr, conv_pos,
-                        conv ? L->conv1d_w : nullptr, W.qn, W.kn, W.vb, D.qkv, D.hk);
+                        conv ? L->conv1d_w : nullptr, W.qn, W.kn, W.vb, L->ssm_a, L->dt_bias, W.glog, W.beta, D.qkv,
+                        D.hk, D.hv);
         if (st) return st;
-        const int64_t n = D.Tp * D.hv;
-        st = launch_pdl("prefill_gates_kernel", prefill_gates_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
-                        s, W.proj, D.ldp, T, D.Tp, L->ssm_a, L->dt_bias, W.glog, W.beta, D.qkv, D.hv);
-        if (st) return st;
-        if (conv) {
-            st = launch_pdl("prefill_window_kernel", prefill_window_kernel, dim3(1), dim3(1024), 0, s, W.proj, D.ldp,
-                            T, conv_buf, conv_pos, D.qkv);
-            if (st) return st;
-        }
     }
 
     // ---- chunked recurrence
@@ -889,7 +914,7 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
         if ((st = set_smem(chunk_local_kernel, sm1))) return st;
         st = launch_pdl("chunk_local_kernel", chunk_local_kernel, dim3((unsigned)D.nc, (unsigned)D.hv), dim3(256),
                         sm1, s, W.kn, W.vb, W.glog, W.beta, W.wp, W.up, W.ek, W.gcum, W.gchunk, D.Tp, D.hk, D.hv,
-                        L->head_map);
+                        L->head_map, conv ? conv_pos : nullptr, T);
         if (st) return st;
         const size_t sm2 = sizeof(ScanSmem) + 128;
         if ((st = set_smem(chunk_scan_kernel, sm2))) return st;
