@@ -78,6 +78,7 @@ struct TcLayout {
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM budget");
     static_assert(BN % 64 == 0 && BN <= 256, "BN");
+    static_assert(B8_OFF % 1024 == 0 && B8_BYTES % 1024 == 0, "64B-swizzled raw tiles start on swizzle atoms");
     static_assert(SA * MT * A_BYTES >= 8u * 32u * 36u * 4u, "epilogue staging lives in the activation ring");
 };
 
@@ -318,11 +319,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int s8 = t % S8, s16 = t % S16;
                 ok = __all_sync(0xffffffffu, mbar_wait(b8_full(s8), (t / S8) & 1, err));
                 if (!ok) break;
-                // raw int8 chunks of this thread -> registers; the slot is released at once
+                // raw int8 chunks of this thread -> registers; the slot is released at once.
+                // The tile arrives 64B-swizzled: 16-byte chunk u of row rr sits at
+                // u ^ ((rr >> 1) & 3), so the 8 lanes of each shared-memory phase
+                // (rows rr..rr+7, or 4 rows x 2 chunks) hit 8 different bank groups.
                 const uint4* src = reinterpret_cast<const uint4*>(smem + L::B8_OFF + s8 * L::B8_BYTES + rr * BK);
                 uint4 raw[CPT];
 #pragma unroll
-                for (int cc = 0; cc < CPT; cc++) raw[cc] = src[c0 + cc];
+                for (int cc = 0; cc < CPT; cc++) raw[cc] = src[(c0 + cc) ^ ((rr >> 1) & 3)];
                 // The next write to this slot is a TMA (async proxy): the generic
                 // reads above must be ordered before it by a proxy fence, or the
                 // refill can overtake a late read (one weight row goes stale).
@@ -585,7 +589,7 @@ int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void
     }
     if (st) return st;
     st = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, qs, (uint64_t)k, (uint64_t)n, (uint64_t)k, BK, BN,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
+                     CU_TENSOR_MAP_SWIZZLE_64B);
     if (st) return st;
     auto kern = q8_0_gemm_tc_kernel<BN, MT, SA, S16, S8, BF16, SPLIT>;
     GDN_CUDA(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM));

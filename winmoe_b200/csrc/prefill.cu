@@ -305,12 +305,11 @@ struct LocalSmem {
     float L[CH][CH + 1];  // strictly lower part: b_i exp(G_i - G_j) k_i . k_j
     float T[CH][CH + 1];  // (I + L)^-1, unit lower triangular
     float M[3][16][17];   // block products of the inversion stages
-    bf16 th[2][CH][LDC];  // T diag(b gam) and T diag(b): high bf16 parts
-    bf16 tl[2][CH][LDC];  // ... and the low parts (x - hi)
     float G[CH], beta[CH];
+    float sc[2][CH];      // column scales of T: b_j gam_j (for W') and b_j (for U')
 };
 
-__global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict__ kn, const bf16* __restrict__ vb,
+__global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restrict__ kn, const bf16* __restrict__ vb,
                                                           const float* __restrict__ glog,
                                                           const float* __restrict__ beta, bf16* __restrict__ wp,
                                                           bf16* __restrict__ up, bf16* __restrict__ ek,
@@ -391,18 +390,26 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
     for (int e = tid; e < CH * (CH + 1); e += 256) (&sm.T[0][0])[e] = 0.0f;
     __syncthreads();
     if (tid < CH) {
+        // column jc of the block's inverse: col[i] = -sum_{kk<i} L_i,kk col[kk], the
+        // sums accumulated column-wise (each step's FMAs independent of each
+        // other; the same terms in the same order as a row-wise dot product)
         const int o = (tid >> 4) * 16, jc = tid & 15;
         float col[16];
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            float acc = 0.0f;
+        for (int i = 0; i < 16; i++) col[i] = i == jc ? 1.0f : 0.0f;
 #pragma unroll
-            for (int kk = 0; kk < 16; kk++)
-                if (kk >= jc && kk < i) acc = fmaf(sm.L[o + i][o + kk], col[kk], acc);
-            col[i] = i < jc ? 0.0f : (i == jc ? 1.0f : -acc);
+        for (int kk = 0; kk < 15; kk++) {
+            if (kk < jc) continue;
+            const float ck = col[kk];
+#pragma unroll
+            for (int i = kk + 1; i < 16; i++) col[i] = fmaf(-sm.L[o + i][o + kk], ck, col[i]);
         }
 #pragma unroll
         for (int i = 0; i < 16; i++) sm.T[o + i][o + jc] = col[i];
+    } else if (tid < 2 * CH) {
+        const int j = tid - CH;
+        sm.sc[0][j] = sm.beta[j] * __expf(sm.G[j]);
+        sm.sc[1][j] = sm.beta[j];
     }
     __syncthreads();
     for (int d = 1; d < 4; d++) {
@@ -430,20 +437,9 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
     }
 
     // ---- W' = (T diag(b gam)) K and U' = (T diag(b)) V on the tensor cores:
-    // K and V are exact bf16, the scaled T enters as hi + lo bf16 (16 bits).
-    for (int e = tid; e < CH * CH; e += 256) {
-        const int i = e >> 6, jc = e & 63;
-        const float t = sm.T[i][jc];
-        const float sc[2] = {sm.beta[jc] * __expf(sm.G[jc]), sm.beta[jc]};
-#pragma unroll
-        for (int m = 0; m < 2; m++) {
-            const float x = t * sc[m];
-            const bf16 hi = __float2bfloat16_rn(x);
-            sm.th[m][i][jc] = hi;
-            sm.tl[m][i][jc] = __float2bfloat16_rn(x - __bfloat162float(hi));
-        }
-    }
-    __syncthreads();
+    // K and V are exact bf16; the scaled T enters as hi + lo bf16 (16 bits), its
+    // A fragments built in registers straight from the fp32 T (m16n8k16 layout:
+    // register i holds row gq + 8 (i & 1), columns 2 qq + 8 (i >> 1) + {0, 1}).
     {
         const int gq = lane >> 2, qq = lane & 3;
         const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
@@ -454,8 +450,15 @@ __global__ void __launch_bounds__(256) chunk_local_kernel(const bf16* __restrict
 #pragma unroll
             for (int kk = 0; kk < CH / 16; kk++) {
                 uint32_t ah[4], al[4];
-                wmma16::load_a(ah, &sm.th[m][0][0], LDC, r0, 16 * kk);
-                wmma16::load_a(al, &sm.tl[m][0][0], LDC, r0, 16 * kk);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int row = r0 + gq + 8 * (i & 1), col = 16 * kk + 2 * qq + 8 * (i >> 1);
+                    const float x0 = sm.T[row][col] * sm.sc[m][col];
+                    const float x1 = sm.T[row][col + 1] * sm.sc[m][col + 1];
+                    const bf16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+                    ah[i] = wmma16::pack_bf16(__bfloat162float(h0), __bfloat162float(h1));
+                    al[i] = wmma16::pack_bf16(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+                }
 #pragma unroll
                 for (int np2 = 0; np2 < 4; np2++) {
                     uint32_t b[4];
