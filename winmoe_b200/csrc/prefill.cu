@@ -506,7 +506,8 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
 // key rows 32w..32w+31).  Per chunk: S -> bf16 (smem, and HBM as the chunk's
 // start state), D = U' - W' S (warp w: token rows 16w..16w+15), then
 // S = gam_63 S + (e K)^T D.  The next chunk's W', e*K and U' stream in with
-// cp.async while this one is computed.
+// cp.async while this one is computed; the stores of the start state and the
+// deltas are issued behind this chunk's MMAs, off the chain of dependent steps.
 constexpr int kMaxChunksInSmem = 2048;  // per-chunk decays staged in smem (T up to 128K tokens)
 
 struct ScanSmem {
@@ -584,10 +585,6 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
             wmma16::cp_async_wait<0>();
         }
         __syncthreads();
-        for (int i = tid; i < HD * BV / 8; i += 128) {  // chunk start state -> HBM, 16-byte stores
-            const int r = i / (BV / 8), q = i % (BV / 8);
-            *reinterpret_cast<uint4*>(scc + (int64_t)r * HD + v0 + q * 8) = *reinterpret_cast<const uint4*>(&sm.s[r][q * 8]);
-        }
 
         // ---- D = U' - W' S   (token rows 16w..16w+15, all BV columns)
         float dacc[BV / 8][4] = {};
@@ -603,6 +600,12 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
                 wmma16::mma(dacc[2 * np2 + 1], a, b[2], b[3]);
             }
         }
+        // chunk start state -> HBM (16-byte stores issued behind the MMAs above; sm.s
+        // is next written after this chunk's last barrier)
+        for (int i = tid; i < HD * BV / 8; i += 128) {
+            const int r = i / (BV / 8), q = i % (BV / 8);
+            *reinterpret_cast<uint4*>(scc + (int64_t)r * HD + v0 + q * 8) = *reinterpret_cast<const uint4*>(&sm.s[r][q * 8]);
+        }
         bf16* dlc = dl + ((int64_t)h * Tp + c * CH) * HD + v0;
 #pragma unroll
         for (int n = 0; n < BV / 8; n++)
@@ -616,10 +619,6 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
                     wmma16::pack_bf16(uf.x - dacc[n][2 * hf], uf.y - dacc[n][2 * hf + 1]);
             }
         __syncthreads();
-        for (int i = tid; i < CH * BV / 8; i += 128) {  // deltas -> HBM, 16-byte stores
-            const int r = i / (BV / 8), q = i % (BV / 8);
-            *reinterpret_cast<uint4*>(dlc + (int64_t)r * HD + q * 8) = *reinterpret_cast<const uint4*>(&sm.d[r][q * 8]);
-        }
 
         // ---- S = gam_63 S + (e K)^T D   (key rows 32w..32w+31)
         const float gC = gc_smem ? sm.gc[c] : gchunk[(int64_t)h * nc + c];
@@ -643,6 +642,10 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
                     wmma16::mma(acc[mt][2 * np2 + 1], a, b[2], b[3]);
                 }
             }
+        }
+        for (int i = tid; i < CH * BV / 8; i += 128) {  // deltas -> HBM, behind the MMAs above
+            const int r = i / (BV / 8), q = i % (BV / 8);
+            *reinterpret_cast<uint4*>(dlc + (int64_t)r * HD + q * 8) = *reinterpret_cast<const uint4*>(&sm.d[r][q * 8]);
         }
         __syncthreads();  // sm.s, sm.d and this buffer are rewritten next chunk
     }
