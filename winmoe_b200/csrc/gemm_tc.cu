@@ -667,8 +667,13 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
     const bool two = m > BM;
     int st;
     if (opt.split_precision) {
-        st = two ? run_tc<128, 2, 4, 2, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
-                 : run_tc<128, 1, 6, 3, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
+        // Two M tiles per CTA share each dequantised tile -- unless the weight has
+        // a single column tile (the gate rows) and one-M-tile CTAs still fit one
+        // wave: then twice the CTAs split the same work.
+        const int64_t mt1 = (m + BM - 1) / BM * splits;
+        const bool pair = two && !(n <= 128 && mt1 <= sm_count());
+        st = pair ? run_tc<128, 2, 4, 2, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
+                  : run_tc<128, 1, 6, 3, 4, false, true>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
     } else {
         // One operand: 256-column tiles halve the activation traffic per MMA, as long
         // as the grid still covers at least half of the SMs.
