@@ -681,11 +681,11 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
         const bool wide = two && tiles256 * 2 >= sm_count();
         if (a_bf16) {
             st = !two ? run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
-                 : wide ? run_tc<256, 2, 3, 2, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
+                 : wide ? run_tc<256, 2, 3, 3, 2, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
                         : run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
         } else {
             st = !two ? run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
-                 : wide ? run_tc<256, 2, 3, 2, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
+                 : wide ? run_tc<256, 2, 3, 3, 2, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
                         : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
         }
     }
