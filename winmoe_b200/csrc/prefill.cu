@@ -38,6 +38,7 @@
 #include "quant.cuh"
 #include "decode.cuh"
 #include "prefill.cuh"
+#include "ptx_sm100.cuh"
 #include "warp_mma.cuh"
 
 namespace gdn {
@@ -94,7 +95,8 @@ struct PWork {
     bf16* vb;         // [Hv][Tp][128] conv'd, SiLU'd
     float *glog, *beta, *gcum;  // [Hv][Tp]
     float* gchunk;    // [Hv][nc] gam_63 of every chunk
-    bf16 *wp, *up, *ek;  // [Hv][Tp][128] W', U', e*K
+    bf16 *wp, *ek;    // [Hv][Tp][LDH] W', e*K, rows padded as the scan's shared-memory tiles
+    bf16* up;         // [Hv][nc][128 / BV][CH][LDV] U', one padded tile per chunk and slab
     bf16* sc;         // [Hv][nc][128][128] state at each chunk start
     bf16* dl;         // [Hv][Tp][128] chunk deltas D
     __half* gated;    // [T][inner] out_proj operand
@@ -125,9 +127,9 @@ PWork pcarve(const gdn_dims& d, int64_t T, void* base) {
     w.beta = reinterpret_cast<float*>(take((size_t)D.Tp * D.hv * 4));
     w.gcum = reinterpret_cast<float*>(take((size_t)D.Tp * D.hv * 4));
     w.gchunk = reinterpret_cast<float*>(take((size_t)D.nc * D.hv * 4));
-    w.wp = reinterpret_cast<bf16*>(take(kv * D.hv));
-    w.up = reinterpret_cast<bf16*>(take(kv * D.hv));
-    w.ek = reinterpret_cast<bf16*>(take(kv * D.hv));
+    w.wp = reinterpret_cast<bf16*>(take((size_t)D.Tp * LDH * 2 * D.hv));
+    w.up = reinterpret_cast<bf16*>(take((size_t)D.nc * (HD / BV) * CH * LDV * 2 * D.hv));
+    w.ek = reinterpret_cast<bf16*>(take((size_t)D.Tp * LDH * 2 * D.hv));
     w.sc = reinterpret_cast<bf16*>(take((size_t)D.nc * D.hv * HD * HD * 2));
     w.dl = reinterpret_cast<bf16*>(take(kv * D.hv));
     w.gated = reinterpret_cast<__half*>(take((size_t)T * D.inner * 2));
@@ -469,13 +471,21 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
                     wmma16::mma(acc[2 * np2 + 1], al, b[2], b[3]);
                 }
             }
-            bf16* dst = (m == 0 ? wp : up) + ((int64_t)h * Tp + t0) * HD;
+            // W' rows at the scan's padded pitch; U' as one [CH][LDV] tile per BV-column slab
 #pragma unroll
             for (int n = 0; n < 8; n++) {
                 const int cl = n0 + 8 * n + 2 * qq;
-                *reinterpret_cast<uint32_t*>(dst + (int64_t)(r0 + gq) * HD + cl) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
-                *reinterpret_cast<uint32_t*>(dst + (int64_t)(r0 + gq + 8) * HD + cl) =
-                    wmma16::pack_bf16(acc[n][2], acc[n][3]);
+                bf16* d0;
+                int64_t ld;
+                if (m == 0) {
+                    d0 = wp + ((int64_t)h * Tp + t0) * LDH + cl;
+                    ld = LDH;
+                } else {
+                    d0 = up + (((int64_t)h * (Tp / CH) + c) * (HD / BV) + cl / BV) * (CH * LDV) + cl % BV;
+                    ld = LDV;
+                }
+                *reinterpret_cast<uint32_t*>(d0 + (int64_t)(r0 + gq) * ld) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
+                *reinterpret_cast<uint32_t*>(d0 + (int64_t)(r0 + gq + 8) * ld) = wmma16::pack_bf16(acc[n][2], acc[n][3]);
             }
         }
     }
@@ -493,7 +503,7 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
             const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw[w4]));
             ow[w4] = wmma16::pack_bf16(ei * f.x, ei * f.y);
         }
-        *reinterpret_cast<uint4*>(ek + ((int64_t)h * Tp + t0 + i) * HD + c8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        *reinterpret_cast<uint4*>(ek + ((int64_t)h * Tp + t0 + i) * LDH + c8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
     }
     if (tid < CH) gcum[(int64_t)h * Tp + t0 + tid] = sm.G[tid];
     if (tid == 0) gchunk[(int64_t)h * (Tp / CH) + c] = expf(G63);
@@ -505,9 +515,10 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
 // The state slab S[:, BV columns] lives in fp32 mma accumulators (warp w owns
 // key rows 32w..32w+31).  Per chunk: S -> bf16 (smem, and HBM as the chunk's
 // start state), D = U' - W' S (warp w: token rows 16w..16w+15), then
-// S = gam_63 S + (e K)^T D.  The next chunk's W', e*K and U' stream in with
-// cp.async while this one is computed; the stores of the start state and the
-// deltas are issued behind this chunk's MMAs, off the chain of dependent steps.
+// S = gam_63 S + (e K)^T D.  The next chunk's W', e*K and U' stream in (three
+// bulk copies, one mbarrier per buffer) while this one is computed; the stores
+// of the start state and the deltas are issued behind this chunk's MMAs, off
+// the chain of dependent steps.
 constexpr int kMaxChunksInSmem = 2048;  // per-chunk decays staged in smem (T up to 128K tokens)
 
 struct ScanSmem {
@@ -517,13 +528,15 @@ struct ScanSmem {
     bf16 s[HD][LDV];
     bf16 d[CH][LDV];
     float gc[kMaxChunksInSmem];
+    uint64_t full[2];  // one mbarrier per buffer: the chunk's three bulk copies landed
 };
+constexpr uint32_t kScanWBytes = CH * LDH * 2, kScanUBytes = CH * LDV * 2;
 
 __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict__ wp, const bf16* __restrict__ up,
                                                          const bf16* __restrict__ ek,
                                                          const float* __restrict__ gchunk, float* __restrict__ S,
                                                          bf16* __restrict__ sc, bf16* __restrict__ dl, int64_t Tp,
-                                                         int64_t nc) {
+                                                         int64_t nc, uint32_t* __restrict__ err) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ uint8_t smem_raw[];
@@ -545,23 +558,27 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
                 acc[mt][n][e] =
                     Sh[(int64_t)(32 * warp + 16 * mt + gq + ((e >> 1) << 3)) * HD + v0 + 8 * n + 2 * qq + (e & 1)];
 
+    // The chunk's W', e*K and U' slab are stored in global memory exactly as the
+    // padded shared-memory tiles: one thread brings them with three bulk copies.
     auto prefetch = [&](int64_t c, int buf) {
-        const int64_t base = ((int64_t)h * Tp + c * CH) * HD;
-        for (int i = tid; i < CH * HD / 8; i += 128) {
-            const int r = i / (HD / 8), q = i % (HD / 8);
-            wmma16::cp_async16(&sm.w[buf][r][q * 8], wp + base + r * HD + q * 8);
-            wmma16::cp_async16(&sm.e[buf][r][q * 8], ek + base + r * HD + q * 8);
-        }
-        for (int i = tid; i < CH * BV / 8; i += 128) {
-            const int r = i / (BV / 8), q = i % (BV / 8);
-            wmma16::cp_async16(&sm.u[buf][r][q * 8], up + base + r * HD + v0 + q * 8);
-        }
-        wmma16::cp_async_commit();
+        const uint32_t bar = sm100::smem_u32(&sm.full[buf]);
+        const int64_t base = ((int64_t)h * Tp + c * CH) * LDH;
+        sm100::mbar_arrive_expect_tx(bar, 2 * kScanWBytes + kScanUBytes);
+        sm100::bulk_load(sm100::smem_u32(&sm.w[buf][0][0]), wp + base, kScanWBytes, bar);
+        sm100::bulk_load(sm100::smem_u32(&sm.e[buf][0][0]), ek + base, kScanWBytes, bar);
+        sm100::bulk_load(sm100::smem_u32(&sm.u[buf][0][0]), up + ((h * nc + c) * (HD / BV) + slab) * (CH * LDV),
+                         kScanUBytes, bar);
     };
-    prefetch(0, 0);
+    if (tid == 0) {
+        sm100::mbar_init(sm100::smem_u32(&sm.full[0]), 1);
+        sm100::mbar_init(sm100::smem_u32(&sm.full[1]), 1);
+        sm100::fence_barrier_init();
+        prefetch(0, 0);
+    }
     const bool gc_smem = nc <= kMaxChunksInSmem;
     if (gc_smem)
         for (int64_t i = tid; i < nc; i += 128) sm.gc[i] = gchunk[(int64_t)h * nc + i];
+    __syncthreads();  // barriers initialised, decays staged
 
     for (int64_t c = 0; c < nc; c++) {
         const int buf = (int)(c & 1);
@@ -578,13 +595,13 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
                     *reinterpret_cast<uint32_t*>(&sm.s[r][cl]) =
                         wmma16::pack_bf16(acc[mt][n][2 * hf], acc[mt][n][2 * hf + 1]);
                 }
-        if (c + 1 < nc) {
-            prefetch(c + 1, buf ^ 1);
-            wmma16::cp_async_wait<1>();
-        } else {
-            wmma16::cp_async_wait<0>();
+        // buf ^ 1 was last read in the previous chunk, before its closing barrier
+        if (tid == 0 && c + 1 < nc) prefetch(c + 1, buf ^ 1);
+        const bool landed = sm100::mbar_wait(sm100::smem_u32(&sm.full[buf]), (uint32_t)((c >> 1) & 1), err);
+        if (!__syncthreads_and(landed)) {  // timed out (error word set): stop, let the copies drain
+            if (c + 1 < nc) sm100::mbar_wait(sm100::smem_u32(&sm.full[buf ^ 1]), (uint32_t)(((c + 1) >> 1) & 1), err);
+            return;
         }
-        __syncthreads();
 
         // ---- D = U' - W' S   (token rows 16w..16w+15, all BV columns)
         float dacc[BV / 8][4] = {};
@@ -647,7 +664,10 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
             const int r = i / (BV / 8), q = i % (BV / 8);
             *reinterpret_cast<uint4*>(dlc + (int64_t)r * HD + q * 8) = *reinterpret_cast<const uint4*>(&sm.d[r][q * 8]);
         }
-        __syncthreads();  // sm.s, sm.d and this buffer are rewritten next chunk
+        // sm.s, sm.d and this buffer are rewritten next chunk, the buffer by a bulk
+        // copy (async proxy): order this thread's reads of it before that
+        sm100::fence_proxy_async_smem();
+        __syncthreads();
     }
 #pragma unroll
     for (int mt = 0; mt < 2; mt++)
@@ -925,7 +945,7 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
         const size_t sm2 = sizeof(ScanSmem) + 128;
         if ((st = set_smem(chunk_scan_kernel, sm2))) return st;
         st = launch_pdl("chunk_scan_kernel", chunk_scan_kernel, dim3(HD / BV, (unsigned)D.hv), dim3(128), sm2, s,
-                        W.wp, W.up, W.ek, W.gchunk, S, W.sc, W.dl, D.Tp, D.nc);
+                        W.wp, W.up, W.ek, W.gchunk, S, W.sc, W.dl, D.Tp, D.nc, device_error_word());
         if (st) return st;
         const size_t sm3 = sizeof(OutSmem) + 128;
         if ((st = set_smem(chunk_out_kernel, sm3))) return st;
