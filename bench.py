@@ -247,6 +247,95 @@ def run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, with_cpu):
     return res
 
 
+GQA_DIMS = {"hidden": 2048, "q_gate": 2 * 16 * 256, "kv": 2 * 256, "attn": 16 * 256}  # 35B-class full-attention layer
+
+
+def run_gqa(dev, hbm_peak, peak_src, with_cpu):
+    """SURVEY (f)3: a full-attention layer's Q8_0 projections per token (Q+gate, K, V, then O),
+    through the reference's own offload calls (host buffers in and out, synchronous) and,
+    device-resident, as the same GEMVs on the library's stream."""
+    import ctypes as C
+    import torch
+    from winmoe_b200 import layer as L, synth
+    from winmoe_b200._lib import lib
+    D = GQA_DIMS
+    H, QG, KV, A = D["hidden"], D["q_gate"], D["kv"], D["attn"]
+    ws = [synth.q8_0_blocks(n, k, seed=60 + i) for i, (n, k) in enumerate([(QG, H), (KV, H), (KV, H), (H, A)])]
+    h = lib()
+    own_init = not h.gpu_is_initialized()
+    if own_init and h.gpu_init() != 0:
+        raise RuntimeError("gpu_init failed")
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    if h.gpu_upload_gqa_weights(0, vp(ws[0]), H, QG, vp(ws[1]), H, KV, vp(ws[2]), H, KV, vp(ws[3]), A, H) != 0:
+        raise RuntimeError("gpu_upload_gqa_weights failed")
+    n_tok = 64
+    xs = synth.hidden_states(n_tok, H, seed=70)
+    at = synth.hidden_states(n_tok, A, seed=71)
+    qg, k, v, o = (np.zeros(n, np.float32) for n in (QG, KV, KV, H))
+
+    def token(i):
+        if h.gpu_gqa_projections(0, vp(xs[i]), H, vp(qg), QG, vp(k), KV, vp(v), KV) != 0:
+            raise RuntimeError("gpu_gqa_projections failed")
+        if h.gpu_gqa_output(0, vp(at[i]), A, vp(o), H) != 0:
+            raise RuntimeError("gpu_gqa_output failed")
+    for i in range(3):
+        token(i)
+    t0 = time.perf_counter()
+    for i in range(n_tok):
+        token(i)
+    e2e_us = (time.perf_counter() - t0) / n_tok * 1e6
+    # device-resident: the library's two GEMVs of a token (Q+gate|K|V as one projection, as
+    # gpu_upload_gqa_weights stores them, then O), queued behind a GPU sleep so that the
+    # events time the kernels and not the host's launches
+    planes = [L.q8_0_planes(np.concatenate(ws[:3]), QG + 2 * KV, H, dev), L.q8_0_planes(ws[3], H, A, dev)]
+    xd = torch.from_numpy(xs).to(dev)
+    ad = torch.from_numpy(at).to(dev)
+    yq = torch.empty((1, QG + 2 * KV), dtype=torch.float32, device=dev)
+    yo = torch.empty((1, H), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def dev_token(i):
+        L.gemm_q8_0(planes[0][0], planes[0][1], xd[i:i + 1], out=yq, stream=stream)
+        L.gemm_q8_0(planes[1][0], planes[1][1], ad[i:i + 1], out=yo, stream=stream)
+    for i in range(3):
+        dev_token(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(20_000_000)  # ~10 ms of GPU time while the host queues 128 launches
+    e0.record(stream)
+    for i in range(n_tok):
+        dev_token(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dev_us = e0.elapsed_time(e1) / n_tok * 1e3
+    nb = sum(w.nbytes for w in ws) + (3 * H + A + QG + 2 * KV + H) * 4
+    if own_init:
+        h.gpu_shutdown()
+    res = {"workload": "GQA projections per token (35B-class full-attention layer: Q+gate 2048->8192, K and V "
+                       "2048->512, O 4096->2048, Q8_0, fp32 activations)",
+           "value": 1e6 / e2e_us, "unit": "tok/s", "us_per_token": e2e_us, "tokens": n_tok,
+           "path": "gpu_gqa_projections + gpu_gqa_output (host buffers, synchronous, as the engine calls them)",
+           "device_us_per_token": dev_us,
+           "roofline": {"bound": "hbm", "kernel": "q8_0_gemv_kernel x 2", "achieved": nb / (dev_us / 1e6) / 1e9,
+                        "peak": hbm_peak, "unit": "GB/s", "frac": nb / (dev_us / 1e6) / 1e9 / hbm_peak,
+                        "peak_source": peak_src, "algorithmic_bytes_per_token": nb}}
+    if with_cpu:
+        from oracle import oracle as O
+        orc = O.ref() if O.ref_available() else O.port()
+        n_cpu = 16
+        t0 = time.perf_counter()
+        for i in range(n_cpu):
+            for w, (n, kk), x in zip(ws, [(QG, H), (KV, H), (KV, H), (H, A)], (xs[i], xs[i], xs[i], at[i])):
+                orc.quant_matvec(w, x, n, kk, 8, 0)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": n_cpu / dt, "unit": "tok/s",
+                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                               "kind": "reference" if O.ref_available() else "port",
+                               "sample": f"{n_cpu} tokens through the reference's quant_matvec (type 8, unmodified "
+                                         "Q8_K dispatch) for the four projections"}
+    return res
+
+
 def q4k_call_bytes(cfg, B):
     """Config 4: Q4_K bytes of the four projections plus fp32 activations in and out."""
     w = (cfg.in_proj_rows * cfg.hidden + cfg.hidden * cfg.inner) // 256 * 144
@@ -584,6 +673,7 @@ def run_ours(args):
     if world == 1 and not args.no_extra_legs:
         line["decode_b1"] = run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, not args.no_cpu_baseline)
         line["q4k_sweep"] = run_q4k_sweep(cfg, dev, hbm_peak, peak_src, not args.no_cpu_baseline)
+        line["gqa"] = run_gqa(dev, hbm_peak, peak_src, not args.no_cpu_baseline)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, kind = cpu_reference_run(cfg, tensors, 64, 4, 0)
         cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))

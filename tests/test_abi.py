@@ -91,5 +91,9 @@ def test_legacy_api_before_init():
     assert "gpu_init" in _lib.last_error()
     assert h.gpu_wait_qkv_gate(0) == -1
     assert h.gpu_upload_deltanet_weights(0, None, 1, 1, None, 1, 1, None, 1, 1) == -1
+    assert h.gpu_upload_gqa_weights(0, None, 1, 1, None, 1, 1, None, 1, 1, None, 1, 1) == -1
+    assert h.gpu_gqa_projections(0, C.cast(x, C.c_void_p), 8, C.cast(x, C.c_void_p), 8, C.cast(x, C.c_void_p), 8,
+                                 C.cast(x, C.c_void_p), 8) == -1
+    assert h.gpu_gqa_output(0, C.cast(x, C.c_void_p), 8, C.cast(x, C.c_void_p), 8) == -1
     assert not h.gpu_get_qkv_out(5)
     assert h.gpu_vram_used_mb() == 0.0

@@ -183,6 +183,38 @@ def test_legacy_offload_api(t35):
     assert h.gpu_is_initialized() == 0
 
 
+def test_legacy_gqa_offload():
+    """gpu_upload_gqa_weights / gpu_gqa_projections / gpu_gqa_output, as the engine calls them
+    for its full-attention layers (35B-class: 16 query heads of 256 with gates, 2 KV heads)."""
+    import ctypes as C
+    from winmoe_b200._lib import lib
+    H, q_gate, kv, attn = 2048, 2 * 16 * 256, 2 * 256, 16 * 256
+    wq = synth.q8_0_blocks(q_gate, H, seed=61)
+    wk = synth.q8_0_blocks(kv, H, seed=62)
+    wv = synth.q8_0_blocks(kv, H, seed=63)
+    wo = synth.q8_0_blocks(H, attn, seed=64)
+    h = lib()
+    assert h.gpu_init() == 0
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    assert h.gpu_upload_gqa_weights(3, vp(wq), H, q_gate, vp(wk), H, kv, vp(wv), H, kv, vp(wo), attn, H) == 0
+    P = O.port()
+    for seed in (5, 6):  # twice: the staging buffers are reused
+        x = synth.hidden_states(1, H, seed=seed)[0]
+        qg, k, v = np.zeros(q_gate, np.float32), np.zeros(kv, np.float32), np.zeros(kv, np.float32)
+        assert h.gpu_gqa_projections(3, vp(x), H, vp(qg), q_gate, vp(k), kv, vp(v), kv) == 0
+        assert rel_l2(qg, P.quant_matvec(wq, x, q_gate, H, 8, O.ACT_FP32)) <= 1e-5
+        assert rel_l2(k, P.quant_matvec(wk, x, kv, H, 8, O.ACT_FP32)) <= 1e-5
+        assert rel_l2(v, P.quant_matvec(wv, x, kv, H, 8, O.ACT_FP32)) <= 1e-5
+        a = synth.hidden_states(1, attn, seed=seed + 10)[0]
+        o = np.zeros(H, np.float32)
+        assert h.gpu_gqa_output(3, vp(a), attn, vp(o), H) == 0
+        assert rel_l2(o, P.quant_matvec(wo, a, H, attn, 8, O.ACT_FP32)) <= 1e-5
+    # a layer without GQA weights, or dims other than the uploaded ones: -1 with a message
+    assert h.gpu_gqa_output(4, vp(a), attn, vp(o), H) == -1
+    assert h.gpu_gqa_projections(3, vp(x), H, vp(qg), q_gate // 2, vp(k), kv, vp(v), kv) == -1
+    h.gpu_shutdown()
+
+
 @pytest.mark.parametrize("cfg,B", [(GDNConfig(256, 1, 3, 128), 2), (GDNConfig(768, 3, 6, 128), 70)])
 def test_decode_odd_shapes(cfg, B):
     """Odd value-head counts (padded projection rows) and a batch above the tensor-core threshold."""

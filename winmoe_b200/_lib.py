@@ -84,6 +84,9 @@ SIGNATURES = {
     "gpu_upload_deltanet_weights": (_int, [_int, _vp, _int, _int, _vp, _int, _int, _vp, _int, _int]),
     "gpu_deltanet_projections": (_int, [_int, _vp, _int, _vp, _int, _vp, _int]),
     "gpu_ssm_out_projection": (_int, [_int, _vp, _int, _vp, _int]),
+    "gpu_upload_gqa_weights": (_int, [_int, _vp, _int, _int, _vp, _int, _int, _vp, _int, _int, _vp, _int, _int]),
+    "gpu_gqa_projections": (_int, [_int, _vp, _int, _vp, _int, _vp, _int, _vp, _int]),
+    "gpu_gqa_output": (_int, [_int, _vp, _int, _vp, _int]),
     "gpu_launch_qkv_gate": (_int, [_int, _int, _vp, _int, _int, _int]),
     "gpu_wait_qkv_gate": (_int, [_int]),
     "gpu_launch_ssm_out": (_int, [_int, _int, _vp, _int, _int]),

@@ -1,7 +1,7 @@
-// The reference engine's DeltaNet offload API (engine/runtime/gpu_offload.h:
-// 19-53), re-implemented on this library's kernels so that the engine
-// (engine/runtime/winmoe_inference.c:868, 938-942, 1215-1226, 1437-1440) can
-// link against it unchanged.
+// The reference engine's DeltaNet and GQA offload API (engine/runtime/
+// gpu_offload.h:19-67), re-implemented on this library's kernels so that the
+// engine (engine/runtime/winmoe_inference.c:868, 938-942, 956-960, 1215-1226,
+// 1437-1440, 1485-1486, 1624) can link against it unchanged.
 //
 // Kept from the reference (gpu_offload.cu:997-1209): one host thread; module
 // state; weights copied to module-owned device memory at upload; three
@@ -36,6 +36,18 @@ struct Proj {
 struct LayerGPU {
     Proj qkv, gate, out;
     bool loaded = false;
+    // A full-attention (GQA) layer: Q+gate, K and V share their input and are
+    // stored as one [q_gate + k + v][hidden] projection (one GEMV per call); O.
+    Proj wqkv, wo;
+    int q_dim = 0, k_dim = 0, v_dim = 0;
+    bool gqa_loaded = false;
+};
+
+// Staging of the synchronous GQA calls: pinned input, device input, device and
+// pinned outputs (grown on demand).
+struct GqaIO {
+    float *h_in = nullptr, *d_in = nullptr, *h_out = nullptr, *d_out = nullptr;
+    size_t cap_in = 0, cap_out = 0;
 };
 
 struct Slot {
@@ -49,6 +61,7 @@ struct Module {
     bool initialized = false;
     LayerGPU layers[kMaxLayers];
     Slot slots[kSlots];
+    GqaIO gqa;
     cudaStream_t compute{}, h2d{}, d2h{};
     double vram_bytes = 0;
 } g;
@@ -61,14 +74,27 @@ void free_proj(Proj& p) {
     p = Proj();
 }
 
-int upload_proj(Proj& p, const void* host_blocks, int in_dim, int out_dim) {
-    if (in_dim <= 0 || out_dim <= 0 || in_dim % 32 != 0)
+// Uploads the row blocks parts[i] (out_dims[i] rows of in_dim Q8_0 weights
+// each, GGUF bytes) one after the other as a single projection.
+int upload_rows(Proj& p, const void* const* parts, const int* out_dims, int nparts, int in_dim) {
+    int out_dim = 0;
+    for (int i = 0; i < nparts; i++) {
+        if (out_dims[i] <= 0) return fail(GDN_ERR_SHAPE, "upload: out_dim %d", out_dims[i]);
+        out_dim += out_dims[i];
+    }
+    if (in_dim <= 0 || in_dim % 32 != 0)
         return fail(GDN_ERR_SHAPE, "upload: in_dim must be a positive multiple of 32 (got %d x %d)", in_dim, out_dim);
     free_proj(p);
     const size_t nb = (size_t)in_dim / 32 * out_dim;
     void* raw = nullptr;
     GDN_CUDA(cudaMalloc(&raw, nb * 34));
-    cudaError_t e = cudaMemcpy(raw, host_blocks, nb * 34, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaSuccess;
+    size_t off = 0;
+    for (int i = 0; i < nparts && e == cudaSuccess; i++) {
+        const size_t bytes = (size_t)in_dim / 32 * out_dims[i] * 34;
+        e = cudaMemcpy(static_cast<char*>(raw) + off, parts[i], bytes, cudaMemcpyHostToDevice);
+        off += bytes;
+    }
     if (e == cudaSuccess) e = cudaMalloc(&p.qs, nb * 32);
     if (e == cudaSuccess) e = cudaMalloc(&p.d, nb * 2);
     if (e != cudaSuccess) {
@@ -85,6 +111,10 @@ int upload_proj(Proj& p, const void* host_blocks, int in_dim, int out_dim) {
     p.out_dim = out_dim;
     g.vram_bytes += (double)nb * 34;
     return GDN_OK;
+}
+
+int upload_proj(Proj& p, const void* host_blocks, int in_dim, int out_dim) {
+    return upload_rows(p, &host_blocks, &out_dim, 1, in_dim);
 }
 
 // Grows a slot's pinned + device buffer pair to at least `count` floats.
@@ -111,6 +141,44 @@ int check_layer(int layer) {
     if (!g.initialized) return fail(GDN_ERR_STATE, "gpu_init has not been called");
     if (layer < 0 || layer >= kMaxLayers || !g.layers[layer].loaded)
         return fail(GDN_ERR_STATE, "layer %d has no uploaded DeltaNet weights", layer);
+    return GDN_OK;
+}
+
+int check_gqa(int layer) {
+    if (!g.initialized) return fail(GDN_ERR_STATE, "gpu_init has not been called");
+    if (layer < 0 || layer >= kMaxLayers || !g.layers[layer].gqa_loaded)
+        return fail(GDN_ERR_STATE, "layer %d has no uploaded GQA weights", layer);
+    return GDN_OK;
+}
+
+int check_dims(const Proj& p, const char* name, int in_dim, int out_dim) {
+    if (p.in_dim != in_dim || p.out_dim != out_dim)
+        return fail(GDN_ERR_SHAPE, "%s: called with %d -> %d, uploaded as %d -> %d", name, in_dim, out_dim, p.in_dim,
+                    p.out_dim);
+    return GDN_OK;
+}
+
+// x (host, in_dim floats) through projection p on the compute stream; its
+// out_dim results go to the host buffers outs[i] (splits[i] floats each, in
+// order).  Returns after the copies are done (the reference's calls are
+// synchronous).
+int gqa_run(const Proj& p, float* const* outs, const int* splits, int n, const float* x, int in_dim) {
+    GqaIO& io = g.gqa;
+    int st = ensure(&io.h_in, &io.d_in, &io.cap_in, (size_t)in_dim);
+    if (!st) st = ensure(&io.h_out, &io.d_out, &io.cap_out, (size_t)p.out_dim);
+    if (st) return st;
+    memcpy(io.h_in, x, sizeof(float) * in_dim);
+    GDN_CUDA(cudaMemcpyAsync(io.d_in, io.h_in, sizeof(float) * in_dim, cudaMemcpyHostToDevice, g.compute));
+    if ((st = launch_q8_0_gemv(p.qs, p.d, p.out_dim, p.in_dim, io.d_in, GDN_DTYPE_F32, 1, io.d_out, p.out_dim,
+                               g.compute)))
+        return st;
+    GDN_CUDA(cudaMemcpyAsync(io.h_out, io.d_out, sizeof(float) * p.out_dim, cudaMemcpyDeviceToHost, g.compute));
+    GDN_CUDA(cudaStreamSynchronize(g.compute));
+    size_t off = 0;
+    for (int i = 0; i < n; i++) {
+        memcpy(outs[i], io.h_out + off, sizeof(float) * splits[i]);
+        off += (size_t)splits[i];
+    }
     return GDN_OK;
 }
 
@@ -204,7 +272,15 @@ void gpu_shutdown(void) {
         free_proj(L.gate);
         free_proj(L.out);
         L.loaded = false;
+        free_proj(L.wqkv);
+        free_proj(L.wo);
+        L.gqa_loaded = false;
     }
+    if (g.gqa.h_in) cudaFreeHost(g.gqa.h_in);
+    if (g.gqa.h_out) cudaFreeHost(g.gqa.h_out);
+    if (g.gqa.d_in) cudaFree(g.gqa.d_in);
+    if (g.gqa.d_out) cudaFree(g.gqa.d_out);
+    g.gqa = GqaIO();
     for (Slot& s : g.slots) {
         float* hs[5] = {s.h_normed, s.h_qkv, s.h_gate, s.h_gated, s.h_ssm};
         float* ds[5] = {s.d_normed, s.d_qkv, s.d_gate, s.d_gated, s.d_ssm};
@@ -281,6 +357,56 @@ int gpu_ssm_out_projection(int layer, const float* gated, int gated_dim, float* 
     if (gpu_wait_ssm_out(0) != 0) return -1;
     memcpy(output, g.slots[0].h_ssm, sizeof(float) * output_dim);
     return 0;
+}
+
+// rows = in_dim, cols = out_dim, as the engine passes them (winmoe_inference.c:956-960:
+// Q+gate and K/V [H -> out], O [attn -> H]); the reference's q8_matvec_kernel
+// (gpu_offload.cu:870-943) is this library's fp32-activation Q8_0 GEMV.
+int gpu_upload_gqa_weights(int layer, const void* wq_q8, int wq_rows, int wq_cols, const void* wk_q8, int wk_rows,
+                           int wk_cols, const void* wv_q8, int wv_rows, int wv_cols, const void* wo_q8, int wo_rows,
+                           int wo_cols) {
+    if (!g.initialized) return legacy(fail(GDN_ERR_STATE, "gpu_init has not been called"));
+    if (layer < 0 || layer >= kMaxLayers) return legacy(fail(GDN_ERR_ARG, "layer %d out of range", layer));
+    if (!wq_q8 || !wk_q8 || !wv_q8 || !wo_q8) return legacy(fail(GDN_ERR_ARG, "NULL weight pointer"));
+    if (wk_rows != wq_rows || wv_rows != wq_rows)
+        return legacy(fail(GDN_ERR_SHAPE, "Q, K and V must share their input width (%d, %d, %d)", wq_rows, wk_rows,
+                           wv_rows));
+    LayerGPU& L = g.layers[layer];
+    L.gqa_loaded = false;
+    const void* parts[3] = {wq_q8, wk_q8, wv_q8};
+    const int outs[3] = {wq_cols, wk_cols, wv_cols};
+    int st = upload_rows(L.wqkv, parts, outs, 3, wq_rows);
+    if (!st) st = upload_proj(L.wo, wo_q8, wo_rows, wo_cols);
+    if (st) return legacy(st);
+    L.q_dim = wq_cols;
+    L.k_dim = wk_cols;
+    L.v_dim = wv_cols;
+    L.gqa_loaded = true;
+    return 0;
+}
+
+int gpu_gqa_projections(int layer, const float* normed, int hidden_dim, float* q_gate_out, int q_gate_dim,
+                        float* k_out, int k_dim, float* v_out, int v_dim) {
+    int st = check_gqa(layer);
+    if (st) return legacy(st);
+    if (!normed || !q_gate_out || !k_out || !v_out) return legacy(fail(GDN_ERR_ARG, "gpu_gqa_projections: NULL"));
+    const LayerGPU& L = g.layers[layer];
+    if (L.wqkv.in_dim != hidden_dim || L.q_dim != q_gate_dim || L.k_dim != k_dim || L.v_dim != v_dim)
+        return legacy(fail(GDN_ERR_SHAPE, "gpu_gqa_projections: called with %d -> %d / %d / %d, uploaded as %d -> %d / "
+                           "%d / %d", hidden_dim, q_gate_dim, k_dim, v_dim, L.wqkv.in_dim, L.q_dim, L.k_dim, L.v_dim));
+    const int splits[3] = {q_gate_dim, k_dim, v_dim};
+    float* outs[3] = {q_gate_out, k_out, v_out};
+    return legacy(gqa_run(L.wqkv, outs, splits, 3, normed, hidden_dim));
+}
+
+int gpu_gqa_output(int layer, const float* attn_out, int attn_dim, float* output, int hidden_dim) {
+    int st = check_gqa(layer);
+    if (st) return legacy(st);
+    if (!attn_out || !output) return legacy(fail(GDN_ERR_ARG, "gpu_gqa_output: NULL"));
+    const LayerGPU& L = g.layers[layer];
+    if ((st = check_dims(L.wo, "gpu_gqa_output", attn_dim, hidden_dim))) return legacy(st);
+    float* outs[1] = {output};
+    return legacy(gqa_run(L.wo, outs, &hidden_dim, 1, attn_out, attn_dim));
 }
 
 }  // extern "C"
