@@ -103,7 +103,11 @@ __device__ __forceinline__ void stage_x_padded(float* xs, const void* x, int dty
 // chunks l, l+32, ... of the row's int8 plane (coalesced 512 B per warp load)
 // and the fp16 scale of the 32-block each chunk belongs to.  The block sum
 // sum(q*x) is scaled by d once per 16-chunk.  The MB activation rows of block
-// row blockIdx.y share every weight load.
+// row blockIdx.y share every weight load.  Weight loads run one batch (four
+// chunks per lane) ahead: the first batch is issued before the activations are
+// staged, and each next batch -- of this row or of the warp's next row --
+// before the current one is reduced, so HBM latency overlaps the staging, the
+// arithmetic and the row sums.
 template <int MB>
 __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict__ qs,
                                                        const uint16_t* __restrict__ dsc,
@@ -111,6 +115,28 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
                                                        int x_dtype, int64_t m, float* __restrict__ y,
                                                        int64_t ldy, int rows_per_block) {
     pdl_trigger();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int64_t nchunk = k >> 4;
+    const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
+    const int64_t row_end = min(row0 + rows_per_block, n_rows);
+    uint4 qv[4];
+    uint16_t sv[4];
+    auto load = [&](int64_t r, int64_t c0) {  // batch of chunks c0 + 32u of row r
+        const uint4* qrow = reinterpret_cast<const uint4*>(qs + r * k);
+        const uint16_t* drow = dsc + r * (k >> 5);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int64_t c = c0 + 32 * u;
+            if (c < nchunk) {
+                qv[u] = __ldg(qrow + c);
+                sv[u] = __ldg(drow + (c >> 1));
+            }
+        }
+    };
+    int64_t r = row0 + warp, c0 = lane;
+    bool have = r < row_end;
+    if (have) load(r, c0);  // weights never come from an earlier kernel: before the wait
     pdl_wait();
     extern __shared__ float xs[];  // [mb][k * 5 / 4], padded (lane l reads chunk l)
     const int64_t m0 = (int64_t)blockIdx.y * MB;
@@ -118,62 +144,54 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
     const int64_t kp = k + (k >> 2);
     stage_x_padded(xs, x, x_dtype, m0, mb, k);
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nwarps = blockDim.x >> 5;
-    const int64_t nchunk = k >> 4;
-    const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
-    for (int64_t r = row0 + warp; r < row0 + rows_per_block && r < n_rows; r += nwarps) {
-        const uint4* qrow = reinterpret_cast<const uint4*>(qs + r * k);
-        const uint16_t* drow = dsc + r * (k >> 5);
-        float acc[MB];
+    float acc[MB];
 #pragma unroll
-        for (int j = 0; j < MB; j++) acc[j] = 0.0f;
-        for (int64_t c0 = lane; c0 < nchunk; c0 += 4 * 32) {  // four chunks per lane in flight
-            uint4 qv[4];
-            uint16_t sv[4];
+    for (int j = 0; j < MB; j++) acc[j] = 0.0f;
+    while (have) {
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int64_t c = c0 + 32 * u;
-                if (c < nchunk) {
-                    qv[u] = __ldg(qrow + c);
-                    sv[u] = __ldg(drow + (c >> 1));
-                }
-            }
+        for (int u = 0; u < 4; u++) {
+            const int64_t c = c0 + 32 * u;
+            if (c >= nchunk) break;
+            const float s = fp16_bits_to_float(sv[u]);
+            float f[16];
+            i8x4_to_f32(qv[u].x, f);
+            i8x4_to_f32(qv[u].y, f + 4);
+            i8x4_to_f32(qv[u].z, f + 8);
+            i8x4_to_f32(qv[u].w, f + 12);
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int64_t c = c0 + 32 * u;
-                if (c >= nchunk) break;
-                const float s = fp16_bits_to_float(sv[u]);
-                float f[16];
-                i8x4_to_f32(qv[u].x, f);
-                i8x4_to_f32(qv[u].y, f + 4);
-                i8x4_to_f32(qv[u].z, f + 8);
-                i8x4_to_f32(qv[u].w, f + 12);
+            for (int j = 0; j < MB; j++) {
+                if (j < mb) {
+                    const float4* xv = reinterpret_cast<const float4*>(xs + (int64_t)j * kp + c * 20);
+                    float bs = 0.0f;
 #pragma unroll
-                for (int j = 0; j < MB; j++) {
-                    if (j < mb) {
-                        const float4* xv = reinterpret_cast<const float4*>(xs + (int64_t)j * kp + c * 20);
-                        float bs = 0.0f;
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const float4 v = xv[e];
-                            bs = fmaf(f[4 * e + 0], v.x, bs);
-                            bs = fmaf(f[4 * e + 1], v.y, bs);
-                            bs = fmaf(f[4 * e + 2], v.z, bs);
-                            bs = fmaf(f[4 * e + 3], v.w, bs);
-                        }
-                        acc[j] = fmaf(s, bs, acc[j]);
+                    for (int e = 0; e < 4; e++) {
+                        const float4 v = xv[e];
+                        bs = fmaf(f[4 * e + 0], v.x, bs);
+                        bs = fmaf(f[4 * e + 1], v.y, bs);
+                        bs = fmaf(f[4 * e + 2], v.z, bs);
+                        bs = fmaf(f[4 * e + 3], v.w, bs);
                     }
+                    acc[j] = fmaf(s, bs, acc[j]);
                 }
             }
         }
+        const bool row_done = c0 + 4 * 32 >= nchunk;
+        const int64_t nr = row_done ? r + nwarps : r, nc0 = row_done ? (int64_t)lane : c0 + 4 * 32;
+        const bool next = nr < row_end;
+        if (next) load(nr, nc0);
+        if (row_done) {
 #pragma unroll
-        for (int j = 0; j < MB; j++) {
-            if (j < mb) {
-                const float v = warp_sum(acc[j]);
-                if (lane == 0) y[(m0 + j) * ldy + r] = v;
+            for (int j = 0; j < MB; j++) {
+                if (j < mb) {
+                    const float v = warp_sum(acc[j]);
+                    if (lane == 0) y[(m0 + j) * ldy + r] = v;
+                }
+                acc[j] = 0.0f;
             }
         }
+        r = nr;
+        c0 = nc0;
+        have = next;
     }
 }
 
