@@ -420,12 +420,6 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
                                                        int x_dtype, int64_t m, float* __restrict__ y,
                                                        int64_t ldy, int rows_per_block) {
     pdl_trigger();
-    pdl_wait();
-    extern __shared__ float xs[];  // [mb][k]
-    const int64_t m0 = (int64_t)blockIdx.y * MB;
-    const int mb = (int)min((int64_t)MB, m - m0);
-    stage_x(xs, x, x_dtype, m0, mb, k);
-    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nwarps = blockDim.x >> 5;
     const int64_t nsb = k >> 8;
@@ -434,27 +428,40 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
     // (sub-block 2c), high nibbles weights 64c + 32 + 4g + e (sub-block 2c + 1).
     // The warp reads the 128 quant bytes as one line and each quarter-warp reads
     // 128 contiguous bytes of x.  w = (d sc) q - dmin m is summed as
-    // (d sc) sum(q x) - (dmin m) sum(x) per lane.
+    // (d sc) sum(q x) - (dmin m) sum(x) per lane.  Loads run one batch (four
+    // superblocks) ahead: the first before the activations are staged, each next
+    // one -- of this row or the warp's next -- before the current is reduced.
     const int c = lane >> 3, g = lane & 7;
     const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
-    for (int64_t r = row0 + warp; r < row0 + rows_per_block && r < n_rows; r += nwarps) {
+    const int64_t row_end = min(row0 + rows_per_block, n_rows);
+    uint4 hv[4];
+    uint32_t qv[4];
+    auto load = [&](int64_t r, int64_t sb0) {
         const uint8_t* row = blocks + r * nsb * 144;
-        float acc[MB];
 #pragma unroll
-        for (int j = 0; j < MB; j++) acc[j] = 0.0f;
-        for (int64_t sb0 = 0; sb0 < nsb; sb0 += 4) {  // four superblocks per warp in flight
-          uint4 hv[4];
-          uint32_t qv[4];
+        for (int u = 0; u < 4; u++) {
+            if (sb0 + u < nsb) {
+                const uint8_t* blk = row + (sb0 + u) * 144;
+                hv[u] = __ldg(reinterpret_cast<const uint4*>(blk));
+                qv[u] = __ldg(reinterpret_cast<const uint32_t*>(blk + 16 + 32 * c + 4 * g));
+            }
+        }
+    };
+    int64_t r = row0 + warp, sb0 = 0;
+    bool have = r < row_end;
+    if (have) load(r, sb0);  // weights never come from an earlier kernel: before the wait
+    pdl_wait();
+    extern __shared__ float xs[];  // [mb][k]
+    const int64_t m0 = (int64_t)blockIdx.y * MB;
+    const int mb = (int)min((int64_t)MB, m - m0);
+    stage_x(xs, x, x_dtype, m0, mb, k);
+    __syncthreads();
+    float acc[MB];
 #pragma unroll
-          for (int u = 0; u < 4; u++) {
-              if (sb0 + u < nsb) {
-                  const uint8_t* blk = row + (sb0 + u) * 144;
-                  hv[u] = __ldg(reinterpret_cast<const uint4*>(blk));
-                  qv[u] = __ldg(reinterpret_cast<const uint32_t*>(blk + 16 + 32 * c + 4 * g));
-              }
-          }
+    for (int j = 0; j < MB; j++) acc[j] = 0.0f;
+    while (have) {
 #pragma unroll
-          for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < 4; u++) {
             const int64_t sb = sb0 + u;
             if (sb >= nsb) break;
             const uint4 hdr = hv[u];
@@ -483,15 +490,24 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
                     acc[j] += (sl * al - ml * sxl) + (sh * ah - mh * sxh);
                 }
             }
-          }
         }
+        const bool row_done = sb0 + 4 >= nsb;
+        const int64_t nr = row_done ? r + nwarps : r, nsb0 = row_done ? 0 : sb0 + 4;
+        const bool next = nr < row_end;
+        if (next) load(nr, nsb0);
+        if (row_done) {
 #pragma unroll
-        for (int j = 0; j < MB; j++) {
-            if (j < mb) {
-                const float v = warp_sum(acc[j]);
-                if (lane == 0) y[(m0 + j) * ldy + r] = v;
+            for (int j = 0; j < MB; j++) {
+                if (j < mb) {
+                    const float v = warp_sum(acc[j]);
+                    if (lane == 0) y[(m0 + j) * ldy + r] = v;
+                }
+                acc[j] = 0.0f;
             }
         }
+        r = nr;
+        sb0 = nsb0;
+        have = next;
     }
 }
 
