@@ -145,9 +145,12 @@ GDN_API int gdn_quantize_q8_K(const float* x, void* out, int64_t n, void* stream
  */
 GDN_API int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, void* stream);
 
-/* y[m][n] = sum_k x[m][k] * W[n][k], W Q4_K [n_rows][k], fp32 activations
- * and accumulation (q4k_matvec_kernel, engine/runtime/gpu_offload.cu:206-268),
- * dequantised in registers.  x_dtype: F32 or BF16.  k % 256 == 0. */
+/* y[m][n] = sum_k x[m][k] * W[n][k], W Q4_K [n_rows][k], fp32 accumulation
+ * (q4k_matvec_kernel, engine/runtime/gpu_offload.cu:206-268).  x_dtype F32,
+ * BF16 or F16; k % 256 == 0.  fp16 x with m >= 8 runs on the tensor cores
+ * (superblocks by TMA, dequantised in shared memory into hi + lo fp16
+ * operands: the fp32 product of those activations up to summation order);
+ * otherwise a CUDA-core GEMV dequantising in registers. */
 GDN_API int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k,
                   const void* x, int x_dtype, int64_t m, float* y, void* stream);
 

@@ -162,3 +162,26 @@ def test_q8_0_gemm_ref_exact_bit_exact(n, k, m):
     y = L.gemm_q8_0(qs, d, torch.from_numpy(x).to(DEV), ref_exact=True).cpu().numpy()
     for i in range(m):
         np.testing.assert_array_equal(y[i], P.quant_matvec(blocks, x[i], n, k, 8, O.ACT_EXACT))
+
+
+@pytest.mark.parametrize("m,n,k", [(8, 12352, 2048), (32, 12352, 2048), (32, 2048, 4096), (130, 2048, 4096),
+                                   (8, 100, 256), (64, 300, 768)])
+def test_q4_k_gemm_tensor_core_exact(m, n, k):
+    """fp16 x, m >= 8: Q4_K superblocks dequantised into hi + lo fp16 tensor-core
+    operands = the fp64 product of the same activations and the bit-exact fp32
+    weights up to summation order (incl. ragged n, one superblock, split K); two
+    launches bit-identical."""
+    blocks = synth.q4_k_blocks(n, k, seed=900 + n + k)
+    dev = torch.from_numpy(blocks.reshape(-1)).to(DEV)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m + n)).half().to(DEV)
+    y = L.gemm_q4_k(dev, n, k, x)
+    y2 = L.gemm_q4_k(dev, n, k, x)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+    w = torch.from_numpy(O.port().q4_k_dequant(blocks, n * k).reshape(n, k)).double().to(DEV)
+    want = x.double() @ w.T
+    got = y.double()
+    err = ((got - want).norm() / want.norm()).item()
+    assert err <= 1e-5, err
+    rows_err = ((got - want).norm(dim=1) / want.norm(dim=1)).max().item()
+    assert rows_err <= 1e-4, rows_err

@@ -4,6 +4,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "gdn_common.cuh"
@@ -138,6 +139,9 @@ int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols,
     return launch_q4_k_dequant(blocks, out, rows, cols, as_stream(stream));
 }
 
+// Q4_K batches from this many rows (fp16 activations) run on the tensor cores.
+constexpr int64_t kQ4kTcMinRows = 8;
+
 int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
                   void* stream) {
     if (n_rows < 0 || m < 0 || k <= 0 || k % 256 != 0) return fail(GDN_ERR_SHAPE, "q4_k gemm: k must be a positive multiple of 256");
@@ -146,7 +150,28 @@ int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, 
     if (st) return st;
     if (!aligned(blocks, 16)) return fail(GDN_ERR_ARG, "q4_k gemm: blocks must be 16-byte aligned");
     if (n_rows == 0 || m == 0) return GDN_OK;
-    return launch_q4_k_gemv(blocks, n_rows, k, x, x_dtype, m, y, n_rows, as_stream(stream));
+    cudaStream_t s = as_stream(stream);
+    if (x_dtype == GDN_DTYPE_F16 && m >= kQ4kTcMinRows && aligned(x, 16)) {
+        // tensor cores, exact weights: the fp32 product of the fp16 activations up to
+        // summation order.  Grids short of the SMs split K (partials in a stream-ordered
+        // allocation, summed in a fixed order).
+        TcOptions opt;
+        const int64_t ctas = (n_rows + 127) / 128 * ((m + 255) / 256);
+        opt.splits = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count() / std::max<int64_t>(ctas, 1), k / 512));
+        void* ws = nullptr;
+        if (opt.splits > 1) {
+            opt.workspace_bytes = gemm_tc_workspace_bytes(m, n_rows, opt.splits);
+            GDN_CUDA(cudaMallocAsync(&ws, opt.workspace_bytes, s));
+            opt.workspace = ws;
+        }
+        const int st = launch_q4_k_gemm_tc(blocks, n_rows, k, x, m, y, n_rows, opt, s);
+        if (ws != nullptr) {
+            const cudaError_t e = cudaFreeAsync(ws, s);
+            if (!st && e != cudaSuccess) return cuda_status(e, "q4_k gemm workspace");
+        }
+        return st;
+    }
+    return launch_q4_k_gemv(blocks, n_rows, k, x, x_dtype, m, y, n_rows, s);
 }
 
 size_t gdn_decode_workspace_size(const gdn_dims* dims, int64_t batch) {

@@ -33,6 +33,12 @@
 // from HBM runs several k-tiles ahead of the tensor cores.
 // Split-K (grid.z > 1) writes fp32 partials that a second kernel sums in a
 // fixed order, so results do not depend on scheduling.
+//
+// Q4_K weights (Q4K = true) use the same pipeline: the raw ring holds whole
+// 144-byte superblock rows (256 weights, four k-tiles), the dequant warps read
+// a superblock row once, release the slot and expand each 64-weight quarter
+// with the reference's formula w = (d sc) q - (dmin m) (gpu_offload.cu:237-250,
+// each operation rounded once) into the operand tiles.
 #include <cuda.h>
 #include <algorithm>
 #include <string.h>
@@ -59,11 +65,14 @@ constexpr int kWin = 8;  // k-tiles per scale window (16 fp16 scales = 32 bytes 
 //   A   [SA]  MT activation tiles (128 x 64, 128B-swizzled), freed by the MMA
 //   B16 [S16] the dequantised weight tile(s) (hi, and lo when split), freed by the MMA
 //   B8  [S8]  the raw int8 weight tile, freed as soon as the dequant warps have read it
-template <int BN, int MT, int SA, int S16, int S8, bool SPLIT>
+constexpr int kQ4kBytes = 144;   // Q4_K superblock: fp16 d, fp16 dmin, 12 scale bytes, 128 quant bytes
+constexpr int kQ4kTiles = 4;     // k-tiles per superblock (256 / BK)
+
+template <int BN, int MT, int SA, int S16, int S8, bool SPLIT, bool Q4K = false>
 struct TcLayout {
     static constexpr uint32_t A_BYTES = BM * BK * 2;  // one 128-row activation tile
     static constexpr uint32_t B16_BYTES = BN * BK * 2;
-    static constexpr uint32_t B8_BYTES = BN * BK;
+    static constexpr uint32_t B8_BYTES = Q4K ? BN * kQ4kBytes : BN * BK;  // raw slot: a k-tile / a superblock
     static constexpr int NB = SPLIT ? 2 : 1;
     static constexpr uint32_t A_OFF = 0;
     static constexpr uint32_t B16_OFF = A_OFF + SA * MT * A_BYTES;
@@ -78,7 +87,8 @@ struct TcLayout {
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM budget");
     static_assert(BN % 64 == 0 && BN <= 256, "BN");
-    static_assert(B8_OFF % 1024 == 0 && B8_BYTES % 1024 == 0, "64B-swizzled raw tiles start on swizzle atoms");
+    static_assert(Q4K || (B8_OFF % 1024 == 0 && B8_BYTES % 1024 == 0), "64B-swizzled raw tiles start on swizzle atoms");
+    static_assert(B8_OFF % 128 == 0 && B8_BYTES % 128 == 0, "TMA destinations");
     static_assert(SA * MT * A_BYTES >= 8u * 32u * 36u * 4u, "epilogue staging lives in the activation ring");
 };
 
@@ -142,6 +152,45 @@ __device__ __forceinline__ void dequant16(const uint4 q, uint16_t dbits, uint32_
     }
 }
 
+// 16 Q4_K weights from the nibbles of 16 quant bytes (low nibbles, or high when
+// `high`): w = sl * q - ml with sl = d sc and ml = dmin m of their sub-block,
+// each operation rounded once as in the reference's dequantisation; then the
+// operand type (fp16 hi, and lo = RN(2^11 (w - hi)) when split).
+template <bool SPLIT>
+__device__ __forceinline__ void dequant16_q4k(const uint4 q, bool high, float sl, float ml, uint32_t (&hi)[8],
+                                              uint32_t (&lo)[8]) {
+    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t v = high ? (w4[j] >> 4) : w4[j];
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const float q0 = (float)((v >> (16 * e)) & 0xFu), q1 = (float)((v >> (16 * e + 8)) & 0xFu);
+            const float w0 = __fsub_rn(__fmul_rn(sl, q0), ml), w1 = __fsub_rn(__fmul_rn(sl, q1), ml);
+            const __half2 h = __floats2half2_rn(w0, w1);
+            hi[2 * j + e] = *reinterpret_cast<const uint32_t*>(&h);
+            if (SPLIT) {
+                const float2 hf = __half22float2(h);
+                const __half2 l = __floats2half2_rn(__fmul_rn(__fsub_rn(w0, hf.x), 2048.0f),
+                                                    __fmul_rn(__fsub_rn(w1, hf.y), 2048.0f));
+                lo[2 * j + e] = *reinterpret_cast<const uint32_t*>(&l);
+            }
+        }
+    }
+}
+
+// Sub-block j's 6-bit scale and min from a superblock's 12 scale bytes
+// (q4k_dequant.h:43-60).
+__device__ __forceinline__ void q4k_scale_min_tc(int j, const uint8_t* sc, int& s, int& m) {
+    if (j < 4) {
+        s = sc[j] & 63;
+        m = sc[j + 4] & 63;
+    } else {
+        s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+}
+
 // Writes the 16-element chunk c (K elements 16c..16c+15) of row rr into a
 // K-major 128B-swizzled tile: 16-byte unit u of row rr sits at unit u ^ (rr & 7).
 __device__ __forceinline__ void store_chunk(uint8_t* tile, int rr, int c, const uint32_t (&w)[8]) {
@@ -157,13 +206,14 @@ struct alignas(64) ABlockMaps {
     int n;  // 0: the activations are tm_a
 };
 
-template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT>
+template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT, bool Q4K = false>
 __global__ void __launch_bounds__(kThreads, 1)
     q8_0_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ ABlockMaps am, const uint16_t* __restrict__ dsc, int n, int k, int m,
                         float* __restrict__ y, int64_t ldy, int kt_per_split, int a_blk_k, int a_row0,
                         uint32_t* __restrict__ err) {
-    using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
+    using L = TcLayout<BN, MT, SA, S16, S8, SPLIT, Q4K>;
+    static_assert(!Q4K || !BF16, "Q4_K operands are fp16");
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -219,9 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // once; the activations wait for the predecessor (programmatic launch).
             if (is_a) pdl_wait();
             const int depth = is_a ? SA : S8;
+            const int nload = (is_a || !Q4K) ? KT : KT / kQ4kTiles;  // k-tiles, or superblocks
             int issued = 0;
             bool ok = true;
-            for (int t = 0; t < KT; t++) {
+            for (int t = 0; t < nload; t++) {
                 const int s = t % depth, r = t / depth;
                 if (t >= depth) ok = mbar_wait(is_a ? a_empty(s) : b8_empty(s), (r - 1) & 1, err);
                 if (!ok) break;
@@ -238,6 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         else
                             tma_load_2d(dst, &tm_a, kk, m0 + mt * BM, a_full(s));
                     }
+                } else if (Q4K) {  // superblock kt0 / 4 + t of rows n0.., bytes at x = 144 sb
+                    mbar_arrive_expect_tx(b8_full(s), L::B8_BYTES);
+                    tma_load_2d(sbase + L::B8_OFF + s * L::B8_BYTES, &tm_b, (kt0 / kQ4kTiles + t) * kQ4kBytes, n0,
+                                b8_full(s));
                 } else {
                     mbar_arrive_expect_tx(b8_full(s), L::B8_BYTES);
                     tma_load_2d(sbase + L::B8_OFF + s * L::B8_BYTES, &tm_b, (kt0 + t) * BK, n0, b8_full(s));
@@ -286,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rr = i / (4 / CPT);
         const int c0 = (i % (4 / CPT)) * CPT;
         const int gr = n0 + rr;
-        const uint16_t* drow = gr < n ? dsc + (int64_t)gr * kb + 2 * kt0 : nullptr;
+        const uint16_t* drow = (!Q4K && gr < n) ? dsc + (int64_t)gr * kb + 2 * kt0 : nullptr;
         // Scales are prefetched kWin k-tiles ahead in registers when every row's
         // window is 16-byte aligned; otherwise they are read per k-tile.
         const bool windowed = (kb % 8 == 0) && (kt0 % 4 == 0);
@@ -306,7 +361,58 @@ __global__ void __launch_bounds__(kThreads, 1)
             load_win(nxt, 1);
         }
         bool ok = true;
-        for (int w = 0; w * kWin < KT && ok; w++) {
+        if constexpr (Q4K) {
+            // one superblock row (header + 128 quant bytes) per 4 k-tiles, kept in registers
+            for (int sbl = 0; sbl < KT / kQ4kTiles && ok; sbl++) {
+                const int s8 = sbl % S8;
+                ok = __all_sync(0xffffffffu, mbar_wait(b8_full(s8), (sbl / S8) & 1, err));
+                if (!ok) break;
+                // rows are 144 bytes apart: the 8 lanes of a shared-memory phase read 8 bank groups
+                const uint4* src = reinterpret_cast<const uint4*>(smem + L::B8_OFF + s8 * L::B8_BYTES + rr * kQ4kBytes);
+                const uint4 hdr = src[0];
+                uint4 qb[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) qb[j] = src[1 + j];
+                fence_proxy_async_smem();  // the slot's next write is a TMA (async proxy)
+                __syncwarp();
+                if (lane == 0) mbar_arrive(b8_empty(s8));
+                const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+                uint8_t scb[12];
+                *reinterpret_cast<uint32_t*>(scb) = hdr.y;
+                *reinterpret_cast<uint32_t*>(scb + 4) = hdr.z;
+                *reinterpret_cast<uint32_t*>(scb + 8) = hdr.w;
+#pragma unroll
+                for (int cq = 0; cq < kQ4kTiles; cq++) {  // sub-blocks 2 cq (weights 0..31) and 2 cq + 1 (32..63)
+                    const int t = sbl * kQ4kTiles + cq, s16 = t % S16;
+                    int sa, ma, sb, mb;
+                    q4k_scale_min_tc(2 * cq, scb, sa, ma);
+                    q4k_scale_min_tc(2 * cq + 1, scb, sb, mb);
+                    const float slo = __fmul_rn(d, (float)sa), mlo = __fmul_rn(dmin, (float)ma);
+                    const float shi = __fmul_rn(d, (float)sb), mhi = __fmul_rn(dmin, (float)mb);
+                    if (t >= S16) ok = __all_sync(0xffffffffu, mbar_wait(b16_empty(s16), ((t / S16) - 1) & 1, err));
+                    if (!ok) break;
+                    uint8_t* bhi = smem + L::B16_OFF + s16 * L::NB * L::B16_BYTES;
+#pragma unroll
+                    for (int cc = 0; cc < CPT; cc++) {
+                        // chunk c: weights 16c..16c+15 = nibbles of quant bytes 32 cq + 16 (c & 1) ..,
+                        // low for c < 2 (sub-block 2 cq), high for c >= 2 (2 cq + 1); rows past n
+                        // arrive as zeros from the TMA (d = dmin = 0), so their weights are 0
+                        const int c = c0 + cc;
+                        uint32_t hi[8], lo[8];
+                        const bool high = c >= 2;
+                        dequant16_q4k<SPLIT>((c & 1) ? qb[2 * cq + 1] : qb[2 * cq], high, high ? shi : slo,
+                                             high ? mhi : mlo, hi, lo);
+                        store_chunk(bhi, rr, c, hi);
+                        if (SPLIT) store_chunk(bhi + L::B16_BYTES, rr, c, lo);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(b16_full(s16));
+                }
+            }
+        }
+        for (int w = 0; !Q4K && w * kWin < KT && ok; w++) {
             if (windowed && w > 0) {
                 cur[0] = nxt[0];
                 cur[1] = nxt[1];
@@ -566,10 +672,10 @@ struct ALayout {
     int nblocks = 0;
 };
 
-template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT>
+template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT, bool Q4K = false>
 int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* a, int64_t m, float* out,
            int64_t ld_out, int splits, int kt_per, const ALayout& al, cudaStream_t s) {
-    using L = TcLayout<BN, MT, SA, S16, S8, SPLIT>;
+    using L = TcLayout<BN, MT, SA, S16, S8, SPLIT, Q4K>;
     CUtensorMap ma, mb;
     const CUtensorMapDataType adt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     ABlockMaps am;
@@ -588,10 +694,14 @@ int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void
                                         CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (st) return st;
-    st = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, qs, (uint64_t)k, (uint64_t)n, (uint64_t)k, BK, BN,
-                     CU_TENSOR_MAP_SWIZZLE_64B);
+    if (Q4K)  // raw superblock rows: n x (k / 256) x 144 bytes, one superblock per box
+        st = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, qs, (uint64_t)(k / 256 * kQ4kBytes), (uint64_t)n,
+                         (uint64_t)(k / 256 * kQ4kBytes), kQ4kBytes, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    else
+        st = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, qs, (uint64_t)k, (uint64_t)n, (uint64_t)k, BK, BN,
+                         CU_TENSOR_MAP_SWIZZLE_64B);
     if (st) return st;
-    auto kern = q8_0_gemm_tc_kernel<BN, MT, SA, S16, S8, BF16, SPLIT>;
+    auto kern = q8_0_gemm_tc_kernel<BN, MT, SA, S16, S8, BF16, SPLIT, Q4K>;
     GDN_CUDA(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM));
     const dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM * MT - 1) / (BM * MT)), (unsigned)splits);
     return launch_pdl("q8_0_gemm_tc_kernel", kern, grid, dim3(kThreads), L::SMEM, s, ma, mb, am, d, (int)n, (int)k,
@@ -695,6 +805,41 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
                     s, (const float*)out, splits, m, n, y, ldy);
     if (st) return st;
     return GDN_OK;
+}
+
+int launch_q4_k_gemm_tc(const void* blocks, int64_t n, int64_t k, const void* a, int64_t m, float* y, int64_t ldy,
+                        const TcOptions& opt, cudaStream_t s) {
+    if (k % 256 != 0 || k <= 0) return fail(GDN_ERR_SHAPE, "Q4_K tensor-core GEMM needs k %% 256 == 0 (k=%lld)", (long long)k);
+    if (n <= 0 || m <= 0) return GDN_OK;
+    if (n > INT32_MAX || m > INT32_MAX || k > INT32_MAX) return fail(GDN_ERR_SHAPE, "GEMM dims exceed int32");
+    if (ldy < n) return fail(GDN_ERR_SHAPE, "ldy < n");
+    if (!aligned(a, 16) || !aligned(blocks, 16))
+        return fail(GDN_ERR_ARG, "Q4_K tensor-core GEMM operands must be 16-byte aligned");
+    if (opt.a_blk_k > 0 || opt.a_nblocks > 0) return fail(GDN_ERR_ARG, "Q4_K tensor-core GEMM: plain activations only");
+    const int KT = (int)(k / BK);
+    int splits = opt.splits < 1 ? 1 : opt.splits;
+    int kt_per = (KT + splits - 1) / splits;
+    kt_per = (kt_per + kWin - 1) / kWin * kWin;  // whole superblocks and scale windows per split
+    splits = (KT + kt_per - 1) / kt_per;
+    float* out = y;
+    int64_t ld_out = ldy;
+    if (splits > 1) {
+        if (opt.workspace == nullptr || opt.workspace_bytes < gemm_tc_workspace_bytes(m, n, splits))
+            return fail(GDN_ERR_ARG, "split-K workspace too small");
+        out = static_cast<float*>(opt.workspace);
+        ld_out = n;
+    }
+    // exact weights (hi + lo fp16 operands); fp16 activations
+    const int8_t* q = static_cast<const int8_t*>(blocks);
+    ALayout al;
+    const int st = m > BM ? run_tc<128, 2, 3, 2, 2, false, true, true>(q, nullptr, n, k, a, m, out, ld_out, splits,
+                                                                       kt_per, al, s)
+                          : run_tc<128, 1, 4, 3, 3, false, true, true>(q, nullptr, n, k, a, m, out, ld_out, splits,
+                                                                       kt_per, al, s);
+    if (st || splits == 1) return st;
+    const int64_t cnt = m * n;
+    return launch_pdl("splitk_reduce_kernel", splitk_reduce_kernel, dim3((unsigned)((cnt + 255) / 256)), dim3(256), 0,
+                      s, (const float*)out, splits, m, n, y, ldy);
 }
 
 }  // namespace gdn

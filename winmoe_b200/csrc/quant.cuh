@@ -41,6 +41,10 @@ size_t gemm_tc_workspace_bytes(int64_t m, int64_t n, int splits);
 // bf16 [m][k] row-major (k % 64 == 0, 16-byte aligned), fp32 out.
 int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* a, bool a_bf16,
                         int64_t m, float* y, int64_t ldy, const TcOptions& opt, cudaStream_t s);
+// The same for GGUF Q4_K blocks [n][k / 256] (144 bytes each), fp16 activations,
+// exact weights (hi + lo operands): the fp32 product up to summation order.
+int launch_q4_k_gemm_tc(const void* blocks, int64_t n, int64_t k, const void* a, int64_t m, float* y, int64_t ldy,
+                        const TcOptions& opt, cudaStream_t s);
 // fp32 / bf16 / fp16 activations -> fp16 or bf16 (the tensor-core operand).
 int launch_convert(const void* x, int x_dtype, void* out, bool to_bf16, int64_t count, cudaStream_t s);
 
