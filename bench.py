@@ -266,7 +266,7 @@ GQA_DIMS = {"hidden": 2048, "q_gate": 2 * 16 * 256, "kv": 2 * 256, "attn": 16 * 
 
 
 def run_gqa(dev, hbm_peak, peak_src, with_cpu):
-    """SURVEY (f)3: a full-attention layer's Q8_0 projections per token (Q+gate, K, V, then O),
+    """The full-attention (GQA) layers' Q8_0 projections per token (Q+gate, K, V, then O),
     through the reference's own offload calls (host buffers in and out, synchronous) and,
     device-resident, as the same GEMVs on the library's stream."""
     import ctypes as C
