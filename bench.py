@@ -243,12 +243,28 @@ def run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, with_cpu):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
+    # the step as one CUDA graph launch per token (DecodeGraph), launched from Python
+    stg = L.DeltaNetState.zeros(cfg, 1, dev)
+    g = L.DecodeGraph(w, stg, x_dtype=xs.dtype)
+    for i in range(3):
+        g.x.copy_(xs[i:i + 1])
+        g.replay()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for i in range(steps):
+        g.x.copy_(xs[i:i + 1])
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_graph = e0.elapsed_time(e1) / steps
     nb = decode_b1_bytes(cfg)
     ach = nb / (ms / 1e3) / 1e9
     res = {"workload": "decode B=1 (config 1): 64 consecutive tokens of one sequence from a zero state, fp32 x; "
                        "steps queued behind a GPU sleep (device pace); ms_per_token_host_paced launches each step "
-                       "from Python as the previous returns",
+                       "from Python as the previous returns; ms_per_token_graph replays the step captured as a "
+                       "CUDA graph, one launch per token",
            "value": 1e3 / ms, "unit": "tok/s", "ms_per_token": ms, "ms_per_token_host_paced": ms_host,
+           "ms_per_token_graph": ms_graph,
            "steps": steps, "warmup": 3,
            "roofline": {"bound": "hbm", "kernel": "whole decode step", "achieved": ach, "peak": hbm_peak,
                         "unit": "GB/s", "frac": ach / hbm_peak, "peak_source": peak_src,

@@ -261,3 +261,27 @@ def test_decode_reference_projections():
                 err[ref].append(rel_l2(got[i][b], want))
     assert max(err[True]) <= 1e-4, max(err[True])
     assert max(err[True]) * 10 <= np.median(err[False]), (max(err[True]), np.median(err[False]))
+
+
+@pytest.mark.parametrize("B,dtype", [(1, torch.float32), (256, torch.bfloat16)])
+def test_decode_graph_replay_matches_eager(t35, w35, B, dtype):
+    """DecodeGraph: replays of the captured step give the eager step's outputs and
+    states bit for bit (same kernels on the same buffers)."""
+    cfg = DIMS_35B
+    gen = torch.Generator().manual_seed(B)
+    S0 = torch.randn((B, cfg.num_v_heads, 128, 128), generator=gen) * 0.05
+    xs = torch.randn((4, B, cfg.hidden), generator=gen).to(dtype).to(DEV)
+    eager, graphed = L.DeltaNetState.zeros(cfg, B, DEV), L.DeltaNetState.zeros(cfg, B, DEV)
+    eager.S.copy_(S0)
+    graphed.S.copy_(S0)
+    g = L.DecodeGraph(w35, graphed, x_dtype=dtype)
+    assert torch.equal(graphed.S, eager.S)  # capturing does not run the step
+    for i in range(4):
+        want = L.decode_step(w35, eager, xs[i].contiguous())
+        g.x.copy_(xs[i])
+        got = g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), i
+    assert torch.equal(graphed.S, eager.S)
+    assert torch.equal(graphed.conv_buf, eager.conv_buf)
+    assert torch.equal(graphed.conv_pos, eager.conv_pos)

@@ -215,6 +215,34 @@ def decode_step(w: DeltaNetWeights, state: DeltaNetState, x: torch.Tensor, out: 
     return out
 
 
+class DecodeGraph:
+    """A decode step captured once as a CUDA graph on fixed buffers: write the
+    next token's activations into `x`, call replay(), read `out`.  Each replay
+    advances `state` exactly as decode_step does (same kernels, same order); one
+    graph launch replaces the step's six kernel launches."""
+
+    def __init__(self, w: DeltaNetWeights, state: DeltaNetState, x_dtype=torch.float32):
+        dev = state.S.device
+        B, H = state.batch, w.cfg.hidden
+        self.x = torch.zeros((B, H), dtype=x_dtype, device=dev)
+        self.out = torch.empty((B, H), dtype=torch.float32, device=dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        # one eager step on a scratch state first: workspace, kernel attributes and the
+        # library's per-device lookups are set up outside the capture
+        scratch = DeltaNetState.zeros(w.cfg, B, dev)
+        decode_step(w, scratch, self.x, self.out, stream=s)
+        s.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):  # captured, not run: `state` is untouched
+            decode_step(w, state, self.x, self.out, stream=s)
+        torch.cuda.current_stream(dev).wait_stream(s)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
+
+
 def prefill_workspace(cfg: GDNConfig, T: int, device) -> torch.Tensor:
     """Cached scratch for gdn_prefill (allocated by torch, outside the C ABI)."""
     device = torch.device(device)
