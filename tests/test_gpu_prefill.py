@@ -128,3 +128,20 @@ def test_prefill_4096_matches_decode_steps():
     err_s = ((st_p.S - st_d.S).norm() / st_d.S.norm()).item()
     assert err_s <= TOL, err_s
     assert torch.equal(st_p.conv_pos, st_d.conv_pos)
+
+
+@pytest.mark.parametrize("T", [5, 70, 300])
+def test_prefill_q4_k_layer(T):
+    """A layer with Q4_K projections: T >= 8 runs them on the tensor cores (fp16
+    activations, exact hi + lo weights), T < 8 on the CUDA-core GEMV."""
+    cfg = GDNConfig(512, 2, 4, 128)
+    t = synth.layer_tensors(cfg, layer=3, weight_type=12)
+    w = L.DeltaNetWeights.upload(cfg, t.in_proj, t.out_proj, t.conv1d_w, t.ssm_a, t.dt_bias, t.head_norm,
+                                 weight_type=12, device=DEV)
+    x = torch.from_numpy(synth.hidden_states(T, cfg.hidden, seed=T + 7)).to(torch.bfloat16)
+    want, S_ref, _, pos_ref = oracle_run(cfg, t, x.float().numpy())
+    st = L.DeltaNetState.zeros(cfg, 1, DEV)
+    y = L.prefill(w, st, x.to(DEV)).cpu().numpy()
+    assert rel_l2(y, want) <= TOL, rel_l2(y, want)
+    assert rel_l2(st.S[0].cpu().numpy(), S_ref) <= TOL
+    assert int(st.conv_pos.cpu()[0]) == pos_ref == T

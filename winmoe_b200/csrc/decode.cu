@@ -330,8 +330,10 @@ inline int mark(PhaseEvents* pe, int i, cudaStream_t s) {
     return GDN_OK;
 }
 
-// Tensor-core projections pay off once a batch fills an M=128 tile reasonably.
+// Tensor-core projections pay off once a batch fills an M=128 tile reasonably
+// (Q4_K: from 8 rows, its CUDA-core GEMV being compute-bound).
 constexpr int64_t kTcMinBatch = 64;
+constexpr int64_t kTcMinBatchQ4k = 8;
 // Split-K factor of the tensor-core out_proj (K = inner is long, N = hidden short).
 constexpr int kOutSplits = 8;
 
@@ -452,8 +454,18 @@ int validate_layer(const gdn_layer* L) {
 static int in_projection(const gdn_layer* L, const Dims& D, int64_t B, const void* x, int x_dtype,
                          const Workspace& ws, cudaStream_t s) {
     const int64_t hidden = L->dims.hidden;
-    if (L->weight_type == GDN_GGML_Q4_K)
-        return launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, B, ws.proj, D.ldp, s);
+    if (L->weight_type == GDN_GGML_Q4_K) {
+        // fp16 x (bf16 / fp16 convert exactly; fp32 would be rounded: CUDA cores then)
+        if (B < kTcMinBatchQ4k || x_dtype == GDN_DTYPE_F32)
+            return launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, B, ws.proj, D.ldp, s);
+        const void* a = x;
+        if (x_dtype != GDN_DTYPE_F16 || !aligned(x, 16)) {
+            const int st = launch_convert(x, x_dtype, ws.xconv, false, B * hidden, s);
+            if (st) return st;
+            a = ws.xconv;
+        }
+        return launch_q4_k_gemm_tc(L->in_blocks, D.np, hidden, a, B, ws.proj, D.ldp, TcOptions(), s);
+    }
     if (B < kTcMinBatch) return launch_q8_0_gemv(L->in_qs, L->in_d, D.np, hidden, x, x_dtype, B, ws.proj, D.ldp, s);
     const void* a = x;
     int st;
@@ -506,7 +518,7 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
         return fail(GDN_ERR_ARG, "workspace must be 256-aligned and hold %zu bytes (got %zu)", need, ws_bytes);
     const Dims D = dims_of(d);
     const Workspace ws = carve(d, B, wsp);
-    const bool tc_out = !ref && (L->weight_type == GDN_GGML_Q8_0) && B >= kTcMinBatch;
+    const bool tc_out = !ref && (L->weight_type == GDN_GGML_Q8_0 ? B >= kTcMinBatch : B >= kTcMinBatchQ4k);
     const bool conv = (L->conv1d_w != nullptr && conv_buf != nullptr);
     PhaseEvents* pe = phase_events();
 
@@ -540,7 +552,15 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
     if (ref) {
         st = launch_q8_0_gemv_ref(L->out_qs, L->out_d, d.hidden, D.inner, ws.gated, B, out, d.hidden, s);
     } else if (L->weight_type == GDN_GGML_Q4_K) {
-        st = launch_q4_k_gemv(L->out_blocks, d.hidden, D.inner, ws.gated, GDN_DTYPE_F32, B, out, d.hidden, s);
+        if (tc_out) {  // the fp16 gated heads on the tensor cores, exact weights, split K
+            TcOptions opt;
+            opt.splits = kOutSplits;
+            opt.workspace = ws.partial;
+            opt.workspace_bytes = ws.partial_bytes;
+            st = launch_q4_k_gemm_tc(L->out_blocks, d.hidden, D.inner, ws.gated_h, B, out, d.hidden, opt, s);
+        } else {
+            st = launch_q4_k_gemv(L->out_blocks, d.hidden, D.inner, ws.gated, GDN_DTYPE_F32, B, out, d.hidden, s);
+        }
     } else if (tc_out) {
         TcOptions opt;
         opt.split_precision = true;

@@ -894,7 +894,16 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     // ---- input projection -> proj [T][ldp]
     if ((st = phase_mark(0, s))) return st;
     if (L->weight_type == GDN_GGML_Q4_K) {
-        st = launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, T, W.proj, D.ldp, s);
+        if (T >= 8 && x_dtype != GDN_DTYPE_F32) {  // tensor cores, exact weights, fp16 x (bf16 converts exactly)
+            const void* a = x;
+            if (x_dtype != GDN_DTYPE_F16 || !aligned(x, 16)) {
+                if ((st = launch_convert(x, x_dtype, W.xconv, false, T * hidden, s))) return st;
+                a = W.xconv;
+            }
+            st = launch_q4_k_gemm_tc(L->in_blocks, D.np, hidden, a, T, W.proj, D.ldp, TcOptions(), s);
+        } else {
+            st = launch_q4_k_gemv(L->in_blocks, D.np, hidden, x, x_dtype, T, W.proj, D.ldp, s);
+        }
         if (st) return st;
     } else {
         const void* a = x;
@@ -960,7 +969,10 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     if ((st = phase_mark(3, s))) return st;
     if (gated_out) return phase_mark(4, s);
     if (L->weight_type == GDN_GGML_Q4_K) {
-        st = launch_q4_k_gemv(L->out_blocks, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
+        if (T >= 8)  // the fp16 gated heads on the tensor cores, exact weights
+            st = launch_q4_k_gemm_tc(L->out_blocks, hidden, D.inner, W.gated, T, out, hidden, TcOptions(), s);
+        else
+            st = launch_q4_k_gemv(L->out_blocks, hidden, D.inner, W.gated, GDN_DTYPE_F16, T, out, hidden, s);
     } else if (T >= 64) {
         TcOptions fast;
         st = launch_q8_0_gemm_tc(L->out_qs, L->out_d, hidden, D.inner, W.gated, false, T, out, hidden, fast, s);
