@@ -414,28 +414,80 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
         sm.sc[1][j] = sm.beta[j];
     }
     __syncthreads();
-    for (int d = 1; d < 4; d++) {
-        const int nblk = 4 - d;  // blocks (bj + d, bj), bj = 0 .. nblk - 1
-        for (int e = tid; e < nblk * 256; e += 256) {
-            const int q = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-            const int bi = q + d, bj = q;
-            float acc = 0.0f;
-            for (int kb = bj; kb < bi; kb++)
+    // Off-diagonal blocks on the tensor cores, one warp per block of the stage: each
+    // 16x16x16 product takes its fp32 operands as hi + lo bf16 pairs (three MMAs:
+    // hi.hi + hi.lo + lo.hi, relative error ~2^-17 -- T then enters W' and U' as a
+    // 16-bit hi + lo pair itself).  Fragments follow the m16n8k16 layout.
+    {
+        const int gq = lane >> 2, qq = lane & 3;
+        auto split2 = [](float x0, float x1, uint32_t& hi, uint32_t& lo) {
+            const bf16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+            hi = wmma16::pack_bf16(__bfloat162float(h0), __bfloat162float(h1));
+            lo = wmma16::pack_bf16(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+        };
+        // A: rows r0..r0+15, cols c0..c0+15 of a row-major fp32 tile (pitch ld)
+        auto frag_a = [&](const float* X, int ld, int r0, int c0, uint32_t (&hi)[4], uint32_t (&lo)[4]) {
 #pragma unroll
-                for (int kk = 0; kk < 16; kk++)
-                    acc = fmaf(sm.L[16 * bi + r][16 * kb + kk], sm.T[16 * kb + kk][16 * bj + cc], acc);
-            sm.M[q][r][cc] = acc;
-        }
-        __syncthreads();
-        for (int e = tid; e < nblk * 256; e += 256) {
-            const int q = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-            const int bi = q + d, bj = q;
-            float acc = 0.0f;
+            for (int i = 0; i < 4; i++) {
+                const float* p = X + (r0 + gq + 8 * (i & 1)) * ld + c0 + 2 * qq + 8 * (i >> 1);
+                split2(p[0], p[1], hi[i], lo[i]);
+            }
+        };
+        // B (16 x 8): B[k][n] = X[k0 + k][n0 + n]
+        auto frag_b = [&](const float* X, int ld, int k0, int n0, uint32_t (&hi)[2], uint32_t (&lo)[2]) {
 #pragma unroll
-            for (int kk = 0; kk < 16; kk++) acc = fmaf(sm.T[16 * bi + r][16 * bi + kk], sm.M[q][kk][cc], acc);
-            sm.T[16 * bi + r][16 * bj + cc] = -acc;
+            for (int i = 0; i < 2; i++) {
+                const float* p = X + (k0 + 2 * qq + 8 * i) * ld + n0 + gq;
+                split2(p[0], p[ld], hi[i], lo[i]);
+            }
+        };
+        auto mma3 = [](float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], const uint32_t (&bh)[2],
+                       const uint32_t (&bl)[2]) {
+            wmma16::mma(c, ah, bh[0], bh[1]);
+            wmma16::mma(c, ah, bl[0], bl[1]);
+            wmma16::mma(c, al, bh[0], bh[1]);
+        };
+        for (int d = 1; d < 4; d++) {
+            const int nblk = 4 - d;  // blocks (bj + d, bj), bj = 0 .. nblk - 1
+            if (warp < nblk) {
+                const int bi = warp + d, bj = warp;
+                // M = sum_{kb=bj}^{bi-1} L_{bi,kb} T_{kb,bj}
+                float m[2][4] = {};
+                for (int kb = bj; kb < bi; kb++) {
+                    uint32_t ah[4], al[4];
+                    frag_a(&sm.L[0][0], CH + 1, 16 * bi, 16 * kb, ah, al);
+#pragma unroll
+                    for (int nt = 0; nt < 2; nt++) {
+                        uint32_t bh[2], bl[2];
+                        frag_b(&sm.T[0][0], CH + 1, 16 * kb, 16 * bj + 8 * nt, bh, bl);
+                        mma3(m[nt], ah, al, bh, bl);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < 2; nt++) {
+                    sm.M[warp][gq][8 * nt + 2 * qq] = m[nt][0];
+                    sm.M[warp][gq][8 * nt + 2 * qq + 1] = m[nt][1];
+                    sm.M[warp][gq + 8][8 * nt + 2 * qq] = m[nt][2];
+                    sm.M[warp][gq + 8][8 * nt + 2 * qq + 1] = m[nt][3];
+                }
+                __syncwarp();
+                // T_{bi,bj} = -T_{bi,bi} M
+                uint32_t ah[4], al[4];
+                frag_a(&sm.T[0][0], CH + 1, 16 * bi, 16 * bi, ah, al);
+#pragma unroll
+                for (int nt = 0; nt < 2; nt++) {
+                    uint32_t bh[2], bl[2];
+                    frag_b(&sm.M[warp][0][0], 17, 0, 8 * nt, bh, bl);
+                    float t[4] = {};
+                    mma3(t, ah, al, bh, bl);
+                    sm.T[16 * bi + gq][16 * bj + 8 * nt + 2 * qq] = -t[0];
+                    sm.T[16 * bi + gq][16 * bj + 8 * nt + 2 * qq + 1] = -t[1];
+                    sm.T[16 * bi + gq + 8][16 * bj + 8 * nt + 2 * qq] = -t[2];
+                    sm.T[16 * bi + gq + 8][16 * bj + 8 * nt + 2 * qq + 1] = -t[3];
+                }
+            }
+            __syncthreads();
         }
-        __syncthreads();
     }
 
     // ---- W' = (T diag(b gam)) K and U' = (T diag(b)) V on the tensor cores:
