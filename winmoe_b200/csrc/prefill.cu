@@ -297,10 +297,10 @@ __global__ void __launch_bounds__(256, 2) prefill_prep_kernel(const float* __res
 // -------------------------------------------------------- K1: chunk_local
 //
 // grid (nc, Hv), 256 threads.  L = strictly lower b_i exp(G_i - G_j) K K^T from
-// a bf16 tensor-core product; then (I + L) X = R solved by fp32 forward
-// substitution with one thread per column of X: threads 0..127 produce W'
-// (R = diag(b gam) K), threads 128..255 produce U' (R = diag(b) V).  Threads
-// 0..127 also write e*K; the chunk's cumulative G and gam_63 go to HBM.
+// a bf16 tensor-core product; T = (I + L)^-1 blocked by 16 (fp32 substitution
+// on the diagonal blocks, hi + lo bf16 MMAs below them); W' = T diag(b gam) K,
+// U' = T diag(b) V and e*K, staged in shared memory in the scan's tile layouts
+// and written by bulk copies; the chunk's cumulative G and gam_63 go to HBM.
 struct LocalSmem {
     bf16 k[CH][LDH];
     bf16 v[CH][LDH];
@@ -310,6 +310,13 @@ struct LocalSmem {
     float G[CH], beta[CH];
     float sc[2][CH];      // column scales of T: b_j gam_j (for W') and b_j (for U')
 };
+// The products leave through shared regions that are dead by then: U' through
+// V + L, W' through T + M (each staged in its HBM layout).
+static_assert(offsetof(LocalSmem, L) == offsetof(LocalSmem, v) + sizeof(LocalSmem::v), "V, L adjacent");
+static_assert(offsetof(LocalSmem, M) == offsetof(LocalSmem, T) + sizeof(LocalSmem::T), "T, M adjacent");
+static_assert(sizeof(LocalSmem::v) + sizeof(LocalSmem::L) >= (HD / BV) * CH * LDV * 2, "U' staging fits");
+static_assert(sizeof(LocalSmem::T) + sizeof(LocalSmem::M) >= CH * LDH * 2, "W' staging fits");
+static_assert(offsetof(LocalSmem, v) % 16 == 0 && offsetof(LocalSmem, T) % 16 == 0, "bulk sources aligned");
 
 __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restrict__ kn, const bf16* __restrict__ vb,
                                                           const float* __restrict__ glog,
@@ -389,8 +396,7 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
     // forward substitution (one thread per block column), then the lower
     // off-diagonal blocks in order of their distance d from the diagonal,
     //   T_ij = -T_ii sum_{k=j}^{i-1} L_ik T_kj   (i - j = d)
-    for (int e = tid; e < CH * (CH + 1); e += 256) (&sm.T[0][0])[e] = 0.0f;
-    __syncthreads();
+    // (T's upper 16-blocks are never read: nothing clears them.)
     if (tid < CH) {
         // column jc of the block's inverse: col[i] = -sum_{kk<i} L_i,kk col[kk], the
         // sums accumulated column-wise (each step's FMAs independent of each
@@ -490,25 +496,32 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
         }
     }
 
-    // ---- W' = (T diag(b gam)) K and U' = (T diag(b)) V on the tensor cores:
-    // K and V are exact bf16; the scaled T enters as hi + lo bf16 (16 bits), its
-    // A fragments built in registers straight from the fp32 T (m16n8k16 layout:
-    // register i holds row gq + 8 (i & 1), columns 2 qq + 8 (i >> 1) + {0, 1}).
+    // ---- U' = (T diag(b)) V, then W' = (T diag(b gam)) K, on the tensor cores:
+    // V and K exact bf16; the scaled T enters as hi + lo bf16 fragments built in
+    // registers from the fp32 T (register i: row gq + 8 (i & 1), columns
+    // 2 qq + 8 (i >> 1) + {0, 1}).  T is block lower triangular, so row block rb
+    // takes k-blocks 0..rb only.  Each result is staged in its HBM layout in a
+    // shared region that is dead by then and leaves as one bulk copy: U' through
+    // V + L (slab-major [HD / BV][CH][LDV]), W' through T + M ([CH][LDH]), e*K
+    // in place in the K tile.
     {
         const int gq = lane >> 2, qq = lane & 3;
-        const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
+        const int rb = warp & 3, r0 = 16 * rb, n0 = 64 * (warp >> 2);
+        float acc[8][4];
+        auto product = [&](const bf16* rhs, const float* scale) {
 #pragma unroll
-        for (int m = 0; m < 2; m++) {
-            const bf16* rhs = m == 0 ? &sm.k[0][0] : &sm.v[0][0];
-            float acc[8][4] = {};
+            for (int n = 0; n < 8; n++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) acc[n][e] = 0.0f;
 #pragma unroll
             for (int kk = 0; kk < CH / 16; kk++) {
+                if (kk > rb) break;
                 uint32_t ah[4], al[4];
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     const int row = r0 + gq + 8 * (i & 1), col = 16 * kk + 2 * qq + 8 * (i >> 1);
-                    const float x0 = sm.T[row][col] * sm.sc[m][col];
-                    const float x1 = sm.T[row][col + 1] * sm.sc[m][col + 1];
+                    const float x0 = sm.T[row][col] * scale[col];
+                    const float x1 = sm.T[row][col + 1] * scale[col + 1];
                     const bf16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
                     ah[i] = wmma16::pack_bf16(__bfloat162float(h0), __bfloat162float(h1));
                     al[i] = wmma16::pack_bf16(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
@@ -523,31 +536,35 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
                     wmma16::mma(acc[2 * np2 + 1], al, b[2], b[3]);
                 }
             }
-            // W' rows at the scan's padded pitch; U' as one [CH][LDV] tile per BV-column slab
+        };
+        product(&sm.v[0][0], sm.sc[1]);
+        __syncthreads();  // V (and L) read by every warp: U' takes their place
+        bf16* ustage = &sm.v[0][0];
 #pragma unroll
-            for (int n = 0; n < 8; n++) {
-                const int cl = n0 + 8 * n + 2 * qq;
-                bf16* d0;
-                int64_t ld;
-                if (m == 0) {
-                    d0 = wp + ((int64_t)h * Tp + t0) * LDH + cl;
-                    ld = LDH;
-                } else {
-                    d0 = up + (((int64_t)h * (Tp / CH) + c) * (HD / BV) + cl / BV) * (CH * LDV) + cl % BV;
-                    ld = LDV;
-                }
-                *reinterpret_cast<uint32_t*>(d0 + (int64_t)(r0 + gq) * ld) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
-                *reinterpret_cast<uint32_t*>(d0 + (int64_t)(r0 + gq + 8) * ld) = wmma16::pack_bf16(acc[n][2], acc[n][3]);
-            }
+        for (int n = 0; n < 8; n++) {
+            const int cl = n0 + 8 * n + 2 * qq;
+            bf16* d0 = ustage + (cl / BV) * (CH * LDV) + cl % BV;
+            *reinterpret_cast<uint32_t*>(d0 + (r0 + gq) * LDV) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
+            *reinterpret_cast<uint32_t*>(d0 + (r0 + gq + 8) * LDV) = wmma16::pack_bf16(acc[n][2], acc[n][3]);
+        }
+        product(&sm.k[0][0], sm.sc[0]);
+        __syncthreads();  // T and K read by every warp: W' takes T's place, e*K K's
+        bf16* wstage = reinterpret_cast<bf16*>(&sm.T[0][0]);
+#pragma unroll
+        for (int n = 0; n < 8; n++) {
+            bf16* d0 = wstage + n0 + 8 * n + 2 * qq;
+            *reinterpret_cast<uint32_t*>(d0 + (r0 + gq) * LDH) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
+            *reinterpret_cast<uint32_t*>(d0 + (r0 + gq + 8) * LDH) = wmma16::pack_bf16(acc[n][2], acc[n][3]);
         }
     }
 
-    // ---- e K with e_i = exp(G_63 - G_i): 8 bf16 per thread and store
+    // ---- e K with e_i = exp(G_63 - G_i), 8 bf16 per thread, in place
     const float G63 = sm.G[CH - 1];
     for (int e = tid; e < CH * HD / 8; e += 256) {
         const int i = e / (HD / 8), c8 = (e % (HD / 8)) * 8;
         const float ei = __expf(G63 - sm.G[i]);
-        const uint4 kv = *reinterpret_cast<const uint4*>(&sm.k[i][c8]);
+        uint4* p = reinterpret_cast<uint4*>(&sm.k[i][c8]);
+        const uint4 kv = *p;
         const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
         uint32_t ow[4];
 #pragma unroll
@@ -555,10 +572,20 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
             const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw[w4]));
             ow[w4] = wmma16::pack_bf16(ei * f.x, ei * f.y);
         }
-        *reinterpret_cast<uint4*>(ek + ((int64_t)h * Tp + t0 + i) * LDH + c8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        *p = make_uint4(ow[0], ow[1], ow[2], ow[3]);
     }
     if (tid < CH) gcum[(int64_t)h * Tp + t0 + tid] = sm.G[tid];
     if (tid == 0) gchunk[(int64_t)h * (Tp / CH) + c] = expf(G63);
+    sm100::fence_proxy_async_smem();  // the staged tiles, written by the generic proxy, leave by bulk copy
+    __syncthreads();
+    if (tid == 0) {
+        sm100::bulk_store(wp + ((int64_t)h * Tp + t0) * LDH, sm100::smem_u32(&sm.T[0][0]), CH * LDH * 2);
+        sm100::bulk_store(up + ((int64_t)h * (Tp / CH) + c) * (HD / BV) * (CH * LDV), sm100::smem_u32(&sm.v[0][0]),
+                          (HD / BV) * CH * LDV * 2);
+        sm100::bulk_store(ek + ((int64_t)h * Tp + t0) * LDH, sm100::smem_u32(&sm.k[0][0]), CH * LDH * 2);
+        sm100::bulk_commit();
+        sm100::bulk_wait_read_all();
+    }
 }
 
 // --------------------------------------------------------- K2: chunk_scan

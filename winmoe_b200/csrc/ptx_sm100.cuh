@@ -100,6 +100,18 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
+// Untiled bulk copy shared -> global of `bytes` (a multiple of 16; both
+// addresses 16-byte aligned), tracked in the issuing thread's bulk groups.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+                 "r"(src), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk store of this thread has read its shared
+// source (the global writes complete on their own before the grid does).
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // -------------------------------------------------------------------- tcgen05
 
 // Allocates `ncols` TMEM columns (power of two >= 32); the base address is
