@@ -82,6 +82,17 @@ int launch_pdl(const char* name, void (*kern)(KArgs...), dim3 grid, dim3 block, 
     return e == cudaSuccess ? 0 : cuda_status(e, name);
 }
 
+__device__ __forceinline__ float tanh_hw(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// SiLU(x) = x sigmoid(x) = x (1 + tanh(x / 2)) / 2: one special-function op.
+__device__ __forceinline__ float silu_fast(float x) {
+    const float h = 0.5f * x;
+    return fmaf(h, tanh_hw(h), h);
+}
+
 // Spin limit of bounded waits, in SM clock cycles (~1 s at 1.9 GHz).
 constexpr long long kWaitCycles = 2000000000LL;
 

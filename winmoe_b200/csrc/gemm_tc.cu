@@ -206,12 +206,128 @@ struct alignas(64) ABlockMaps {
     int n;  // 0: the activations are tm_a
 };
 
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kDeqThreads) : "memory"); }
+
+// Prefill preprocessing of this CTA's q / k / v head groups (PrepEpilogue), on
+// the 8 epilogue warps once the plain epilogue is done.  Per 128-column head
+// group: the fp32 tile [MT * BM][128] goes from TMEM to shared memory (raw rows
+// 0..2 and the last 3 also to `edge`, rows T-4..T-1 to `win`); then warp w takes
+// rows [w R/8, (w+1) R/8) and lane l columns 4l..4l+3: conv1d over the 3 rows
+// above (a sliding window in registers) + SiLU, in the prep kernel's arithmetic;
+// for q and k the row's L2 norm (a butterfly over the lanes), then bf16 out.
+// Both named barriers run on every epilogue warp, `ok` or not.
+template <int BN, int MT>
+__device__ __forceinline__ void prep_epilogue(const PrepEpilogue& pe, float* S, uint32_t tmem, int n0, int64_t m0,
+                                              int tile, int warp, int lane, bool ok) {
+    constexpr int R = MT * BM;  // tokens per M tile
+    constexpr int SP = 132;     // staged row pitch (floats): 16-byte row phases on distinct bank groups
+    constexpr int RC = R / 8;   // rows per warp in the conv pass
+    static_assert(RC == 16 || RC == 32, "rows per warp");
+    const int q = warp & 3, half = (warp - kDeqWarp0) >> 2, wi = warp - kDeqWarp0;
+    for (int hg = 0; hg < BN / 128; hg++) {
+        const int hc0 = n0 + hg * 128;  // channel of the head group's column 0
+        if (hc0 >= pe.qkv) break;       // z columns: the plain epilogue
+        epi_bar();                      // the staging area is free
+        if (ok) {
+            const int mt = MT == 2 ? half : 0;
+            const int c_lo = MT == 2 ? 0 : half * 64, c_hi = MT == 2 ? 128 : c_lo + 64;
+            const int row = mt * BM + q * 32 + lane;
+            const int64_t tok = m0 + row;
+            const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(mt * BN + hg * 128);
+            float* edge_row = nullptr;
+            if (tok < pe.T && row < 3) edge_row = pe.edge + ((int64_t)tile * 6 + row) * pe.qkv + hc0;
+            if (tok < pe.T && row >= R - 3) edge_row = pe.edge + ((int64_t)tile * 6 + 3 + row - (R - 3)) * pe.qkv + hc0;
+            float* win_row = (tok < pe.T && tok >= pe.T - 4) ? pe.win + (tok - (pe.T - 4)) * pe.qkv + hc0 : nullptr;
+            for (int c = c_lo; c < c_hi; c += 32) {
+                uint32_t v[32];
+                tmem_load_32x32b_x32(tb + (uint32_t)c, v);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const uint4 u = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    *reinterpret_cast<uint4*>(S + row * SP + c + j) = u;
+                    if (edge_row != nullptr) *reinterpret_cast<uint4*>(edge_row + c + j) = u;
+                    if (win_row != nullptr) *reinterpret_cast<uint4*>(win_row + c + j) = u;
+                }
+            }
+        }
+        epi_bar();
+        if (ok) {
+            const int c4 = 4 * lane, ch = hc0 + c4, hidx = hc0 / 128;
+            __nv_bfloat16* dst;
+            if (hidx < pe.hk) dst = pe.qn + (int64_t)hidx * pe.Tp * 128;
+            else if (hidx < 2 * pe.hk) dst = pe.kn + (int64_t)(hidx - pe.hk) * pe.Tp * 128;
+            else dst = pe.vb + (int64_t)(hidx - 2 * pe.hk) * pe.Tp * 128;
+            dst += c4;
+            const bool l2 = hidx < 2 * pe.hk, conv = pe.conv_w != nullptr;
+            float4 wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                wv[i] = conv ? __ldg(reinterpret_cast<const float4*>(pe.conv_w) + ch + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const int r0 = wi * RC;
+            const float* col = S + c4;
+            // One pass over the warp's rows with a branch-free body (rows in flight
+            // overlap): rows 0..2 of the tile, whose window lies in the previous
+            // tile, are computed from clamped rows and not stored (the edge kernel's).
+            auto rows = [&](auto l2_tag, auto conv_tag) {
+                constexpr bool L2 = decltype(l2_tag)::value, CONV = decltype(conv_tag)::value;
+                float4 h0 = *reinterpret_cast<const float4*>(col + max(r0 - 3, 0) * SP);
+                float4 h1 = *reinterpret_cast<const float4*>(col + max(r0 - 2, 0) * SP);
+                float4 h2 = *reinterpret_cast<const float4*>(col + max(r0 - 1, 0) * SP);
+#pragma unroll 8
+                for (int i = 0; i < RC; i++) {
+                    const float4 x = *reinterpret_cast<const float4*>(col + (r0 + i) * SP);
+                    float o[4] = {x.x, x.y, x.z, x.w};
+                    if constexpr (CONV) {
+                        const float a0[4] = {h0.x, h0.y, h0.z, h0.w}, a1[4] = {h1.x, h1.y, h1.z, h1.w};
+                        const float a2[4] = {h2.x, h2.y, h2.z, h2.w};
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            float sum = wv[c].x * a0[c];
+                            sum = fmaf(wv[c].y, a1[c], sum);
+                            sum = fmaf(wv[c].z, a2[c], sum);
+                            sum = fmaf(wv[c].w, o[c], sum);
+                            o[c] = silu_fast(sum);
+                        }
+                    }
+                    h0 = h1;
+                    h1 = h2;
+                    h2 = x;
+                    if constexpr (L2) {
+                        // the row's sum of squares over the 32 lanes (128 columns);
+                        // 1 / (sqrt(ss) + 1e-6) (deltanet_impl.h:89) as the prep kernel has it
+                        float ss = fmaf(o[0], o[0], fmaf(o[1], o[1], fmaf(o[2], o[2], o[3] * o[3])));
+#pragma unroll
+                        for (int sh = 16; sh > 0; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
+                        const float inv = ss > 1e-4f ? rsqrtf(ss) : 1.0f / (sqrtf(ss) + 1e-6f);
+#pragma unroll
+                        for (int c = 0; c < 4; c++) o[c] *= inv;
+                    }
+                    const int64_t t = m0 + r0 + i;
+                    __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]), b = __floats2bfloat162_rn(o[2], o[3]);
+                    uint2 val = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+                    if (t >= pe.T) val = make_uint2(0u, 0u);
+                    if (r0 + i >= 3 && t < pe.Tp) *reinterpret_cast<uint2*>(dst + t * 128) = val;
+                }
+            };
+            using T1 = std::true_type;
+            using F0 = std::false_type;
+            if (l2) {
+                if (conv) rows(T1(), T1());
+                else rows(T1(), F0());
+            } else {
+                if (conv) rows(F0(), T1());
+                else rows(F0(), F0());
+            }
+        }
+    }
+}
+
 template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT, bool Q4K = false>
 __global__ void __launch_bounds__(kThreads, 1)
     q8_0_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ ABlockMaps am, const uint16_t* __restrict__ dsc, int n, int k, int m,
                         float* __restrict__ y, int64_t ldy, int kt_per_split, int a_blk_k, int a_row0,
-                        uint32_t* __restrict__ err) {
+                        const PrepEpilogue pe, uint32_t* __restrict__ err) {
     using L = TcLayout<BN, MT, SA, S16, S8, SPLIT, Q4K>;
     static_assert(!Q4K || !BF16, "Q4_K operands are fp16");
     pdl_trigger();
@@ -483,6 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(mt * L::NB * BN);
 #pragma unroll 1
                 for (int cg = half * 32; cg < BN; cg += 64) {
+                    if (!SPLIT && pe.enabled && n0 + cg < pe.qkv) continue;  // fused preprocessing below
                     uint32_t v[32];
                     tmem_load_32x32b_x32(tbase + (uint32_t)cg, v);
                     if (SPLIT) {
@@ -516,6 +633,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                 }
             }
+        }
+        if constexpr (!SPLIT) {
+            static_assert(SPLIT || (uint32_t)MT * BM * 132 * 4 <= L::B8_OFF, "preprocessing stage fits the rings");
+            if (pe.enabled)
+                prep_epilogue<BN, MT>(pe, reinterpret_cast<float*>(smem), tmem, n0, m0, (int)blockIdx.y, warp, lane, ok);
         }
     }
 
@@ -674,7 +796,8 @@ struct ALayout {
 
 template <int BN, int MT, int SA, int S16, int S8, bool BF16, bool SPLIT, bool Q4K = false>
 int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* a, int64_t m, float* out,
-           int64_t ld_out, int splits, int kt_per, const ALayout& al, cudaStream_t s) {
+           int64_t ld_out, int splits, int kt_per, const ALayout& al, cudaStream_t s,
+           const PrepEpilogue& pe = PrepEpilogue()) {
     using L = TcLayout<BN, MT, SA, S16, S8, SPLIT, Q4K>;
     CUtensorMap ma, mb;
     const CUtensorMapDataType adt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -705,7 +828,7 @@ int run_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void
     GDN_CUDA(cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM));
     const dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM * MT - 1) / (BM * MT)), (unsigned)splits);
     return launch_pdl("q8_0_gemm_tc_kernel", kern, grid, dim3(kThreads), L::SMEM, s, ma, mb, am, d, (int)n, (int)k,
-                      (int)m, out, ld_out, kt_per, (int)al.blk_k, (int)al.row0, device_error_word());
+                      (int)m, out, ld_out, kt_per, (int)al.blk_k, (int)al.row0, pe, device_error_word());
 }
 
 }  // namespace
@@ -753,6 +876,8 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
     // Ring depths <SA, S16, S8> fill ~224 KB of shared memory.
     if (opt.split_precision && a_bf16)
         return fail(GDN_ERR_TYPE, "split-precision tensor-core GEMM takes fp16 activations");
+    if (opt.split_precision && opt.prep != nullptr && opt.prep->enabled)
+        return fail(GDN_ERR_ARG, "fused preprocessing runs on the single-operand GEMM only");
     ALayout al;
     if (opt.a_nblocks > 0) {
         if (opt.a_nblocks > kMaxABlocks || opt.a_block_ptrs == nullptr || opt.a_blk_k * opt.a_nblocks != k)
@@ -789,14 +914,24 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
         // as the grid still covers at least half of the SMs.
         const int64_t tiles256 = (n + 255) / 256 * ((m + 2 * BM - 1) / (2 * BM)) * splits;
         const bool wide = two && tiles256 * 2 >= sm_count();
+        PrepEpilogue pe;
+        if (opt.prep != nullptr && opt.prep->enabled) {
+            const PrepEpilogue& p = *opt.prep;
+            if (splits != 1 || p.qkv <= 0 || p.qkv % 128 != 0 || p.qkv > n || p.hk < 0 || 2 * p.hk * 128 > p.qkv ||
+                p.T != m || p.Tp < m || !p.qn || !p.kn || !p.vb || !p.edge || !p.win ||
+                (p.conv_w && !aligned(p.conv_w, 16)))
+                return fail(GDN_ERR_ARG, "fused preprocessing: inconsistent options");
+            opt.prep->rows = two ? 2 * BM : BM;
+            pe = *opt.prep;
+        }
         if (a_bf16) {
-            st = !two ? run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
-                 : wide ? run_tc<256, 2, 3, 3, 2, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
-                        : run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
+            st = !two ? run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                 : wide ? run_tc<256, 2, 3, 3, 2, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                        : run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe);
         } else {
-            st = !two ? run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
-                 : wide ? run_tc<256, 2, 3, 3, 2, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s)
-                        : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s);
+            st = !two ? run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                 : wide ? run_tc<256, 2, 3, 3, 2, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                        : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe);
         }
     }
     if (st || splits == 1) return st;

@@ -55,17 +55,6 @@ constexpr int LDH = HD + 8;             // padded smem row (bf16 elements) of 12
 constexpr int LDC = CH + 8;             // ... of 64-wide tiles
 constexpr int LDV = BV + 8;             // ... of BV-wide tiles
 
-__device__ __forceinline__ float tanh_hw(float x) {
-    float y;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-// SiLU(x) = x sigmoid(x) = x (1 + tanh(x / 2)) / 2: one special-function op.
-__device__ __forceinline__ float silu_fast(float x) {
-    const float h = 0.5f * x;
-    return fmaf(h, tanh_hw(h), h);
-}
-
 struct PDims {
     int hk, hv, key, inner, qkv;
     int64_t np, ldp, T, Tp, nc;
@@ -100,6 +89,8 @@ struct PWork {
     bf16* sc;         // [Hv][nc][128][128] state at each chunk start
     bf16* dl;         // [Hv][Tp][128] chunk deltas D
     __half* gated;    // [T][inner] out_proj operand
+    float* edge;      // [ceil(T / 128)][6][qkv] raw rows at the M-tile edges (fused preprocessing)
+    float* win;       // [4][qkv] raw rows T-4..T-1 (fused preprocessing)
     size_t total;
 };
 
@@ -133,6 +124,8 @@ PWork pcarve(const gdn_dims& d, int64_t T, void* base) {
     w.sc = reinterpret_cast<bf16*>(take((size_t)D.nc * D.hv * HD * HD * 2));
     w.dl = reinterpret_cast<bf16*>(take(kv * D.hv));
     w.gated = reinterpret_cast<__half*>(take((size_t)T * D.inner * 2));
+    w.edge = reinterpret_cast<float*>(take((size_t)((T + 127) / 128) * 6 * D.qkv * 4));
+    w.win = reinterpret_cast<float*>(take((size_t)4 * D.qkv * 4));
     w.total = off;
     return w;
 }
@@ -165,6 +158,47 @@ PWork pcarve(const gdn_dims& d, int64_t T, void* base) {
 // and beta = stable sigmoid (260).
 constexpr int kTokBlock = 16;
 
+// Gates of all value heads for tokens tb .. tb + ntok - 1 (one warp; lane = head).
+template <int ntok>
+__device__ __forceinline__ void gate_block(const float* __restrict__ proj, int64_t ldp, int64_t T, int64_t tb,
+                                           int64_t Tp, const float* __restrict__ ssm_a,
+                                           const float* __restrict__ dt_bias, float* __restrict__ glog,
+                                           float* __restrict__ beta, int qkv, int hv, int lane) {
+    const int64_t gate0 = (int64_t)qkv + (int64_t)hv * HD;
+    for (int h = lane; h < hv; h += 32) {
+        const float sa = ssm_a != nullptr ? ssm_a[h] : 0.0f;
+        const float db = dt_bias != nullptr ? dt_bias[h] : 0.0f;
+#pragma unroll 4
+        for (int64_t t = tb; t < tb + ntok; t++) {
+            const int64_t i = (int64_t)h * Tp + t;
+            if (t >= T) {
+                glog[i] = 0.0f;
+                beta[i] = 0.0f;
+                continue;
+            }
+            const float* pr = proj + t * ldp + gate0;
+            const float beta_raw = pr[h], alpha_raw = pr[hv + h];
+            float gl = logf(0.99f);
+            if (ssm_a != nullptr && dt_bias != nullptr) {
+                const float x = alpha_raw + db;
+                gl = sa * (log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f));
+                if (isnan(gl)) gl = logf(0.99f);
+                gl = fminf(gl, 0.0f);
+            }
+            glog[i] = fmaxf(gl, kLogDecayMin);
+            float bt;
+            if (beta_raw >= 0.0f) {
+                bt = 1.0f / (1.0f + expf(-beta_raw));
+            } else {
+                const float z = expf(beta_raw);
+                bt = z / (1.0f + z);
+            }
+            beta[i] = bt;
+        }
+    }
+}
+
+
 __global__ void __launch_bounds__(256, 2) prefill_prep_kernel(const float* __restrict__ proj, int64_t ldp, int64_t T,
                                                            int64_t Tp, float* __restrict__ conv_buf,
                                                            const int32_t* __restrict__ conv_pos,
@@ -184,38 +218,7 @@ __global__ void __launch_bounds__(256, 2) prefill_prep_kernel(const float* __res
     const int64_t tb = (gw / nchunk) * kTokBlock;
 
     if (hc == nchunk - 1) {  // ---- gates of all heads for this token block
-        const int64_t gate0 = (int64_t)qkv + (int64_t)hv * HD;
-        for (int h = lane; h < hv; h += 32) {
-            const float sa = ssm_a != nullptr ? ssm_a[h] : 0.0f;
-            const float db = dt_bias != nullptr ? dt_bias[h] : 0.0f;
-#pragma unroll 4
-            for (int64_t t = tb; t < tb + kTokBlock; t++) {
-                const int64_t i = (int64_t)h * Tp + t;
-                if (t >= T) {
-                    glog[i] = 0.0f;
-                    beta[i] = 0.0f;
-                    continue;
-                }
-                const float* pr = proj + t * ldp + gate0;
-                const float beta_raw = pr[h], alpha_raw = pr[hv + h];
-                float gl = logf(0.99f);
-                if (ssm_a != nullptr && dt_bias != nullptr) {
-                    const float x = alpha_raw + db;
-                    gl = sa * (log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f));
-                    if (isnan(gl)) gl = logf(0.99f);
-                    gl = fminf(gl, 0.0f);
-                }
-                glog[i] = fmaxf(gl, kLogDecayMin);
-                float bt;
-                if (beta_raw >= 0.0f) {
-                    bt = 1.0f / (1.0f + expf(-beta_raw));
-                } else {
-                    const float z = expf(beta_raw);
-                    bt = z / (1.0f + z);
-                }
-                beta[i] = bt;
-            }
-        }
+        gate_block<kTokBlock>(proj, ldp, T, tb, Tp, ssm_a, dt_bias, glog, beta, qkv, hv, lane);
         return;
     }
 
@@ -289,6 +292,111 @@ __global__ void __launch_bounds__(256, 2) prefill_prep_kernel(const float* __res
     for (int j = 0; j < kTokBlock; j++) {
         const int64_t t = tb + j;
         const uint2 v = t < T ? make_uint2(wmma16::pack_bf16(x[j].x, x[j].y), wmma16::pack_bf16(x[j].z, x[j].w))
+                              : make_uint2(0u, 0u);
+        *reinterpret_cast<uint2*>(dst + t * HD) = v;
+    }
+}
+
+// ----------------------------------------------------------------- edges
+//
+// The prep kernel's remainder when the input projection's epilogue has done
+// conv1d + SiLU + L2 for rows 3.. of every M tile (PrepEpilogue): warps per
+// (tile j, 128-channel chunk hc) finish the tile's rows 0..2 -- their conv
+// reads the raw rows above them from the previous tile's edge rows, or for
+// tile 0 from the conv window of the state -- and the warps of tile 0 then
+// write the window after the prompt from `win`; plus one gate warp per
+// kGateTok tokens.  Same arithmetic as the prep kernel, row for row.
+constexpr int kGateTok = 4;
+__global__ void __launch_bounds__(256) prefill_edge_kernel(const float* __restrict__ edge,
+                                                           const float* __restrict__ win, int rows, int64_t ntiles,
+                                                           const float* __restrict__ proj, int64_t ldp, int64_t T,
+                                                           int64_t Tp, float* __restrict__ conv_buf,
+                                                           const int32_t* __restrict__ conv_pos,
+                                                           const float* __restrict__ conv_w, bf16* __restrict__ qn,
+                                                           bf16* __restrict__ kn, bf16* __restrict__ vb,
+                                                           const float* __restrict__ ssm_a,
+                                                           const float* __restrict__ dt_bias,
+                                                           float* __restrict__ glog, float* __restrict__ beta,
+                                                           int qkv, int hk, int hv) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int nchunk = qkv / HD;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t n_gate = Tp / kGateTok;  // gate warps first: theirs is the longest chain
+    if (gw < n_gate) {
+        gate_block<kGateTok>(proj, ldp, T, gw * kGateTok, Tp, ssm_a, dt_bias, glog, beta, qkv, hv, lane);
+        return;
+    }
+    if (gw >= n_gate + ntiles * nchunk) return;
+    const int64_t j = (gw - n_gate) / nchunk;
+    const int hc = (int)((gw - n_gate) % nchunk);
+    const int ch = hc * HD + 4 * lane;
+    const int64_t t0 = j * rows;
+    const bool conv = conv_buf != nullptr && conv_w != nullptr;
+    float4 x[3], hist[3];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        x[i] = t0 + i < T ? *reinterpret_cast<const float4*>(edge + (j * 6 + i) * qkv + ch) : make_float4(0.f, 0.f, 0.f, 0.f);
+        hist[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (conv) {
+        const int p0 = *conv_pos;
+#pragma unroll
+        for (int i = 0; i < 3; i++)
+            hist[i] = j > 0 ? *reinterpret_cast<const float4*>(edge + ((j - 1) * 6 + 3 + i) * qkv + ch)
+                            : *reinterpret_cast<const float4*>(conv_buf + (int64_t)((p0 + i - 3) & 3) * qkv + ch);
+        if (j == 0) {  // the window after the prompt (the old one is read above, in program order)
+            for (int64_t i = (T > 4 ? T - 4 : 0); i < T; i++)
+                *reinterpret_cast<float4*>(conv_buf + (int64_t)((p0 + (int)i) & 3) * qkv + ch) =
+                    *reinterpret_cast<const float4*>(win + (i - (T - 4)) * qkv + ch);
+        }
+        float4 wv[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++) wv[c] = reinterpret_cast<const float4*>(conv_w)[ch + c];
+        float4 o[3];
+#pragma unroll
+        for (int i = 0; i < 3; i++) {
+            const float4 r0 = i >= 3 ? x[0] : hist[i];
+            const float4 r1 = i >= 2 ? x[i - 2] : hist[i + 1];
+            const float4 r2 = i >= 1 ? x[i - 1] : hist[i + 2];
+            const float h0[4] = {r0.x, r0.y, r0.z, r0.w}, h1[4] = {r1.x, r1.y, r1.z, r1.w};
+            const float h2[4] = {r2.x, r2.y, r2.z, r2.w}, in[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
+            float v[4];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float4 w = wv[c];
+                float sum = w.x * h0[c];
+                sum = fmaf(w.y, h1[c], sum);
+                sum = fmaf(w.z, h2[c], sum);
+                sum = fmaf(w.w, in[c], sum);
+                v[c] = silu_fast(sum);
+            }
+            o[i] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+#pragma unroll
+        for (int i = 0; i < 3; i++) x[i] = o[i];
+    }
+    if (hc < 2 * hk) {
+#pragma unroll
+        for (int i = 0; i < 3; i++) {
+            float ss = fmaf(x[i].x, x[i].x, fmaf(x[i].y, x[i].y, fmaf(x[i].z, x[i].z, x[i].w * x[i].w)));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = ss > 1e-4f ? rsqrtf(ss) : 1.0f / (sqrtf(ss) + 1e-6f);
+            x[i] = make_float4(x[i].x * inv, x[i].y * inv, x[i].z * inv, x[i].w * inv);
+        }
+    }
+    bf16* dst;
+    if (hc < hk) dst = qn + (int64_t)hc * Tp * HD;
+    else if (hc < 2 * hk) dst = kn + (int64_t)(hc - hk) * Tp * HD;
+    else dst = vb + (int64_t)(hc - 2 * hk) * Tp * HD;
+    dst += 4 * lane;
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const int64_t t = t0 + i;
+        if (t >= Tp) break;
+        const uint2 v = t < T ? make_uint2(wmma16::pack_bf16(x[i].x, x[i].y), wmma16::pack_bf16(x[i].z, x[i].w))
                               : make_uint2(0u, 0u);
         *reinterpret_cast<uint2*>(dst + t * HD) = v;
     }
@@ -972,6 +1080,7 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
 
     // ---- input projection -> proj [T][ldp]
     if ((st = phase_mark(0, s))) return st;
+    PrepEpilogue prep;  // Q8_0: the preprocessing runs in the projection's epilogue
     if (L->weight_type == GDN_GGML_Q4_K) {
         if (T >= 8 && x_dtype != GDN_DTYPE_F32) {  // tensor cores, exact weights, fp16 x (bf16 converts exactly)
             const void* a = x;
@@ -991,7 +1100,19 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
             a = W.xconv;
         }
         const int64_t n_main = (int64_t)D.qkv + D.inner;
-        TcOptions fast;  // q, k, v, z rows: one fp16 weight operand
+        TcOptions fast;  // q, k, v, z rows: one fp16 weight operand; conv1d, SiLU, L2 in its epilogue
+        prep.enabled = 1;
+        prep.qkv = D.qkv;
+        prep.hk = D.hk;
+        prep.T = T;
+        prep.Tp = D.Tp;
+        prep.conv_w = conv ? L->conv1d_w : nullptr;
+        prep.qn = W.qn;
+        prep.kn = W.kn;
+        prep.vb = W.vb;
+        prep.edge = W.edge;
+        prep.win = W.win;
+        fast.prep = &prep;
         if ((st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_main, hidden, a, false, T, W.proj, D.ldp, fast, s)))
             return st;
         const int8_t* gq = L->in_qs + n_main * hidden;
@@ -1012,7 +1133,15 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
 
     // ---- conv1d + SiLU + L2 norm, gates, window hand-off
     if ((st = phase_mark(1, s))) return st;
-    {
+    if (prep.enabled) {
+        const int64_t ntiles = (T + prep.rows - 1) / prep.rows;
+        const int64_t warps = ntiles * (D.qkv / HD) + D.Tp / kGateTok;
+        st = launch_pdl("prefill_edge_kernel", prefill_edge_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s,
+                        (const float*)W.edge, (const float*)W.win, prep.rows, ntiles, (const float*)W.proj, D.ldp, T,
+                        D.Tp, conv ? conv_buf : nullptr, (const int32_t*)conv_pos, conv ? L->conv1d_w : nullptr,
+                        W.qn, W.kn, W.vb, L->ssm_a, L->dt_bias, W.glog, W.beta, D.qkv, D.hk, D.hv);
+        if (st) return st;
+    } else {
         const int64_t warps = (D.Tp / kTokBlock) * (D.qkv / HD + 1);
         st = launch_pdl("prefill_prep_kernel", prefill_prep_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0,
                         s, W.proj, D.ldp, T, D.Tp, conv ? conv_buf : nullptr, conv_pos,

@@ -21,6 +21,25 @@ int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t co
 int launch_q4_k_gemv(const void* blocks, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
                      int64_t ldy, cudaStream_t s);
 
+// Prefill preprocessing fused into the tensor-core GEMM's epilogue (the single
+// fp16-operand path): output columns [0, qkv) are the q, k, v channels of the
+// input projection, 128 per head (heads 0..hk-1 q, hk..2hk-1 k, then v).  For
+// each M tile of `rows` tokens, rows 3.. leave as conv1d + SiLU (+ L2 norm for q
+// and k) in bf16 [head][Tp][128]; rows 0..2 need the previous tile's raw rows and
+// are finished by the prefill's edge kernel from `edge` (per tile: raw rows 0..2
+// and rows-3..rows-1).  Raw rows T-4..T-1 go to `win` (the next conv window).
+// Columns >= qkv take the plain fp32 epilogue.
+struct PrepEpilogue {
+    int enabled = 0;
+    int qkv = 0, hk = 0;
+    int rows = 0;                  // set by the launcher: tokens per M tile (128 or 256)
+    int64_t T = 0, Tp = 0;         // tokens, and rows of the bf16 outputs (T rounded up; zeros past T)
+    const float* conv_w = nullptr; // [qkv][4], or none: no conv, no SiLU
+    __nv_bfloat16 *qn = nullptr, *kn = nullptr, *vb = nullptr;
+    float* edge = nullptr;         // [ceil(T / rows)][6][qkv]
+    float* win = nullptr;          // [4][qkv]: raw row t at slot t - (T - 4)
+};
+
 // Options of the tensor-core GEMM.
 struct TcOptions {
     bool split_precision = false;  // weights as hi + lo operands (two MMAs): fp32-GEMV accuracy
@@ -34,6 +53,7 @@ struct TcOptions {
     // NVLink, each [a_rows][a_blk_k]): a_block_ptrs[k / a_blk_k], a_nblocks <= 8
     const void* const* a_block_ptrs = nullptr;
     int a_nblocks = 0;
+    PrepEpilogue* prep = nullptr;  // single-operand path only; `rows` is filled in
 };
 size_t gemm_tc_workspace_bytes(int64_t m, int64_t n, int splits);
 
