@@ -93,6 +93,16 @@ __device__ __forceinline__ float silu_fast(float x) {
     return fmaf(h, tanh_hw(h), h);
 }
 
+// 1 / (sqrt(ss) + 1e-6), the L2 normalisation of q and k (deltanet_impl.h:89),
+// branch-free: above ss = 1e-4 the epsilon moves the result by under 1e-4
+// relative and one rsqrt is as good; below it sqrt(ss) = ss rsqrt(ss) (0 at 0)
+// and a fast reciprocal, within a few ulp of the exact expression.
+__device__ __forceinline__ float inv_l2(float ss) {
+    const float r = rsqrtf(ss);
+    const float root = ss > 0.0f ? ss * r : 0.0f;
+    return ss > 1e-4f ? r : __fdividef(1.0f, root + 1e-6f);
+}
+
 // Spin limit of bounded waits, in SM clock cycles (~1 s at 1.9 GHz).
 constexpr long long kWaitCycles = 2000000000LL;
 

@@ -265,48 +265,80 @@ __device__ __forceinline__ void prep_epilogue(const PrepEpilogue& pe, float* S, 
                 wv[i] = conv ? __ldg(reinterpret_cast<const float4*>(pe.conv_w) + ch + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             const int r0 = wi * RC;
             const float* col = S + c4;
-            // One pass over the warp's rows with a branch-free body (rows in flight
-            // overlap): rows 0..2 of the tile, whose window lies in the previous
-            // tile, are computed from clamped rows and not stored (the edge kernel's).
+            // One pass over the warp's rows, eight at a time, with a branch-free body:
+            // rows 0..2 of the tile, whose window lies in the previous tile, are
+            // computed from clamped rows and not stored (the edge kernel's).  SiLU's
+            // 1/2 is folded into the taps (exact: a power of two), and for q and k
+            // the eight rows' sums of squares over the 32 lanes share one exchange
+            // that halves the values each lane holds at every step.
+            float4 w2[4];
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                w2[c] = make_float4(0.5f * wv[c].x, 0.5f * wv[c].y, 0.5f * wv[c].z, 0.5f * wv[c].w);
             auto rows = [&](auto l2_tag, auto conv_tag) {
                 constexpr bool L2 = decltype(l2_tag)::value, CONV = decltype(conv_tag)::value;
                 float4 h0 = *reinterpret_cast<const float4*>(col + max(r0 - 3, 0) * SP);
                 float4 h1 = *reinterpret_cast<const float4*>(col + max(r0 - 2, 0) * SP);
                 float4 h2 = *reinterpret_cast<const float4*>(col + max(r0 - 1, 0) * SP);
-#pragma unroll 8
-                for (int i = 0; i < RC; i++) {
-                    const float4 x = *reinterpret_cast<const float4*>(col + (r0 + i) * SP);
-                    float o[4] = {x.x, x.y, x.z, x.w};
-                    if constexpr (CONV) {
-                        const float a0[4] = {h0.x, h0.y, h0.z, h0.w}, a1[4] = {h1.x, h1.y, h1.z, h1.w};
-                        const float a2[4] = {h2.x, h2.y, h2.z, h2.w};
+#pragma unroll 1
+                for (int g = 0; g < RC; g += 8) {
+                    float o[8][4], ss[8];
 #pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            float sum = wv[c].x * a0[c];
-                            sum = fmaf(wv[c].y, a1[c], sum);
-                            sum = fmaf(wv[c].z, a2[c], sum);
-                            sum = fmaf(wv[c].w, o[c], sum);
-                            o[c] = silu_fast(sum);
+                    for (int i = 0; i < 8; i++) {
+                        const float4 x = *reinterpret_cast<const float4*>(col + (r0 + g + i) * SP);
+                        o[i][0] = x.x;
+                        o[i][1] = x.y;
+                        o[i][2] = x.z;
+                        o[i][3] = x.w;
+                        if constexpr (CONV) {
+                            const float a0[4] = {h0.x, h0.y, h0.z, h0.w}, a1[4] = {h1.x, h1.y, h1.z, h1.w};
+                            const float a2[4] = {h2.x, h2.y, h2.z, h2.w};
+#pragma unroll
+                            for (int c = 0; c < 4; c++) {
+                                float hh = w2[c].x * a0[c];  // (w . window) / 2
+                                hh = fmaf(w2[c].y, a1[c], hh);
+                                hh = fmaf(w2[c].z, a2[c], hh);
+                                hh = fmaf(w2[c].w, o[i][c], hh);
+                                o[i][c] = fmaf(hh, tanh_hw(hh), hh);  // SiLU
+                            }
+                        }
+                        h0 = h1;
+                        h1 = h2;
+                        h2 = x;
+                        ss[i] = fmaf(o[i][0], o[i][0], fmaf(o[i][1], o[i][1], fmaf(o[i][2], o[i][2], o[i][3] * o[i][3])));
+                    }
+                    if constexpr (L2) {
+                        // after the xor-16, -8, -4 halvings and two butterflies lane l holds
+                        // row (l >> 2) & 7's sum in ss[0]
+#pragma unroll
+                        for (int st = 16, nv = 8; st >= 4; st >>= 1, nv >>= 1) {
+                            const bool up = (lane & st) != 0;
+#pragma unroll
+                            for (int i = 0; i < nv / 2; i++) {
+                                const float send = up ? ss[i] : ss[i + nv / 2];
+                                const float keep = up ? ss[i + nv / 2] : ss[i];
+                                ss[i] = keep + __shfl_xor_sync(0xffffffffu, send, st);
+                            }
+                        }
+                        ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], 2);
+                        ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], 1);
+                        const float inv_mine = inv_l2(ss[0]);
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float inv = __shfl_sync(0xffffffffu, inv_mine, 4 * i);
+#pragma unroll
+                            for (int c = 0; c < 4; c++) o[i][c] *= inv;
                         }
                     }
-                    h0 = h1;
-                    h1 = h2;
-                    h2 = x;
-                    if constexpr (L2) {
-                        // the row's sum of squares over the 32 lanes (128 columns);
-                        // 1 / (sqrt(ss) + 1e-6) (deltanet_impl.h:89) as the prep kernel has it
-                        float ss = fmaf(o[0], o[0], fmaf(o[1], o[1], fmaf(o[2], o[2], o[3] * o[3])));
 #pragma unroll
-                        for (int sh = 16; sh > 0; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
-                        const float inv = ss > 1e-4f ? rsqrtf(ss) : 1.0f / (sqrtf(ss) + 1e-6f);
-#pragma unroll
-                        for (int c = 0; c < 4; c++) o[c] *= inv;
+                    for (int i = 0; i < 8; i++) {
+                        const int64_t t = m0 + r0 + g + i;
+                        __nv_bfloat162 a = __floats2bfloat162_rn(o[i][0], o[i][1]);
+                        __nv_bfloat162 b = __floats2bfloat162_rn(o[i][2], o[i][3]);
+                        uint2 val = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+                        if (t >= pe.T) val = make_uint2(0u, 0u);
+                        if (r0 + g + i >= 3 && t < pe.Tp) *reinterpret_cast<uint2*>(dst + t * 128) = val;
                     }
-                    const int64_t t = m0 + r0 + i;
-                    __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]), b = __floats2bfloat162_rn(o[2], o[3]);
-                    uint2 val = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-                    if (t >= pe.T) val = make_uint2(0u, 0u);
-                    if (r0 + i >= 3 && t < pe.Tp) *reinterpret_cast<uint2*>(dst + t * 128) = val;
                 }
             };
             using T1 = std::true_type;

@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(256, 2) prefill_prep_kernel(const float* __res
         for (int j = 0; j < kTokBlock; j++) {
             // 1 / (sqrt(ss) + 1e-6) (deltanet_impl.h:89): the epsilon shifts the result by
             // 1e-6 / sqrt(ss) relative, so above ss = 1e-4 one rsqrt is as good
-            const float inv = ss[j] > 1e-4f ? rsqrtf(ss[j]) : 1.0f / (sqrtf(ss[j]) + 1e-6f);
+            const float inv = inv_l2(ss[j]);
             x[j] = make_float4(x[j].x * inv, x[j].y * inv, x[j].z * inv, x[j].w * inv);
         }
     }
@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(256) prefill_edge_kernel(const float* __restri
             float ss = fmaf(x[i].x, x[i].x, fmaf(x[i].y, x[i].y, fmaf(x[i].z, x[i].z, x[i].w * x[i].w)));
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float inv = ss > 1e-4f ? rsqrtf(ss) : 1.0f / (sqrtf(ss) + 1e-6f);
+            const float inv = inv_l2(ss);
             x[i] = make_float4(x[i].x * inv, x[i].y * inv, x[i].z * inv, x[i].w * inv);
         }
     }
