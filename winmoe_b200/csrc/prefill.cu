@@ -1048,6 +1048,36 @@ int set_smem(K kern, size_t bytes) {
 
 size_t prefill_workspace_bytes(const gdn_dims& d, int64_t T) { return pcarve(d, T, nullptr).total; }
 
+namespace {
+
+// A highest-priority stream per host thread and device, with fork / join events.
+// The prefill's input projection (hundreds of one-per-SM CTAs, a partly empty
+// last wave) runs there; the gate rows, on the caller's stream meanwhile, get
+// only the SMs it leaves idle -- its last wave -- instead of running after it.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+int side_stream(SideStream** out) {
+    thread_local SideStream tls[16];
+    int dev = 0;
+    GDN_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 16) return fail(GDN_ERR_CUDA, "device index %d out of range", dev);
+    SideStream& r = tls[dev];
+    if (r.s == nullptr) {
+        int least = 0, greatest = 0;
+        GDN_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+        GDN_CUDA(cudaEventCreateWithFlags(&r.fork, cudaEventDisableTiming));
+        GDN_CUDA(cudaEventCreateWithFlags(&r.join, cudaEventDisableTiming));
+        GDN_CUDA(cudaStreamCreateWithPriority(&r.s, cudaStreamNonBlocking, greatest));
+    }
+    *out = &r;
+    return GDN_OK;
+}
+
+}  // namespace
+
 int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, const RowDest* gated_out,
             float* S, float* conv_buf, int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s) {
     int st = validate_layer(L);
@@ -1113,8 +1143,16 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
         prep.edge = W.edge;
         prep.win = W.win;
         fast.prep = &prep;
-        if ((st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_main, hidden, a, false, T, W.proj, D.ldp, fast, s)))
+        SideStream* side = nullptr;
+        if ((st = side_stream(&side))) return st;
+        GDN_CUDA(cudaEventRecord(side->fork, s));
+        GDN_CUDA(cudaStreamWaitEvent(side->s, side->fork, 0));
+        st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_main, hidden, a, false, T, W.proj, D.ldp, fast, side->s);
+        GDN_CUDA(cudaEventRecord(side->join, side->s));
+        if (st) {
+            (void)cudaStreamWaitEvent(s, side->join, 0);
             return st;
+        }
         const int8_t* gq = L->in_qs + n_main * hidden;
         const uint16_t* gd = L->in_d + n_main * (hidden / 32);
         if (x_dtype == GDN_DTYPE_F32) {
@@ -1128,7 +1166,9 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
             exact.workspace_bytes = W.partial_bytes;
             st = launch_q8_0_gemm_tc(gq, gd, 2 * D.hv, hidden, a, false, T, W.proj + n_main, D.ldp, exact, s);
         }
+        const cudaError_t ej = cudaStreamWaitEvent(s, side->join, 0);  // joined on every path
         if (st) return st;
+        if (ej != cudaSuccess) return cuda_status(ej, "prefill: join of the input projection");
     }
 
     // ---- conv1d + SiLU + L2 norm, gates, window hand-off
