@@ -875,15 +875,13 @@ __global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict_
 // (deltanet_impl.h:350-361) and the SiLU(z) gate (364-371) -> fp16 out_proj operand.
 struct OutSmem {
     bf16 q[CH][LDH];
-    bf16 k[CH][LDH];
+    bf16 kd[CH][LDH];  // K for P, then the chunk's deltas D
     bf16 s[HD][LDH];
-    bf16 d[CH][LDH];
-    bf16 p[CH][LDC];
     float G[CH];
     float hn[HD];
 };
 
-__global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__ qn, const bf16* __restrict__ kn,
+__global__ void __launch_bounds__(128, 3) chunk_out_kernel(const bf16* __restrict__ qn, const bf16* __restrict__ kn,
                                                         const bf16* __restrict__ sc, const bf16* __restrict__ dl,
                                                         const float* __restrict__ gcum,
                                                         const float* __restrict__ proj, int64_t ldp,
@@ -904,13 +902,11 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
     {
         const bf16* qc = qn + ((int64_t)g * Tp + t0) * HD;
         const bf16* kc = kn + ((int64_t)g * Tp + t0) * HD;
-        const bf16* dc = dl + ((int64_t)h * Tp + t0) * HD;
         const bf16* s0 = sc + (((int64_t)h * nc + c) * HD) * HD;
         for (int i = tid; i < CH * HD / 8; i += 128) {
             const int r = i / (HD / 8), q = i % (HD / 8);
             wmma16::cp_async16(&sm.q[r][q * 8], qc + r * HD + q * 8);
-            wmma16::cp_async16(&sm.k[r][q * 8], kc + r * HD + q * 8);
-            wmma16::cp_async16(&sm.d[r][q * 8], dc + r * HD + q * 8);
+            wmma16::cp_async16(&sm.kd[r][q * 8], kc + r * HD + q * 8);
         }
         for (int i = tid; i < HD * HD / 8; i += 128) {
             const int r = i / (HD / 8), q = i % (HD / 8);
@@ -933,7 +929,10 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
     }
     wmma16::cp_async_wait<0>();
     __syncthreads();
-    // ---- P = mask(exp(G_i - G_j) Q K^T), only this warp's rows
+    // ---- P = mask(exp(G_i - G_j) Q K^T), only this warp's rows, kept in registers
+    // as the A fragments of P D: the accumulators of n-tiles 2kk and 2kk+1 are,
+    // packed to bf16, the m16k16 fragment of k-block kk.
+    uint32_t pa[CH / 16][4];
     {
         float pacc[CH / 8][4] = {};
 #pragma unroll
@@ -943,7 +942,7 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
 #pragma unroll
             for (int np2 = 0; np2 < CH / 16; np2++) {
                 uint32_t b[4];
-                wmma16::load_b_nk(b, &sm.k[0][0], LDH, 16 * kk, 16 * np2);
+                wmma16::load_b_nk(b, &sm.kd[0][0], LDH, 16 * kk, 16 * np2);
                 wmma16::mma(pacc[2 * np2], a, b[0], b[1]);
                 wmma16::mma(pacc[2 * np2 + 1], a, b[2], b[3]);
             }
@@ -957,11 +956,19 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
                 const int i = (e >> 1) ? rB : rA, jj = j + (e & 1);
                 v[e] = (jj <= i) ? __expf(sm.G[i] - sm.G[jj]) * pacc[n][e] : 0.0f;
             }
-            *reinterpret_cast<uint32_t*>(&sm.p[rA][j]) = wmma16::pack_bf16(v[0], v[1]);
-            *reinterpret_cast<uint32_t*>(&sm.p[rB][j]) = wmma16::pack_bf16(v[2], v[3]);
+            pa[n >> 1][2 * (n & 1)] = wmma16::pack_bf16(v[0], v[1]);
+            pa[n >> 1][2 * (n & 1) + 1] = wmma16::pack_bf16(v[2], v[3]);
         }
     }
-    __syncwarp();
+    __syncthreads();  // every warp is done with K: the deltas take its place, loaded behind Q S0
+    {
+        const bf16* dc = dl + ((int64_t)h * Tp + t0) * HD;
+        for (int i = tid; i < CH * HD / 8; i += 128) {
+            const int r = i / (HD / 8), q = i % (HD / 8);
+            wmma16::cp_async16(&sm.kd[r][q * 8], dc + r * HD + q * 8);
+        }
+        wmma16::cp_async_commit();
+    }
     // ---- O = diag(gam) Q S0 + P D
     float o[HD / 8][4] = {};
 #pragma unroll
@@ -984,16 +991,16 @@ __global__ void __launch_bounds__(128) chunk_out_kernel(const bf16* __restrict__
         o[n][2] *= gamB;
         o[n][3] *= gamB;
     }
+    wmma16::cp_async_wait<0>();
+    __syncthreads();
 #pragma unroll
     for (int kk = 0; kk < CH / 16; kk++) {
-        uint32_t a[4];
-        wmma16::load_a(a, &sm.p[0][0], LDC, 16 * warp, 16 * kk);
 #pragma unroll
         for (int np2 = 0; np2 < HD / 16; np2++) {
             uint32_t b[4];
-            wmma16::load_b_kn(b, &sm.d[0][0], LDH, 16 * kk, 16 * np2);
-            wmma16::mma(o[2 * np2], a, b[0], b[1]);
-            wmma16::mma(o[2 * np2 + 1], a, b[2], b[3]);
+            wmma16::load_b_kn(b, &sm.kd[0][0], LDH, 16 * kk, 16 * np2);
+            wmma16::mma(o[2 * np2], pa[kk], b[0], b[1]);
+            wmma16::mma(o[2 * np2 + 1], pa[kk], b[2], b[3]);
         }
     }
     // ---- scale, per-token RMSNorm over the head, SiLU(z) gate
