@@ -44,8 +44,11 @@ def upload(cfg, t, **kw):
                                     device=DEV, **kw)
 
 
-@pytest.mark.parametrize("T", [1, 3, 63, 64, 65, 130, 256])
+@pytest.mark.parametrize("T", [1, 3, 63, 64, 65, 130, 256, 258, 515])
 def test_prefill_small_dims(T):
+    """Single and multi-tile prompts: the input projection works in 256-token tiles
+    whose rows 0..2 the edge kernel finishes; T = 258 puts the next conv window
+    across two tiles, T = 515 leaves a last tile of edge rows only."""
     cfg = GDNConfig(512, 2, 4, 128)
     t = synth.layer_tensors(cfg, layer=1)
     w = upload(cfg, t)
@@ -60,14 +63,16 @@ def test_prefill_small_dims(T):
     assert int(st.conv_pos.cpu()[0]) == pos_ref == T
 
 
-def test_prefill_from_a_running_state():
-    """Non-zero state and conv window with conv_pos = 5 (the window's slots rotate)."""
+@pytest.mark.parametrize("T", [100, 300])
+def test_prefill_from_a_running_state(T):
+    """Non-zero state and conv window with conv_pos = 5 (the window's slots rotate);
+    T = 300 spans two tiles of the input projection."""
     cfg = GDNConfig(512, 2, 4, 128)
     t = synth.layer_tensors(cfg, layer=2)
     w = upload(cfg, t)
     warm = synth.hidden_states(5, cfg.hidden, seed=50)
     _, S0, cb0, p0 = oracle_run(cfg, t, warm)
-    x = torch.from_numpy(synth.hidden_states(100, cfg.hidden, seed=51)).to(torch.bfloat16)
+    x = torch.from_numpy(synth.hidden_states(T, cfg.hidden, seed=51)).to(torch.bfloat16)
     want, S_ref, cb_ref, pos_ref = oracle_run(cfg, t, x.float().numpy(), S0=S0, cb0=cb0, pos0=p0)
     st = L.DeltaNetState.zeros(cfg, 1, DEV)
     st.S.copy_(torch.from_numpy(S0)[None])
