@@ -596,8 +596,9 @@ def run_ours(args):
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": pre["workload"], "hidden": cfg.hidden, "k_heads": cfg.num_k_heads,
                            "v_heads": cfg.num_v_heads, "head_dim": cfg.head_dim, "weights": "Q8_0 (seeded)"},
-                # per prefill: x -> fp16, in_proj GEMM, gate-row GEMM + split-K sum, prep (+ gates, window),
-                # chunk_local, chunk_scan, chunk_out, out_proj GEMM
+                # per prefill: x -> fp16, in_proj GEMM (with conv1d + SiLU + L2 in its epilogue), gate-row
+                # GEMM + its split-K sum into the gates, edge rows + conv window, chunk_local, chunk_scan,
+                # chunk_out, out_proj GEMM
                 "gpu_launches": 9 * K, "roofline": pre["roofline"], "prefill": pre}
         print(json.dumps(line), flush=True)
         return

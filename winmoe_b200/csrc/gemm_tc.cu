@@ -904,6 +904,8 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
         out = static_cast<float*>(opt.workspace);
         ld_out = n;
     }
+    if (opt.partials_only && (y != opt.workspace || ldy != n))
+        return fail(GDN_ERR_ARG, "partials_only: y must be the workspace with ldy = n");
     // Two M tiles per CTA share each dequantised weight tile once m > 128.
     // Ring depths <SA, S16, S8> fill ~224 KB of shared memory.
     if (opt.split_precision && a_bf16)
@@ -966,7 +968,8 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
                         : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe);
         }
     }
-    if (st || splits == 1) return st;
+    if (opt.splits_used != nullptr) *opt.splits_used = splits;
+    if (st || splits == 1 || opt.partials_only) return st;
     const int64_t cnt = m * n;
     st = launch_pdl("splitk_reduce_kernel", splitk_reduce_kernel, dim3((unsigned)((cnt + 255) / 256)), dim3(256), 0,
                     s, (const float*)out, splits, m, n, y, ldy);

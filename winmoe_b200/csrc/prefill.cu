@@ -52,7 +52,6 @@ constexpr int CH = 64;                  // chunk length
 constexpr int BV = 16;                  // state columns per scan CTA
 constexpr float kLogDecayMin = -110.0f;  // exp() of anything <= this is 0 in fp32
 constexpr int LDH = HD + 8;             // padded smem row (bf16 elements) of 128-wide tiles
-constexpr int LDC = CH + 8;             // ... of 64-wide tiles
 constexpr int LDV = BV + 8;             // ... of BV-wide tiles
 
 struct PDims {
@@ -158,6 +157,26 @@ PWork pcarve(const gdn_dims& d, int64_t T, void* base) {
 // and beta = stable sigmoid (260).
 constexpr int kTokBlock = 16;
 
+// Log decay and beta of one (token, head) from its raw projections, with the
+// reference's clamps (deltanet_impl.h:247-260) in log space.
+__device__ __forceinline__ void gate_values(float beta_raw, float alpha_raw, float sa, float db, bool have_a,
+                                            float& gl_out, float& beta_out) {
+    float gl = logf(0.99f);
+    if (have_a) {
+        const float x = alpha_raw + db;
+        gl = sa * (log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f));
+        if (isnan(gl)) gl = logf(0.99f);
+        gl = fminf(gl, 0.0f);
+    }
+    gl_out = fmaxf(gl, kLogDecayMin);
+    if (beta_raw >= 0.0f) {
+        beta_out = 1.0f / (1.0f + expf(-beta_raw));
+    } else {
+        const float z = expf(beta_raw);
+        beta_out = z / (1.0f + z);
+    }
+}
+
 // Gates of all value heads for tokens tb .. tb + ntok - 1 (one warp; lane = head).
 template <int ntok>
 __device__ __forceinline__ void gate_block(const float* __restrict__ proj, int64_t ldp, int64_t T, int64_t tb,
@@ -177,23 +196,7 @@ __device__ __forceinline__ void gate_block(const float* __restrict__ proj, int64
                 continue;
             }
             const float* pr = proj + t * ldp + gate0;
-            const float beta_raw = pr[h], alpha_raw = pr[hv + h];
-            float gl = logf(0.99f);
-            if (ssm_a != nullptr && dt_bias != nullptr) {
-                const float x = alpha_raw + db;
-                gl = sa * (log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f));
-                if (isnan(gl)) gl = logf(0.99f);
-                gl = fminf(gl, 0.0f);
-            }
-            glog[i] = fmaxf(gl, kLogDecayMin);
-            float bt;
-            if (beta_raw >= 0.0f) {
-                bt = 1.0f / (1.0f + expf(-beta_raw));
-            } else {
-                const float z = expf(beta_raw);
-                bt = z / (1.0f + z);
-            }
-            beta[i] = bt;
+            gate_values(pr[h], pr[hv + h], sa, db, ssm_a != nullptr && dt_bias != nullptr, glog[i], beta[i]);
         }
     }
 }
@@ -297,6 +300,38 @@ __global__ void __launch_bounds__(256, 2) prefill_prep_kernel(const float* __res
     }
 }
 
+// ----------------------------------------------------------------- gates
+//
+// The gate rows' split-K partials part[z][t][2 Hv] (beta rows, then alpha rows)
+// summed in split order -- the additions of splitk_reduce_kernel -- and turned
+// into the log decay and beta of every (head, token) at once: thread per
+// (token, head), zeros for the padding tokens T .. Tp-1.
+__global__ void __launch_bounds__(256) prefill_gate_kernel(const float* __restrict__ part, int splits, int64_t T,
+                                                           int64_t Tp, int hv, const float* __restrict__ ssm_a,
+                                                           const float* __restrict__ dt_bias,
+                                                           float* __restrict__ glog, float* __restrict__ beta) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= Tp * hv) return;
+    const int64_t t = i / hv;
+    const int h = (int)(i % hv);
+    const int64_t o = (int64_t)h * Tp + t;
+    if (t >= T) {
+        glog[o] = 0.0f;
+        beta[o] = 0.0f;
+        return;
+    }
+    const int64_t slice = T * 2 * (int64_t)hv;
+    float braw = 0.0f, araw = 0.0f;
+    for (int z = 0; z < splits; z++) {
+        braw += part[z * slice + t * 2 * hv + h];
+        araw += part[z * slice + t * 2 * hv + hv + h];
+    }
+    const bool have_a = ssm_a != nullptr && dt_bias != nullptr;
+    gate_values(braw, araw, have_a ? ssm_a[h] : 0.0f, have_a ? dt_bias[h] : 0.0f, have_a, glog[o], beta[o]);
+}
+
 // ----------------------------------------------------------------- edges
 //
 // The prep kernel's remainder when the input projection's epilogue has done
@@ -317,13 +352,13 @@ __global__ void __launch_bounds__(256) prefill_edge_kernel(const float* __restri
                                                            const float* __restrict__ ssm_a,
                                                            const float* __restrict__ dt_bias,
                                                            float* __restrict__ glog, float* __restrict__ beta,
-                                                           int qkv, int hk, int hv) {
+                                                           int qkv, int hk, int hv, int with_gates) {
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31;
     const int nchunk = qkv / HD;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int64_t n_gate = Tp / kGateTok;  // gate warps first: theirs is the longest chain
+    const int64_t n_gate = with_gates ? Tp / kGateTok : 0;  // gate warps first: theirs is the longest chain
     if (gw < n_gate) {
         gate_block<kGateTok>(proj, ldp, T, gw * kGateTok, Tp, ssm_a, dt_bias, glog, beta, qkv, hv, lane);
         return;
@@ -1118,6 +1153,7 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     // ---- input projection -> proj [T][ldp]
     if ((st = phase_mark(0, s))) return st;
     PrepEpilogue prep;  // Q8_0: the preprocessing runs in the projection's epilogue
+    bool gates_done = false;
     if (L->weight_type == GDN_GGML_Q4_K) {
         if (T >= 8 && x_dtype != GDN_DTYPE_F32) {  // tensor cores, exact weights, fp16 x (bf16 converts exactly)
             const void* a = x;
@@ -1166,12 +1202,24 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
             // the fp16 copy of fp32 x is rounded: the gate rows stay on fp32 CUDA cores
             st = launch_q8_0_gemv(gq, gd, 2 * D.hv, hidden, x, x_dtype, T, W.proj + n_main, D.ldp, s);
         } else {
-            TcOptions exact;  // beta/alpha rows: exact hi + lo weights (exp(ssm_a * softplus(alpha)) is sensitive)
+            // beta/alpha rows: exact hi + lo weights (exp(ssm_a * softplus(alpha)) is sensitive);
+            // their partials summed straight into the gates, still beside the projection's last wave
+            TcOptions exact;
             exact.split_precision = true;
             exact.splits = kGateSplits;
             exact.workspace = W.partial;
             exact.workspace_bytes = W.partial_bytes;
-            st = launch_q8_0_gemm_tc(gq, gd, 2 * D.hv, hidden, a, false, T, W.proj + n_main, D.ldp, exact, s);
+            exact.partials_only = true;
+            int used = 0;
+            exact.splits_used = &used;
+            st = launch_q8_0_gemm_tc(gq, gd, 2 * D.hv, hidden, a, false, T, W.partial, 2 * D.hv, exact, s);
+            if (!st) {
+                const int64_t n = D.Tp * D.hv;
+                st = launch_pdl("prefill_gate_kernel", prefill_gate_kernel, dim3((unsigned)((n + 255) / 256)),
+                                dim3(256), 0, s, (const float*)W.partial, used, T, D.Tp, D.hv, L->ssm_a, L->dt_bias,
+                                W.glog, W.beta);
+                gates_done = true;
+            }
         }
         const cudaError_t ej = cudaStreamWaitEvent(s, side->join, 0);  // joined on every path
         if (st) return st;
@@ -1182,11 +1230,12 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
     if ((st = phase_mark(1, s))) return st;
     if (prep.enabled) {
         const int64_t ntiles = (T + prep.rows - 1) / prep.rows;
-        const int64_t warps = ntiles * (D.qkv / HD) + D.Tp / kGateTok;
+        const int64_t warps = ntiles * (D.qkv / HD) + (gates_done ? 0 : D.Tp / kGateTok);
         st = launch_pdl("prefill_edge_kernel", prefill_edge_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s,
                         (const float*)W.edge, (const float*)W.win, prep.rows, ntiles, (const float*)W.proj, D.ldp, T,
                         D.Tp, conv ? conv_buf : nullptr, (const int32_t*)conv_pos, conv ? L->conv1d_w : nullptr,
-                        W.qn, W.kn, W.vb, L->ssm_a, L->dt_bias, W.glog, W.beta, D.qkv, D.hk, D.hv);
+                        W.qn, W.kn, W.vb, L->ssm_a, L->dt_bias, W.glog, W.beta, D.qkv, D.hk, D.hv,
+                        gates_done ? 0 : 1);
         if (st) return st;
     } else {
         const int64_t warps = (D.Tp / kTokBlock) * (D.qkv / HD + 1);

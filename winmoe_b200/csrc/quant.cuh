@@ -54,6 +54,11 @@ struct TcOptions {
     const void* const* a_block_ptrs = nullptr;
     int a_nblocks = 0;
     PrepEpilogue* prep = nullptr;  // single-operand path only; `rows` is filled in
+    // Leave the split-K partials [splits][m][n] for the caller to sum (y must then
+    // be `workspace` with ldy = n: with one split the product lands there as
+    // [1][m][n]); the split count used is written to *splits_used.
+    bool partials_only = false;
+    int* splits_used = nullptr;
 };
 size_t gemm_tc_workspace_bytes(int64_t m, int64_t n, int splits);
 
