@@ -690,8 +690,12 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
             *reinterpret_cast<uint32_t*>(d0 + (r0 + gq) * LDV) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
             *reinterpret_cast<uint32_t*>(d0 + (r0 + gq + 8) * LDV) = wmma16::pack_bf16(acc[n][2], acc[n][3]);
         }
+        sm100::fence_proxy_async_smem();  // the staged U' leaves by bulk copy
         product(&sm.k[0][0], sm.sc[0]);
         __syncthreads();  // T and K read by every warp: W' takes T's place, e*K K's
+        if (tid == 0)  // U' is complete: its copy runs while W' and e*K are staged
+            sm100::bulk_store(up + ((int64_t)h * (Tp / CH) + c) * (HD / BV) * (CH * LDV),
+                              sm100::smem_u32(&sm.v[0][0]), (HD / BV) * CH * LDV * 2);
         bf16* wstage = reinterpret_cast<bf16*>(&sm.T[0][0]);
 #pragma unroll
         for (int n = 0; n < 8; n++) {
@@ -723,8 +727,6 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
     __syncthreads();
     if (tid == 0) {
         sm100::bulk_store(wp + ((int64_t)h * Tp + t0) * LDH, sm100::smem_u32(&sm.T[0][0]), CH * LDH * 2);
-        sm100::bulk_store(up + ((int64_t)h * (Tp / CH) + c) * (HD / BV) * (CH * LDV), sm100::smem_u32(&sm.v[0][0]),
-                          (HD / BV) * CH * LDV * 2);
         sm100::bulk_store(ek + ((int64_t)h * Tp + t0) * LDH, sm100::smem_u32(&sm.k[0][0]), CH * LDH * 2);
         sm100::bulk_commit();
         sm100::bulk_wait_read_all();
