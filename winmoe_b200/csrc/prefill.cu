@@ -506,29 +506,36 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
     wmma16::cp_async_wait<0>();
     __syncthreads();
 
-    // ---- L = mask(b_i exp(G_i - G_j) K K^T): warp -> (m tile warp%4, n tiles 4*(warp/4) .. +3)
+    // ---- L = mask(b_i exp(G_i - G_j) K K^T), the 20 n8 tiles on or below the
+    // diagonal blocks only (nothing reads the upper blocks): warp w takes m tile
+    // mt(w) and n8 tiles n0(w) .. n0(w) + cnt(w) - 1 (nibble w of the constants),
+    // at most three each -- 3,3,2 of m tile 3, 3,3 of m tile 2, 2,2 of 1, 2 of 0.
     {
-        const int mt = warp & 3, nb = (warp >> 2) * 4;
-        float acc[4][4] = {};
+        const int mt = (0x01122333 >> (4 * warp)) & 15;
+        const int nt0 = (0x02030630 >> (4 * warp)) & 15;
+        const int cnt = (0x22233233 >> (4 * warp)) & 15;
+        float acc[3][4] = {};
 #pragma unroll
         for (int kk = 0; kk < HD / 16; kk++) {
             uint32_t a[4];
             wmma16::load_a(a, &sm.k[0][0], LDH, 16 * mt, 16 * kk);
 #pragma unroll
-            for (int np2 = 0; np2 < 2; np2++) {
+            for (int pr = 0; pr < 2; pr++) {  // n8 tiles nt0 + 2 pr, nt0 + 2 pr + 1 (within 0..7)
+                if (2 * pr >= cnt) break;
                 uint32_t b[4];
-                wmma16::load_b_nk(b, &sm.k[0][0], LDH, 16 * kk, 8 * (nb + 2 * np2));
-                wmma16::mma(acc[2 * np2], a, b[0], b[1]);
-                wmma16::mma(acc[2 * np2 + 1], a, b[2], b[3]);
+                wmma16::load_b_nk(b, &sm.k[0][0], LDH, 16 * kk, 8 * (nt0 + 2 * pr));
+                wmma16::mma(acc[2 * pr], a, b[0], b[1]);
+                if (2 * pr + 1 < cnt) wmma16::mma(acc[2 * pr + 1], a, b[2], b[3]);
             }
         }
         const int gq = lane >> 2, qq = lane & 3;
 #pragma unroll
-        for (int n = 0; n < 4; n++) {
+        for (int n = 0; n < 3; n++) {
+            if (n >= cnt) break;
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int i = 16 * mt + gq + ((e >> 1) << 3);
-                const int j = 8 * (nb + n) + 2 * qq + (e & 1);
+                const int j = 8 * (nt0 + n) + 2 * qq + (e & 1);
                 sm.L[i][j] = (j < i) ? sm.beta[i] * __expf(sm.G[i] - sm.G[j]) * acc[n][e] : 0.0f;
             }
         }
