@@ -449,7 +449,7 @@ struct LocalSmem {
     bf16 v[CH][LDH];
     float L[CH][CH + 1];  // strictly lower part: b_i exp(G_i - G_j) k_i . k_j
     float T[CH][CH + 1];  // (I + L)^-1, unit lower triangular
-    float M[3][16][17];   // block products of the inversion stages
+    float M[4][16][17];   // block products of the inversion stages
     float G[CH], beta[CH];
     float sc[2][CH];      // column scales of T: b_j gam_j (for W') and b_j (for U')
 };
@@ -544,8 +544,7 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
 
     // ---- T = (I + L)^-1 (fp32), blocked by 16: the four diagonal blocks by
     // forward substitution (one thread per block column), then the lower
-    // off-diagonal blocks in order of their distance d from the diagonal,
-    //   T_ij = -T_ii sum_{k=j}^{i-1} L_ik T_kj   (i - j = d)
+    // off-diagonal blocks through the 2 x 2 split into 32-row halves (below).
     // (T's upper 16-blocks are never read: nothing clears them.)
     if (tid < CH) {
         // column jc of the block's inverse: col[i] = -sum_{kk<i} L_i,kk col[kk], the
@@ -570,7 +569,7 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
         sm.sc[1][j] = sm.beta[j];
     }
     __syncthreads();
-    // Off-diagonal blocks on the tensor cores, one warp per block of the stage: each
+    // Off-diagonal blocks on the tensor cores, one warp per output block: each
     // 16x16x16 product takes its fp32 operands as hi + lo bf16 pairs (three MMAs:
     // hi.hi + hi.lo + lo.hi, relative error ~2^-17 -- T then enters W' and U' as a
     // 16-bit hi + lo pair itself).  Fragments follow the m16n8k16 layout.
@@ -603,47 +602,67 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
             wmma16::mma(c, ah, bl[0], bl[1]);
             wmma16::mma(c, al, bh[0], bh[1]);
         };
-        for (int d = 1; d < 4; d++) {
-            const int nblk = 4 - d;  // blocks (bj + d, bj), bj = 0 .. nblk - 1
-            if (warp < nblk) {
-                const int bi = warp + d, bj = warp;
-                // M = sum_{kb=bj}^{bi-1} L_{bi,kb} T_{kb,bj}
-                float m[2][4] = {};
-                for (int kb = bj; kb < bi; kb++) {
-                    uint32_t ah[4], al[4];
-                    frag_a(&sm.L[0][0], CH + 1, 16 * bi, 16 * kb, ah, al);
+        // T as 2 x 2 blocks of 32: [[A, 0], [C, B]]^-1 = [[A^-1, 0], [-B^-1 C A^-1, B^-1]].
+        // Stage 1 completes A^-1 and B^-1 (blocks (1,0) and (3,2), one warp each);
+        // stage 2 forms X = C A^-1 (four warps, into M); stage 3 T_C = -B^-1 X (four
+        // warps).  Dependent chains of two block products per stage.
+        auto store_m = [&](int idx, const float (&m)[2][4]) {
 #pragma unroll
-                    for (int nt = 0; nt < 2; nt++) {
-                        uint32_t bh[2], bl[2];
-                        frag_b(&sm.T[0][0], CH + 1, 16 * kb, 16 * bj + 8 * nt, bh, bl);
-                        mma3(m[nt], ah, al, bh, bl);
-                    }
-                }
-#pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
-                    sm.M[warp][gq][8 * nt + 2 * qq] = m[nt][0];
-                    sm.M[warp][gq][8 * nt + 2 * qq + 1] = m[nt][1];
-                    sm.M[warp][gq + 8][8 * nt + 2 * qq] = m[nt][2];
-                    sm.M[warp][gq + 8][8 * nt + 2 * qq + 1] = m[nt][3];
-                }
-                __syncwarp();
-                // T_{bi,bj} = -T_{bi,bi} M
-                uint32_t ah[4], al[4];
-                frag_a(&sm.T[0][0], CH + 1, 16 * bi, 16 * bi, ah, al);
-#pragma unroll
-                for (int nt = 0; nt < 2; nt++) {
-                    uint32_t bh[2], bl[2];
-                    frag_b(&sm.M[warp][0][0], 17, 0, 8 * nt, bh, bl);
-                    float t[4] = {};
-                    mma3(t, ah, al, bh, bl);
-                    sm.T[16 * bi + gq][16 * bj + 8 * nt + 2 * qq] = -t[0];
-                    sm.T[16 * bi + gq][16 * bj + 8 * nt + 2 * qq + 1] = -t[1];
-                    sm.T[16 * bi + gq + 8][16 * bj + 8 * nt + 2 * qq] = -t[2];
-                    sm.T[16 * bi + gq + 8][16 * bj + 8 * nt + 2 * qq + 1] = -t[3];
-                }
+            for (int nt = 0; nt < 2; nt++) {
+                sm.M[idx][gq][8 * nt + 2 * qq] = m[nt][0];
+                sm.M[idx][gq][8 * nt + 2 * qq + 1] = m[nt][1];
+                sm.M[idx][gq + 8][8 * nt + 2 * qq] = m[nt][2];
+                sm.M[idx][gq + 8][8 * nt + 2 * qq + 1] = m[nt][3];
             }
-            __syncthreads();
+        };
+        auto store_t_neg = [&](int bi, int bj, const float (&t)[2][4]) {
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                sm.T[16 * bi + gq][16 * bj + 8 * nt + 2 * qq] = -t[nt][0];
+                sm.T[16 * bi + gq][16 * bj + 8 * nt + 2 * qq + 1] = -t[nt][1];
+                sm.T[16 * bi + gq + 8][16 * bj + 8 * nt + 2 * qq] = -t[nt][2];
+                sm.T[16 * bi + gq + 8][16 * bj + 8 * nt + 2 * qq + 1] = -t[nt][3];
+            }
+        };
+        // the block product acc += X1[r1 / 16, c1 / 16] X2[k0 / 16, n0 / 16] (16 x 16 x 16)
+        auto block_mma = [&](float (&acc)[2][4], const float* X1, int ld1, int r1, int c1, const float* X2, int ld2,
+                             int k0, int n0) {
+            uint32_t ah[4], al[4];
+            frag_a(X1, ld1, r1, c1, ah, al);
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                uint32_t bh[2], bl[2];
+                frag_b(X2, ld2, k0, n0 + 8 * nt, bh, bl);
+                mma3(acc[nt], ah, al, bh, bl);
+            }
+        };
+        const float* Lp = &sm.L[0][0];
+        const float* Tp_ = &sm.T[0][0];
+        if (warp < 2) {  // T_{bi,bj} = -T_{bi,bi} L_{bi,bj} T_{bj,bj}, (bi, bj) = (1,0), (3,2)
+            const int bi = 2 * warp + 1, bj = 2 * warp;
+            float m[2][4] = {};
+            block_mma(m, Lp, CH + 1, 16 * bi, 16 * bj, Tp_, CH + 1, 16 * bj, 16 * bj);
+            store_m(warp, m);
+            __syncwarp();
+            float t[2][4] = {};
+            block_mma(t, Tp_, CH + 1, 16 * bi, 16 * bi, &sm.M[warp][0][0], 17, 0, 0);
+            store_t_neg(bi, bj, t);
         }
+        __syncthreads();
+        const int xi = 2 + (warp >> 1), xj = warp & 1;
+        if (warp < 4) {  // X_{i,j} = sum_{k=j}^{1} L_{i,k} T_{k,j} -> M[warp]
+            float m[2][4] = {};
+            for (int k = xj; k < 2; k++) block_mma(m, Lp, CH + 1, 16 * xi, 16 * k, Tp_, CH + 1, 16 * k, 16 * xj);
+            store_m(warp, m);
+        }
+        __syncthreads();
+        if (warp < 4) {  // T_{i,j} = -sum_{k=2}^{i} T_{i,k} X_{k,j}
+            float t[2][4] = {};
+            for (int k = 2; k <= xi; k++)
+                block_mma(t, Tp_, CH + 1, 16 * xi, 16 * k, &sm.M[2 * (k - 2) + xj][0][0], 17, 0, 0);
+            store_t_neg(xi, xj, t);
+        }
+        __syncthreads();
     }
 
     // ---- U' = (T diag(b)) V, then W' = (T diag(b gam)) K, on the tensor cores:
