@@ -214,7 +214,8 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"
 // 0..2 and the last 3 also to `edge`, rows T-4..T-1 to `win`); then warp w takes
 // rows [w R/8, (w+1) R/8) and lane l columns 4l..4l+3: conv1d over the 3 rows
 // above (a sliding window in registers) + SiLU, in the prep kernel's arithmetic;
-// for q and k the row's L2 norm (a butterfly over the lanes), then bf16 out.
+// for q and k the row's L2 norm (eight rows' sums of squares share one exchange
+// over the lanes), then bf16 out.
 // Both named barriers run on every epilogue warp, `ok` or not.
 template <int BN, int MT>
 __device__ __forceinline__ void prep_epilogue(const PrepEpilogue& pe, float* S, uint32_t tmem, int n0, int64_t m0,
