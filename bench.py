@@ -38,8 +38,24 @@ sys.path.insert(0, str(ROOT))
 METRIC = "gated-DeltaNet tok/s (decode B=256, prefill T=4k); % of HBM/TC roofline"
 BATCH = 256
 # dram__bytes_read.sum + dram__bytes_write.sum of one gdn_state_kernel launch at
-# B = 256, from the ncu capture summarised in profiles/gdn_state_kernel_decode_b256.md.
+# B = 256 (35B-class dims), read from one ncu capture of that launch; the bench
+# cannot count DRAM bytes itself, so the line labels this figure as captured.
 NCU_STATE_TRAFFIC = 549_619_712 + 479_335_680
+NCU_STATE_TRAFFIC_SOURCE = ("ncu capture of one gdn_state_kernel launch at B=256: dram__bytes_read.sum + "
+                            "dram__bytes_write.sum (not measured in this run)")
+
+
+def host_cpu():
+    """Threads the CPU baselines use and the host's CPU model (/proc/cpuinfo)."""
+    model = "unknown"
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)), model
 
 
 def parse():
@@ -272,7 +288,7 @@ def run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, with_cpu):
     if with_cpu:
         dt, kind = cpu_reference_run(cfg, tensors, 64, 1, 0, zero_state=True)
         res["cpu_baseline"] = {"value": 64 / dt, "unit": "tok/s",
-                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)), "kind": kind,
+                               "cores": host_cpu()[0], "cpu_model": host_cpu()[1], "kind": kind,
                                "sample": "the same 64 tokens through the reference's deltanet_forward (unmodified "
                                          "Q8_0/Q8_K dispatch)"}
     return res
@@ -360,7 +376,7 @@ def run_gqa(dev, hbm_peak, peak_src, with_cpu):
                 orc.quant_matvec(w, x, n, kk, 8, 0)
         dt = time.perf_counter() - t0
         res["cpu_baseline"] = {"value": n_cpu / dt, "unit": "tok/s",
-                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                               "cores": host_cpu()[0], "cpu_model": host_cpu()[1],
                                "kind": "reference" if O.ref_available() else "port",
                                "sample": f"{n_cpu} tokens through the reference's quant_matvec (type 8, unmodified "
                                          "Q8_K dispatch) for the four projections"}
@@ -427,7 +443,7 @@ def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
             orc.quant_matvec(t.out_proj, x[i % 2], cfg.hidden, cfg.inner, 12, O.ACT_EXACT)
         dt = time.perf_counter() - t0
         res["cpu_baseline"] = {"value": n / dt, "unit": "tok/s",
-                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                               "cores": host_cpu()[0], "cpu_model": host_cpu()[1],
                                "kind": "reference" if O.ref_available() else "port",
                                "sample": f"{n} tokens through the reference's quant_matvec type 12 (q4k_matvec with "
                                          "Q8_K activations) for the four projections; the reference has no batched "
@@ -510,7 +526,7 @@ def run_stack(cfg, dev, world, rank, steps, warmup, tc_peak, peak_src, with_cpu,
                 x = x + orc.deltanet_forward(cfg, orc.rmsnorm(x, ones), S[l], cb[l], pos[l], tensors[l], act_mode=0)
         dt = time.perf_counter() - t0
         res["cpu_baseline"] = {"value": n_tok * n_layers / dt, "unit": "token-layers/s",
-                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                               "cores": host_cpu()[0], "cpu_model": host_cpu()[1],
                                "kind": "reference" if O.ref_available() else "port",
                                "sample": f"prefix of {n_tok} tokens through layers 0-1 (rmsnorm + the reference's "
                                          "deltanet_forward per token); the GPU figure in the same unit is "
@@ -550,7 +566,7 @@ def run_reference(args):
     dt, kind = cpu_reference_run(cfg, tensors, per_step * args.steps, per_step, 0)
     toks = per_step * args.steps
     v = toks / dt
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    cores, cpu_model = host_cpu()
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
@@ -558,7 +574,7 @@ def run_reference(args):
         "config": {"workload": "decode B=256 (config 2), reference deltanet_forward per sequence-token",
                    "hidden": cfg.hidden, "k_heads": cfg.num_k_heads, "v_heads": cfg.num_v_heads,
                    "head_dim": cfg.head_dim, "weights": "Q8_0"},
-        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "cpu_model": cpu_model, "kind": kind,
                          "sample": f"{per_step} sequence-tokens per step x {args.steps} steps of the B=256 decode "
                                    "workload (prefilled states), engine/runtime/deltanet_impl.h:deltanet_forward "
                                    "with its unmodified Q8_0/Q8_K dispatch, OpenMP over all host threads"},
@@ -724,7 +740,8 @@ def run_ours(args):
         "gpu_launches": 6 * K,
         "roofline": {"bound": "hbm", "kernel": "gdn_state_kernel", "achieved": achieved, "peak": hbm_peak,
                      "unit": "GB/s", "frac": achieved / hbm_peak, "peak_source": peak_src,
-                     "traffic": NCU_STATE_TRAFFIC, "algorithmic_bytes_per_launch": sk_bytes,
+                     "traffic": NCU_STATE_TRAFFIC, "traffic_source": NCU_STATE_TRAFFIC_SOURCE,
+                     "algorithmic_bytes_per_launch": sk_bytes,
                      "launch_ms": state_ms},
         "phases_ms": {"in_proj": float(ph[0]), "prep": float(ph[1]), "state": float(ph[2]),
                       "out_proj": float(ph[3])},
@@ -744,15 +761,15 @@ def run_ours(args):
         line["gqa"] = run_gqa(dev, hbm_peak, peak_src, not args.no_cpu_baseline)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, kind = cpu_reference_run(cfg, tensors, 64, 4, 0)
-        cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+        cores, cpu_model = host_cpu()
         line["cpu_baseline"] = {
-            "value": 64 / dt, "unit": "tok/s", "cores": cores,
+            "value": 64 / dt, "unit": "tok/s", "cores": cores, "cpu_model": cpu_model,
             "kind": kind, "sample": "64 sequence-tokens (4 prefilled sequences x 16 tokens) of the B=256 decode "
                                     "workload through the reference's deltanet_forward, unmodified dispatch"}
         if "prefill" in line:
             dtp, kindp = cpu_reference_run(cfg, tensors, 64, 1, 0)
             line["prefill"]["cpu_baseline"] = {
-                "value": 64 / dtp, "unit": "tok/s", "cores": cores, "kind": kindp,
+                "value": 64 / dtp, "unit": "tok/s", "cores": cores, "cpu_model": cpu_model, "kind": kindp,
                 "sample": "64 consecutive prompt tokens of one sequence through the reference's deltanet_forward "
                           "(the reference has no chunked prefill; tokens go one by one)"}
     if world > 1:

@@ -237,7 +237,8 @@ GDN_API int gdn_decode_step_ex(const gdn_layer* layer, int64_t batch,
  * CPU stack).  Same arguments, results and errors as gdn_decode_step; the
  * scratch is one static device array per device, GDN_NOALLOC_SCRATCH_BYTES
  * long, so batches whose gdn_decode_workspace_size exceeds it are rejected
- * with GDN_ERR_SHAPE (the 35B layer fits up to 47 sequences).
+ * with GDN_ERR_SHAPE (the 35B Q8_0 layer fits up to 63 sequences: its
+ * out_proj split-K partials, needed from 64 on, are reserved only then).
  *   - The first call on each device (with that device current) resolves the
  *     scratch address with cudaGetSymbolAddress; make that first call before
  *     any stream capture.

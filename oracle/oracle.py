@@ -31,10 +31,21 @@ ACT_EXACT, ACT_FP32 = 0, 1
 _vp, _i, _l = C.c_void_p, C.c_int, C.c_long
 
 
+def ref_dir() -> Path | None:
+    """The reference tree whose headers the ref library compiles in place:
+    $REF_DIR, else a `reference` directory beside this repository; None when
+    neither holds engine/runtime/deltanet_impl.h."""
+    env = os.environ.get("REF_DIR")
+    cand = Path(env) if env else HERE.parent.parent / "reference"
+    return cand if (cand / "engine" / "runtime" / "deltanet_impl.h").is_file() else None
+
+
 def build(ref: bool | None = None) -> None:
     """Runs oracle/Makefile (port always; ref when the reference tree exists)."""
     target = [] if ref is None else (["port", "ref"] if ref else ["port"])
-    r = subprocess.run(["make", "-s", "-C", str(HERE), *target], capture_output=True, text=True)
+    rd = ref_dir()
+    args = [f"REF_DIR={rd}"] if rd is not None else []
+    r = subprocess.run(["make", "-s", "-C", str(HERE), *args, *target], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{r.stdout}\n{r.stderr}")
 

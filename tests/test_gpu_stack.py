@@ -104,9 +104,9 @@ def test_add_rmsnorm_broadcast(dtype):
         assert not d[:row0].any() and not d[row0 + T:].any()
 
 
-def _oracle_stack(cfg, tensors, xs):
+def _oracle_stack(cfg, tensors, xs, orc=None):
     """Token by token through every layer: x <- x + deltanet_forward_l(rmsnorm(x)) (ones weight)."""
-    P = O.port()
+    P = orc if orc is not None else O.port()
     n = len(tensors)
     S = [np.zeros((cfg.num_v_heads, 128, 128), np.float32) for _ in range(n)]
     cb = [np.zeros((4, cfg.qkv_dim), np.float32) for _ in range(n)]
@@ -133,6 +133,27 @@ def test_two_layer_stack_matches_oracle():
     x = torch.from_numpy(xs).to(DEV)
     prefill_stack(layers, states, x)
     assert rel_l2(x.cpu().numpy() - xs, want - xs) <= TOL  # the layers' contribution
+
+
+def test_stack_prefix_35b_matches_oracle():
+    """Config 5's oracle prefix: T = 1024 tokens through layers 0 and 1 at the
+    35B-class dims (seeded Q8_0 weights of layers 0 and 1), against the
+    reference's token-by-token recurrence (its deltanet_forward and rmsnorm);
+    the layers' contribution x_out - x_in within the prefill bound."""
+    cfg = DIMS_35B
+    T = 1024
+    tensors = [synth.layer_tensors(cfg, layer=l) for l in range(2)]
+    xs = synth.hidden_states(T, cfg.hidden, seed=0)
+    want = _oracle_stack(cfg, tensors, xs, orc=O.best())
+    layers = [StackLayer.upload(cfg, t, 0, 1, DEV) for t in tensors]
+    states = [lay.state(DEV) for lay in layers]
+    x = torch.from_numpy(xs).to(DEV)
+    prefill_stack(layers, states, x)
+    got = x.cpu().numpy()
+    err = rel_l2(got - xs, want - xs)
+    assert err <= TOL, err
+    worst = max(rel_l2(got[i:i + 64] - xs[i:i + 64], want[i:i + 64] - xs[i:i + 64]) for i in range(0, T, 64))
+    assert worst <= TOL, worst
 
 
 def _nccl_worker(rank, world, port, q):

@@ -153,23 +153,8 @@ int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, 
     cudaStream_t s = as_stream(stream);
     if (x_dtype == GDN_DTYPE_F16 && m >= kQ4kTcMinRows && aligned(x, 16)) {
         // tensor cores, exact weights: the fp32 product of the fp16 activations up to
-        // summation order.  Grids short of the SMs split K (partials in a stream-ordered
-        // allocation, summed in a fixed order).
-        TcOptions opt;
-        const int64_t ctas = (n_rows + 127) / 128 * ((m + 255) / 256);
-        opt.splits = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count() / std::max<int64_t>(ctas, 1), k / 512));
-        void* ws = nullptr;
-        if (opt.splits > 1) {
-            opt.workspace_bytes = gemm_tc_workspace_bytes(m, n_rows, opt.splits);
-            GDN_CUDA(cudaMallocAsync(&ws, opt.workspace_bytes, s));
-            opt.workspace = ws;
-        }
-        const int st = launch_q4_k_gemm_tc(blocks, n_rows, k, x, m, y, n_rows, opt, s);
-        if (ws != nullptr) {
-            const cudaError_t e = cudaFreeAsync(ws, s);
-            if (!st && e != cudaSuccess) return cuda_status(e, "q4_k gemm workspace");
-        }
-        return st;
+        // summation order; one split (no workspace: this entry point allocates nothing)
+        return launch_q4_k_gemm_tc(blocks, n_rows, k, x, m, y, n_rows, TcOptions(), s);
     }
     return launch_q4_k_gemv(blocks, n_rows, k, x, x_dtype, m, y, n_rows, s);
 }
@@ -214,7 +199,7 @@ int gdn_decode_step_noalloc(const gdn_layer* layer, int64_t batch, const void* x
     if (st) return st;
     if (batch <= 0 || batch > 65535)
         return fail(GDN_ERR_SHAPE, "batch must be in [1, 65535] (got %lld)", (long long)batch);
-    const size_t need = decode_workspace_bytes(layer->dims, batch);
+    const size_t need = decode_workspace_bytes_for(*layer, batch);
     if (need > GDN_NOALLOC_SCRATCH_BYTES)
         return fail(GDN_ERR_SHAPE,
                     "gdn_decode_step_noalloc: batch %lld needs %zu bytes of scratch, more than the fixed %zu; "

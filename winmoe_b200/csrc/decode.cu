@@ -192,13 +192,13 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
     // from which every warp forms the whole output row (the RMSNorm needs all 128).
     const float4 hn = head_norm != nullptr ? reinterpret_cast<const float4*>(head_norm)[l]
                                            : make_float4(1.f, 1.f, 1.f, 1.f);
-    bool ok = true;
     for (int i = 0; i < count; i++) {
         const int64_t tile = first + i;
         const int64_t b = tile / hv;
         const int h = (int)(tile % hv);
         StateSlot& sl = sm.slot[i % kStateBufs];
-        ok = ok && sm100::mbar_wait(sm100::smem_u32(&sm.full[i % kStateBufs]), (uint32_t)((i / kStateBufs) & 1), err);
+        const bool landed =
+            sm100::mbar_wait(sm100::smem_u32(&sm.full[i % kStateBufs]), (uint32_t)((i / kStateBufs) & 1), err);
         const float4* Sv = reinterpret_cast<const float4*>(sl.S);
         float4 s[16];
 #pragma unroll
@@ -229,7 +229,18 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
             rp.w = fmaf(kr[r], s[r].w, rp.w);
         }
         reinterpret_cast<float4*>(sm.red[w])[l] = rp;
-        __syncthreads();  // (A)
+        // (A).  A timed-out copy (error word set) stops the CTA here, before this
+        // tile's state or outputs are stored: this tile and the CTA's later ones
+        // keep their state of before the step instead of taking stale slot data.
+        // The decision is block-uniform; thread 0 then waits (bounded) for the
+        // copies still in flight into this CTA's slots before the CTA exits.
+        if (!__syncthreads_and(landed)) {
+            if (t == 0)
+                for (int j = i; j < i + kStateBufs && j < count; j++)
+                    sm100::mbar_wait(sm100::smem_u32(&sm.full[j % kStateBufs]), (uint32_t)((j / kStateBufs) & 1), err);
+            __syncthreads();
+            return;
+        }
         float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int ww = 0; ww < 8; ww++) {
@@ -265,7 +276,7 @@ __global__ void __launch_bounds__(256, 1) gdn_state_kernel(
         // the write-back.)
         sm100::fence_proxy_async_smem();
         __syncthreads();  // (B)
-        if (t == 0 && ok && i + kStateBufs < count) issue(i + kStateBufs);  // no new copy after a timeout
+        if (t == 0 && i + kStateBufs < count) issue(i + kStateBufs);
 
         // ---- output, per-head RMSNorm (deltanet_impl.h:350-361) and SiLU(z) gate (364-371)
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -367,7 +378,14 @@ struct Workspace {
     size_t total = 0;
 };
 
-Workspace carve(const gdn_dims& d, int64_t B, void* base) {
+// out_proj runs on the tensor cores with split K (partials in the workspace)
+// from these batches on: Q8_0 from kTcMinBatch, Q4_K from kTcMinBatchQ4k.
+bool out_proj_splits(int weight_type, int64_t B) {
+    return weight_type == GDN_GGML_Q8_0 ? B >= kTcMinBatch : B >= kTcMinBatchQ4k;
+}
+
+// split_out: reserve the split-K partials of out_proj (only used when it splits).
+Workspace carve(const gdn_dims& d, int64_t B, void* base, bool split_out) {
     const Dims D = dims_of(d);
     Workspace w;
     char* p = static_cast<char*>(base);
@@ -383,8 +401,10 @@ Workspace carve(const gdn_dims& d, int64_t B, void* base) {
     w.gated = reinterpret_cast<float*>(take((size_t)B * D.inner * 4));
     w.gated_h = reinterpret_cast<__half*>(take((size_t)B * D.inner * 2));
     w.xconv = take((size_t)B * d.hidden * 2);
-    w.partial_bytes = gemm_tc_workspace_bytes(B, d.hidden, kOutSplits);
-    w.partial = reinterpret_cast<float*>(take(w.partial_bytes));
+    if (split_out) {
+        w.partial_bytes = gemm_tc_workspace_bytes(B, d.hidden, kOutSplits);
+        w.partial = reinterpret_cast<float*>(take(w.partial_bytes));
+    }
     w.total = off;
     return w;
 }
@@ -416,7 +436,15 @@ int phase_ms(float* ms, int n) {
     return w;
 }
 
-size_t decode_workspace_bytes(const gdn_dims& d, int64_t batch) { return carve(d, batch, nullptr).total; }
+// Covers both weight types (the Q4_K split starts at the smaller batch).
+size_t decode_workspace_bytes(const gdn_dims& d, int64_t batch) {
+    return carve(d, batch, nullptr, batch >= kTcMinBatchQ4k).total;
+}
+
+size_t decode_workspace_bytes_for(const gdn_layer& L, int64_t batch, int flags) {
+    const bool ref = (flags & GDN_DECODE_REF_PROJECTIONS) != 0;
+    return carve(L.dims, batch, nullptr, !ref && out_proj_splits(L.weight_type, batch)).total;
+}
 
 int validate_layer(const gdn_layer* L) {
     if (L == nullptr) return fail(GDN_ERR_ARG, "layer is NULL");
@@ -513,12 +541,12 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
         return fail(GDN_ERR_TYPE, "x_dtype %d is not supported", x_dtype);
     if (!aligned(S, 16)) return fail(GDN_ERR_ARG, "S must be 16-byte aligned");
     const gdn_dims& d = L->dims;
-    const size_t need = decode_workspace_bytes(d, B);
+    const bool tc_out = !ref && out_proj_splits(L->weight_type, B);
+    const size_t need = decode_workspace_bytes_for(*L, B, flags);
     if (wsp == nullptr || ws_bytes < need || !aligned(wsp, 256))
         return fail(GDN_ERR_ARG, "workspace must be 256-aligned and hold %zu bytes (got %zu)", need, ws_bytes);
     const Dims D = dims_of(d);
-    const Workspace ws = carve(d, B, wsp);
-    const bool tc_out = !ref && (L->weight_type == GDN_GGML_Q8_0 ? B >= kTcMinBatch : B >= kTcMinBatchQ4k);
+    const Workspace ws = carve(d, B, wsp, tc_out);
     const bool conv = (L->conv1d_w != nullptr && conv_buf != nullptr);
     PhaseEvents* pe = phase_events();
 
