@@ -18,6 +18,10 @@
  *     GGUF Q8_0 / Q4_K dequant + GEMV kernels behind quant_matvec
  *     (engine/runtime/transformer.h:157-194).
  *
+ *  3. gdn_layer_forward: deltanet_forward's own argument list (raw GGUF
+ *     blocks + GGML type ids, dims from gdn_dn_init_dims) for batch x T
+ *     tokens; like group 1 it owns the device memory it prepares.
+ *
  * Conventions: all pointers of group 2 are device pointers unless stated;
  * `stream` is a cudaStream_t (NULL = legacy default stream); every call is
  * stream-ordered and returns after enqueueing.  Shapes use int64_t.
@@ -173,8 +177,8 @@ typedef struct gdn_dims {
  *         cols = hidden.  (Rows are independent in a GEMV, so stacking the
  *         reference's four tensors is exact.)
  *   out_*: ssm_out, rows = hidden, cols = inner.
- *   weight_type: GDN_GGML_Q8_0 (planes in *_qs/*_d) or GDN_GGML_Q4_K
- *         (raw superblocks in *_blocks).
+ *   weight_type: GDN_GGML_Q8_0 (planes in in_qs / in_d, out_qs / out_d) or
+ *         GDN_GGML_Q4_K (raw superblocks in in_blocks, out_blocks).
  *   conv1d_w [QKV][4] fp32 (ssm_conv1d.weight, tap k=0 oldest);
  *   ssm_a [Hv] (= -exp(A_log)), dt_bias [Hv], head_norm [head_dim] or NULL.
  */
@@ -359,6 +363,65 @@ GDN_API int gdn_add_rmsnorm(float* x, const float* add, const float* w, void* y,
  */
 GDN_API int gdn_add_rmsnorm_bcast(float* x, const float* add, const float* w, void* const* y, int ny,
                                   int y_dtype, int64_t T, int64_t hidden, int64_t row0, void* stream);
+
+/* ------------------------------------------------------ the reference's call */
+
+/* dn_init_dims (engine/runtime/deltanet_impl.h:32-44): the dims every later
+ * gdn_layer_forward uses, from the GGUF keys ssm.inner_size, ssm.group_count
+ * and ssm.state_size; 0 or less picks the reference's defaults (8192, 16,
+ * 128).  head_dim must be 128.  Process-wide, like the reference's statics. */
+GDN_API int gdn_dn_init_dims(int ssm_inner_size, int ssm_group_count, int ssm_head_dim);
+
+/* DeltaNetState (deltanet_impl.h:48-60) on the device: S [batch][Hv][d][d]
+ * fp32, conv_buf [batch][4][QKV] fp32 (NULL: no conv1d), conv_pos [batch]
+ * int32 -- the reference's per-call scratch (tmp_*) is the library's. */
+typedef struct gdn_dn_state {
+    float* S;
+    float* conv_buf;
+    int32_t* conv_pos;
+} gdn_dn_state;
+
+/*
+ * deltanet_forward (engine/runtime/deltanet_impl.h:145-162; the engine's CPU
+ * route, winmoe_inference.c:1450-1460) on the GPU, same arguments in the same
+ * order plus batch, T and a stream; returns a gdn_status.
+ *   output [batch][T][hidden_dim] fp32, x [batch][T][hidden_dim] fp32 and the
+ *   state: device memory.  T == 1: one decode token for `batch` sequences
+ *   (gdn_decode_step); T > 1: a prompt of T tokens per sequence (gdn_prefill,
+ *   sequence after sequence).
+ *   w_*: raw GGUF blocks with their GGML type ids -- all Q8_0 (8) or all Q4_K
+ *   (12); w_alpha / w_beta may be NULL (those projections are 0, as in the
+ *   reference).  conv1d_w [QKV][4], a_log (the GGUF ssm_a = -exp(A_log), as
+ *   the engine passes it), dt_bias [Hv], head_norm [128]: fp32, NULL as in
+ *   the reference.  All of these may be host or device memory.
+ * The first call with a weight set (the pointers above, on this device)
+ * prepares it into library-owned device memory (a copy, Q8_0 repacked to
+ * planes, the projections fused), kept until gdn_layer_release; later calls
+ * with the same pointers reuse it, so the tensors must not change in place.
+ * The step runs on one library-owned scratch per device, grown (after a
+ * device synchronisation) when a call needs more.  Calls that prepare or grow
+ * allocate; make them before any stream capture.  Calls share that scratch:
+ * issue them on one stream per device, as the engine's single host thread does.
+ */
+GDN_API int gdn_layer_forward(float* output, const float* x, gdn_dn_state* state,
+                              const void* w_qkv, int w_qkv_type,
+                              const void* w_gate, int w_gate_type,
+                              const void* w_alpha, int w_alpha_type,
+                              const void* w_beta, int w_beta_type,
+                              const void* w_out, int w_out_type,
+                              const float* conv1d_w, const float* a_log,
+                              const float* dt_bias, const float* head_norm,
+                              int hidden_dim, int64_t batch, int64_t T, void* stream);
+/* Frees the prepared copies of the weight sets whose w_qkv is this pointer
+ * (current device).  No counterpart in the reference (its weights are the
+ * caller's RAM). */
+GDN_API int gdn_layer_release(const void* w_qkv);
+/* Frees every prepared weight set and the scratch of the current device. */
+GDN_API int gdn_layer_release_all(void);
+/* 1 when the reference's expert-cache module is linked beside this library
+ * with the renames of gpu_offload_coexist.h (gpu_init then initialises it
+ * too), else 0.  No counterpart in the reference. */
+GDN_API int gdn_offload_experts_linked(void);
 
 /*
  * Optional phase timing of gdn_decode_step / gdn_prefill, for benchmarks.

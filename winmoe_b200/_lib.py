@@ -45,6 +45,10 @@ class gdn_layer(C.Structure):
     ]
 
 
+class gdn_dn_state(C.Structure):
+    _fields_ = [("S", C.c_void_p), ("conv_buf", C.c_void_p), ("conv_pos", C.c_void_p)]
+
+
 _vp, _i64, _int, _sz = C.c_void_p, C.c_int64, C.c_int, C.c_size_t
 
 # name -> (restype, argtypes) for every entry point of include/*.h
@@ -75,6 +79,12 @@ SIGNATURES = {
     "gdn_ipc_close": (_int, [_vp]),
     "gdn_ipc_free": (_int, [_vp]),
     "gdn_prefill": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "gdn_dn_init_dims": (_int, [_int, _int, _int]),
+    "gdn_layer_forward": (_int, [_vp, _vp, C.POINTER(gdn_dn_state)] + [_vp, _int] * 5 + [_vp] * 4
+                          + [_int, _i64, _i64, _vp]),
+    "gdn_layer_release": (_int, [_vp]),
+    "gdn_layer_release_all": (_int, []),
+    "gdn_offload_experts_linked": (_int, []),
     "gdn_profile_enable": (_int, [_int]),
     "gdn_decode_phase_ms": (_int, [C.POINTER(C.c_float), _int]),
     "gpu_init": (_int, []),

@@ -22,6 +22,14 @@
 #include "../../include/gpu_offload_gdn.h"
 
 namespace gdn {
+
+// The reference's expert-cache module, when linked beside this library with
+// its lifetime functions renamed (layer_api.cu): initialised, shut down and
+// counted together with this module; no-ops when it is not linked.
+int ref_offload_init();
+void ref_offload_shutdown();
+float ref_offload_vram_mb();
+
 namespace {
 
 constexpr int kMaxLayers = 256;
@@ -245,6 +253,10 @@ extern "C" {
 
 int gpu_init(void) {
     if (g.initialized) return 0;
+    if (ref_offload_init() != 0) {
+        fail(GDN_ERR_CUDA, "gpu_init: the linked expert-cache module failed to initialise");
+        return -1;
+    }
     if (cudaStreamCreateWithFlags(&g.compute, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&g.h2d, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&g.d2h, cudaStreamNonBlocking) != cudaSuccess) {
@@ -266,6 +278,7 @@ int gpu_init(void) {
 
 void gpu_shutdown(void) {
     if (!g.initialized) return;
+    ref_offload_shutdown();
     cudaDeviceSynchronize();
     for (LayerGPU& L : g.layers) {
         free_proj(L.qkv);
@@ -301,7 +314,7 @@ void gpu_shutdown(void) {
 
 int gpu_is_initialized(void) { return g.initialized ? 1 : 0; }
 
-float gpu_vram_used_mb(void) { return (float)(g.vram_bytes / (1024.0 * 1024.0)); }
+float gpu_vram_used_mb(void) { return (float)(g.vram_bytes / (1024.0 * 1024.0)) + ref_offload_vram_mb(); }
 
 // rows = in_dim, cols = out_dim, as the engine passes them (winmoe_inference.c:938-942).
 int gpu_upload_deltanet_weights(int layer, const void* qkv_q8, int qkv_rows, int qkv_cols, const void* gate_q8,
