@@ -667,30 +667,31 @@ def run_ours(args):
     od = torch.empty((2, B, cfg.hidden), dtype=torch.float32, device=dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
+    # three events per buffer, created once and re-recorded (a wait uses the most
+    # recent record, issued in stream order before it)
+    ev_h2d = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_d2h = [torch.cuda.Event() for _ in range(2)]
+
     def pipelined(first, n, start_ev):
-        ev = lambda: torch.cuda.Event()
-        h2d, comp, d2h = {}, {}, {}
         s_in.wait_event(start_ev)
         for i in range(first, first + n):
             b = i % 2
+            if i - 2 >= first:
+                s_in.wait_event(ev_comp[b])  # xd[b] was step i-2's input
             with torch.cuda.stream(s_in):
-                if i - 2 in comp:
-                    s_in.wait_event(comp[i - 2])  # xd[b] was step i-2's input
                 xd[b].copy_(xh[i], non_blocking=True)
-                h2d[i] = ev()
-                h2d[i].record(s_in)
-            stream.wait_event(h2d[i])
-            if i - 2 in d2h:
-                stream.wait_event(d2h[i - 2])  # od[b] held step i-2's output
+            ev_h2d[b].record(s_in)
+            stream.wait_event(ev_h2d[b])
+            if i - 2 >= first:
+                stream.wait_event(ev_d2h[b])  # od[b] held step i-2's output
             L.decode_step(w, st, xd[b], od[b], stream)
-            comp[i] = ev()
-            comp[i].record(stream)
+            ev_comp[b].record(stream)
+            s_out.wait_event(ev_comp[b])
             with torch.cuda.stream(s_out):
-                s_out.wait_event(comp[i])
                 oh[b].copy_(od[b], non_blocking=True)
-                d2h[i] = ev()
-                d2h[i].record(s_out)
-        stream.wait_event(d2h[first + n - 1])  # the last output is on the host
+            ev_d2h[b].record(s_out)
+        stream.wait_event(ev_d2h[(first + n - 1) % 2])  # the last output is on the host
     e_w = torch.cuda.Event()
     e_w.record(stream)
     pipelined(0, W, e_w)

@@ -21,6 +21,7 @@
 #include "ptx_sm100.cuh"
 #include "quant.cuh"
 #include "decode.cuh"
+#include "prefill.cuh"
 
 namespace gdn {
 
@@ -347,6 +348,8 @@ constexpr int64_t kTcMinBatch = 64;
 constexpr int64_t kTcMinBatchQ4k = 8;
 // Split-K factor of the tensor-core out_proj (K = inner is long, N = hidden short).
 constexpr int kOutSplits = 8;
+// Split-K factor of the 2 Hv gate rows' exact tensor-core GEMM (one column tile).
+constexpr int kGateSplits = 8;
 
 struct Dims {
     int hv, hk, key, inner, qkv;
@@ -375,6 +378,8 @@ struct Workspace {
     void* xconv = nullptr;      // [B][hidden] 2-byte operand copy of x
     float* partial = nullptr;   // split-K partials of out_proj
     size_t partial_bytes = 0;
+    float* gpartial = nullptr;  // split-K partials of the gate rows (tensor-core in_proj)
+    size_t gpartial_bytes = 0;
     size_t total = 0;
 };
 
@@ -384,8 +389,9 @@ bool out_proj_splits(int weight_type, int64_t B) {
     return weight_type == GDN_GGML_Q8_0 ? B >= kTcMinBatch : B >= kTcMinBatchQ4k;
 }
 
-// split_out: reserve the split-K partials of out_proj (only used when it splits).
-Workspace carve(const gdn_dims& d, int64_t B, void* base, bool split_out) {
+// split_out: reserve the split-K partials of out_proj (only used when it splits);
+// tc_in: those of the gate rows of a tensor-core input projection.
+Workspace carve(const gdn_dims& d, int64_t B, void* base, bool split_out, bool tc_in) {
     const Dims D = dims_of(d);
     Workspace w;
     char* p = static_cast<char*>(base);
@@ -404,6 +410,10 @@ Workspace carve(const gdn_dims& d, int64_t B, void* base, bool split_out) {
     if (split_out) {
         w.partial_bytes = gemm_tc_workspace_bytes(B, d.hidden, kOutSplits);
         w.partial = reinterpret_cast<float*>(take(w.partial_bytes));
+    }
+    if (tc_in) {
+        w.gpartial_bytes = gemm_tc_workspace_bytes(B, 2 * (int64_t)D.hv, kGateSplits);
+        w.gpartial = reinterpret_cast<float*>(take(w.gpartial_bytes));
     }
     w.total = off;
     return w;
@@ -438,12 +448,16 @@ int phase_ms(float* ms, int n) {
 
 // Covers both weight types (the Q4_K split starts at the smaller batch).
 size_t decode_workspace_bytes(const gdn_dims& d, int64_t batch) {
-    return carve(d, batch, nullptr, batch >= kTcMinBatchQ4k).total;
+    return carve(d, batch, nullptr, batch >= kTcMinBatchQ4k, batch >= kTcMinBatch).total;
 }
+
+// The input projection runs on the tensor cores (Q8_0 weights, B >= kTcMinBatch).
+bool in_proj_tc(int weight_type, int64_t B) { return weight_type == GDN_GGML_Q8_0 && B >= kTcMinBatch; }
 
 size_t decode_workspace_bytes_for(const gdn_layer& L, int64_t batch, int flags) {
     const bool ref = (flags & GDN_DECODE_REF_PROJECTIONS) != 0;
-    return carve(L.dims, batch, nullptr, !ref && out_proj_splits(L.weight_type, batch)).total;
+    return carve(L.dims, batch, nullptr, !ref && out_proj_splits(L.weight_type, batch),
+                 !ref && in_proj_tc(L.weight_type, batch)).total;
 }
 
 int validate_layer(const gdn_layer* L) {
@@ -473,12 +487,14 @@ int validate_layer(const gdn_layer* L) {
 }
 
 // Input projection: proj[B][np] = x . in_proj^T.
-// Q8_0, B >= 64: tensor cores with split-precision fp16 weights (exact) and
-// fp16 activations.  bf16/fp16 x converts to fp16 exactly, so every row --
-// including the gate rows, where exp(ssm_a * softplus(alpha)) magnifies any
-// rounding of alpha -- matches an fp32 GEMV up to summation order.  fp32 x
-// would be rounded by that conversion: then the 2*Hv gate rows run on CUDA
-// cores in fp32 instead.  Otherwise one CUDA-core GEMV over all rows.
+// Q8_0, B >= 64: tensor cores with fp16 activations (bf16 / fp16 x converts
+// exactly).  The q, k, v and z rows take one fp16 weight operand (each weight
+// d*q rounded once, ~2^-12 relative: ~1e-4 of a projection); the 2 Hv gate
+// rows take exact hi + lo weights, since exp(ssm_a * softplus(alpha))
+// magnifies any rounding of alpha, split K on the caller's stream beside the
+// main GEMM (on the side stream, 96 of 148 SMs at the 35B dims).  fp32 x is
+// rounded by the fp16 conversion: then the gate rows run on fp32 CUDA cores
+// from the unrounded x.  Otherwise one CUDA-core GEMV over all rows.
 static int in_projection(const gdn_layer* L, const Dims& D, int64_t B, const void* x, int x_dtype,
                          const Workspace& ws, cudaStream_t s) {
     const int64_t hidden = L->dims.hidden;
@@ -501,13 +517,31 @@ static int in_projection(const gdn_layer* L, const Dims& D, int64_t B, const voi
         if ((st = launch_convert(x, x_dtype, ws.xconv, false, B * hidden, s))) return st;
         a = ws.xconv;
     }
-    TcOptions opt;
-    opt.split_precision = true;
-    const int64_t n_tc = (x_dtype == GDN_DTYPE_F32) ? (int64_t)D.qkv + D.inner : D.np;
-    if ((st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_tc, hidden, a, false, B, ws.proj, D.ldp, opt, s))) return st;
-    if (n_tc == D.np) return GDN_OK;
-    return launch_q8_0_gemv(L->in_qs + n_tc * hidden, L->in_d + n_tc * (hidden / 32), D.np - n_tc, hidden, x,
-                            x_dtype, B, ws.proj + n_tc, D.ldp, s);
+    const int64_t n_main = (int64_t)D.qkv + D.inner;
+    SideStream* side = nullptr;
+    if ((st = side_stream(&side))) return st;
+    GDN_CUDA(cudaEventRecord(side->fork, s));
+    GDN_CUDA(cudaStreamWaitEvent(side->s, side->fork, 0));
+    st = launch_q8_0_gemm_tc(L->in_qs, L->in_d, n_main, hidden, a, false, B, ws.proj, D.ldp, TcOptions(), side->s);
+    GDN_CUDA(cudaEventRecord(side->join, side->s));
+    if (!st) {
+        const int8_t* gq = L->in_qs + n_main * hidden;
+        const uint16_t* gd = L->in_d + n_main * (hidden / 32);
+        if (x_dtype == GDN_DTYPE_F32) {
+            st = launch_q8_0_gemv(gq, gd, D.np - n_main, hidden, x, x_dtype, B, ws.proj + n_main, D.ldp, s);
+        } else {
+            TcOptions exact;
+            exact.split_precision = true;
+            exact.splits = kGateSplits;
+            exact.workspace = ws.gpartial;
+            exact.workspace_bytes = ws.gpartial_bytes;
+            st = launch_q8_0_gemm_tc(gq, gd, D.np - n_main, hidden, a, false, B, ws.proj + n_main, D.ldp, exact, s);
+        }
+    }
+    const cudaError_t ej = cudaStreamWaitEvent(s, side->join, 0);  // joined on every path
+    if (st) return st;
+    if (ej != cudaSuccess) return cuda_status(ej, "decode: join of the input projection");
+    return GDN_OK;
 }
 
 // The projections as the reference's CPU computes them (quant_matvec per
@@ -546,7 +580,7 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
     if (wsp == nullptr || ws_bytes < need || !aligned(wsp, 256))
         return fail(GDN_ERR_ARG, "workspace must be 256-aligned and hold %zu bytes (got %zu)", need, ws_bytes);
     const Dims D = dims_of(d);
-    const Workspace ws = carve(d, B, wsp, tc_out);
+    const Workspace ws = carve(d, B, wsp, tc_out, !ref && in_proj_tc(L->weight_type, B));
     const bool conv = (L->conv1d_w != nullptr && conv_buf != nullptr);
     PhaseEvents* pe = phase_events();
 
@@ -589,9 +623,8 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
         } else {
             st = launch_q4_k_gemv(L->out_blocks, d.hidden, D.inner, ws.gated, GDN_DTYPE_F32, B, out, d.hidden, s);
         }
-    } else if (tc_out) {
+    } else if (tc_out) {  // the fp16 gated heads, one fp16 weight operand (as the q/k/v/z rows), split K
         TcOptions opt;
-        opt.split_precision = true;
         opt.splits = kOutSplits;
         opt.workspace = ws.partial;
         opt.workspace_bytes = ws.partial_bytes;

@@ -1118,17 +1118,11 @@ int set_smem(K kern, size_t bytes) {
 
 size_t prefill_workspace_bytes(const gdn_dims& d, int64_t T) { return pcarve(d, T, nullptr).total; }
 
-namespace {
-
 // A highest-priority stream per host thread and device, with fork / join events.
 // The prefill's input projection (hundreds of one-per-SM CTAs, a partly empty
 // last wave) runs there; the gate rows, on the caller's stream meanwhile, get
 // only the SMs it leaves idle -- its last wave -- instead of running after it.
-struct SideStream {
-    cudaStream_t s = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-};
-
+// The decode step's input projection does the same.
 int side_stream(SideStream** out) {
     thread_local SideStream tls[16];
     int dev = 0;
@@ -1145,8 +1139,6 @@ int side_stream(SideStream** out) {
     *out = &r;
     return GDN_OK;
 }
-
-}  // namespace
 
 int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* out, const RowDest* gated_out,
             float* S, float* conv_buf, int32_t* conv_pos, void* wsp, size_t ws_bytes, cudaStream_t s) {

@@ -173,14 +173,14 @@ _ws_cache: dict[tuple, torch.Tensor] = {}
 
 
 def workspace(cfg: GDNConfig, batch: int, device) -> torch.Tensor:
-    """Cached scratch for gdn_decode_step (allocated by torch, outside the C ABI)."""
-    device = torch.device(device)
-    dims = _lib.gdn_dims(cfg.hidden, cfg.num_k_heads, cfg.num_v_heads, cfg.head_dim)
-    need = lib().gdn_decode_workspace_size(C.byref(dims), batch)
-    key = (device, need)
+    """Cached scratch for gdn_decode_step (allocated by torch, outside the C ABI),
+    looked up by (dims, batch, device) so that a decode loop pays one dict hit."""
+    key = (cfg, batch, device)
     ws = _ws_cache.get(key)
     if ws is None:
-        ws = torch.empty(need + 256, dtype=torch.uint8, device=device)
+        dims = _lib.gdn_dims(cfg.hidden, cfg.num_k_heads, cfg.num_v_heads, cfg.head_dim)
+        need = lib().gdn_decode_workspace_size(C.byref(dims), batch)
+        ws = torch.empty(need + 256, dtype=torch.uint8, device=torch.device(device))
         _ws_cache[key] = ws
     return ws
 
