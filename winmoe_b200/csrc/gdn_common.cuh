@@ -52,7 +52,16 @@ struct RowDest {
     template <typename E>
     __device__ __forceinline__ E* row(int64_t t) const {
         const int64_t r = t / rows;
-        return static_cast<E*>(ptr[r]) + (t - r * rows) * ld + col0;
+        return static_cast<E*>(pick(r)) + (t - r * rows) * ld + col0;
+    }
+    // ptr[r] by a chain of constant-index selects: a dynamic index into the
+    // kernel parameter's array would go through local memory on every call.
+    __device__ __forceinline__ void* pick(int64_t r) const {
+        void* p = ptr[0];
+#pragma unroll
+        for (int i = 1; i < kMaxRowDest; i++)
+            if (r == i) p = ptr[i];
+        return p;
     }
 };
 

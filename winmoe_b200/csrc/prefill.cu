@@ -40,6 +40,7 @@
 #include "prefill.cuh"
 #include "ptx_sm100.cuh"
 #include "warp_mma.cuh"
+#include "chunk_tc.cuh"
 
 namespace gdn {
 
@@ -49,10 +50,8 @@ namespace {
 
 constexpr int HD = 128;                 // head dim
 constexpr int CH = 64;                  // chunk length
-constexpr int BV = 16;                  // state columns per scan CTA
 constexpr float kLogDecayMin = -110.0f;  // exp() of anything <= this is 0 in fp32
 constexpr int LDH = HD + 8;             // padded smem row (bf16 elements) of 128-wide tiles
-constexpr int LDV = BV + 8;             // ... of BV-wide tiles
 
 struct PDims {
     int hk, hv, key, inner, qkv;
@@ -83,10 +82,10 @@ struct PWork {
     bf16* vb;         // [Hv][Tp][128] conv'd, SiLU'd
     float *glog, *beta, *gcum;  // [Hv][Tp]
     float* gchunk;    // [Hv][nc] gam_63 of every chunk
-    bf16 *wp, *ek;    // [Hv][Tp][LDH] W', e*K, rows padded as the scan's shared-memory tiles
-    bf16* up;         // [Hv][nc][128 / BV][CH][LDV] U', one padded tile per chunk and slab
-    bf16* sc;         // [Hv][nc][128][128] state at each chunk start
-    bf16* dl;         // [Hv][Tp][128] chunk deltas D
+    // per (head, chunk) tile images (img_off): W' [64 t][128 k], E^T [128 k][64 t],
+    // U'^T [128 v][64 t] from chunk_local; the chunk's start state S^T [128 v][128 k]
+    // and deltas D^T [128 v][64 t] from the scan
+    uint8_t *wimg, *eimg, *uimg, *simg, *dimg;
     __half* gated;    // [T][inner] out_proj operand
     float* edge;      // [ceil(T / 128)][6][qkv] raw rows at the M-tile edges (fused preprocessing)
     float* win;       // [4][qkv] raw rows T-4..T-1 (fused preprocessing)
@@ -117,11 +116,12 @@ PWork pcarve(const gdn_dims& d, int64_t T, void* base) {
     w.beta = reinterpret_cast<float*>(take((size_t)D.Tp * D.hv * 4));
     w.gcum = reinterpret_cast<float*>(take((size_t)D.Tp * D.hv * 4));
     w.gchunk = reinterpret_cast<float*>(take((size_t)D.nc * D.hv * 4));
-    w.wp = reinterpret_cast<bf16*>(take((size_t)D.Tp * LDH * 2 * D.hv));
-    w.up = reinterpret_cast<bf16*>(take((size_t)D.nc * (HD / BV) * CH * LDV * 2 * D.hv));
-    w.ek = reinterpret_cast<bf16*>(take((size_t)D.Tp * LDH * 2 * D.hv));
-    w.sc = reinterpret_cast<bf16*>(take((size_t)D.nc * D.hv * HD * HD * 2));
-    w.dl = reinterpret_cast<bf16*>(take(kv * D.hv));
+    const size_t tiles = (size_t)D.nc * D.hv;
+    w.wimg = reinterpret_cast<uint8_t*>(take(tiles * chunk_img_w_bytes()));
+    w.eimg = reinterpret_cast<uint8_t*>(take(tiles * chunk_img_e_bytes()));
+    w.uimg = reinterpret_cast<uint8_t*>(take(tiles * chunk_img_e_bytes()));
+    w.simg = reinterpret_cast<uint8_t*>(take(tiles * chunk_img_s_bytes()));
+    w.dimg = reinterpret_cast<uint8_t*>(take(tiles * chunk_img_e_bytes()));
     w.gated = reinterpret_cast<__half*>(take((size_t)T * D.inner * 2));
     w.edge = reinterpret_cast<float*>(take((size_t)((T + 127) / 128) * 6 * D.qkv * 4));
     w.win = reinterpret_cast<float*>(take((size_t)4 * D.qkv * 4));
@@ -442,8 +442,9 @@ __global__ void __launch_bounds__(256) prefill_edge_kernel(const float* __restri
 // grid (nc, Hv), 256 threads.  L = strictly lower b_i exp(G_i - G_j) K K^T from
 // a bf16 tensor-core product; T = (I + L)^-1 blocked by 16 (fp32 substitution
 // on the diagonal blocks, hi + lo bf16 MMAs below them); W' = T diag(b gam) K,
-// U' = T diag(b) V and e*K, staged in shared memory in the scan's tile layouts
-// and written by bulk copies; the chunk's cumulative G and gam_63 go to HBM.
+// U'^T = (T diag(b) V)^T and E^T = (diag(e) K)^T, staged in shared memory as the
+// tile images the tensor-core scan reads (img_off) and written by bulk copies;
+// the chunk's cumulative G and gam_63 go to HBM.
 struct LocalSmem {
     bf16 k[CH][LDH];
     bf16 v[CH][LDH];
@@ -453,18 +454,19 @@ struct LocalSmem {
     float G[CH], beta[CH];
     float sc[2][CH];      // column scales of T: b_j gam_j (for W') and b_j (for U')
 };
-// The products leave through shared regions that are dead by then: U' through
-// V + L, W' through T + M (each staged in its HBM layout).
-static_assert(offsetof(LocalSmem, L) == offsetof(LocalSmem, v) + sizeof(LocalSmem::v), "V, L adjacent");
-static_assert(offsetof(LocalSmem, M) == offsetof(LocalSmem, T) + sizeof(LocalSmem::T), "T, M adjacent");
-static_assert(sizeof(LocalSmem::v) + sizeof(LocalSmem::L) >= (HD / BV) * CH * LDV * 2, "U' staging fits");
-static_assert(sizeof(LocalSmem::T) + sizeof(LocalSmem::M) >= CH * LDH * 2, "W' staging fits");
-static_assert(offsetof(LocalSmem, v) % 16 == 0 && offsetof(LocalSmem, T) % 16 == 0, "bulk sources aligned");
+// The products leave through shared regions that are dead by then, each
+// staged as its 16 KB image: U'^T through V, W' through T, E^T through L.
+constexpr uint32_t kImgW = CH * HD * 2, kImgE = HD * CH * 2;
+static_assert(sizeof(LocalSmem::v) >= kImgE && sizeof(LocalSmem::T) >= kImgW && sizeof(LocalSmem::L) >= kImgE,
+              "images fit their staging regions");
+static_assert(offsetof(LocalSmem, v) % 16 == 0 && offsetof(LocalSmem, T) % 16 == 0 &&
+              offsetof(LocalSmem, L) % 16 == 0, "bulk sources aligned");
 
 __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restrict__ kn, const bf16* __restrict__ vb,
                                                           const float* __restrict__ glog,
-                                                          const float* __restrict__ beta, bf16* __restrict__ wp,
-                                                          bf16* __restrict__ up, bf16* __restrict__ ek,
+                                                          const float* __restrict__ beta,
+                                                          uint8_t* __restrict__ wimg, uint8_t* __restrict__ uimg,
+                                                          uint8_t* __restrict__ eimg,
                                                           float* __restrict__ gcum, float* __restrict__ gchunk,
                                                           int64_t Tp, int hk, int hv, int head_map,
                                                           int32_t* __restrict__ conv_pos, int64_t T) {
@@ -669,10 +671,9 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
     // V and K exact bf16; the scaled T enters as hi + lo bf16 fragments built in
     // registers from the fp32 T (register i: row gq + 8 (i & 1), columns
     // 2 qq + 8 (i >> 1) + {0, 1}).  T is block lower triangular, so row block rb
-    // takes k-blocks 0..rb only.  Each result is staged in its HBM layout in a
-    // shared region that is dead by then and leaves as one bulk copy: U' through
-    // V + L (slab-major [HD / BV][CH][LDV]), W' through T + M ([CH][LDH]), e*K
-    // in place in the K tile.
+    // takes k-blocks 0..rb only.  Each result is staged as its tile image in a
+    // shared region that is dead by then and leaves as one bulk copy: U'^T
+    // through V, W' through T (E^T follows, through L).
     {
         const int gq = lane >> 2, qq = lane & 3;
         const int rb = warp & 3, r0 = 16 * rb, n0 = 64 * (warp >> 2);
@@ -707,404 +708,56 @@ __global__ void __launch_bounds__(256, 3) chunk_local_kernel(const bf16* __restr
             }
         };
         product(&sm.v[0][0], sm.sc[1]);
-        __syncthreads();  // V (and L) read by every warp: U' takes their place
-        bf16* ustage = &sm.v[0][0];
+        __syncthreads();  // V read by every warp: U'^T takes its place (rows v, as the scan reads it)
+        uint8_t* ustage = reinterpret_cast<uint8_t*>(&sm.v[0][0]);
 #pragma unroll
         for (int n = 0; n < 8; n++) {
             const int cl = n0 + 8 * n + 2 * qq;
-            bf16* d0 = ustage + (cl / BV) * (CH * LDV) + cl % BV;
-            *reinterpret_cast<uint32_t*>(d0 + (r0 + gq) * LDV) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
-            *reinterpret_cast<uint32_t*>(d0 + (r0 + gq + 8) * LDV) = wmma16::pack_bf16(acc[n][2], acc[n][3]);
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                *reinterpret_cast<bf16*>(ustage + sm100::img_off(HD, cl + (e & 1), r0 + gq + 8 * (e >> 1))) =
+                    __float2bfloat16_rn(acc[n][e]);
         }
-        sm100::fence_proxy_async_smem();  // the staged U' leaves by bulk copy
+        sm100::fence_proxy_async_smem();  // the staged U'^T leaves by bulk copy
         product(&sm.k[0][0], sm.sc[0]);
-        __syncthreads();  // T and K read by every warp: W' takes T's place, e*K K's
-        if (tid == 0)  // U' is complete: its copy runs while W' and e*K are staged
-            sm100::bulk_store(up + ((int64_t)h * (Tp / CH) + c) * (HD / BV) * (CH * LDV),
-                              sm100::smem_u32(&sm.v[0][0]), (HD / BV) * CH * LDV * 2);
-        bf16* wstage = reinterpret_cast<bf16*>(&sm.T[0][0]);
+        __syncthreads();  // T and K read by every warp: W' takes T's place
+        if (tid == 0)  // U'^T is complete: its copy runs while W' and E^T are staged
+            sm100::bulk_store(uimg + ((int64_t)h * (Tp / CH) + c) * kImgE, sm100::smem_u32(&sm.v[0][0]), kImgE);
+        uint8_t* wstage = reinterpret_cast<uint8_t*>(&sm.T[0][0]);
 #pragma unroll
         for (int n = 0; n < 8; n++) {
-            bf16* d0 = wstage + n0 + 8 * n + 2 * qq;
-            *reinterpret_cast<uint32_t*>(d0 + (r0 + gq) * LDH) = wmma16::pack_bf16(acc[n][0], acc[n][1]);
-            *reinterpret_cast<uint32_t*>(d0 + (r0 + gq + 8) * LDH) = wmma16::pack_bf16(acc[n][2], acc[n][3]);
+            const int cl = n0 + 8 * n + 2 * qq;
+            *reinterpret_cast<uint32_t*>(wstage + sm100::img_off(CH, r0 + gq, cl)) =
+                wmma16::pack_bf16(acc[n][0], acc[n][1]);
+            *reinterpret_cast<uint32_t*>(wstage + sm100::img_off(CH, r0 + gq + 8, cl)) =
+                wmma16::pack_bf16(acc[n][2], acc[n][3]);
         }
     }
 
-    // ---- e K with e_i = exp(G_63 - G_i), 8 bf16 per thread, in place
+    // ---- E^T [k][t] = e_t K[t][k], e_t = exp(G_63 - G_t), into its image in L's place
+    // (L is dead since the inversion): thread per (k, 8 tokens), consecutive
+    // threads consecutive k -- conflict-free column reads of K
     const float G63 = sm.G[CH - 1];
-    for (int e = tid; e < CH * HD / 8; e += 256) {
-        const int i = e / (HD / 8), c8 = (e % (HD / 8)) * 8;
-        const float ei = __expf(G63 - sm.G[i]);
-        uint4* p = reinterpret_cast<uint4*>(&sm.k[i][c8]);
-        const uint4 kv = *p;
-        const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
-        uint32_t ow[4];
+    uint8_t* estage = reinterpret_cast<uint8_t*>(&sm.L[0][0]);
+    for (int e = tid; e < HD * (CH / 8); e += 256) {
+        const int kc = e % HD, j = e / HD;
+        float f[8];
 #pragma unroll
-        for (int w4 = 0; w4 < 4; w4++) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw[w4]));
-            ow[w4] = wmma16::pack_bf16(ei * f.x, ei * f.y);
-        }
-        *p = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        for (int i = 0; i < 8; i++) f[i] = __expf(G63 - sm.G[8 * j + i]) * __bfloat162float(sm.k[8 * j + i][kc]);
+        *reinterpret_cast<uint4*>(estage + sm100::img_off(HD, kc, 8 * j)) =
+            make_uint4(wmma16::pack_bf16(f[0], f[1]), wmma16::pack_bf16(f[2], f[3]), wmma16::pack_bf16(f[4], f[5]),
+                       wmma16::pack_bf16(f[6], f[7]));
     }
     if (tid < CH) gcum[(int64_t)h * Tp + t0 + tid] = sm.G[tid];
     if (tid == 0) gchunk[(int64_t)h * (Tp / CH) + c] = expf(G63);
     sm100::fence_proxy_async_smem();  // the staged tiles, written by the generic proxy, leave by bulk copy
     __syncthreads();
     if (tid == 0) {
-        sm100::bulk_store(wp + ((int64_t)h * Tp + t0) * LDH, sm100::smem_u32(&sm.T[0][0]), CH * LDH * 2);
-        sm100::bulk_store(ek + ((int64_t)h * Tp + t0) * LDH, sm100::smem_u32(&sm.k[0][0]), CH * LDH * 2);
+        const int64_t i = (int64_t)h * (Tp / CH) + c;
+        sm100::bulk_store(wimg + i * kImgW, sm100::smem_u32(&sm.T[0][0]), kImgW);
+        sm100::bulk_store(eimg + i * kImgE, sm100::smem_u32(&sm.L[0][0]), kImgE);
         sm100::bulk_commit();
         sm100::bulk_wait_read_all();
-    }
-}
-
-// --------------------------------------------------------- K2: chunk_scan
-//
-// grid (128 / BV, Hv), 128 threads; sequential over the chunks of the prompt.
-// The state slab S[:, BV columns] lives in fp32 mma accumulators (warp w owns
-// key rows 32w..32w+31).  Per chunk: S -> bf16 (smem, and HBM as the chunk's
-// start state), D = U' - W' S (warp w: token rows 16w..16w+15), then
-// S = gam_63 S + (e K)^T D.  The next chunk's W', e*K and U' stream in (three
-// bulk copies, one mbarrier per buffer) while this one is computed; the stores
-// of the start state and the deltas are issued behind this chunk's MMAs, off
-// the chain of dependent steps.
-constexpr int kMaxChunksInSmem = 2048;  // per-chunk decays staged in smem (T up to 128K tokens)
-
-struct ScanSmem {
-    bf16 w[2][CH][LDH];
-    bf16 e[2][CH][LDH];
-    bf16 u[2][CH][LDV];
-    bf16 s[HD][LDV];
-    bf16 d[CH][LDV];
-    float gc[kMaxChunksInSmem];
-    uint64_t full[2];  // one mbarrier per buffer: the chunk's three bulk copies landed
-};
-constexpr uint32_t kScanWBytes = CH * LDH * 2, kScanUBytes = CH * LDV * 2;
-
-__global__ void __launch_bounds__(128) chunk_scan_kernel(const bf16* __restrict__ wp, const bf16* __restrict__ up,
-                                                         const bf16* __restrict__ ek,
-                                                         const float* __restrict__ gchunk, float* __restrict__ S,
-                                                         bf16* __restrict__ sc, bf16* __restrict__ dl, int64_t Tp,
-                                                         int64_t nc, uint32_t* __restrict__ err) {
-    pdl_trigger();
-    pdl_wait();
-    extern __shared__ uint8_t smem_raw[];
-    ScanSmem& sm = *reinterpret_cast<ScanSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    const int slab = blockIdx.x, h = blockIdx.y;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int gq = lane >> 2, qq = lane & 3;
-    const int v0 = slab * BV;
-    float* Sh = S + (int64_t)h * HD * HD;
-
-    // state slab -> accumulators: acc[mt][n][e] = S[32w + 16mt + gq + 8(e>>1)][v0 + 8n + 2qq + (e&1)]
-    float acc[2][BV / 8][4];
-#pragma unroll
-    for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-        for (int n = 0; n < BV / 8; n++)
-#pragma unroll
-            for (int e = 0; e < 4; e++)
-                acc[mt][n][e] =
-                    Sh[(int64_t)(32 * warp + 16 * mt + gq + ((e >> 1) << 3)) * HD + v0 + 8 * n + 2 * qq + (e & 1)];
-
-    // The chunk's W', e*K and U' slab are stored in global memory exactly as the
-    // padded shared-memory tiles: one thread brings them with three bulk copies.
-    auto prefetch = [&](int64_t c, int buf) {
-        const uint32_t bar = sm100::smem_u32(&sm.full[buf]);
-        const int64_t base = ((int64_t)h * Tp + c * CH) * LDH;
-        sm100::mbar_arrive_expect_tx(bar, 2 * kScanWBytes + kScanUBytes);
-        sm100::bulk_load(sm100::smem_u32(&sm.w[buf][0][0]), wp + base, kScanWBytes, bar);
-        sm100::bulk_load(sm100::smem_u32(&sm.e[buf][0][0]), ek + base, kScanWBytes, bar);
-        sm100::bulk_load(sm100::smem_u32(&sm.u[buf][0][0]), up + ((h * nc + c) * (HD / BV) + slab) * (CH * LDV),
-                         kScanUBytes, bar);
-    };
-    if (tid == 0) {
-        sm100::mbar_init(sm100::smem_u32(&sm.full[0]), 1);
-        sm100::mbar_init(sm100::smem_u32(&sm.full[1]), 1);
-        sm100::fence_barrier_init();
-        prefetch(0, 0);
-    }
-    const bool gc_smem = nc <= kMaxChunksInSmem;
-    if (gc_smem)
-        for (int64_t i = tid; i < nc; i += 128) sm.gc[i] = gchunk[(int64_t)h * nc + i];
-    __syncthreads();  // barriers initialised, decays staged
-
-    for (int64_t c = 0; c < nc; c++) {
-        const int buf = (int)(c & 1);
-        // ---- chunk start state: bf16 copy in smem (B operand) and in HBM (for the output kernel)
-        bf16* scc = sc + (((int64_t)h * nc + c) * HD) * HD;
-#pragma unroll
-        for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-            for (int n = 0; n < BV / 8; n++)
-#pragma unroll
-                for (int hf = 0; hf < 2; hf++) {
-                    const int r = 32 * warp + 16 * mt + gq + 8 * hf;
-                    const int cl = 8 * n + 2 * qq;
-                    *reinterpret_cast<uint32_t*>(&sm.s[r][cl]) =
-                        wmma16::pack_bf16(acc[mt][n][2 * hf], acc[mt][n][2 * hf + 1]);
-                }
-        // buf ^ 1 was last read in the previous chunk, before its closing barrier
-        if (tid == 0 && c + 1 < nc) prefetch(c + 1, buf ^ 1);
-        const bool landed = sm100::mbar_wait(sm100::smem_u32(&sm.full[buf]), (uint32_t)((c >> 1) & 1), err);
-        if (!__syncthreads_and(landed)) {  // timed out (error word set): stop, let the copies drain
-            if (c + 1 < nc) sm100::mbar_wait(sm100::smem_u32(&sm.full[buf ^ 1]), (uint32_t)(((c + 1) >> 1) & 1), err);
-            return;
-        }
-
-        // ---- D = U' - W' S   (token rows 16w..16w+15, all BV columns)
-        float dacc[BV / 8][4] = {};
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; kk++) {
-            uint32_t a[4];
-            wmma16::load_a(a, &sm.w[buf][0][0], LDH, 16 * warp, 16 * kk);
-#pragma unroll
-            for (int np2 = 0; np2 < BV / 16; np2++) {
-                uint32_t b[4];
-                wmma16::load_b_kn(b, &sm.s[0][0], LDV, 16 * kk, 16 * np2);
-                wmma16::mma(dacc[2 * np2], a, b[0], b[1]);
-                wmma16::mma(dacc[2 * np2 + 1], a, b[2], b[3]);
-            }
-        }
-        // chunk start state -> HBM (16-byte stores issued behind the MMAs above; sm.s
-        // is next written after this chunk's last barrier)
-        for (int i = tid; i < HD * BV / 8; i += 128) {
-            const int r = i / (BV / 8), q = i % (BV / 8);
-            *reinterpret_cast<uint4*>(scc + (int64_t)r * HD + v0 + q * 8) = *reinterpret_cast<const uint4*>(&sm.s[r][q * 8]);
-        }
-        bf16* dlc = dl + ((int64_t)h * Tp + c * CH) * HD + v0;
-#pragma unroll
-        for (int n = 0; n < BV / 8; n++)
-#pragma unroll
-            for (int hf = 0; hf < 2; hf++) {
-                const int r = 16 * warp + gq + 8 * hf;
-                const int cl = 8 * n + 2 * qq;
-                const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(&sm.u[buf][r][cl]);
-                const float2 uf = __bfloat1622float2(u2);
-                *reinterpret_cast<uint32_t*>(&sm.d[r][cl]) =
-                    wmma16::pack_bf16(uf.x - dacc[n][2 * hf], uf.y - dacc[n][2 * hf + 1]);
-            }
-        __syncthreads();
-
-        // ---- S = gam_63 S + (e K)^T D   (key rows 32w..32w+31)
-        const float gC = gc_smem ? sm.gc[c] : gchunk[(int64_t)h * nc + c];
-#pragma unroll
-        for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-            for (int n = 0; n < BV / 8; n++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) acc[mt][n][e] *= gC;
-#pragma unroll
-        for (int kk = 0; kk < CH / 16; kk++) {
-#pragma unroll
-            for (int mt = 0; mt < 2; mt++) {
-                uint32_t a[4];
-                wmma16::load_a_t(a, &sm.e[buf][0][0], LDH, 32 * warp + 16 * mt, 16 * kk);
-#pragma unroll
-                for (int np2 = 0; np2 < BV / 16; np2++) {
-                    uint32_t b[4];
-                    wmma16::load_b_kn(b, &sm.d[0][0], LDV, 16 * kk, 16 * np2);
-                    wmma16::mma(acc[mt][2 * np2], a, b[0], b[1]);
-                    wmma16::mma(acc[mt][2 * np2 + 1], a, b[2], b[3]);
-                }
-            }
-        }
-        for (int i = tid; i < CH * BV / 8; i += 128) {  // deltas -> HBM, behind the MMAs above
-            const int r = i / (BV / 8), q = i % (BV / 8);
-            *reinterpret_cast<uint4*>(dlc + (int64_t)r * HD + q * 8) = *reinterpret_cast<const uint4*>(&sm.d[r][q * 8]);
-        }
-        // sm.s, sm.d and this buffer are rewritten next chunk, the buffer by a bulk
-        // copy (async proxy): order this thread's reads of it before that
-        sm100::fence_proxy_async_smem();
-        __syncthreads();
-    }
-#pragma unroll
-    for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-        for (int n = 0; n < BV / 8; n++)
-#pragma unroll
-            for (int e = 0; e < 4; e++)
-                Sh[(int64_t)(32 * warp + 16 * mt + gq + ((e >> 1) << 3)) * HD + v0 + 8 * n + 2 * qq + (e & 1)] =
-                    acc[mt][n][e];
-}
-
-// ---------------------------------------------------------- K3: chunk_out
-//
-// grid (nc, Hv), 128 threads; warp w owns token rows 16w..16w+15 of the chunk.
-//   P = mask(exp(G_i - G_j) Q K^T)                      (bf16, smem)
-//   O = scale * (diag(gam) Q S0 + P D)                   (fp32 accumulators)
-// then per token: RMSNorm over the head's 128 values times the norm weight
-// (deltanet_impl.h:350-361) and the SiLU(z) gate (364-371) -> fp16 out_proj operand.
-struct OutSmem {
-    bf16 q[CH][LDH];
-    bf16 kd[CH][LDH];  // K for P, then the chunk's deltas D
-    bf16 s[HD][LDH];
-    float G[CH];
-    float hn[HD];
-};
-
-__global__ void __launch_bounds__(128, 3) chunk_out_kernel(const bf16* __restrict__ qn, const bf16* __restrict__ kn,
-                                                        const bf16* __restrict__ sc, const bf16* __restrict__ dl,
-                                                        const float* __restrict__ gcum,
-                                                        const float* __restrict__ proj, int64_t ldp,
-                                                        const float* __restrict__ head_norm,
-                                                        __half* __restrict__ gated, const RowDest dst,
-                                                        int64_t T, int64_t Tp, int hk,
-                                                        int hv, int qkv, int head_map) {
-    pdl_trigger();
-    pdl_wait();
-    extern __shared__ uint8_t smem_raw[];
-    OutSmem& sm = *reinterpret_cast<OutSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    const int c = blockIdx.x, h = blockIdx.y;
-    const int g = head_map ? (h % hk) : (h / (hv / hk));
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int gq = lane >> 2, qq = lane & 3;
-    const int64_t t0 = (int64_t)c * CH;
-    const int64_t nc = Tp / CH;
-    {
-        const bf16* qc = qn + ((int64_t)g * Tp + t0) * HD;
-        const bf16* kc = kn + ((int64_t)g * Tp + t0) * HD;
-        const bf16* s0 = sc + (((int64_t)h * nc + c) * HD) * HD;
-        for (int i = tid; i < CH * HD / 8; i += 128) {
-            const int r = i / (HD / 8), q = i % (HD / 8);
-            wmma16::cp_async16(&sm.q[r][q * 8], qc + r * HD + q * 8);
-            wmma16::cp_async16(&sm.kd[r][q * 8], kc + r * HD + q * 8);
-        }
-        for (int i = tid; i < HD * HD / 8; i += 128) {
-            const int r = i / (HD / 8), q = i % (HD / 8);
-            wmma16::cp_async16(&sm.s[r][q * 8], s0 + r * HD + q * 8);
-        }
-        wmma16::cp_async_commit();
-        if (tid < CH) sm.G[tid] = gcum[(int64_t)h * Tp + t0 + tid];
-        sm.hn[tid] = head_norm != nullptr ? head_norm[tid] : 1.0f;
-    }
-    const int rA = 16 * warp + gq, rB = rA + 8;  // this thread's two token rows
-    // The gate inputs z of this thread's two rows and 32 columns, fetched now so
-    // the loads are in flight during the products below.
-    float2 zr[2][HD / 8];
-#pragma unroll
-    for (int hf = 0; hf < 2; hf++) {
-        const int64_t t = t0 + (hf ? rB : rA);
-        const float* z = proj + min(t, T - 1) * ldp + qkv + h * HD;
-#pragma unroll
-        for (int n = 0; n < HD / 8; n++) zr[hf][n] = *reinterpret_cast<const float2*>(z + 8 * n + 2 * qq);
-    }
-    wmma16::cp_async_wait<0>();
-    __syncthreads();
-    // ---- P = mask(exp(G_i - G_j) Q K^T), only this warp's rows, kept in registers
-    // as the A fragments of P D: the accumulators of n-tiles 2kk and 2kk+1 are,
-    // packed to bf16, the m16k16 fragment of k-block kk.
-    uint32_t pa[CH / 16][4];
-    {
-        float pacc[CH / 8][4] = {};
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; kk++) {
-            uint32_t a[4];
-            wmma16::load_a(a, &sm.q[0][0], LDH, 16 * warp, 16 * kk);
-#pragma unroll
-            for (int np2 = 0; np2 < CH / 16; np2++) {
-                uint32_t b[4];
-                wmma16::load_b_nk(b, &sm.kd[0][0], LDH, 16 * kk, 16 * np2);
-                wmma16::mma(pacc[2 * np2], a, b[0], b[1]);
-                wmma16::mma(pacc[2 * np2 + 1], a, b[2], b[3]);
-            }
-        }
-#pragma unroll
-        for (int n = 0; n < CH / 8; n++) {
-            const int j = 8 * n + 2 * qq;
-            float v[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int i = (e >> 1) ? rB : rA, jj = j + (e & 1);
-                v[e] = (jj <= i) ? __expf(sm.G[i] - sm.G[jj]) * pacc[n][e] : 0.0f;
-            }
-            pa[n >> 1][2 * (n & 1)] = wmma16::pack_bf16(v[0], v[1]);
-            pa[n >> 1][2 * (n & 1) + 1] = wmma16::pack_bf16(v[2], v[3]);
-        }
-    }
-    __syncthreads();  // every warp is done with K: the deltas take its place, loaded behind Q S0
-    {
-        const bf16* dc = dl + ((int64_t)h * Tp + t0) * HD;
-        for (int i = tid; i < CH * HD / 8; i += 128) {
-            const int r = i / (HD / 8), q = i % (HD / 8);
-            wmma16::cp_async16(&sm.kd[r][q * 8], dc + r * HD + q * 8);
-        }
-        wmma16::cp_async_commit();
-    }
-    // ---- O = diag(gam) Q S0 + P D
-    float o[HD / 8][4] = {};
-#pragma unroll
-    for (int kk = 0; kk < HD / 16; kk++) {
-        uint32_t a[4];
-        wmma16::load_a(a, &sm.q[0][0], LDH, 16 * warp, 16 * kk);
-#pragma unroll
-        for (int np2 = 0; np2 < HD / 16; np2++) {
-            uint32_t b[4];
-            wmma16::load_b_kn(b, &sm.s[0][0], LDH, 16 * kk, 16 * np2);
-            wmma16::mma(o[2 * np2], a, b[0], b[1]);
-            wmma16::mma(o[2 * np2 + 1], a, b[2], b[3]);
-        }
-    }
-    const float gamA = expf(sm.G[rA]), gamB = expf(sm.G[rB]);
-#pragma unroll
-    for (int n = 0; n < HD / 8; n++) {
-        o[n][0] *= gamA;
-        o[n][1] *= gamA;
-        o[n][2] *= gamB;
-        o[n][3] *= gamB;
-    }
-    wmma16::cp_async_wait<0>();
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < CH / 16; kk++) {
-#pragma unroll
-        for (int np2 = 0; np2 < HD / 16; np2++) {
-            uint32_t b[4];
-            wmma16::load_b_kn(b, &sm.kd[0][0], LDH, 16 * kk, 16 * np2);
-            wmma16::mma(o[2 * np2], pa[kk], b[0], b[1]);
-            wmma16::mma(o[2 * np2 + 1], pa[kk], b[2], b[3]);
-        }
-    }
-    // ---- scale, per-token RMSNorm over the head, SiLU(z) gate
-    const float scale = 1.0f / sqrtf((float)HD);
-    double ssA = 0.0, ssB = 0.0;
-#pragma unroll
-    for (int n = 0; n < HD / 8; n++) {
-#pragma unroll
-        for (int e = 0; e < 4; e++) o[n][e] = __fmul_rn(o[n][e], scale);
-        ssA += (double)o[n][0] * o[n][0] + (double)o[n][1] * o[n][1];
-        ssB += (double)o[n][2] * o[n][2] + (double)o[n][3] * o[n][3];
-    }
-#pragma unroll
-    for (int off = 1; off < 4; off <<= 1) {
-        ssA += __shfl_xor_sync(0xffffffffu, ssA, off);
-        ssB += __shfl_xor_sync(0xffffffffu, ssB, off);
-    }
-    const float invA = 1.0f / sqrtf((float)(ssA / HD) + 1e-6f);
-    const float invB = 1.0f / sqrtf((float)(ssB / HD) + 1e-6f);
-    const int inner = hv * HD;
-#pragma unroll
-    for (int hf = 0; hf < 2; hf++) {
-        const int64_t t = t0 + (hf ? rB : rA);
-        if (t >= T) continue;
-        const float inv = hf ? invB : invA;
-        __half* gout = (gated != nullptr ? gated + t * inner : dst.row<__half>(t)) + h * HD;
-#pragma unroll
-        for (int n = 0; n < HD / 8; n++) {
-            const int v = 8 * n + 2 * qq;
-            const float2 zz = zr[hf][n];
-            float r2[2];
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                float nv = __fmul_rn(o[n][2 * hf + e], inv);
-                if (head_norm != nullptr) nv = __fmul_rn(nv, sm.hn[v + e]);
-                float zv = e ? zz.y : zz.x;
-                zv = fminf(fmaxf(zv, -88.0f), 88.0f);
-                r2[e] = __fmul_rn(nv, silu_fast(zv));
-            }
-            *reinterpret_cast<__half2*>(gout + v) = __floats2half2_rn(r2[0], r2[1]);
-        }
     }
 }
 
@@ -1272,20 +925,13 @@ int prefill(const gdn_layer* L, int64_t T, const void* x, int x_dtype, float* ou
         const size_t sm1 = sizeof(LocalSmem) + 128;
         if ((st = set_smem(chunk_local_kernel, sm1))) return st;
         st = launch_pdl("chunk_local_kernel", chunk_local_kernel, dim3((unsigned)D.nc, (unsigned)D.hv), dim3(256),
-                        sm1, s, W.kn, W.vb, W.glog, W.beta, W.wp, W.up, W.ek, W.gcum, W.gchunk, D.Tp, D.hk, D.hv,
-                        L->head_map, conv ? conv_pos : nullptr, T);
+                        sm1, s, W.kn, W.vb, W.glog, W.beta, W.wimg, W.uimg, W.eimg, W.gcum, W.gchunk, D.Tp, D.hk,
+                        D.hv, L->head_map, conv ? conv_pos : nullptr, T);
         if (st) return st;
-        const size_t sm2 = sizeof(ScanSmem) + 128;
-        if ((st = set_smem(chunk_scan_kernel, sm2))) return st;
-        st = launch_pdl("chunk_scan_kernel", chunk_scan_kernel, dim3(HD / BV, (unsigned)D.hv), dim3(128), sm2, s,
-                        W.wp, W.up, W.ek, W.gchunk, S, W.sc, W.dl, D.Tp, D.nc, device_error_word());
-        if (st) return st;
-        const size_t sm3 = sizeof(OutSmem) + 128;
-        if ((st = set_smem(chunk_out_kernel, sm3))) return st;
-        st = launch_pdl("chunk_out_kernel", chunk_out_kernel, dim3((unsigned)D.nc, (unsigned)D.hv), dim3(128), sm3, s,
-                        W.qn, W.kn, W.sc, W.dl, W.gcum, W.proj, D.ldp, L->head_norm,
-                        gated_out ? nullptr : W.gated, gated_out ? *gated_out : RowDest{}, T, D.Tp, D.hk, D.hv,
-                        D.qkv, L->head_map);
+        if ((st = launch_chunk_scan_tc(W.wimg, W.eimg, W.uimg, W.gchunk, S, W.simg, W.dimg, D.hv, D.nc, s))) return st;
+        st = launch_chunk_out_tc(W.qn, W.kn, W.simg, W.dimg, W.gcum, W.proj, D.ldp, L->head_norm,
+                                 gated_out ? nullptr : W.gated, gated_out ? *gated_out : RowDest{}, T, D.Tp, D.hk,
+                                 D.hv, D.qkv, L->head_map, s);
         if (st) return st;
     }
 
