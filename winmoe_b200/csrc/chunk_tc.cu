@@ -305,8 +305,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
 struct OutTcSmem {
     uint8_t s[kImgSBytes];   // S_c^T image [128 v][128 k]   (A of the first product)
     uint8_t q[kImgWBytes];   // Q image [64 t][128 k]        (B of the first product; A of Q K^T)
-    uint8_t k[kImgWBytes];   // K image [64 t][128 k]        (B of Q K^T)
-    uint8_t d[kImgEBytes];   // D_c^T image [128 v][64 t]    (A of the second product)
+    uint8_t kd[kImgWBytes];  // K image [64 t][128 k] for Q K^T, then the D_c^T image [128 v][64 t]
     uint8_t p[CH * CH * 2];  // P image [64 t][64 t']        (B of the second product)
     float G[CH], gam[CH], hn[HD];
     uint64_t ld_s, ld_d, mma;
@@ -317,8 +316,8 @@ struct OutTcRed {
     float red[4][CH];
     float inv[CH];
 };
-static_assert(offsetof(OutTcSmem, q) % 1024 == 0 && offsetof(OutTcSmem, k) % 1024 == 0 &&
-              offsetof(OutTcSmem, d) % 1024 == 0 && offsetof(OutTcSmem, p) % 1024 == 0, "images 1024-aligned");
+static_assert(offsetof(OutTcSmem, q) % 1024 == 0 && offsetof(OutTcSmem, kd) % 1024 == 0 &&
+              offsetof(OutTcSmem, p) % 1024 == 0, "images 1024-aligned");
 
 constexpr uint32_t kOutTmemCols = 128;  // S^T Q^T: columns 0..63; D^T P^T: 64..127
 
@@ -358,13 +357,14 @@ __device__ __forceinline__ float warp_token_sums(const float (&x)[32], int lane)
     return keep + __shfl_xor_sync(0xffffffffu, send, 1);
 }
 
-// Memory-bound: every input of the CTA -- the S^T and D^T images (bulk
-// copies), Q and K (cp.async into their images) and the 64 z values of this
-// thread's column (registers) -- is requested at once, before any arithmetic,
-// so each CTA keeps ~112 KB in flight (two CTAs per SM).  The epilogue loops
-// over the two 32-token halves without unrolling: one copy of its body keeps
-// the kernel's code small enough for the instruction cache.
-__global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __restrict__ qn, const bf16* __restrict__ kn,
+// Three CTAs per SM (72 KB of shared memory each): the D^T image reuses the K
+// image's buffer once P is formed, and the z inputs arrive in two halves (the
+// first during the products, the second during the epilogue's reduction).
+// (All loads issued at once with two CTAs per SM measured slower: 135 against
+// 103 us at T = 4096.)  The epilogue loops over the two 32-token halves without
+// unrolling: one copy of its body keeps the kernel's code small enough for the
+// instruction cache (fully unrolled, instruction fetch stalls dominated).
+__global__ void __launch_bounds__(128, 3) chunk_out_tc_kernel(const bf16* __restrict__ qn, const bf16* __restrict__ kn,
                                                               const uint8_t* __restrict__ simg,
                                                               const uint8_t* __restrict__ dimg,
                                                               const float* __restrict__ gcum,
@@ -397,11 +397,8 @@ __global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __rest
     __syncthreads();
     pdl_wait();  // S^T and D^T images come from chunk_scan
     if (tid == 0) {
-        const int64_t i = (int64_t)h * nc + c;
         mbar_arrive_expect_tx(smem_u32(&sm.ld_s), kImgSBytes);
-        bulk_load(smem_u32(sm.s), simg + i * kImgSBytes, kImgSBytes, smem_u32(&sm.ld_s));
-        mbar_arrive_expect_tx(smem_u32(&sm.ld_d), kImgEBytes);
-        bulk_load(smem_u32(sm.d), dimg + i * kImgEBytes, kImgEBytes, smem_u32(&sm.ld_d));
+        bulk_load(smem_u32(sm.s), simg + ((int64_t)h * nc + c) * kImgSBytes, kImgSBytes, smem_u32(&sm.ld_s));
     }
     {  // Q and K rows [t][128] -> their images (16-byte chunks to their swizzled places)
         const bf16* qc = qn + ((int64_t)g * Tp + t0) * HD;
@@ -409,15 +406,10 @@ __global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __rest
         for (int i = tid; i < CH * HD / 8; i += 128) {
             const int r = i >> 4, j = i & 15;
             wmma16::cp_async16(sm.q + img_off(CH, r, 8 * j), qc + r * HD + 8 * j);
-            wmma16::cp_async16(sm.k + img_off(CH, r, 8 * j), kc + r * HD + 8 * j);
+            wmma16::cp_async16(sm.kd + img_off(CH, r, 8 * j), kc + r * HD + 8 * j);
         }
         wmma16::cp_async_commit();
     }
-    // the gate inputs z of this thread's column, tokens 0..63 of the chunk
-    const float* zcol = proj + qkv + (int64_t)h * HD + v;
-    float z[CH];
-#pragma unroll
-    for (int i = 0; i < CH; i++) z[i] = (t0 + i < T) ? zcol[(t0 + i) * ldp] : 0.0f;
     if (tid < CH) {
         const float G = gcum[(int64_t)h * Tp + t0 + tid];
         sm.G[tid] = G;
@@ -442,7 +434,7 @@ __global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __rest
                 uint32_t b[4];
                 const int j = lane >> 3;
                 const int n = 16 * np2 + (lane & 7) + ((j >> 1) << 3), col = 16 * kk + ((j & 1) << 3);
-                wmma16::ldsm_x4(b, sm.k + img_off(CH, n, col));
+                wmma16::ldsm_x4(b, sm.kd + img_off(CH, n, col));
                 wmma16::mma(pacc[2 * np2], a, b[0], b[1]);
                 wmma16::mma(pacc[2 * np2 + 1], a, b[2], b[3]);
             }
@@ -461,7 +453,14 @@ __global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __rest
             *reinterpret_cast<uint32_t*>(sm.p + img_off(CH, rB, j)) = pack2(pv[2], pv[3]);
         }
     }
-    fence_proxy_async_smem();  // P and Q (generic writes) are read by the MMAs
+    // The gate inputs z of this thread's column for tokens 0..31, loaded now so
+    // that they are in flight during the products (tokens 32..63 follow during
+    // the epilogue's reduction).
+    const float* zcol = proj + qkv + (int64_t)h * HD + v;
+    float z0[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) z0[i] = (t0 + i < T) ? zcol[(t0 + i) * ldp] : 0.0f;
+    fence_proxy_async_smem();  // P and Q (generic writes) are read by the MMAs; K's buffer is refilled
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -470,6 +469,8 @@ __global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __rest
     if (warp == 0) {  // lane 0 issues; the warp waits for it (no lane spins beside it)
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16(128, 64, true);
+            mbar_arrive_expect_tx(smem_u32(&sm.ld_d), kImgEBytes);
+            bulk_load(smem_u32(sm.kd), dimg + ((int64_t)h * nc + c) * kImgEBytes, kImgEBytes, smem_u32(&sm.ld_d));
             ok = mbar_wait(smem_u32(&sm.ld_s), 0, err);
             if (ok) {
                 const uint32_t a0 = smem_u32(sm.s), b0 = smem_u32(sm.q);
@@ -481,7 +482,7 @@ __global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __rest
                                    umma_desc_sw128(b0 + kb * (CH * 128) + ks * 32), idesc, (kb | ks) != 0);
                 ok = mbar_wait(smem_u32(&sm.ld_d), 0, err);
                 if (ok) {
-                    const uint32_t a1 = smem_u32(sm.d), b1 = smem_u32(sm.p);
+                    const uint32_t a1 = smem_u32(sm.kd), b1 = smem_u32(sm.p);
 #pragma unroll
                     for (int ks = 0; ks < 4; ks++)
                         mma_f16_ss(tmem + 64, umma_desc_sw128(a1 + ks * 32), umma_desc_sw128(b1 + ks * 32), idesc,
@@ -514,6 +515,9 @@ __global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __rest
         }
         rd.red[warp][32 * half + lane] = warp_token_sums(sq, lane);
     }
+    float z1[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) z1[i] = (t0 + 32 + i < T) ? zcol[(t0 + 32 + i) * ldp] : 0.0f;
     __syncthreads();
     if (tid < CH) {
         const float ss = (rd.red[0][tid] + rd.red[1][tid]) + (rd.red[2][tid] + rd.red[3][tid]);
@@ -544,7 +548,7 @@ __global__ void __launch_bounds__(128, 2) chunk_out_tc_kernel(const bf16* __rest
                 const int64_t tok = t0 + t;
                 if (tok >= T) continue;
                 const float o = scale * fmaf(sm.gam[t], __uint_as_float(a1[i]), __uint_as_float(a2[i]));
-                const float zv = fminf(fmaxf(half ? z[32 + i] : z[i], -88.0f), 88.0f);
+                const float zv = fminf(fmaxf(half ? z1[i] : z0[i], -88.0f), 88.0f);
                 const float nv = (o * rd.inv[t]) * hnv;
                 __half* out = base != nullptr ? base + t * pitch : dst.row<__half>(tok) + h * HD + v;
                 *out = __float2half_rn(nv * silu_fast(zv));
