@@ -59,7 +59,7 @@ def test_q8_0_gemv_fp32(m, n, k):
         assert rel_l2(y[i], want) <= 1e-5, i
 
 
-@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 32])
 @pytest.mark.parametrize("n,k", [(12352, 2048), (2048, 4096), (64, 2048)])
 def test_q4_k_gemv_fp32(m, n, k):
     blocks = synth.q4_k_blocks(n, k, seed=400 + n)
@@ -70,6 +70,44 @@ def test_q4_k_gemv_fp32(m, n, k):
     for i in range(m):
         want = P.quant_matvec(blocks, x[i], n, k, 12, O.ACT_FP32)
         assert rel_l2(y[i], want) <= 1e-5, i
+
+
+def _edge_activations(k):
+    """Activation rows whose 32-blocks test the streamed GEMV's split of x into
+    int8 levels: all-zero blocks, a lone outlier, and rows scaled near and far
+    below 2^-64 (where the block scale is formed from x * 2^64)."""
+    x = synth.hidden_states(4, k, seed=501).astype(np.float32)
+    x[0, :64] = 0.0           # two zero blocks
+    x[0, 100] = 3.0e4         # an outlier in its block
+    x[1] *= np.float32(1e-30)  # every block scaled below 2^-64
+    x[2, ::2] *= np.float32(1e-20)  # blocks straddling 2^-64: tiny and ordinary values mixed
+    x[3, 32:64] = np.float32(-7.5)  # a constant block
+    return x
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_k"])
+def test_gemv_edge_activations(fmt):
+    n, k = 2048, 2048
+    x = _edge_activations(k)
+    P = O.port()
+    if fmt == "q8_0":
+        blocks = synth.q8_0_blocks(n, k, seed=502)
+        qs, d = L.q8_0_planes(blocks, n, k, DEV)
+        run = lambda xi: L.gemm_q8_0(qs, d, xi)
+        ty = 8
+    else:
+        blocks = synth.q4_k_blocks(n, k, seed=503)
+        dev = torch.from_numpy(blocks.reshape(-1)).to(DEV)
+        run = lambda xi: L.gemm_q4_k(dev, n, k, xi)
+        ty = 12
+    for i in range(x.shape[0]):  # one row per call: the batch-1 streamed path
+        y = run(torch.from_numpy(x[i:i + 1]).to(DEV)).cpu().numpy()[0]
+        want = P.quant_matvec(blocks, x[i], n, k, ty, O.ACT_FP32)
+        assert rel_l2(y, want) <= 1e-5, i
+    xn = x[3:4].copy()
+    xn[0, 1000] = np.nan  # a NaN activation reaches every output, as through fp32 products
+    y = run(torch.from_numpy(xn).to(DEV)).cpu().numpy()[0]
+    assert np.isnan(y).all()
 
 
 GEMM_SHAPES = [(128, 256, 64), (256, 12352, 2048), (256, 2048, 4096), (200, 300, 2048), (64, 128, 128),

@@ -1,0 +1,425 @@
+// Streamed dequant-GEMV for one to four activation rows (decode of single
+// sequences, the GQA projections, the Q4_K sweep at small batches).
+//
+// Memory side.  The row-per-warp GEMVs in quant.cu keep one batch of register
+// loads in flight per warp, so at batch 1 their speed is set by HBM latency;
+// a warp streaming its own rows as separate 2-4 KB bulk copies is no better
+// (about 190 small copies per SM, each with its own fixed cost in the copy
+// engine).  Here CTA c owns a contiguous range of about n / 148 weight rows and
+// one producer warp streams it in stages of 16 rows -- one bulk copy of the
+// int8 rows (Q8_0: plus one of their fp16 scale rows), 18-70 KB each, into a
+// ring of 2-8 stages in shared memory with mbarrier completion -- while 16
+// consumer warps take one row of a stage each and release it on the stage's
+// `empty` barrier.  The stage copies start only once the activation loads are
+// requested (a named barrier): issued earlier, they held those loads back by
+// microseconds on the SM's return path.  Before griddepcontrol.wait the first
+// stages are only prefetched into L2.  Every wait is bounded, and the producer
+// leaves no copy in flight.
+//
+// Arithmetic.  Converting every int8 / 4-bit weight to fp32 and multiplying
+// costs about six instructions per weight and lane, which bounds a batch-1
+// GEMV by instruction issue, not by HBM.  Instead each CTA splits every 32-block
+// of the activations into three int8 levels,
+//     x ~= s (a + b / 254 + c / 254^2),   s = max|x| / 127,
+// (a = rint(x / s), b and c the rounded residuals, all within +-127; the
+// representation error is below 3e-7 max|x| of the block, a few fp32
+// roundings), and the dot products become exact integer sums on __dp4a:
+//     sum q x = s (A + (B + C / 254) / 254),   A = sum q a, B = sum q b, C = sum q c.
+// That keeps the fp32-activation semantics of the reference GPU kernels
+//   Q8_0: w = d q                      engine/runtime/gpu_offload.cu:152-199
+//   Q4_K: w = (d sc) q - dmin m        engine/runtime/gpu_offload.cu:90-98, 237-250
+// to fp32 rounding (results differ from an fp32 FMA chain in the last bits,
+// as any other summation order does).  The Q4_K min term uses fp32 sums of x
+// over every 16, staged with the levels.
+//
+// Lanes.  Q8_0: lane l takes the 16 weights at 512 i + 16 l of the row (a
+// 512-byte line per warp load), inside one 32-block.  Q4_K: lanes 8 g .. 8 g + 7
+// share a superblock (g = 0..3, superblocks g, g + 4, ...): lane j = 2 c + h
+// reads quant bytes 32 c + 16 h .. + 15, whose low nibbles are weights
+// 64 c + 16 h + e (sub-block 2 c) and high nibbles 64 c + 32 + 16 h + e
+// (sub-block 2 c + 1).  The level planes carry 32 bytes of padding after every
+// 128 (xq_off), so the 16-byte pieces that a quarter-warp reads fall on 8
+// distinct bank groups in both mappings.
+#include "gdn_common.cuh"
+#include "ptx_sm100.cuh"
+#include "quant.cuh"
+#include <algorithm>
+
+namespace gdn {
+namespace {
+
+using namespace sm100;
+
+constexpr int kWarps = 16;      // consumer warps; one more warp produces
+constexpr int kStageRows = 16;  // weight rows per stage: one per consumer warp
+constexpr int kMaxSlots = 8;
+constexpr int kBarBytes = 1024;  // full[kMaxSlots], empty[kMaxSlots], padded
+constexpr size_t kSmemLimit = 227 * 1024;
+constexpr float kInv254 = 1.0f / 254.0f;
+constexpr int kStageBatch = 8;  // activation blocks a warp loads before it reduces them
+
+__host__ __device__ constexpr int64_t plane_len(int64_t k) { return k + (k >> 2); }
+__device__ __forceinline__ int64_t xq_off(int64_t i) { return i + ((i >> 7) << 5); }
+
+// Bytes of the staged activations: MB x 3 level planes, the block scales and,
+// for Q4_K, the sums of every 16.
+__host__ __device__ constexpr size_t staged_bytes(int fmt, int mb, int64_t k) {
+    return (size_t)mb * (3 * plane_len(k) + (k / 32) * 4 + (fmt == 1 ? (k / 16) * 4 : 0));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Q4_K 6-bit scale and min of sub-block j from the 12 packed bytes.
+__device__ __forceinline__ void scale_min(int j, const uint8_t* sc, int& s, int& m) {
+    if (j < 4) {
+        s = sc[j] & 63;
+        m = sc[j + 4] & 63;
+    } else {
+        s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+}
+
+// One warp per 32-block of one activation row: lane l holds x[32 b + l].
+// Writes the three level bytes, the block scale and (Q4_K) the two 16-sums.
+template <int FMT>
+__device__ __forceinline__ void stage_block(float xv, int lane, int8_t* pa, int8_t* pb, int8_t* pc, float* sx,
+                                            float* x16) {
+    // max |x| over the block as an integer max of the magnitude bits: a NaN
+    // (bits above those of inf) wins, so that it reaches the outputs through
+    // the block scale as it would through fp32 products
+    uint32_t ab = __float_as_uint(xv) & 0x7fffffffu;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, o));
+    const float mx = __uint_as_float(ab);
+    // blocks below 2^-64 are scaled up by 2^64 first so that 1 / s stays finite
+    const bool tiny = mx < 5.421010862427522e-20f;
+    const float K = tiny ? 18446744073709551616.0f : 1.0f;
+    const float s = (mx * K) * (1.0f / 127.0f);
+    const float inv = mx > 0.0f ? __frcp_rn(s) : 0.0f;  // u * s = x K up to two roundings
+    const float u = (xv * K) * inv;
+    const float a = rintf(u);
+    const float r1 = u - a;  // exact: a is u rounded to an integer, |u| <= 127
+    const float b = rintf(r1 * 254.0f);
+    const float r2 = fmaf(r1, 254.0f, -b);
+    const float c = rintf(r2 * 254.0f);
+    *pa = (int8_t)(int)a;
+    *pb = (int8_t)(int)b;
+    *pc = (int8_t)(int)c;
+    if (lane == 0) *sx = tiny ? s * 5.421010862427522e-20f : s;
+    if (FMT == 1) {
+        float t = xv;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if ((lane & 15) == 0) x16[lane >> 4] = t;
+    }
+}
+
+__device__ __forceinline__ int dot16(const uint4 w, const uint4 p) {
+    int s = __dp4a((int)w.x, (int)p.x, 0);
+    s = __dp4a((int)w.y, (int)p.y, s);
+    s = __dp4a((int)w.z, (int)p.z, s);
+    return __dp4a((int)w.w, (int)p.w, s);
+}
+
+// s (A + (B + C / 254) / 254) for the integer sums of the three levels.
+__device__ __forceinline__ float levels(int A, int B, int C) {
+    return fmaf(fmaf((float)C, kInv254, (float)B), kInv254, (float)A);
+}
+
+struct Staged {
+    const int8_t* q;   // [MB][3][plane_len(k)]
+    const float* sx;   // [MB][k / 32]
+    const float* x16;  // [MB][k / 16]
+    int64_t pl;        // plane_len(k)
+};
+
+template <int MB>
+__device__ __forceinline__ void q8_row(const uint8_t* row, const uint8_t* scales, int64_t k, const Staged& st, int mb,
+                                       int lane, float (&acc)[MB]) {
+    const uint16_t* dr = reinterpret_cast<const uint16_t*>(scales);
+    const int64_t iters = k >> 9;
+#pragma unroll 2
+    for (int64_t it = 0; it < iters; it++) {
+        const int64_t e = (it << 9) + 16 * lane;
+        const uint4 q = *reinterpret_cast<const uint4*>(row + e);
+        const float dw = fp16_bits_to_float(dr[e >> 5]);
+        const int64_t o = xq_off(e);
+#pragma unroll
+        for (int j = 0; j < MB; j++) {
+            if (j < mb) {
+                const int8_t* pj = st.q + (int64_t)j * 3 * st.pl + o;
+                const int A = dot16(q, *reinterpret_cast<const uint4*>(pj));
+                const int B = dot16(q, *reinterpret_cast<const uint4*>(pj + st.pl));
+                const int C = dot16(q, *reinterpret_cast<const uint4*>(pj + 2 * st.pl));
+                acc[j] = fmaf(dw * st.sx[j * (k >> 5) + (e >> 5)], levels(A, B, C), acc[j]);
+            }
+        }
+    }
+}
+
+template <int MB>
+__device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Staged& st, int mb, int lane,
+                                        float (&acc)[MB]) {
+    const int64_t nsb = k >> 8;
+    const int g = lane >> 3, j = lane & 7, c = j >> 1;
+    for (int64_t sb = g; sb < nsb; sb += 4) {
+        const uint8_t* blk = row + sb * 144;
+        const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+        const uint4 q4 = *reinterpret_cast<const uint4*>(blk + 16 + 16 * j);
+        const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
+        const float d = fp16_bits_to_float((uint16_t)(hdr.x & 0xFFFFu));
+        const float dmin = fp16_bits_to_float((uint16_t)(hdr.x >> 16));
+        int s_lo, m_lo, s_hi, m_hi;
+        scale_min(2 * c, hb + 4, s_lo, m_lo);
+        scale_min(2 * c + 1, hb + 4, s_hi, m_hi);
+        const float sl = d * (float)s_lo, ml = dmin * (float)m_lo;
+        const float sh = d * (float)s_hi, mh = dmin * (float)m_hi;
+        const uint4 lo = make_uint4(q4.x & 0x0F0F0F0Fu, q4.y & 0x0F0F0F0Fu, q4.z & 0x0F0F0F0Fu, q4.w & 0x0F0F0F0Fu);
+        const uint4 hi = make_uint4((q4.x >> 4) & 0x0F0F0F0Fu, (q4.y >> 4) & 0x0F0F0F0Fu, (q4.z >> 4) & 0x0F0F0F0Fu,
+                                    (q4.w >> 4) & 0x0F0F0F0Fu);
+        const int64_t klo = sb * 256 + 64 * c + 16 * (j & 1), khi = klo + 32;
+        const int64_t ol = xq_off(klo), oh = xq_off(khi);
+#pragma unroll
+        for (int jj = 0; jj < MB; jj++) {
+            if (jj < mb) {
+                const int8_t* pj = st.q + (int64_t)jj * 3 * st.pl;
+                const float vl = levels(dot16(lo, *reinterpret_cast<const uint4*>(pj + ol)),
+                                        dot16(lo, *reinterpret_cast<const uint4*>(pj + st.pl + ol)),
+                                        dot16(lo, *reinterpret_cast<const uint4*>(pj + 2 * st.pl + ol)));
+                const float vh = levels(dot16(hi, *reinterpret_cast<const uint4*>(pj + oh)),
+                                        dot16(hi, *reinterpret_cast<const uint4*>(pj + st.pl + oh)),
+                                        dot16(hi, *reinterpret_cast<const uint4*>(pj + 2 * st.pl + oh)));
+                const float* sx = st.sx + jj * (k >> 5);
+                const float* s16 = st.x16 + jj * (k >> 4);
+                acc[jj] += (sl * sx[klo >> 5] * vl - ml * s16[klo >> 4]) + (sh * sx[khi >> 5] * vh - mh * s16[khi >> 4]);
+            }
+        }
+    }
+}
+
+// FMT 0: Q8_0 planes (wq = int8 [n][k], wd = fp16 [n][k / 32]); FMT 1: Q4_K
+// superblocks (wq = [n][k / 256][144], wd unused).  CTA c owns the contiguous
+// rows [c n / G, (c + 1) n / G) of G CTAs; warp kWarps (the producer) streams
+// them kStageRows at a time through `slots` stages, each one bulk copy of the
+// int8 rows (plus one of their scale rows), and the consumer warps take one row
+// of a stage each, then release the stage on its `empty` barrier.
+template <int FMT, int MB>
+__global__ void __launch_bounds__((kWarps + 1) * 32, 1)
+    gemv_stream_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wd, int64_t n, int64_t k,
+                       const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots,
+                       uint32_t* __restrict__ err) {
+    pdl_trigger();
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t qbytes = FMT == 0 ? (uint32_t)k : (uint32_t)(k >> 8) * 144u;  // one row
+    const uint32_t dbytes = FMT == 0 ? (uint32_t)(k >> 4) : 0u;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxSlots;
+    Staged st;
+    st.pl = plane_len(k);
+    int8_t* xq = reinterpret_cast<int8_t*>(smem + kBarBytes);
+    float* sx = reinterpret_cast<float*>(xq + (size_t)MB * 3 * st.pl);
+    float* x16 = sx + MB * (k >> 5);
+    st.q = xq;
+    st.sx = sx;
+    st.x16 = x16;
+    uint8_t* ring = smem + kBarBytes + staged_bytes(FMT, MB, k);
+    const uint32_t qstage = kStageRows * qbytes;  // a stage: kStageRows int8 rows, then their scale rows
+    const uint32_t stage_bytes = qstage + kStageRows * dbytes;
+
+    const int64_t r0 = (int64_t)blockIdx.x * n / gridDim.x, r1 = ((int64_t)blockIdx.x + 1) * n / gridDim.x;
+    const int64_t nst = (r1 - r0 + kStageRows - 1) / kStageRows;
+    auto issue = [&](int64_t i, int slot) {  // producer lane 0: stage i into `slot` (= i mod slots)
+        const int64_t ra = r0 + i * kStageRows;
+        const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
+        const uint32_t bar = smem_u32(full + slot);
+        const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
+        mbar_arrive_expect_tx(bar, rows * (qbytes + dbytes));
+        bulk_load(dst, wq + ra * (int64_t)qbytes, rows * qbytes, bar);
+        if (FMT == 0) bulk_load(dst + qstage, wd + ra * (int64_t)dbytes, rows * dbytes, bar);
+    };
+    // Before the wait only L2 prefetches of the first stages go out (the weights
+    // never come from an earlier kernel): copies into shared memory issued now
+    // would sit ahead of the activation loads on the SM's return path.
+    if (warp == kWarps && lane == 0) {
+        for (int s = 0; s < slots; s++) {
+            mbar_init(smem_u32(full + s), 1);
+            mbar_init(smem_u32(empty + s), kWarps);
+        }
+        fence_barrier_init();
+        for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {
+            const int64_t ra = r0 + i * kStageRows;
+            const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
+            bulk_prefetch_l2(wq + ra * (int64_t)qbytes, rows * qbytes);
+            if (FMT == 0) bulk_prefetch_l2(wd + ra * (int64_t)dbytes, rows * dbytes);
+        }
+    }
+    __syncthreads();  // the barriers are initialised
+
+    pdl_wait();
+    const int64_t m0 = (int64_t)blockIdx.y * MB;
+    const int mb = (int)min((int64_t)MB, m - m0);
+    if (warp < kWarps) {
+        // the warp's blocks kStageBatch at a time: every load of a batch is in
+        // flight before the first block's reductions wait on one; once the first
+        // batch is requested the producer may start the copies (named barrier 1)
+        const int nblk = (int)(k >> 5);
+        bool announced = false;
+        for (int j = 0; j < mb; j++) {
+            for (int b0 = warp; b0 < nblk; b0 += kWarps * kStageBatch) {
+                float xv[kStageBatch];
+#pragma unroll
+                for (int u = 0; u < kStageBatch; u++) {
+                    const int b = b0 + u * kWarps;
+                    xv[u] = b < nblk ? load_act(x, x_dtype, (size_t)(m0 + j) * k + 32 * b + lane) : 0.0f;
+                }
+                if (!announced) {
+                    bar_arrive(1, (kWarps + 1) * 32);
+                    announced = true;
+                }
+#pragma unroll
+                for (int u = 0; u < kStageBatch; u++) {
+                    const int b = b0 + u * kWarps;
+                    if (b < nblk) {  // warp-uniform
+                        int8_t* pa = xq + (size_t)j * 3 * st.pl + xq_off(32 * b + lane);
+                        stage_block<FMT>(xv[u], lane, pa, pa + st.pl, pa + 2 * st.pl, sx + j * nblk + b,
+                                         x16 + j * (k >> 4) + 2 * b);
+                    }
+                }
+            }
+        }
+        if (!announced) bar_arrive(1, (kWarps + 1) * 32);
+        bar_sync(2, kWarps * 32);  // the consumers: every block staged
+    }
+
+    if (warp == kWarps) {  // producer
+        bar_sync(1, (kWarps + 1) * 32);  // the activation loads are requested
+        if (lane == 0) {
+            // slot and phase advance with i (no division in the loop)
+            int64_t issued = 0;
+            int slot = 0;
+            uint32_t phase = 0;  // parity of the slot's current use: 0 on the first pass over the ring
+            for (int64_t i = 0; i < nst; i++) {
+                if (i >= slots) {  // the stage that used this slot has been read by every consumer
+                    if (!mbar_wait(smem_u32(empty + slot), phase ^ 1u, err)) break;
+                    fence_proxy_async_smem();
+                }
+                issue(i, slot);
+                issued = i + 1;
+                if (++slot == slots) {
+                    slot = 0;
+                    phase ^= 1u;
+                }
+            }
+            // leave no copy in flight into this CTA's shared memory: the last
+            // min(slots, issued) stages, one per slot, walked backwards
+            for (int64_t q = 0; q < min((int64_t)slots, issued); q++) {
+                slot = slot == 0 ? slots - 1 : slot - 1;
+                if (slot == slots - 1) phase ^= 1u;
+                mbar_wait(smem_u32(full + slot), phase, err);
+            }
+        }
+        return;
+    }
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int64_t i = 0; i < nst; i++) {
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(full + slot), phase, err))) break;
+        const int64_t r = r0 + i * kStageRows + warp;
+        if (r < r1) {
+            const uint8_t* stage = ring + (size_t)slot * stage_bytes;
+            float acc[MB];
+#pragma unroll
+            for (int j = 0; j < MB; j++) acc[j] = 0.0f;
+            if (FMT == 0) {
+                q8_row<MB>(stage + (size_t)warp * qbytes, stage + qstage + (size_t)warp * dbytes, k, st, mb, lane,
+                           acc);
+            } else {
+                q4k_row<MB>(stage + (size_t)warp * qbytes, k, st, mb, lane, acc);
+            }
+#pragma unroll
+            for (int j = 0; j < MB; j++) {
+                if (j < mb) {
+                    const float v = warp_sum(acc[j]);
+                    if (lane == 0) y[(m0 + j) * ldy + r] = v;
+                }
+            }
+        }
+        __syncwarp();  // every lane has read its row of the stage
+        if (lane == 0) mbar_arrive(smem_u32(empty + slot));
+        if (++slot == slots) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+}
+
+template <int FMT, int MB>
+int run(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
+        int64_t ldy, int slots, size_t smem, cudaStream_t s) {
+    const void* fn = (const void*)gemv_stream_kernel<FMT, MB>;
+    GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int64_t ctas = std::min<int64_t>(sm_count(), n);
+    const dim3 grid((unsigned)ctas, (unsigned)((m + MB - 1) / MB));
+    return launch_pdl(FMT == 0 ? "gemv_stream_kernel<q8_0>" : "gemv_stream_kernel<q4_k>",
+                      gemv_stream_kernel<FMT, MB>, grid, dim3((kWarps + 1) * 32), smem, s,
+                      static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
+                      slots, device_error_word());
+}
+
+}  // namespace
+
+// Plans a streamed launch: the activation rows per CTA (1, 2 or 4), the stage
+// slots and the shared memory.  0 when the shape does not qualify (k not a
+// multiple of 512 for Q8_0 or 256 for Q4_K, a base address not 16-byte
+// aligned, more than four activation rows, or fewer than 2 stages fit beside
+// the staged activations).
+static int plan(int fmt, const void* wq, const void* wd, int64_t k, int64_t m, int* mb_out, int* slots_out,
+                size_t* smem_out) {
+    if (m < 1 || m > 4 || k < 256 || (k & (fmt == 0 ? 511 : 255)) != 0) return 0;
+    if ((reinterpret_cast<uintptr_t>(wq) & 15) != 0) return 0;
+    if (fmt == 0 && (reinterpret_cast<uintptr_t>(wd) & 15) != 0) return 0;
+    const int mb = m == 1 ? 1 : m == 2 ? 2 : 4;
+    const int64_t stage = (int64_t)kStageRows * (fmt == 0 ? k + k / 16 : (k / 256) * 144);
+    const size_t base = kBarBytes + staged_bytes(fmt, mb, k);
+    if (base >= kSmemLimit) return 0;
+    const int slots = (int)std::min<int64_t>(kMaxSlots, (int64_t)(kSmemLimit - base) / stage);
+    if (slots < 2) return 0;
+    *mb_out = mb;
+    *slots_out = slots;
+    *smem_out = base + (size_t)slots * stage;
+    return 1;
+}
+
+int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt,
+                       int64_t m, float* y, int64_t ldy, cudaStream_t s) {
+    int mb = 0, slots = 0;
+    size_t smem = 0;
+    if (!plan(fmt, wq, wd, k, m, &mb, &slots, &smem)) return GDN_ERR_SHAPE;
+    if (n <= 0) return GDN_OK;
+    if (fmt == 0) {
+        switch (mb) {
+            case 1: return run<0, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+            case 2: return run<0, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+            default: return run<0, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+        }
+    }
+    switch (mb) {
+        case 1: return run<1, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+        case 2: return run<1, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+        default: return run<1, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+    }
+}
+
+bool gemv_stream_fits(int fmt, const void* wq, const void* wd, int64_t k, int64_t m) {
+    int mb, slots;
+    size_t smem;
+    return plan(fmt, wq, wd, k, m, &mb, &slots, &smem) != 0;
+}
+
+}  // namespace gdn

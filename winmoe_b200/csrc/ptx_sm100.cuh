@@ -100,6 +100,22 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
+// Untiled bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) from
+// global memory into L2; nothing lands in shared memory and nothing waits.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+                 : "memory");
+}
+
+// Named barriers (ids 1..15; 0 is __syncthreads): `count` threads, a multiple
+// of 32.  bar_arrive does not wait.
+__device__ __forceinline__ void bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Untiled bulk copy shared -> global of `bytes` (a multiple of 16; both
 // addresses 16-byte aligned), tracked in the issuing thread's bulk groups.
 __device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {

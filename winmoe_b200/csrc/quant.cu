@@ -108,7 +108,7 @@ __device__ __forceinline__ void stage_x_padded(float* xs, const void* x, int dty
 // staged, and each next batch -- of this row or of the warp's next row --
 // before the current one is reduced, so HBM latency overlaps the staging, the
 // arithmetic and the row sums.
-template <int MB, int UN>
+template <int MB>
 __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict__ qs,
                                                        const uint16_t* __restrict__ dsc,
                                                        int64_t n_rows, int64_t k, const void* x,
@@ -120,13 +120,13 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
     const int64_t nchunk = k >> 4;
     const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
     const int64_t row_end = min(row0 + rows_per_block, n_rows);
-    uint4 qv[UN];
-    uint16_t sv[UN];
+    uint4 qv[4];
+    uint16_t sv[4];
     auto load = [&](int64_t r, int64_t c0) {  // batch of chunks c0 + 32u of row r
         const uint4* qrow = reinterpret_cast<const uint4*>(qs + r * k);
         const uint16_t* drow = dsc + r * (k >> 5);
 #pragma unroll
-        for (int u = 0; u < UN; u++) {
+        for (int u = 0; u < 4; u++) {
             const int64_t c = c0 + 32 * u;
             if (c < nchunk) {
                 qv[u] = __ldg(qrow + c);
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
     for (int j = 0; j < MB; j++) acc[j] = 0.0f;
     while (have) {
 #pragma unroll
-        for (int u = 0; u < UN; u++) {
+        for (int u = 0; u < 4; u++) {
             const int64_t c = c0 + 32 * u;
             if (c >= nchunk) break;
             const float s = fp16_bits_to_float(sv[u]);
@@ -175,8 +175,8 @@ __global__ void __launch_bounds__(256) q8_0_gemv_kernel(const int8_t* __restrict
                 }
             }
         }
-        const bool row_done = c0 + UN * 32 >= nchunk;
-        const int64_t nr = row_done ? r + nwarps : r, nc0 = row_done ? (int64_t)lane : c0 + UN * 32;
+        const bool row_done = c0 + 4 * 32 >= nchunk;
+        const int64_t nr = row_done ? r + nwarps : r, nc0 = row_done ? (int64_t)lane : c0 + 4 * 32;
         const bool next = nr < row_end;
         if (next) load(nr, nc0);
         if (row_done) {
@@ -414,24 +414,6 @@ __global__ void q4_k_dequant_kernel(const uint8_t* __restrict__ blocks, float* _
 // kernel is engine/runtime/gpu_offload.cu:237-250).  A sub-block's contribution
 // is (d sc) sum(q x) - (dmin m) sum(x); the MB activation rows of block row
 // blockIdx.y share every weight load.
-//
-// A warp walks one row, four superblocks at a time: the 8 lanes of group
-// l / 8 share superblock sb0 + l / 8, and lane j = l % 8 takes its quant bytes
-// 16 j .. 16 j + 15 -- chunk c = j / 2, the low nibbles weights
-// 64 c + 16 (j % 2) + 0..15 (sub-block 2c), the high nibbles the same + 32
-// (sub-block 2c + 1).  One 16-byte load of quants and one of the header (the
-// group's eight lanes read the same 16 bytes) per 32 weights, so the 6-bit
-// scale decode is paid once per 32 weights.  A nibble becomes a float with one
-// byte permute (into the low byte of 2^23) and one subtraction.  The sums of x
-// over every 16 weights, staged with x, make the min term one product.  Loads
-// run one batch ahead: the first before the activations are staged, each next
-// one (of this row or the warp's next) before the current one is reduced.
-__device__ __forceinline__ float nib_f32(uint32_t bytes, uint32_t sel) {
-    // bytes holds four values 0..15 in its bytes; sel picks one into the low
-    // byte of 0x4B000000 (2^23): the float 2^23 + v, minus 2^23, is v exactly
-    return __uint_as_float(__byte_perm(bytes, 0x4B000000u, sel)) - 8388608.0f;
-}
-
 template <int MB>
 __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restrict__ blocks,
                                                        int64_t n_rows, int64_t k, const void* x,
@@ -441,46 +423,49 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nwarps = blockDim.x >> 5;
     const int64_t nsb = k >> 8;
-    const int grp = lane >> 3, j = lane & 7, c = j >> 1;
+    // A warp walks one row's superblocks; lane l takes the 4 quant bytes
+    // 32c + 4g .. +3 (c = l / 8, g = l % 8): low nibbles are weights 64c + 4g + e
+    // (sub-block 2c), high nibbles weights 64c + 32 + 4g + e (sub-block 2c + 1).
+    // The warp reads the 128 quant bytes as one line and each quarter-warp reads
+    // 128 contiguous bytes of x.  w = (d sc) q - dmin m is summed as
+    // (d sc) sum(q x) - (dmin m) sum(x) per lane.  Loads run one batch (four
+    // superblocks) ahead: the first before the activations are staged, each next
+    // one -- of this row or the warp's next -- before the current is reduced.
+    const int c = lane >> 3, g = lane & 7;
     const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
     const int64_t row_end = min(row0 + rows_per_block, n_rows);
-    uint4 hv, qv;
+    uint4 hv[4];
+    uint32_t qv[4];
     auto load = [&](int64_t r, int64_t sb0) {
-        const int64_t sb = sb0 + grp;
-        if (sb < nsb) {
-            const uint8_t* blk = blocks + (r * nsb + sb) * 144;
-            hv = __ldg(reinterpret_cast<const uint4*>(blk));
-            qv = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * j));
+        const uint8_t* row = blocks + r * nsb * 144;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (sb0 + u < nsb) {
+                const uint8_t* blk = row + (sb0 + u) * 144;
+                hv[u] = __ldg(reinterpret_cast<const uint4*>(blk));
+                qv[u] = __ldg(reinterpret_cast<const uint32_t*>(blk + 16 + 32 * c + 4 * g));
+            }
         }
     };
     int64_t r = row0 + warp, sb0 = 0;
     bool have = r < row_end;
     if (have) load(r, sb0);  // weights never come from an earlier kernel: before the wait
     pdl_wait();
-    extern __shared__ float xs[];  // [mb][k] activations, then [mb][k / 16] sums of every 16
+    extern __shared__ float xs[];  // [mb][k]
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
-    float* x16 = xs + (int64_t)MB * k;
     stage_x(xs, x, x_dtype, m0, mb, k);
-    __syncthreads();
-    for (int64_t i = threadIdx.x; i < (int64_t)mb * (k >> 4); i += blockDim.x) {
-        const float4* p = reinterpret_cast<const float4*>(xs + (i / (k >> 4)) * k + (i % (k >> 4)) * 16);
-        float sum = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const float4 v4 = p[e];
-            sum += (v4.x + v4.y) + (v4.z + v4.w);
-        }
-        x16[i] = sum;
-    }
     __syncthreads();
     float acc[MB];
 #pragma unroll
-    for (int jj = 0; jj < MB; jj++) acc[jj] = 0.0f;
+    for (int j = 0; j < MB; j++) acc[j] = 0.0f;
     while (have) {
-        const int64_t sb = sb0 + grp;
-        if (sb < nsb) {
-            const uint4 hdr = hv, q4 = qv;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int64_t sb = sb0 + u;
+            if (sb >= nsb) break;
+            const uint4 hdr = hv[u];
+            const uint32_t qw = qv[u];
             const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
             const float d = fp16_bits_to_float((uint16_t)(hdr.x & 0xFFFFu));
             const float dmin = fp16_bits_to_float((uint16_t)(hdr.x >> 16));
@@ -489,32 +474,20 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
             q4k_scale_min(2 * c + 1, hb + 4, s_hi, m_hi);
             const float sl = d * (float)s_lo, ml = dmin * (float)m_lo;
             const float sh = d * (float)s_hi, mh = dmin * (float)m_hi;
-            const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
-            float lo[16], hi[16];
+            float lo[4], hi[4];
+            u4x4_to_f32(qw, lo);
+            u4x4_to_f32(qw >> 4, hi);
+            const int64_t klo = sb * 256 + 64 * c + 4 * g;
 #pragma unroll
-            for (int w = 0; w < 4; w++) {
-                const uint32_t l4 = qw[w] & 0x0F0F0F0Fu, h4 = (qw[w] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-                for (int b = 0; b < 4; b++) {
-                    lo[4 * w + b] = nib_f32(l4, 0x7540u | (uint32_t)b);
-                    hi[4 * w + b] = nib_f32(h4, 0x7540u | (uint32_t)b);
-                }
-            }
-            const int64_t klo = sb * 256 + 64 * c + 16 * (j & 1);
-#pragma unroll
-            for (int jj = 0; jj < MB; jj++) {
-                if (jj < mb) {
-                    const float4* xl = reinterpret_cast<const float4*>(xs + (int64_t)jj * k + klo);
-                    const float4* xh = reinterpret_cast<const float4*>(xs + (int64_t)jj * k + klo + 32);
-                    float al = 0.0f, ah = 0.0f;
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float4 a = xl[e], b = xh[e];
-                        al = fmaf(lo[4 * e + 3], a.w, fmaf(lo[4 * e + 2], a.z, fmaf(lo[4 * e + 1], a.y, fmaf(lo[4 * e], a.x, al))));
-                        ah = fmaf(hi[4 * e + 3], b.w, fmaf(hi[4 * e + 2], b.z, fmaf(hi[4 * e + 1], b.y, fmaf(hi[4 * e], b.x, ah))));
-                    }
-                    const float* s16 = x16 + (int64_t)jj * (k >> 4) + (klo >> 4);
-                    acc[jj] += (sl * al - ml * s16[0]) + (sh * ah - mh * s16[2]);
+            for (int j = 0; j < MB; j++) {
+                if (j < mb) {
+                    const float4 xl = *reinterpret_cast<const float4*>(xs + (int64_t)j * k + klo);
+                    const float4 xh = *reinterpret_cast<const float4*>(xs + (int64_t)j * k + klo + 32);
+                    const float al = fmaf(lo[3], xl.w, fmaf(lo[2], xl.z, fmaf(lo[1], xl.y, lo[0] * xl.x)));
+                    const float ah = fmaf(hi[3], xh.w, fmaf(hi[2], xh.z, fmaf(hi[1], xh.y, hi[0] * xh.x)));
+                    const float sxl = (xl.x + xl.y) + (xl.z + xl.w);
+                    const float sxh = (xh.x + xh.y) + (xh.z + xh.w);
+                    acc[j] += (sl * al - ml * sxl) + (sh * ah - mh * sxh);
                 }
             }
         }
@@ -524,12 +497,12 @@ __global__ void __launch_bounds__(256) q4_k_gemv_kernel(const uint8_t* __restric
         if (next) load(nr, nsb0);
         if (row_done) {
 #pragma unroll
-            for (int jj = 0; jj < MB; jj++) {
-                if (jj < mb) {
-                    const float v = warp_sum(acc[jj]);
-                    if (lane == 0) y[(m0 + jj) * ldy + r] = v;
+            for (int j = 0; j < MB; j++) {
+                if (j < mb) {
+                    const float v = warp_sum(acc[j]);
+                    if (lane == 0) y[(m0 + j) * ldy + r] = v;
                 }
-                acc[jj] = 0.0f;
+                acc[j] = 0.0f;
             }
         }
         r = nr;
@@ -568,14 +541,6 @@ int launch_q8_0_dequant(const int8_t* qs, const uint16_t* d, float* out, int64_t
 // Weight rows per block (a multiple of the 8 warps, at most 32): fewer when
 // the grid would otherwise leave SMs idle (few weight rows, e.g. the gates).
 static int rows_per_block(int64_t n, int64_t groups, int mb) {
-    if (mb == 1 && groups == 1) {
-        // one activation row: about two blocks per SM, every warp walking several
-        // rows, so that a row's loads are in flight while the previous one is
-        // reduced and x is staged twice per SM rather than once per 8 rows
-        int64_t rpb = (n + 2 * (int64_t)sm_count() - 1) / (2 * (int64_t)sm_count());
-        rpb = std::min<int64_t>(256, std::max<int64_t>(8, (rpb + 7) / 8 * 8));
-        return (int)rpb;
-    }
     // one activation row per block: x staging is trivial, so aim for ~8 resident
     // blocks per SM (one weight row per warp in flight); with more rows, larger
     // blocks amortise the staging
@@ -593,25 +558,16 @@ static int pick_mb(int64_t m, int64_t floats_per_row) {
     return mb;
 }
 
-// UN chunks of 16 weights per lane per batch: 8 for rows of 4096 and more (a
-// warp keeps a whole row in flight), else 4.
-template <int MB, int UN>
-static int run_q8_gemv_un(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
-                          int64_t m, float* y, int64_t ldy, cudaStream_t s) {
-    const size_t smem = (size_t)MB * (k + k / 4) * sizeof(float);
-    int st = smem_optin((const void*)q8_0_gemv_kernel<MB, UN>, smem);
-    if (st) return st;
-    const int rpb = rows_per_block(n, (m + MB - 1) / MB, MB);
-    const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
-    return launch_pdl("q8_0_gemv_kernel", q8_0_gemv_kernel<MB, UN>, grid, dim3(256), smem, s, qs, d, n, k, x, dt, m,
-                      y, ldy, rpb);
-}
-
 template <int MB>
 static int run_q8_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
                        int64_t m, float* y, int64_t ldy, cudaStream_t s) {
-    if (MB <= 2 && k >= 4096) return run_q8_gemv_un<MB, 8>(qs, d, n, k, x, dt, m, y, ldy, s);
-    return run_q8_gemv_un<MB, 4>(qs, d, n, k, x, dt, m, y, ldy, s);
+    const size_t smem = (size_t)MB * (k + k / 4) * sizeof(float);
+    int st = smem_optin((const void*)q8_0_gemv_kernel<MB>, smem);
+    if (st) return st;
+    const int rpb = rows_per_block(n, (m + MB - 1) / MB, MB);
+    const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
+    return launch_pdl("q8_0_gemv_kernel", q8_0_gemv_kernel<MB>, grid, dim3(256), smem, s, qs, d, n, k, x, dt, m, y,
+                      ldy, rpb);
 }
 
 int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int dt,
@@ -619,6 +575,7 @@ int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, 
     if ((size_t)(k + k / 4) * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q8_0 gemv: k=%lld too large", (long long)k);
     if (m <= 0 || n <= 0) return GDN_OK;
     if ((m + 7) / 8 > 65535) return fail(GDN_ERR_SHAPE, "q8_0 gemv: m=%lld too large", (long long)m);
+    if (gemv_stream_fits(0, qs, d, k, m)) return launch_gemv_stream(0, qs, d, n, k, x, dt, m, y, ldy, s);
     switch (pick_mb(m, k + k / 4)) {
         case 1: return run_q8_gemv<1>(qs, d, n, k, x, dt, m, y, ldy, s);
         case 2: return run_q8_gemv<2>(qs, d, n, k, x, dt, m, y, ldy, s);
@@ -672,7 +629,7 @@ int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t co
 template <int MB>
 static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
                        int64_t ldy, cudaStream_t s) {
-    const size_t smem = (size_t)MB * (k + k / 16) * sizeof(float);
+    const size_t smem = (size_t)MB * k * sizeof(float);
     int st = smem_optin((const void*)q4_k_gemv_kernel<MB>, smem);
     if (st) return st;
     const int rpb = rows_per_block(n, (m + MB - 1) / MB, MB);
@@ -683,10 +640,11 @@ static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int d
 
 int launch_q4_k_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
                      int64_t ldy, cudaStream_t s) {
-    if ((size_t)(k + k / 16) * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q4_k gemv: k=%lld too large", (long long)k);
+    if ((size_t)k * 4 > 200 * 1024) return fail(GDN_ERR_SHAPE, "q4_k gemv: k=%lld too large", (long long)k);
     if (m <= 0 || n <= 0) return GDN_OK;
     if ((m + 7) / 8 > 65535) return fail(GDN_ERR_SHAPE, "q4_k gemv: m=%lld too large", (long long)m);
-    switch (pick_mb(m, k + k / 16)) {
+    if (gemv_stream_fits(1, w, nullptr, k, m)) return launch_gemv_stream(1, w, nullptr, n, k, x, dt, m, y, ldy, s);
+    switch (pick_mb(m, k)) {
         case 1: return run_q4_gemv<1>(w, n, k, x, dt, m, y, ldy, s);
         case 2: return run_q4_gemv<2>(w, n, k, x, dt, m, y, ldy, s);
         case 4: return run_q4_gemv<4>(w, n, k, x, dt, m, y, ldy, s);

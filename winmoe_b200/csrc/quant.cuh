@@ -17,6 +17,12 @@ int launch_q8_0_gemv_ref(const int8_t* qs, const uint16_t* d, int64_t n, int64_t
 int launch_quantize_q8_K(const float* x, void* out, int64_t n, cudaStream_t s);
 int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int x_dtype,
                      int64_t m, float* y, int64_t ldy, cudaStream_t s);
+// Streamed GEMV (gemv_stream.cu), fmt 0 = Q8_0 planes (wd = the fp16 scale
+// plane), 1 = Q4_K blocks: for m <= 4 activation rows, k a multiple of 256 and
+// 16-byte aligned weights; gemv_stream_fits says whether a call qualifies.
+bool gemv_stream_fits(int fmt, const void* wq, const void* wd, int64_t k, int64_t m);
+int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int x_dtype,
+                       int64_t m, float* y, int64_t ldy, cudaStream_t s);
 int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s);
 int launch_q4_k_gemv(const void* blocks, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
                      int64_t ldy, cudaStream_t s);
