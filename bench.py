@@ -227,58 +227,70 @@ def decode_b1_bytes(cfg):
     return w + cfg.num_v_heads * d2 * 8 + 4 * cfg.qkv_dim * 4 + cfg.qkv_dim * 16 + act
 
 
+B1_LAYERS = 8  # distinct weight sets cycled by the batch-1 legs: 8 x 36 MB > the 126 MB L2
+
+
 def run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, with_cpu):
-    """Config 1: one sequence from a zero state, 64 fp32 tokens (seed 0), one token per step."""
+    """Config 1: one sequence from a zero state, 64 fp32 tokens (seed 0), one token per
+    step.  Step i runs layer i % 8 of eight layers with distinct copies of the weights
+    (and their own states), as a model's layers follow one another: 8 x 36 MB of Q8_0
+    exceed the L2, so every step's weights stream from HBM."""
     import torch
     from winmoe_b200 import layer as L, synth
     steps = 64
+    t = tensors
+    ws = [w] + [L.DeltaNetWeights.upload(cfg, t.in_proj, t.out_proj, t.conv1d_w, t.ssm_a, t.dt_bias, t.head_norm,
+                                         device=dev) for _ in range(B1_LAYERS - 1)]
     xs = torch.from_numpy(synth.hidden_states(steps, cfg.hidden)).to(dev)
     out = torch.empty((1, cfg.hidden), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    warm = L.DeltaNetState.zeros(cfg, 1, dev)
-    for i in range(3):
-        L.decode_step(w, warm, xs[i:i + 1], out, stream)
-    st = L.DeltaNetState.zeros(cfg, 1, dev)
+    warm = [L.DeltaNetState.zeros(cfg, 1, dev) for _ in ws]
+    for i in range(2 * B1_LAYERS):
+        L.decode_step(ws[i % B1_LAYERS], warm[i % B1_LAYERS], xs[i:i + 1], out, stream)
+    st = [L.DeltaNetState.zeros(cfg, 1, dev) for _ in ws]
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # host-paced: each step launched as the previous one's launches return
     e0.record(stream)
     for i in range(steps):
-        L.decode_step(w, st, xs[i:i + 1], out, stream)
+        L.decode_step(ws[i % B1_LAYERS], st[i % B1_LAYERS], xs[i:i + 1], out, stream)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms_host = e0.elapsed_time(e1) / steps
     # device-paced: the 64 steps queued behind a GPU sleep, so the events time the kernels
     # (the pace of a captured or pre-queued decode loop)
-    st = L.DeltaNetState.zeros(cfg, 1, dev)
+    st = [L.DeltaNetState.zeros(cfg, 1, dev) for _ in ws]
     torch.cuda.synchronize(dev)
     torch.cuda._sleep(20_000_000)
     e0.record(stream)
     for i in range(steps):
-        L.decode_step(w, st, xs[i:i + 1], out, stream)
+        L.decode_step(ws[i % B1_LAYERS], st[i % B1_LAYERS], xs[i:i + 1], out, stream)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
-    # the step as one CUDA graph launch per token (DecodeGraph), launched from Python
-    stg = L.DeltaNetState.zeros(cfg, 1, dev)
-    g = L.DecodeGraph(w, stg, x_dtype=xs.dtype)
-    for i in range(3):
+    # the step as one CUDA graph launch per token (DecodeGraph per layer), launched from Python
+    gs = [L.DecodeGraph(wl, L.DeltaNetState.zeros(cfg, 1, dev), x_dtype=xs.dtype) for wl in ws]
+    for i in range(2 * B1_LAYERS):
+        g = gs[i % B1_LAYERS]
         g.x.copy_(xs[i:i + 1])
         g.replay()
     torch.cuda.synchronize(dev)
     e0.record(stream)
     for i in range(steps):
+        g = gs[i % B1_LAYERS]
         g.x.copy_(xs[i:i + 1])
         g.replay()
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms_graph = e0.elapsed_time(e1) / steps
+    del gs, ws, st, warm
     nb = decode_b1_bytes(cfg)
     ach = nb / (ms / 1e3) / 1e9
-    res = {"workload": "decode B=1 (config 1): 64 consecutive tokens of one sequence from a zero state, fp32 x; "
-                       "steps queued behind a GPU sleep (device pace); ms_per_token_host_paced launches each step "
-                       "from Python as the previous returns; ms_per_token_graph replays the step captured as a "
-                       "CUDA graph, one launch per token",
+    res = {"workload": "decode B=1 (config 1): 64 tokens of one sequence from a zero state, fp32 x, step i "
+                       "through layer i % 8 of eight layers with distinct weight copies (8 x 36 MB of Q8_0 > L2: "
+                       "every step's weights come from HBM); steps queued behind a GPU sleep (device pace); "
+                       "ms_per_token_host_paced launches each step from Python as the previous returns; "
+                       "ms_per_token_graph replays each layer's step captured as a CUDA graph, one launch per token",
            "value": 1e3 / ms, "unit": "tok/s", "ms_per_token": ms, "ms_per_token_host_paced": ms_host,
            "ms_per_token_graph": ms_graph,
            "steps": steps, "warmup": 3,
@@ -334,7 +346,10 @@ def run_gqa(dev, hbm_peak, peak_src, with_cpu):
     # device-resident: the library's two GEMVs of a token (Q+gate|K|V as one projection, as
     # gpu_upload_gqa_weights stores them, then O), queued behind a GPU sleep so that the
     # events time the kernels and not the host's launches
-    planes = [L.q8_0_planes(np.concatenate(ws[:3]), QG + 2 * KV, H, dev), L.q8_0_planes(ws[3], H, A, dev)]
+    # eight copies of the weights cycled over the tokens (8 x 29 MB > L2), as eight layers' weights
+    qkv_blocks = np.concatenate(ws[:3])
+    sets = [[L.q8_0_planes(qkv_blocks, QG + 2 * KV, H, dev), L.q8_0_planes(ws[3], H, A, dev)]
+            for _ in range(B1_LAYERS)]
     xd = torch.from_numpy(xs).to(dev)
     ad = torch.from_numpy(at).to(dev)
     yq = torch.empty((1, QG + 2 * KV), dtype=torch.float32, device=dev)
@@ -342,9 +357,10 @@ def run_gqa(dev, hbm_peak, peak_src, with_cpu):
     stream = torch.cuda.current_stream(dev)
 
     def dev_token(i):
+        planes = sets[i % B1_LAYERS]
         L.gemm_q8_0(planes[0][0], planes[0][1], xd[i:i + 1], out=yq, stream=stream)
         L.gemm_q8_0(planes[1][0], planes[1][1], ad[i:i + 1], out=yo, stream=stream)
-    for i in range(3):
+    for i in range(2 * B1_LAYERS):
         dev_token(i)
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -355,6 +371,7 @@ def run_gqa(dev, hbm_peak, peak_src, with_cpu):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     dev_us = e0.elapsed_time(e1) / n_tok * 1e3
+    del sets
     nb = sum(w.nbytes for w in ws) + (3 * H + A + QG + 2 * KV + H) * 4
     if own_init:
         h.gpu_shutdown()
@@ -363,7 +380,9 @@ def run_gqa(dev, hbm_peak, peak_src, with_cpu):
            "value": 1e6 / e2e_us, "unit": "tok/s", "us_per_token": e2e_us, "tokens": n_tok,
            "path": "gpu_gqa_projections + gpu_gqa_output (host buffers, synchronous, as the engine calls them)",
            "device_us_per_token": dev_us,
-           "roofline": {"bound": "hbm", "kernel": "q8_0_gemv_kernel x 2", "achieved": nb / (dev_us / 1e6) / 1e9,
+           "device_path": "the library's two GEMVs per token on device buffers, token i on weight copy i % 8 "
+                          "(8 x 29 MB > L2: weights from HBM), queued behind a GPU sleep",
+           "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel<q8_0> x 2", "achieved": nb / (dev_us / 1e6) / 1e9,
                         "peak": hbm_peak, "unit": "GB/s", "frac": nb / (dev_us / 1e6) / 1e9 / hbm_peak,
                         "peak_source": peak_src, "algorithmic_bytes_per_token": nb}}
     if with_cpu:
@@ -394,8 +413,10 @@ def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
     import torch
     from winmoe_b200 import layer as L, synth
     t = synth.layer_tensors(cfg, weight_type=12)
-    w_in = torch.from_numpy(t.in_proj).to(dev)
-    w_out = torch.from_numpy(t.out_proj).to(dev)
+    # ten copies of the weights cycled over the calls (10 x 19 MB > L2): weights from HBM
+    n_sets = 10
+    w_in = [torch.from_numpy(t.in_proj).to(dev) for _ in range(n_sets)]
+    w_out = [torch.from_numpy(t.out_proj).to(dev) for _ in range(n_sets)]
     stream = torch.cuda.current_stream(dev)
     rows = {}
     for B, half in ((1, False), (8, False), (32, False), (8, True), (32, True)):
@@ -407,18 +428,18 @@ def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
         yi = torch.empty((B, cfg.in_proj_rows), dtype=torch.float32, device=dev)
         yo = torch.empty((B, cfg.hidden), dtype=torch.float32, device=dev)
 
-        def call():
-            L.gemm_q4_k(w_in, cfg.in_proj_rows, cfg.hidden, xi, out=yi, stream=stream)
-            L.gemm_q4_k(w_out, cfg.hidden, cfg.inner, xo, out=yo, stream=stream)
-        for _ in range(3):
-            call()
+        def call(i):
+            L.gemm_q4_k(w_in[i % n_sets], cfg.in_proj_rows, cfg.hidden, xi, out=yi, stream=stream)
+            L.gemm_q4_k(w_out[i % n_sets], cfg.hidden, cfg.inner, xo, out=yo, stream=stream)
+        for i in range(n_sets):
+            call(i)
         reps = 50
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda._sleep(20_000_000)  # the calls queue behind ~10 ms of GPU time: events time the kernels
         e0.record(stream)
-        for _ in range(reps):
-            call()
+        for i in range(reps):
+            call(i)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         ms = e0.elapsed_time(e1) / reps
@@ -430,7 +451,8 @@ def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
     res = {"workload": "Q4_K projection sweep (config 4): in_proj (qkvz + ba rows) and out_proj, dequant-GEMV, "
                        "fp32 activations; one call = the four projections for B tokens; the 'fp16 x' rows take "
                        "the same batches as fp16 activations through the tensor-core path; 50 calls queued behind "
-                       "a GPU sleep, so the events time the kernels rather than the host's launches",
+                       "a GPU sleep, so the events time the kernels rather than the host's launches; call i uses "
+                       "weight copy i % 10 (10 x 19 MB > L2: weights from HBM)",
            "roofline_peak": {"unit": "GB/s", "peak": hbm_peak, "peak_source": peak_src}, "batches": rows}
     if with_cpu:
         from oracle import oracle as O

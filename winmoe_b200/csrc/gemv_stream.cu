@@ -57,6 +57,7 @@ constexpr int kBarBytes = 1024;  // full[kMaxSlots], empty[kMaxSlots], padded
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr float kInv254 = 1.0f / 254.0f;
 constexpr int kStageBatch = 8;  // activation blocks a warp loads before it reduces them
+constexpr int kEarlyStages = 0;  // stages copied before griddepcontrol.wait (the rest after the activation loads)
 
 __host__ __device__ constexpr int64_t plane_len(int64_t k) { return k + (k >> 2); }
 __device__ __forceinline__ int64_t xq_off(int64_t i) { return i + ((i >> 7) << 5); }
@@ -84,38 +85,57 @@ __device__ __forceinline__ void scale_min(int j, const uint8_t* sc, int& s, int&
     }
 }
 
-// One warp per 32-block of one activation row: lane l holds x[32 b + l].
-// Writes the three level bytes, the block scale and (Q4_K) the two 16-sums.
-template <int FMT>
-__device__ __forceinline__ void stage_block(float xv, int lane, int8_t* pa, int8_t* pb, int8_t* pc, float* sx,
-                                            float* x16) {
-    // max |x| over the block as an integer max of the magnitude bits: a NaN
-    // (bits above those of inf) wins, so that it reaches the outputs through
-    // the block scale as it would through fp32 products
-    uint32_t ab = __float_as_uint(xv) & 0x7fffffffu;
+// One warp stages U 32-blocks of one activation row at once (lane l holds
+// x[32 b_u + l]; blocks with valid[u] false are computed on and not stored):
+// the level bytes, the block scales and (Q4_K) the two 16-sums per block.  The
+// U blocks advance step by step together, so their shuffle and rounding
+// chains overlap instead of running one after another.
+template <int FMT, int U>
+__device__ __forceinline__ void stage_blocks(const float (&xv)[U], const bool (&valid)[U], const int (&b)[U],
+                                             int lane, int8_t* pa, int64_t pl, float* sx, float* x16) {
+    // max |x| per block as an integer max of the magnitude bits: a NaN (bits
+    // above those of inf) wins, so that it reaches the outputs through the
+    // block scale as it would through fp32 products
+    uint32_t ab[U];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, o));
-    const float mx = __uint_as_float(ab);
-    // blocks below 2^-64 are scaled up by 2^64 first so that 1 / s stays finite
-    const bool tiny = mx < 5.421010862427522e-20f;
-    const float K = tiny ? 18446744073709551616.0f : 1.0f;
-    const float s = (mx * K) * (1.0f / 127.0f);
-    const float inv = mx > 0.0f ? __frcp_rn(s) : 0.0f;  // u * s = x K up to two roundings
-    const float u = (xv * K) * inv;
-    const float a = rintf(u);
-    const float r1 = u - a;  // exact: a is u rounded to an integer, |u| <= 127
-    const float b = rintf(r1 * 254.0f);
-    const float r2 = fmaf(r1, 254.0f, -b);
-    const float c = rintf(r2 * 254.0f);
-    *pa = (int8_t)(int)a;
-    *pb = (int8_t)(int)b;
-    *pc = (int8_t)(int)c;
-    if (lane == 0) *sx = tiny ? s * 5.421010862427522e-20f : s;
+    for (int u = 0; u < U; u++) ab[u] = __float_as_uint(xv[u]) & 0x7fffffffu;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < U; u++) ab[u] = max(ab[u], __shfl_xor_sync(0xffffffffu, ab[u], o));
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const float mx = __uint_as_float(ab[u]);
+        // blocks below 2^-64 are scaled up by 2^64 first so that 1 / s stays finite
+        const bool tiny = mx < 5.421010862427522e-20f;
+        const float K = tiny ? 18446744073709551616.0f : 1.0f;
+        const float s = (mx * K) * (1.0f / 127.0f);
+        const float inv = mx > 0.0f ? __frcp_rn(s) : 0.0f;  // u * s = x K up to two roundings
+        const float v = (xv[u] * K) * inv;
+        const float a = rintf(v);
+        const float r1 = v - a;  // exact: a is v rounded to an integer, |v| <= 127
+        const float bb = rintf(r1 * 254.0f);
+        const float r2 = fmaf(r1, 254.0f, -bb);
+        const float c = rintf(r2 * 254.0f);
+        if (valid[u]) {
+            int8_t* p = pa + xq_off(32 * b[u] + lane);
+            p[0] = (int8_t)(int)a;
+            p[pl] = (int8_t)(int)bb;
+            p[2 * pl] = (int8_t)(int)c;
+            if (lane == 0) sx[b[u]] = tiny ? s * 5.421010862427522e-20f : s;
+        }
+    }
     if (FMT == 1) {
-        float t = xv;
+        float t[U];
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if ((lane & 15) == 0) x16[lane >> 4] = t;
+        for (int u = 0; u < U; u++) t[u] = xv[u];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+            for (int u = 0; u < U; u++) t[u] += __shfl_xor_sync(0xffffffffu, t[u], o);
+#pragma unroll
+        for (int u = 0; u < U; u++)
+            if (valid[u] && (lane & 15) == 0) x16[2 * b[u] + (lane >> 4)] = t[u];
     }
 }
 
@@ -252,7 +272,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             mbar_init(smem_u32(empty + s), kWarps);
         }
         fence_barrier_init();
-        for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {
+        for (int64_t i = 0; i < min(nst, (int64_t)kEarlyStages); i++) issue(i, (int)i);
+        for (int64_t i = kEarlyStages; i < min(nst, (int64_t)kEarlyStages + 2); i++) {
             const int64_t ra = r0 + i * kStageRows;
             const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
             bulk_prefetch_l2(wq + ra * (int64_t)qbytes, rows * qbytes);
@@ -273,24 +294,20 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         for (int j = 0; j < mb; j++) {
             for (int b0 = warp; b0 < nblk; b0 += kWarps * kStageBatch) {
                 float xv[kStageBatch];
+                bool valid[kStageBatch];
+                int bs[kStageBatch];
 #pragma unroll
                 for (int u = 0; u < kStageBatch; u++) {
-                    const int b = b0 + u * kWarps;
-                    xv[u] = b < nblk ? load_act(x, x_dtype, (size_t)(m0 + j) * k + 32 * b + lane) : 0.0f;
+                    bs[u] = b0 + u * kWarps;
+                    valid[u] = bs[u] < nblk;
+                    xv[u] = valid[u] ? load_act(x, x_dtype, (size_t)(m0 + j) * k + 32 * bs[u] + lane) : 0.0f;
                 }
                 if (!announced) {
                     bar_arrive(1, (kWarps + 1) * 32);
                     announced = true;
                 }
-#pragma unroll
-                for (int u = 0; u < kStageBatch; u++) {
-                    const int b = b0 + u * kWarps;
-                    if (b < nblk) {  // warp-uniform
-                        int8_t* pa = xq + (size_t)j * 3 * st.pl + xq_off(32 * b + lane);
-                        stage_block<FMT>(xv[u], lane, pa, pa + st.pl, pa + 2 * st.pl, sx + j * nblk + b,
-                                         x16 + j * (k >> 4) + 2 * b);
-                    }
-                }
+                stage_blocks<FMT, kStageBatch>(xv, valid, bs, lane, xq + (size_t)j * 3 * st.pl, st.pl, sx + j * nblk,
+                                               x16 + j * (k >> 4));
             }
         }
         if (!announced) bar_arrive(1, (kWarps + 1) * 32);
@@ -301,10 +318,14 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         bar_sync(1, (kWarps + 1) * 32);  // the activation loads are requested
         if (lane == 0) {
             // slot and phase advance with i (no division in the loop)
-            int64_t issued = 0;
-            int slot = 0;
+            int64_t issued = min(nst, (int64_t)kEarlyStages);
+            int slot = (int)issued;
             uint32_t phase = 0;  // parity of the slot's current use: 0 on the first pass over the ring
-            for (int64_t i = 0; i < nst; i++) {
+            if (slot == slots) {
+                slot = 0;
+                phase = 1;
+            }
+            for (int64_t i = issued; i < nst; i++) {
                 if (i >= slots) {  // the stage that used this slot has been read by every consumer
                     if (!mbar_wait(smem_u32(empty + slot), phase ^ 1u, err)) break;
                     fence_proxy_async_smem();
