@@ -18,7 +18,7 @@ int launch_quantize_q8_K(const float* x, void* out, int64_t n, cudaStream_t s);
 int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, const void* x, int x_dtype,
                      int64_t m, float* y, int64_t ldy, cudaStream_t s);
 // Streamed GEMV (gemv_stream.cu), fmt 0 = Q8_0 planes (wd = the fp16 scale
-// plane), 1 = Q4_K blocks: for m <= 4 activation rows, k a multiple of 256 and
+// plane), 1 = Q4_K blocks: k a multiple of 512 (Q8_0) or 256 (Q4_K) and
 // 16-byte aligned weights; gemv_stream_fits says whether a call qualifies.
 bool gemv_stream_fits(int fmt, const void* wq, const void* wd, int64_t k, int64_t m);
 int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int x_dtype,
