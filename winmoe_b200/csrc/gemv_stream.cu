@@ -23,7 +23,7 @@
 // of the activations into three int8 levels,
 //     x ~= s (a + b / 254 + c / 254^2),   s = max|x| / 127,
 // (a = rint(x / s), b and c the rounded residuals, all within +-127; the
-// representation error is below 3e-7 max|x| of the block, a few fp32
+// representation error is below 5e-7 max|x| of the block, a few fp32
 // roundings), and the dot products become exact integer sums on __dp4a:
 //     sum q x = s (A + (B + C / 254) / 254),   A = sum q a, B = sum q b, C = sum q c.
 // That keeps the fp32-activation semantics of the reference GPU kernels
@@ -57,8 +57,8 @@ constexpr int kMaxSlots = 8;
 constexpr int kBarBytes = 1024;  // full[kMaxSlots], empty[kMaxSlots], padded
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr float kInv254 = 1.0f / 254.0f;
-constexpr int kStageBatch = 8;  // activation blocks a warp loads before it reduces them
-constexpr int kEarlyStages = 0;  // stages copied before griddepcontrol.wait (the rest after the activation loads)
+constexpr int kStageBatch = 4;  // 128-element pieces a warp loads from global memory before it reduces them
+constexpr int kSmemBatch = 2;   // ... from shared memory (the activations brought in by a bulk copy)
 
 __host__ __device__ constexpr int64_t plane_len(int64_t k) { return k + (k >> 2); }
 __device__ __forceinline__ int64_t xq_off(int64_t i) { return i + ((i >> 7) << 5); }
@@ -86,58 +86,77 @@ __device__ __forceinline__ void scale_min(int j, const uint8_t* sc, int& s, int&
     }
 }
 
-// One warp stages U 32-blocks of one activation row at once (lane l holds
-// x[32 b_u + l]; blocks with valid[u] false are computed on and not stored):
-// the level bytes, the block scales and (Q4_K) the two 16-sums per block.  The
-// U blocks advance step by step together, so their shuffle and rounding
-// chains overlap instead of running one after another.
-template <int FMT, int U, bool PADDED = true>
-__device__ __forceinline__ void stage_blocks(const float (&xv)[U], const bool (&valid)[U], const int (&b)[U],
-                                             int lane, int8_t* pa, int64_t pl, float* sx, float* x16) {
-    // max |x| per block as an integer max of the magnitude bits: a NaN (bits
-    // above those of inf) wins, so that it reaches the outputs through the
-    // block scale as it would through fp32 products
-    uint32_t ab[U];
+// Rounds v (|v| < 2^22) to the nearest integer, ties to even, by adding
+// 1.5 * 2^23: returns the integer, and the rounded value as a float in *f.
+__device__ __forceinline__ int round_magic(float v, float* f) {
+    const float t = v + 12582912.0f;
+    *f = t - 12582912.0f;
+    return __float_as_int(t) - 0x4B400000;
+}
+
+__device__ __forceinline__ float rcp_approx(float s) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+    return r;
+}
+
+// One warp stages 128 activations of one row (four 32-blocks): lane l holds
+// x[4 l .. 4 l + 3] (its block is l / 8), writes the four level bytes of each
+// plane as one 32-bit word at p (plane a; b and c at +pl, +2 pl), lanes 8 q
+// the block scales at sxp[q], and (Q4_K) lanes 4 h the 16-sums at x16p[h].
+// The block max needs three lane exchanges.  Every CTA stages the
+// activations itself, so this is kept to about twenty instructions per block.
+template <int FMT>
+__device__ __forceinline__ void stage_128(float4 xv, bool valid, int8_t* p, float* sxp, float* x16p, int pl,
+                                          int lane) {
+    // max |x| of the block as an integer max of the magnitude bits: a NaN (bits
+    // above those of inf) wins and makes the block scale NaN, so that it
+    // reaches the outputs as it would through fp32 products
+    uint32_t ab = max(max(__float_as_uint(xv.x) & 0x7fffffffu, __float_as_uint(xv.y) & 0x7fffffffu),
+                      max(__float_as_uint(xv.z) & 0x7fffffffu, __float_as_uint(xv.w) & 0x7fffffffu));
 #pragma unroll
-    for (int u = 0; u < U; u++) ab[u] = __float_as_uint(xv[u]) & 0x7fffffffu;
+    for (int o = 4; o > 0; o >>= 1) ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, o));
+    const float mx = __uint_as_float(ab);
+    // blocks below 2^-64 are scaled up by 2^64 first so that 1 / s stays finite
+    const bool tiny = mx < 5.421010862427522e-20f;
+    const float K = tiny ? 18446744073709551616.0f : 1.0f;
+    const float s = (mx * K) * (1.0f / 127.0f);
+    // 1 / s within an ulp: v s = x K up to a few roundings, |v| <= 127 + tiny
+    const float inv = mx > 0.0f ? rcp_approx(s) : 0.0f;
+    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t wa = 0, wb = 0, wc = 0;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int u = 0; u < U; u++) ab[u] = max(ab[u], __shfl_xor_sync(0xffffffffu, ab[u], o));
-#pragma unroll
-    for (int u = 0; u < U; u++) {
-        const float mx = __uint_as_float(ab[u]);
-        // blocks below 2^-64 are scaled up by 2^64 first so that 1 / s stays finite
-        const bool tiny = mx < 5.421010862427522e-20f;
-        const float K = tiny ? 18446744073709551616.0f : 1.0f;
-        const float s = (mx * K) * (1.0f / 127.0f);
-        const float inv = mx > 0.0f ? __frcp_rn(s) : 0.0f;  // u * s = x K up to two roundings
-        const float v = (xv[u] * K) * inv;
-        const float a = rintf(v);
-        const float r1 = v - a;  // exact: a is v rounded to an integer, |v| <= 127
-        const float bb = rintf(r1 * 254.0f);
-        const float r2 = fmaf(r1, 254.0f, -bb);
-        const float c = rintf(r2 * 254.0f);
-        if (valid[u]) {
-            int8_t* p = pa + (PADDED ? xq_off(32 * b[u] + lane) : (int64_t)(32 * b[u] + lane));
-            p[0] = (int8_t)(int)a;
-            p[pl] = (int8_t)(int)bb;
-            p[2 * pl] = (int8_t)(int)c;
-            if (lane == 0) sx[b[u]] = tiny ? s * 5.421010862427522e-20f : s;
-        }
+    for (int e = 0; e < 4; e++) {
+        const float v = (xs[e] * K) * inv;  // x K exact (a power of two), below 1 when tiny
+        float af, bf, cf;
+        const int a = round_magic(v, &af);
+        const float r1 = v - af;  // exact: af is v rounded to an integer
+        const int bb = round_magic(r1 * 254.0f, &bf);
+        const float r2 = fmaf(r1, 254.0f, -bf);
+        const int c = round_magic(r2 * 254.0f, &cf);
+        wa |= (uint32_t)(a & 0xff) << (8 * e);
+        wb |= (uint32_t)(bb & 0xff) << (8 * e);
+        wc |= (uint32_t)(c & 0xff) << (8 * e);
+    }
+    if (valid) {
+        *reinterpret_cast<uint32_t*>(p) = wa;
+        *reinterpret_cast<uint32_t*>(p + pl) = wb;
+        *reinterpret_cast<uint32_t*>(p + 2 * pl) = wc;
+        if ((lane & 7) == 0) sxp[lane >> 3] = tiny ? s * 5.421010862427522e-20f : s;
     }
     if (FMT == 1) {
-        float t[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) t[u] = xv[u];
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1)
-#pragma unroll
-            for (int u = 0; u < U; u++) t[u] += __shfl_xor_sync(0xffffffffu, t[u], o);
-#pragma unroll
-        for (int u = 0; u < U; u++)
-            if (valid[u] && (lane & 15) == 0) x16[2 * b[u] + (lane >> 4)] = t[u];
+        float t = (xv.x + xv.y) + (xv.z + xv.w);
+        t += __shfl_xor_sync(0xffffffffu, t, 1);
+        t += __shfl_xor_sync(0xffffffffu, t, 2);
+        if (valid && (lane & 3) == 0) x16p[lane >> 2] = t;
     }
+}
+
+// Plane a of activation row j at xq + 3 j pl; element e at xq_off(e)
+// (PADDED) or e.
+template <bool PADDED>
+__device__ __forceinline__ int8_t* level_ptr(int8_t* xq, int pl, int j, int e) {
+    return xq + 3 * j * pl + (PADDED ? (int)xq_off(e) : e);
 }
 
 __device__ __forceinline__ int dot16(const uint4 w, const uint4 p) {
@@ -223,6 +242,154 @@ __device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Sta
     }
 }
 
+// Stages rows 0 .. rows-1 of the activations (x read for rows < mb, zeros
+// beyond) into level planes, from global memory (x: all rows, this CTA's from
+// row m0) or from shared memory (SMEM: xs holds this CTA's rows).  The
+// 128-element pieces of all rows form one list; warp w takes pieces w,
+// w + kWarps, ..., U at a time, every read of a batch issued before its
+// reductions.  From global memory the warp arrives on named barrier 1 (the
+// producer's go) once its first batch is requested.
+template <int FMT, bool PADDED, bool SMEM, int U>
+__device__ __forceinline__ void stage_rows(const void* x, int x_dtype, int64_t m0, int mb, int rows, int64_t k,
+                                           int warp, int lane, int8_t* xq, int pl, float* sx, float* x16) {
+    const int npc = (int)(k >> 7), nblk = (int)(k >> 5);
+    const size_t es = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
+    const char* x0 = static_cast<const char*>(x) + (SMEM ? 0 : (size_t)m0 * k * es);
+    const bool vec = x_dtype == GDN_DTYPE_F32 && (reinterpret_cast<uintptr_t>(x0) & 15) == 0;
+    bool announced = SMEM;
+    // (j, c): row and piece of this warp's next item; advanced by kWarps pieces
+    int j = 0, c = warp;
+    while (c >= npc && j < rows) {
+        c -= npc;
+        j++;
+    }
+    while (j < rows) {
+        float4 xv[U];
+        int ju[U], cu[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            ju[u] = j;
+            cu[u] = c;
+            const int e = 128 * c + 4 * lane;
+            xv[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (j < rows && j < mb) {
+                const char* xr = x0 + (size_t)j * k * es;
+                if (vec) {
+                    xv[u] = *reinterpret_cast<const float4*>(xr + (size_t)e * 4);
+                } else {
+                    xv[u] = make_float4(load_act(xr, x_dtype, e), load_act(xr, x_dtype, e + 1),
+                                        load_act(xr, x_dtype, e + 2), load_act(xr, x_dtype, e + 3));
+                }
+            }
+            c += kWarps;
+            while (c >= npc && j < rows) {
+                c -= npc;
+                j++;
+            }
+        }
+        if (!announced) {
+            bar_arrive(1, (kWarps + 1) * 32);
+            announced = true;
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const bool valid = ju[u] < rows;
+            const int jj = valid ? ju[u] : 0, cc = valid ? cu[u] : 0;
+            stage_128<FMT>(xv[u], valid, level_ptr<PADDED>(xq, pl, jj, 128 * cc + 4 * lane), sx + jj * nblk + 4 * cc,
+                           FMT == 1 ? x16 + jj * 2 * nblk + 8 * cc : nullptr, pl, lane);
+        }
+    }
+    if (!announced) bar_arrive(1, (kWarps + 1) * 32);
+}
+
+// The ring shared by both kernels.  Before griddepcontrol.wait the producer
+// lane only initialises the barriers and prefetches the first stages into L2.
+// After it, when the activations come by bulk copy (nx > 0 slots at the end of
+// the ring hold them until every consumer warp has staged its blocks: `xdone`),
+// that copy is issued first, so that no weight stage sits ahead of it; else the
+// consumers load them from global memory and the producer waits (named barrier
+// 1) until those loads are requested.  Every wait is bounded; the producer
+// leaves no copy in flight into the CTA's shared memory.
+struct Ring {
+    uint64_t* full;   // [kMaxSlots] a stage landed
+    uint64_t* empty;  // [kMaxSlots] every consumer warp has read it
+    uint64_t* xbar;   // the activations landed
+    uint64_t* xdone;  // every consumer warp has staged its activation blocks
+    int slots, nx;
+};
+
+__device__ __forceinline__ Ring ring_of(uint8_t* smem, int slots, int nx) {
+    uint64_t* b = reinterpret_cast<uint64_t*>(smem);
+    return Ring{b, b + kMaxSlots, b + 2 * kMaxSlots, b + 2 * kMaxSlots + 1, slots, nx};
+}
+
+__device__ __forceinline__ void ring_init(const Ring& R) {
+    for (int s = 0; s < R.slots; s++) {
+        mbar_init(smem_u32(R.full + s), 1);
+        mbar_init(smem_u32(R.empty + s), kWarps);
+    }
+    mbar_init(smem_u32(R.xbar), 1);
+    mbar_init(smem_u32(R.xdone), kWarps);
+    fence_barrier_init();
+}
+
+template <class Issue>
+__device__ __forceinline__ void produce(const Ring& R, int64_t nst, Issue issue, const void* xsrc, uint32_t xbytes,
+                                        const uint8_t* xdst, uint32_t* err) {
+    if (R.nx > 0) {
+        mbar_arrive_expect_tx(smem_u32(R.xbar), xbytes);
+        bulk_load(smem_u32(xdst), xsrc, xbytes, smem_u32(R.xbar));
+    }
+    int64_t issued = 0;
+    int slot = 0;
+    uint32_t phase = 0;  // parity of the slot's current use: 0 on the first pass over the ring
+    bool xfree = R.nx == 0;
+    for (int64_t i = 0; i < nst; i++) {
+        if (i >= R.slots) {  // the stage that used this slot has been read by every consumer
+            if (!mbar_wait(smem_u32(R.empty + slot), phase ^ 1u, err)) break;
+            fence_proxy_async_smem();
+        } else if (!xfree && slot >= R.slots - R.nx) {  // the slot still holds the activations
+            if (!mbar_wait(smem_u32(R.xdone), 0, err)) break;
+            xfree = true;
+            fence_proxy_async_smem();
+        }
+        issue(i, slot);
+        issued = i + 1;
+        if (++slot == R.slots) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+    // the last min(slots, issued) stages, one per slot, walked backwards
+    for (int64_t q = 0; q < min((int64_t)R.slots, issued); q++) {
+        slot = slot == 0 ? R.slots - 1 : slot - 1;
+        if (slot == R.slots - 1) phase ^= 1u;
+        mbar_wait(smem_u32(R.full + slot), phase, err);
+    }
+    if (R.nx > 0) mbar_wait(smem_u32(R.xbar), 0, err);
+}
+
+// Consumers: the activations into level planes, then named barrier 2 (every
+// block staged).  Returns false if the activation copy never landed (the
+// error word is set; the planes are then not staged, and every wait of the
+// caller still ends).
+template <int FMT, bool PADDED>
+__device__ __forceinline__ bool consume_activations(const Ring& R, const void* x, int x_dtype, const uint8_t* xs,
+                                                    int64_t m0, int mb, int rows, int64_t k, int warp, int lane,
+                                                    int8_t* xq, int pl, float* sx, float* x16, uint32_t* err) {
+    bool ok = true;
+    if (R.nx > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(R.xbar), 0, err));
+        if (ok) stage_rows<FMT, PADDED, true, kSmemBatch>(xs, x_dtype, 0, mb, rows, k, warp, lane, xq, pl, sx, x16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(R.xdone));
+    } else {
+        stage_rows<FMT, PADDED, false, kStageBatch>(x, x_dtype, m0, mb, rows, k, warp, lane, xq, pl, sx, x16);
+    }
+    bar_sync(2, kWarps * 32);
+    return ok;
+}
+
 // FMT 0: Q8_0 planes (wq = int8 [n][k], wd = fp16 [n][k / 32]); FMT 1: Q4_K
 // superblocks (wq = [n][k / 256][144], wd unused).  CTA c owns the contiguous
 // rows [c n / G, (c + 1) n / G) of G CTAs; warp kWarps (the producer) streams
@@ -232,15 +399,14 @@ __device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Sta
 template <int FMT, int MB>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     gemv_stream_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wd, int64_t n, int64_t k,
-                       const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots,
+                       const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots, int nx,
                        uint32_t* __restrict__ err) {
     pdl_trigger();
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t qbytes = FMT == 0 ? (uint32_t)k : (uint32_t)(k >> 8) * 144u;  // one row
     const uint32_t dbytes = FMT == 0 ? (uint32_t)(k >> 4) : 0u;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kMaxSlots;
+    const Ring R = ring_of(smem, slots, nx);
     Staged st;
     st.pl = plane_len(k);
     int8_t* xq = reinterpret_cast<int8_t*>(smem + kBarBytes);
@@ -258,23 +424,15 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     auto issue = [&](int64_t i, int slot) {  // producer lane 0: stage i into `slot` (= i mod slots)
         const int64_t ra = r0 + i * kStageRows;
         const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
-        const uint32_t bar = smem_u32(full + slot);
+        const uint32_t bar = smem_u32(R.full + slot);
         const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
         mbar_arrive_expect_tx(bar, rows * (qbytes + dbytes));
         bulk_load(dst, wq + ra * (int64_t)qbytes, rows * qbytes, bar);
         if (FMT == 0) bulk_load(dst + qstage, wd + ra * (int64_t)dbytes, rows * dbytes, bar);
     };
-    // Before the wait only L2 prefetches of the first stages go out (the weights
-    // never come from an earlier kernel): copies into shared memory issued now
-    // would sit ahead of the activation loads on the SM's return path.
     if (warp == kWarps && lane == 0) {
-        for (int s = 0; s < slots; s++) {
-            mbar_init(smem_u32(full + s), 1);
-            mbar_init(smem_u32(empty + s), kWarps);
-        }
-        fence_barrier_init();
-        for (int64_t i = 0; i < min(nst, (int64_t)kEarlyStages); i++) issue(i, (int)i);
-        for (int64_t i = kEarlyStages; i < min(nst, (int64_t)kEarlyStages + 2); i++) {
+        ring_init(R);
+        for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {  // the weights never come from an earlier kernel
             const int64_t ra = r0 + i * kStageRows;
             const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
             bulk_prefetch_l2(wq + ra * (int64_t)qbytes, rows * qbytes);
@@ -286,72 +444,22 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     pdl_wait();
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
-    if (warp < kWarps) {
-        // the warp's blocks kStageBatch at a time: every load of a batch is in
-        // flight before the first block's reductions wait on one; once the first
-        // batch is requested the producer may start the copies (named barrier 1)
-        const int nblk = (int)(k >> 5);
-        bool announced = false;
-        for (int j = 0; j < mb; j++) {
-            for (int b0 = warp; b0 < nblk; b0 += kWarps * kStageBatch) {
-                float xv[kStageBatch];
-                bool valid[kStageBatch];
-                int bs[kStageBatch];
-#pragma unroll
-                for (int u = 0; u < kStageBatch; u++) {
-                    bs[u] = b0 + u * kWarps;
-                    valid[u] = bs[u] < nblk;
-                    xv[u] = valid[u] ? load_act(x, x_dtype, (size_t)(m0 + j) * k + 32 * bs[u] + lane) : 0.0f;
-                }
-                if (!announced) {
-                    bar_arrive(1, (kWarps + 1) * 32);
-                    announced = true;
-                }
-                stage_blocks<FMT, kStageBatch>(xv, valid, bs, lane, xq + (size_t)j * 3 * st.pl, st.pl, sx + j * nblk,
-                                               x16 + j * (k >> 4));
-            }
-        }
-        if (!announced) bar_arrive(1, (kWarps + 1) * 32);
-        bar_sync(2, kWarps * 32);  // the consumers: every block staged
-    }
+    const size_t esize = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
+    const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
+    if (warp < kWarps)
+        consume_activations<FMT, true>(R, x, x_dtype, xs, m0, mb, mb, k, warp, lane, xq, (int)st.pl, sx, x16, err);
 
     if (warp == kWarps) {  // producer
-        bar_sync(1, (kWarps + 1) * 32);  // the activation loads are requested
-        if (lane == 0) {
-            // slot and phase advance with i (no division in the loop)
-            int64_t issued = min(nst, (int64_t)kEarlyStages);
-            int slot = (int)issued;
-            uint32_t phase = 0;  // parity of the slot's current use: 0 on the first pass over the ring
-            if (slot == slots) {
-                slot = 0;
-                phase = 1;
-            }
-            for (int64_t i = issued; i < nst; i++) {
-                if (i >= slots) {  // the stage that used this slot has been read by every consumer
-                    if (!mbar_wait(smem_u32(empty + slot), phase ^ 1u, err)) break;
-                    fence_proxy_async_smem();
-                }
-                issue(i, slot);
-                issued = i + 1;
-                if (++slot == slots) {
-                    slot = 0;
-                    phase ^= 1u;
-                }
-            }
-            // leave no copy in flight into this CTA's shared memory: the last
-            // min(slots, issued) stages, one per slot, walked backwards
-            for (int64_t q = 0; q < min((int64_t)slots, issued); q++) {
-                slot = slot == 0 ? slots - 1 : slot - 1;
-                if (slot == slots - 1) phase ^= 1u;
-                mbar_wait(smem_u32(full + slot), phase, err);
-            }
-        }
+        if (nx == 0) bar_sync(1, (kWarps + 1) * 32);  // the activation loads are requested
+        if (lane == 0)
+            produce(R, nst, issue, static_cast<const uint8_t*>(x) + (size_t)m0 * k * esize,
+                    (uint32_t)((size_t)mb * k * esize), xs, err);
         return;
     }
     int slot = 0;
     uint32_t phase = 0;
     for (int64_t i = 0; i < nst; i++) {
-        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(full + slot), phase, err))) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(R.full + slot), phase, err))) break;
         const int64_t r = r0 + i * kStageRows + warp;
         if (r < r1) {
             const uint8_t* stage = ring + (size_t)slot * stage_bytes;
@@ -373,7 +481,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             }
         }
         __syncwarp();  // every lane has read its row of the stage
-        if (lane == 0) mbar_arrive(smem_u32(empty + slot));
+        if (lane == 0) mbar_arrive(smem_u32(R.empty + slot));
         if (++slot == slots) {
             slot = 0;
             phase ^= 1u;
@@ -421,7 +529,7 @@ __host__ __device__ constexpr size_t mma_fixed_bytes(int mt, int64_t k) {
 template <int MT>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     gemv_mma_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wd, int64_t n, int64_t k,
-                    const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots,
+                    const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots, int nx,
                     uint32_t* __restrict__ err) {
     constexpr int MB = 4 * MT;
     pdl_trigger();
@@ -431,8 +539,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int nblk = (int)(k >> 5);
     const int64_t plm = mma_plane_len(k), rl = mma_row_len(k);
     const uint32_t dbytes = (uint32_t)(k >> 4);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kMaxSlots;
+    const Ring R = ring_of(smem, slots, nx);
     int8_t* xq = reinterpret_cast<int8_t*>(smem + kBarBytes);             // [MB][3][plm]
     float* sx = reinterpret_cast<float*>(xq + (size_t)MB * 3 * plm);     // [MB][nblk]
     float* red = sx + MB * nblk;                                         // [2][kWarps][2][MT][32]
@@ -445,19 +552,15 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     auto issue = [&](int64_t i, int slot) {  // producer lane 0: stage i into `slot`
         const int64_t ra = r0 + i * kStageRows;
         const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
-        const uint32_t bar = smem_u32(full + slot);
+        const uint32_t bar = smem_u32(R.full + slot);
         const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
         mbar_arrive_expect_tx(bar, rows * ((uint32_t)k + dbytes));
         for (uint32_t r = 0; r < rows; r++) bulk_load(dst + r * (uint32_t)rl, wq + (ra + r) * k, (uint32_t)k, bar);
         bulk_load(dst + (uint32_t)scale_off, wd + ra * (int64_t)dbytes, rows * dbytes, bar);
     };
     if (warp == kWarps && lane == 0) {
-        for (int s = 0; s < slots; s++) {
-            mbar_init(smem_u32(full + s), 1);
-            mbar_init(smem_u32(empty + s), kWarps);
-        }
-        fence_barrier_init();
-        for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {
+        ring_init(R);
+        for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {  // the weights never come from an earlier kernel
             const int64_t ra = r0 + i * kStageRows;
             const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
             bulk_prefetch_l2(wq + ra * k, rows * (uint32_t)k);
@@ -469,56 +572,16 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     pdl_wait();
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
-    if (warp < kWarps) {
-        bool announced = false;
-        for (int j = 0; j < MB; j++) {  // rows past mb are staged as zeros (their outputs are not stored)
-            for (int b0 = warp; b0 < nblk; b0 += kWarps * kStageBatch) {
-                float xv[kStageBatch];
-                bool valid[kStageBatch];
-                int bs[kStageBatch];
-#pragma unroll
-                for (int u = 0; u < kStageBatch; u++) {
-                    bs[u] = b0 + u * kWarps;
-                    valid[u] = bs[u] < nblk;
-                    xv[u] = valid[u] && j < mb ? load_act(x, x_dtype, (size_t)(m0 + j) * k + 32 * bs[u] + lane)
-                                               : 0.0f;
-                }
-                if (!announced) {
-                    bar_arrive(1, (kWarps + 1) * 32);
-                    announced = true;
-                }
-                stage_blocks<0, kStageBatch, false>(xv, valid, bs, lane, xq + (size_t)j * 3 * plm, plm,
-                                                    sx + j * nblk, nullptr);
-            }
-        }
-        if (!announced) bar_arrive(1, (kWarps + 1) * 32);
-        bar_sync(2, kWarps * 32);  // the consumers: every block staged
-    }
+    const size_t esize = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
+    const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
+    if (warp < kWarps)  // rows past mb are staged as zeros (their outputs are not stored)
+        consume_activations<0, false>(R, x, x_dtype, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx, nullptr, err);
 
     if (warp == kWarps) {  // producer
-        bar_sync(1, (kWarps + 1) * 32);
-        if (lane == 0) {
-            int64_t issued = 0;
-            int slot = 0;
-            uint32_t phase = 0;
-            for (int64_t i = 0; i < nst; i++) {
-                if (i >= slots) {
-                    if (!mbar_wait(smem_u32(empty + slot), phase ^ 1u, err)) break;
-                    fence_proxy_async_smem();
-                }
-                issue(i, slot);
-                issued = i + 1;
-                if (++slot == slots) {
-                    slot = 0;
-                    phase ^= 1u;
-                }
-            }
-            for (int64_t q = 0; q < min((int64_t)slots, issued); q++) {
-                slot = slot == 0 ? slots - 1 : slot - 1;
-                if (slot == slots - 1) phase ^= 1u;
-                mbar_wait(smem_u32(full + slot), phase, err);
-            }
-        }
+        if (nx == 0) bar_sync(1, (kWarps + 1) * 32);
+        if (lane == 0)
+            produce(R, nst, issue, static_cast<const uint8_t*>(x) + (size_t)m0 * k * esize,
+                    (uint32_t)((size_t)mb * k * esize), xs, err);
         return;
     }
 
@@ -544,7 +607,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     int slot = 0;
     uint32_t phase = 0;
     for (int64_t i = 0; i < nst; i++) {
-        if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait(smem_u32(full + slot), phase, err));
+        if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait(smem_u32(R.full + slot), phase, err));
         const uint8_t* stage = ring + (size_t)slot * stage_bytes;
         const uint16_t* dsc = reinterpret_cast<const uint16_t*>(stage + scale_off);
         float acc[2][MT][4];
@@ -554,6 +617,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             for (int mt = 0; mt < MT; mt++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) acc[g][mt][e] = 0.0f;
+#pragma unroll 2
         for (int kb = bad ? nblk : warp; kb < nblk; kb += kWarps) {
             uint32_t a[MT][4];
             float f[MT][2];
@@ -585,7 +649,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             }
         }
         __syncwarp();  // every lane has read the stage
-        if (lane == 0) mbar_arrive(smem_u32(empty + slot));
+        if (lane == 0) mbar_arrive(smem_u32(R.empty + slot));
         // sum over the levels (lanes 4 gq + qq with gq's low two bits = l), then
         // the lanes of level 0 leave the warp's partials for rows jj0 and jj0 + 2
         float* rb = red + (size_t)(i & 1) * kWarps * 2 * MT * 32 + (size_t)warp * 2 * MT * 32;
@@ -624,19 +688,19 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
 
 template <int MT>
 int run_mma(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
-            int64_t ldy, int slots, size_t smem, cudaStream_t s) {
+            int64_t ldy, int slots, int nx, size_t smem, cudaStream_t s) {
     const void* fn = (const void*)gemv_mma_kernel<MT>;
     GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t ctas = std::min<int64_t>(sm_count(), n);
     const dim3 grid((unsigned)ctas, (unsigned)((m + 4 * MT - 1) / (4 * MT)));
     return launch_pdl("gemv_mma_kernel<q8_0>", gemv_mma_kernel<MT>, grid, dim3((kWarps + 1) * 32), smem, s,
                       static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
-                      slots, device_error_word());
+                      slots, nx, device_error_word());
 }
 
 template <int FMT, int MB>
 int run(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
-        int64_t ldy, int slots, size_t smem, cudaStream_t s) {
+        int64_t ldy, int slots, int nx, size_t smem, cudaStream_t s) {
     const void* fn = (const void*)gemv_stream_kernel<FMT, MB>;
     GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t ctas = std::min<int64_t>(sm_count(), n);
@@ -644,7 +708,17 @@ int run(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int
     return launch_pdl(FMT == 0 ? "gemv_stream_kernel<q8_0>" : "gemv_stream_kernel<q4_k>",
                       gemv_stream_kernel<FMT, MB>, grid, dim3((kWarps + 1) * 32), smem, s,
                       static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
-                      slots, device_error_word());
+                      slots, nx, device_error_word());
+}
+
+// Ring slots that first hold the activations (one bulk copy of the CTA's
+// rows): 0 -- load them from global memory instead -- unless x is 16-byte
+// aligned and they leave at least one slot for the weights.
+static int activation_slots(const void* x, int dt, int64_t k, int mb, size_t stage_bytes, int slots) {
+    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return 0;
+    const size_t bytes = (size_t)mb * k * (dt == GDN_DTYPE_F32 ? 4 : 2);
+    const int nx = (int)((bytes + stage_bytes - 1) / stage_bytes);
+    return nx < slots ? nx : 0;
 }
 
 }  // namespace
@@ -697,24 +771,28 @@ int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64
                        int64_t m, float* y, int64_t ldy, cudaStream_t s) {
     int mb = 0, slots = 0;
     size_t smem = 0;
-    if (fmt == 0 && n > 0 && plan_mma(wq, wd, k, m, &mb, &slots, &smem))
-        return mb == 2 ? run_mma<2>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s)
-                       : run_mma<1>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+    if (fmt == 0 && n > 0 && plan_mma(wq, wd, k, m, &mb, &slots, &smem)) {
+        const int nx = activation_slots(x, dt, k, 4 * mb, mma_stage_bytes(k), slots);
+        return mb == 2 ? run_mma<2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s)
+                       : run_mma<1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+    }
     if (!plan(fmt, wq, wd, k, m, &mb, &slots, &smem)) return GDN_ERR_SHAPE;
     if (n <= 0) return GDN_OK;
+    const size_t stage = (size_t)kStageRows * (fmt == 0 ? k + k / 16 : (k / 256) * 144);
+    const int nx = activation_slots(x, dt, k, mb, stage, slots);
     if (fmt == 0) {
         switch (mb) {
-            case 1: return run<0, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
-            case 2: return run<0, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
-            case 4: return run<0, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
-            default: return run<0, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+            case 1: return run<0, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+            case 2: return run<0, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+            case 4: return run<0, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+            default: return run<0, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
         }
     }
     switch (mb) {
-        case 1: return run<1, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
-        case 2: return run<1, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
-        case 4: return run<1, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
-        default: return run<1, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, smem, s);
+        case 1: return run<1, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        case 2: return run<1, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        case 4: return run<1, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        default: return run<1, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
     }
 }
 
