@@ -516,17 +516,21 @@ __device__ __forceinline__ void imma_16832(int (&c)[4], const uint32_t (&a)[4], 
 }
 
 __host__ __device__ constexpr int64_t mma_plane_len(int64_t k) { return k + 16; }
-__host__ __device__ constexpr int64_t mma_row_len(int64_t k) { return k + 16; }
-__host__ __device__ constexpr size_t mma_stage_bytes(int64_t k) {
-    return (size_t)kStageRows * mma_row_len(k) + (size_t)kStageRows * (k / 16);
+// Bytes of a weight row in the stage: Q8_0 k int8 + 16; Q4_K its superblocks
+// (144 B each) padded so that the row stride is 4 (mod 32) words.
+__host__ __device__ constexpr int64_t mma_row_len(int fmt, int64_t k) {
+    return fmt == 0 ? k + 16 : (k / 256) * 144 + 4 * ((4 - 36 * (k / 256)) & 31);
 }
-// activation planes, block scales, and the two reduction buffers
-__host__ __device__ constexpr size_t mma_fixed_bytes(int mt, int64_t k) {
+__host__ __device__ constexpr size_t mma_stage_bytes(int fmt, int64_t k) {
+    return (size_t)kStageRows * mma_row_len(fmt, k) + (fmt == 0 ? (size_t)kStageRows * (k / 16) : 0);
+}
+// activation planes, block scales, (Q4_K) 16-sums, and the two reduction buffers
+__host__ __device__ constexpr size_t mma_fixed_bytes(int fmt, int mt, int64_t k) {
     return (size_t)(4 * mt) * 3 * mma_plane_len(k) + (size_t)(4 * mt) * (k / 32) * 4 +
-           (size_t)2 * kWarps * 2 * mt * 32 * 4;
+           (fmt == 1 ? (size_t)(4 * mt) * (k / 16) * 4 : 0) + (size_t)2 * kWarps * 2 * mt * 32 * 4;
 }
 
-template <int MT>
+template <int FMT, int MT>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     gemv_mma_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wd, int64_t n, int64_t k,
                     const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots, int nx,
@@ -537,14 +541,16 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, qq = lane & 3;
     const int nblk = (int)(k >> 5);
-    const int64_t plm = mma_plane_len(k), rl = mma_row_len(k);
-    const uint32_t dbytes = (uint32_t)(k >> 4);
+    const int64_t plm = mma_plane_len(k), rl = mma_row_len(FMT, k);
+    const uint32_t qbytes = FMT == 0 ? (uint32_t)k : (uint32_t)(k >> 8) * 144u;  // one row in global memory
+    const uint32_t dbytes = FMT == 0 ? (uint32_t)(k >> 4) : 0u;
     const Ring R = ring_of(smem, slots, nx);
     int8_t* xq = reinterpret_cast<int8_t*>(smem + kBarBytes);             // [MB][3][plm]
     float* sx = reinterpret_cast<float*>(xq + (size_t)MB * 3 * plm);     // [MB][nblk]
-    float* red = sx + MB * nblk;                                         // [2][kWarps][2][MT][32]
-    uint8_t* ring = smem + kBarBytes + mma_fixed_bytes(MT, k);
-    const size_t stage_bytes = mma_stage_bytes(k);
+    float* x16 = sx + MB * nblk;                                         // Q4_K: [MB][2 nblk]
+    float* red = x16 + (FMT == 1 ? MB * 2 * nblk : 0);                   // [2][kWarps][2][MT][32]
+    uint8_t* ring = smem + kBarBytes + mma_fixed_bytes(FMT, MT, k);
+    const size_t stage_bytes = mma_stage_bytes(FMT, k);
     const size_t scale_off = (size_t)kStageRows * rl;
 
     const int64_t r0 = (int64_t)blockIdx.x * n / gridDim.x, r1 = ((int64_t)blockIdx.x + 1) * n / gridDim.x;
@@ -554,17 +560,18 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
         const uint32_t bar = smem_u32(R.full + slot);
         const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
-        mbar_arrive_expect_tx(bar, rows * ((uint32_t)k + dbytes));
-        for (uint32_t r = 0; r < rows; r++) bulk_load(dst + r * (uint32_t)rl, wq + (ra + r) * k, (uint32_t)k, bar);
-        bulk_load(dst + (uint32_t)scale_off, wd + ra * (int64_t)dbytes, rows * dbytes, bar);
+        mbar_arrive_expect_tx(bar, rows * (qbytes + dbytes));
+        for (uint32_t r = 0; r < rows; r++)
+            bulk_load(dst + r * (uint32_t)rl, wq + (ra + r) * (int64_t)qbytes, qbytes, bar);
+        if (FMT == 0) bulk_load(dst + (uint32_t)scale_off, wd + ra * (int64_t)dbytes, rows * dbytes, bar);
     };
     if (warp == kWarps && lane == 0) {
         ring_init(R);
         for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {  // the weights never come from an earlier kernel
             const int64_t ra = r0 + i * kStageRows;
             const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
-            bulk_prefetch_l2(wq + ra * k, rows * (uint32_t)k);
-            bulk_prefetch_l2(wd + ra * (int64_t)dbytes, rows * dbytes);
+            bulk_prefetch_l2(wq + ra * (int64_t)qbytes, rows * qbytes);
+            if (FMT == 0) bulk_prefetch_l2(wd + ra * (int64_t)dbytes, rows * dbytes);
         }
     }
     __syncthreads();  // the barriers are initialised
@@ -575,7 +582,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const size_t esize = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)  // rows past mb are staged as zeros (their outputs are not stored)
-        consume_activations<0, false>(R, x, x_dtype, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx, nullptr, err);
+        consume_activations<FMT, false>(R, x, x_dtype, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx, x16, err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);
@@ -592,6 +599,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int lp = l == 3 ? 0 : l;
     const int8_t* arow[MT][2];
     const float* srow[MT][2];
+    const float* mrow[MT][2];  // Q4_K: the 16-sums of the row (level-0 rows only; else unused)
 #pragma unroll
     for (int mt = 0; mt < MT; mt++)
 #pragma unroll
@@ -599,7 +607,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             const int j = 4 * mt + jj0 + 2 * h;
             arow[mt][h] = xq + ((size_t)j * 3 + lp) * plm + 4 * qq;
             srow[mt][h] = sx + j * nblk;
+            mrow[mt][h] = x16 + j * 2 * nblk;
         }
+    const float mf = l == 0 ? 1.0f : 0.0f;  // the min term enters through level 0 only
     // The consumers meet at a named barrier every stage, so none may leave the
     // loop alone: a warp whose wait gave up (the error word is set) stops
     // waiting and computing but keeps arriving, so that every warp ends.
@@ -617,34 +627,90 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             for (int mt = 0; mt < MT; mt++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) acc[g][mt][e] = 0.0f;
+        if (FMT == 0) {
 #pragma unroll 2
-        for (int kb = bad ? nblk : warp; kb < nblk; kb += kWarps) {
-            uint32_t a[MT][4];
-            float f[MT][2];
-#pragma unroll
-            for (int mt = 0; mt < MT; mt++) {
-                a[mt][0] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb);
-                a[mt][1] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb);
-                a[mt][2] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb + 16);
-                a[mt][3] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb + 16);
-                f[mt][0] = srow[mt][0][kb] * lf;
-                f[mt][1] = srow[mt][1][kb] * lf;
-            }
-#pragma unroll
-            for (int g = 0; g < 2; g++) {
-                const uint8_t* brow = stage + (size_t)(8 * g + gq) * rl + 32 * kb + 4 * qq;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(brow + 16);
-                const float d0 = fp16_bits_to_float(dsc[(8 * g + 2 * qq) * nblk + kb]);
-                const float d1 = fp16_bits_to_float(dsc[(8 * g + 2 * qq + 1) * nblk + kb]);
+            for (int kb = bad ? nblk : warp; kb < nblk; kb += kWarps) {
+                uint32_t a[MT][4];
+                float f[MT][2];
 #pragma unroll
                 for (int mt = 0; mt < MT; mt++) {
-                    int c[4];
-                    imma_16832(c, a[mt], b0, b1);
-                    acc[g][mt][0] = fmaf((float)c[0], f[mt][0] * d0, acc[g][mt][0]);
-                    acc[g][mt][1] = fmaf((float)c[1], f[mt][0] * d1, acc[g][mt][1]);
-                    acc[g][mt][2] = fmaf((float)c[2], f[mt][1] * d0, acc[g][mt][2]);
-                    acc[g][mt][3] = fmaf((float)c[3], f[mt][1] * d1, acc[g][mt][3]);
+                    a[mt][0] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb);
+                    a[mt][1] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb);
+                    a[mt][2] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb + 16);
+                    a[mt][3] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb + 16);
+                    f[mt][0] = srow[mt][0][kb] * lf;
+                    f[mt][1] = srow[mt][1][kb] * lf;
+                }
+#pragma unroll
+                for (int g = 0; g < 2; g++) {
+                    const uint8_t* brow = stage + (size_t)(8 * g + gq) * rl + 32 * kb + 4 * qq;
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(brow + 16);
+                    const float d0 = fp16_bits_to_float(dsc[(8 * g + 2 * qq) * nblk + kb]);
+                    const float d1 = fp16_bits_to_float(dsc[(8 * g + 2 * qq + 1) * nblk + kb]);
+#pragma unroll
+                    for (int mt = 0; mt < MT; mt++) {
+                        int c[4];
+                        imma_16832(c, a[mt], b0, b1);
+                        acc[g][mt][0] = fmaf((float)c[0], f[mt][0] * d0, acc[g][mt][0]);
+                        acc[g][mt][1] = fmaf((float)c[1], f[mt][0] * d1, acc[g][mt][1]);
+                        acc[g][mt][2] = fmaf((float)c[2], f[mt][1] * d0, acc[g][mt][2]);
+                        acc[g][mt][3] = fmaf((float)c[3], f[mt][1] * d1, acc[g][mt][3]);
+                    }
+                }
+            }
+        } else {
+            // Q4_K: warp w takes the sub-block pairs (superblock sb, group cg)
+            // w, w + 16, ...: sub-blocks 2 cg (low nibbles of quant bytes
+            // 32 cg ..) and 2 cg + 1 (their high nibbles), k blocks 8 sb + 2 cg, + 1
+            const int npair = nblk >> 1;
+            for (int pi = bad ? npair : warp; pi < npair; pi += kWarps) {
+                const int sb = pi >> 2, cg = pi & 3;
+#pragma unroll
+                for (int half = 0; half < 2; half++) {
+                    const int kb = 8 * sb + 2 * cg + half;
+                    uint32_t a[MT][4];
+                    float f[MT][2], gm[MT][2];
+#pragma unroll
+                    for (int mt = 0; mt < MT; mt++) {
+                        a[mt][0] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb);
+                        a[mt][1] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb);
+                        a[mt][2] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb + 16);
+                        a[mt][3] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb + 16);
+                        f[mt][0] = srow[mt][0][kb] * lf;
+                        f[mt][1] = srow[mt][1][kb] * lf;
+                        gm[mt][0] = (mrow[mt][0][2 * kb] + mrow[mt][0][2 * kb + 1]) * mf;
+                        gm[mt][1] = (mrow[mt][1][2 * kb] + mrow[mt][1][2 * kb + 1]) * mf;
+                    }
+#pragma unroll
+                    for (int g = 0; g < 2; g++) {
+                        const uint8_t* blk = stage + (size_t)(8 * g + gq) * rl + sb * 144;
+                        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(blk + 16 + 32 * cg + 4 * qq);
+                        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(blk + 32 + 32 * cg + 4 * qq);
+                        const uint32_t b0 = (w0 >> (4 * half)) & 0x0F0F0F0Fu;
+                        const uint32_t b1 = (w1 >> (4 * half)) & 0x0F0F0F0Fu;
+                        float ds[2], dm[2];  // d sc and dmin m of this thread's two columns (weight rows)
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const uint8_t* hb = stage + (size_t)(8 * g + 2 * qq + e) * rl + sb * 144;
+                            const uint32_t dd = *reinterpret_cast<const uint32_t*>(hb);
+                            int sc, mn;
+                            scale_min(2 * cg + half, hb + 4, sc, mn);
+                            ds[e] = fp16_bits_to_float((uint16_t)(dd & 0xFFFFu)) * (float)sc;
+                            dm[e] = fp16_bits_to_float((uint16_t)(dd >> 16)) * (float)mn;
+                        }
+#pragma unroll
+                        for (int mt = 0; mt < MT; mt++) {
+                            int c[4];
+                            imma_16832(c, a[mt], b0, b1);
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                const int h = e >> 1, col = e & 1;
+                                acc[g][mt][e] = fmaf((float)c[e], f[mt][h] * ds[col], acc[g][mt][e]);
+                                acc[g][mt][e] = fmaf(-gm[mt][h], dm[col], acc[g][mt][e]);
+                            }
+                        }
+                    }
                 }
             }
         }
@@ -686,14 +752,15 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     }
 }
 
-template <int MT>
+template <int FMT, int MT>
 int run_mma(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
             int64_t ldy, int slots, int nx, size_t smem, cudaStream_t s) {
-    const void* fn = (const void*)gemv_mma_kernel<MT>;
+    const void* fn = (const void*)gemv_mma_kernel<FMT, MT>;
     GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t ctas = std::min<int64_t>(sm_count(), n);
     const dim3 grid((unsigned)ctas, (unsigned)((m + 4 * MT - 1) / (4 * MT)));
-    return launch_pdl("gemv_mma_kernel<q8_0>", gemv_mma_kernel<MT>, grid, dim3((kWarps + 1) * 32), smem, s,
+    return launch_pdl(FMT == 0 ? "gemv_mma_kernel<q8_0>" : "gemv_mma_kernel<q4_k>", gemv_mma_kernel<FMT, MT>, grid,
+                      dim3((kWarps + 1) * 32), smem, s,
                       static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
                       slots, nx, device_error_word());
 }
@@ -748,20 +815,21 @@ static int plan(int fmt, const void* wq, const void* wd, int64_t k, int64_t m, i
     return 0;
 }
 
-// The IMMA plan (Q8_0, three or more activation rows): 2 m-tiles (8 rows per
-// CTA) when 2 stages fit beside them, else 1; 0 if neither fits.
-static int plan_mma(const void* wq, const void* wd, int64_t k, int64_t m, int* mt_out, int* slots_out,
+// The IMMA plan (three or more activation rows): 2 m-tiles (8 rows per CTA)
+// when 2 stages fit beside them, else 1; 0 if neither fits.
+static int plan_mma(int fmt, const void* wq, const void* wd, int64_t k, int64_t m, int* mt_out, int* slots_out,
                     size_t* smem_out) {
     if (m < 3 || (m + 3) / 4 > 65535 || k < 512 || (k & 511) != 0) return 0;
-    if ((reinterpret_cast<uintptr_t>(wq) & 15) != 0 || (reinterpret_cast<uintptr_t>(wd) & 15) != 0) return 0;
+    if ((reinterpret_cast<uintptr_t>(wq) & 15) != 0) return 0;
+    if (fmt == 0 && (reinterpret_cast<uintptr_t>(wd) & 15) != 0) return 0;
     for (int mt = m > 4 ? 2 : 1; mt >= 1; mt--) {
-        const size_t base = kBarBytes + mma_fixed_bytes(mt, k);
+        const size_t base = kBarBytes + mma_fixed_bytes(fmt, mt, k);
         if (base >= kSmemLimit) continue;
-        const int slots = (int)std::min<size_t>(kMaxSlots, (kSmemLimit - base) / mma_stage_bytes(k));
+        const int slots = (int)std::min<size_t>(kMaxSlots, (kSmemLimit - base) / mma_stage_bytes(fmt, k));
         if (slots < 2) continue;
         *mt_out = mt;
         *slots_out = slots;
-        *smem_out = base + (size_t)slots * mma_stage_bytes(k);
+        *smem_out = base + (size_t)slots * mma_stage_bytes(fmt, k);
         return 1;
     }
     return 0;
@@ -771,10 +839,13 @@ int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64
                        int64_t m, float* y, int64_t ldy, cudaStream_t s) {
     int mb = 0, slots = 0;
     size_t smem = 0;
-    if (fmt == 0 && n > 0 && plan_mma(wq, wd, k, m, &mb, &slots, &smem)) {
-        const int nx = activation_slots(x, dt, k, 4 * mb, mma_stage_bytes(k), slots);
-        return mb == 2 ? run_mma<2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s)
-                       : run_mma<1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+    if (n > 0 && plan_mma(fmt, wq, wd, k, m, &mb, &slots, &smem)) {
+        const int nx = activation_slots(x, dt, k, 4 * mb, mma_stage_bytes(fmt, k), slots);
+        if (fmt == 0)
+            return mb == 2 ? run_mma<0, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s)
+                           : run_mma<0, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        return mb == 2 ? run_mma<1, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s)
+                       : run_mma<1, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
     }
     if (!plan(fmt, wq, wd, k, m, &mb, &slots, &smem)) return GDN_ERR_SHAPE;
     if (n <= 0) return GDN_OK;
