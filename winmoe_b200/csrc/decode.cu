@@ -343,9 +343,10 @@ inline int mark(PhaseEvents* pe, int i, cudaStream_t s) {
 }
 
 // Tensor-core projections pay off once a batch fills an M=128 tile reasonably
-// (Q4_K: from 8 rows, its CUDA-core GEMV being compute-bound).
+// (Q4_K: from 16 rows; below, the int8-tensor-core GEMV of gemv_stream.cu is
+// faster: 8 rows 42 against 78 us for the 35B layer's projections).
 constexpr int64_t kTcMinBatch = 64;
-constexpr int64_t kTcMinBatchQ4k = 8;
+constexpr int64_t kTcMinBatchQ4k = 16;
 // Split-K factor of the tensor-core out_proj (K = inner is long, N = hidden short).
 constexpr int kOutSplits = 8;
 // Split-K factor of the 2 Hv gate rows' exact tensor-core GEMM (one column tile).
