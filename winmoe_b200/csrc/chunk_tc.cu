@@ -55,12 +55,20 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) { return wmma16::p
 constexpr int kRing = 3;
 constexpr int kScanChunksInSmem = 1024;  // chunk decays staged in shared memory (T up to 64K)
 
+// A head's value rows are split over two CTAs (kVRows = 64 each, M = 64 MMA
+// tiles): the images a CTA moves per chunk are its halves of U'^T, S^T and D^T
+// plus the full W' and E^T -- 64 KB instead of 96 KB through one SM, which is
+// what bounds a chunk step -- and the chain of steps runs on twice the SMs.
+constexpr int kVRows = 64;
+constexpr uint32_t kHalfUBytes = kVRows * CH * 2;  // U'^T / D^T rows of one CTA: [64 v][64 t]
+constexpr uint32_t kHalfSBytes = kVRows * HD * 2;  // S^T rows of one CTA: [64 v][128 k] (two K blocks of 8 KB)
+
 struct ScanTcSmem {
-    uint8_t w[kRing][kImgWBytes];  // W' images [64 t][128 k]    (B of MMA1)
-    uint8_t e[kRing][kImgEBytes];  // E^T images [128 k][64 t]   (B of MMA2)
-    uint8_t u[kRing][kImgEBytes];  // U'^T images [128 v][64 t]  (row v read by its threads)
-    uint8_t s[kImgSBytes];         // S^T image [128 v][128 k]   (A of MMA1; the chunk's start state)
-    uint8_t d[kImgEBytes];         // D^T image [128 v][64 t]    (A of MMA2; the chunk's deltas)
+    uint8_t w[kRing][kImgWBytes];   // W' images [64 t][128 k]        (B of MMA1)
+    uint8_t e[kRing][kImgEBytes];   // E^T images [128 k][64 t]       (B of MMA2)
+    uint8_t u[kRing][kHalfUBytes];  // this CTA's U'^T rows [64 v][64 t]
+    uint8_t s[kHalfSBytes];         // S^T rows [64 v][128 k]         (A of MMA1; the chunk's start state)
+    uint8_t d[kHalfUBytes];         // D^T rows [64 v][64 t]          (A of MMA2; the chunk's deltas)
     float gc[kScanChunksInSmem];
     uint64_t full[kRing];          // a chunk's three images landed
     uint64_t mma_d, mma_s;         // MMA1 / MMA2 of a chunk completed
@@ -75,8 +83,11 @@ static_assert(offsetof(ScanTcSmem, e) % 1024 == 0 && offsetof(ScanTcSmem, u) % 1
 constexpr uint32_t kScanTmemCols = 256;  // S^T: columns 0..127; D^T: 128..191
 constexpr int kScanThreads = 256;
 
-// 256 threads: warps w and w + 4 share TMEM lanes 32 (w % 4) .. + 31 (value
-// columns v) and split the columns into halves: warps 0..3 take S^T columns
+// One CTA per (head, half of the value rows); 256 threads.  With M = 64 the
+// accumulator row i (local value row) sits in TMEM lane 32 (i / 16) + i % 16:
+// lanes 0..15 of each warp carry a row, lanes 16..31 only take part in the
+// warp-wide TMEM instructions.  Warps w and w + 4 share TMEM lanes
+// 32 (w % 4) .. and split the columns into halves: warps 0..3 take S^T columns
 // 0..63 (the image's first K block) and D^T columns 0..31, warps 4..7 the rest.
 // No block barrier sits on the chain of a chunk: each half announces its part
 // of an image on an mbarrier, and thread 0 issues the MMAs of that K block as
@@ -95,10 +106,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     ScanTcSmem& sm = *reinterpret_cast<ScanTcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int h = blockIdx.x;
+    const int h = blockIdx.x >> 1, vh = blockIdx.x & 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quad = warp & 3, half = warp >> 2;
-    const int v = 32 * quad + lane;  // TMEM lane = value column
+    const bool row_lane = lane < 16;               // this lane holds a row of the M = 64 tiles
+    const int vr = 16 * quad + (lane & 15);        // the local value row (image row)
+    const int v = kVRows * vh + vr;                // ... its value column of S
     const bool issuer = tid == 0, copier = tid == 32;
 
     if (warp == 0) {
@@ -126,10 +139,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
         const int buf = (int)(c % kRing);
         const uint32_t bar = smem_u32(&sm.full[buf]);
         const int64_t i = (int64_t)h * nc + c;
-        mbar_arrive_expect_tx(bar, kImgWBytes + 2 * kImgEBytes);
+        mbar_arrive_expect_tx(bar, kImgWBytes + kImgEBytes + kHalfUBytes);
         bulk_load(smem_u32(sm.w[buf]), wimg + i * kImgWBytes, kImgWBytes, bar);
         bulk_load(smem_u32(sm.e[buf]), eimg + i * kImgEBytes, kImgEBytes, bar);
-        bulk_load(smem_u32(sm.u[buf]), uimg + i * kImgEBytes, kImgEBytes, bar);
+        // rows 64 vh .. of the [128 v][64 t] image: one contiguous 8 KB (same swizzle phase)
+        bulk_load(smem_u32(sm.u[buf]), uimg + i * kImgEBytes + vh * kHalfUBytes, kHalfUBytes, bar);
     };
     tc_fence_before();
     __syncthreads();
@@ -149,12 +163,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
     {
         uint32_t r[64];
 #pragma unroll
-        for (int i = 0; i < 64; i++) r[i] = __float_as_uint(Sh[(int64_t)(64 * half + i) * HD + v]);
+        for (int i = 0; i < 64; i++) r[i] = row_lane ? __float_as_uint(Sh[(int64_t)(64 * half + i) * HD + v]) : 0u;
         tmem_store_32x32b_x64(tS, r);
     }
 
-    constexpr uint32_t idesc1 = umma_idesc_f16(128, 64, true);   // D^T = S^T W'^T
-    constexpr uint32_t idesc2 = umma_idesc_f16(128, 128, true);  // S^T += D^T E
+    constexpr uint32_t idesc1 = umma_idesc_f16(kVRows, 64, true);   // D^T = S^T W'^T
+    constexpr uint32_t idesc2 = umma_idesc_f16(kVRows, 128, true);  // S^T += D^T E
     bool ok = true;
     int64_t c = 0;
     for (; c < nc && ok; c++) {
@@ -178,7 +192,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
                     pack2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
                     pack2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
                     pack2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
-                *reinterpret_cast<uint4*>(sm.s + img_off(HD, v, 64 * half + 8 * q)) = pk;
+                if (row_lane) *reinterpret_cast<uint4*>(sm.s + img_off(kVRows, vr, 64 * half + 8 * q)) = pk;
             }
 #pragma unroll
             for (int i = 0; i < 64; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * gam);
@@ -198,7 +212,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
                 if (ok) {
 #pragma unroll
                     for (int ks = 0; ks < 4; ks++)
-                        mma_f16_ss(tmem + 128, umma_desc_sw128(a0 + kb * (HD * 128) + ks * 32),
+                        mma_f16_ss(tmem + 128, umma_desc_sw128(a0 + kb * (kVRows * 128) + ks * 32),
                                    umma_desc_sw128(b0 + kb * (CH * 128) + ks * 32), idesc1, (kb | ks) != 0);
                 }
             }
@@ -207,8 +221,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
             // the chunk's start state leaves; the previous deltas' store has read its image
             ok = mbar_wait(smem_u32(&sm.s_half[0]), par, err) && ok;
             ok = mbar_wait(smem_u32(&sm.s_half[1]), par, err) && ok;
-            if (ok) {
-                bulk_store(simg + ((int64_t)h * nc + c) * kImgSBytes, smem_u32(sm.s), kImgSBytes);
+            if (ok) {  // this CTA's rows of each K block of the [128 v][128 k] image
+                uint8_t* dst = simg + ((int64_t)h * nc + c) * kImgSBytes + vh * (kHalfSBytes / 2);
+                bulk_store(dst, smem_u32(sm.s), kHalfSBytes / 2);
+                bulk_store(dst + kImgSBytes / 2, smem_u32(sm.s) + kHalfSBytes / 2, kHalfSBytes / 2);
                 bulk_commit();
             }
             bulk_wait_read<1>();
@@ -231,7 +247,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 const int t8 = 32 * half + 8 * q;
-                const uint4 u4 = *reinterpret_cast<const uint4*>(sm.u[buf] + img_off(HD, v, t8));
+                const uint4 u4 = *reinterpret_cast<const uint4*>(sm.u[buf] + img_off(kVRows, vr, t8));
                 const uint32_t uw[4] = {u4.x, u4.y, u4.z, u4.w};
                 uint32_t dw[4];
 #pragma unroll
@@ -239,7 +255,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
                     const float2 uf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[i]));
                     dw[i] = pack2(uf.x - __uint_as_float(r[8 * q + 2 * i]), uf.y - __uint_as_float(r[8 * q + 2 * i + 1]));
                 }
-                *reinterpret_cast<uint4*>(sm.d + img_off(HD, v, t8)) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
+                if (row_lane) *reinterpret_cast<uint4*>(sm.d + img_off(kVRows, vr, t8)) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
             }
         }
         fence_proxy_async_smem();
@@ -264,7 +280,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
             ok = mbar_wait(smem_u32(&sm.d_half[0]), par, err) && ok;
             ok = mbar_wait(smem_u32(&sm.d_half[1]), par, err) && ok;
             if (ok) {
-                bulk_store(dimg + ((int64_t)h * nc + c) * kImgEBytes, smem_u32(sm.d), kImgEBytes);
+                bulk_store(dimg + ((int64_t)h * nc + c) * kImgEBytes + vh * kHalfUBytes, smem_u32(sm.d), kHalfUBytes);
                 bulk_commit();
             }
             bulk_wait_read<1>();
@@ -281,8 +297,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_tc_kernel(const ui
         if (okf) {
             uint32_t r[64];
             tmem_load_32x32b_x64(tS, r);
+            if (row_lane)
 #pragma unroll
-            for (int i = 0; i < 64; i++) Sh[(int64_t)(64 * half + i) * HD + v] = __uint_as_float(r[i]);
+                for (int i = 0; i < 64; i++) Sh[(int64_t)(64 * half + i) * HD + v] = __uint_as_float(r[i]);
         }
     } else if (issuer) {
         // the error word is set: let the MMAs already issued finish (bounded)
@@ -582,7 +599,7 @@ int launch_chunk_scan_tc(const uint8_t* wimg, const uint8_t* eimg, const uint8_t
     const size_t smem = sizeof(ScanTcSmem) + 1024;
     int st = set_smem(chunk_scan_tc_kernel, smem);
     if (st) return st;
-    return launch_pdl("chunk_scan_tc_kernel", chunk_scan_tc_kernel, dim3((unsigned)hv), dim3(kScanThreads), smem, s,
+    return launch_pdl("chunk_scan_tc_kernel", chunk_scan_tc_kernel, dim3((unsigned)(2 * hv)), dim3(kScanThreads), smem, s,
                       wimg, eimg, uimg, gchunk, S, simg, dimg, nc, device_error_word());
 }
 
