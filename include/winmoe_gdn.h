@@ -61,7 +61,7 @@ typedef enum gdn_status {
 enum { GDN_DTYPE_F32 = 0, GDN_DTYPE_BF16 = 1, GDN_DTYPE_F16 = 2 };
 
 /* GGML type ids (engine/runtime/gguf_parser.h:21-29). */
-enum { GDN_GGML_F32 = 0, GDN_GGML_Q8_0 = 8, GDN_GGML_Q4_K = 12 };
+enum { GDN_GGML_F32 = 0, GDN_GGML_Q8_0 = 8, GDN_GGML_Q4_K = 12, GDN_GGML_Q5_K = 13 };
 
 /* Head maps of the Q/K key group shared by a value head h (hpg = Hv / Hk). */
 enum {
@@ -151,12 +151,50 @@ GDN_API int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64
 
 /* y[m][n] = sum_k x[m][k] * W[n][k], W Q4_K [n_rows][k], fp32 accumulation
  * (q4k_matvec_kernel, engine/runtime/gpu_offload.cu:206-268).  x_dtype F32,
- * BF16 or F16; k % 256 == 0.  fp16 x with m >= 8 runs on the tensor cores
- * (superblocks by TMA, dequantised in shared memory into hi + lo fp16
+ * BF16 or F16; k % 256 == 0.  fp16 x with m >= 8 runs on the tcgen05 tensor
+ * cores (superblocks by TMA, dequantised in shared memory into hi + lo fp16
  * operands: the fp32 product of those activations up to summation order);
- * otherwise a CUDA-core GEMV dequantising in registers. */
+ * otherwise the streamed GEMV: weight rows by bulk copy, the activations split
+ * per 32-block into three int8 levels (error below 5e-7 of the block's
+ * max |x|) and the products summed exactly in int32 (dp4a for m <= 2, the
+ * int8 tensor cores for m >= 3 when k % 512 == 0), scaled in fp32. */
 GDN_API int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k,
                   const void* x, int x_dtype, int64_t m, float* y, void* stream);
+
+/*
+ * Q5_K: GGUF superblocks of 256 weights, {fp16 d; fp16 dmin; u8 scales[12];
+ * u8 qh[32]; u8 qs[128]} (176 bytes, engine/runtime/q5k_dequant.h:19-25), used
+ * as stored: weight 64c + j of a superblock is the low nibble of qs[32c + j]
+ * with bit 2c of qh[j] as its fifth bit, weight 64c + 32 + j the high nibble
+ * with bit 2c + 1 (engine/runtime/gpu_offload.cu:302-309).
+ * gdn_q5_k_dequant: fp32 weights, w = (d*sc)*q - (dmin*m), each operation
+ * rounded once; cols % 256 == 0.
+ */
+GDN_API int gdn_q5_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, void* stream);
+
+/* y[m][n] = sum_k x[m][k] * W[n][k], W Q5_K [n_rows][k], fp32 activations
+ * (q5k_matvec_kernel / q5k_expert_kernel, engine/runtime/gpu_offload.cu:271-331,
+ * 400-457); the streamed GEMV as gdn_q4_k_gemm's.  blocks 16-byte aligned,
+ * k % 256 == 0 (GDN_ERR_SHAPE if a row's stages do not fit). */
+GDN_API int gdn_q5_k_gemm(const void* blocks, int64_t n_rows, int64_t k,
+                  const void* x, int x_dtype, int64_t m, float* y, void* stream);
+
+/*
+ * One MoE expert's FFN for m tokens, the reference's fused GPU route
+ * (gpu_expert_ffn_fused, engine/runtime/gpu_offload.cu:718-751): gate and up
+ * projections [inter][hidden] (GDN_GGML_Q4_K or GDN_GGML_Q5_K, gate_type for
+ * both), a = (g * sigmoid(g)) * u (swiglu_kernel, :460-466), then the down
+ * projection [hidden][inter] (down_type).  accumulate == 0: out[m][hidden] =
+ * y (weight unused, as gpu_expert_ffn_fused returns it); accumulate != 0:
+ * out += weight * y (gpu_expert_batch_add / weighted_add_kernel, :766-793).
+ * Device pointers; x fp32, bf16 or fp16; hidden and inter multiples of 256;
+ * the caller's workspace of gdn_expert_ffn_workspace_size(m, hidden, inter)
+ * bytes.  The expert cache that owns the weights is the reference's.
+ */
+GDN_API size_t gdn_expert_ffn_workspace_size(int64_t m, int64_t hidden, int64_t inter);
+GDN_API int gdn_expert_ffn(const void* w_gate, const void* w_up, const void* w_down, int gate_type, int down_type,
+                  int64_t hidden, int64_t inter, const void* x, int x_dtype, int64_t m, float* out,
+                  float weight, int accumulate, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- the layer */
 

@@ -34,6 +34,7 @@
 #define Q8_0_BYTES 34
 #define QK_K 256
 #define Q4_K_BYTES 144
+#define Q5_K_BYTES 176
 #define Q8_K_BYTES 292 /* float d; int8 qs[256]; int16 bsums[16] */
 #define CONV_W 4
 
@@ -281,16 +282,121 @@ EXPORT void orc_q4_k_matvec(float* out, const uint8_t* W, const float* x,
     free(xq);
 }
 
+/* ---------------------------------------------------------------- Q5_K */
+
+/* The 5-bit value of weight 64c + j (low: half 0) or 64c + 32 + j (half 1) of a
+ * Q5_K superblock in the GGML layout of engine/runtime/gpu_offload.cu:302-309
+ * (and q5k_dot_q8k, q5k_dequant.h:103-128): the nibble of qs[32c + j] with bit
+ * 2c + half of qh[j] as its fifth bit. */
+static inline int q5_k_value(const uint8_t* blk, int c, int j, int half) {
+    const uint8_t* qh = blk + 16;
+    const uint8_t* qs = blk + 48;
+    int nib = half ? (qs[32 * c + j] >> 4) : (qs[32 * c + j] & 0x0F);
+    return nib | (((qh[j] >> (2 * c + half)) & 1) << 4);
+}
+
+/* Q5_K float dequant, fp32 expression of engine/runtime/gpu_offload.cu:302-309:
+ * w = (d*sc)*q - (dmin*m), each operation rounded once. */
+EXPORT void orc_q5_k_dequant(float* out, const uint8_t* blocks, long n) {
+    for (long b = 0; b < n / QK_K; b++) {
+        const uint8_t* blk = blocks + b * Q5_K_BYTES;
+        float d = orc_fp16_to_fp32(rd16(blk)), dmin = orc_fp16_to_fp32(rd16(blk + 2));
+        uint8_t sc[8], mn[8];
+        orc_q4_k_scales(blk + 4, sc, mn);
+        for (int c = 0; c < 4; c++) {
+            float sl = d * (float)sc[2 * c], ml = dmin * (float)mn[2 * c];
+            float sh = d * (float)sc[2 * c + 1], mh = dmin * (float)mn[2 * c + 1];
+            for (int j = 0; j < 32; j++) {
+                float pl = sl * (float)q5_k_value(blk, c, j, 0), ph = sh * (float)q5_k_value(blk, c, j, 1);
+                out[b * QK_K + 64 * c + j] = pl - ml;
+                out[b * QK_K + 64 * c + 32 + j] = ph - mh;
+            }
+        }
+    }
+}
+
+/* q5k_dot_q8k: engine/runtime/q5k_dequant.h:80-157, the same integer lanes as
+ * Q4_K (lane l holds bytes 4l..4l+3 of every 32-byte chunk), then d times each
+ * lane, reduced as add(lo128, hi128), hadd, hadd. */
+static float q5_k_dot_q8k(const uint8_t* blk, const uint8_t* kb) {
+    float ad = *(const float*)kb;
+    const int8_t* q8 = (const int8_t*)(kb + 4);
+    const int16_t* bs = (const int16_t*)(kb + 4 + QK_K);
+    float d = orc_fp16_to_fp32(rd16(blk)) * ad;
+    float dmin = orc_fp16_to_fp32(rd16(blk + 2)) * ad;
+    uint8_t sc[8], mn[8];
+    orc_q4_k_scales(blk + 4, sc, mn);
+    int32_t min_sum = 0;
+    for (int s = 0; s < 8; s++) min_sum += (int32_t)mn[s] * (bs[2 * s] + bs[2 * s + 1]);
+    int32_t lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int c = 0; c < 4; c++) {
+        for (int b = 0; b < 32; b++) {
+            int l = b / 4;
+            lane[l] += (int32_t)sc[2 * c] * (int32_t)q5_k_value(blk, c, b, 0) * (int32_t)q8[64 * c + b];
+            lane[l] += (int32_t)sc[2 * c + 1] * (int32_t)q5_k_value(blk, c, b, 1) * (int32_t)q8[64 * c + 32 + b];
+        }
+    }
+    float v[8];
+    for (int l = 0; l < 8; l++) v[l] = d * (float)lane[l];
+    float s4[4];
+    for (int i = 0; i < 4; i++) s4[i] = v[i] + v[4 + i];
+    float h0 = s4[0] + s4[1], h1 = s4[2] + s4[3];
+    float result = h0 + h1;
+    return result - dmin * (float)min_sum;
+}
+
+/* Q5_K GEMV.  act_mode 0: q5k_matvec (engine/runtime/q5k_dequant.h:160-195),
+ * Q8_K activations.  act_mode 1: fp32 activations, per-superblock sum of
+ * w_lo*x + w_hi*x in the loop order of engine/runtime/gpu_offload.cu:296-317. */
+EXPORT void orc_q5_k_matvec(float* out, const uint8_t* W, const float* x,
+                            int out_dim, int in_dim, int act_mode) {
+    int bpr = in_dim / QK_K;
+    uint8_t* xq = NULL;
+    if (act_mode == 0) {
+        xq = (uint8_t*)malloc((size_t)bpr * Q8_K_BYTES);
+        orc_quantize_row_q8_K(xq, x, (long)bpr * QK_K);
+    }
+    for (int r = 0; r < out_dim; r++) {
+        const uint8_t* row = W + (size_t)r * bpr * Q5_K_BYTES;
+        float sum = 0.0f;
+        for (int b = 0; b < bpr; b++) {
+            const uint8_t* blk = row + (size_t)b * Q5_K_BYTES;
+            if (xq) {
+                sum += q5_k_dot_q8k(blk, xq + (size_t)b * Q8_K_BYTES);
+                continue;
+            }
+            float d = orc_fp16_to_fp32(rd16(blk)), dmin = orc_fp16_to_fp32(rd16(blk + 2));
+            uint8_t sc[8], mn[8];
+            orc_q4_k_scales(blk + 4, sc, mn);
+            float bsum = 0.0f;
+            for (int c = 0; c < 4; c++) {
+                float sl = d * (float)sc[2 * c], ml = dmin * (float)mn[2 * c];
+                float sh = d * (float)sc[2 * c + 1], mh = dmin * (float)mn[2 * c + 1];
+                for (int j = 0; j < 32; j++) {
+                    float wl = sl * (float)q5_k_value(blk, c, j, 0) - ml;
+                    float wh = sh * (float)q5_k_value(blk, c, j, 1) - mh;
+                    bsum += wl * x[b * QK_K + 64 * c + j] + wh * x[b * QK_K + 64 * c + 32 + j];
+                }
+            }
+            sum += bsum;
+        }
+        out[r] = sum;
+    }
+    free(xq);
+}
+
 /* ------------------------------------------------------------ projection */
 
-/* quant_matvec dispatch: engine/runtime/transformer.h:157-194, types 8 (Q8_0)
- * and 12 (Q4_K); any other type is read as fp32 rows. */
+/* quant_matvec dispatch: engine/runtime/transformer.h:157-194, types 8 (Q8_0),
+ * 12 (Q4_K) and 13 (Q5_K); any other type is read as fp32 rows. */
 EXPORT void orc_quant_matvec(float* out, const void* W, const float* x,
                              int out_dim, int in_dim, int type, int act_mode) {
     if (type == 8) {
         orc_q8_0_matvec(out, (const uint8_t*)W, x, out_dim, in_dim, act_mode);
     } else if (type == 12) {
         orc_q4_k_matvec(out, (const uint8_t*)W, x, out_dim, in_dim, act_mode);
+    } else if (type == 13) {
+        orc_q5_k_matvec(out, (const uint8_t*)W, x, out_dim, in_dim, act_mode);
     } else {
         const float* wf = (const float*)W;
         for (int r = 0; r < out_dim; r++) {
@@ -299,6 +405,32 @@ EXPORT void orc_quant_matvec(float* out, const void* W, const float* x,
             out[r] = s;
         }
     }
+}
+
+/* One expert's FFN for one token, the fused GPU route of
+ * engine/runtime/gpu_offload.cu:718-751 (gpu_expert_ffn_fused): gate and up
+ * projections (hidden -> inter), SwiGLU act = (g * sigmoid(g)) * up with
+ * sigmoid = 1 / (1 + expf(-g)) (swiglu_kernel, gpu_offload.cu:460-466), then the
+ * down projection (inter -> hidden).  `weight` scales the result into out
+ * (accumulate != 0: out += weight * y, gpu_offload.cu:469-471 and 785-789;
+ * else out = y). */
+EXPORT void orc_expert_ffn(float* out, const float* x, const void* w_gate, const void* w_up, const void* w_down,
+                           int gate_type, int down_type, int hidden, int inter, float weight, int accumulate,
+                           int act_mode) {
+    float* g = (float*)malloc((size_t)inter * sizeof(float));
+    float* u = (float*)malloc((size_t)inter * sizeof(float));
+    float* y = (float*)malloc((size_t)hidden * sizeof(float));
+    orc_quant_matvec(g, w_gate, x, inter, hidden, gate_type, act_mode);
+    orc_quant_matvec(u, w_up, x, inter, hidden, gate_type, act_mode);
+    for (int i = 0; i < inter; i++) {
+        float sig = 1.0f / (1.0f + expf(-g[i]));
+        g[i] = (g[i] * sig) * u[i];
+    }
+    orc_quant_matvec(y, w_down, g, hidden, inter, down_type, act_mode);
+    for (int i = 0; i < hidden; i++) out[i] = accumulate ? out[i] + weight * y[i] : y[i];
+    free(g);
+    free(u);
+    free(y);
 }
 
 /* ------------------------------------------------------------ GDN helpers */

@@ -76,10 +76,12 @@ class Port:
         h = self.h
         h.orc_fp16_to_fp32.restype = C.c_float
         h.orc_fp16_to_fp32.argtypes = [C.c_uint16]
-        for n in ("orc_q8_0_dequant", "orc_q4_k_dequant", "orc_quantize_row_q8_K"):
+        for n in ("orc_q8_0_dequant", "orc_q4_k_dequant", "orc_q5_k_dequant", "orc_quantize_row_q8_K"):
             getattr(h, n).argtypes = [_vp, _vp, _l]
         h.orc_q8_0_matvec.argtypes = [_vp, _vp, _vp, _i, _i, _i]
         h.orc_q4_k_matvec.argtypes = [_vp, _vp, _vp, _i, _i, _i]
+        h.orc_q5_k_matvec.argtypes = [_vp, _vp, _vp, _i, _i, _i]
+        h.orc_expert_ffn.argtypes = [_vp] * 5 + [_i] * 4 + [C.c_float, _i, _i]
         h.orc_quant_matvec.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i]
         h.orc_q4_k_scales.argtypes = [_vp, _vp, _vp]
         h.orc_rmsnorm.argtypes = [_vp, _vp, _vp, _i]
@@ -96,10 +98,27 @@ class Port:
         self.h.orc_q4_k_dequant(_f(out), _f(np.ascontiguousarray(blocks)), n)
         return out
 
+    def q5_k_dequant(self, blocks: np.ndarray, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self.h.orc_q5_k_dequant(_f(out), _f(np.ascontiguousarray(blocks)), n)
+        return out
+
     def quantize_q8_K(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32)
         out = np.zeros(x.size // 256 * 292, np.uint8)
         self.h.orc_quantize_row_q8_K(_f(out), _f(x), x.size)
+        return out
+
+    def expert_ffn(self, x, w_gate, w_up, w_down, gate_type: int, down_type: int, hidden: int, inter: int,
+                   weight: float = 1.0, out: np.ndarray | None = None, act_mode: int = ACT_FP32) -> np.ndarray:
+        """One expert's gate / up / SwiGLU / down for one token (gpu_expert_ffn_fused);
+        with `out` given, out += weight * y, else a new y."""
+        acc = out is not None
+        if out is None:
+            out = np.empty(hidden, np.float32)
+        self.h.orc_expert_ffn(_f(out), _f(np.ascontiguousarray(x, np.float32)), _f(np.ascontiguousarray(w_gate)),
+                              _f(np.ascontiguousarray(w_up)), _f(np.ascontiguousarray(w_down)), gate_type,
+                              down_type, hidden, inter, weight, int(acc), act_mode)
         return out
 
     def quant_matvec(self, W: np.ndarray, x: np.ndarray, out_dim: int, in_dim: int, wtype: int,

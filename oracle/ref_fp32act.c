@@ -12,7 +12,9 @@
  *     over its 32-blocks, the per-row semantics of q8_matvec_kernel
  *     (engine/runtime/gpu_offload.cu:152-199) -- no Q8_K activation quantisation;
  *   - Q4_K: the float dequant w = (d*sc)*q - (dmin*m) of q4k_matvec_kernel
- *     (engine/runtime/gpu_offload.cu:237-250) against fp32 activations.
+ *     (engine/runtime/gpu_offload.cu:237-250) against fp32 activations;
+ *   - Q5_K: the same with the fifth bit from qh, q5k_matvec_kernel
+ *     (engine/runtime/gpu_offload.cu:296-317).
  * Everything else in the layer (conv1d, gates, L2-norm, recurrence, RMSNorm,
  * SiLU gate) is the reference's code, unmodified.
  *
@@ -35,6 +37,7 @@
 #include "iq2_dequant.h"
 #include "q8k_quant.h"
 #include "q4k_dequant.h"
+#include "q5k_dequant.h"
 #include "q8_dequant.h"
 
 #define EXPORT __attribute__((visibility("default")))
@@ -64,6 +67,32 @@ static float q4k_row_fp32act(const block_q4_K* row, const float* x, int nblk) {
     return total;
 }
 
+/* One Q5_K row with fp32 activations, following gpu_offload.cu:296-317. */
+static float q5k_row_fp32act(const block_q5_K* row, const float* x, int nblk) {
+    float total = 0.0f;
+    for (int b = 0; b < nblk; b++) {
+        const block_q5_K* blk = &row[b];
+        float d = fp16_to_fp32(blk->d), dmin = fp16_to_fp32(blk->dmin);
+        uint8_t sc[8], mn[8];
+        decode_q4k_scales(blk->scales, sc, mn);
+        float bs = 0.0f;
+        for (int c = 0; c < 4; c++) {
+            float sc_lo = d * (float)sc[2 * c], mn_lo = dmin * (float)mn[2 * c];
+            float sc_hi = d * (float)sc[2 * c + 1], mn_hi = dmin * (float)mn[2 * c + 1];
+            for (int j = 0; j < 32; j++) {
+                uint8_t p = blk->qs[32 * c + j];
+                int q_lo = (p & 0x0F) | (((blk->qh[j] >> (2 * c)) & 1) << 4);
+                int q_hi = (p >> 4) | (((blk->qh[j] >> (2 * c + 1)) & 1) << 4);
+                float w_lo = sc_lo * (float)q_lo - mn_lo;
+                float w_hi = sc_hi * (float)q_hi - mn_hi;
+                bs += w_lo * x[b * 256 + 64 * c + j] + w_hi * x[b * 256 + 64 * c + 32 + j];
+            }
+        }
+        total += bs;
+    }
+    return total;
+}
+
 static void quant_matvec(float* out, const void* W, const float* x,
                          int out_dim, int in_dim, int type) {
     if (type == 8) {
@@ -78,6 +107,10 @@ static void quant_matvec(float* out, const void* W, const float* x,
         const block_q4_K* blocks = (const block_q4_K*)W;
         int bpr = in_dim / 256;
         for (int r = 0; r < out_dim; r++) out[r] = q4k_row_fp32act(&blocks[(size_t)r * bpr], x, bpr);
+    } else if (type == 13) {
+        const block_q5_K* blocks = (const block_q5_K*)W;
+        int bpr = in_dim / 256;
+        for (int r = 0; r < out_dim; r++) out[r] = q5k_row_fp32act(&blocks[(size_t)r * bpr], x, bpr);
     } else {
         const float* wf = (const float*)W;
         for (int r = 0; r < out_dim; r++) {

@@ -37,6 +37,41 @@ def test_q4_k_matvec_both_modes(rows, cols, seed):
                          O.ref().quant_matvec(b, x, rows, cols, 12, mode))
 
 
+@pytest.mark.parametrize("rows,cols,seed", [(128, 256, 8), (64, 2048, 9), (129, 512, 10)])
+def test_q5_k_matvec_both_modes(rows, cols, seed):
+    """Q5_K (the expert FFN's down projections): the restatement against the
+    reference's q5k_matvec (Q8_K activations) and the shim's fp32-activation
+    rows of q5k_matvec_kernel, bit for bit."""
+    b = synth.q5_k_blocks(rows, cols, seed)
+    x = synth.hidden_states(1, cols, seed + 50)[0] * 4.0
+    for mode in (O.ACT_EXACT, O.ACT_FP32):
+        assert same_bits(O.port().quant_matvec(b, x, rows, cols, 13, mode),
+                         O.ref().quant_matvec(b, x, rows, cols, 13, mode))
+
+
+@pytest.mark.parametrize("mode", [O.ACT_EXACT, O.ACT_FP32])
+def test_expert_ffn_is_the_reference_projections(mode):
+    """The oracle's expert FFN = the reference build's gate / up / down
+    projections around swiglu_kernel's (g * sigmoid(g)) * u, bit for bit."""
+    hidden, inter = 512, 256
+    wg, wu = synth.q4_k_blocks(inter, hidden, 11), synth.q4_k_blocks(inter, hidden, 12)
+    wd = synth.q5_k_blocks(hidden, inter, 13)
+    x = synth.hidden_states(1, hidden, 14)[0]
+    R = O.ref()
+    g = R.quant_matvec(wg, x, inter, hidden, 12, mode)
+    u = R.quant_matvec(wu, x, inter, hidden, 12, mode)
+    a = ((g * (np.float32(1) / (np.float32(1) + np.exp(-g).astype(np.float32)))) * u).astype(np.float32)
+    want = R.quant_matvec(wd, a, hidden, inter, 13, mode)
+    got = O.port().expert_ffn(x, wg, wu, wd, 12, 13, hidden, inter, act_mode=mode)
+    # the SwiGLU here uses numpy's exp, which may differ from expf in the last
+    # bit: the whole is compared at 1e-6 (the projections themselves are pinned
+    # bit for bit by test_q4_k_matvec_both_modes / test_q5_k_matvec_both_modes)
+    assert np.linalg.norm(got - want) <= 1e-6 * np.linalg.norm(want)
+    acc = np.full(hidden, 0.5, np.float32)
+    O.port().expert_ffn(x, wg, wu, wd, 12, 13, hidden, inter, weight=0.25, out=acc, act_mode=mode)
+    assert np.allclose(acc, 0.5 + 0.25 * got, rtol=1e-6, atol=1e-6)
+
+
 def test_q8_k_edge_values():
     x = synth.hidden_states(1, 2048, 9)[0]
     x[0:256] = 0.0                      # zero block

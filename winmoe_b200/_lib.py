@@ -61,6 +61,11 @@ SIGNATURES = {
     "gdn_q8_0_gemm": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _i64, _vp, _int, _vp]),
     "gdn_q4_k_dequant": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "gdn_q4_k_gemm": (_int, [_vp, _i64, _i64, _vp, _int, _i64, _vp, _vp]),
+    "gdn_q5_k_dequant": (_int, [_vp, _vp, _i64, _i64, _vp]),
+    "gdn_q5_k_gemm": (_int, [_vp, _i64, _i64, _vp, _int, _i64, _vp, _vp]),
+    "gdn_expert_ffn_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "gdn_expert_ffn": (_int, [_vp, _vp, _vp, _int, _int, _i64, _i64, _vp, _int, _i64, _vp, C.c_float, _int, _vp,
+                              _sz, _vp]),
     "gdn_decode_workspace_size": (_sz, [C.POINTER(gdn_dims), _i64]),
     "gdn_decode_step": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gdn_decode_step_ex": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _int, _vp]),

@@ -159,6 +159,48 @@ int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, 
     return launch_q4_k_gemv(blocks, n_rows, k, x, x_dtype, m, y, n_rows, s);
 }
 
+int gdn_q5_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, void* stream) {
+    if (rows < 0 || cols < 0 || cols % 256 != 0) return fail(GDN_ERR_SHAPE, "q5_k dequant: cols %% 256 != 0");
+    if (!blocks || !out) return fail(GDN_ERR_ARG, "q5_k dequant: NULL pointer");
+    return launch_q5_k_dequant(blocks, out, rows, cols, as_stream(stream));
+}
+
+int gdn_q5_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
+                  void* stream) {
+    if (n_rows < 0 || m < 0 || k <= 0 || k % 256 != 0) return fail(GDN_ERR_SHAPE, "q5_k gemm: k must be a positive multiple of 256");
+    if (!blocks || !x || !y) return fail(GDN_ERR_ARG, "q5_k gemm: NULL pointer");
+    int st = check_act_dtype(x_dtype);
+    if (st) return st;
+    if (!aligned(blocks, 16)) return fail(GDN_ERR_ARG, "q5_k gemm: blocks must be 16-byte aligned");
+    if (n_rows == 0 || m == 0) return GDN_OK;
+    return launch_q5_k_gemv(blocks, n_rows, k, x, x_dtype, m, y, n_rows, as_stream(stream));
+}
+
+size_t gdn_expert_ffn_workspace_size(int64_t m, int64_t hidden, int64_t inter) {
+    if (m <= 0 || hidden <= 0 || inter <= 0) return 0;
+    return expert_ffn_workspace_bytes(m, hidden, inter);
+}
+
+int gdn_expert_ffn(const void* w_gate, const void* w_up, const void* w_down, int gate_type, int down_type,
+                   int64_t hidden, int64_t inter, const void* x, int x_dtype, int64_t m, float* out, float weight,
+                   int accumulate, void* workspace, size_t workspace_bytes, void* stream) {
+    auto kq = [](int t) { return t == GDN_GGML_Q4_K || t == GDN_GGML_Q5_K; };
+    if (!kq(gate_type) || !kq(down_type))
+        return fail(GDN_ERR_TYPE, "expert ffn: weight types must be Q4_K (12) or Q5_K (13), got %d / %d", gate_type,
+                    down_type);
+    if (m < 0 || hidden <= 0 || inter <= 0 || hidden % 256 != 0 || inter % 256 != 0)
+        return fail(GDN_ERR_SHAPE, "expert ffn: hidden and inter must be positive multiples of 256");
+    if (!w_gate || !w_up || !w_down || !x || !out || (m > 0 && !workspace))
+        return fail(GDN_ERR_ARG, "expert ffn: NULL pointer");
+    if (!aligned(w_gate, 16) || !aligned(w_up, 16) || !aligned(w_down, 16))
+        return fail(GDN_ERR_ARG, "expert ffn: weights must be 16-byte aligned");
+    if (!aligned(workspace, 256)) return fail(GDN_ERR_ARG, "expert ffn: workspace must be 256-byte aligned");
+    int st = check_act_dtype(x_dtype);
+    if (st) return st;
+    return launch_expert_ffn(w_gate, w_up, w_down, gate_type, down_type, hidden, inter, x, x_dtype, m, out, weight,
+                             accumulate, workspace, workspace_bytes, as_stream(stream));
+}
+
 size_t gdn_decode_workspace_size(const gdn_dims* dims, int64_t batch) {
     if (dims == nullptr || batch <= 0) return 0;
     return decode_workspace_bytes(*dims, batch);

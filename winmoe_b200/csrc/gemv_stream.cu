@@ -1,6 +1,6 @@
 // Streamed dequant-GEMV for small activation batches (decode of up to 63
-// sequences, the GQA projections, the Q4_K sweep), 1, 2, 4 or 8 activation
-// rows per CTA.
+// sequences, the GQA projections, the Q4_K sweep, the expert FFN's Q4_K / Q5_K
+// projections), 1, 2, 4 or 8 activation rows per CTA.
 //
 // Memory side.  The row-per-warp GEMVs in quant.cu keep one batch of register
 // loads in flight per warp, so at batch 1 their speed is set by HBM latency;
@@ -61,12 +61,19 @@ constexpr int kStageBatch = 4;  // 128-element pieces a warp loads from global m
 constexpr int kSmemBatch = 2;   // ... from shared memory (the activations brought in by a bulk copy)
 
 __host__ __device__ constexpr int64_t plane_len(int64_t k) { return k + (k >> 2); }
+
+// Weight formats: 0 = Q8_0 planes (int8 row + fp16 scale row), 1 = Q4_K and
+// 2 = Q5_K superblocks (144 / 176 bytes per 256 weights).  Bytes of one
+// weight row in global memory (the int8 plane's row for Q8_0).
+__host__ __device__ constexpr int64_t row_qbytes(int fmt, int64_t k) {
+    return fmt == 0 ? k : (k / 256) * (fmt == 1 ? 144 : 176);
+}
 __device__ __forceinline__ int64_t xq_off(int64_t i) { return i + ((i >> 7) << 5); }
 
 // Bytes of the staged activations: MB x 3 level planes, the block scales and,
 // for Q4_K, the sums of every 16.
 __host__ __device__ constexpr size_t staged_bytes(int fmt, int mb, int64_t k) {
-    return (size_t)mb * (3 * plane_len(k) + (k / 32) * 4 + (fmt == 1 ? (k / 16) * 4 : 0));
+    return (size_t)mb * (3 * plane_len(k) + (k / 32) * 4 + (fmt != 0 ? (k / 16) * 4 : 0));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -144,7 +151,7 @@ __device__ __forceinline__ void stage_128(float4 xv, bool valid, int8_t* p, floa
         *reinterpret_cast<uint32_t*>(p + 2 * pl) = wc;
         if ((lane & 7) == 0) sxp[lane >> 3] = tiny ? s * 5.421010862427522e-20f : s;
     }
-    if (FMT == 1) {
+    if (FMT != 0) {
         float t = (xv.x + xv.y) + (xv.z + xv.w);
         t += __shfl_xor_sync(0xffffffffu, t, 1);
         t += __shfl_xor_sync(0xffffffffu, t, 2);
@@ -202,15 +209,19 @@ __device__ __forceinline__ void q8_row(const uint8_t* row, const uint8_t* scales
     }
 }
 
-template <int MB>
+// Q4_K (Q5 = false) or Q5_K (Q5 = true, 176-byte superblocks: d, dmin, the
+// 12 scale bytes, qh[32], qs[128]; weight 64 c + 16 h + e takes bit 2 c of
+// qh[16 h + e] as its fifth bit, weight 64 c + 32 + 16 h + e bit 2 c + 1,
+// gpu_offload.cu:302-309).
+template <int MB, bool Q5 = false>
 __device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Staged& st, int mb, int lane,
                                         float (&acc)[MB]) {
     const int64_t nsb = k >> 8;
     const int g = lane >> 3, j = lane & 7, c = j >> 1;
     for (int64_t sb = g; sb < nsb; sb += 4) {
-        const uint8_t* blk = row + sb * 144;
+        const uint8_t* blk = row + sb * (Q5 ? 176 : 144);
         const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-        const uint4 q4 = *reinterpret_cast<const uint4*>(blk + 16 + 16 * j);
+        const uint4 q4 = *reinterpret_cast<const uint4*>(blk + (Q5 ? 48 : 16) + 16 * j);
         const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
         const float d = fp16_bits_to_float((uint16_t)(hdr.x & 0xFFFFu));
         const float dmin = fp16_bits_to_float((uint16_t)(hdr.x >> 16));
@@ -219,9 +230,21 @@ __device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Sta
         scale_min(2 * c + 1, hb + 4, s_hi, m_hi);
         const float sl = d * (float)s_lo, ml = dmin * (float)m_lo;
         const float sh = d * (float)s_hi, mh = dmin * (float)m_hi;
-        const uint4 lo = make_uint4(q4.x & 0x0F0F0F0Fu, q4.y & 0x0F0F0F0Fu, q4.z & 0x0F0F0F0Fu, q4.w & 0x0F0F0F0Fu);
-        const uint4 hi = make_uint4((q4.x >> 4) & 0x0F0F0F0Fu, (q4.y >> 4) & 0x0F0F0F0Fu, (q4.z >> 4) & 0x0F0F0F0Fu,
-                                    (q4.w >> 4) & 0x0F0F0F0Fu);
+        uint4 lo = make_uint4(q4.x & 0x0F0F0F0Fu, q4.y & 0x0F0F0F0Fu, q4.z & 0x0F0F0F0Fu, q4.w & 0x0F0F0F0Fu);
+        uint4 hi = make_uint4((q4.x >> 4) & 0x0F0F0F0Fu, (q4.y >> 4) & 0x0F0F0F0Fu, (q4.z >> 4) & 0x0F0F0F0Fu,
+                              (q4.w >> 4) & 0x0F0F0F0Fu);
+        if (Q5) {
+            const uint4 qh = *reinterpret_cast<const uint4*>(blk + 16 + 16 * (j & 1));
+            const int bl = 2 * c, bh = 2 * c + 1;
+            lo.x |= ((qh.x >> bl) & 0x01010101u) << 4;
+            lo.y |= ((qh.y >> bl) & 0x01010101u) << 4;
+            lo.z |= ((qh.z >> bl) & 0x01010101u) << 4;
+            lo.w |= ((qh.w >> bl) & 0x01010101u) << 4;
+            hi.x |= ((qh.x >> bh) & 0x01010101u) << 4;
+            hi.y |= ((qh.y >> bh) & 0x01010101u) << 4;
+            hi.z |= ((qh.z >> bh) & 0x01010101u) << 4;
+            hi.w |= ((qh.w >> bh) & 0x01010101u) << 4;
+        }
         const int64_t klo = sb * 256 + 64 * c + 16 * (j & 1), khi = klo + 32;
         const int64_t ol = xq_off(klo), oh = xq_off(khi);
 #pragma unroll
@@ -296,7 +319,7 @@ __device__ __forceinline__ void stage_rows(const void* x, int x_dtype, int64_t m
             const bool valid = ju[u] < rows;
             const int jj = valid ? ju[u] : 0, cc = valid ? cu[u] : 0;
             stage_128<FMT>(xv[u], valid, level_ptr<PADDED>(xq, pl, jj, 128 * cc + 4 * lane), sx + jj * nblk + 4 * cc,
-                           FMT == 1 ? x16 + jj * 2 * nblk + 8 * cc : nullptr, pl, lane);
+                           FMT != 0 ? x16 + jj * 2 * nblk + 8 * cc : nullptr, pl, lane);
         }
     }
     if (!announced) bar_arrive(1, (kWarps + 1) * 32);
@@ -404,7 +427,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     pdl_trigger();
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t qbytes = FMT == 0 ? (uint32_t)k : (uint32_t)(k >> 8) * 144u;  // one row
+    const uint32_t qbytes = (uint32_t)row_qbytes(FMT, k);  // one row
     const uint32_t dbytes = FMT == 0 ? (uint32_t)(k >> 4) : 0u;
     const Ring R = ring_of(smem, slots, nx);
     Staged st;
@@ -470,7 +493,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
                 q8_row<MB>(stage + (size_t)warp * qbytes, stage + qstage + (size_t)warp * dbytes, k, st, mb, lane,
                            acc);
             } else {
-                q4k_row<MB>(stage + (size_t)warp * qbytes, k, st, mb, lane, acc);
+                q4k_row<MB, FMT == 2>(stage + (size_t)warp * qbytes, k, st, mb, lane, acc);
             }
 #pragma unroll
             for (int j = 0; j < MB; j++) {
@@ -516,10 +539,11 @@ __device__ __forceinline__ void imma_16832(int (&c)[4], const uint32_t (&a)[4], 
 }
 
 __host__ __device__ constexpr int64_t mma_plane_len(int64_t k) { return k + 16; }
-// Bytes of a weight row in the stage: Q8_0 k int8 + 16; Q4_K its superblocks
-// (144 B each) padded so that the row stride is 4 (mod 32) words.
+// Bytes of a weight row in the stage: Q8_0 k int8 + 16; Q4_K / Q5_K its
+// superblocks (144 / 176 B each) padded so that the row stride is 4 (mod 32)
+// words.
 __host__ __device__ constexpr int64_t mma_row_len(int fmt, int64_t k) {
-    return fmt == 0 ? k + 16 : (k / 256) * 144 + 4 * ((4 - 36 * (k / 256)) & 31);
+    return fmt == 0 ? k + 16 : row_qbytes(fmt, k) + 4 * ((4 - row_qbytes(fmt, k) / 4) & 31);
 }
 __host__ __device__ constexpr size_t mma_stage_bytes(int fmt, int64_t k) {
     return (size_t)kStageRows * mma_row_len(fmt, k) + (fmt == 0 ? (size_t)kStageRows * (k / 16) : 0);
@@ -527,7 +551,7 @@ __host__ __device__ constexpr size_t mma_stage_bytes(int fmt, int64_t k) {
 // activation planes, block scales, (Q4_K) 16-sums, and the two reduction buffers
 __host__ __device__ constexpr size_t mma_fixed_bytes(int fmt, int mt, int64_t k) {
     return (size_t)(4 * mt) * 3 * mma_plane_len(k) + (size_t)(4 * mt) * (k / 32) * 4 +
-           (fmt == 1 ? (size_t)(4 * mt) * (k / 16) * 4 : 0) + (size_t)2 * kWarps * 2 * mt * 32 * 4;
+           (fmt != 0 ? (size_t)(4 * mt) * (k / 16) * 4 : 0) + (size_t)2 * kWarps * 2 * mt * 32 * 4;
 }
 
 template <int FMT, int MT>
@@ -542,13 +566,13 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int gq = lane >> 2, qq = lane & 3;
     const int nblk = (int)(k >> 5);
     const int64_t plm = mma_plane_len(k), rl = mma_row_len(FMT, k);
-    const uint32_t qbytes = FMT == 0 ? (uint32_t)k : (uint32_t)(k >> 8) * 144u;  // one row in global memory
+    const uint32_t qbytes = (uint32_t)row_qbytes(FMT, k);  // one row in global memory
     const uint32_t dbytes = FMT == 0 ? (uint32_t)(k >> 4) : 0u;
     const Ring R = ring_of(smem, slots, nx);
     int8_t* xq = reinterpret_cast<int8_t*>(smem + kBarBytes);             // [MB][3][plm]
     float* sx = reinterpret_cast<float*>(xq + (size_t)MB * 3 * plm);     // [MB][nblk]
     float* x16 = sx + MB * nblk;                                         // Q4_K: [MB][2 nblk]
-    float* red = x16 + (FMT == 1 ? MB * 2 * nblk : 0);                   // [2][kWarps][2][MT][32]
+    float* red = x16 + (FMT != 0 ? MB * 2 * nblk : 0);                   // [2][kWarps][2][MT][32]
     uint8_t* ring = smem + kBarBytes + mma_fixed_bytes(FMT, MT, k);
     const size_t stage_bytes = mma_stage_bytes(FMT, k);
     const size_t scale_off = (size_t)kStageRows * rl;
@@ -684,15 +708,22 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
                     }
 #pragma unroll
                     for (int g = 0; g < 2; g++) {
-                        const uint8_t* blk = stage + (size_t)(8 * g + gq) * rl + sb * 144;
-                        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(blk + 16 + 32 * cg + 4 * qq);
-                        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(blk + 32 + 32 * cg + 4 * qq);
-                        const uint32_t b0 = (w0 >> (4 * half)) & 0x0F0F0F0Fu;
-                        const uint32_t b1 = (w1 >> (4 * half)) & 0x0F0F0F0Fu;
+                        constexpr int kSb = FMT == 2 ? 176 : 144, kQs = FMT == 2 ? 48 : 16;
+                        const uint8_t* blk = stage + (size_t)(8 * g + gq) * rl + sb * kSb;
+                        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(blk + kQs + 32 * cg + 4 * qq);
+                        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(blk + kQs + 16 + 32 * cg + 4 * qq);
+                        uint32_t b0 = (w0 >> (4 * half)) & 0x0F0F0F0Fu;
+                        uint32_t b1 = (w1 >> (4 * half)) & 0x0F0F0F0Fu;
+                        if (FMT == 2) {  // the fifth bits: bit 2 cg + half of qh[4 qq ..] and qh[16 + 4 qq ..]
+                            const uint32_t h0 = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * qq);
+                            const uint32_t h1 = *reinterpret_cast<const uint32_t*>(blk + 32 + 4 * qq);
+                            b0 |= ((h0 >> (2 * cg + half)) & 0x01010101u) << 4;
+                            b1 |= ((h1 >> (2 * cg + half)) & 0x01010101u) << 4;
+                        }
                         float ds[2], dm[2];  // d sc and dmin m of this thread's two columns (weight rows)
 #pragma unroll
                         for (int e = 0; e < 2; e++) {
-                            const uint8_t* hb = stage + (size_t)(8 * g + 2 * qq + e) * rl + sb * 144;
+                            const uint8_t* hb = stage + (size_t)(8 * g + 2 * qq + e) * rl + sb * kSb;
                             const uint32_t dd = *reinterpret_cast<const uint32_t*>(hb);
                             int sc, mn;
                             scale_min(2 * cg + half, hb + 4, sc, mn);
@@ -759,7 +790,8 @@ int run_mma(const void* wq, const void* wd, int64_t n, int64_t k, const void* x,
     GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t ctas = std::min<int64_t>(sm_count(), n);
     const dim3 grid((unsigned)ctas, (unsigned)((m + 4 * MT - 1) / (4 * MT)));
-    return launch_pdl(FMT == 0 ? "gemv_mma_kernel<q8_0>" : "gemv_mma_kernel<q4_k>", gemv_mma_kernel<FMT, MT>, grid,
+    return launch_pdl(FMT == 0 ? "gemv_mma_kernel<q8_0>" : FMT == 1 ? "gemv_mma_kernel<q4_k>" : "gemv_mma_kernel<q5_k>",
+                      gemv_mma_kernel<FMT, MT>, grid,
                       dim3((kWarps + 1) * 32), smem, s,
                       static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
                       slots, nx, device_error_word());
@@ -772,7 +804,8 @@ int run(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int
     GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t ctas = std::min<int64_t>(sm_count(), n);
     const dim3 grid((unsigned)ctas, (unsigned)((m + MB - 1) / MB));
-    return launch_pdl(FMT == 0 ? "gemv_stream_kernel<q8_0>" : "gemv_stream_kernel<q4_k>",
+    return launch_pdl(FMT == 0 ? "gemv_stream_kernel<q8_0>" : FMT == 1 ? "gemv_stream_kernel<q4_k>"
+                                                                    : "gemv_stream_kernel<q5_k>",
                       gemv_stream_kernel<FMT, MB>, grid, dim3((kWarps + 1) * 32), smem, s,
                       static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
                       slots, nx, device_error_word());
@@ -801,7 +834,7 @@ static int plan(int fmt, const void* wq, const void* wd, int64_t k, int64_t m, i
     if (m < 1 || (m + 7) / 8 > 65535 || k < 256 || (k & (fmt == 0 ? 511 : 255)) != 0) return 0;
     if ((reinterpret_cast<uintptr_t>(wq) & 15) != 0) return 0;
     if (fmt == 0 && (reinterpret_cast<uintptr_t>(wd) & 15) != 0) return 0;
-    const int64_t stage = (int64_t)kStageRows * (fmt == 0 ? k + k / 16 : (k / 256) * 144);
+    const int64_t stage = (int64_t)kStageRows * (fmt == 0 ? k + k / 16 : row_qbytes(fmt, k));
     for (int mb = m >= 5 ? 8 : m >= 3 ? 4 : (int)m; mb >= 1; mb >>= 1) {
         const size_t base = kBarBytes + staged_bytes(fmt, mb, k);
         if (base >= kSmemLimit) continue;
@@ -835,36 +868,36 @@ static int plan_mma(int fmt, const void* wq, const void* wd, int64_t k, int64_t 
     return 0;
 }
 
+template <int FMT>
+static int run_fmt(int mb, int mma, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt,
+                   int64_t m, float* y, int64_t ldy, int slots, int nx, size_t smem, cudaStream_t s) {
+    if (mma) return mb == 2 ? run_mma<FMT, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s)
+                            : run_mma<FMT, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+    switch (mb) {
+        case 1: return run<FMT, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        case 2: return run<FMT, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        case 4: return run<FMT, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        default: return run<FMT, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+    }
+}
+
 int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt,
                        int64_t m, float* y, int64_t ldy, cudaStream_t s) {
-    int mb = 0, slots = 0;
+    if (fmt < 0 || fmt > 2) return GDN_ERR_TYPE;
+    int mb = 0, slots = 0, nx = 0, mma = 0;
     size_t smem = 0;
     if (n > 0 && plan_mma(fmt, wq, wd, k, m, &mb, &slots, &smem)) {
-        const int nx = activation_slots(x, dt, k, 4 * mb, mma_stage_bytes(fmt, k), slots);
-        if (fmt == 0)
-            return mb == 2 ? run_mma<0, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s)
-                           : run_mma<0, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-        return mb == 2 ? run_mma<1, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s)
-                       : run_mma<1, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        mma = 1;
+        nx = activation_slots(x, dt, k, 4 * mb, mma_stage_bytes(fmt, k), slots);
+    } else {
+        if (!plan(fmt, wq, wd, k, m, &mb, &slots, &smem)) return GDN_ERR_SHAPE;
+        if (n <= 0) return GDN_OK;
+        const size_t stage = (size_t)kStageRows * (fmt == 0 ? k + k / 16 : row_qbytes(fmt, k));
+        nx = activation_slots(x, dt, k, mb, stage, slots);
     }
-    if (!plan(fmt, wq, wd, k, m, &mb, &slots, &smem)) return GDN_ERR_SHAPE;
-    if (n <= 0) return GDN_OK;
-    const size_t stage = (size_t)kStageRows * (fmt == 0 ? k + k / 16 : (k / 256) * 144);
-    const int nx = activation_slots(x, dt, k, mb, stage, slots);
-    if (fmt == 0) {
-        switch (mb) {
-            case 1: return run<0, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-            case 2: return run<0, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-            case 4: return run<0, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-            default: return run<0, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-        }
-    }
-    switch (mb) {
-        case 1: return run<1, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-        case 2: return run<1, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-        case 4: return run<1, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-        default: return run<1, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-    }
+    if (fmt == 0) return run_fmt<0>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+    if (fmt == 1) return run_fmt<1>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+    return run_fmt<2>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
 }
 
 bool gemv_stream_fits(int fmt, const void* wq, const void* wd, int64_t k, int64_t m) {

@@ -410,6 +410,37 @@ __global__ void q4_k_dequant_kernel(const uint8_t* __restrict__ blocks, float* _
     }
 }
 
+// One thread per (superblock, chunk c, 16-byte half) of a Q5_K tensor (176-byte
+// superblocks: d, dmin, 12 scale bytes, qh[32], qs[128]): 32 weights out, the
+// nibble of qs[32c + j] with bit 2c (low) / 2c + 1 (high) of qh[j] as the fifth
+// bit (engine/runtime/gpu_offload.cu:302-309), w = (d*sc)*q - (dmin*m) with
+// each operation rounded once.
+__global__ void q5_k_dequant_kernel(const uint8_t* __restrict__ blocks, float* __restrict__ out, int64_t nsb) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nsb * 8) return;
+    const int64_t sb = t >> 3;
+    const int c = (int)(t & 7) >> 1, half = (int)(t & 1);
+    const uint8_t* blk = blocks + sb * 176;
+    const float d = fp16_bits_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+    const float dmin = fp16_bits_to_float((uint16_t)(blk[2] | (blk[3] << 8)));
+    int s_lo, m_lo, s_hi, m_hi;
+    q4k_scale_min(2 * c, blk + 4, s_lo, m_lo);
+    q4k_scale_min(2 * c + 1, blk + 4, s_hi, m_hi);
+    const float sl = __fmul_rn(d, (float)s_lo), ml = __fmul_rn(dmin, (float)m_lo);
+    const float sh = __fmul_rn(d, (float)s_hi), mh = __fmul_rn(dmin, (float)m_hi);
+    const uint8_t* qh = blk + 16 + 16 * half;
+    const uint8_t* qs = blk + 48 + 32 * c + 16 * half;
+    float* o_lo = out + sb * 256 + 64 * c + 16 * half;
+    float* o_hi = o_lo + 32;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int ql = (qs[j] & 0x0F) | (((qh[j] >> (2 * c)) & 1) << 4);
+        const int qv = (qs[j] >> 4) | (((qh[j] >> (2 * c + 1)) & 1) << 4);
+        o_lo[j] = __fsub_rn(__fmul_rn(sl, (float)ql), ml);
+        o_hi[j] = __fsub_rn(__fmul_rn(sh, (float)qv), mh);
+    }
+}
+
 // Q4_K GEMV (quant_matvec type 12 with fp32 activations; the reference GPU
 // kernel is engine/runtime/gpu_offload.cu:237-250).  A sub-block's contribution
 // is (d sc) sum(q x) - (dmin m) sum(x); the MB activation rows of block row
@@ -636,6 +667,25 @@ static int run_q4_gemv(const void* w, int64_t n, int64_t k, const void* x, int d
     const dim3 grid((unsigned)((n + rpb - 1) / rpb), (unsigned)((m + MB - 1) / MB));
     return launch_pdl("q4_k_gemv_kernel", q4_k_gemv_kernel<MB>, grid, dim3(256), smem, s,
                       static_cast<const uint8_t*>(w), n, k, x, dt, m, y, ldy, rpb);
+}
+
+int launch_q5_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s) {
+    const int64_t nsb = rows * (cols / 256);
+    if (nsb == 0) return GDN_OK;
+    q5_k_dequant_kernel<<<(unsigned)((nsb * 8 + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t*>(blocks), out,
+                                                                        nsb);
+    GDN_LAUNCH_CHECK("q5_k_dequant_kernel");
+    return GDN_OK;
+}
+
+// Q5_K GEMV: the streamed kernels only (there is no row-per-warp Q5_K GEMV).
+int launch_q5_k_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y, int64_t ldy,
+                     cudaStream_t s) {
+    if (m <= 0 || n <= 0) return GDN_OK;
+    if (!gemv_stream_fits(2, w, nullptr, k, m))
+        return fail(GDN_ERR_SHAPE, "q5_k gemv: k=%lld must be a multiple of 256 (16-byte aligned blocks)",
+                    (long long)k);
+    return launch_gemv_stream(2, w, nullptr, n, k, x, dt, m, y, ldy, s);
 }
 
 int launch_q4_k_gemv(const void* w, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,

@@ -24,6 +24,14 @@ bool gemv_stream_fits(int fmt, const void* wq, const void* wd, int64_t k, int64_
 int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int x_dtype,
                        int64_t m, float* y, int64_t ldy, cudaStream_t s);
 int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s);
+int launch_q5_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s);
+int launch_q5_k_gemv(const void* blocks, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
+                     int64_t ldy, cudaStream_t s);
+// The expert FFN (expert.cu): out[m][hidden] (+)= weight * down(SwiGLU(gate x, up x)).
+size_t expert_ffn_workspace_bytes(int64_t m, int64_t hidden, int64_t inter);
+int launch_expert_ffn(const void* w_gate, const void* w_up, const void* w_down, int gate_type, int down_type,
+                      int64_t hidden, int64_t inter, const void* x, int x_dtype, int64_t m, float* out, float weight,
+                      int accumulate, void* workspace, size_t workspace_bytes, cudaStream_t s);
 int launch_q4_k_gemv(const void* blocks, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
                      int64_t ldy, cudaStream_t s);
 

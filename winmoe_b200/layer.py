@@ -325,6 +325,40 @@ def dequant_q4_k(blocks: torch.Tensor, rows: int, cols: int, stream=None) -> tor
     return out
 
 
+def dequant_q5_k(blocks: torch.Tensor, rows: int, cols: int, stream=None) -> torch.Tensor:
+    out = torch.empty((rows, cols), dtype=torch.float32, device=blocks.device)
+    check(lib().gdn_q5_k_dequant(blocks.data_ptr(), out.data_ptr(), rows, cols, _stream(stream, blocks.device)))
+    return out
+
+
+def gemm_q5_k(blocks: torch.Tensor, n: int, k: int, x: torch.Tensor, out: torch.Tensor | None = None,
+              stream=None) -> torch.Tensor:
+    """y[m][n] = x[m] . W[n] for GGUF Q5_K blocks (quant_matvec type 13, fp32 activations)."""
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    check(lib().gdn_q5_k_gemm(blocks.data_ptr(), n, k, x.data_ptr(), _act_dtype(x), m, out.data_ptr(),
+                              _stream(stream, x.device)))
+    return out
+
+
+def expert_ffn(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, gate_type: int, down_type: int,
+               hidden: int, inter: int, x: torch.Tensor, out: torch.Tensor | None = None, weight: float = 1.0,
+               accumulate: bool = False, workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """One MoE expert's FFN for the m rows of x (gpu_expert_ffn_fused): down(SwiGLU(gate x, up x));
+    accumulate=True adds weight * y into `out` (the batched expert path)."""
+    m = x.shape[0]
+    if out is None:
+        out = torch.zeros((m, hidden), dtype=torch.float32, device=x.device)
+    need = lib().gdn_expert_ffn_workspace_size(m, hidden, inter)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    check(lib().gdn_expert_ffn(w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), gate_type, down_type, hidden,
+                               inter, x.data_ptr(), _act_dtype(x), m, out.data_ptr(), float(weight), int(accumulate),
+                               workspace.data_ptr(), workspace.numel(), _stream(stream, x.device)))
+    return out
+
+
 # ------------------------------------------------------------------ drop-in mirror
 
 _weight_cache: dict[tuple, DeltaNetWeights] = {}

@@ -8,6 +8,7 @@ Distributions (the benchmark configs' own, with the unspecified ones fixed here)
   Q8_0 blocks: qs ~ U{-127..127}, d = fp16(|N(0,1)| * 0.02)
   Q4_K blocks: d, dmin = fp16(|N(0,1)| * 0.02), 12 scale bytes ~ U{0..255},
                nibbles ~ U{0..15}
+  Q5_K blocks: d, dmin = fp16(|N(0,1)| * 0.01), the other 172 bytes ~ U{0..255}
   A_log ~ U(0, 2.7) -> ssm_a = -exp(A_log); dt_bias = 0
   conv1d weight ~ N(0, 0.5^2); head-norm weight = 1 + 0.1 N(0,1)
   hidden states ~ N(0,1); pre-filled states ~ N(0, 0.05^2)
@@ -60,6 +61,21 @@ def q4_k_blocks(rows: int, cols: int, seed: int) -> np.ndarray:
     out[:, :, 4:16] = scales
     out[:, :, 16:] = lo | (hi << 4)
     return out.reshape(rows, nb * 144)
+
+
+def q5_k_blocks(rows: int, cols: int, seed: int) -> np.ndarray:
+    """Random Q5_K tensor as GGUF bytes (d, dmin, 12 scale bytes, qh[32], qs[128]),
+    shape [rows, cols/256*176] uint8."""
+    assert cols % 256 == 0
+    g = rng(seed)
+    nb = cols // 256
+    d = (np.abs(g.standard_normal((rows, nb))) * 0.01).astype(np.float16)
+    dmin = (np.abs(g.standard_normal((rows, nb))) * 0.01).astype(np.float16)
+    out = np.empty((rows, nb, 176), dtype=np.uint8)
+    out[:, :, 0:2] = d.view(np.uint8).reshape(rows, nb, 2)
+    out[:, :, 2:4] = dmin.view(np.uint8).reshape(rows, nb, 2)
+    out[:, :, 4:] = g.integers(0, 256, size=(rows, nb, 172), dtype=np.uint8)
+    return out.reshape(rows, nb * 176)
 
 
 def q8_0_split(blocks: np.ndarray, rows: int, cols: int) -> tuple[np.ndarray, np.ndarray]:
