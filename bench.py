@@ -402,6 +402,81 @@ def run_gqa(dev, hbm_peak, peak_src, with_cpu):
     return res
 
 
+EXPERT_HIDDEN, EXPERT_INTER, EXPERT_TOPK, EXPERT_POOL = 2048, 512, 8, 128
+
+
+def run_expert_ffn(dev, hbm_peak, peak_src, with_cpu):
+    """(f)4: the MoE experts of one token, the reference's batched GPU route
+    (gpu_expert_batch_add, gpu_offload.cu:766-793): for each of 8 experts, Q4_K
+    gate / up, SwiGLU, Q5_K down, weighted into the token's output.  Token i uses
+    experts 8i .. 8i+7 of a pool of 128 distinct experts (243 MB > L2: weights from
+    HBM), weights 1/8."""
+    import torch
+    from winmoe_b200 import layer as L, synth
+    from winmoe_b200._lib import lib
+    H, I, K, NP = EXPERT_HIDDEN, EXPERT_INTER, EXPERT_TOPK, EXPERT_POOL
+    g = torch.Generator(device=dev).manual_seed(77)
+
+    def blocks(rows, cols, nbytes):
+        t = torch.randint(0, 256, (rows * (cols // 256) * nbytes,), generator=g, device=dev, dtype=torch.uint8)
+        sb = t.view(rows * (cols // 256), nbytes)
+        sb[:, 0:4] = torch.tensor([0x00, 0x20, 0x00, 0x20], dtype=torch.uint8, device=dev)  # d = dmin = fp16 0.0078
+        return t
+    pool = [(blocks(I, H, 144), blocks(I, H, 144), blocks(H, I, 176)) for _ in range(NP)]
+    n_tok = 16
+    xs = torch.from_numpy(synth.hidden_states(n_tok, H, seed=78)).to(dev)
+    out = torch.zeros((n_tok, H), dtype=torch.float32, device=dev)
+    ws = torch.empty(lib().gdn_expert_ffn_workspace_size(1, H, I), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def token(i):
+        for e in range(K):
+            wg, wu, wd = pool[(K * i + e) % NP]
+            L.expert_ffn(wg, wu, wd, 12, 13, H, I, xs[i:i + 1], out=out[i:i + 1], weight=1.0 / K, accumulate=True,
+                         workspace=ws, stream=stream)
+    for i in range(4):
+        token(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(20_000_000)  # the calls queue behind ~10 ms of GPU time: events time the kernels
+    e0.record(stream)
+    for i in range(n_tok):
+        token(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) / n_tok * 1e3
+    nb = K * (2 * I * (H // 256) * 144 + H * (I // 256) * 176) + (H + K * (3 * I + 2 * H)) * 4
+    res = {"workload": "MoE experts of one token (35B-class: hidden 2048, expert intermediate 512, top-8): Q4_K "
+                       "gate + up, SwiGLU, Q5_K down, weighted accumulation, 8 experts per token from a pool of "
+                       "128 (243 MB > L2: weights from HBM); 16 tokens queued behind a GPU sleep",
+           "value": 1e6 / us, "unit": "tok/s", "us_per_token": us, "us_per_expert": us / K,
+           "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel<q4_k/q5_k> x 3 per expert",
+                        "achieved": nb / (us / 1e6) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                        "frac": nb / (us / 1e6) / 1e9 / hbm_peak, "peak_source": peak_src,
+                        "algorithmic_bytes_per_token": nb}}
+    if with_cpu:
+        from oracle import oracle as O
+        orc = O.ref() if O.ref_available() else O.port()
+        host = [tuple(t.cpu().numpy() for t in pool[e]) for e in range(K)]
+        x0 = xs[0].cpu().numpy()
+        n_cpu = 4
+        t0 = time.perf_counter()
+        for _ in range(n_cpu):
+            acc = np.zeros(H, np.float32)
+            for wg, wu, wd in host:  # the reference's own q4k / q5k matvecs around the SwiGLU
+                gg = orc.quant_matvec(wg, x0, I, H, 12, O.ACT_EXACT)
+                uu = orc.quant_matvec(wu, x0, I, H, 12, O.ACT_EXACT)
+                a = (gg * (1.0 / (1.0 + np.exp(-gg)))).astype(np.float32) * uu
+                acc += np.float32(1.0 / K) * orc.quant_matvec(wd, a, H, I, 13, O.ACT_EXACT)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": n_cpu / dt, "unit": "tok/s", "cores": host_cpu()[0],
+                               "cpu_model": host_cpu()[1], "kind": "reference" if O.ref_available() else "port",
+                               "sample": f"{n_cpu} tokens x 8 experts through the reference's q4k_matvec / "
+                                         "q5k_matvec (Q8_K activations) and a numpy SwiGLU"}
+    del pool
+    return res
+
+
 def q4k_call_bytes(cfg, B):
     """Config 4: Q4_K bytes of the four projections plus fp32 activations in and out."""
     w = (cfg.in_proj_rows * cfg.hidden + cfg.hidden * cfg.inner) // 256 * 144
@@ -782,6 +857,7 @@ def run_ours(args):
         line["decode_b1"] = run_decode_b1(cfg, w, dev, hbm_peak, peak_src, tensors, not args.no_cpu_baseline)
         line["q4k_sweep"] = run_q4k_sweep(cfg, dev, hbm_peak, peak_src, not args.no_cpu_baseline)
         line["gqa"] = run_gqa(dev, hbm_peak, peak_src, not args.no_cpu_baseline)
+        line["expert_ffn"] = run_expert_ffn(dev, hbm_peak, peak_src, not args.no_cpu_baseline)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, kind = cpu_reference_run(cfg, tensors, 64, 4, 0)
         cores, cpu_model = host_cpu()
