@@ -70,6 +70,7 @@ __host__ __device__ constexpr int64_t row_qbytes(int fmt, int64_t k) {
 }
 __device__ __forceinline__ int64_t xq_off(int64_t i) { return i + ((i >> 7) << 5); }
 
+
 // Bytes of the staged activations: MB x 3 level planes, the block scales and,
 // for Q4_K, the sums of every 16.
 __host__ __device__ constexpr size_t staged_bytes(int fmt, int mb, int64_t k) {
@@ -274,10 +275,12 @@ __device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Sta
 // producer's go) once its first batch is requested.
 template <int FMT, bool PADDED, bool SMEM, int U>
 __device__ __forceinline__ void stage_rows(const void* x, int x_dtype, int64_t m0, int mb, int rows, int64_t k,
-                                           int warp, int lane, int8_t* xq, int pl, float* sx, float* x16) {
+                                           int warp, int lane, int8_t* xq, int pl, float* sx, float* x16,
+                                           int swiglu) {
     const int npc = (int)(k >> 7), nblk = (int)(k >> 5);
     const size_t es = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
-    const char* x0 = static_cast<const char*>(x) + (SMEM ? 0 : (size_t)m0 * k * es);
+    const int64_t xk = swiglu ? 2 * k : k;  // elements per activation row in memory
+    const char* x0 = static_cast<const char*>(x) + (SMEM ? 0 : (size_t)m0 * xk * es);
     const bool vec = x_dtype == GDN_DTYPE_F32 && (reinterpret_cast<uintptr_t>(x0) & 15) == 0;
     bool announced = SMEM;
     // (j, c): row and piece of this warp's next item; advanced by kWarps pieces
@@ -296,8 +299,15 @@ __device__ __forceinline__ void stage_rows(const void* x, int x_dtype, int64_t m
             const int e = 128 * c + 4 * lane;
             xv[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             if (j < rows && j < mb) {
-                const char* xr = x0 + (size_t)j * k * es;
-                if (vec) {
+                const char* xr = x0 + (size_t)j * xk * es;
+                if (swiglu) {  // fp32 [g | u]: (g * sigmoid(g)) * u, as the reference's swiglu_kernel
+                    const float4 gv = *reinterpret_cast<const float4*>(xr + (size_t)e * 4);
+                    const float4 uv = *reinterpret_cast<const float4*>(xr + (size_t)(k + e) * 4);
+                    xv[u] = make_float4((gv.x * (1.0f / (1.0f + expf(-gv.x)))) * uv.x,
+                                        (gv.y * (1.0f / (1.0f + expf(-gv.y)))) * uv.y,
+                                        (gv.z * (1.0f / (1.0f + expf(-gv.z)))) * uv.z,
+                                        (gv.w * (1.0f / (1.0f + expf(-gv.w)))) * uv.w);
+                } else if (vec) {
                     xv[u] = *reinterpret_cast<const float4*>(xr + (size_t)e * 4);
                 } else {
                     xv[u] = make_float4(load_act(xr, x_dtype, e), load_act(xr, x_dtype, e + 1),
@@ -399,18 +409,52 @@ __device__ __forceinline__ void produce(const Ring& R, int64_t nst, Issue issue,
 template <int FMT, bool PADDED>
 __device__ __forceinline__ bool consume_activations(const Ring& R, const void* x, int x_dtype, const uint8_t* xs,
                                                     int64_t m0, int mb, int rows, int64_t k, int warp, int lane,
-                                                    int8_t* xq, int pl, float* sx, float* x16, uint32_t* err) {
+                                                    int8_t* xq, int pl, float* sx, float* x16, int swiglu,
+                                                    uint32_t* err) {
     bool ok = true;
     if (R.nx > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(R.xbar), 0, err));
-        if (ok) stage_rows<FMT, PADDED, true, kSmemBatch>(xs, x_dtype, 0, mb, rows, k, warp, lane, xq, pl, sx, x16);
+        if (ok)
+            stage_rows<FMT, PADDED, true, kSmemBatch>(xs, x_dtype, 0, mb, rows, k, warp, lane, xq, pl, sx, x16,
+                                                      swiglu);
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(R.xdone));
     } else {
-        stage_rows<FMT, PADDED, false, kStageBatch>(x, x_dtype, m0, mb, rows, k, warp, lane, xq, pl, sx, x16);
+        stage_rows<FMT, PADDED, false, kStageBatch>(x, x_dtype, m0, mb, rows, k, warp, lane, xq, pl, sx, x16,
+                                                    swiglu);
     }
     bar_sync(2, kWarps * 32);
     return ok;
+}
+
+// This CTA's weight rows [r0, r1): with one matrix CTA c of G owns rows
+// [c n / G, (c + 1) n / G); with two (o.wq2), the first half of the CTAs splits
+// the first matrix's n1 rows and the second half the other n - n1, so that no
+// CTA's rows (and no stage's bulk copy) straddle the two.  Row r is then row
+// r - rb of the matrix wb.
+__device__ __forceinline__ void row_range(int64_t n, const GemvOpts& o, int64_t& r0, int64_t& r1,
+                                          const uint8_t*& wb, int64_t& rb, const uint8_t* wq) {
+    const int64_t c = blockIdx.x, G = gridDim.x;
+    if (o.wq2 == nullptr) {
+        r0 = c * n / G;
+        r1 = (c + 1) * n / G;
+        wb = wq;
+        rb = 0;
+        return;
+    }
+    const int64_t G1 = G / 2;
+    if (c < G1) {
+        r0 = c * o.n1 / G1;
+        r1 = (c + 1) * o.n1 / G1;
+        wb = wq;
+        rb = 0;
+    } else {
+        const int64_t n2 = n - o.n1, c2 = c - G1, G2 = G - G1;
+        r0 = o.n1 + c2 * n2 / G2;
+        r1 = o.n1 + (c2 + 1) * n2 / G2;
+        wb = o.wq2;
+        rb = o.n1;
+    }
 }
 
 // FMT 0: Q8_0 planes (wq = int8 [n][k], wd = fp16 [n][k / 32]); FMT 1: Q4_K
@@ -423,7 +467,7 @@ template <int FMT, int MB>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     gemv_stream_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wd, int64_t n, int64_t k,
                        const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots, int nx,
-                       uint32_t* __restrict__ err) {
+                       GemvOpts o, uint32_t* __restrict__ err) {
     pdl_trigger();
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -442,7 +486,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const uint32_t qstage = kStageRows * qbytes;  // a stage: kStageRows int8 rows, then their scale rows
     const uint32_t stage_bytes = qstage + kStageRows * dbytes;
 
-    const int64_t r0 = (int64_t)blockIdx.x * n / gridDim.x, r1 = ((int64_t)blockIdx.x + 1) * n / gridDim.x;
+    int64_t r0, r1, rb;  // this CTA's rows [r0, r1); row r is row r - rb of matrix wb
+    const uint8_t* wb;
+    row_range(n, o, r0, r1, wb, rb, wq);
     const int64_t nst = (r1 - r0 + kStageRows - 1) / kStageRows;
     auto issue = [&](int64_t i, int slot) {  // producer lane 0: stage i into `slot` (= i mod slots)
         const int64_t ra = r0 + i * kStageRows;
@@ -450,7 +496,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         const uint32_t bar = smem_u32(R.full + slot);
         const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
         mbar_arrive_expect_tx(bar, rows * (qbytes + dbytes));
-        bulk_load(dst, wq + ra * (int64_t)qbytes, rows * qbytes, bar);
+        bulk_load(dst, wb + (ra - rb) * (int64_t)qbytes, rows * qbytes, bar);
         if (FMT == 0) bulk_load(dst + qstage, wd + ra * (int64_t)dbytes, rows * dbytes, bar);
     };
     if (warp == kWarps && lane == 0) {
@@ -458,7 +504,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {  // the weights never come from an earlier kernel
             const int64_t ra = r0 + i * kStageRows;
             const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
-            bulk_prefetch_l2(wq + ra * (int64_t)qbytes, rows * qbytes);
+            bulk_prefetch_l2(wb + (ra - rb) * (int64_t)qbytes, rows * qbytes);
             if (FMT == 0) bulk_prefetch_l2(wd + ra * (int64_t)dbytes, rows * dbytes);
         }
     }
@@ -468,15 +514,17 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
     const size_t esize = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
+    const int64_t xrow = o.swiglu ? 2 * k : k;  // activation elements per row in memory
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)
-        consume_activations<FMT, true>(R, x, x_dtype, xs, m0, mb, mb, k, warp, lane, xq, (int)st.pl, sx, x16, err);
+        consume_activations<FMT, true>(R, x, x_dtype, xs, m0, mb, mb, k, warp, lane, xq, (int)st.pl, sx, x16, o.swiglu,
+                                       err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);  // the activation loads are requested
         if (lane == 0)
-            produce(R, nst, issue, static_cast<const uint8_t*>(x) + (size_t)m0 * k * esize,
-                    (uint32_t)((size_t)mb * k * esize), xs, err);
+            produce(R, nst, issue, static_cast<const uint8_t*>(x) + (size_t)m0 * xrow * esize,
+                    (uint32_t)((size_t)mb * xrow * esize), xs, err);
         return;
     }
     int slot = 0;
@@ -499,7 +547,10 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             for (int j = 0; j < MB; j++) {
                 if (j < mb) {
                     const float v = warp_sum(acc[j]);
-                    if (lane == 0) y[(m0 + j) * ldy + r] = v;
+                    if (lane == 0) {
+                        float* yp = y + (m0 + j) * ldy + r;
+                        *yp = o.accumulate ? fmaf(o.alpha, v, *yp) : v;
+                    }
                 }
             }
         }
@@ -558,7 +609,7 @@ template <int FMT, int MT>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     gemv_mma_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wd, int64_t n, int64_t k,
                     const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots, int nx,
-                    uint32_t* __restrict__ err) {
+                    GemvOpts o, uint32_t* __restrict__ err) {
     constexpr int MB = 4 * MT;
     pdl_trigger();
     extern __shared__ __align__(128) uint8_t smem[];
@@ -577,7 +628,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const size_t stage_bytes = mma_stage_bytes(FMT, k);
     const size_t scale_off = (size_t)kStageRows * rl;
 
-    const int64_t r0 = (int64_t)blockIdx.x * n / gridDim.x, r1 = ((int64_t)blockIdx.x + 1) * n / gridDim.x;
+    int64_t r0, r1, rb;  // this CTA's rows [r0, r1); row r is row r - rb of matrix wb
+    const uint8_t* wb;
+    row_range(n, o, r0, r1, wb, rb, wq);
     const int64_t nst = (r1 - r0 + kStageRows - 1) / kStageRows;
     auto issue = [&](int64_t i, int slot) {  // producer lane 0: stage i into `slot`
         const int64_t ra = r0 + i * kStageRows;
@@ -586,7 +639,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
         mbar_arrive_expect_tx(bar, rows * (qbytes + dbytes));
         for (uint32_t r = 0; r < rows; r++)
-            bulk_load(dst + r * (uint32_t)rl, wq + (ra + r) * (int64_t)qbytes, qbytes, bar);
+            bulk_load(dst + r * (uint32_t)rl, wb + (ra - rb + r) * (int64_t)qbytes, qbytes, bar);
         if (FMT == 0) bulk_load(dst + (uint32_t)scale_off, wd + ra * (int64_t)dbytes, rows * dbytes, bar);
     };
     if (warp == kWarps && lane == 0) {
@@ -594,7 +647,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {  // the weights never come from an earlier kernel
             const int64_t ra = r0 + i * kStageRows;
             const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
-            bulk_prefetch_l2(wq + ra * (int64_t)qbytes, rows * qbytes);
+            bulk_prefetch_l2(wb + (ra - rb) * (int64_t)qbytes, rows * qbytes);
             if (FMT == 0) bulk_prefetch_l2(wd + ra * (int64_t)dbytes, rows * dbytes);
         }
     }
@@ -604,15 +657,17 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
     const size_t esize = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
+    const int64_t xrow = o.swiglu ? 2 * k : k;  // activation elements per row in memory
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)  // rows past mb are staged as zeros (their outputs are not stored)
-        consume_activations<FMT, false>(R, x, x_dtype, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx, x16, err);
+        consume_activations<FMT, false>(R, x, x_dtype, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx, x16, o.swiglu,
+                                        err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);
         if (lane == 0)
-            produce(R, nst, issue, static_cast<const uint8_t*>(x) + (size_t)m0 * k * esize,
-                    (uint32_t)((size_t)mb * k * esize), xs, err);
+            produce(R, nst, issue, static_cast<const uint8_t*>(x) + (size_t)m0 * xrow * esize,
+                    (uint32_t)((size_t)mb * xrow * esize), xs, err);
         return;
     }
 
@@ -773,7 +828,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
                 float sum = 0.0f;
 #pragma unroll 4
                 for (int w = 0; w < kWarps; w++) sum += rs[(size_t)w * 2 * MT * 32 + (g * MT + mt) * 32 + jj * 8 + col];
-                y[(m0 + j) * ldy + r] = sum;
+                float* yp = y + (m0 + j) * ldy + r;
+                *yp = o.accumulate ? fmaf(o.alpha, sum, *yp) : sum;
             }
         }
         if (++slot == slots) {
@@ -785,7 +841,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
 
 template <int FMT, int MT>
 int run_mma(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
-            int64_t ldy, int slots, int nx, size_t smem, cudaStream_t s) {
+            int64_t ldy, int slots, int nx, const GemvOpts& o, size_t smem, cudaStream_t s) {
     const void* fn = (const void*)gemv_mma_kernel<FMT, MT>;
     GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t ctas = std::min<int64_t>(sm_count(), n);
@@ -794,12 +850,12 @@ int run_mma(const void* wq, const void* wd, int64_t n, int64_t k, const void* x,
                       gemv_mma_kernel<FMT, MT>, grid,
                       dim3((kWarps + 1) * 32), smem, s,
                       static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
-                      slots, nx, device_error_word());
+                      slots, nx, o, device_error_word());
 }
 
 template <int FMT, int MB>
 int run(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y,
-        int64_t ldy, int slots, int nx, size_t smem, cudaStream_t s) {
+        int64_t ldy, int slots, int nx, const GemvOpts& o, size_t smem, cudaStream_t s) {
     const void* fn = (const void*)gemv_stream_kernel<FMT, MB>;
     GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t ctas = std::min<int64_t>(sm_count(), n);
@@ -808,15 +864,15 @@ int run(const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int
                                                                     : "gemv_stream_kernel<q5_k>",
                       gemv_stream_kernel<FMT, MB>, grid, dim3((kWarps + 1) * 32), smem, s,
                       static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
-                      slots, nx, device_error_word());
+                      slots, nx, o, device_error_word());
 }
 
 // Ring slots that first hold the activations (one bulk copy of the CTA's
 // rows): 0 -- load them from global memory instead -- unless x is 16-byte
 // aligned and they leave at least one slot for the weights.
-static int activation_slots(const void* x, int dt, int64_t k, int mb, size_t stage_bytes, int slots) {
+static int activation_slots(const void* x, int dt, int64_t xrow, int mb, size_t stage_bytes, int slots) {
     if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return 0;
-    const size_t bytes = (size_t)mb * k * (dt == GDN_DTYPE_F32 ? 4 : 2);
+    const size_t bytes = (size_t)mb * xrow * (dt == GDN_DTYPE_F32 ? 4 : 2);
     const int nx = (int)((bytes + stage_bytes - 1) / stage_bytes);
     return nx < slots ? nx : 0;
 }
@@ -870,34 +926,40 @@ static int plan_mma(int fmt, const void* wq, const void* wd, int64_t k, int64_t 
 
 template <int FMT>
 static int run_fmt(int mb, int mma, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt,
-                   int64_t m, float* y, int64_t ldy, int slots, int nx, size_t smem, cudaStream_t s) {
-    if (mma) return mb == 2 ? run_mma<FMT, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s)
-                            : run_mma<FMT, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+                   int64_t m, float* y, int64_t ldy, int slots, int nx, const GemvOpts& o, size_t smem,
+                   cudaStream_t s) {
+    if (mma) return mb == 2 ? run_mma<FMT, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s)
+                            : run_mma<FMT, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
     switch (mb) {
-        case 1: return run<FMT, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-        case 2: return run<FMT, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-        case 4: return run<FMT, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-        default: return run<FMT, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+        case 1: return run<FMT, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
+        case 2: return run<FMT, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
+        case 4: return run<FMT, 4>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
+        default: return run<FMT, 8>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
     }
 }
 
 int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt,
-                       int64_t m, float* y, int64_t ldy, cudaStream_t s) {
+                       int64_t m, float* y, int64_t ldy, cudaStream_t s, const GemvOpts& o) {
     if (fmt < 0 || fmt > 2) return GDN_ERR_TYPE;
+    if (o.wq2 && (fmt == 0 || o.n1 <= 0 || o.n1 >= n || (reinterpret_cast<uintptr_t>(o.wq2) & 15) != 0))
+        return GDN_ERR_ARG;
+    if (o.swiglu && (dt != GDN_DTYPE_F32 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)) return GDN_ERR_ARG;
+    const int64_t xrow = o.swiglu ? 2 * k : k;
     int mb = 0, slots = 0, nx = 0, mma = 0;
     size_t smem = 0;
     if (n > 0 && plan_mma(fmt, wq, wd, k, m, &mb, &slots, &smem)) {
         mma = 1;
-        nx = activation_slots(x, dt, k, 4 * mb, mma_stage_bytes(fmt, k), slots);
+        nx = activation_slots(x, dt, xrow, 4 * mb, mma_stage_bytes(fmt, k), slots);
     } else {
         if (!plan(fmt, wq, wd, k, m, &mb, &slots, &smem)) return GDN_ERR_SHAPE;
         if (n <= 0) return GDN_OK;
         const size_t stage = (size_t)kStageRows * (fmt == 0 ? k + k / 16 : row_qbytes(fmt, k));
-        nx = activation_slots(x, dt, k, mb, stage, slots);
+        nx = activation_slots(x, dt, xrow, mb, stage, slots);
     }
-    if (fmt == 0) return run_fmt<0>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-    if (fmt == 1) return run_fmt<1>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
-    return run_fmt<2>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, smem, s);
+    if (o.wq2 && std::min<int64_t>(sm_count(), n) < 2) return GDN_ERR_SHAPE;
+    if (fmt == 0) return run_fmt<0>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
+    if (fmt == 1) return run_fmt<1>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
+    return run_fmt<2>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
 }
 
 bool gemv_stream_fits(int fmt, const void* wq, const void* wd, int64_t k, int64_t m) {

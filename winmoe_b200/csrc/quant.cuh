@@ -20,9 +20,19 @@ int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, 
 // Streamed GEMV (gemv_stream.cu), fmt 0 = Q8_0 planes (wd = the fp16 scale
 // plane), 1 = Q4_K blocks: k a multiple of 512 (Q8_0) or 256 (Q4_K) and
 // 16-byte aligned weights; gemv_stream_fits says whether a call qualifies.
+// Options (the expert FFN's fusions): rows n1 .. n - 1 from a second Q4_K /
+// Q5_K matrix wq2 (its rows 0 ..); fp32 activation rows holding [g | u] (2 k
+// values) whose input is (g * sigmoid(g)) * u; y += alpha * result.
+struct GemvOpts {
+    const uint8_t* wq2 = nullptr;
+    int64_t n1 = 0;
+    int swiglu = 0;
+    int accumulate = 0;
+    float alpha = 1.0f;
+};
 bool gemv_stream_fits(int fmt, const void* wq, const void* wd, int64_t k, int64_t m);
 int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int x_dtype,
-                       int64_t m, float* y, int64_t ldy, cudaStream_t s);
+                       int64_t m, float* y, int64_t ldy, cudaStream_t s, const GemvOpts& o = GemvOpts());
 int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s);
 int launch_q5_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s);
 int launch_q5_k_gemv(const void* blocks, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
