@@ -407,10 +407,12 @@ EXPERT_HIDDEN, EXPERT_INTER, EXPERT_TOPK, EXPERT_POOL = 2048, 512, 8, 128
 
 def run_expert_ffn(dev, hbm_peak, peak_src, with_cpu):
     """(f)4: the MoE experts of one token, the reference's batched GPU route
-    (gpu_expert_batch_add, gpu_offload.cu:766-793): for each of 8 experts, Q4_K
-    gate / up, SwiGLU, Q5_K down, weighted into the token's output.  Token i uses
-    experts 8i .. 8i+7 of a pool of 128 distinct experts (243 MB > L2: weights from
-    HBM), weights 1/8."""
+    (gpu_expert_batch_start / _add / _finish, gpu_offload.cu:756-809): 8 experts,
+    each Q4_K gate / up, SwiGLU, Q5_K down, weighted into the token's output --
+    one gdn_experts_ffn call per token (three launches).  Token i uses experts
+    8i .. 8i+7 of a pool of 128 distinct experts (243 MB > L2: weights from HBM),
+    weights 1/8.  Beside it, the same tokens as 8 single-expert accumulating
+    calls each (the reference's call pattern, two launches per expert)."""
     import torch
     from winmoe_b200 import layer as L, synth
     from winmoe_b200._lib import lib
@@ -426,31 +428,43 @@ def run_expert_ffn(dev, hbm_peak, peak_src, with_cpu):
     n_tok = 16
     xs = torch.from_numpy(synth.hidden_states(n_tok, H, seed=78)).to(dev)
     out = torch.zeros((n_tok, H), dtype=torch.float32, device=dev)
-    ws = torch.empty(lib().gdn_expert_ffn_workspace_size(1, H, I), dtype=torch.uint8, device=dev)
+    ws = torch.empty(lib().gdn_experts_ffn_workspace_size(K, 1, H, I), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+    wts = [1.0 / K] * K
 
-    def token(i):
+    def token_batched(i):
+        sel = [pool[(K * i + e) % NP] for e in range(K)]
+        L.experts_ffn([w[0] for w in sel], [w[1] for w in sel], [w[2] for w in sel], 12, 13, H, I, xs[i:i + 1],
+                      weights=wts, out=out[i:i + 1], accumulate=True, workspace=ws, stream=stream)
+
+    def token_single(i):
         for e in range(K):
             wg, wu, wd = pool[(K * i + e) % NP]
             L.expert_ffn(wg, wu, wd, 12, 13, H, I, xs[i:i + 1], out=out[i:i + 1], weight=1.0 / K, accumulate=True,
                          workspace=ws, stream=stream)
-    for i in range(4):
-        token(i)
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda._sleep(20_000_000)  # the calls queue behind ~10 ms of GPU time: events time the kernels
-    e0.record(stream)
-    for i in range(n_tok):
-        token(i)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    us = e0.elapsed_time(e1) / n_tok * 1e3
+
+    def timed(token):
+        for i in range(4):
+            token(i)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(20_000_000)  # the calls queue behind ~10 ms of GPU time: events time the kernels
+        e0.record(stream)
+        for i in range(n_tok):
+            token(i)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n_tok * 1e3
+    us_single = timed(token_single)
+    us = timed(token_batched)
     nb = K * (2 * I * (H // 256) * 144 + H * (I // 256) * 176) + (H + K * (3 * I + 2 * H)) * 4
     res = {"workload": "MoE experts of one token (35B-class: hidden 2048, expert intermediate 512, top-8): Q4_K "
                        "gate + up, SwiGLU, Q5_K down, weighted accumulation, 8 experts per token from a pool of "
-                       "128 (243 MB > L2: weights from HBM); 16 tokens queued behind a GPU sleep",
+                       "128 (243 MB > L2: weights from HBM); one gdn_experts_ffn call (3 launches) per token; "
+                       "16 tokens queued behind a GPU sleep",
            "value": 1e6 / us, "unit": "tok/s", "us_per_token": us, "us_per_expert": us / K,
-           "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel<q4_k/q5_k> x 3 per expert",
+           "us_per_token_single_expert_calls": us_single,
+           "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel<q4_k/q5_k> x 2 + experts_sum_kernel per token",
                         "achieved": nb / (us / 1e6) / 1e9, "peak": hbm_peak, "unit": "GB/s",
                         "frac": nb / (us / 1e6) / 1e9 / hbm_peak, "peak_source": peak_src,
                         "algorithmic_bytes_per_token": nb}}

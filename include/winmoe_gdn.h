@@ -196,6 +196,27 @@ GDN_API int gdn_expert_ffn(const void* w_gate, const void* w_up, const void* w_d
                   int64_t hidden, int64_t inter, const void* x, int x_dtype, int64_t m, float* out,
                   float weight, int accumulate, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * All selected experts of m tokens in one call, the reference's batched expert
+ * block (gpu_expert_batch_start / gpu_expert_batch_add per expert /
+ * gpu_expert_batch_finish, engine/runtime/gpu_offload.cu:756-809):
+ *   out[m][hidden] = sum_e weights[e] * y_e      (accumulate == 0)
+ *   out[m][hidden] += sum_e weights[e] * y_e     (accumulate != 0)
+ * with y_e expert e's FFN as gdn_expert_ffn's, the sum in expert order
+ * (weights NULL: all 1).  w_gate / w_up / w_down: host arrays of n_experts
+ * device pointers, 1 <= n_experts <= GDN_MAX_EXPERTS_PER_CALL; three launches
+ * whatever n_experts (one streamed GEMV over all gate and up matrices, one over
+ * all down matrices, the weighted sum).  Workspace of
+ * gdn_experts_ffn_workspace_size(n_experts, m, hidden, inter) bytes, 256-byte
+ * aligned; weights read on the host when the call is made.
+ */
+#define GDN_MAX_EXPERTS_PER_CALL 8
+GDN_API size_t gdn_experts_ffn_workspace_size(int n_experts, int64_t m, int64_t hidden, int64_t inter);
+GDN_API int gdn_experts_ffn(int n_experts, const void* const* w_gate, const void* const* w_up,
+                  const void* const* w_down, int gate_type, int down_type, int64_t hidden, int64_t inter,
+                  const void* x, int x_dtype, int64_t m, const float* weights, float* out, int accumulate,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- the layer */
 
 /* Dimensions, as dn_init_dims derives them (engine/runtime/deltanet_impl.h:32-44):

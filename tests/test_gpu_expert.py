@@ -1,5 +1,6 @@
-"""The expert FFN's GGUF projections and its fused route on the GPU (SURVEY
-row (f)4; gpu_offload.cu:271-331, 341-457, 718-793) against the CPU oracle.
+"""The expert FFN's GGUF projections and its fused and batched routes on the
+GPU (engine/runtime/gpu_offload.cu:271-331, 341-457, 718-809) against the CPU
+oracle.
 
 Bit-exact: Q5_K dequantised weights.  Tolerances: the streamed Q5_K GEMV with
 fp32 activations vs the oracle's fp32-activation rows (q5k_matvec_kernel),
@@ -86,6 +87,64 @@ def test_expert_batch_accumulates_weighted_experts():
                      workspace=ws)
         P.expert_ffn(x[0], wg, wu, wd, Q4K, Q5K, hidden, inter, weight=w, out=want)
     assert rel_l2(out.cpu().numpy()[0], want) <= 1e-4
+
+
+@pytest.mark.parametrize("ne,m,accumulate", [(1, 1, False), (2, 3, True), (8, 1, True), (8, 4, False),
+                                               (5, 2, True)])
+def test_experts_ffn_batched_matches_oracle(ne, m, accumulate):
+    """gpu_expert_batch_start / _add x ne / _finish as one call: three launches
+    whatever ne; out (+)= sum_e w_e * expert_e(x), in expert order."""
+    hidden, inter = 2048, 512
+    experts = [_expert(hidden, inter, Q4K, Q5K, seed=700 + 3 * e) for e in range(ne)]
+    weights = [0.9 / (e + 1) for e in range(ne)]
+    x = synth.hidden_states(m, hidden, seed=701)
+    base = synth.hidden_states(m, hidden, seed=702) if accumulate else np.zeros((m, hidden), np.float32)
+    out = torch.from_numpy(base.copy()).to(DEV)
+    L.experts_ffn([dev(e[0]) for e in experts], [dev(e[1]) for e in experts], [dev(e[2]) for e in experts], Q4K,
+                  Q5K, hidden, inter, torch.from_numpy(x).to(DEV), weights=weights, out=out, accumulate=accumulate)
+    got = out.cpu().numpy()
+    P = O.port()
+    for i in range(m):
+        want = base[i].copy()
+        for (wg, wu, wd), w in zip(experts, weights):
+            P.expert_ffn(x[i], wg, wu, wd, Q4K, Q5K, hidden, inter, weight=w, out=want)
+        assert rel_l2(got[i], want) <= 1e-4, i
+    # and the same sum as ne single-expert accumulating calls
+    seq = torch.from_numpy(base.copy()).to(DEV)
+    for (wg, wu, wd), w in zip(experts, weights):
+        L.expert_ffn(dev(wg), dev(wu), dev(wd), Q4K, Q5K, hidden, inter, torch.from_numpy(x).to(DEV), out=seq,
+                     weight=w, accumulate=True)
+    assert rel_l2(got, seq.cpu().numpy()) <= 1e-6
+
+
+def test_experts_ffn_unweighted_and_empty():
+    hidden, inter = 512, 256
+    experts = [_expert(hidden, inter, Q5K, Q5K, seed=720 + 3 * e) for e in range(3)]
+    x = synth.hidden_states(2, hidden, seed=721)
+    args = ([dev(e[0]) for e in experts], [dev(e[1]) for e in experts], [dev(e[2]) for e in experts], Q5K, Q5K,
+            hidden, inter, torch.from_numpy(x).to(DEV))
+    got = L.experts_ffn(*args).cpu().numpy()  # weights None: all 1
+    P = O.port()
+    for i in range(2):
+        want = np.zeros(hidden, np.float32)
+        for wg, wu, wd in experts:
+            P.expert_ffn(x[i], wg, wu, wd, Q5K, Q5K, hidden, inter, weight=1.0, out=want)
+        assert rel_l2(got[i], want) <= 1e-4, i
+    out = torch.full((2, hidden), 3.0, device=DEV)
+    L.experts_ffn([], [], [], Q5K, Q5K, hidden, inter, torch.from_numpy(x).to(DEV), out=out, accumulate=True)
+    assert bool((out == 3.0).all())  # no experts: nothing launched, out untouched
+
+
+def test_experts_ffn_rejects_bad_arguments():
+    hidden, inter = 512, 256
+    wg, wu, wd = (dev(a) for a in _expert(hidden, inter, Q4K, Q5K, seed=730))
+    x = torch.zeros((1, hidden), device=DEV)
+    with pytest.raises(GDNError):  # more experts than one call takes
+        L.experts_ffn([wg] * 9, [wu] * 9, [wd] * 9, Q4K, Q5K, hidden, inter, x)
+    with pytest.raises(GDNError):  # a misaligned expert among aligned ones
+        L.experts_ffn([wg, wg[1:]], [wu, wu], [wd, wd], Q4K, Q5K, hidden, inter, x)
+    with pytest.raises(GDNError):
+        L.experts_ffn([wg], [wu], [wd, wd], Q4K, Q5K, hidden, inter, x)
 
 
 def test_expert_ffn_rejects_bad_arguments():

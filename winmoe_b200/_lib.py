@@ -66,6 +66,9 @@ SIGNATURES = {
     "gdn_expert_ffn_workspace_size": (_sz, [_i64, _i64, _i64]),
     "gdn_expert_ffn": (_int, [_vp, _vp, _vp, _int, _int, _i64, _i64, _vp, _int, _i64, _vp, C.c_float, _int, _vp,
                               _sz, _vp]),
+    "gdn_experts_ffn_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
+    "gdn_experts_ffn": (_int, [_int, _vp, _vp, _vp, _int, _int, _i64, _i64, _vp, _int, _i64, _vp, _vp, _int, _vp,
+                               _sz, _vp]),
     "gdn_decode_workspace_size": (_sz, [C.POINTER(gdn_dims), _i64]),
     "gdn_decode_step": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gdn_decode_step_ex": (_int, [C.POINTER(gdn_layer), _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _sz, _int, _vp]),

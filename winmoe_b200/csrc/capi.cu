@@ -178,27 +178,46 @@ int gdn_q5_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, 
 
 size_t gdn_expert_ffn_workspace_size(int64_t m, int64_t hidden, int64_t inter) {
     if (m <= 0 || hidden <= 0 || inter <= 0) return 0;
-    return expert_ffn_workspace_bytes(m, hidden, inter);
+    return experts_ffn_workspace_bytes(1, m, hidden, inter);
+}
+
+size_t gdn_experts_ffn_workspace_size(int n_experts, int64_t m, int64_t hidden, int64_t inter) {
+    if (n_experts <= 0 || n_experts > GDN_MAX_EXPERTS_PER_CALL || m <= 0 || hidden <= 0 || inter <= 0) return 0;
+    return experts_ffn_workspace_bytes(n_experts, m, hidden, inter);
+}
+
+int gdn_experts_ffn(int n_experts, const void* const* w_gate, const void* const* w_up, const void* const* w_down,
+                    int gate_type, int down_type, int64_t hidden, int64_t inter, const void* x, int x_dtype, int64_t m,
+                    const float* weights, float* out, int accumulate, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+    auto kq = [](int t) { return t == GDN_GGML_Q4_K || t == GDN_GGML_Q5_K; };
+    if (!kq(gate_type) || !kq(down_type))
+        return fail(GDN_ERR_TYPE, "expert ffn: weight types must be Q4_K (12) or Q5_K (13), got %d / %d", gate_type,
+                    down_type);
+    if (n_experts < 0 || n_experts > GDN_MAX_EXPERTS_PER_CALL)
+        return fail(GDN_ERR_ARG, "expert ffn: %d experts, 0..%d per call", n_experts, GDN_MAX_EXPERTS_PER_CALL);
+    if (m < 0 || hidden <= 0 || inter <= 0 || hidden % 256 != 0 || inter % 256 != 0)
+        return fail(GDN_ERR_SHAPE, "expert ffn: hidden and inter must be positive multiples of 256");
+    if (n_experts == 0 || m == 0) return GDN_OK;
+    if (!w_gate || !w_up || !w_down || !x || !out || !workspace) return fail(GDN_ERR_ARG, "expert ffn: NULL pointer");
+    for (int e = 0; e < n_experts; e++) {
+        if (!w_gate[e] || !w_up[e] || !w_down[e]) return fail(GDN_ERR_ARG, "expert ffn: NULL weights of expert %d", e);
+        if (!aligned(w_gate[e], 16) || !aligned(w_up[e], 16) || !aligned(w_down[e], 16))
+            return fail(GDN_ERR_ARG, "expert ffn: weights of expert %d must be 16-byte aligned", e);
+    }
+    if (!aligned(workspace, 256)) return fail(GDN_ERR_ARG, "expert ffn: workspace must be 256-byte aligned");
+    int st = check_act_dtype(x_dtype);
+    if (st) return st;
+    return launch_experts_ffn(n_experts, w_gate, w_up, w_down, gate_type, down_type, hidden, inter, x, x_dtype, m,
+                              weights, out, accumulate, workspace, workspace_bytes, as_stream(stream));
 }
 
 int gdn_expert_ffn(const void* w_gate, const void* w_up, const void* w_down, int gate_type, int down_type,
                    int64_t hidden, int64_t inter, const void* x, int x_dtype, int64_t m, float* out, float weight,
                    int accumulate, void* workspace, size_t workspace_bytes, void* stream) {
-    auto kq = [](int t) { return t == GDN_GGML_Q4_K || t == GDN_GGML_Q5_K; };
-    if (!kq(gate_type) || !kq(down_type))
-        return fail(GDN_ERR_TYPE, "expert ffn: weight types must be Q4_K (12) or Q5_K (13), got %d / %d", gate_type,
-                    down_type);
-    if (m < 0 || hidden <= 0 || inter <= 0 || hidden % 256 != 0 || inter % 256 != 0)
-        return fail(GDN_ERR_SHAPE, "expert ffn: hidden and inter must be positive multiples of 256");
-    if (!w_gate || !w_up || !w_down || !x || !out || (m > 0 && !workspace))
-        return fail(GDN_ERR_ARG, "expert ffn: NULL pointer");
-    if (!aligned(w_gate, 16) || !aligned(w_up, 16) || !aligned(w_down, 16))
-        return fail(GDN_ERR_ARG, "expert ffn: weights must be 16-byte aligned");
-    if (!aligned(workspace, 256)) return fail(GDN_ERR_ARG, "expert ffn: workspace must be 256-byte aligned");
-    int st = check_act_dtype(x_dtype);
-    if (st) return st;
-    return launch_expert_ffn(w_gate, w_up, w_down, gate_type, down_type, hidden, inter, x, x_dtype, m, out, weight,
-                             accumulate, workspace, workspace_bytes, as_stream(stream));
+    const float w = accumulate ? weight : 1.0f;  // stored unweighted, as gpu_expert_ffn_fused returns it
+    return gdn_experts_ffn(1, &w_gate, &w_up, &w_down, gate_type, down_type, hidden, inter, x, x_dtype, m, &w, out,
+                           accumulate, workspace, workspace_bytes, stream);
 }
 
 size_t gdn_decode_workspace_size(const gdn_dims* dims, int64_t batch) {

@@ -274,12 +274,12 @@ __device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Sta
 // reductions.  From global memory the warp arrives on named barrier 1 (the
 // producer's go) once its first batch is requested.
 template <int FMT, bool PADDED, bool SMEM, int U>
-__device__ __forceinline__ void stage_rows(const void* x, int x_dtype, int64_t m0, int mb, int rows, int64_t k,
-                                           int warp, int lane, int8_t* xq, int pl, float* sx, float* x16,
+__device__ __forceinline__ void stage_rows(const void* x, int x_dtype, int64_t ldx, int64_t m0, int mb, int rows,
+                                           int64_t k, int warp, int lane, int8_t* xq, int pl, float* sx, float* x16,
                                            int swiglu) {
     const int npc = (int)(k >> 7), nblk = (int)(k >> 5);
     const size_t es = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
-    const int64_t xk = swiglu ? 2 * k : k;  // elements per activation row in memory
+    const int64_t xk = ldx;  // elements between activation rows
     const char* x0 = static_cast<const char*>(x) + (SMEM ? 0 : (size_t)m0 * xk * es);
     const bool vec = x_dtype == GDN_DTYPE_F32 && (reinterpret_cast<uintptr_t>(x0) & 15) == 0;
     bool announced = SMEM;
@@ -367,11 +367,17 @@ __device__ __forceinline__ void ring_init(const Ring& R) {
 }
 
 template <class Issue>
-__device__ __forceinline__ void produce(const Ring& R, int64_t nst, Issue issue, const void* xsrc, uint32_t xbytes,
-                                        const uint8_t* xdst, uint32_t* err) {
-    if (R.nx > 0) {
-        mbar_arrive_expect_tx(smem_u32(R.xbar), xbytes);
-        bulk_load(smem_u32(xdst), xsrc, xbytes, smem_u32(R.xbar));
+__device__ __forceinline__ void produce(const Ring& R, int64_t nst, Issue issue, const void* xsrc, int xrows,
+                                        uint32_t xrow_bytes, size_t xsrc_stride, const uint8_t* xdst, uint32_t* err) {
+    if (R.nx > 0) {  // the activation rows, packed at xdst (one copy, or one per row when strided)
+        mbar_arrive_expect_tx(smem_u32(R.xbar), (uint32_t)xrows * xrow_bytes);
+        if (xsrc_stride == xrow_bytes) {
+            bulk_load(smem_u32(xdst), xsrc, (uint32_t)xrows * xrow_bytes, smem_u32(R.xbar));
+        } else {
+            for (int j = 0; j < xrows; j++)
+                bulk_load(smem_u32(xdst) + (uint32_t)j * xrow_bytes, static_cast<const char*>(xsrc) + j * xsrc_stride,
+                          xrow_bytes, smem_u32(R.xbar));
+        }
     }
     int64_t issued = 0;
     int slot = 0;
@@ -407,20 +413,20 @@ __device__ __forceinline__ void produce(const Ring& R, int64_t nst, Issue issue,
 // error word is set; the planes are then not staged, and every wait of the
 // caller still ends).
 template <int FMT, bool PADDED>
-__device__ __forceinline__ bool consume_activations(const Ring& R, const void* x, int x_dtype, const uint8_t* xs,
-                                                    int64_t m0, int mb, int rows, int64_t k, int warp, int lane,
-                                                    int8_t* xq, int pl, float* sx, float* x16, int swiglu,
-                                                    uint32_t* err) {
+__device__ __forceinline__ bool consume_activations(const Ring& R, const void* x, int x_dtype, int64_t ldx,
+                                                    const uint8_t* xs, int64_t m0, int mb, int rows, int64_t k,
+                                                    int warp, int lane, int8_t* xq, int pl, float* sx, float* x16,
+                                                    int swiglu, uint32_t* err) {
     bool ok = true;
     if (R.nx > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(R.xbar), 0, err));
         if (ok)
-            stage_rows<FMT, PADDED, true, kSmemBatch>(xs, x_dtype, 0, mb, rows, k, warp, lane, xq, pl, sx, x16,
-                                                      swiglu);
+            stage_rows<FMT, PADDED, true, kSmemBatch>(xs, x_dtype, swiglu ? 2 * k : k, 0, mb, rows, k, warp, lane,
+                                                      xq, pl, sx, x16, swiglu);
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(R.xdone));
     } else {
-        stage_rows<FMT, PADDED, false, kStageBatch>(x, x_dtype, m0, mb, rows, k, warp, lane, xq, pl, sx, x16,
+        stage_rows<FMT, PADDED, false, kStageBatch>(x, x_dtype, ldx, m0, mb, rows, k, warp, lane, xq, pl, sx, x16,
                                                     swiglu);
     }
     bar_sync(2, kWarps * 32);
@@ -428,33 +434,32 @@ __device__ __forceinline__ bool consume_activations(const Ring& R, const void* x
 }
 
 // This CTA's weight rows [r0, r1): with one matrix CTA c of G owns rows
-// [c n / G, (c + 1) n / G); with two (o.wq2), the first half of the CTAs splits
-// the first matrix's n1 rows and the second half the other n - n1, so that no
-// CTA's rows (and no stage's bulk copy) straddle the two.  Row r is then row
-// r - rb of the matrix wb.
+// [c n / G, (c + 1) n / G); with a segment table (o.nseg matrices of seg_rows
+// rows), G / nseg CTAs split each matrix (the rest own nothing), so that no
+// CTA's rows -- and no stage's bulk copy -- straddle two matrices.  Row r is
+// then row r - rb of the matrix wb, and sg the CTA's matrix (0 without a table).
 __device__ __forceinline__ void row_range(int64_t n, const GemvOpts& o, int64_t& r0, int64_t& r1,
-                                          const uint8_t*& wb, int64_t& rb, const uint8_t* wq) {
+                                          const uint8_t*& wb, int64_t& rb, int& sg, const uint8_t* wq) {
     const int64_t c = blockIdx.x, G = gridDim.x;
-    if (o.wq2 == nullptr) {
+    if (o.nseg == 0) {
         r0 = c * n / G;
         r1 = (c + 1) * n / G;
         wb = wq;
         rb = 0;
+        sg = 0;
         return;
     }
-    const int64_t G1 = G / 2;
-    if (c < G1) {
-        r0 = c * o.n1 / G1;
-        r1 = (c + 1) * o.n1 / G1;
-        wb = wq;
-        rb = 0;
-    } else {
-        const int64_t n2 = n - o.n1, c2 = c - G1, G2 = G - G1;
-        r0 = o.n1 + c2 * n2 / G2;
-        r1 = o.n1 + (c2 + 1) * n2 / G2;
-        wb = o.wq2;
-        rb = o.n1;
+    const int64_t Gs = G / o.nseg;
+    sg = (int)min(c / Gs, (int64_t)o.nseg - 1);
+    const int64_t cs = c - (int64_t)sg * Gs;
+    rb = (int64_t)sg * o.seg_rows;
+    wb = o.seg[sg];
+    if (cs >= Gs) {  // beyond the last matrix's share: nothing
+        r0 = r1 = rb;
+        return;
     }
+    r0 = rb + cs * o.seg_rows / Gs;
+    r1 = rb + (cs + 1) * o.seg_rows / Gs;
 }
 
 // FMT 0: Q8_0 planes (wq = int8 [n][k], wd = fp16 [n][k / 32]); FMT 1: Q4_K
@@ -488,7 +493,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
 
     int64_t r0, r1, rb;  // this CTA's rows [r0, r1); row r is row r - rb of matrix wb
     const uint8_t* wb;
-    row_range(n, o, r0, r1, wb, rb, wq);
+    int sg;
+    row_range(n, o, r0, r1, wb, rb, sg, wq);
     const int64_t nst = (r1 - r0 + kStageRows - 1) / kStageRows;
     auto issue = [&](int64_t i, int slot) {  // producer lane 0: stage i into `slot` (= i mod slots)
         const int64_t ra = r0 + i * kStageRows;
@@ -514,17 +520,19 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
     const size_t esize = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
-    const int64_t xrow = o.swiglu ? 2 * k : k;  // activation elements per row in memory
+    const int64_t xrow = o.swiglu ? 2 * k : k;  // activation elements per row read
+    const int64_t ldx = o.ldx ? o.ldx : xrow;   // ... and between rows in memory
+    const void* xe = static_cast<const char*>(x) + (size_t)sg * o.x_seg * esize;  // this CTA's matrix's input
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)
-        consume_activations<FMT, true>(R, x, x_dtype, xs, m0, mb, mb, k, warp, lane, xq, (int)st.pl, sx, x16, o.swiglu,
-                                       err);
+        consume_activations<FMT, true>(R, xe, x_dtype, ldx, xs, m0, mb, mb, k, warp, lane, xq, (int)st.pl, sx, x16,
+                                       o.swiglu, err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);  // the activation loads are requested
         if (lane == 0)
-            produce(R, nst, issue, static_cast<const uint8_t*>(x) + (size_t)m0 * xrow * esize,
-                    (uint32_t)((size_t)mb * xrow * esize), xs, err);
+            produce(R, nst, issue, static_cast<const uint8_t*>(xe) + (size_t)m0 * ldx * esize, mb,
+                    (uint32_t)((size_t)xrow * esize), (size_t)ldx * esize, xs, err);
         return;
     }
     int slot = 0;
@@ -549,7 +557,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
                     const float v = warp_sum(acc[j]);
                     if (lane == 0) {
                         float* yp = y + (m0 + j) * ldy + r;
-                        *yp = o.accumulate ? fmaf(o.alpha, v, *yp) : v;
+                        *yp = o.accumulate ? fmaf(o.alpha, v, *yp) : o.alpha * v;
                     }
                 }
             }
@@ -630,7 +638,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
 
     int64_t r0, r1, rb;  // this CTA's rows [r0, r1); row r is row r - rb of matrix wb
     const uint8_t* wb;
-    row_range(n, o, r0, r1, wb, rb, wq);
+    int sg;
+    row_range(n, o, r0, r1, wb, rb, sg, wq);
     const int64_t nst = (r1 - r0 + kStageRows - 1) / kStageRows;
     auto issue = [&](int64_t i, int slot) {  // producer lane 0: stage i into `slot`
         const int64_t ra = r0 + i * kStageRows;
@@ -657,17 +666,19 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int64_t m0 = (int64_t)blockIdx.y * MB;
     const int mb = (int)min((int64_t)MB, m - m0);
     const size_t esize = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
-    const int64_t xrow = o.swiglu ? 2 * k : k;  // activation elements per row in memory
+    const int64_t xrow = o.swiglu ? 2 * k : k;  // activation elements per row read
+    const int64_t ldx = o.ldx ? o.ldx : xrow;   // ... and between rows in memory
+    const void* xe = static_cast<const char*>(x) + (size_t)sg * o.x_seg * esize;  // this CTA's matrix's input
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)  // rows past mb are staged as zeros (their outputs are not stored)
-        consume_activations<FMT, false>(R, x, x_dtype, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx, x16, o.swiglu,
-                                        err);
+        consume_activations<FMT, false>(R, xe, x_dtype, ldx, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx, x16,
+                                        o.swiglu, err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);
         if (lane == 0)
-            produce(R, nst, issue, static_cast<const uint8_t*>(x) + (size_t)m0 * xrow * esize,
-                    (uint32_t)((size_t)mb * xrow * esize), xs, err);
+            produce(R, nst, issue, static_cast<const uint8_t*>(xe) + (size_t)m0 * ldx * esize, mb,
+                    (uint32_t)((size_t)xrow * esize), (size_t)ldx * esize, xs, err);
         return;
     }
 
@@ -829,7 +840,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
 #pragma unroll 4
                 for (int w = 0; w < kWarps; w++) sum += rs[(size_t)w * 2 * MT * 32 + (g * MT + mt) * 32 + jj * 8 + col];
                 float* yp = y + (m0 + j) * ldy + r;
-                *yp = o.accumulate ? fmaf(o.alpha, sum, *yp) : sum;
+                *yp = o.accumulate ? fmaf(o.alpha, sum, *yp) : o.alpha * sum;
             }
         }
         if (++slot == slots) {
@@ -941,10 +952,17 @@ static int run_fmt(int mb, int mma, const void* wq, const void* wd, int64_t n, i
 int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt,
                        int64_t m, float* y, int64_t ldy, cudaStream_t s, const GemvOpts& o) {
     if (fmt < 0 || fmt > 2) return GDN_ERR_TYPE;
-    if (o.wq2 && (fmt == 0 || o.n1 <= 0 || o.n1 >= n || (reinterpret_cast<uintptr_t>(o.wq2) & 15) != 0))
-        return GDN_ERR_ARG;
+    if (o.nseg) {
+        if (fmt == 0 || o.nseg > kGemvMaxSeg || o.seg_rows <= 0 || n != o.nseg * o.seg_rows) return GDN_ERR_ARG;
+        for (int i = 0; i < o.nseg; i++)
+            if (!o.seg[i] || (reinterpret_cast<uintptr_t>(o.seg[i]) & 15) != 0) return GDN_ERR_ARG;
+        if (std::min<int64_t>(sm_count(), n) < o.nseg) return GDN_ERR_SHAPE;
+    }
     if (o.swiglu && (dt != GDN_DTYPE_F32 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)) return GDN_ERR_ARG;
     const int64_t xrow = o.swiglu ? 2 * k : k;
+    // strided or offset activations: every row start 16-byte aligned for the bulk copies
+    const size_t es = dt == GDN_DTYPE_F32 ? 4 : 2;
+    if ((o.ldx && (o.ldx < xrow || (o.ldx * es) % 16)) || (o.x_seg * es) % 16) return GDN_ERR_ARG;
     int mb = 0, slots = 0, nx = 0, mma = 0;
     size_t smem = 0;
     if (n > 0 && plan_mma(fmt, wq, wd, k, m, &mb, &slots, &smem)) {
@@ -956,7 +974,6 @@ int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64
         const size_t stage = (size_t)kStageRows * (fmt == 0 ? k + k / 16 : row_qbytes(fmt, k));
         nx = activation_slots(x, dt, xrow, mb, stage, slots);
     }
-    if (o.wq2 && std::min<int64_t>(sm_count(), n) < 2) return GDN_ERR_SHAPE;
     if (fmt == 0) return run_fmt<0>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
     if (fmt == 1) return run_fmt<1>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
     return run_fmt<2>(mb, mma, wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);

@@ -20,12 +20,20 @@ int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, 
 // Streamed GEMV (gemv_stream.cu), fmt 0 = Q8_0 planes (wd = the fp16 scale
 // plane), 1 = Q4_K blocks: k a multiple of 512 (Q8_0) or 256 (Q4_K) and
 // 16-byte aligned weights; gemv_stream_fits says whether a call qualifies.
-// Options (the expert FFN's fusions): rows n1 .. n - 1 from a second Q4_K /
-// Q5_K matrix wq2 (its rows 0 ..); fp32 activation rows holding [g | u] (2 k
-// values) whose input is (g * sigmoid(g)) * u; y += alpha * result.
+// Options (the expert FFN's fusions).  nseg > 0: the n = nseg * seg_rows
+// weight rows come from nseg Q4_K / Q5_K matrices seg[s] (row r from matrix
+// r / seg_rows), the CTAs split evenly over the matrices; matrix s's input is
+// the activations offset by s * x_seg elements within each row, rows ldx
+// elements apart (0: the input length).  swiglu: fp32 activation rows hold
+// [g | u] (2 k values) and the input is (g * sigmoid(g)) * u.  y = alpha *
+// result, or with accumulate y += alpha * result.
+constexpr int kGemvMaxSeg = 16;
 struct GemvOpts {
-    const uint8_t* wq2 = nullptr;
-    int64_t n1 = 0;
+    int nseg = 0;
+    const uint8_t* seg[kGemvMaxSeg] = {};
+    int64_t seg_rows = 0;
+    int64_t x_seg = 0;
+    int64_t ldx = 0;
     int swiglu = 0;
     int accumulate = 0;
     float alpha = 1.0f;
@@ -37,11 +45,14 @@ int launch_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t co
 int launch_q5_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols, cudaStream_t s);
 int launch_q5_k_gemv(const void* blocks, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
                      int64_t ldy, cudaStream_t s);
-// The expert FFN (expert.cu): out[m][hidden] (+)= weight * down(SwiGLU(gate x, up x)).
-size_t expert_ffn_workspace_bytes(int64_t m, int64_t hidden, int64_t inter);
-int launch_expert_ffn(const void* w_gate, const void* w_up, const void* w_down, int gate_type, int down_type,
-                      int64_t hidden, int64_t inter, const void* x, int x_dtype, int64_t m, float* out, float weight,
-                      int accumulate, void* workspace, size_t workspace_bytes, cudaStream_t s);
+// The expert FFN (expert.cu): out[m][hidden] (+)= sum_e weight_e * down_e(SwiGLU(gate_e x, up_e x))
+// over n_experts <= kMaxExpertsPerCall experts (one expert: gdn_expert_ffn).
+constexpr int kMaxExpertsPerCall = kGemvMaxSeg / 2;
+size_t experts_ffn_workspace_bytes(int n_experts, int64_t m, int64_t hidden, int64_t inter);
+int launch_experts_ffn(int n_experts, const void* const* w_gate, const void* const* w_up, const void* const* w_down,
+                       int gate_type, int down_type, int64_t hidden, int64_t inter, const void* x, int x_dtype,
+                       int64_t m, const float* weights, float* out, int accumulate, void* workspace,
+                       size_t workspace_bytes, cudaStream_t s);
 int launch_q4_k_gemv(const void* blocks, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
                      int64_t ldy, cudaStream_t s);
 

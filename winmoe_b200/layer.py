@@ -359,6 +359,32 @@ def expert_ffn(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, g
     return out
 
 
+MAX_EXPERTS_PER_CALL = 8
+
+
+def experts_ffn(w_gate: list, w_up: list, w_down: list, gate_type: int, down_type: int, hidden: int, inter: int,
+                x: torch.Tensor, weights=None, out: torch.Tensor | None = None, accumulate: bool = False,
+                workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """The batched expert block of m tokens (gpu_expert_batch_start / _add / _finish):
+    out (+)= sum_e weights[e] * down_e(SwiGLU(gate_e x, up_e x)), summed in expert
+    order, in three launches for up to MAX_EXPERTS_PER_CALL experts."""
+    ne = len(w_gate)
+    if not (len(w_up) == len(w_down) == ne):
+        raise GDNError(-1, "w_gate, w_up and w_down must list the same experts")
+    m = x.shape[0]
+    if out is None:
+        out = torch.zeros((m, hidden), dtype=torch.float32, device=x.device)
+    need = lib().gdn_experts_ffn_workspace_size(ne, m, hidden, inter)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    ptrs = lambda ts: (C.c_void_p * max(ne, 1))(*[t.data_ptr() for t in ts])
+    wts = None if weights is None else (C.c_float * max(ne, 1))(*[float(w) for w in weights])
+    check(lib().gdn_experts_ffn(ne, ptrs(w_gate), ptrs(w_up), ptrs(w_down), gate_type, down_type, hidden, inter,
+                                x.data_ptr(), _act_dtype(x), m, wts, out.data_ptr(), int(accumulate),
+                                workspace.data_ptr(), workspace.numel(), _stream(stream, x.device)))
+    return out
+
+
 # ------------------------------------------------------------------ drop-in mirror
 
 _weight_cache: dict[tuple, DeltaNetWeights] = {}
