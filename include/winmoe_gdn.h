@@ -151,13 +151,15 @@ GDN_API int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64
 
 /* y[m][n] = sum_k x[m][k] * W[n][k], W Q4_K [n_rows][k], fp32 accumulation
  * (q4k_matvec_kernel, engine/runtime/gpu_offload.cu:206-268).  x_dtype F32,
- * BF16 or F16; k % 256 == 0.  fp16 x with m >= 8 runs on the tcgen05 tensor
+ * BF16 or F16; k % 256 == 0.  fp16 x with m >= 32 runs on the tcgen05 tensor
  * cores (superblocks by TMA, dequantised in shared memory into hi + lo fp16
  * operands: the fp32 product of those activations up to summation order);
- * otherwise the streamed GEMV: weight rows by bulk copy, the activations split
- * per 32-block into three int8 levels (error below 5e-7 of the block's
- * max |x|) and the products summed exactly in int32 (dp4a for m <= 2, the
- * int8 tensor cores for m >= 3 when k % 512 == 0), scaled in fp32. */
+ * otherwise the streamed GEMV, weight rows by bulk copy: m <= 2 splits the
+ * activations per 32-block into three int8 levels (error below 5e-7 of the
+ * block's max |x|) summed exactly by dp4a; m >= 3 splits them per 256-element
+ * piece into a power-of-two scale and fp16 hi + lo parts (error about 1e-7 of
+ * the piece's max |x|) against the exact fp16 weights q * sc on the fp16
+ * tensor cores (mma.sync, fp32 accumulation over a superblock). */
 GDN_API int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k,
                   const void* x, int x_dtype, int64_t m, float* y, void* stream);
 

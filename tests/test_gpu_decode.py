@@ -293,11 +293,13 @@ def test_decode_graph_replay_matches_eager(t35, w35, B, dtype):
     assert torch.equal(graphed.conv_pos, eager.conv_pos)
 
 
-def test_decode_q4_k_layer_batched():
-    """A Q4_K layer at B = 16 with bf16 activations: the projections on the tensor
-    cores (fp16 operands, exact weights, split-K out_proj); 3 steps from prefilled states."""
+@pytest.mark.parametrize("B", [16, 32])
+def test_decode_q4_k_layer_batched(B):
+    """A Q4_K layer with bf16 activations, 3 steps from prefilled states: B = 16 on
+    the fp16-MMA GEMV, B = 32 on the tcgen05 GEMM (fp16 operands, exact weights,
+    split-K out_proj)."""
     cfg = DIMS_35B
-    B, steps = 16, 3
+    steps = 3
     t = synth.layer_tensors(cfg, weight_type=12)
     w = L.DeltaNetWeights.upload(cfg, t.in_proj, t.out_proj, t.conv1d_w, t.ssm_a, t.dt_bias, t.head_norm,
                                  weight_type=12, device=DEV)
@@ -308,7 +310,7 @@ def test_decode_q4_k_layer_batched():
     st = L.DeltaNetState.zeros(cfg, B, DEV)
     st.S.copy_(torch.from_numpy(S0))
     outs = [L.decode_step(w, st, xs_t[s].to(DEV).contiguous()).cpu().numpy() for s in range(steps)]
-    for b in (0, 7, 15):
+    for b in (0, 7, B - 1):
         want, S_ref, _, _ = run_oracle(cfg, t, xs_in[:, b], S0=S0[b])
         for s in range(steps):
             assert rel_l2(outs[s][b], want[s]) <= TOL, (b, s, rel_l2(outs[s][b], want[s]))

@@ -59,8 +59,8 @@ def test_q8_0_gemv_fp32(m, n, k):
         assert rel_l2(y[i], want) <= 1e-5, i
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 32])
-@pytest.mark.parametrize("n,k", [(12352, 2048), (2048, 4096), (64, 2048)])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 13, 16, 32])
+@pytest.mark.parametrize("n,k", [(12352, 2048), (2048, 4096), (64, 2048), (300, 256), (200, 768)])
 def test_q4_k_gemv_fp32(m, n, k):
     blocks = synth.q4_k_blocks(n, k, seed=400 + n)
     x = synth.hidden_states(m, k, seed=401)
@@ -108,6 +108,50 @@ def test_gemv_edge_activations(fmt):
     xn[0, 1000] = np.nan  # a NaN activation reaches every output, as through fp32 products
     y = run(torch.from_numpy(xn).to(DEV)).cpu().numpy()[0]
     assert np.isnan(y).all()
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_k", "q5_k"])
+def test_gemv_edge_activations_batched(fmt):
+    """The same edge rows as one 4-row call: the tensor-core batch paths (IMMA for
+    Q8_0; fp16 MMA for the K-quants, whose activations are split per 256-element
+    piece into a power-of-two scale and fp16 hi + lo parts)."""
+    n, k = 2048, 2048
+    x = _edge_activations(k)
+    P = O.port()
+    if fmt == "q8_0":
+        blocks = synth.q8_0_blocks(n, k, seed=502)
+        qs, d = L.q8_0_planes(blocks, n, k, DEV)
+        run = lambda xi: L.gemm_q8_0(qs, d, xi)
+        ty = 8
+    else:
+        gen, ty = (synth.q4_k_blocks, 12) if fmt == "q4_k" else (synth.q5_k_blocks, 13)
+        blocks = gen(n, k, seed=503)
+        dev = torch.from_numpy(blocks.reshape(-1)).to(DEV)
+        run = lambda xi: (L.gemm_q4_k if ty == 12 else L.gemm_q5_k)(dev, n, k, xi)
+    y = run(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    for i in range(x.shape[0]):
+        want = P.quant_matvec(blocks, x[i], n, k, ty, O.ACT_FP32)
+        assert rel_l2(y[i], want) <= 1e-5, i
+    xn = x.copy()
+    xn[3, 1000] = np.nan  # reaches every output of its row only
+    xn[1, 5] = np.inf  # as an inf among fp32 products of either sign: NaN (the rows' other outputs too)
+    y = run(torch.from_numpy(xn).to(DEV)).cpu().numpy()
+    assert np.isnan(y[3]).all() and np.isnan(y[1]).all() and np.isfinite(y[[0, 2]]).all()
+
+
+@pytest.mark.parametrize("xdt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("m", [3, 5])
+def test_q4_k_gemv_half_activations(xdt, m):
+    """fp16 / bf16 activations below the tensor-core GEMM's batch threshold go
+    through the batched GEMV: the fp32 product of the same (rounded) activations."""
+    n, k = 2048, 4096
+    blocks = synth.q4_k_blocks(n, k, seed=510)
+    xh = torch.from_numpy(synth.hidden_states(m, k, seed=511)).to(xdt)
+    y = L.gemm_q4_k(torch.from_numpy(blocks.reshape(-1)).to(DEV), n, k, xh.to(DEV)).cpu().numpy()
+    P = O.port()
+    x32 = xh.float().numpy()
+    for i in range(m):
+        assert rel_l2(y[i], P.quant_matvec(blocks, x32[i], n, k, 12, O.ACT_FP32)) <= 1e-5, i
 
 
 GEMM_SHAPES = [(128, 256, 64), (256, 12352, 2048), (256, 2048, 4096), (200, 300, 2048), (64, 128, 128),
@@ -203,12 +247,12 @@ def test_q8_0_gemm_ref_exact_bit_exact(n, k, m):
 
 
 @pytest.mark.parametrize("m,n,k", [(8, 12352, 2048), (32, 12352, 2048), (32, 2048, 4096), (130, 2048, 4096),
-                                   (8, 100, 256), (64, 300, 768)])
+                                   (40, 100, 256), (64, 300, 768)])
 def test_q4_k_gemm_tensor_core_exact(m, n, k):
-    """fp16 x, m >= 8: Q4_K superblocks dequantised into hi + lo fp16 tensor-core
-    operands = the fp64 product of the same activations and the bit-exact fp32
-    weights up to summation order (incl. ragged n, one superblock, split K); two
-    launches bit-identical."""
+    """fp16 x: from 32 rows Q4_K superblocks dequantised into hi + lo fp16
+    tcgen05 operands (below, the fp16-MMA GEMV) = the fp64 product of the same
+    activations and the bit-exact fp32 weights up to summation order (incl.
+    ragged n, one superblock, split K); two launches bit-identical."""
     blocks = synth.q4_k_blocks(n, k, seed=900 + n + k)
     dev = torch.from_numpy(blocks.reshape(-1)).to(DEV)
     x = torch.randn(m, k, generator=torch.Generator().manual_seed(m + n)).half().to(DEV)

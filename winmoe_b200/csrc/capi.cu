@@ -139,8 +139,10 @@ int gdn_q4_k_dequant(const void* blocks, float* out, int64_t rows, int64_t cols,
     return launch_q4_k_dequant(blocks, out, rows, cols, as_stream(stream));
 }
 
-// Q4_K batches from this many rows (fp16 activations) run on the tensor cores.
-constexpr int64_t kQ4kTcMinRows = 8;
+// Q4_K batches from this many rows (fp16 activations) run on the tcgen05 GEMM;
+// below, the fp16-MMA GEMV is faster (35B in_proj + out_proj at 16 rows: 42
+// against 80 us; about even at 32).
+constexpr int64_t kQ4kTcMinRows = 32;
 
 int gdn_q4_k_gemm(const void* blocks, int64_t n_rows, int64_t k, const void* x, int x_dtype, int64_t m, float* y,
                   void* stream) {

@@ -343,10 +343,10 @@ inline int mark(PhaseEvents* pe, int i, cudaStream_t s) {
 }
 
 // Tensor-core projections pay off once a batch fills an M=128 tile reasonably
-// (Q4_K: from 16 rows; below, the int8-tensor-core GEMV of gemv_stream.cu is
-// faster: 8 rows 42 against 78 us for the 35B layer's projections).
+// (Q4_K: from 32 rows; below, the fp16-MMA GEMV of gemv_stream.cu is faster:
+// the 35B layer's input projection 15 / 21 us at 8 / 16 rows against 29 us).
 constexpr int64_t kTcMinBatch = 64;
-constexpr int64_t kTcMinBatchQ4k = 16;
+constexpr int64_t kTcMinBatchQ4k = 32;
 // Split-K factor of the tensor-core out_proj (K = inner is long, N = hidden short).
 constexpr int kOutSplits = 8;
 // Split-K factor of the 2 Hv gate rows' exact tensor-core GEMM (one column tile).

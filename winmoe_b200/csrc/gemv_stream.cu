@@ -385,10 +385,10 @@ __device__ __forceinline__ void produce(const Ring& R, int64_t nst, Issue issue,
     bool xfree = R.nx == 0;
     for (int64_t i = 0; i < nst; i++) {
         if (i >= R.slots) {  // the stage that used this slot has been read by every consumer
-            if (!mbar_wait(smem_u32(R.empty + slot), phase ^ 1u, err)) break;
+            if (!mbar_wait_sleep(smem_u32(R.empty + slot), phase ^ 1u, err)) break;
             fence_proxy_async_smem();
         } else if (!xfree && slot >= R.slots - R.nx) {  // the slot still holds the activations
-            if (!mbar_wait(smem_u32(R.xdone), 0, err)) break;
+            if (!mbar_wait_sleep(smem_u32(R.xdone), 0, err)) break;
             xfree = true;
             fence_proxy_async_smem();
         }
@@ -403,9 +403,9 @@ __device__ __forceinline__ void produce(const Ring& R, int64_t nst, Issue issue,
     for (int64_t q = 0; q < min((int64_t)R.slots, issued); q++) {
         slot = slot == 0 ? R.slots - 1 : slot - 1;
         if (slot == R.slots - 1) phase ^= 1u;
-        mbar_wait(smem_u32(R.full + slot), phase, err);
+        mbar_wait_sleep(smem_u32(R.full + slot), phase, err);
     }
-    if (R.nx > 0) mbar_wait(smem_u32(R.xbar), 0, err);
+    if (R.nx > 0) mbar_wait_sleep(smem_u32(R.xbar), 0, err);
 }
 
 // Consumers: the activations into level planes, then named barrier 2 (every
@@ -419,7 +419,7 @@ __device__ __forceinline__ bool consume_activations(const Ring& R, const void* x
                                                     int swiglu, uint32_t* err) {
     bool ok = true;
     if (R.nx > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(R.xbar), 0, err));
+        ok = __all_sync(0xffffffffu, mbar_wait_sleep(smem_u32(R.xbar), 0, err));
         if (ok)
             stage_rows<FMT, PADDED, true, kSmemBatch>(xs, x_dtype, swiglu ? 2 * k : k, 0, mb, rows, k, warp, lane,
                                                       xq, pl, sx, x16, swiglu);
@@ -538,7 +538,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     int slot = 0;
     uint32_t phase = 0;
     for (int64_t i = 0; i < nst; i++) {
-        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(R.full + slot), phase, err))) break;
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(smem_u32(R.full + slot), phase, err))) break;
         const int64_t r = r0 + i * kStageRows + warp;
         if (r < r1) {
             const uint8_t* stage = ring + (size_t)slot * stage_bytes;
@@ -607,10 +607,10 @@ __host__ __device__ constexpr int64_t mma_row_len(int fmt, int64_t k) {
 __host__ __device__ constexpr size_t mma_stage_bytes(int fmt, int64_t k) {
     return (size_t)kStageRows * mma_row_len(fmt, k) + (fmt == 0 ? (size_t)kStageRows * (k / 16) : 0);
 }
-// activation planes, block scales, (Q4_K) 16-sums, and the two reduction buffers
-__host__ __device__ constexpr size_t mma_fixed_bytes(int fmt, int mt, int64_t k) {
+// activation planes, block scales and the two reduction buffers (Q8_0)
+__host__ __device__ constexpr size_t mma_fixed_bytes(int mt, int64_t k) {
     return (size_t)(4 * mt) * 3 * mma_plane_len(k) + (size_t)(4 * mt) * (k / 32) * 4 +
-           (fmt != 0 ? (size_t)(4 * mt) * (k / 16) * 4 : 0) + (size_t)2 * kWarps * 2 * mt * 32 * 4;
+           (size_t)2 * kWarps * 2 * mt * 32 * 4;
 }
 
 template <int FMT, int MT>
@@ -618,6 +618,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     gemv_mma_kernel(const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wd, int64_t n, int64_t k,
                     const void* x, int x_dtype, int64_t m, float* __restrict__ y, int64_t ldy, int slots, int nx,
                     GemvOpts o, uint32_t* __restrict__ err) {
+    static_assert(FMT == 0, "Q8_0 only: the K-quants take gemv_hmma_kernel");
     constexpr int MB = 4 * MT;
     pdl_trigger();
     extern __shared__ __align__(128) uint8_t smem[];
@@ -630,9 +631,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const Ring R = ring_of(smem, slots, nx);
     int8_t* xq = reinterpret_cast<int8_t*>(smem + kBarBytes);             // [MB][3][plm]
     float* sx = reinterpret_cast<float*>(xq + (size_t)MB * 3 * plm);     // [MB][nblk]
-    float* x16 = sx + MB * nblk;                                         // Q4_K: [MB][2 nblk]
-    float* red = x16 + (FMT != 0 ? MB * 2 * nblk : 0);                   // [2][kWarps][2][MT][32]
-    uint8_t* ring = smem + kBarBytes + mma_fixed_bytes(FMT, MT, k);
+    float* red = sx + MB * nblk;                                         // [2][kWarps][2][MT][32]
+    uint8_t* ring = smem + kBarBytes + mma_fixed_bytes(MT, k);
     const size_t stage_bytes = mma_stage_bytes(FMT, k);
     const size_t scale_off = (size_t)kStageRows * rl;
 
@@ -671,8 +671,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const void* xe = static_cast<const char*>(x) + (size_t)sg * o.x_seg * esize;  // this CTA's matrix's input
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)  // rows past mb are staged as zeros (their outputs are not stored)
-        consume_activations<FMT, false>(R, xe, x_dtype, ldx, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx, x16,
-                                        o.swiglu, err);
+        consume_activations<FMT, false>(R, xe, x_dtype, ldx, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx,
+                                        nullptr, o.swiglu, err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);
@@ -689,7 +689,6 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const int lp = l == 3 ? 0 : l;
     const int8_t* arow[MT][2];
     const float* srow[MT][2];
-    const float* mrow[MT][2];  // Q4_K: the 16-sums of the row (level-0 rows only; else unused)
 #pragma unroll
     for (int mt = 0; mt < MT; mt++)
 #pragma unroll
@@ -697,9 +696,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             const int j = 4 * mt + jj0 + 2 * h;
             arow[mt][h] = xq + ((size_t)j * 3 + lp) * plm + 4 * qq;
             srow[mt][h] = sx + j * nblk;
-            mrow[mt][h] = x16 + j * 2 * nblk;
         }
-    const float mf = l == 0 ? 1.0f : 0.0f;  // the min term enters through level 0 only
     // The consumers meet at a named barrier every stage, so none may leave the
     // loop alone: a warp whose wait gave up (the error word is set) stops
     // waiting and computing but keeps arriving, so that every warp ends.
@@ -707,7 +704,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     int slot = 0;
     uint32_t phase = 0;
     for (int64_t i = 0; i < nst; i++) {
-        if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait(smem_u32(R.full + slot), phase, err));
+        if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait_sleep(smem_u32(R.full + slot), phase, err));
         const uint8_t* stage = ring + (size_t)slot * stage_bytes;
         const uint16_t* dsc = reinterpret_cast<const uint16_t*>(stage + scale_off);
         float acc[2][MT][4];
@@ -717,100 +714,38 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
             for (int mt = 0; mt < MT; mt++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) acc[g][mt][e] = 0.0f;
-        if (FMT == 0) {
 #pragma unroll 2
-            for (int kb = bad ? nblk : warp; kb < nblk; kb += kWarps) {
-                uint32_t a[MT][4];
-                float f[MT][2];
+        for (int kb = bad ? nblk : warp; kb < nblk; kb += kWarps) {
+            uint32_t a[MT][4];
+            float f[MT][2];
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) {
+                a[mt][0] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb);
+                a[mt][1] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb);
+                a[mt][2] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb + 16);
+                a[mt][3] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb + 16);
+                f[mt][0] = srow[mt][0][kb] * lf;
+                f[mt][1] = srow[mt][1][kb] * lf;
+            }
+#pragma unroll
+            for (int g = 0; g < 2; g++) {
+                const uint8_t* brow = stage + (size_t)(8 * g + gq) * rl + 32 * kb + 4 * qq;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(brow + 16);
+                const float d0 = fp16_bits_to_float(dsc[(8 * g + 2 * qq) * nblk + kb]);
+                const float d1 = fp16_bits_to_float(dsc[(8 * g + 2 * qq + 1) * nblk + kb]);
 #pragma unroll
                 for (int mt = 0; mt < MT; mt++) {
-                    a[mt][0] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb);
-                    a[mt][1] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb);
-                    a[mt][2] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb + 16);
-                    a[mt][3] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb + 16);
-                    f[mt][0] = srow[mt][0][kb] * lf;
-                    f[mt][1] = srow[mt][1][kb] * lf;
-                }
-#pragma unroll
-                for (int g = 0; g < 2; g++) {
-                    const uint8_t* brow = stage + (size_t)(8 * g + gq) * rl + 32 * kb + 4 * qq;
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow);
-                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(brow + 16);
-                    const float d0 = fp16_bits_to_float(dsc[(8 * g + 2 * qq) * nblk + kb]);
-                    const float d1 = fp16_bits_to_float(dsc[(8 * g + 2 * qq + 1) * nblk + kb]);
-#pragma unroll
-                    for (int mt = 0; mt < MT; mt++) {
-                        int c[4];
-                        imma_16832(c, a[mt], b0, b1);
-                        acc[g][mt][0] = fmaf((float)c[0], f[mt][0] * d0, acc[g][mt][0]);
-                        acc[g][mt][1] = fmaf((float)c[1], f[mt][0] * d1, acc[g][mt][1]);
-                        acc[g][mt][2] = fmaf((float)c[2], f[mt][1] * d0, acc[g][mt][2]);
-                        acc[g][mt][3] = fmaf((float)c[3], f[mt][1] * d1, acc[g][mt][3]);
-                    }
-                }
-            }
-        } else {
-            // Q4_K: warp w takes the sub-block pairs (superblock sb, group cg)
-            // w, w + 16, ...: sub-blocks 2 cg (low nibbles of quant bytes
-            // 32 cg ..) and 2 cg + 1 (their high nibbles), k blocks 8 sb + 2 cg, + 1
-            const int npair = nblk >> 1;
-            for (int pi = bad ? npair : warp; pi < npair; pi += kWarps) {
-                const int sb = pi >> 2, cg = pi & 3;
-#pragma unroll
-                for (int half = 0; half < 2; half++) {
-                    const int kb = 8 * sb + 2 * cg + half;
-                    uint32_t a[MT][4];
-                    float f[MT][2], gm[MT][2];
-#pragma unroll
-                    for (int mt = 0; mt < MT; mt++) {
-                        a[mt][0] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb);
-                        a[mt][1] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb);
-                        a[mt][2] = *reinterpret_cast<const uint32_t*>(arow[mt][0] + 32 * kb + 16);
-                        a[mt][3] = *reinterpret_cast<const uint32_t*>(arow[mt][1] + 32 * kb + 16);
-                        f[mt][0] = srow[mt][0][kb] * lf;
-                        f[mt][1] = srow[mt][1][kb] * lf;
-                        gm[mt][0] = (mrow[mt][0][2 * kb] + mrow[mt][0][2 * kb + 1]) * mf;
-                        gm[mt][1] = (mrow[mt][1][2 * kb] + mrow[mt][1][2 * kb + 1]) * mf;
-                    }
-#pragma unroll
-                    for (int g = 0; g < 2; g++) {
-                        constexpr int kSb = FMT == 2 ? 176 : 144, kQs = FMT == 2 ? 48 : 16;
-                        const uint8_t* blk = stage + (size_t)(8 * g + gq) * rl + sb * kSb;
-                        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(blk + kQs + 32 * cg + 4 * qq);
-                        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(blk + kQs + 16 + 32 * cg + 4 * qq);
-                        uint32_t b0 = (w0 >> (4 * half)) & 0x0F0F0F0Fu;
-                        uint32_t b1 = (w1 >> (4 * half)) & 0x0F0F0F0Fu;
-                        if (FMT == 2) {  // the fifth bits: bit 2 cg + half of qh[4 qq ..] and qh[16 + 4 qq ..]
-                            const uint32_t h0 = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * qq);
-                            const uint32_t h1 = *reinterpret_cast<const uint32_t*>(blk + 32 + 4 * qq);
-                            b0 |= ((h0 >> (2 * cg + half)) & 0x01010101u) << 4;
-                            b1 |= ((h1 >> (2 * cg + half)) & 0x01010101u) << 4;
-                        }
-                        float ds[2], dm[2];  // d sc and dmin m of this thread's two columns (weight rows)
-#pragma unroll
-                        for (int e = 0; e < 2; e++) {
-                            const uint8_t* hb = stage + (size_t)(8 * g + 2 * qq + e) * rl + sb * kSb;
-                            const uint32_t dd = *reinterpret_cast<const uint32_t*>(hb);
-                            int sc, mn;
-                            scale_min(2 * cg + half, hb + 4, sc, mn);
-                            ds[e] = fp16_bits_to_float((uint16_t)(dd & 0xFFFFu)) * (float)sc;
-                            dm[e] = fp16_bits_to_float((uint16_t)(dd >> 16)) * (float)mn;
-                        }
-#pragma unroll
-                        for (int mt = 0; mt < MT; mt++) {
-                            int c[4];
-                            imma_16832(c, a[mt], b0, b1);
-#pragma unroll
-                            for (int e = 0; e < 4; e++) {
-                                const int h = e >> 1, col = e & 1;
-                                acc[g][mt][e] = fmaf((float)c[e], f[mt][h] * ds[col], acc[g][mt][e]);
-                                acc[g][mt][e] = fmaf(-gm[mt][h], dm[col], acc[g][mt][e]);
-                            }
-                        }
-                    }
+                    int c[4];
+                    imma_16832(c, a[mt], b0, b1);
+                    acc[g][mt][0] = fmaf((float)c[0], f[mt][0] * d0, acc[g][mt][0]);
+                    acc[g][mt][1] = fmaf((float)c[1], f[mt][0] * d1, acc[g][mt][1]);
+                    acc[g][mt][2] = fmaf((float)c[2], f[mt][1] * d0, acc[g][mt][2]);
+                    acc[g][mt][3] = fmaf((float)c[3], f[mt][1] * d1, acc[g][mt][3]);
                 }
             }
         }
+
         __syncwarp();  // every lane has read the stage
         if (lane == 0) mbar_arrive(smem_u32(R.empty + slot));
         // sum over the levels (lanes 4 gq + qq with gq's low two bits = l), then
@@ -861,6 +796,547 @@ int run_mma(const void* wq, const void* wd, int64_t n, int64_t k, const void* x,
                       gemv_mma_kernel<FMT, MT>, grid,
                       dim3((kWarps + 1) * 32), smem, s,
                       static_cast<const uint8_t*>(wq), static_cast<const uint8_t*>(wd), n, k, x, dt, m, y, ldy,
+                      slots, nx, o, device_error_word());
+}
+
+// ------------------------------------------------- Q4_K / Q5_K on fp16 MMA
+//
+// A K-quant weight is d sc q - dmin m with integers q < 32 and sc, m < 64, so
+// q sc (< 2048) is exact in fp16.  Each activation row's 256-element piece (one
+// superblock's columns) is scaled by a power of two 2^E that brings its max |x|
+// into [2^14, 2^15) and split into two fp16 parts, x 2^E = hi + lo (22
+// significant bits; the sum of the parts is x 2^E to within 2^-25 of the
+// piece's scaled max).  One mma.sync m16n8k16 takes A = the hi parts of 8
+// activation rows (A rows 0-7) and their lo parts (rows 8-15), B = q sc of 8
+// weight rows, and its fp32 accumulators sum a whole superblock, so that the
+// only per-superblock work left is (C_hi + C_lo) d 2^-E per output.  The min
+// term dmin sum_s m_s X_s (X_s the fp32 sum of sub-block s's activations) is
+// one more mma per superblock: A = the eight X_s 2^(E-5) as hi + lo, B = the
+// eight m_s.  The k order inside an mma is free: k slots 2 t, 2 t + 1, 2 t + 8,
+// 2 t + 9 of lane group t hold elements 4 t .. 4 t + 3 of the 16-element run,
+// so that both operands are plain 4-element loads.  The 16 consumer warps
+// split a stage into (n-tile, superblock, sub-block range) units and add their
+// partial sums through shared memory as the IMMA kernel does.
+
+__host__ __device__ constexpr int64_t h_plane(int64_t k) { return 2 * k + 32; }      // fp16 row, 32 (mod 128) B
+__host__ __device__ constexpr int64_t h_sums(int64_t k) { return 16 * (k >> 8) + 16; }  // 8 fp16 per superblock
+// floats per warp, [mt][16][8] + 8: the warps a reducing thread reads are 8 banks apart
+__host__ __device__ constexpr int h_red_stride(int mt) { return 128 * mt + 8; }
+// hi and lo planes, hi and lo sub-block sums, the 2^-E factors, the two reduction buffers
+__host__ __device__ constexpr size_t hmma_fixed_bytes(int mt, int64_t k) {
+    return (size_t)(8 * mt) * (2 * h_plane(k) + 2 * h_sums(k) + 4 * (k >> 8)) +
+           (size_t)2 * kWarps * h_red_stride(mt) * 4;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {  // lo -> bits 0-15
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ void unpack_h2(uint32_t h, float& lo, float& hi) {
+    asm("{.reg .f16 a, b;\n mov.b32 {a, b}, %2;\n cvt.f32.f16 %0, a;\n cvt.f32.f16 %1, b;}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(h));
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ void hmma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+
+constexpr uint32_t kH2Magic = 0x64006400u;  // fp16 1024 in both halves: 0x6400 | i = 1024 + i for i < 1024
+
+// Integer bytes b (< 1024) of w at the byte positions of selector sel (two
+// bytes) as an exact fp16 pair.
+__device__ __forceinline__ uint32_t bytes_h2(uint32_t w, uint32_t sel) {
+    return hsub2(__byte_perm(w, 0, sel) | kH2Magic, kH2Magic);
+}
+
+// The staged activations of one CTA row of the grid.
+struct HPlanes {
+    uint8_t* hi;   // [MB][h_plane] fp16 hi parts
+    uint8_t* lo;   // [MB][h_plane] fp16 lo parts
+    uint8_t* shi;  // [MB][h_sums] sub-block sums 2^(E-5), hi parts
+    uint8_t* slo;  // [MB][h_sums] lo parts
+    float* sc;     // [MB][k / 256] 2^-E (NaN when the piece holds an inf or NaN)
+    int64_t P, SS;
+    int nsb;
+};
+
+// One warp stages piece c (256 elements, one superblock's columns) of
+// activation row j: lane l holds elements 8 l .. 8 l + 7 (sub-block l / 4).
+__device__ __forceinline__ void stage_256(const float (&v)[8], bool valid, const HPlanes& h, int j, int c,
+                                          int lane) {
+    // max |x| of the piece as an integer max of the magnitude bits (a NaN wins)
+    uint32_t ab = max(max(max(__float_as_uint(v[0]) & 0x7fffffffu, __float_as_uint(v[1]) & 0x7fffffffu),
+                          max(__float_as_uint(v[2]) & 0x7fffffffu, __float_as_uint(v[3]) & 0x7fffffffu)),
+                      max(max(__float_as_uint(v[4]) & 0x7fffffffu, __float_as_uint(v[5]) & 0x7fffffffu),
+                          max(__float_as_uint(v[6]) & 0x7fffffffu, __float_as_uint(v[7]) & 0x7fffffffu)));
+    ab = __reduce_max_sync(0xffffffffu, ab);
+    // 2^E = p1 p2 (each a normal power of two; p2 = 1 unless E > 127) and
+    // s = 2^-E (subnormal for E > 126); all warp-uniform
+    float p1 = 1.0f, p2 = 1.0f, s = 0.0f;
+    if (ab >= 0x7f800000u) {
+        s = __uint_as_float(0x7fc00000u);  // an inf or NaN: every output of the row becomes NaN
+    } else if (ab != 0) {
+        const int E = 141 - (int)(ab >> 23);  // max 2^E in [2^14, 2^15); E in [-113, 141]
+        const int e1 = min(E, 127), e2 = E - e1;
+        p1 = __int_as_float((e1 + 127) << 23);
+        p2 = __int_as_float((e2 + 127) << 23);
+        s = E <= 126 ? __int_as_float((127 - E) << 23) : __int_as_float(1 << (149 - E));
+    }
+    float xs[8];
+    if (p2 == 1.0f) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) xs[e] = v[e] * p1;  // exact: a power of two, no overflow
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) xs[e] = (v[e] * p1) * p2;
+    }
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        const uint32_t hh = pack_h2(xs[e], xs[e + 1]);
+        float ha, hb;
+        unpack_h2(hh, ha, hb);
+        hw[e >> 1] = hh;
+        lw[e >> 1] = pack_h2(xs[e] - ha, xs[e + 1] - hb);  // the differences are exact in fp32
+    }
+    float t = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    t += __shfl_xor_sync(0xffffffffu, t, 1);  // the sub-block's 32 activations
+    t += __shfl_xor_sync(0xffffffffu, t, 2);
+    const float ts = (t * p1) * (p2 * 0.03125f);  // X 2^(E-5), |.| < 2^15
+    const uint32_t th = pack_h2(ts, 0.0f);
+    float thf, unused;
+    unpack_h2(th, thf, unused);
+    const uint32_t tl = pack_h2(ts - thf, 0.0f);
+    if (valid) {
+        const size_t off = (size_t)j * h.P + 512 * c + 16 * lane;
+        *reinterpret_cast<uint4*>(h.hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(h.lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        if ((lane & 3) == 0) {
+            const size_t so = (size_t)j * h.SS + 16 * c + 2 * (lane >> 2);
+            *reinterpret_cast<uint16_t*>(h.shi + so) = (uint16_t)(th & 0xFFFFu);
+            *reinterpret_cast<uint16_t*>(h.slo + so) = (uint16_t)(tl & 0xFFFFu);
+        }
+        if (lane == 0) h.sc[j * h.nsb + c] = s;
+    }
+}
+
+// stage_rows for the fp16 planes: the 256-element pieces of all rows form one
+// list, warp w takes pieces w, w + kWarps, ..., U at a time.
+template <bool SMEM, int U>
+__device__ __forceinline__ void stage_f16_rows(const void* x, int x_dtype, int64_t ldx, int64_t m0, int mb, int rows,
+                                               int64_t k, int warp, int lane, const HPlanes& h, int swiglu) {
+    const int npc = h.nsb;
+    const size_t es = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
+    const char* x0 = static_cast<const char*>(x) + (SMEM ? 0 : (size_t)m0 * ldx * es);
+    const bool vec = x_dtype == GDN_DTYPE_F32 && (reinterpret_cast<uintptr_t>(x0) & 15) == 0 &&
+                     ((size_t)ldx * 4) % 16 == 0;
+    bool announced = SMEM;
+    int j = 0, c = warp;
+    while (c >= npc && j < rows) {
+        c -= npc;
+        j++;
+    }
+    while (j < rows) {
+        float v[U][8];
+        int ju[U], cu[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            ju[u] = j;
+            cu[u] = c;
+            const int64_t e = 256 * (int64_t)c + 8 * lane;
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[u][i] = 0.0f;
+            if (j < rows && j < mb) {
+                const char* xr = x0 + (size_t)j * ldx * es;
+                if (swiglu) {  // fp32 [g | u]: (g * sigmoid(g)) * u, as the reference's swiglu_kernel
+#pragma unroll
+                    for (int q = 0; q < 2; q++) {
+                        const float4 gv = *reinterpret_cast<const float4*>(xr + (size_t)(e + 4 * q) * 4);
+                        const float4 uv = *reinterpret_cast<const float4*>(xr + (size_t)(k + e + 4 * q) * 4);
+                        v[u][4 * q + 0] = (gv.x * (1.0f / (1.0f + expf(-gv.x)))) * uv.x;
+                        v[u][4 * q + 1] = (gv.y * (1.0f / (1.0f + expf(-gv.y)))) * uv.y;
+                        v[u][4 * q + 2] = (gv.z * (1.0f / (1.0f + expf(-gv.z)))) * uv.z;
+                        v[u][4 * q + 3] = (gv.w * (1.0f / (1.0f + expf(-gv.w)))) * uv.w;
+                    }
+                } else if (vec) {
+                    const float4 a = *reinterpret_cast<const float4*>(xr + (size_t)e * 4);
+                    const float4 b = *reinterpret_cast<const float4*>(xr + (size_t)(e + 4) * 4);
+                    v[u][0] = a.x, v[u][1] = a.y, v[u][2] = a.z, v[u][3] = a.w;
+                    v[u][4] = b.x, v[u][5] = b.y, v[u][6] = b.z, v[u][7] = b.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[u][i] = load_act(xr, x_dtype, (size_t)e + i);
+                }
+            }
+            c += kWarps;
+            while (c >= npc && j < rows) {
+                c -= npc;
+                j++;
+            }
+        }
+        if (!announced) {
+            bar_arrive(1, (kWarps + 1) * 32);
+            announced = true;
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const bool valid = ju[u] < rows;
+            stage_256(v[u], valid, h, valid ? ju[u] : 0, valid ? cu[u] : 0, lane);
+        }
+    }
+    if (!announced) bar_arrive(1, (kWarps + 1) * 32);
+}
+
+// consume_activations for the fp16 planes.
+__device__ __forceinline__ bool consume_activations_f16(const Ring& R, const void* x, int x_dtype, int64_t ldx,
+                                                        const uint8_t* xs, int64_t m0, int mb, int rows, int64_t k,
+                                                        int warp, int lane, const HPlanes& h, int swiglu,
+                                                        uint32_t* err) {
+    bool ok = true;
+    if (R.nx > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait_sleep(smem_u32(R.xbar), 0, err));
+        if (ok)
+            stage_f16_rows<true, kSmemBatch>(xs, x_dtype, swiglu ? 2 * k : k, 0, mb, rows, k, warp, lane, h, swiglu);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(R.xdone));
+    } else {
+        stage_f16_rows<false, kStageBatch>(x, x_dtype, ldx, m0, mb, rows, k, warp, lane, h, swiglu);
+    }
+    bar_sync(2, kWarps * 32);
+    return ok;
+}
+
+// q sc of sub-blocks 2 cg (low nibbles: rows' A registers 0-3 of `lo`) and 2 cg
+// + 1 (high nibbles: `hi`) for the 4 elements of each of this lane's two weight
+// rows (gq: word w0, gq + 8: w1) in one 16-element chunk, as the A fragment
+// (row gq, k slots 2 qq ..), (gq + 8, 2 qq ..), (gq, 2 qq + 8 ..), (gq + 8, 2 qq + 8 ..).
+template <int FMT>
+__device__ __forceinline__ void k_quant_a(uint32_t w0, uint32_t w1, uint32_t hw0, uint32_t hw1, int cg,
+                                          const uint32_t (&SA)[2], const uint32_t (&NA)[2], const uint32_t (&SB)[2],
+                                          const uint32_t (&NB)[2], uint32_t (&lo)[4], uint32_t (&hi)[4]) {
+    const uint32_t w[2] = {w0, w1}, hw[2] = {hw0, hw1};
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const uint32_t t01 = __byte_perm(w[r], 0, 0x4140), t23 = __byte_perm(w[r], 0, 0x4342);
+        uint32_t vl0 = (t01 & 0x000F000Fu) | kH2Magic, vl1 = (t23 & 0x000F000Fu) | kH2Magic;
+        uint32_t vh0 = (t01 & 0x00F000F0u) | kH2Magic, vh1 = (t23 & 0x00F000F0u) | kH2Magic;
+        if (FMT == 2) {  // fifth bits: bit 2 cg (low) and 2 cg + 1 (high) of each qh byte
+            const uint32_t h01 = __byte_perm(hw[r], 0, 0x4140), h23 = __byte_perm(hw[r], 0, 0x4342);
+            vl0 |= ((h01 >> (2 * cg)) & 0x00010001u) << 4;
+            vl1 |= ((h23 >> (2 * cg)) & 0x00010001u) << 4;
+            vh0 |= ((h01 >> (2 * cg + 1)) & 0x00010001u) << 8;
+            vh1 |= ((h23 >> (2 * cg + 1)) & 0x00010001u) << 8;
+        }
+        // (1024 + q) sc - 1024 sc and (1024 + 16 q) sc / 16 - 64 sc: q sc, exact
+        lo[r] = hfma2(vl0, SA[r], NA[r]);
+        lo[2 + r] = hfma2(vl1, SA[r], NA[r]);
+        hi[r] = hfma2(vh0, SB[r], NB[r]);
+        hi[2 + r] = hfma2(vh1, SB[r], NB[r]);
+    }
+}
+
+// Sub-block pair cg of a unit: the two 16-element chunks of sub-blocks 2 cg and
+// 2 cg + 1 of the stage's 16 weight rows (A) against every m-tile of
+// activations (B: hi parts, then lo parts, into the same accumulators).  blk0
+// / blk1 are this lane's rows' superblock in the stage, sc_lo / sc_hi their
+// eight 6-bit scales, one per byte.
+template <int FMT, int MT>
+__device__ __forceinline__ void hmma_pair(int cg, uint32_t blk0, uint32_t blk1, const uint32_t (&sc_lo)[2],
+                                          const uint32_t (&sc_hi)[2], int qq, uint32_t sbo, const uint32_t (&hrow)[MT],
+                                          const uint32_t (&lrow)[MT], float (&C)[MT][4]) {
+    constexpr int kQs = FMT == 2 ? 48 : 16;
+    const uint32_t bl = (uint32_t)(2 * cg) & 3u;  // byte of sub-block 2 cg; 2 cg + 1 is the next
+    uint32_t SA[2], NA[2], SB[2], NB[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const uint32_t scw = cg < 2 ? sc_lo[r] : sc_hi[r];
+        SA[r] = bytes_h2(scw, 0x4040u | bl | (bl << 8));
+        const uint32_t sb1 = bytes_h2(scw, 0x4040u | (bl + 1) | ((bl + 1) << 8));
+        NA[r] = hmul2(SA[r], 0xE400E400u);   // -1024 sc
+        SB[r] = hmul2(sb1, 0x2C002C00u);     // sc / 16
+        NB[r] = hmul2(sb1, 0xD400D400u);     // -64 sc
+    }
+#pragma unroll
+    for (int ch = 0; ch < 2; ch++) {
+        // quant bytes 32 cg + 16 ch + 4 qq ..: low nibbles = elements of sub-block
+        // 2 cg, high nibbles = the same elements of 2 cg + 1
+        const uint32_t qo = kQs + 32 * cg + 16 * ch;  // blk0 / blk1 include 4 qq
+        const uint32_t w0 = lds32(blk0 + qo), w1 = lds32(blk1 + qo);
+        uint32_t hw0 = 0, hw1 = 0;
+        if (FMT == 2) {
+            hw0 = lds32(blk0 + 16 + 16 * ch);
+            hw1 = lds32(blk1 + 16 + 16 * ch);
+        }
+        uint32_t alo[4], ahi[4];
+        k_quant_a<FMT>(w0, w1, hw0, hw1, cg, SA, NA, SB, NB, alo, ahi);
+        const uint32_t eo = sbo + 2 * (64 * cg + 16 * ch);  // byte offset of the chunk of sub-block 2 cg
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) {
+            const uint2 h0 = lds64(hrow[mt] + eo), l0 = lds64(lrow[mt] + eo);
+            const uint2 h1 = lds64(hrow[mt] + eo + 64), l1 = lds64(lrow[mt] + eo + 64);
+            hmma_16816(C[mt], alo, h0.x, h0.y);
+            hmma_16816(C[mt], alo, l0.x, l0.y);
+            hmma_16816(C[mt], ahi, h1.x, h1.y);
+            hmma_16816(C[mt], ahi, l1.x, l1.y);
+        }
+    }
+}
+
+// FMT 1: Q4_K, 2: Q5_K; 8 MT activation rows per CTA row of the grid.
+template <int FMT, int MT>
+__global__ void __launch_bounds__((kWarps + 1) * 32, 1)
+    gemv_hmma_kernel(const uint8_t* __restrict__ wq, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,
+                     float* __restrict__ y, int64_t ldy, int slots, int nx, GemvOpts o, uint32_t* __restrict__ err) {
+    static_assert(FMT == 1 || FMT == 2, "K-quants only");
+    static_assert(MT == 1 || MT == 2, "one or two m-tiles");
+    constexpr int MB = 8 * MT;
+    constexpr int kSb = FMT == 2 ? 176 : 144;
+    constexpr int RW = h_red_stride(MT);
+    pdl_trigger();
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, qq = lane & 3;
+    const int nsb = (int)(k >> 8);
+    const int64_t rl = mma_row_len(FMT, k);
+    const uint32_t qbytes = (uint32_t)row_qbytes(FMT, k);
+    const Ring R = ring_of(smem, slots, nx);
+    HPlanes hp;
+    hp.P = h_plane(k);
+    hp.SS = h_sums(k);
+    hp.nsb = nsb;
+    hp.hi = smem + kBarBytes;
+    hp.lo = hp.hi + MB * hp.P;
+    hp.shi = hp.lo + MB * hp.P;
+    hp.slo = hp.shi + MB * hp.SS;
+    hp.sc = reinterpret_cast<float*>(hp.slo + MB * hp.SS);
+    float* red = hp.sc + MB * nsb;  // [2][kWarps][RW]
+    uint8_t* ring = smem + kBarBytes + hmma_fixed_bytes(MT, k);
+    const size_t stage_bytes = mma_stage_bytes(FMT, k);
+
+    int64_t r0, r1, rb;  // this CTA's rows [r0, r1); row r is row r - rb of matrix wb
+    const uint8_t* wb;
+    int sg;
+    row_range(n, o, r0, r1, wb, rb, sg, wq);
+    const int64_t nst = (r1 - r0 + kStageRows - 1) / kStageRows;
+    auto issue = [&](int64_t i, int slot) {  // producer lane 0: stage i into `slot`
+        const int64_t ra = r0 + i * kStageRows;
+        const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
+        const uint32_t bar = smem_u32(R.full + slot);
+        const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
+        mbar_arrive_expect_tx(bar, rows * qbytes);
+        for (uint32_t r = 0; r < rows; r++)
+            bulk_load(dst + r * (uint32_t)rl, wb + (ra - rb + r) * (int64_t)qbytes, qbytes, bar);
+    };
+    if (warp == kWarps && lane == 0) {
+        ring_init(R);
+        for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {  // the weights never come from an earlier kernel
+            const int64_t ra = r0 + i * kStageRows;
+            const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
+            bulk_prefetch_l2(wb + (ra - rb) * (int64_t)qbytes, rows * qbytes);
+        }
+    }
+    __syncthreads();  // the barriers are initialised
+
+    pdl_wait();
+    const int64_t m0 = (int64_t)blockIdx.y * MB;
+    const int mb = (int)min((int64_t)MB, m - m0);
+    const size_t esize = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
+    const int64_t xrow = o.swiglu ? 2 * k : k;  // activation elements per row read
+    const int64_t ldx = o.ldx ? o.ldx : xrow;   // ... and between rows in memory
+    const void* xe = static_cast<const char*>(x) + (size_t)sg * o.x_seg * esize;  // this CTA's matrix's input
+    const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
+    if (warp < kWarps)  // rows past mb are not staged: their A rows only reach outputs that are not stored
+        consume_activations_f16(R, xe, x_dtype, ldx, xs, m0, mb, mb, k, warp, lane, hp, o.swiglu, err);
+
+    if (warp == kWarps) {  // producer
+        if (nx == 0) bar_sync(1, (kWarps + 1) * 32);
+        if (lane == 0)
+            produce(R, nst, issue, static_cast<const uint8_t*>(xe) + (size_t)m0 * ldx * esize, mb,
+                    (uint32_t)((size_t)xrow * esize), (size_t)ldx * esize, xs, err);
+        return;
+    }
+
+    // Units of a stage: (superblock sb, part p of np = 2^lnp: sub-block pairs
+    // [4 p / np, 4 (p + 1) / np)) of all 16 weight rows; np grows for short
+    // rows so that the 16 warps have work.  Warp w takes units w, w + 16, ...
+    const int lnp = nsb >= 16 ? 0 : nsb >= 8 ? 1 : 2;
+    const int nu = nsb << lnp;
+    // shared-memory addresses: this lane's activation fragments, sums, factors
+    uint32_t hrow[MT], lrow[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+        hrow[mt] = smem_u32(hp.hi) + (uint32_t)((8 * mt + gq) * hp.P + 8 * qq);
+        lrow[mt] = smem_u32(hp.lo) + (uint32_t)((8 * mt + gq) * hp.P + 8 * qq);
+    }
+    const uint32_t shi_s = smem_u32(hp.shi), slo_s = smem_u32(hp.slo), sc_s = smem_u32(hp.sc);
+    // The consumers meet at a named barrier every stage, so none may leave the
+    // loop alone: a warp whose wait gave up (the error word is set) stops
+    // waiting and computing but keeps arriving, so that every warp ends.
+    bool bad = false;
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int64_t i = 0; i < nst; i++) {
+        if (!bad) bad = !__all_sync(0xffffffffu, mbar_wait_sleep(smem_u32(R.full + slot), phase, err));
+        const uint32_t stage = smem_u32(ring) + (uint32_t)(slot * stage_bytes);
+        // this lane's outputs: weight rows gq, gq + 8 (e = 0, 1 / 2, 3) x activation
+        // rows 8 mt + 2 qq, + 1 (e = 0, 2 / 1, 3)
+        float acc[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
+        for (int u = bad ? nu : warp; u < nu; u += kWarps) {
+            const int sb = u >> lnp, p = u & ((1 << lnp) - 1);
+            const uint32_t blk0 = stage + (uint32_t)(gq * rl + sb * kSb);  // this lane's A rows gq, gq + 8
+            const uint32_t blk1 = blk0 + (uint32_t)(8 * rl);
+            uint32_t hdr[2], W1[2], W2[2], sc_lo[2], sc_hi[2];
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const uint32_t b = r ? blk1 : blk0;
+                hdr[r] = lds32(b);
+                const uint32_t W0 = lds32(b + 4);
+                W1[r] = lds32(b + 8);
+                W2[r] = lds32(b + 12);
+                sc_lo[r] = W0 & 0x3F3F3F3Fu;  // the 6-bit scales of sub-blocks 0-3 and 4-7, one per byte
+                sc_hi[r] = (W2[r] & 0x0F0F0F0Fu) | ((W0 >> 2) & 0x30303030u);
+            }
+            float C[MT][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) C[mt][0] = C[mt][1] = C[mt][2] = C[mt][3] = 0.0f;
+            const uint32_t sbo = 512u * (uint32_t)sb;  // byte offset of the superblock's activations
+            const uint32_t q0 = blk0 + 4 * qq, q1 = blk1 + 4 * qq;
+            if (lnp == 0) {  // the whole superblock: selectors and branches fold
+#pragma unroll
+                for (int cg = 0; cg < 4; cg++) hmma_pair<FMT, MT>(cg, q0, q1, sc_lo, sc_hi, qq, sbo, hrow, lrow, C);
+            } else {
+                const int cg0 = p << (2 - lnp);
+                for (int cg = cg0; cg < cg0 + (4 >> lnp); cg++)
+                    hmma_pair<FMT, MT>(cg, q0, q1, sc_lo, sc_hi, qq, sbo, hrow, lrow, C);
+            }
+            // the min term (unit part 0): A = m of sub-blocks 4 qq .. 4 qq + 3 for
+            // lane groups 0 and 1, zero for 2 and 3 (k slots 4-7 and 12-15 unused);
+            // B = the activations' sub-block sums, hi then lo
+            float Cm[MT][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) Cm[mt][0] = Cm[mt][1] = Cm[mt][2] = Cm[mt][3] = 0.0f;
+            if (p == 0) {
+                uint32_t am[4] = {0u, 0u, 0u, 0u};
+                if (qq < 2) {
+#pragma unroll
+                    for (int r = 0; r < 2; r++) {
+                        const uint32_t mw = qq == 0 ? (W1[r] & 0x3F3F3F3Fu)
+                                                    : (((W2[r] >> 4) & 0x0F0F0F0Fu) | ((W1[r] >> 2) & 0x30303030u));
+                        am[r] = bytes_h2(mw, 0x4140);
+                        am[2 + r] = bytes_h2(mw, 0x4342);
+                    }
+                }
+#pragma unroll
+                for (int mt = 0; mt < MT; mt++) {
+                    uint2 sh = make_uint2(0u, 0u), sl = make_uint2(0u, 0u);
+                    if (qq < 2) {
+                        const uint32_t so = (uint32_t)((8 * mt + gq) * hp.SS + 16 * sb + 8 * qq);
+                        sh = lds64(shi_s + so);
+                        sl = lds64(slo_s + so);
+                    }
+                    hmma_16816(Cm[mt], am, sh.x, sh.y);
+                    hmma_16816(Cm[mt], am, sl.x, sl.y);
+                }
+            }
+            // (C d - 32 dmin Cm) 2^-E per output
+            float d[2], nm[2];
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                d[r] = fp16_bits_to_float((uint16_t)(hdr[r] & 0xFFFFu));
+                nm[r] = -32.0f * fp16_bits_to_float((uint16_t)(hdr[r] >> 16));
+            }
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) {
+                const float s0 = lds_f32(sc_s + 4u * (uint32_t)((8 * mt + 2 * qq) * nsb + sb));
+                const float s1 = lds_f32(sc_s + 4u * (uint32_t)((8 * mt + 2 * qq + 1) * nsb + sb));
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int r = e >> 1;
+                    const float v = fmaf(nm[r], Cm[mt][e], C[mt][e] * d[r]);
+                    acc[mt][e] = fmaf(v, (e & 1) ? s1 : s0, acc[mt][e]);
+                }
+            }
+        }
+        __syncwarp();  // every lane has read the stage
+        if (lane == 0) mbar_arrive(smem_u32(R.empty + slot));
+        // partials as [mt][weight row][activation row]
+        float* rw = red + ((size_t)(i & 1) * kWarps + warp) * RW;
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) {
+            *reinterpret_cast<float2*>(rw + mt * 128 + gq * 8 + 2 * qq) = make_float2(acc[mt][0], acc[mt][1]);
+            *reinterpret_cast<float2*>(rw + mt * 128 + (gq + 8) * 8 + 2 * qq) = make_float2(acc[mt][2], acc[mt][3]);
+        }
+        bar_sync(3, kWarps * 32);  // every warp's partials of this stage
+        {   // output t of the 128 MT: TPO = 4 / MT consecutive threads add warps q, q + TPO, ...
+            constexpr int TPO = 4 / MT;
+            const float* rs = red + (size_t)(i & 1) * kWarps * RW;
+            const int t = threadIdx.x / TPO, q = threadIdx.x % TPO;
+            float sum = 0.0f;
+#pragma unroll
+            for (int w = q; w < kWarps; w += TPO) sum += rs[(size_t)w * RW + t];
+#pragma unroll
+            for (int o2 = 1; o2 < TPO; o2 <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o2);
+            const int row = (t >> 3) & 15, j = 8 * (t >> 7) + (t & 7);
+            const int64_t r = r0 + i * kStageRows + row;
+            if (q == 0 && j < mb && r < r1) {
+                float* yp = y + (m0 + j) * ldy + r;
+                *yp = o.accumulate ? fmaf(o.alpha, sum, *yp) : o.alpha * sum;
+            }
+        }
+        if (++slot == slots) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+}
+
+template <int FMT, int MT>
+int run_hmma(const void* wq, int64_t n, int64_t k, const void* x, int dt, int64_t m, float* y, int64_t ldy, int slots,
+             int nx, const GemvOpts& o, size_t smem, cudaStream_t s) {
+    const void* fn = (const void*)gemv_hmma_kernel<FMT, MT>;
+    GDN_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int64_t ctas = std::min<int64_t>(sm_count(), n);
+    const dim3 grid((unsigned)ctas, (unsigned)((m + 8 * MT - 1) / (8 * MT)));
+    return launch_pdl(FMT == 1 ? "gemv_hmma_kernel<q4_k>" : "gemv_hmma_kernel<q5_k>", gemv_hmma_kernel<FMT, MT>, grid,
+                      dim3((kWarps + 1) * 32), smem, s, static_cast<const uint8_t*>(wq), n, k, x, dt, m, y, ldy,
                       slots, nx, o, device_error_word());
 }
 
@@ -915,15 +1391,15 @@ static int plan(int fmt, const void* wq, const void* wd, int64_t k, int64_t m, i
     return 0;
 }
 
-// The IMMA plan (three or more activation rows): 2 m-tiles (8 rows per CTA)
-// when 2 stages fit beside them, else 1; 0 if neither fits.
+// The IMMA plan (Q8_0, three or more activation rows): 2 m-tiles (8 rows per
+// CTA) when 2 stages fit beside them, else 1; 0 if neither fits.
 static int plan_mma(int fmt, const void* wq, const void* wd, int64_t k, int64_t m, int* mt_out, int* slots_out,
                     size_t* smem_out) {
-    if (m < 3 || (m + 3) / 4 > 65535 || k < 512 || (k & 511) != 0) return 0;
+    if (fmt != 0 || m < 3 || (m + 3) / 4 > 65535 || k < 512 || (k & 511) != 0) return 0;
     if ((reinterpret_cast<uintptr_t>(wq) & 15) != 0) return 0;
     if (fmt == 0 && (reinterpret_cast<uintptr_t>(wd) & 15) != 0) return 0;
     for (int mt = m > 4 ? 2 : 1; mt >= 1; mt--) {
-        const size_t base = kBarBytes + mma_fixed_bytes(fmt, mt, k);
+        const size_t base = kBarBytes + mma_fixed_bytes(mt, k);
         if (base >= kSmemLimit) continue;
         const int slots = (int)std::min<size_t>(kMaxSlots, (kSmemLimit - base) / mma_stage_bytes(fmt, k));
         if (slots < 2) continue;
@@ -935,12 +1411,35 @@ static int plan_mma(int fmt, const void* wq, const void* wd, int64_t k, int64_t 
     return 0;
 }
 
+// The fp16-MMA plan (Q4_K / Q5_K, three or more activation rows): 2 m-tiles
+// (16 rows per CTA) for more than 8 rows when 2 stages fit beside them, else 1.
+static int plan_hmma(int fmt, const void* wq, int64_t k, int64_t m, int* mt_out, int* slots_out, size_t* smem_out) {
+    if (fmt == 0 || m < 3 || (m + 7) / 8 > 65535 || k < 256 || (k & 255) != 0) return 0;
+    if ((reinterpret_cast<uintptr_t>(wq) & 15) != 0) return 0;
+    for (int mt = m > 8 ? 2 : 1; mt >= 1; mt--) {
+        const size_t base = kBarBytes + hmma_fixed_bytes(mt, k);
+        if (base >= kSmemLimit) continue;
+        const int slots = (int)std::min<size_t>(kMaxSlots, (kSmemLimit - base) / mma_stage_bytes(fmt, k));
+        if (slots < 2) continue;
+        *mt_out = mt;
+        *slots_out = slots;
+        *smem_out = base + (size_t)slots * mma_stage_bytes(fmt, k);
+        return 1;
+    }
+    return 0;
+}
+
+// mma: 1 = IMMA (Q8_0), 2 = fp16 MMA (K-quants), 0 = the streamed dp4a kernel.
 template <int FMT>
 static int run_fmt(int mb, int mma, const void* wq, const void* wd, int64_t n, int64_t k, const void* x, int dt,
                    int64_t m, float* y, int64_t ldy, int slots, int nx, const GemvOpts& o, size_t smem,
                    cudaStream_t s) {
-    if (mma) return mb == 2 ? run_mma<FMT, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s)
-                            : run_mma<FMT, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
+    if (FMT == 0 && mma == 1)
+        return mb == 2 ? run_mma<0, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s)
+                       : run_mma<0, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
+    if (FMT != 0 && mma == 2)
+        return mb == 2 ? run_hmma<FMT != 0 ? FMT : 1, 2>(wq, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s)
+                       : run_hmma<FMT != 0 ? FMT : 1, 1>(wq, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
     switch (mb) {
         case 1: return run<FMT, 1>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
         case 2: return run<FMT, 2>(wq, wd, n, k, x, dt, m, y, ldy, slots, nx, o, smem, s);
@@ -968,6 +1467,9 @@ int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64
     if (n > 0 && plan_mma(fmt, wq, wd, k, m, &mb, &slots, &smem)) {
         mma = 1;
         nx = activation_slots(x, dt, xrow, 4 * mb, mma_stage_bytes(fmt, k), slots);
+    } else if (n > 0 && plan_hmma(fmt, wq, k, m, &mb, &slots, &smem)) {
+        mma = 2;
+        nx = activation_slots(x, dt, xrow, 8 * mb, mma_stage_bytes(fmt, k), slots);
     } else {
         if (!plan(fmt, wq, wd, k, m, &mb, &slots, &smem)) return GDN_ERR_SHAPE;
         if (n <= 0) return GDN_OK;

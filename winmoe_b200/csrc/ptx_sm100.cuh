@@ -60,6 +60,32 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     return true;
 }
 
+// mbar_wait whose polls suspend the thread for up to 1 us each while the phase
+// is incomplete (the suspend-time hint), so that waiting warps of a
+// throughput-bound kernel take few issue slots from the working ones.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, uint32_t* err) {
+    auto poll = [&]() {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity), "r"(1000u)
+            : "memory");
+        return ok != 0;
+    };
+    if (poll()) return true;
+    const long long t0 = clock64();
+    while (!poll()) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicOr(err, DEV_ERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
 // Orders this thread's generic-proxy shared-memory accesses before later
 // async-proxy ones: writes that an MMA reads next, and reads of a slot that a
 // TMA overwrites next.
