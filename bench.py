@@ -512,7 +512,7 @@ def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
         gen = torch.Generator().manual_seed(40 + B)
         xi = torch.randn((B, cfg.hidden), generator=gen).to(dev)
         xo = torch.randn((B, cfg.inner), generator=gen).to(dev)
-        if half:  # fp16 activations: the tensor-core path (exact hi + lo weights)
+        if half:  # fp16 activations: from 32 rows the tcgen05 GEMM (exact hi + lo weights), below the GEMV
             xi, xo = xi.half(), xo.half()
         yi = torch.empty((B, cfg.in_proj_rows), dtype=torch.float32, device=dev)
         yo = torch.empty((B, cfg.hidden), dtype=torch.float32, device=dev)
@@ -534,12 +534,14 @@ def run_q4k_sweep(cfg, dev, hbm_peak, peak_src, with_cpu):
         ms = e0.elapsed_time(e1) / reps
         nb = q4k_call_bytes(cfg, B)
         ach = nb / (ms / 1e3) / 1e9
-        rows[f"B={B}" + (" fp16 x (tensor cores)" if half else "")] = {
+        path = "" if not half else " fp16 x (tcgen05 GEMM)" if B >= 32 else " fp16 x (fp16-MMA GEMV)"
+        rows[f"B={B}" + path] = {
             "us_per_call": ms * 1e3, "tok_per_s": B / (ms / 1e3), "achieved_gbs": ach, "frac": ach / hbm_peak,
             "algorithmic_bytes_per_call": nb}
     res = {"workload": "Q4_K projection sweep (config 4): in_proj (qkvz + ba rows) and out_proj, dequant-GEMV, "
-                       "fp32 activations; one call = the four projections for B tokens; the 'fp16 x' rows take "
-                       "the same batches as fp16 activations through the tensor-core path; 50 calls queued behind "
+                       "fp32 activations (m <= 2: dp4a GEMV, m >= 3: fp16-MMA GEMV); one call = the four projections "
+                       "for B tokens; the 'fp16 x' rows take the same batches as fp16 activations (B = 32: the "
+                       "tcgen05 GEMM); 50 calls queued behind "
                        "a GPU sleep, so the events time the kernels rather than the host's launches; call i uses "
                        "weight copy i % 10 (10 x 19 MB > L2: weights from HBM)",
            "roofline_peak": {"unit": "GB/s", "peak": hbm_peak, "peak_source": peak_src}, "batches": rows}
