@@ -384,8 +384,8 @@ GDN_API int gdn_out_proj_gathered(const int8_t* out_qs, const uint16_t* out_d, i
  * The same out_proj with the head blocks left where the ranks wrote them:
  * blocks[b] points at rank b's gated[T][inner / blocks] (fp16 bits) -- this
  * GPU's buffer or a peer's opened with gdn_ipc_open -- and the tensor cores
- * read each token slice's K blocks straight from there (TMA loads over
- * NVLink, no copy, no multicast), in the single-GPU k order.  T >= 64,
+ * read each token slice's K blocks straight from there (plain TMA loads over
+ * NVLink, each CTA its own; no copy), in the single-GPU k order.  T >= 64,
  * blocks <= 8.  Replaces the all-gather of the gated heads: each rank reads
  * only the rows of its own token range.  No counterpart in the reference.
  */
