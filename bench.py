@@ -409,7 +409,7 @@ def run_expert_ffn(dev, hbm_peak, peak_src, with_cpu):
     """(f)4: the MoE experts of one token, the reference's batched GPU route
     (gpu_expert_batch_start / _add / _finish, gpu_offload.cu:756-809): 8 experts,
     each Q4_K gate / up, SwiGLU, Q5_K down, weighted into the token's output --
-    one gdn_experts_ffn call per token (three launches).  Token i uses experts
+    one gdn_experts_ffn call per token (two launches).  Token i uses experts
     8i .. 8i+7 of a pool of 128 distinct experts (243 MB > L2: weights from HBM),
     weights 1/8.  Beside it, the same tokens as 8 single-expert accumulating
     calls each (the reference's call pattern, two launches per expert)."""
@@ -460,11 +460,11 @@ def run_expert_ffn(dev, hbm_peak, peak_src, with_cpu):
     nb = K * (2 * I * (H // 256) * 144 + H * (I // 256) * 176) + (H + K * (3 * I + 2 * H)) * 4
     res = {"workload": "MoE experts of one token (35B-class: hidden 2048, expert intermediate 512, top-8): Q4_K "
                        "gate + up, SwiGLU, Q5_K down, weighted accumulation, 8 experts per token from a pool of "
-                       "128 (243 MB > L2: weights from HBM); one gdn_experts_ffn call (3 launches) per token; "
+                       "128 (243 MB > L2: weights from HBM); one gdn_experts_ffn call (2 launches) per token; "
                        "16 tokens queued behind a GPU sleep",
            "value": 1e6 / us, "unit": "tok/s", "us_per_token": us, "us_per_expert": us / K,
            "us_per_token_single_expert_calls": us_single,
-           "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel<q4_k/q5_k> x 2 + experts_sum_kernel per token",
+           "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel<q4_k> (gate + up) + gemv_stream_kernel<q5_k> (down, k-segments) per token",
                         "achieved": nb / (us / 1e6) / 1e9, "peak": hbm_peak, "unit": "GB/s",
                         "frac": nb / (us / 1e6) / 1e9 / hbm_peak, "peak_source": peak_src,
                         "algorithmic_bytes_per_token": nb}}

@@ -204,11 +204,13 @@ GDN_API int gdn_expert_ffn(const void* w_gate, const void* w_up, const void* w_d
  * gpu_expert_batch_finish, engine/runtime/gpu_offload.cu:756-809):
  *   out[m][hidden] = sum_e weights[e] * y_e      (accumulate == 0)
  *   out[m][hidden] += sum_e weights[e] * y_e     (accumulate != 0)
- * with y_e expert e's FFN as gdn_expert_ffn's, the sum in expert order
- * (weights NULL: all 1).  w_gate / w_up / w_down: host arrays of n_experts
- * device pointers, 1 <= n_experts <= GDN_MAX_EXPERTS_PER_CALL; three launches
- * whatever n_experts (one streamed GEMV over all gate and up matrices, one over
- * all down matrices, the weighted sum).  Workspace of
+ * with y_e expert e's FFN as gdn_expert_ffn's (weights NULL: all 1).
+ * w_gate / w_up / w_down: host arrays of n_experts device pointers,
+ * 1 <= n_experts <= GDN_MAX_EXPERTS_PER_CALL; two launches whatever n_experts:
+ * one streamed GEMV over all gate and up matrices, then one over all down
+ * matrices side by side along k, expert e's inputs its SwiGLU times
+ * weights[e] (the weighted sum formed in the GEMV's fp32 sums: equal to the
+ * per-expert accumulation up to rounding).  Workspace of
  * gdn_experts_ffn_workspace_size(n_experts, m, hidden, inter) bytes, 256-byte
  * aligned; weights read on the host when the call is made.
  */

@@ -92,7 +92,7 @@ def test_expert_batch_accumulates_weighted_experts():
 @pytest.mark.parametrize("ne,m,accumulate", [(1, 1, False), (2, 3, True), (8, 1, True), (8, 4, False),
                                                (5, 2, True)])
 def test_experts_ffn_batched_matches_oracle(ne, m, accumulate):
-    """gpu_expert_batch_start / _add x ne / _finish as one call: three launches
+    """gpu_expert_batch_start / _add x ne / _finish as one call: two launches
     whatever ne; out (+)= sum_e w_e * expert_e(x), in expert order."""
     hidden, inter = 2048, 512
     experts = [_expert(hidden, inter, Q4K, Q5K, seed=700 + 3 * e) for e in range(ne)]

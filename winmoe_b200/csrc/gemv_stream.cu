@@ -273,10 +273,34 @@ __device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Sta
 // w + kWarps, ..., U at a time, every read of a batch issued before its
 // reductions.  From global memory the warp arrives on named barrier 1 (the
 // producer's go) once its first batch is requested.
+// The SwiGLU input for elements e .. e + 3 of an fp32 activation row xr that
+// holds [g | u] (k values each), or [s][g | u] per k-segment s of k / kseg
+// values (o.kseg > 0; the four elements lie in one segment), times the
+// segment's scale: (g * sigmoid(g)) * u, as the reference's swiglu_kernel.
+__device__ __forceinline__ float4 swiglu4(const char* xr, int64_t e, int64_t k, const GemvOpts& o) {
+    int64_t go = e, uo = k + e;
+    float sc = 1.0f;
+    if (o.kseg) {
+        const int64_t ks = k / o.kseg;
+        const int sgm = (int)(e / ks);
+        go = e + (int64_t)sgm * ks;
+        uo = go + ks;
+#pragma unroll
+        for (int i = 0; i < kGemvMaxSeg; i++)  // static indices: no copy of the parameter block
+            if (i == sgm) sc = o.kscale[i];
+    }
+    const float4 gv = *reinterpret_cast<const float4*>(xr + (size_t)go * 4);
+    const float4 uv = *reinterpret_cast<const float4*>(xr + (size_t)uo * 4);
+    float4 r = make_float4((gv.x * (1.0f / (1.0f + expf(-gv.x)))) * uv.x, (gv.y * (1.0f / (1.0f + expf(-gv.y)))) * uv.y,
+                           (gv.z * (1.0f / (1.0f + expf(-gv.z)))) * uv.z, (gv.w * (1.0f / (1.0f + expf(-gv.w)))) * uv.w);
+    if (o.kseg) r = make_float4(r.x * sc, r.y * sc, r.z * sc, r.w * sc);
+    return r;
+}
+
 template <int FMT, bool PADDED, bool SMEM, int U>
 __device__ __forceinline__ void stage_rows(const void* x, int x_dtype, int64_t ldx, int64_t m0, int mb, int rows,
                                            int64_t k, int warp, int lane, int8_t* xq, int pl, float* sx, float* x16,
-                                           int swiglu) {
+                                           const GemvOpts& o) {
     const int npc = (int)(k >> 7), nblk = (int)(k >> 5);
     const size_t es = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
     const int64_t xk = ldx;  // elements between activation rows
@@ -300,13 +324,8 @@ __device__ __forceinline__ void stage_rows(const void* x, int x_dtype, int64_t l
             xv[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             if (j < rows && j < mb) {
                 const char* xr = x0 + (size_t)j * xk * es;
-                if (swiglu) {  // fp32 [g | u]: (g * sigmoid(g)) * u, as the reference's swiglu_kernel
-                    const float4 gv = *reinterpret_cast<const float4*>(xr + (size_t)e * 4);
-                    const float4 uv = *reinterpret_cast<const float4*>(xr + (size_t)(k + e) * 4);
-                    xv[u] = make_float4((gv.x * (1.0f / (1.0f + expf(-gv.x)))) * uv.x,
-                                        (gv.y * (1.0f / (1.0f + expf(-gv.y)))) * uv.y,
-                                        (gv.z * (1.0f / (1.0f + expf(-gv.z)))) * uv.z,
-                                        (gv.w * (1.0f / (1.0f + expf(-gv.w)))) * uv.w);
+                if (o.swiglu) {
+                    xv[u] = swiglu4(xr, e, k, o);
                 } else if (vec) {
                     xv[u] = *reinterpret_cast<const float4*>(xr + (size_t)e * 4);
                 } else {
@@ -416,18 +435,17 @@ template <int FMT, bool PADDED>
 __device__ __forceinline__ bool consume_activations(const Ring& R, const void* x, int x_dtype, int64_t ldx,
                                                     const uint8_t* xs, int64_t m0, int mb, int rows, int64_t k,
                                                     int warp, int lane, int8_t* xq, int pl, float* sx, float* x16,
-                                                    int swiglu, uint32_t* err) {
+                                                    const GemvOpts& o, uint32_t* err) {
     bool ok = true;
     if (R.nx > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait_sleep(smem_u32(R.xbar), 0, err));
         if (ok)
-            stage_rows<FMT, PADDED, true, kSmemBatch>(xs, x_dtype, swiglu ? 2 * k : k, 0, mb, rows, k, warp, lane,
-                                                      xq, pl, sx, x16, swiglu);
+            stage_rows<FMT, PADDED, true, kSmemBatch>(xs, x_dtype, o.swiglu ? 2 * k : k, 0, mb, rows, k, warp, lane,
+                                                      xq, pl, sx, x16, o);
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(R.xdone));
     } else {
-        stage_rows<FMT, PADDED, false, kStageBatch>(x, x_dtype, ldx, m0, mb, rows, k, warp, lane, xq, pl, sx, x16,
-                                                    swiglu);
+        stage_rows<FMT, PADDED, false, kStageBatch>(x, x_dtype, ldx, m0, mb, rows, k, warp, lane, xq, pl, sx, x16, o);
     }
     bar_sync(2, kWarps * 32);
     return ok;
@@ -502,7 +520,14 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         const uint32_t bar = smem_u32(R.full + slot);
         const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
         mbar_arrive_expect_tx(bar, rows * (qbytes + dbytes));
-        bulk_load(dst, wb + (ra - rb) * (int64_t)qbytes, rows * qbytes, bar);
+        if (FMT != 0 && o.kseg) {  // k-segments: row r = the matrices' rows r side by side
+            const uint32_t qs = qbytes / (uint32_t)o.kseg;
+            for (uint32_t r = 0; r < rows; r++)
+                for (int sgm = 0; sgm < o.kseg; sgm++)
+                    bulk_load(dst + r * qbytes + (uint32_t)sgm * qs, o.seg[sgm] + (ra + r) * (int64_t)qs, qs, bar);
+        } else {
+            bulk_load(dst, wb + (ra - rb) * (int64_t)qbytes, rows * qbytes, bar);
+        }
         if (FMT == 0) bulk_load(dst + qstage, wd + ra * (int64_t)dbytes, rows * dbytes, bar);
     };
     if (warp == kWarps && lane == 0) {
@@ -510,7 +535,12 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {  // the weights never come from an earlier kernel
             const int64_t ra = r0 + i * kStageRows;
             const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
-            bulk_prefetch_l2(wb + (ra - rb) * (int64_t)qbytes, rows * qbytes);
+            if (FMT != 0 && o.kseg) {
+                const uint32_t qs = qbytes / (uint32_t)o.kseg;
+                for (int sgm = 0; sgm < o.kseg; sgm++) bulk_prefetch_l2(o.seg[sgm] + ra * (int64_t)qs, rows * qs);
+            } else {
+                bulk_prefetch_l2(wb + (ra - rb) * (int64_t)qbytes, rows * qbytes);
+            }
             if (FMT == 0) bulk_prefetch_l2(wd + ra * (int64_t)dbytes, rows * dbytes);
         }
     }
@@ -526,7 +556,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)
         consume_activations<FMT, true>(R, xe, x_dtype, ldx, xs, m0, mb, mb, k, warp, lane, xq, (int)st.pl, sx, x16,
-                                       o.swiglu, err);
+                                       o, err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);  // the activation loads are requested
@@ -672,7 +702,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)  // rows past mb are staged as zeros (their outputs are not stored)
         consume_activations<FMT, false>(R, xe, x_dtype, ldx, xs, m0, mb, MB, k, warp, lane, xq, (int)plm, sx,
-                                        nullptr, o.swiglu, err);
+                                        nullptr, o, err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);
@@ -960,7 +990,7 @@ __device__ __forceinline__ void stage_256(const float (&v)[8], bool valid, const
 // list, warp w takes pieces w, w + kWarps, ..., U at a time.
 template <bool SMEM, int U>
 __device__ __forceinline__ void stage_f16_rows(const void* x, int x_dtype, int64_t ldx, int64_t m0, int mb, int rows,
-                                               int64_t k, int warp, int lane, const HPlanes& h, int swiglu) {
+                                               int64_t k, int warp, int lane, const HPlanes& h, const GemvOpts& o) {
     const int npc = h.nsb;
     const size_t es = x_dtype == GDN_DTYPE_F32 ? 4 : 2;
     const char* x0 = static_cast<const char*>(x) + (SMEM ? 0 : (size_t)m0 * ldx * es);
@@ -984,15 +1014,11 @@ __device__ __forceinline__ void stage_f16_rows(const void* x, int x_dtype, int64
             for (int i = 0; i < 8; i++) v[u][i] = 0.0f;
             if (j < rows && j < mb) {
                 const char* xr = x0 + (size_t)j * ldx * es;
-                if (swiglu) {  // fp32 [g | u]: (g * sigmoid(g)) * u, as the reference's swiglu_kernel
+                if (o.swiglu) {
 #pragma unroll
                     for (int q = 0; q < 2; q++) {
-                        const float4 gv = *reinterpret_cast<const float4*>(xr + (size_t)(e + 4 * q) * 4);
-                        const float4 uv = *reinterpret_cast<const float4*>(xr + (size_t)(k + e + 4 * q) * 4);
-                        v[u][4 * q + 0] = (gv.x * (1.0f / (1.0f + expf(-gv.x)))) * uv.x;
-                        v[u][4 * q + 1] = (gv.y * (1.0f / (1.0f + expf(-gv.y)))) * uv.y;
-                        v[u][4 * q + 2] = (gv.z * (1.0f / (1.0f + expf(-gv.z)))) * uv.z;
-                        v[u][4 * q + 3] = (gv.w * (1.0f / (1.0f + expf(-gv.w)))) * uv.w;
+                        const float4 a = swiglu4(xr, e + 4 * q, k, o);
+                        v[u][4 * q + 0] = a.x, v[u][4 * q + 1] = a.y, v[u][4 * q + 2] = a.z, v[u][4 * q + 3] = a.w;
                     }
                 } else if (vec) {
                     const float4 a = *reinterpret_cast<const float4*>(xr + (size_t)e * 4);
@@ -1026,17 +1052,17 @@ __device__ __forceinline__ void stage_f16_rows(const void* x, int x_dtype, int64
 // consume_activations for the fp16 planes.
 __device__ __forceinline__ bool consume_activations_f16(const Ring& R, const void* x, int x_dtype, int64_t ldx,
                                                         const uint8_t* xs, int64_t m0, int mb, int rows, int64_t k,
-                                                        int warp, int lane, const HPlanes& h, int swiglu,
+                                                        int warp, int lane, const HPlanes& h, const GemvOpts& o,
                                                         uint32_t* err) {
     bool ok = true;
     if (R.nx > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait_sleep(smem_u32(R.xbar), 0, err));
         if (ok)
-            stage_f16_rows<true, kSmemBatch>(xs, x_dtype, swiglu ? 2 * k : k, 0, mb, rows, k, warp, lane, h, swiglu);
+            stage_f16_rows<true, kSmemBatch>(xs, x_dtype, o.swiglu ? 2 * k : k, 0, mb, rows, k, warp, lane, h, o);
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(R.xdone));
     } else {
-        stage_f16_rows<false, kStageBatch>(x, x_dtype, ldx, m0, mb, rows, k, warp, lane, h, swiglu);
+        stage_f16_rows<false, kStageBatch>(x, x_dtype, ldx, m0, mb, rows, k, warp, lane, h, o);
     }
     bar_sync(2, kWarps * 32);
     return ok;
@@ -1160,15 +1186,28 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
         const uint32_t bar = smem_u32(R.full + slot);
         const uint32_t dst = smem_u32(ring + (size_t)slot * stage_bytes);
         mbar_arrive_expect_tx(bar, rows * qbytes);
-        for (uint32_t r = 0; r < rows; r++)
-            bulk_load(dst + r * (uint32_t)rl, wb + (ra - rb + r) * (int64_t)qbytes, qbytes, bar);
+        if (o.kseg) {  // k-segments: row r = the matrices' rows r side by side
+            const uint32_t qs = qbytes / (uint32_t)o.kseg;
+            for (uint32_t r = 0; r < rows; r++)
+                for (int sgm = 0; sgm < o.kseg; sgm++)
+                    bulk_load(dst + r * (uint32_t)rl + (uint32_t)sgm * qs, o.seg[sgm] + (ra + r) * (int64_t)qs, qs,
+                              bar);
+        } else {
+            for (uint32_t r = 0; r < rows; r++)
+                bulk_load(dst + r * (uint32_t)rl, wb + (ra - rb + r) * (int64_t)qbytes, qbytes, bar);
+        }
     };
     if (warp == kWarps && lane == 0) {
         ring_init(R);
         for (int64_t i = 0; i < min(nst, (int64_t)2); i++) {  // the weights never come from an earlier kernel
             const int64_t ra = r0 + i * kStageRows;
             const uint32_t rows = (uint32_t)min((int64_t)kStageRows, r1 - ra);
-            bulk_prefetch_l2(wb + (ra - rb) * (int64_t)qbytes, rows * qbytes);
+            if (o.kseg) {
+                const uint32_t qs = qbytes / (uint32_t)o.kseg;
+                for (int sgm = 0; sgm < o.kseg; sgm++) bulk_prefetch_l2(o.seg[sgm] + ra * (int64_t)qs, rows * qs);
+            } else {
+                bulk_prefetch_l2(wb + (ra - rb) * (int64_t)qbytes, rows * qbytes);
+            }
         }
     }
     __syncthreads();  // the barriers are initialised
@@ -1182,7 +1221,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     const void* xe = static_cast<const char*>(x) + (size_t)sg * o.x_seg * esize;  // this CTA's matrix's input
     const uint8_t* xs = ring + (size_t)(slots - nx) * stage_bytes;  // the activations, when nx > 0
     if (warp < kWarps)  // rows past mb are not staged: their A rows only reach outputs that are not stored
-        consume_activations_f16(R, xe, x_dtype, ldx, xs, m0, mb, mb, k, warp, lane, hp, o.swiglu, err);
+        consume_activations_f16(R, xe, x_dtype, ldx, xs, m0, mb, mb, k, warp, lane, hp, o, err);
 
     if (warp == kWarps) {  // producer
         if (nx == 0) bar_sync(1, (kWarps + 1) * 32);
@@ -1456,6 +1495,12 @@ int launch_gemv_stream(int fmt, const void* wq, const void* wd, int64_t n, int64
         for (int i = 0; i < o.nseg; i++)
             if (!o.seg[i] || (reinterpret_cast<uintptr_t>(o.seg[i]) & 15) != 0) return GDN_ERR_ARG;
         if (std::min<int64_t>(sm_count(), n) < o.nseg) return GDN_ERR_SHAPE;
+    }
+    if (o.kseg) {  // K-quant matrices side by side along k, SwiGLU inputs, no row segments
+        if (fmt == 0 || !o.swiglu || o.nseg || o.kseg > kGemvMaxSeg || k % o.kseg != 0 || (k / o.kseg) % 256 != 0)
+            return GDN_ERR_ARG;
+        for (int i = 0; i < o.kseg; i++)
+            if (!o.seg[i] || (reinterpret_cast<uintptr_t>(o.seg[i]) & 15) != 0) return GDN_ERR_ARG;
     }
     if (o.swiglu && (dt != GDN_DTYPE_F32 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)) return GDN_ERR_ARG;
     const int64_t xrow = o.swiglu ? 2 * k : k;

@@ -25,7 +25,10 @@ int launch_q8_0_gemv(const int8_t* qs, const uint16_t* d, int64_t n, int64_t k, 
 // r / seg_rows), the CTAs split evenly over the matrices; matrix s's input is
 // the activations offset by s * x_seg elements within each row, rows ldx
 // elements apart (0: the input length).  swiglu: fp32 activation rows hold
-// [g | u] (2 k values) and the input is (g * sigmoid(g)) * u.  y = alpha *
+// [g | u] (2 k values) and the input is (g * sigmoid(g)) * u.  kseg > 0 (with
+// swiglu, K-quants): the k axis is kseg matrices seg[s] side by side, each
+// [n][k / kseg]; activation rows hold [s][g | u] per segment and segment s's
+// inputs are scaled by kscale[s] (y = sum_s W_s (kscale_s a_s)).  y = alpha *
 // result, or with accumulate y += alpha * result.
 constexpr int kGemvMaxSeg = 16;
 struct GemvOpts {
@@ -35,6 +38,8 @@ struct GemvOpts {
     int64_t x_seg = 0;
     int64_t ldx = 0;
     int swiglu = 0;
+    int kseg = 0;
+    float kscale[kGemvMaxSeg] = {};
     int accumulate = 0;
     float alpha = 1.0f;
 };

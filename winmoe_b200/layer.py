@@ -367,7 +367,7 @@ def experts_ffn(w_gate: list, w_up: list, w_down: list, gate_type: int, down_typ
                 workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """The batched expert block of m tokens (gpu_expert_batch_start / _add / _finish):
     out (+)= sum_e weights[e] * down_e(SwiGLU(gate_e x, up_e x)), summed in expert
-    order, in three launches for up to MAX_EXPERTS_PER_CALL experts."""
+    order up to rounding, in two launches for up to MAX_EXPERTS_PER_CALL experts."""
     ne = len(w_gate)
     if not (len(w_up) == len(w_down) == ne):
         raise GDNError(-1, "w_gate, w_up and w_down must list the same experts")
