@@ -1,6 +1,11 @@
 // Streamed dequant-GEMV for small activation batches (decode of up to 63
 // sequences, the GQA projections, the Q4_K sweep, the expert FFN's Q4_K / Q5_K
-// projections), 1, 2, 4 or 8 activation rows per CTA.
+// projections).  Three consumers of one streaming scheme: gemv_stream_kernel
+// (dp4a, 1, 2, 4 or 8 activation rows per CTA; every format at 1-2 rows),
+// gemv_mma_kernel (Q8_0, 3..63 rows, int8 mma.sync) and gemv_hmma_kernel
+// (Q4_K / Q5_K, 3 or more rows, fp16 mma.sync on exact q*sc weights); row
+// segment tables (several matrices in one launch) and k-segments (matrices
+// side by side along k) serve the expert FFN.
 //
 // Memory side.  The row-per-warp GEMVs in quant.cu keep one batch of register
 // loads in flight per warp, so at batch 1 their speed is set by HBM latency;
@@ -14,8 +19,8 @@
 // `empty` barrier.  The stage copies start only once the activation loads are
 // requested (a named barrier): issued earlier, they held those loads back by
 // microseconds on the SM's return path.  Before griddepcontrol.wait the first
-// stages are only prefetched into L2.  Every wait is bounded, and the producer
-// leaves no copy in flight.
+// stages are only prefetched into L2.  Every wait is bounded (the GEMV waits
+// poll with a suspend-time hint), and the producer leaves no copy in flight.
 //
 // Arithmetic.  Converting every int8 / 4-bit weight to fp32 and multiplying
 // costs about six instructions per weight and lane, which bounds a batch-1
@@ -835,18 +840,18 @@ int run_mma(const void* wq, const void* wd, int64_t n, int64_t k, const void* x,
 // q sc (< 2048) is exact in fp16.  Each activation row's 256-element piece (one
 // superblock's columns) is scaled by a power of two 2^E that brings its max |x|
 // into [2^14, 2^15) and split into two fp16 parts, x 2^E = hi + lo (22
-// significant bits; the sum of the parts is x 2^E to within 2^-25 of the
-// piece's scaled max).  One mma.sync m16n8k16 takes A = the hi parts of 8
-// activation rows (A rows 0-7) and their lo parts (rows 8-15), B = q sc of 8
-// weight rows, and its fp32 accumulators sum a whole superblock, so that the
-// only per-superblock work left is (C_hi + C_lo) d 2^-E per output.  The min
-// term dmin sum_s m_s X_s (X_s the fp32 sum of sub-block s's activations) is
-// one more mma per superblock: A = the eight X_s 2^(E-5) as hi + lo, B = the
-// eight m_s.  The k order inside an mma is free: k slots 2 t, 2 t + 1, 2 t + 8,
-// 2 t + 9 of lane group t hold elements 4 t .. 4 t + 3 of the 16-element run,
-// so that both operands are plain 4-element loads.  The 16 consumer warps
-// split a stage into (n-tile, superblock, sub-block range) units and add their
-// partial sums through shared memory as the IMMA kernel does.
+// significant bits; the sum of the parts is x 2^E to within about 1e-7 of the
+// piece's scaled max).  mma.sync m16n8k16 takes A = q sc of the stage's 16
+// weight rows and B = 8 activation rows, the hi parts and then the lo parts
+// into the same fp32 accumulators, which sum a whole superblock, so that the
+// only per-superblock work left is C d 2^-E per output.  The min term
+// dmin sum_s m_s X_s (X_s the fp32 sum of sub-block s's activations) is one
+// more mma pair per superblock: A = the rows' eight m_s, B = the eight
+// X_s 2^(E-5) as hi + lo.  The k order inside an mma is free: k slots 2 t,
+// 2 t + 1, 2 t + 8, 2 t + 9 of lane group t hold elements 4 t .. 4 t + 3 of the
+// 16-element run, so that both operands are plain 4-element loads.  The 16
+// consumer warps split a stage into (superblock, sub-block range) units of all
+// 16 rows and add their partial sums through shared memory once per stage.
 
 __host__ __device__ constexpr int64_t h_plane(int64_t k) { return 2 * k + 32; }      // fp16 row, 32 (mod 128) B
 __host__ __device__ constexpr int64_t h_sums(int64_t k) { return 16 * (k >> 8) + 16; }  // 8 fp16 per superblock
