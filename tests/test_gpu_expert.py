@@ -117,6 +117,25 @@ def test_experts_ffn_batched_matches_oracle(ne, m, accumulate):
     assert rel_l2(got, seq.cpu().numpy()) <= 1e-6
 
 
+@pytest.mark.parametrize("gate_type,down_type", [(Q5K, Q4K), (Q4K, Q4K)])
+@pytest.mark.parametrize("m", [1, 4])
+def test_experts_ffn_batched_other_types(gate_type, down_type, m):
+    """The batched block with Q5_K gate / up segments and Q4_K down k-segments, on
+    the dp4a (m = 1) and fp16-MMA (m = 4) GEMVs."""
+    hidden, inter, ne = 2048, 512, 3
+    experts = [_expert(hidden, inter, gate_type, down_type, seed=760 + 3 * e) for e in range(ne)]
+    weights = [0.5, -0.25, 0.125]
+    x = synth.hidden_states(m, hidden, seed=761)
+    got = L.experts_ffn([dev(e[0]) for e in experts], [dev(e[1]) for e in experts], [dev(e[2]) for e in experts],
+                        gate_type, down_type, hidden, inter, torch.from_numpy(x).to(DEV), weights=weights).cpu().numpy()
+    P = O.port()
+    for i in range(m):
+        want = np.zeros(hidden, np.float32)
+        for (wg, wu, wd), w in zip(experts, weights):
+            P.expert_ffn(x[i], wg, wu, wd, gate_type, down_type, hidden, inter, weight=w, out=want)
+        assert rel_l2(got[i], want) <= 1e-4, i
+
+
 def test_experts_ffn_unweighted_and_empty():
     hidden, inter = 512, 256
     experts = [_expert(hidden, inter, Q5K, Q5K, seed=720 + 3 * e) for e in range(3)]
