@@ -88,16 +88,12 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// Q4_K 6-bit scale and min of sub-block j from the 12 packed bytes.
-__device__ __forceinline__ void scale_min(int j, const uint8_t* sc, int& s, int& m) {
-    if (j < 4) {
-        s = sc[j] & 63;
-        m = sc[j + 4] & 63;
-    } else {
-        s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
-        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-    }
-}
+// Q4_K / Q5_K 6-bit scales and mins (q4k_dequant.h:43-60): sub-block j < 4 takes
+// scale = sc[j] & 63, min = sc[j + 4] & 63; j >= 4 takes scale = (sc[j + 4] & 15)
+// | (sc[j - 4] >> 6) << 4, min = (sc[j + 4] >> 4) | (sc[j] >> 6) << 4.  With the
+// 12 bytes as words W0 W1 W2, one byte per sub-block:
+//   scales 0-3 = W0 & 0x3F3F3F3F,  4-7 = (W2 & 0x0F0F0F0F) | ((W0 >> 2) & 0x30303030)
+//   mins   0-3 = W1 & 0x3F3F3F3F,  4-7 = ((W2 >> 4) & 0x0F0F0F0F) | ((W1 >> 2) & 0x30303030)
 
 // Rounds v (|v| < 2^22) to the nearest integer, ties to even, by adding
 // 1.5 * 2^23: returns the integer, and the rounded value as a float in *f.
@@ -228,12 +224,16 @@ __device__ __forceinline__ void q4k_row(const uint8_t* row, int64_t k, const Sta
         const uint8_t* blk = row + sb * (Q5 ? 176 : 144);
         const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
         const uint4 q4 = *reinterpret_cast<const uint4*>(blk + (Q5 ? 48 : 16) + 16 * j);
-        const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
         const float d = fp16_bits_to_float((uint16_t)(hdr.x & 0xFFFFu));
         const float dmin = fp16_bits_to_float((uint16_t)(hdr.x >> 16));
-        int s_lo, m_lo, s_hi, m_hi;
-        scale_min(2 * c, hb + 4, s_lo, m_lo);
-        scale_min(2 * c + 1, hb + 4, s_hi, m_hi);
+        // the 6-bit scales / mins of sub-blocks 2 c and 2 c + 1 from the packed
+        // words (all eight at once, one byte each)
+        const uint32_t scw = c < 2 ? (hdr.y & 0x3F3F3F3Fu) : ((hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u));
+        const uint32_t mnw = c < 2 ? (hdr.z & 0x3F3F3F3Fu)
+                                   : (((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u));
+        const int bs = 16 * (c & 1);  // byte 2 c & 3 of the word, and the next
+        const int s_lo = (int)((scw >> bs) & 0xFFu), s_hi = (int)((scw >> (bs + 8)) & 0xFFu);
+        const int m_lo = (int)((mnw >> bs) & 0xFFu), m_hi = (int)((mnw >> (bs + 8)) & 0xFFu);
         const float sl = d * (float)s_lo, ml = dmin * (float)m_lo;
         const float sh = d * (float)s_hi, mh = dmin * (float)m_hi;
         uint4 lo = make_uint4(q4.x & 0x0F0F0F0Fu, q4.y & 0x0F0F0F0Fu, q4.z & 0x0F0F0F0Fu, q4.w & 0x0F0F0F0Fu);
