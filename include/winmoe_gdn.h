@@ -303,9 +303,11 @@ GDN_API int gdn_decode_step_ex(const gdn_layer* layer, int64_t batch,
  * counterpart in the reference (its deltanet_forward keeps its scratch on the
  * CPU stack).  Same arguments, results and errors as gdn_decode_step; the
  * scratch is one static device array per device, GDN_NOALLOC_SCRATCH_BYTES
- * long, so batches whose gdn_decode_workspace_size exceeds it are rejected
- * with GDN_ERR_SHAPE (the 35B Q8_0 layer fits up to 63 sequences: its
- * out_proj split-K partials, needed from 64 on, are reserved only then).
+ * long, so batches whose workspace (as gdn_decode_workspace_size, for the
+ * call's x_dtype) exceeds it are rejected with GDN_ERR_SHAPE: the 35B Q8_0
+ * layer fits up to 63 sequences with fp32 x and up to 46 with bf16 / fp16 x,
+ * whose projections run on the tensor cores from 9 sequences (fp32 x from 64)
+ * with split-K partials that are reserved only then.
  *   - The first call on each device (with that device current) resolves the
  *     scratch address with cudaGetSymbolAddress; make that first call before
  *     any stream capture.

@@ -74,8 +74,10 @@ def two_steps_identical(cfg, batch, dtype, seed):
 
 @pytest.mark.parametrize("cfg,batch,dtype", [
     (DIMS_35B, 1, torch.float32),                    # the reference engine's single-sequence decode
-    (DIMS_35B, 32, torch.bfloat16),                  # CUDA-core projections
-    (DIMS_35B, 63, torch.float16),                   # the largest 35B batch the scratch holds
+    (DIMS_35B, 8, torch.bfloat16),                   # CUDA-core projections
+    (DIMS_35B, 32, torch.bfloat16),                  # tensor-core projections and split-K out_proj
+    (DIMS_35B, 46, torch.float16),                   # the largest 35B 16-bit batch the scratch holds
+    (DIMS_35B, 63, torch.float32),                   # the largest 35B fp32 batch (CUDA-core projections)
     (GDNConfig(512, 2, 4, 128), 64, torch.bfloat16),  # tensor-core projections and split-K out_proj
 ])
 def test_noalloc_matches_workspace_entry(cfg, batch, dtype):
@@ -91,13 +93,15 @@ def test_noalloc_larger_then_smaller_batch():
     two_steps_identical(GDNConfig(512, 2, 4, 128), 5, torch.float32, seed=4)
 
 
-def test_noalloc_rejects_batches_above_the_scratch():
+@pytest.mark.parametrize("batch,dtype", [(64, torch.float32), (47, torch.bfloat16)])
+def test_noalloc_rejects_batches_above_the_scratch(batch, dtype):
+    # fp32 x: from 64 sequences the 35B out_proj splits K; 16-bit x: from 9, and
+    # from 47 its partials no longer fit
     cfg = DIMS_35B
     dims = gdn_dims(cfg.hidden, cfg.num_k_heads, cfg.num_v_heads, cfg.head_dim)
-    batch = 64  # from 64 sequences the 35B out_proj splits K: its partials no longer fit
     assert lib().gdn_decode_workspace_size(C.byref(dims), batch) > SCRATCH_BYTES
     w, st = setup(cfg, batch)
-    x = torch.zeros((batch, cfg.hidden), dtype=torch.float32, device=DEV)
+    x = torch.zeros((batch, cfg.hidden), dtype=dtype, device=DEV)
     y = torch.zeros_like(x)
     S0 = st.S.clone()
     rc = step_noalloc(w, st, x, y)

@@ -342,11 +342,17 @@ inline int mark(PhaseEvents* pe, int i, cudaStream_t s) {
     return GDN_OK;
 }
 
-// Tensor-core projections pay off once a batch fills an M=128 tile reasonably
-// (Q4_K: from 32 rows; below, the fp16-MMA GEMV of gemv_stream.cu is faster:
+// Tensor-core projections.  Q8_0 with 16-bit x from 9 sequences: the 35B
+// layer's in_proj + out_proj take ~65 us at any batch up to 128, the int8-MMA
+// GEMV ~4.3 us per row (step 57 / 67 / 81 / 102 us at B = 8 / 16 / 32 / 63
+// against 56 / 100 / 179 / 340 us); with fp32 x, whose exact activations the
+// GEMV keeps, from 64.  Q4_K from 32 rows (below, the fp16-MMA GEMV is faster:
 // the 35B layer's input projection 15 / 21 us at 8 / 16 rows against 29 us).
 constexpr int64_t kTcMinBatch = 64;
+constexpr int64_t kTcMinBatch16 = 9;
 constexpr int64_t kTcMinBatchQ4k = 32;
+
+bool q8_tc(int64_t B, int x_dtype) { return B >= kTcMinBatch || (B >= kTcMinBatch16 && x_dtype != GDN_DTYPE_F32); }
 // Split-K factor of the tensor-core out_proj (K = inner is long, N = hidden short).
 constexpr int kOutSplits = 8;
 // Split-K factor of the 2 Hv gate rows' exact tensor-core GEMM (one column tile).
@@ -385,9 +391,9 @@ struct Workspace {
 };
 
 // out_proj runs on the tensor cores with split K (partials in the workspace)
-// from these batches on: Q8_0 from kTcMinBatch, Q4_K from kTcMinBatchQ4k.
-bool out_proj_splits(int weight_type, int64_t B) {
-    return weight_type == GDN_GGML_Q8_0 ? B >= kTcMinBatch : B >= kTcMinBatchQ4k;
+// from these batches on: Q8_0 as q8_tc, Q4_K from kTcMinBatchQ4k.
+bool out_proj_splits(int weight_type, int64_t B, int x_dtype) {
+    return weight_type == GDN_GGML_Q8_0 ? q8_tc(B, x_dtype) : B >= kTcMinBatchQ4k;
 }
 
 // split_out: reserve the split-K partials of out_proj (only used when it splits);
@@ -447,18 +453,21 @@ int phase_ms(float* ms, int n) {
     return w;
 }
 
-// Covers both weight types (the Q4_K split starts at the smaller batch).
+// Covers both weight types and every activation type (the split-K buffers from
+// the smallest batch that may take them).
 size_t decode_workspace_bytes(const gdn_dims& d, int64_t batch) {
-    return carve(d, batch, nullptr, batch >= kTcMinBatchQ4k, batch >= kTcMinBatch).total;
+    return carve(d, batch, nullptr, batch >= std::min(kTcMinBatch16, kTcMinBatchQ4k), batch >= kTcMinBatch16).total;
 }
 
-// The input projection runs on the tensor cores (Q8_0 weights, B >= kTcMinBatch).
-bool in_proj_tc(int weight_type, int64_t B) { return weight_type == GDN_GGML_Q8_0 && B >= kTcMinBatch; }
+// The input projection runs on the tensor cores (Q8_0 weights, q8_tc).
+bool in_proj_tc(int weight_type, int64_t B, int x_dtype) {
+    return weight_type == GDN_GGML_Q8_0 && q8_tc(B, x_dtype);
+}
 
-size_t decode_workspace_bytes_for(const gdn_layer& L, int64_t batch, int flags) {
+size_t decode_workspace_bytes_for(const gdn_layer& L, int64_t batch, int flags, int x_dtype) {
     const bool ref = (flags & GDN_DECODE_REF_PROJECTIONS) != 0;
-    return carve(L.dims, batch, nullptr, !ref && out_proj_splits(L.weight_type, batch),
-                 !ref && in_proj_tc(L.weight_type, batch)).total;
+    return carve(L.dims, batch, nullptr, !ref && out_proj_splits(L.weight_type, batch, x_dtype),
+                 !ref && in_proj_tc(L.weight_type, batch, x_dtype)).total;
 }
 
 int validate_layer(const gdn_layer* L) {
@@ -511,7 +520,7 @@ static int in_projection(const gdn_layer* L, const Dims& D, int64_t B, const voi
         }
         return launch_q4_k_gemm_tc(L->in_blocks, D.np, hidden, a, B, ws.proj, D.ldp, TcOptions(), s);
     }
-    if (B < kTcMinBatch) return launch_q8_0_gemv(L->in_qs, L->in_d, D.np, hidden, x, x_dtype, B, ws.proj, D.ldp, s);
+    if (!q8_tc(B, x_dtype)) return launch_q8_0_gemv(L->in_qs, L->in_d, D.np, hidden, x, x_dtype, B, ws.proj, D.ldp, s);
     const void* a = x;
     int st;
     if (x_dtype != GDN_DTYPE_F16 || !aligned(x, 16)) {
@@ -576,12 +585,12 @@ int decode_step(const gdn_layer* L, int64_t B, const void* x, int x_dtype, float
         return fail(GDN_ERR_TYPE, "x_dtype %d is not supported", x_dtype);
     if (!aligned(S, 16)) return fail(GDN_ERR_ARG, "S must be 16-byte aligned");
     const gdn_dims& d = L->dims;
-    const bool tc_out = !ref && out_proj_splits(L->weight_type, B);
-    const size_t need = decode_workspace_bytes_for(*L, B, flags);
+    const bool tc_out = !ref && out_proj_splits(L->weight_type, B, x_dtype);
+    const size_t need = decode_workspace_bytes_for(*L, B, flags, x_dtype);
     if (wsp == nullptr || ws_bytes < need || !aligned(wsp, 256))
         return fail(GDN_ERR_ARG, "workspace must be 256-aligned and hold %zu bytes (got %zu)", need, ws_bytes);
     const Dims D = dims_of(d);
-    const Workspace ws = carve(d, B, wsp, tc_out, !ref && in_proj_tc(L->weight_type, B));
+    const Workspace ws = carve(d, B, wsp, tc_out, !ref && in_proj_tc(L->weight_type, B, x_dtype));
     const bool conv = (L->conv1d_w != nullptr && conv_buf != nullptr);
     PhaseEvents* pe = phase_events();
 
