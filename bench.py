@@ -703,9 +703,11 @@ def run_ours(args):
 
     world, rank, local = dist_env()
     if world > 1:
-        # NCCL's communicator log (stderr): its init lines name every rank and device
+        # NCCL's communicator log, on stderr (stdout carries only the JSON line): its
+        # init lines name every rank and device
         os.environ.setdefault("NCCL_DEBUG", "INFO")
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", torch.cuda.current_device())
