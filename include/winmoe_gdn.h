@@ -112,14 +112,14 @@ enum {
  * batch of m activation rows (the reference computes one row per call, with
  * fp32 activations on its GPU route: q8_matvec_kernel,
  * engine/runtime/gpu_offload.cu:152-199).  x_dtype: F32, BF16 or F16; k % 32 == 0.
- * m >= 64, k % 64 == 0, 16-byte aligned x: tcgen05 tensor cores with fp32
+ * m >= 16, k % 64 == 0, 16-byte aligned x: tcgen05 tensor cores with fp32
  * accumulation in TMEM --
  *   GDN_GEMM_EXACT, fp16 x: each weight split into exact hi + lo fp16
  *     operands (two MMAs), so only the summation order differs from fp32;
  *   GDN_GEMM_FAST, fp16 or bf16 x: one operand, weights rounded once to the
  *     x type.
- * Every other case (small m, fp32 x, bf16 x with EXACT): CUDA cores,
- * dequantising in registers, fp32 math.
+ * Every other case (m < 16, fp32 x, bf16 x with EXACT): the streamed GEMVs
+ * (int8 tensor cores from 3 rows), fp32-activation arithmetic.
  */
 GDN_API int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k,
                   const void* x, int x_dtype, int64_t m, float* y, int flags, void* stream);

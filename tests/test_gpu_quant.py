@@ -155,7 +155,7 @@ def test_q4_k_gemv_half_activations(xdt, m):
 
 
 GEMM_SHAPES = [(128, 256, 64), (256, 12352, 2048), (256, 2048, 4096), (200, 300, 2048), (64, 128, 128),
-               (1000, 12352, 2048), (4096, 2048, 4096), (130, 12288, 2048)]
+               (1000, 12352, 2048), (4096, 2048, 4096), (130, 12288, 2048), (16, 12352, 2048), (40, 2048, 4096)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)

@@ -115,9 +115,9 @@ int gdn_q8_0_gemm(const int8_t* qs, const uint16_t* d, int64_t n_rows, int64_t k
         return launch_q8_0_gemv_ref(qs, d, n_rows, k, static_cast<const float*>(x), m, y, n_rows, s);
     }
     if (flags != GDN_GEMM_EXACT && flags != GDN_GEMM_FAST) return fail(GDN_ERR_ARG, "q8_0 gemm: unknown flags %d", flags);
-    // FAST from 16 rows (one tensor-core weight operand: ~65 us for the 35B layer's in_proj + out_proj at
-    // any batch up to 128, the GEMV 70 us at 16 rows and 4.3 us per further row); EXACT from 64
-    const bool tc_shape = m >= (flags == GDN_GEMM_FAST ? 16 : 64) && k % 64 == 0 && aligned(x, 16) && aligned(d, 4);
+    // From 16 rows: the 35B layer's in_proj + out_proj take ~65 us (FAST, one weight operand) or ~70 us
+    // (EXACT, hi + lo) at any batch up to 128, the GEMV 70 us at 16 rows and 4.3 us per further row
+    const bool tc_shape = m >= 16 && k % 64 == 0 && aligned(x, 16) && aligned(d, 4);
     const bool tc = tc_shape && (flags == GDN_GEMM_FAST ? x_dtype != GDN_DTYPE_F32 : x_dtype == GDN_DTYPE_F16);
     if (tc) {
         TcOptions opt;
