@@ -84,6 +84,26 @@ def dist_env():
     return world, rank, local
 
 
+_json_out = None
+
+
+def reserve_stdout():
+    """Keeps file descriptor 1 for the JSON line alone: everything else written to stdout,
+    by Python or by native libraries (NCCL prints its version banner there whenever NCCL_DEBUG
+    is set), goes to stderr from here on."""
+    global _json_out
+    sys.stdout.flush()
+    _json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+
+
+def emit(line):
+    out = _json_out if _json_out is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -693,7 +713,7 @@ def run_reference(args):
                                    "with its unmodified Q8_0/Q8_K dispatch, OpenMP over all host threads"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_ours(args):
@@ -703,13 +723,13 @@ def run_ours(args):
 
     world, rank, local = dist_env()
     if world > 1:
-        # NCCL's communicator log, on stderr (stdout carries only the JSON line): its
-        # init lines name every rank and device
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # one communicator line per rank on stderr (stdout carries only the JSON line)
+        nv = ".".join(str(v) for v in torch.cuda.nccl.version())
+        print(f"[bench] nccl {nv} communicator: rank {dist.get_rank()} of {dist.get_world_size()}, local rank "
+              f"{local}, device {torch.cuda.get_device_name(local)} ({torch.cuda.get_device_properties(local).uuid})",
+              file=sys.stderr, flush=True)
     dev = torch.device("cuda", torch.cuda.current_device())
 
     from winmoe_b200 import layer as L, synth
@@ -734,7 +754,7 @@ def run_ours(args):
                 # GEMM + its split-K sum into the gates, edge rows + conv window, chunk_local, chunk_scan,
                 # chunk_out, out_proj GEMM
                 "gpu_launches": 9 * K, "roofline": pre["roofline"], "prefill": pre}
-        print(json.dumps(line), flush=True)
+        emit(line)
         return
 
     gen = torch.Generator(device=dev).manual_seed(7 + 1000 * rank)
@@ -895,11 +915,12 @@ def run_ours(args):
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def main():
     args = parse()
+    reserve_stdout()
     if args.impl == "reference":
         run_reference(args)
     else:
