@@ -723,10 +723,12 @@ def run_ours(args):
 
     world, rank, local = dist_env()
     if world > 1:
-        # NCCL's communicator log (INIT lines: rank, nranks, device, ring/tree setup) on stderr;
-        # its version banner goes to fd 1, which reserve_stdout() points at stderr too
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # NCCL's communicator log (INIT lines: rank, nranks, device, ring/tree setup) on stderr,
+        # raised to INFO where the environment leaves it off or lower (VERSION / WARN); its version
+        # banner goes to fd 1, which reserve_stdout() points at stderr too
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
         # one communicator line per rank on stderr (stdout carries only the JSON line)
