@@ -83,10 +83,16 @@ struct TcLayout {
     static constexpr uint32_t TMEM_SLOT_OFF = BAR_OFF + NBARS * 8;
     static constexpr uint32_t BYTES = TMEM_SLOT_OFF + 16;
     static constexpr size_t SMEM = BYTES + 1024;  // + alignment slack
-    static constexpr uint32_t TMEM_COLS = MT * NB * BN;
+    // Each M tile's accumulator(s) start on a 128-column boundary; TMEM is allocated
+    // in powers of two columns (>= 32)
+    static constexpr uint32_t ACC_STRIDE = (NB * BN + 127) / 128 * 128;
+    static constexpr uint32_t ACC_COLS = MT == 1 ? NB * BN : MT * ACC_STRIDE;
+    static constexpr uint32_t TMEM_COLS = ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
+                                          : ACC_COLS <= 256 ? 256 : 512;
     static_assert(SMEM <= 232448, "shared memory budget");
-    static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM budget");
-    static_assert(BN % 64 == 0 && BN <= 256, "BN");
+    static_assert(ACC_COLS <= 512, "TMEM budget");
+    // 96-column tiles (single operand, Q8_0) fill one wave where 128 would leave SMs idle
+    static_assert((BN % 64 == 0 && BN <= 256) || (BN == 96 && !SPLIT && !Q4K), "BN");
     static_assert(Q4K || (B8_OFF % 1024 == 0 && B8_BYTES % 1024 == 0), "64B-swizzled raw tiles start on swizzle atoms");
     static_assert(B8_OFF % 128 == 0 && B8_BYTES % 128 == 0, "TMA destinations");
     static_assert(SA * MT * A_BYTES >= 8u * 32u * 36u * 4u, "epilogue staging lives in the activation ring");
@@ -466,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int mt = 0; mt < MT; mt++) {
                     const uint32_t a0 = sbase + L::A_OFF + (sa * MT + mt) * L::A_BYTES;
-                    const uint32_t acc_col = tmem + (uint32_t)(mt * L::NB * BN);
+                    const uint32_t acc_col = tmem + (uint32_t)(mt * L::ACC_STRIDE);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++) {
                         const uint64_t ad = umma_desc_sw128(a0 + kk * 32);
@@ -483,12 +489,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---- dequant: BN rows x 4 chunks of 16 per k-tile over 256 threads
-        constexpr int UNITS = BN * 4 / kDeqThreads;  // (row, chunk) units per thread: 1, 2 or 4
-        constexpr int CPT = UNITS;                   // chunks of one row per thread
+        constexpr int CPT = (BN * 4 + kDeqThreads - 1) / kDeqThreads;  // chunks of one row per thread: 1, 2 or 4
         const int i = threadIdx.x - 32 * kDeqWarp0;
         const int kb = k >> 5;
-        const int rr = i / (4 / CPT);
-        const int c0 = (i % (4 / CPT)) * CPT;
+        // BN = 96 (384 units): warps 0-3 take rows 0..63 two chunks a thread, warps 4-7
+        // rows 64..95 one chunk a thread (each scheduler holds one warp of either kind)
+        int rr, c0, ncpt = CPT;
+        if constexpr (BN * 4 % kDeqThreads == 0) {
+            rr = i / (4 / CPT);
+            c0 = (i % (4 / CPT)) * CPT;
+        } else {
+            static_assert(BN == 96 && CPT == 2, "uneven dequant split for 96-column tiles only");
+            rr = i < 128 ? (i >> 1) : 64 + ((i - 128) >> 2);
+            c0 = i < 128 ? (i & 1) * 2 : (i - 128) & 3;
+            ncpt = i < 128 ? 2 : 1;
+        }
         const int gr = n0 + rr;
         const uint16_t* drow = (!Q4K && gr < n) ? dsc + (int64_t)gr * kb + 2 * kt0 : nullptr;
         // Scales are prefetched kWin k-tiles ahead in registers when every row's
@@ -581,7 +596,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint4* src = reinterpret_cast<const uint4*>(smem + L::B8_OFF + s8 * L::B8_BYTES + rr * BK);
                 uint4 raw[CPT];
 #pragma unroll
-                for (int cc = 0; cc < CPT; cc++) raw[cc] = src[(c0 + cc) ^ ((rr >> 1) & 3)];
+                for (int cc = 0; cc < CPT; cc++)
+                    if (cc < ncpt) raw[cc] = src[(c0 + cc) ^ ((rr >> 1) & 3)];
                 // The next write to this slot is a TMA (async proxy): the generic
                 // reads above must be ordered before it by a proxy fence, or the
                 // refill can overtake a late read (one weight row goes stale).
@@ -600,6 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint8_t* bhi = smem + L::B16_OFF + s16 * L::NB * L::B16_BYTES;
 #pragma unroll
                 for (int cc = 0; cc < CPT; cc++) {
+                    if (cc >= ncpt) break;
                     const int c = c0 + cc;
                     uint32_t hi[8], lo[8];
                     dequant16<BF16, SPLIT>(raw[cc], (uint16_t)(c < 2 ? (sc2 & 0xFFFFu) : (sc2 >> 16)), hi, lo);
@@ -629,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int mt = 0; mt < MT; mt++) {
                 const int row0 = m0 + mt * BM + q * 32;
-                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(mt * L::NB * BN);
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(mt * L::ACC_STRIDE);
 #pragma unroll 1
                 for (int cg = half * 32; cg < BN; cg += 64) {
                     if (!SPLIT && pe.enabled && n0 + cg < pe.qkv) continue;  // fused preprocessing below
@@ -667,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-        if constexpr (!SPLIT) {
+        if constexpr (!SPLIT && BN % 128 == 0) {
             static_assert(SPLIT || (uint32_t)MT * BM * 132 * 4 <= L::B8_OFF, "preprocessing stage fits the rings");
             if (pe.enabled)
                 prep_epilogue<BN, MT>(pe, reinterpret_cast<float*>(smem), tmem, n0, m0, (int)blockIdx.y, warp, lane, ok);
@@ -959,14 +976,31 @@ int launch_q8_0_gemm_tc(const int8_t* qs, const uint16_t* d, int64_t n, int64_t 
             opt.prep->rows = two ? 2 * BM : BM;
             pe = *opt.prep;
         }
+        // One M tile (m <= 128): a grid short of one wave leaves SMs idle while each CTA
+        // streams BN weight rows, so take the narrowest tile whose grid still fits one
+        // wave (fewest rows per SM; 12288 rows: 96 columns, 128 CTAs; the decode step at
+        // 16-63 sequences 10-15% faster).  Paired M tiles keep theirs: every CTA reads all
+        // 256 activation rows per k-tile whatever its width, and 128 CTAs of 96 columns
+        // measured slower than 96 of 128 (decode step at 256 sequences 253 vs 246-250 us).
+        // The fused preprocessing keeps its tiles.
+        const int64_t mtiles = (m + BM - 1) / BM;
+        auto ctas = [&](int64_t bn) { return (n + bn - 1) / bn * mtiles * splits; };
+        int bn = !two || wide ? 256 : 128;
+        if (!two && !pe.enabled && ctas(bn) < sm_count())
+            for (const int c : {128, 96})
+                if (c < bn && ctas(c) <= sm_count()) bn = c;
         if (a_bf16) {
-            st = !two ? run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
-                 : wide ? run_tc<256, 2, 3, 3, 2, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
-                        : run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe);
+            st = !two ? (bn == 256   ? run_tc<256, 1, 4, 3, 4, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                         : bn == 128 ? run_tc<128, 1, 6, 4, 8, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                                     : run_tc<96, 1, 6, 4, 12, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe))
+                      : (bn == 256 ? run_tc<256, 2, 3, 3, 2, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                                   : run_tc<128, 2, 4, 3, 6, true, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe));
         } else {
-            st = !two ? run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
-                 : wide ? run_tc<256, 2, 3, 3, 2, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
-                        : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe);
+            st = !two ? (bn == 256   ? run_tc<256, 1, 4, 3, 4, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                         : bn == 128 ? run_tc<128, 1, 6, 4, 8, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                                     : run_tc<96, 1, 6, 4, 12, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe))
+                      : (bn == 256 ? run_tc<256, 2, 3, 3, 2, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe)
+                                   : run_tc<128, 2, 4, 3, 6, false, false>(qs, d, n, k, a, m, out, ld_out, splits, kt_per, al, s, pe));
         }
     }
     if (opt.splits_used != nullptr) *opt.splits_used = splits;
