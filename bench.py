@@ -790,6 +790,9 @@ def run_ours(args):
     vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
     smi_id = vis[torch.cuda.current_device()] if vis else str(torch.cuda.current_device())
     with ClockSampler(smi_id) as clk:
+        # the K steps queue behind ~1 ms of GPU time, so the events time the device and not the
+        # host's issue of the first step (which matters most for short runs, --steps 4)
+        torch.cuda._sleep(2_000_000)
         e0.record(stream)
         for i in range(K):
             L.decode_step(w, st, xs[W + i], out, stream)
@@ -841,6 +844,7 @@ def run_ours(args):
     pipelined(0, W, e_w)
     torch.cuda.synchronize(dev)
     barrier()
+    torch.cuda._sleep(2_000_000)  # as above: the steps and their copies queue behind ~1 ms of GPU time
     e0.record(stream)
     pipelined(W, K, e0)
     e1.record(stream)
