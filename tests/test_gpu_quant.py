@@ -154,8 +154,12 @@ def test_q4_k_gemv_half_activations(xdt, m):
         assert rel_l2(y[i], P.quant_matvec(blocks, x32[i], n, k, 12, O.ACT_FP32)) <= 1e-5, i
 
 
+# One M tile (m <= 128) short of one wave takes the narrowest single-wave tile: 96 weight rows for
+# most of these (ragged last tile where 96 does not divide n), 128 for n = 16384 (171 tiles of 96
+# would exceed one wave); m > 128 pairs two M tiles per CTA.
 GEMM_SHAPES = [(128, 256, 64), (256, 12352, 2048), (256, 2048, 4096), (200, 300, 2048), (64, 128, 128),
-               (1000, 12352, 2048), (4096, 2048, 4096), (130, 12288, 2048), (16, 12352, 2048), (40, 2048, 4096)]
+               (1000, 12352, 2048), (4096, 2048, 4096), (130, 12288, 2048), (16, 12352, 2048), (40, 2048, 4096),
+               (100, 16384, 128), (33, 1000, 256)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
