@@ -306,7 +306,7 @@ GDN_API int gdn_decode_step_ex(const gdn_layer* layer, int64_t batch,
  * long, so batches whose workspace (as gdn_decode_workspace_size, for the
  * call's x_dtype) exceeds it are rejected with GDN_ERR_SHAPE: the 35B Q8_0
  * layer fits up to 63 sequences with fp32 x and up to 46 with bf16 / fp16 x,
- * whose projections run on the tensor cores from 9 sequences (fp32 x from 64)
+ * whose projections run on the tensor cores from 5 sequences (fp32 x from 64)
  * with split-K partials that are reserved only then.
  *   - The first call on each device (with that device current) resolves the
  *     scratch address with cudaGetSymbolAddress; make that first call before

@@ -67,13 +67,14 @@ def test_decode_b1_64_steps(t35, w35):
     assert int(st.conv_pos.cpu()[0]) == int(pos_ref[0]) == 64
 
 
-@pytest.mark.parametrize("B,dtype", [(3, torch.float32), (8, torch.bfloat16), (9, torch.bfloat16),
+@pytest.mark.parametrize("B,dtype", [(3, torch.float32), (4, torch.bfloat16), (5, torch.bfloat16),
+                                     (8, torch.bfloat16), (9, torch.bfloat16),
                                      (32, torch.float16), (40, torch.float32), (64, torch.bfloat16),
                                      (64, torch.float32), (96, torch.float16), (130, torch.bfloat16)])
 def test_decode_batched_prefilled(t35, w35, B, dtype):
     """Independent sequences with prefilled states (config 2 style), a few steps:
-    CUDA-core projections (fp32 x below 64 sequences, 16-bit x below 9) and the
-    tensor-core ones (16-bit x from 9, any x from 64)."""
+    CUDA-core projections (fp32 x below 64 sequences, 16-bit x below 5) and the
+    tensor-core ones (16-bit x from 5, any x from 64)."""
     cfg = DIMS_35B
     steps = 3
     S0 = np.stack([synth.prefilled_state(cfg, b) for b in range(B)])

@@ -95,7 +95,7 @@ def test_noalloc_larger_then_smaller_batch():
 
 @pytest.mark.parametrize("batch,dtype", [(64, torch.float32), (47, torch.bfloat16)])
 def test_noalloc_rejects_batches_above_the_scratch(batch, dtype):
-    # fp32 x: from 64 sequences the 35B out_proj splits K; 16-bit x: from 9, and
+    # fp32 x: from 64 sequences the 35B out_proj splits K; 16-bit x: from 5, and
     # from 47 its partials no longer fit
     cfg = DIMS_35B
     dims = gdn_dims(cfg.hidden, cfg.num_k_heads, cfg.num_v_heads, cfg.head_dim)

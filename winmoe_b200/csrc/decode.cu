@@ -342,14 +342,15 @@ inline int mark(PhaseEvents* pe, int i, cudaStream_t s) {
     return GDN_OK;
 }
 
-// Tensor-core projections.  Q8_0 with 16-bit x from 9 sequences: the 35B
-// layer's in_proj + out_proj take ~65 us at any batch up to 128, the int8-MMA
-// GEMV ~4.3 us per row (step 57 / 67 / 81 / 102 us at B = 8 / 16 / 32 / 63
-// against 56 / 100 / 179 / 340 us); with fp32 x, whose exact activations the
-// GEMV keeps, from 64.  Q4_K from 32 rows (below, the fp16-MMA GEMV is faster:
+// Tensor-core projections.  Q8_0 with 16-bit x from 5 sequences: with one M
+// tile the GEMM streams the 35B layer's weights over 128 CTAs, a nearly fixed
+// cost, while the int8-MMA GEMV costs ~4.3 us per row and steps up past 4 rows
+// (device-paced step at B = 4 / 5 / 8: GEMV 33.7 / 50.8 / 51.7 us, GEMM 42.9 /
+// 46.4 / 45.2 us; at 16 / 32 / 63 the GEMM's 55 / 69 / 93 us against 100 / 179
+// / 340 us); with fp32 x, whose exact activations the GEMV keeps, from 64.  Q4_K from 32 rows (below, the fp16-MMA GEMV is faster:
 // the 35B layer's input projection 15 / 21 us at 8 / 16 rows against 29 us).
 constexpr int64_t kTcMinBatch = 64;
-constexpr int64_t kTcMinBatch16 = 9;
+constexpr int64_t kTcMinBatch16 = 5;
 constexpr int64_t kTcMinBatchQ4k = 32;
 
 bool q8_tc(int64_t B, int x_dtype) { return B >= kTcMinBatch || (B >= kTcMinBatch16 && x_dtype != GDN_DTYPE_F32); }
