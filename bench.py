@@ -826,12 +826,14 @@ def run_ours(args):
             b = i % 2
             if i - 2 >= first:
                 s_in.wait_event(ev_comp[b])  # xd[b] was step i-2's input
+                # od[b] held step i-2's output: the compute stream is ordered behind its read-out
+                # through ev_h2d[b] below, so it waits on one copy-engine event per step, not two
+                # (each such wait costs the compute engine ~10 us here, however early the copy ended)
+                s_in.wait_event(ev_d2h[b])
             with torch.cuda.stream(s_in):
                 xd[b].copy_(xh[i], non_blocking=True)
             ev_h2d[b].record(s_in)
             stream.wait_event(ev_h2d[b])
-            if i - 2 >= first:
-                stream.wait_event(ev_d2h[b])  # od[b] held step i-2's output
             L.decode_step(w, st, xd[b], od[b], stream)
             ev_comp[b].record(stream)
             s_out.wait_event(ev_comp[b])
