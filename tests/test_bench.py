@@ -50,7 +50,11 @@ def test_reference_arm_line():
     r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
                         "--warmup", "0"], capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stderr[-2000:]
-    line = json.loads(r.stdout.strip().splitlines()[-1])
+    # stdout carries the JSON line alone: what native code prints (the reference build's own
+    # diagnostics, NCCL's version banner) goes to stderr
+    lines = r.stdout.strip().splitlines()
+    assert len(lines) == 1, lines[:3]
+    line = json.loads(lines[0])
     assert line["impl"] == "reference"
     for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
                 "cpu_baseline", "e2e"):
